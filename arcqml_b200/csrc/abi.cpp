@@ -1,0 +1,541 @@
+// abi.cpp — the exported C ABI: the 14 v1 symbols of arcqml-runtime-sys
+// (crates/arcqml-runtime-sys/src/lib.rs:28-103) and the device-resident v2 extension.
+//
+// Every entry point converts C++ failures into a non-zero status plus a thread-local
+// message; nothing throws or aborts across the boundary.
+#include <cmath>
+#include <new>
+#include <sstream>
+
+#include "../../include/arcqml_runtime.h"
+#include "../../include/arcqml_runtime_v2.h"
+#include "launch.h"
+#include "rt_internal.h"
+
+using namespace arcqml;
+
+namespace {
+
+template <class F>
+int32_t guarded(F &&f) {
+    try {
+        f();
+        return 0;
+    } catch (const Error &e) {
+        set_last_error(e.msg);
+        return 1;
+    } catch (const std::bad_alloc &) {
+        set_last_error("out of host memory");
+        return 2;
+    } catch (const std::exception &e) {
+        set_last_error(std::string("runtime failure: ") + e.what());
+        return 3;
+    } catch (...) {
+        set_last_error("runtime failure");
+        return 3;
+    }
+}
+
+// 2^num_qubits with the reference's overflow and length errors
+// (crates/arcqml-kernel/src/statevector/single.rs:137-148).
+size_t state_dimension(size_t num_qubits) {
+    if (num_qubits >= kMaxQubits) {
+        std::ostringstream s;
+        s << "state dimension overflow for " << num_qubits << " qubits";
+        fail(s.str());
+    }
+    return size_t(1) << num_qubits;
+}
+
+void check_state_length(size_t len, size_t num_qubits) {
+    const size_t expected = state_dimension(num_qubits);
+    if (len != expected) {
+        std::ostringstream s;
+        s << "state length mismatch for " << num_qubits << " qubits: expected " << expected
+          << ", got " << len;
+        fail(s.str());
+    }
+}
+
+uint32_t qubits_of_length(size_t len) {
+    if (len == 0 || (len & (len - 1)) != 0) {
+        std::ostringstream s;
+        s << "state length " << len << " is not a power of two";
+        fail(s.str());
+    }
+    uint32_t n = 0;
+    while ((size_t(1) << n) < len) ++n;
+    if (n >= kMaxQubits) fail("state dimension overflow");
+    return n;
+}
+
+Plan *plan_of(const CircuitPlanHandle *h) {
+    if (!h || !h->opaque) fail("circuit plan handle is null");
+    return static_cast<Plan *>(h->opaque);
+}
+
+Observable *obs_of(const ArcqmlObservableHandle *h) {
+    if (!h || !h->opaque) fail("observable handle is null");
+    return static_cast<Observable *>(h->opaque);
+}
+
+// v2 calls run on the caller's stream; NULL is CUDA's legacy default stream, so work queued
+// by other libraries on it (e.g. torch's default stream) stays ordered with ours.
+cudaStream_t pick_stream(ThreadContext &, void *stream) { return static_cast<cudaStream_t>(stream); }
+
+// Host state -> device buffer `which` of this thread's context.
+double2 *upload_state(ThreadContext &ctx, int which, const arcqml_c128 *host, size_t len) {
+    if (!host) fail("amplitude buffer is null");
+    auto *d = static_cast<double2 *>(ctx_buffer(ctx, which, len * sizeof(double2)));
+    check_cuda(cudaMemcpyAsync(d, host, len * sizeof(double2), cudaMemcpyHostToDevice, ctx.stream),
+               "cudaMemcpyAsync (host to device)");
+    return d;
+}
+
+void download_state(ThreadContext &ctx, const double2 *dev, arcqml_c128 *host, size_t len) {
+    check_cuda(cudaMemcpyAsync(host, dev, len * sizeof(double2), cudaMemcpyDeviceToHost, ctx.stream),
+               "cudaMemcpyAsync (device to host)");
+}
+
+void sync(cudaStream_t s) { check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize"); }
+
+OpRecord push_record(const OperationDescriptor *op) {
+    if (!op) fail("operation descriptor is null");
+    OpRecord r = record_from_descriptor(&op->gate, op->qubits, op->qubits_len, -1);
+    if (op->parameters_len > 3)
+        fail("a gate has more parameter slots than the runtime ABI supports");
+    if (op->parameters_len && !op->parameters) fail("parameter binding list is null");
+    r.num_bindings = uint32_t(op->parameters_len);
+    for (size_t b = 0; b < op->parameters_len; ++b) {
+        const size_t slot = op->parameters[b].parameter_slot;
+        if (slot >= slot_count(r.opcode)) {
+            std::ostringstream s;
+            s << "gate " << r.name << " does not have parameter slot " << slot;
+            fail(s.str());
+        }
+        r.slots[b] = slot;
+        r.parents[b] = op->parameters[b].parent_index;
+    }
+    return r;
+}
+
+// Applies one host-described gate to device amplitudes.
+void apply_gate_device(double2 *d, size_t batch, uint32_t n, const OpRecord &rec, bool adjoint,
+                       ThreadContext &ctx, cudaStream_t s) {
+    DevGate g = lower(rec, adjoint ? LOWER_ADJOINT : LOWER_FORWARD, 0);
+    if (g.kind == KIND_DENSE) {
+        std::vector<double2> m = rec.custom;
+        if (adjoint) {
+            const size_t dim = size_t(1) << rec.qubits.size();
+            for (size_t i = 0; i < dim; ++i)
+                for (size_t j = 0; j < dim; ++j)
+                    m[j * dim + i] = make_double2(rec.custom[i * dim + j].x, -rec.custom[i * dim + j].y);
+        }
+        std::vector<const std::vector<double2> *> refs{&m};
+        g.dense = upload_tables(refs, ctx, s)[0];
+        launch_gate(d, batch, n, g, s);
+        sync(s);  // the table lives in host memory owned by this frame
+        return;
+    }
+    launch_gate(d, batch, n, g, s);
+}
+
+void check_slot(const OpRecord &rec, size_t slot) {
+    if (slot >= slot_count(rec.opcode)) {
+        std::ostringstream s;
+        s << "gate " << rec.name << " does not have parameter slot " << slot;
+        fail(s.str());
+    }
+}
+
+}  // namespace
+
+// The library is built with -fvisibility=hidden; only the C ABI below is exported.
+#pragma GCC visibility push(default)
+extern "C" {
+
+// ============================================================================ v1
+
+uint32_t arcqml_rt_abi_version(void) { return ARCQML_RT_ABI_VERSION; }
+
+static int32_t apply_gate_v1(arcqml_c128 *amplitudes, size_t len, size_t num_qubits,
+                             const GateDescriptor *gate, const size_t *qubits, size_t qlen,
+                             bool adjoint) {
+    return guarded([&] {
+        check_state_length(len, num_qubits);
+        OpRecord rec = record_from_descriptor(gate, qubits, qlen, int64_t(num_qubits));
+        ThreadContext &ctx = thread_context();
+        double2 *d = upload_state(ctx, 0, amplitudes, len);
+        apply_gate_device(d, 1, uint32_t(num_qubits), rec, adjoint, ctx, ctx.stream);
+        download_state(ctx, d, amplitudes, len);
+        sync(ctx.stream);
+    });
+}
+
+int32_t arcqml_rt_v1_apply_gate(arcqml_c128 *amplitudes, size_t amplitudes_len, size_t num_qubits,
+                                const GateDescriptor *gate, const size_t *qubits,
+                                size_t qubits_len) {
+    return apply_gate_v1(amplitudes, amplitudes_len, num_qubits, gate, qubits, qubits_len, false);
+}
+
+int32_t arcqml_rt_v1_apply_adjoint_gate(arcqml_c128 *amplitudes, size_t amplitudes_len,
+                                        size_t num_qubits, const GateDescriptor *gate,
+                                        const size_t *qubits, size_t qubits_len) {
+    return apply_gate_v1(amplitudes, amplitudes_len, num_qubits, gate, qubits, qubits_len, true);
+}
+
+int32_t arcqml_rt_v1_parameter_derivative_into(const arcqml_c128 *input, size_t input_len,
+                                               arcqml_c128 *output, size_t output_len,
+                                               const GateDescriptor *gate, const size_t *qubits,
+                                               size_t qubits_len, size_t parameter_slot) {
+    return guarded([&] {
+        const uint32_t n = qubits_of_length(input_len);
+        if (output_len != input_len) {
+            std::ostringstream s;
+            s << "state length mismatch for " << n << " qubits: expected " << input_len
+              << ", got " << output_len;
+            fail(s.str());
+        }
+        if (!output) fail("output buffer is null");
+        OpRecord rec = record_from_descriptor(gate, qubits, qubits_len, int64_t(n));
+        check_slot(rec, parameter_slot);
+        ThreadContext &ctx = thread_context();
+        double2 *din = upload_state(ctx, 0, input, input_len);
+        auto *dout = static_cast<double2 *>(ctx_buffer(ctx, 1, input_len * sizeof(double2)));
+        DevGate g = lower(rec, LOWER_DERIVATIVE, uint32_t(parameter_slot));
+        launch_gate_out(din, dout, 1, n, g, ctx.stream);
+        download_state(ctx, dout, output, output_len);
+        sync(ctx.stream);
+    });
+}
+
+int32_t arcqml_rt_v1_derivative_matrix_create(const GateDescriptor *gate, size_t parameter_slot,
+                                              DerivativeMatrixHandle *output) {
+    return guarded([&] {
+        if (!output) fail("derivative matrix handle is null");
+        if (!gate) fail("gate descriptor is null");
+        // Validate against a canonical qubit list 0..arity-1 (the matrix is position-free).
+        std::vector<size_t> q(gate->arity);
+        for (size_t i = 0; i < q.size(); ++i) q[i] = i;
+        OpRecord rec = record_from_descriptor(gate, q.data(), q.size(), -1);
+        check_slot(rec, parameter_slot);
+        std::vector<double2> m = dense_matrix(rec, true, uint32_t(parameter_slot));
+        auto *data = new arcqml_c128[m.size()];
+        for (size_t i = 0; i < m.size(); ++i) data[i] = arcqml_c128{m[i].x, m[i].y};
+        output->data = data;
+        output->len = m.size();
+        output->capacity = m.size();
+    });
+}
+
+int32_t arcqml_rt_v1_derivative_matrix_apply(arcqml_c128 *amplitudes, size_t amplitudes_len,
+                                             const DerivativeMatrixHandle *matrix,
+                                             const size_t *qubits, size_t qubits_len) {
+    return guarded([&] {
+        if (!matrix || !matrix->data) fail("derivative matrix handle is null");
+        const uint32_t n = qubits_of_length(amplitudes_len);
+        const size_t k = qubits_len;
+        if (k == 0 || k > kMaxDenseArity || matrix->len != (size_t(1) << (2 * k))) {
+            std::ostringstream s;
+            s << "derivative matrix of " << matrix->len << " entries does not act on " << k
+              << " qubits";
+            fail(s.str());
+        }
+        if (!qubits) fail("qubit list is null");
+        OpRecord rec;
+        rec.opcode = ARCQML_OP_CUSTOM_UNITARY;
+        rec.name = "derivative";
+        for (size_t i = 0; i < k; ++i) {
+            if (qubits[i] >= n) {
+                std::ostringstream s;
+                s << "qubit index " << qubits[i] << " is out of range for " << n << " qubits";
+                fail(s.str());
+            }
+            for (size_t j = 0; j < i; ++j)
+                if (qubits[j] == qubits[i]) fail("duplicate qubit index " + std::to_string(qubits[i]));
+            rec.qubits.push_back(uint32_t(qubits[i]));
+        }
+        rec.custom.resize(matrix->len);
+        for (size_t i = 0; i < matrix->len; ++i)
+            rec.custom[i] = make_double2(matrix->data[i].re, matrix->data[i].im);
+        ThreadContext &ctx = thread_context();
+        double2 *d = upload_state(ctx, 0, amplitudes, amplitudes_len);
+        DevGate g = lower(rec, LOWER_FORWARD, 0, false);
+        if (g.kind == KIND_DENSE) {
+            std::vector<const std::vector<double2> *> refs{&rec.custom};
+            g.dense = upload_tables(refs, ctx, ctx.stream)[0];
+        }
+        launch_gate(d, 1, n, g, ctx.stream);
+        download_state(ctx, d, amplitudes, amplitudes_len);
+        sync(ctx.stream);
+    });
+}
+
+void arcqml_rt_v1_derivative_matrix_destroy(DerivativeMatrixHandle *matrix) {
+    if (!matrix || !matrix->data) return;
+    delete[] matrix->data;
+    matrix->data = nullptr;
+    matrix->len = 0;
+    matrix->capacity = 0;
+}
+
+int32_t arcqml_rt_v1_circuit_plan_create(const OperationDescriptor *operations,
+                                         size_t operations_len, CircuitPlanHandle *output) {
+    return guarded([&] {
+        if (!output) fail("circuit plan handle is null");
+        if (operations_len && !operations) fail("operation list is null");
+        std::unique_ptr<Plan> p(new Plan());
+        p->ops.reserve(operations_len);
+        for (size_t i = 0; i < operations_len; ++i) p->ops.push_back(push_record(&operations[i]));
+        output->opaque = p.release();
+    });
+}
+
+int32_t arcqml_rt_v1_circuit_plan_create_empty(size_t operation_capacity,
+                                               CircuitPlanHandle *output) {
+    return guarded([&] {
+        if (!output) fail("circuit plan handle is null");
+        std::unique_ptr<Plan> p(new Plan());
+        p->ops.reserve(operation_capacity < (size_t(1) << 24) ? operation_capacity : 0);
+        output->opaque = p.release();
+    });
+}
+
+int32_t arcqml_rt_v1_circuit_plan_push(CircuitPlanHandle *plan,
+                                       const OperationDescriptor *operation) {
+    return guarded([&] { plan_of(plan)->ops.push_back(push_record(operation)); });
+}
+
+int32_t arcqml_rt_v1_circuit_plan_apply(const CircuitPlanHandle *plan, arcqml_c128 *amplitudes,
+                                        size_t amplitudes_len, size_t num_qubits) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        check_state_length(amplitudes_len, num_qubits);
+        validate_plan_for_state(*p, uint32_t(num_qubits));
+        ThreadContext &ctx = thread_context();
+        double2 *d = upload_state(ctx, 0, amplitudes, amplitudes_len);
+        plan_apply_device(*p, d, 1, uint32_t(num_qubits), ctx, ctx.stream);
+        download_state(ctx, d, amplitudes, amplitudes_len);
+        sync(ctx.stream);
+    });
+}
+
+int32_t arcqml_rt_v1_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
+                                      arcqml_c128 *adjoint_state, size_t state_len,
+                                      arcqml_c128 *derivative_state, size_t num_qubits,
+                                      double upstream, const uint8_t *parameter_requires_grad,
+                                      size_t parameter_requires_grad_len, double *gradients,
+                                      size_t gradients_len) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        check_state_length(state_len, num_qubits);
+        if (!derivative_state) fail("derivative state buffer is null");
+        if (parameter_requires_grad_len && !parameter_requires_grad)
+            fail("requires-grad list is null");
+        if (gradients_len && !gradients) fail("gradient buffer is null");
+        validate_plan_for_state(*p, uint32_t(num_qubits));
+        check_bindings(*p, parameter_requires_grad_len, gradients_len);
+        ThreadContext &ctx = thread_context();
+        double2 *dpsi = upload_state(ctx, 0, forward_state, state_len);
+        double2 *dlam = upload_state(ctx, 1, adjoint_state, state_len);
+        adjoint_backward_device(*p, dpsi, dlam, 1, uint32_t(num_qubits), &upstream,
+                                parameter_requires_grad, parameter_requires_grad_len, gradients,
+                                gradients_len, ctx, ctx.stream);
+        download_state(ctx, dpsi, forward_state, state_len);
+        download_state(ctx, dlam, adjoint_state, state_len);
+        sync(ctx.stream);
+    });
+}
+
+void arcqml_rt_v1_circuit_plan_destroy(CircuitPlanHandle *plan) {
+    if (!plan || !plan->opaque) return;
+    delete static_cast<Plan *>(plan->opaque);
+    plan->opaque = nullptr;
+}
+
+size_t arcqml_rt_last_error(uint8_t *buffer, size_t capacity) {
+    const std::string &m = last_error();
+    if (buffer && capacity) {
+        const size_t n = m.size() < capacity ? m.size() : capacity;
+        std::memcpy(buffer, m.data(), n);
+        if (n < capacity) buffer[n] = 0;
+    }
+    return m.size();
+}
+
+// ============================================================================ v2
+
+int32_t arcqml_rt_v2_observable_create(size_t num_qubits, const double *coefficients,
+                                       const uint64_t *flip_masks, const uint64_t *phase_masks,
+                                       size_t num_terms, ArcqmlObservableHandle *output) {
+    return guarded([&] {
+        if (!output) fail("observable handle is null");
+        output->opaque = make_observable(num_qubits, coefficients, flip_masks, phase_masks, num_terms);
+    });
+}
+
+void arcqml_rt_v2_observable_destroy(ArcqmlObservableHandle *observable) {
+    if (!observable || !observable->opaque) return;
+    delete static_cast<Observable *>(observable->opaque);
+    observable->opaque = nullptr;
+}
+
+static void check_device_state(const void *amps, size_t batch, size_t num_qubits) {
+    if (!amps) fail("amplitude buffer is null");
+    if (batch == 0) fail("batch size must be non-zero");
+    state_dimension(num_qubits);
+}
+
+int32_t arcqml_rt_v2_plan_apply(const CircuitPlanHandle *plan, arcqml_c128 *amplitudes,
+                                size_t batch, size_t num_qubits, void *stream) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        check_device_state(amplitudes, batch, num_qubits);
+        ThreadContext &ctx = thread_context();
+        cudaStream_t s = pick_stream(ctx, stream);
+        plan_apply_device(*p, reinterpret_cast<double2 *>(amplitudes), batch, uint32_t(num_qubits),
+                          ctx, s);
+        // Tables uploaded for dense gates live in a per-thread buffer; the next call on this
+        // thread may overwrite them only after this stream's work (stream order).
+    });
+}
+
+int32_t arcqml_rt_v2_apply_gate(arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                const GateDescriptor *gate, const size_t *qubits,
+                                size_t qubits_len, int32_t adjoint, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        OpRecord rec = record_from_descriptor(gate, qubits, qubits_len, int64_t(num_qubits));
+        ThreadContext &ctx = thread_context();
+        apply_gate_device(reinterpret_cast<double2 *>(amplitudes), batch, uint32_t(num_qubits), rec,
+                          adjoint != 0, ctx, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_parameter_derivative(const arcqml_c128 *input, arcqml_c128 *output,
+                                          size_t batch, size_t num_qubits,
+                                          const GateDescriptor *gate, const size_t *qubits,
+                                          size_t qubits_len, size_t parameter_slot,
+                                          void *stream) {
+    return guarded([&] {
+        check_device_state(input, batch, num_qubits);
+        if (!output) fail("output buffer is null");
+        OpRecord rec = record_from_descriptor(gate, qubits, qubits_len, int64_t(num_qubits));
+        check_slot(rec, parameter_slot);
+        ThreadContext &ctx = thread_context();
+        DevGate g = lower(rec, LOWER_DERIVATIVE, uint32_t(parameter_slot));
+        launch_gate_out(reinterpret_cast<const double2 *>(input), reinterpret_cast<double2 *>(output),
+                        batch, uint32_t(num_qubits), g, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_expectation(const ArcqmlObservableHandle *observable,
+                                 const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                 double *values, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (!values) fail("value buffer is null");
+        ThreadContext &ctx = thread_context();
+        observable_device(*obs_of(observable), reinterpret_cast<const double2 *>(amplitudes), nullptr,
+                          batch, uint32_t(num_qubits), values, ctx, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_expectation_and_apply(const ArcqmlObservableHandle *observable,
+                                           const arcqml_c128 *amplitudes, arcqml_c128 *output,
+                                           size_t batch, size_t num_qubits, double *values,
+                                           void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (!values || !output) fail("output buffer is null");
+        ThreadContext &ctx = thread_context();
+        observable_device(*obs_of(observable), reinterpret_cast<const double2 *>(amplitudes),
+                          reinterpret_cast<double2 *>(output), batch, uint32_t(num_qubits), values,
+                          ctx, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
+                                      arcqml_c128 *adjoint_state, size_t batch,
+                                      size_t num_qubits, const double *upstream,
+                                      const uint8_t *parameter_requires_grad,
+                                      size_t parameter_requires_grad_len, double *gradients,
+                                      size_t gradients_len, void *stream) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        check_device_state(forward_state, batch, num_qubits);
+        if (!adjoint_state) fail("adjoint state buffer is null");
+        if (!upstream) fail("upstream buffer is null");
+        if (parameter_requires_grad_len && !parameter_requires_grad)
+            fail("requires-grad list is null");
+        if (gradients_len && !gradients) fail("gradient buffer is null");
+        ThreadContext &ctx = thread_context();
+        adjoint_backward_device(*p, reinterpret_cast<double2 *>(forward_state),
+                                reinterpret_cast<double2 *>(adjoint_state), batch,
+                                uint32_t(num_qubits), upstream, parameter_requires_grad,
+                                parameter_requires_grad_len, gradients, gradients_len, ctx,
+                                pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                           double *norms, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (!norms) fail("norm buffer is null");
+        ThreadContext &ctx = thread_context();
+        cudaStream_t s = pick_stream(ctx, stream);
+        const size_t chunk = 65535;
+        const size_t dim = size_t(1) << num_qubits;
+        for (size_t b0 = 0; b0 < batch; b0 += chunk) {
+            const size_t rows = std::min(chunk, batch - b0);
+            double *partials = ctx_partials(ctx, rows * size_t(adjoint_max_blocks()));
+            const unsigned bx = launch_norms(reinterpret_cast<const double2 *>(amplitudes) + b0 * dim,
+                                             rows, uint32_t(num_qubits), partials, s);
+            double *sums = ctx_dgrads(ctx, rows);
+            launch_reduce_rows(partials, uint32_t(rows), bx, sums, s);
+            double *h = ctx_hvals(ctx, rows);
+            check_cuda(cudaMemcpyAsync(h, sums, rows * sizeof(double), cudaMemcpyDeviceToHost, s),
+                       "cudaMemcpyAsync (norms)");
+            sync(s);
+            std::memcpy(norms + b0, h, rows * sizeof(double));
+        }
+    });
+}
+
+int32_t arcqml_rt_v2_set_basis_state(arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                     uint64_t index, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (index >= (uint64_t(1) << num_qubits)) fail("basis index out of range");
+        ThreadContext &ctx = thread_context();
+        launch_basis_state(reinterpret_cast<double2 *>(amplitudes), batch, uint32_t(num_qubits),
+                           index, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_plan_set_parameters(CircuitPlanHandle *plan, const double *parent_values,
+                                         size_t parent_values_len) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        if (parent_values_len && !parent_values) fail("parameter value list is null");
+        for (auto &op : p->ops)
+            for (uint32_t b = 0; b < op.num_bindings; ++b)
+                if (op.parents[b] >= parent_values_len)
+                    fail("parameter parent index " + std::to_string(op.parents[b]) + " is out of range");
+        for (auto &op : p->ops)
+            for (uint32_t b = 0; b < op.num_bindings; ++b) {
+                const double v = parent_values[op.parents[b]];
+                if (!std::isfinite(v)) fail("parameter value is not finite");
+                op.params[op.slots[b]] = v;
+            }
+    });
+}
+
+size_t arcqml_rt_v2_plan_len(const CircuitPlanHandle *plan) {
+    if (!plan || !plan->opaque) return 0;
+    return static_cast<const Plan *>(plan->opaque)->ops.size();
+}
+
+}  // extern "C"
+#pragma GCC visibility pop

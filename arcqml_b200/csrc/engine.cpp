@@ -1,0 +1,392 @@
+// engine.cpp — device orchestration: per-thread contexts, plan execution, the adjoint
+// reverse sweep and Pauli observables on device-resident states.
+//
+// Reverse sweep (docs/ArcQML技术手册.md:426-454, loop order of
+// crates/arcqml-unitary/src/fit/adjoint.rs:19-66): lambda <- g lambda; for k = m..1:
+// psi <- U_k^dag psi; grads[parent] += 2 Re<lambda|dU_k/dp psi>; lambda <- U_k^dag lambda.
+// Each reversed gate with a required slot is ONE kernel pass over psi and lambda
+// (k_adjoint): 64 bytes of HBM traffic per touched amplitude, no derivative scratch state.
+#include <algorithm>
+#include <cmath>
+#include <sstream>
+#include <unordered_map>
+
+#include "launch.h"
+#include "rt_internal.h"
+
+namespace arcqml {
+
+// ------------------------------------------------------------------ errors
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+void set_last_error(const std::string &msg) { t_last_error = msg; }
+const std::string &last_error() { return t_last_error; }
+
+void fail(const std::string &msg) { throw Error{msg}; }
+
+void check_cuda(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) {
+        std::ostringstream s;
+        s << what << " failed: " << cudaGetErrorString(e);
+        throw Error{s.str()};
+    }
+}
+
+// ------------------------------------------------------------------ thread contexts
+
+namespace {
+
+struct ContextSlot {
+    ThreadContext ctx;
+    ~ContextSlot() {
+        // Thread exit: release device buffers (the CUDA context may already be gone at
+        // process exit; errors are ignored).
+        int prev = -1;
+        if (cudaGetDevice(&prev) != cudaSuccess) return;
+        if (ctx.device >= 0 && cudaSetDevice(ctx.device) == cudaSuccess) {
+            for (int i = 0; i < 4; ++i)
+                if (ctx.buf[i]) cudaFree(ctx.buf[i]);
+            if (ctx.partials) cudaFree(ctx.partials);
+            if (ctx.dgrads) cudaFree(ctx.dgrads);
+            if (ctx.hvals) cudaFreeHost(ctx.hvals);
+            if (ctx.stream) cudaStreamDestroy(ctx.stream);
+        }
+        cudaSetDevice(prev);
+    }
+};
+
+thread_local std::unordered_map<int, std::unique_ptr<ContextSlot>> t_contexts;
+
+}  // namespace
+
+ThreadContext &thread_context() {
+    int dev = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    auto &slot = t_contexts[dev];
+    if (!slot) {
+        slot.reset(new ContextSlot());
+        slot->ctx.device = dev;
+        check_cuda(cudaStreamCreateWithFlags(&slot->ctx.stream, cudaStreamNonBlocking),
+                   "cudaStreamCreateWithFlags");
+    }
+    return slot->ctx;
+}
+
+void *ctx_buffer(ThreadContext &c, int which, size_t bytes) {
+    if (bytes > c.cap[which]) {
+        if (c.buf[which]) {
+            check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+            check_cuda(cudaFree(c.buf[which]), "cudaFree");
+            c.buf[which] = nullptr;
+            c.cap[which] = 0;
+        }
+        check_cuda(cudaMalloc(&c.buf[which], bytes), "cudaMalloc");
+        c.cap[which] = bytes;
+    }
+    return c.buf[which];
+}
+
+double *ctx_partials(ThreadContext &c, size_t count) {
+    if (count > c.partials_cap) {
+        if (c.partials) {
+            check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+            check_cuda(cudaFree(c.partials), "cudaFree");
+            c.partials = nullptr;
+            c.partials_cap = 0;
+        }
+        check_cuda(cudaMalloc(&c.partials, count * sizeof(double)), "cudaMalloc");
+        c.partials_cap = count;
+    }
+    return c.partials;
+}
+
+double *ctx_dgrads(ThreadContext &c, size_t count) {
+    if (count > c.dgrads_cap) {
+        if (c.dgrads) {
+            check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+            check_cuda(cudaFree(c.dgrads), "cudaFree");
+            c.dgrads = nullptr;
+            c.dgrads_cap = 0;
+        }
+        check_cuda(cudaMalloc(&c.dgrads, count * sizeof(double)), "cudaMalloc");
+        c.dgrads_cap = count;
+    }
+    return c.dgrads;
+}
+
+double *ctx_hvals(ThreadContext &c, size_t count) {
+    if (count > c.hvals_cap) {
+        if (c.hvals) {
+            check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+            check_cuda(cudaFreeHost(c.hvals), "cudaFreeHost");
+            c.hvals = nullptr;
+            c.hvals_cap = 0;
+        }
+        check_cuda(cudaMallocHost(&c.hvals, count * sizeof(double)), "cudaMallocHost");
+        c.hvals_cap = count;
+    }
+    return c.hvals;
+}
+
+std::vector<const double2 *> upload_tables(const std::vector<const std::vector<double2> *> &ms,
+                                           ThreadContext &ctx, cudaStream_t s) {
+    size_t total = 0;
+    for (auto *m : ms) total += m->size();
+    std::vector<const double2 *> out;
+    if (total == 0) return out;
+    // The table buffer may still be read by kernels queued on another stream by an earlier
+    // call of this thread; wait for them before overwriting it.
+    if (ctx.table_stream && ctx.table_stream != s)
+        check_cuda(cudaStreamSynchronize(ctx.table_stream), "cudaStreamSynchronize");
+    ctx.table_stream = s;
+    auto *dev = static_cast<double2 *>(ctx_buffer(ctx, 3, total * sizeof(double2)));
+    size_t off = 0;
+    for (auto *m : ms) {
+        check_cuda(cudaMemcpyAsync(dev + off, m->data(), m->size() * sizeof(double2),
+                                   cudaMemcpyHostToDevice, s),
+                   "cudaMemcpyAsync (tables)");
+        out.push_back(dev + off);
+        off += m->size();
+    }
+    return out;
+}
+
+// ------------------------------------------------------------------ plan execution
+
+void validate_plan_for_state(const Plan &plan, uint32_t n) {
+    for (const auto &op : plan.ops) check_qubits_for_state(op, n);
+}
+
+void plan_apply_device(Plan &plan, double2 *amps, size_t batch, uint32_t n, ThreadContext &ctx,
+                       cudaStream_t s) {
+    validate_plan_for_state(plan, n);
+    std::vector<std::vector<double2>> dense;
+    std::vector<DevGate> gates;
+    gates.reserve(plan.ops.size());
+    for (const auto &op : plan.ops) {
+        DevGate g = lower(op, LOWER_FORWARD, 0);
+        if (g.kind == KIND_DENSE) dense.push_back(op.custom);
+        gates.push_back(g);
+    }
+    std::vector<const std::vector<double2> *> refs;
+    for (auto &d : dense) refs.push_back(&d);
+    auto ptrs = upload_tables(refs, ctx, s);
+    size_t di = 0;
+    for (auto &g : gates) {
+        if (g.kind == KIND_DENSE) g.dense = ptrs[di++];
+        launch_gate(amps, batch, n, g, s);
+    }
+}
+
+namespace {
+
+// Dense (conjugate-transposed) custom matrix for the adjoint of a KIND_DENSE gate.
+std::vector<double2> dagger(const std::vector<double2> &m, size_t dim) {
+    std::vector<double2> t(dim * dim);
+    for (size_t i = 0; i < dim; ++i)
+        for (size_t j = 0; j < dim; ++j) t[j * dim + i] = make_double2(m[i * dim + j].x, -m[i * dim + j].y);
+    return t;
+}
+
+}  // namespace
+
+void check_bindings(const Plan &plan, size_t req_len, size_t grads_len) {
+    for (const auto &op : plan.ops)
+        for (uint32_t b = 0; b < op.num_bindings; ++b) {
+            if (op.parents[b] >= req_len || op.parents[b] >= grads_len) {
+                std::ostringstream s;
+                s << "parameter parent index " << op.parents[b]
+                  << " is out of range (requires_grad length " << req_len
+                  << ", gradients length " << grads_len << ")";
+                fail(s.str());
+            }
+        }
+}
+
+void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batch, uint32_t n,
+                             const double *upstream_host, const uint8_t *req, size_t req_len,
+                             double *grads_host, size_t grads_len, ThreadContext &ctx,
+                             cudaStream_t s) {
+    validate_plan_for_state(plan, n);
+    check_bindings(plan, req_len, grads_len);
+
+    // lambda <- g lambda (per row)
+    {
+        // pack the per-row factors as doubles inside the table buffer
+        std::vector<double2> packed((batch + 1) / 2);
+        std::memcpy(packed.data(), upstream_host, batch * sizeof(double));
+        std::vector<const std::vector<double2> *> refs{&packed};
+        auto p = upload_tables(refs, ctx, s);
+        launch_scale(lam, batch, n, reinterpret_cast<const double *>(p[0]), s);
+        // The table buffer is reused below for dense matrices; keep the scale ordered first.
+    }
+
+    // Rows of partial sums, one per (op, binding) that needs a gradient, in sweep order.
+    struct Row {
+        size_t parent;
+    };
+    std::vector<Row> rows;
+    for (size_t k = plan.ops.size(); k-- > 0;) {
+        const auto &op = plan.ops[k];
+        for (uint32_t b = 0; b < op.num_bindings; ++b)
+            if (req[op.parents[b]]) rows.push_back({op.parents[b]});
+    }
+    const unsigned cap = adjoint_max_blocks();
+    double *partials = nullptr;
+    if (!rows.empty()) {
+        partials = ctx_partials(ctx, rows.size() * size_t(cap));
+        check_cuda(cudaMemsetAsync(partials, 0, rows.size() * size_t(cap) * sizeof(double), s),
+                   "cudaMemsetAsync");
+    }
+
+    // Dense custom gates (arity > 2) need their adjoint matrices on the device.
+    std::vector<std::vector<double2>> dense;
+    for (size_t k = plan.ops.size(); k-- > 0;) {
+        const auto &op = plan.ops[k];
+        if (op.opcode == ARCQML_OP_CUSTOM_UNITARY && op.qubits.size() > 2)
+            dense.push_back(dagger(op.custom, size_t(1) << op.qubits.size()));
+    }
+    std::vector<const std::vector<double2> *> refs;
+    for (auto &d : dense) refs.push_back(&d);
+    auto dptr = upload_tables(refs, ctx, s);
+    size_t di = 0;
+
+    size_t row = 0;
+    for (size_t k = plan.ops.size(); k-- > 0;) {
+        const auto &op = plan.ops[k];
+        double2 d[3][16];
+        int ns = 0;
+        for (uint32_t b = 0; b < op.num_bindings; ++b) {
+            if (!req[op.parents[b]]) continue;
+            DevGate dg = lower(op, LOWER_DERIVATIVE, uint32_t(op.slots[b]), false);
+            for (int i = 0; i < 16; ++i) d[ns][i] = dg.m[i];
+            ++ns;
+        }
+        if (ns == 0) {
+            DevGate u = lower(op, LOWER_ADJOINT, 0);
+            if (u.kind == KIND_DENSE) u.dense = dptr[di++];
+            launch_gate(psi, batch, n, u, s);
+            launch_gate(lam, batch, n, u, s);
+            continue;
+        }
+        DevGate u = lower(op, LOWER_ADJOINT, 0, false);
+        launch_adjoint_raw(psi, lam, batch, n, u, d, ns, partials + row * size_t(cap), s);
+        row += size_t(ns);
+    }
+
+    if (!rows.empty()) {
+        double *sums = ctx_dgrads(ctx, rows.size());
+        launch_reduce_rows(partials, uint32_t(rows.size()), cap, sums, s);
+        double *h = ctx_hvals(ctx, rows.size());
+        check_cuda(cudaMemcpyAsync(h, sums, rows.size() * sizeof(double), cudaMemcpyDeviceToHost, s),
+                   "cudaMemcpyAsync (gradients)");
+        check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        for (size_t j = 0; j < rows.size(); ++j) grads_host[rows[j].parent] += 2.0 * h[j];
+    }
+}
+
+// ------------------------------------------------------------------ observables
+
+void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
+                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s) {
+    if (obs.num_qubits != n) {
+        std::ostringstream m;
+        m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
+        fail(m.str());
+    }
+    const size_t nt = obs.coef.size();
+    const size_t ng = obs.groups.size();
+    // Pack tables: w (double2 per term), z (u64 per term), flip (u64 per group),
+    // first/count (u32 per group), all in one upload.
+    const size_t wz_bytes = nt * 16 + nt * 8;
+    const size_t g_bytes = ng * 8 + ng * 8;
+    std::vector<double2> pack((wz_bytes + g_bytes + 15) / 16 + 1);
+    char *base = reinterpret_cast<char *>(pack.data());
+    double2 *w = reinterpret_cast<double2 *>(base);
+    uint64_t *z = reinterpret_cast<uint64_t *>(base + nt * 16);
+    uint64_t *flip = reinterpret_cast<uint64_t *>(base + nt * 24);
+    uint32_t *first = reinterpret_cast<uint32_t *>(base + nt * 24 + ng * 8);
+    uint32_t *count = first + ng;
+    for (size_t k = 0; k < nt; ++k) {
+        const double c = obs.coef[k];
+        switch (obs.ymod4[k] & 3u) {
+        case 0: w[k] = make_double2(c, 0.0); break;
+        case 1: w[k] = make_double2(0.0, c); break;
+        case 2: w[k] = make_double2(-c, 0.0); break;
+        default: w[k] = make_double2(0.0, -c); break;
+        }
+        z[k] = obs.zmask[k];
+    }
+    for (size_t g = 0; g < ng; ++g) {
+        flip[g] = obs.groups[g].flip;
+        first[g] = obs.groups[g].first;
+        count[g] = obs.groups[g].count;
+    }
+    std::vector<const std::vector<double2> *> refs{&pack};
+    auto p = upload_tables(refs, ctx, s);
+    const char *dbase = reinterpret_cast<const char *>(p[0]);
+    const double2 *dw = reinterpret_cast<const double2 *>(dbase);
+    const uint64_t *dz = reinterpret_cast<const uint64_t *>(dbase + nt * 16);
+    const uint64_t *dflip = reinterpret_cast<const uint64_t *>(dbase + nt * 24);
+    const uint32_t *dfirst = reinterpret_cast<const uint32_t *>(dbase + nt * 24 + ng * 8);
+    const uint32_t *dcount = dfirst + ng;
+
+    const size_t dim = size_t(1) << n;
+    const size_t chunk = 65535;  // grid.y limit
+    for (size_t b0 = 0; b0 < batch; b0 += chunk) {
+        const size_t rows = std::min(chunk, batch - b0);
+        const unsigned bx_cap = adjoint_max_blocks();
+        double *partials = ctx_partials(ctx, rows * size_t(bx_cap));
+        const unsigned bx = launch_pauli(psi + b0 * dim, out ? out + b0 * dim : nullptr, rows, n,
+                                         dw, dz, dflip, dfirst, dcount, uint32_t(ng), partials, s);
+        double *sums = ctx_dgrads(ctx, rows);
+        launch_reduce_rows(partials, uint32_t(rows), bx, sums, s);
+        double *h = ctx_hvals(ctx, rows);
+        check_cuda(cudaMemcpyAsync(h, sums, rows * sizeof(double), cudaMemcpyDeviceToHost, s),
+                   "cudaMemcpyAsync (values)");
+        check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        std::memcpy(values_host + b0, h, rows * sizeof(double));
+    }
+}
+
+Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,
+                            const uint64_t *phase, size_t num_terms) {
+    if (num_qubits >= 64) fail("observable qubit count must be below 64");
+    if (num_terms && (!coef || !flip || !phase)) fail("observable term arrays are null");
+    std::unique_ptr<Observable> o(new Observable());
+    o->num_qubits = uint32_t(num_qubits);
+    const uint64_t limit = num_qubits >= 64 ? ~uint64_t(0) : ((uint64_t(1) << num_qubits) - 1);
+    // Group terms by flip mask in first-appearance order; the diagonal group (flip 0) is
+    // evaluated with the same code path.
+    std::vector<uint64_t> order;
+    std::unordered_map<uint64_t, std::vector<size_t>> by_flip;
+    for (size_t k = 0; k < num_terms; ++k) {
+        if ((flip[k] | phase[k]) & ~limit) fail("Pauli term acts on a qubit outside the observable");
+        if (!std::isfinite(coef[k])) fail("Pauli term coefficient is not finite");
+        auto it = by_flip.find(flip[k]);
+        if (it == by_flip.end()) {
+            order.push_back(flip[k]);
+            by_flip[flip[k]] = {k};
+        } else {
+            it->second.push_back(k);
+        }
+    }
+    for (uint64_t f : order) {
+        PauliGroup g;
+        g.flip = f;
+        g.first = uint32_t(o->coef.size());
+        g.count = uint32_t(by_flip[f].size());
+        for (size_t k : by_flip[f]) {
+            o->coef.push_back(coef[k]);
+            o->zmask.push_back(phase[k]);
+            o->ymod4.push_back(uint32_t(__builtin_popcountll(flip[k] & phase[k]) & 3));
+        }
+        o->groups.push_back(g);
+    }
+    return o.release();
+}
+
+}  // namespace arcqml

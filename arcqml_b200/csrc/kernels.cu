@@ -1,0 +1,494 @@
+// kernels.cu — per-gate statevector kernels for sm_100a (complex128, HBM-bound).
+//
+// Every kernel walks "groups": the 2^nt amplitudes a gate mixes, found by inserting zero
+// bits at the gate's sorted fixed positions (targets and controls) into a group counter and
+// OR-ing the control mask. Consecutive threads take consecutive group counters, so for any
+// target above bit 0 a warp reads 32 consecutive 16-byte amplitudes per load (fully
+// coalesced 512 B), and for target 0 each thread reads one 32-byte pair (also coalesced).
+// Batches [batch, 2^n] are one flat group range: row = counter >> (n - npos).
+#include <cuda_runtime.h>
+
+#include "rt_internal.h"
+
+namespace arcqml {
+
+namespace {
+
+__device__ __forceinline__ double2 cmul(double2 a, double2 b) {
+    return make_double2(fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x));
+}
+__device__ __forceinline__ double2 cfma(double2 a, double2 b, double2 c) {
+    // a*b + c
+    return make_double2(fma(a.x, b.x, fma(-a.y, b.y, c.x)), fma(a.x, b.y, fma(a.y, b.x, c.y)));
+}
+__device__ __forceinline__ double re_conj_mul(double2 a, double2 b) {
+    // Re(conj(a) * b)
+    return fma(a.x, b.x, a.y * b.y);
+}
+
+__device__ __forceinline__ uint64_t insert_zeros(uint64_t g, const uint8_t *pos, int npos) {
+    for (int b = 0; b < npos; ++b) {
+        const uint32_t p = pos[b];
+        const uint64_t low = g & ((uint64_t(1) << p) - 1);
+        g = ((g >> p) << (p + 1)) | low;
+    }
+    return g;
+}
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ double block_sum(double v, double *smem) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    double r = 0.0;
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < int(blockDim.x >> 5); ++w) r += smem[w];
+    }
+    return r;  // valid in thread 0
+}
+
+// ---------------------------------------------------------------- in-place gate kernels
+
+__global__ void __launch_bounds__(kThreads) k_gate_1q(double2 *__restrict__ a, uint64_t total,
+                                                      uint32_t n, uint32_t glog,
+                                                      const __grid_constant__ DevGate g) {
+    const uint64_t gmask = (uint64_t(1) << glog) - 1;
+    const uint64_t tb = uint64_t(1) << g.t[0];
+    const double2 m0 = g.m[0], m1 = g.m[1], m2 = g.m[2], m3 = g.m[3];
+    for (uint64_t gid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; gid < total;
+         gid += uint64_t(gridDim.x) * blockDim.x) {
+        double2 *r = a + ((gid >> glog) << n);
+        const uint64_t i0 = insert_zeros(gid & gmask, g.positions, g.npos) | g.cmask;
+        const uint64_t i1 = i0 | tb;
+        const double2 x0 = r[i0], x1 = r[i1];
+        r[i0] = cfma(m0, x0, cmul(m1, x1));
+        r[i1] = cfma(m2, x0, cmul(m3, x1));
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) k_gate_2q(double2 *__restrict__ a, uint64_t total,
+                                                      uint32_t n, uint32_t glog,
+                                                      const __grid_constant__ DevGate g) {
+    const uint64_t gmask = (uint64_t(1) << glog) - 1;
+    const uint64_t b0 = uint64_t(1) << g.t[0], b1 = uint64_t(1) << g.t[1];
+    for (uint64_t gid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; gid < total;
+         gid += uint64_t(gridDim.x) * blockDim.x) {
+        double2 *r = a + ((gid >> glog) << n);
+        const uint64_t i0 = insert_zeros(gid & gmask, g.positions, g.npos) | g.cmask;
+        const uint64_t idx[4] = {i0, i0 | b0, i0 | b1, i0 | b0 | b1};
+        double2 x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = r[idx[j]];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            double2 acc = cmul(g.m[i * 4 + 0], x[0]);
+            acc = cfma(g.m[i * 4 + 1], x[1], acc);
+            acc = cfma(g.m[i * 4 + 2], x[2], acc);
+            acc = cfma(g.m[i * 4 + 3], x[3], acc);
+            r[idx[i]] = acc;
+        }
+    }
+}
+
+// Diagonal gates: one amplitude per item; the enumeration covers only the controlled
+// subspace (and only target=1 when the |0> phase is 1).
+__global__ void __launch_bounds__(kThreads) k_gate_diag(double2 *__restrict__ a, uint64_t total,
+                                                        uint32_t n, uint32_t glog,
+                                                        const __grid_constant__ DevGate g) {
+    const uint64_t gmask = (uint64_t(1) << glog) - 1;
+    for (uint64_t gid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; gid < total;
+         gid += uint64_t(gridDim.x) * blockDim.x) {
+        double2 *r = a + ((gid >> glog) << n);
+        const uint64_t i = insert_zeros(gid & gmask, g.positions, g.npos) | g.cmask;
+        uint32_t b = uint32_t((i >> g.t[0]) & 1);
+        if (g.kind == KIND_DIAG2) b |= uint32_t((i >> g.t[1]) & 1) << 1;
+        r[i] = cmul(g.m[b], r[i]);
+    }
+}
+
+// Generic dense k-qubit gate (custom unitaries of arity > 2): one block per group at a time,
+// the group staged in shared memory, one output row per thread.
+__global__ void __launch_bounds__(kThreads) k_gate_dense(double2 *__restrict__ a, uint64_t groups,
+                                                         uint32_t n, uint32_t glog,
+                                                         const __grid_constant__ DevGate g) {
+    extern __shared__ double2 s_in[];
+    const uint32_t k = uint32_t(g.nt);
+    const uint32_t dim = 1u << k;
+    const uint64_t gmask = (uint64_t(1) << glog) - 1;
+    for (uint64_t gid = blockIdx.x; gid < groups; gid += gridDim.x) {
+        double2 *r = a + ((gid >> glog) << n);
+        const uint64_t base = insert_zeros(gid & gmask, g.positions, g.npos);
+        for (uint32_t j = threadIdx.x; j < dim; j += blockDim.x) {
+            uint64_t off = 0;
+            for (uint32_t b = 0; b < k; ++b)
+                if ((j >> b) & 1) off |= uint64_t(1) << g.dense_targets[b];
+            s_in[j] = r[base | off];
+        }
+        __syncthreads();
+        for (uint32_t row = threadIdx.x; row < dim; row += blockDim.x) {
+            double2 acc = make_double2(0.0, 0.0);
+            const double2 *mr = g.dense + size_t(row) * dim;
+            for (uint32_t c = 0; c < dim; ++c) acc = cfma(__ldg(&mr[c]), s_in[c], acc);
+            uint64_t off = 0;
+            for (uint32_t b = 0; b < k; ++b)
+                if ((row >> b) & 1) off |= uint64_t(1) << g.dense_targets[b];
+            r[base | off] = acc;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------- out-of-place (derivatives)
+
+// out <- M in where M acts on the targets when every control bit is set; elsewhere out is
+// in (gate) or zero (derivative of a controlled gate). Groups enumerate targets only.
+__global__ void __launch_bounds__(kThreads) k_gate_out(const double2 *__restrict__ in,
+                                                       double2 *__restrict__ out, uint64_t total,
+                                                       uint32_t n, uint32_t glog,
+                                                       const __grid_constant__ DevGate g) {
+    const uint64_t gmask = (uint64_t(1) << glog) - 1;
+    const bool diag = g.kind == KIND_DIAG1 || g.kind == KIND_DIAG2;
+    const int nt = g.nt;
+    uint8_t tpos[2];
+    tpos[0] = uint8_t(nt == 2 ? min(g.t[0], g.t[1]) : g.t[0]);
+    tpos[1] = uint8_t(nt == 2 ? max(g.t[0], g.t[1]) : 0);
+    const uint64_t b0 = uint64_t(1) << g.t[0];
+    const uint64_t b1 = nt == 2 ? uint64_t(1) << g.t[1] : 0;
+    for (uint64_t gid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; gid < total;
+         gid += uint64_t(gridDim.x) * blockDim.x) {
+        const size_t roff = size_t(gid >> glog) << n;
+        const double2 *ri = in + roff;
+        double2 *ro = out + roff;
+        const uint64_t i0 = insert_zeros(gid & gmask, tpos, nt);
+        const uint32_t cnt = 1u << nt;
+        uint64_t idx[4] = {i0, i0 | b0, i0 | b1, i0 | b0 | b1};
+        double2 x[4];
+        for (uint32_t j = 0; j < cnt; ++j) x[j] = ri[idx[j]];
+        for (uint32_t j = 0; j < cnt; ++j) {
+            const uint64_t i = idx[j];
+            double2 y;
+            if ((i & g.cmask) != g.cmask) {
+                y = g.zero_uncontrolled ? make_double2(0.0, 0.0) : x[j];
+            } else if (diag) {
+                y = cmul(g.m[j], x[j]);
+            } else {
+                y = make_double2(0.0, 0.0);
+                for (uint32_t c = 0; c < cnt; ++c) y = cfma(g.m[j * cnt + c], x[c], y);
+            }
+            ro[i] = y;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- adjoint step
+
+struct AdjArgs {
+    DevGate u;               // U^dagger, dense small form (KIND_1Q / KIND_2Q)
+    int32_t ns;              // number of derivative slots (0..3)
+    double2 d[3][16];        // dU/dp per slot, same targets as u
+};
+
+// One pass over the controlled subspace of psi and lambda:
+//   psi <- U^dag psi;  acc_s += Re sum conj(lambda) (dU_s psi);  lambda <- U^dag lambda.
+// Outside the controlled subspace U is the identity and dU is zero, so nothing is read.
+template <int NT>
+__global__ void __launch_bounds__(kThreads) k_adjoint(double2 *__restrict__ psi,
+                                                      double2 *__restrict__ lam, uint64_t total,
+                                                      uint32_t n, uint32_t glog,
+                                                      const __grid_constant__ AdjArgs A,
+                                                      double *__restrict__ partials) {
+    constexpr int D = 1 << NT;
+    __shared__ double s_red[kThreads / 32];
+    const uint64_t gmask = (uint64_t(1) << glog) - 1;
+    const uint64_t b0 = uint64_t(1) << A.u.t[0];
+    const uint64_t b1 = NT == 2 ? uint64_t(1) << A.u.t[1] : 0;
+    double acc[3] = {0.0, 0.0, 0.0};
+    for (uint64_t gid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; gid < total;
+         gid += uint64_t(gridDim.x) * blockDim.x) {
+        const size_t roff = size_t(gid >> glog) << n;
+        double2 *P = psi + roff;
+        double2 *L = lam + roff;
+        const uint64_t i0 = insert_zeros(gid & gmask, A.u.positions, A.u.npos) | A.u.cmask;
+        uint64_t idx[D];
+        idx[0] = i0;
+        idx[1] = i0 | b0;
+        if constexpr (NT == 2) {
+            idx[2] = i0 | b1;
+            idx[3] = i0 | b0 | b1;
+        }
+        double2 p[D], l[D], q[D];
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+            p[j] = P[idx[j]];
+            l[j] = L[idx[j]];
+        }
+#pragma unroll
+        for (int i = 0; i < D; ++i) {
+            double2 t = make_double2(0.0, 0.0);
+#pragma unroll
+            for (int c = 0; c < D; ++c) t = cfma(A.u.m[i * D + c], p[c], t);
+            q[i] = t;
+        }
+#pragma unroll
+        for (int s = 0; s < 3; ++s) {
+            if (s < A.ns) {
+                double v = 0.0;
+#pragma unroll
+                for (int i = 0; i < D; ++i) {
+                    double2 t = make_double2(0.0, 0.0);
+#pragma unroll
+                    for (int c = 0; c < D; ++c) t = cfma(A.d[s][i * D + c], q[c], t);
+                    v += re_conj_mul(l[i], t);
+                }
+                acc[s] += v;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < D; ++i) {
+            double2 t = make_double2(0.0, 0.0);
+#pragma unroll
+            for (int c = 0; c < D; ++c) t = cfma(A.u.m[i * D + c], l[c], t);
+            P[idx[i]] = q[i];
+            L[idx[i]] = t;
+        }
+    }
+    for (int s = 0; s < A.ns; ++s) {
+        const double r = block_sum(acc[s], s_red);
+        if (threadIdx.x == 0) partials[size_t(s) * gridDim.x + blockIdx.x] = r;
+    }
+}
+
+// ---------------------------------------------------------------- reductions, scaling
+
+// sums[j] = sum over blocks of partials[j * nblocks + b], fixed order (deterministic).
+__global__ void k_reduce_rows(const double *__restrict__ partials, uint32_t nblocks,
+                              double *__restrict__ sums) {
+    __shared__ double s_red[kThreads / 32];
+    const double *p = partials + size_t(blockIdx.x) * nblocks;
+    double v = 0.0;
+    for (uint32_t b = threadIdx.x; b < nblocks; b += blockDim.x) v += p[b];
+    const double r = block_sum(v, s_red);
+    if (threadIdx.x == 0) sums[blockIdx.x] = r;
+}
+
+__global__ void k_scale_rows(double2 *__restrict__ a, uint64_t total, uint32_t n,
+                             const double *__restrict__ scale) {
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const double s = scale[i >> n];
+        double2 v = a[i];
+        a[i] = make_double2(v.x * s, v.y * s);
+    }
+}
+
+__global__ void k_basis_state(double2 *__restrict__ a, uint64_t total, uint32_t n,
+                              uint64_t index) {
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const uint64_t local = i & ((uint64_t(1) << n) - 1);
+        a[i] = make_double2(local == index ? 1.0 : 0.0, 0.0);
+    }
+}
+
+// Row norms: partials[row * gridDim.x + block] = sum |a|^2 over the block's slice of the row.
+__global__ void __launch_bounds__(kThreads) k_norms(const double2 *__restrict__ a, uint64_t dim,
+                                                    double *__restrict__ partials) {
+    __shared__ double s_red[kThreads / 32];
+    const double2 *r = a + size_t(blockIdx.y) * dim;
+    double v = 0.0;
+    for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < dim;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const double2 x = r[i];
+        v = fma(x.x, x.x, fma(x.y, x.y, v));
+    }
+    const double t = block_sum(v, s_red);
+    if (threadIdx.x == 0) partials[size_t(blockIdx.y) * gridDim.x + blockIdx.x] = t;
+}
+
+// ---------------------------------------------------------------- Pauli observable
+
+struct PauliArgs {
+    const double2 *w;      // per term: coefficient * i^(y mod 4)
+    const uint64_t *z;     // per term: phase mask
+    const uint64_t *flip;  // per group: flip mask
+    const uint32_t *first; // per group: first term
+    const uint32_t *count; // per group: number of terms
+    uint32_t ngroups;
+};
+
+// out[t] = sum_groups sum_terms w_k (-1)^popc((t^f) & z_k) psi[t^f]   (= (H psi)[t])
+// partials[row, block] = sum_t Re(conj(psi[t]) out[t]).
+__global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ psi,
+                                                    double2 *__restrict__ out, uint64_t dim,
+                                                    const __grid_constant__ PauliArgs P,
+                                                    double *__restrict__ partials) {
+    __shared__ double s_red[kThreads / 32];
+    const size_t roff = size_t(blockIdx.y) * dim;
+    const double2 *r = psi + roff;
+    double ev = 0.0;
+    for (uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < dim;
+         t += uint64_t(gridDim.x) * blockDim.x) {
+        const double2 pt = r[t];
+        double2 acc = make_double2(0.0, 0.0);
+        for (uint32_t gi = 0; gi < P.ngroups; ++gi) {
+            const uint64_t f = __ldg(&P.flip[gi]);
+            const uint64_t s = t ^ f;
+            const uint32_t k0 = __ldg(&P.first[gi]), k1 = k0 + __ldg(&P.count[gi]);
+            double2 w = make_double2(0.0, 0.0);
+            for (uint32_t k = k0; k < k1; ++k) {
+                const double2 wk = __ldg(&P.w[k]);
+                const bool neg = __popcll(s & __ldg(&P.z[k])) & 1;
+                w.x += neg ? -wk.x : wk.x;
+                w.y += neg ? -wk.y : wk.y;
+            }
+            const double2 ps = f ? r[s] : pt;
+            acc = cfma(w, ps, acc);
+        }
+        if (out) out[roff + t] = acc;
+        ev += re_conj_mul(pt, acc);
+    }
+    const double tsum = block_sum(ev, s_red);
+    if (threadIdx.x == 0) partials[size_t(blockIdx.y) * gridDim.x + blockIdx.x] = tsum;
+}
+
+// ---------------------------------------------------------------- launch helpers
+
+int g_num_sms = 0;
+
+int num_sms() {
+    if (g_num_sms == 0) {
+        int dev = 0;
+        check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+        check_cuda(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev),
+                   "cudaDeviceGetAttribute");
+    }
+    return g_num_sms;
+}
+
+// Blocks for a grid-stride loop over `items`: at most 8 resident 256-thread blocks per SM.
+unsigned grid_for(uint64_t items) {
+    const uint64_t need = (items + kThreads - 1) / kThreads;
+    const uint64_t cap = uint64_t(num_sms()) * 8;
+    return unsigned(need < 1 ? 1 : (need < cap ? need : cap));
+}
+
+uint32_t ilog2(uint64_t x) {
+    uint32_t r = 0;
+    while ((uint64_t(1) << r) < x) ++r;
+    return r;
+}
+
+}  // namespace
+
+void launch_gate(double2 *amps, size_t batch, uint32_t n, const DevGate &g, cudaStream_t s) {
+    if (g.kind == KIND_NONE) return;
+    if (uint32_t(g.npos) > n) fail("internal: gate wider than the state");
+    const uint32_t glog = n - uint32_t(g.npos);
+    const uint64_t total = uint64_t(batch) << glog;
+    switch (g.kind) {
+    case KIND_1Q: k_gate_1q<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, glog, g); break;
+    case KIND_2Q: k_gate_2q<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, glog, g); break;
+    case KIND_DIAG1:
+    case KIND_DIAG2:
+        k_gate_diag<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, glog, g);
+        break;
+    case KIND_DENSE: {
+        const size_t smem = sizeof(double2) << g.nt;
+        const unsigned blocks = unsigned(total < uint64_t(num_sms()) * 8 ? total : uint64_t(num_sms()) * 8);
+        if (smem > 48 * 1024)
+            check_cuda(cudaFuncSetAttribute(k_gate_dense, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            int(smem)), "cudaFuncSetAttribute");
+        k_gate_dense<<<blocks, kThreads, smem, s>>>(amps, total, n, glog, g);
+        break;
+    }
+    default: fail("internal: bad gate kind");
+    }
+    check_cuda(cudaGetLastError(), "gate kernel launch");
+}
+
+void launch_gate_out(const double2 *in, double2 *out, size_t batch, uint32_t n,
+                     const DevGate &g, cudaStream_t s) {
+    if (g.kind == KIND_DENSE || g.kind == KIND_NONE) fail("internal: unsupported out-of-place gate");
+    if (uint32_t(g.nt) > n) fail("internal: gate wider than the state");
+    const uint32_t glog = n - uint32_t(g.nt);
+    const uint64_t total = uint64_t(batch) << glog;
+    k_gate_out<<<grid_for(total), kThreads, 0, s>>>(in, out, total, n, glog, g);
+    check_cuda(cudaGetLastError(), "derivative kernel launch");
+}
+
+// Returns the number of blocks; partials receives [slot][block].
+unsigned launch_adjoint_raw(double2 *psi, double2 *lam, size_t batch, uint32_t n,
+                            const DevGate &uadj, const double2 (*d)[16], int ns,
+                            double *partials, cudaStream_t s) {
+    AdjArgs A;
+    std::memset(&A, 0, sizeof(A));
+    A.u = uadj;
+    A.ns = ns;
+    const int dim = uadj.nt == 2 ? 16 : 4;
+    for (int j = 0; j < ns; ++j)
+        for (int i = 0; i < dim; ++i) A.d[j][i] = d[j][i];
+    const uint32_t glog = n - uint32_t(uadj.npos);
+    const uint64_t total = uint64_t(batch) << glog;
+    const unsigned blocks = grid_for(total);
+    if (uadj.kind == KIND_1Q)
+        k_adjoint<1><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials);
+    else if (uadj.kind == KIND_2Q)
+        k_adjoint<2><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials);
+    else
+        fail("internal: adjoint step needs a dense small form");
+    check_cuda(cudaGetLastError(), "adjoint kernel launch");
+    return blocks;
+}
+
+unsigned adjoint_max_blocks() { return unsigned(num_sms()) * 8; }
+
+void launch_reduce_rows(const double *partials, uint32_t rows, uint32_t nblocks, double *sums,
+                        cudaStream_t s) {
+    if (rows == 0) return;
+    k_reduce_rows<<<rows, kThreads, 0, s>>>(partials, nblocks, sums);
+    check_cuda(cudaGetLastError(), "reduce kernel launch");
+}
+
+void launch_scale(double2 *amps, size_t batch, uint32_t n, const double *row_scale_dev,
+                  cudaStream_t s) {
+    const uint64_t total = uint64_t(batch) << n;
+    k_scale_rows<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, row_scale_dev);
+    check_cuda(cudaGetLastError(), "scale kernel launch");
+}
+
+void launch_basis_state(double2 *amps, size_t batch, uint32_t n, uint64_t index, cudaStream_t s) {
+    const uint64_t total = uint64_t(batch) << n;
+    k_basis_state<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, index);
+    check_cuda(cudaGetLastError(), "basis-state kernel launch");
+}
+
+// Per-row partial sums: grid (bx, batch). Returns bx.
+unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *partials,
+                      cudaStream_t s) {
+    const uint64_t dim = uint64_t(1) << n;
+    unsigned bx = grid_for(dim);
+    const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);
+    if (bx > cap) bx = cap < 1 ? 1 : cap;
+    k_norms<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(amps, dim, partials);
+    check_cuda(cudaGetLastError(), "norm kernel launch");
+    return bx;
+}
+
+unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
+                      const double2 *w, const uint64_t *z, const uint64_t *flip,
+                      const uint32_t *first, const uint32_t *count, uint32_t ngroups,
+                      double *partials, cudaStream_t s) {
+    PauliArgs P{w, z, flip, first, count, ngroups};
+    const uint64_t dim = uint64_t(1) << n;
+    unsigned bx = grid_for(dim);
+    const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);
+    if (bx > cap) bx = cap < 1 ? 1 : cap;
+    k_pauli<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(psi, out, dim, P, partials);
+    check_cuda(cudaGetLastError(), "observable kernel launch");
+    return bx;
+}
+
+}  // namespace arcqml

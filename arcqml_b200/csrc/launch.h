@@ -1,0 +1,32 @@
+// launch.h — host entry points of the kernels in kernels.cu.
+#pragma once
+
+#include "rt_internal.h"
+
+namespace arcqml {
+
+// Adjoint step over psi and lambda for one reversed gate with `ns` required slots.
+// uadj must be a dense small form (KIND_1Q / KIND_2Q); d[s] holds dU/dp_s on the same targets.
+// Writes partials[s * blocks + b]; returns the block count (<= adjoint_max_blocks()).
+unsigned launch_adjoint_raw(double2 *psi, double2 *lam, size_t batch, uint32_t n,
+                            const DevGate &uadj, const double2 (*d)[16], int ns,
+                            double *partials, cudaStream_t s);
+unsigned adjoint_max_blocks();
+// sums[r] = sum_b partials[r * nblocks + b] in a fixed order.
+void launch_reduce_rows(const double *partials, uint32_t rows, uint32_t nblocks, double *sums,
+                        cudaStream_t s);
+void launch_basis_state(double2 *amps, size_t batch, uint32_t n, uint64_t index, cudaStream_t s);
+unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *partials,
+                      cudaStream_t s);
+unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
+                      const double2 *w, const uint64_t *z, const uint64_t *flip,
+                      const uint32_t *first, const uint32_t *count, uint32_t ngroups,
+                      double *partials, cudaStream_t s);
+
+Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,
+                            const uint64_t *phase, size_t num_terms);
+const std::string &last_error();
+void check_bindings(const Plan &plan, size_t req_len, size_t grads_len);
+void validate_plan_for_state(const Plan &plan, uint32_t n);
+
+}  // namespace arcqml

@@ -1,0 +1,447 @@
+"""ctypes binding of the sm_100a runtime's C ABI.
+
+The v1 half mirrors ArcQML's safe FFI facade ``arcqml-runtime-sys``
+(``crates/arcqml-runtime-sys/src/lib.rs:123-336``): the same function names, argument meaning and
+error behaviour (a non-zero status becomes ``RuntimeError`` carrying the runtime's thread-local
+message, read as in ``last_error`` at ``lib.rs:330-336``). The v2 half drives device-resident
+states held in torch CUDA tensors (``complex128``, ``[batch, 2^n]``).
+
+There is no CPU fallback: importing this module loads ``libarcqml_runtime_private.so`` and fails
+loudly if it is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Optional, Sequence
+
+import numpy as np
+
+from .circuit import PlanOp
+
+ABI_VERSION = 1
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libarcqml_runtime_private.so")
+
+
+class RuntimeError(Exception):  # noqa: A001 - mirrors arcqml_runtime_sys::RuntimeError
+    """A failed runtime call; ``str(e)`` is the runtime's message."""
+
+    def message(self) -> str:
+        return str(self)
+
+
+class C128(C.Structure):
+    _fields_ = [("re", C.c_double), ("im", C.c_double)]
+
+
+class GateDescriptor(C.Structure):
+    _fields_ = [
+        ("abi_version", C.c_uint32),
+        ("opcode", C.c_uint32),
+        ("arity", C.c_size_t),
+        ("parameters", C.c_double * 3),
+        ("matrix", C.c_void_p),
+        ("matrix_len", C.c_size_t),
+        ("name", C.c_void_p),
+        ("name_len", C.c_size_t),
+    ]
+
+
+class DerivativeMatrixHandle(C.Structure):
+    _fields_ = [("data", C.POINTER(C128)), ("len", C.c_size_t), ("capacity", C.c_size_t)]
+
+
+class ParameterBindingDescriptor(C.Structure):
+    _fields_ = [("parameter_slot", C.c_size_t), ("parent_index", C.c_size_t)]
+
+
+class OperationDescriptor(C.Structure):
+    _fields_ = [
+        ("gate", GateDescriptor),
+        ("qubits", C.POINTER(C.c_size_t)),
+        ("qubits_len", C.c_size_t),
+        ("parameters", C.POINTER(ParameterBindingDescriptor)),
+        ("parameters_len", C.c_size_t),
+    ]
+
+
+class CircuitPlanHandle(C.Structure):
+    _fields_ = [("opaque", C.c_void_p)]
+
+
+class ObservableHandle(C.Structure):
+    _fields_ = [("opaque", C.c_void_p)]
+
+
+V1_SYMBOLS = (
+    "arcqml_rt_abi_version", "arcqml_rt_v1_apply_gate", "arcqml_rt_v1_apply_adjoint_gate",
+    "arcqml_rt_v1_parameter_derivative_into", "arcqml_rt_v1_derivative_matrix_create",
+    "arcqml_rt_v1_derivative_matrix_apply", "arcqml_rt_v1_derivative_matrix_destroy",
+    "arcqml_rt_v1_circuit_plan_create", "arcqml_rt_v1_circuit_plan_create_empty",
+    "arcqml_rt_v1_circuit_plan_push", "arcqml_rt_v1_circuit_plan_apply",
+    "arcqml_rt_v1_adjoint_backward", "arcqml_rt_v1_circuit_plan_destroy", "arcqml_rt_last_error",
+)
+
+_lib = None
+
+
+def load():
+    """Loads the runtime library (once). Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m arcqml_b200.build` "
+            "(the statevector path has no CPU fallback)")
+    L = C.CDLL(LIB_PATH)
+    P, S, I32, D = C.c_void_p, C.c_size_t, C.c_int32, C.c_double
+    sig = {
+        "arcqml_rt_abi_version": (C.c_uint32, []),
+        "arcqml_rt_v1_apply_gate": (I32, [P, S, S, P, P, S]),
+        "arcqml_rt_v1_apply_adjoint_gate": (I32, [P, S, S, P, P, S]),
+        "arcqml_rt_v1_parameter_derivative_into": (I32, [P, S, P, S, P, P, S, S]),
+        "arcqml_rt_v1_derivative_matrix_create": (I32, [P, S, P]),
+        "arcqml_rt_v1_derivative_matrix_apply": (I32, [P, S, P, P, S]),
+        "arcqml_rt_v1_derivative_matrix_destroy": (None, [P]),
+        "arcqml_rt_v1_circuit_plan_create": (I32, [P, S, P]),
+        "arcqml_rt_v1_circuit_plan_create_empty": (I32, [S, P]),
+        "arcqml_rt_v1_circuit_plan_push": (I32, [P, P]),
+        "arcqml_rt_v1_circuit_plan_apply": (I32, [P, P, S, S]),
+        "arcqml_rt_v1_adjoint_backward": (I32, [P, P, P, S, P, S, D, P, S, P, S]),
+        "arcqml_rt_v1_circuit_plan_destroy": (None, [P]),
+        "arcqml_rt_last_error": (S, [P, S]),
+        "arcqml_rt_v2_observable_create": (I32, [S, P, P, P, S, P]),
+        "arcqml_rt_v2_observable_destroy": (None, [P]),
+        "arcqml_rt_v2_plan_apply": (I32, [P, P, S, S, P]),
+        "arcqml_rt_v2_apply_gate": (I32, [P, S, S, P, P, S, I32, P]),
+        "arcqml_rt_v2_parameter_derivative": (I32, [P, P, S, S, P, P, S, S, P]),
+        "arcqml_rt_v2_expectation": (I32, [P, P, S, S, P, P]),
+        "arcqml_rt_v2_expectation_and_apply": (I32, [P, P, P, S, S, P, P]),
+        "arcqml_rt_v2_adjoint_backward": (I32, [P, P, P, S, S, P, P, S, P, S, P]),
+        "arcqml_rt_v2_norms": (I32, [P, S, S, P, P]),
+        "arcqml_rt_v2_set_basis_state": (I32, [P, S, S, C.c_uint64, P]),
+        "arcqml_rt_v2_plan_set_parameters": (I32, [P, P, S]),
+        "arcqml_rt_v2_plan_len": (S, [P]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    L = load()
+    n = L.arcqml_rt_last_error(None, 0)
+    buf = (C.c_uint8 * (n + 1))()
+    L.arcqml_rt_last_error(buf, n + 1)
+    return bytes(buf[:n]).decode("utf-8", errors="replace")
+
+
+def _status(code: int) -> None:
+    if code != 0:
+        raise RuntimeError(last_error())
+
+
+def ensure_compatible() -> None:
+    actual = load().arcqml_rt_abi_version()
+    if actual != ABI_VERSION:
+        raise RuntimeError(f"ArcQML runtime ABI mismatch: expected {ABI_VERSION}, got {actual}")
+
+
+# ------------------------------------------------------------------ descriptors
+
+
+class _Keep:
+    """Owns the ctypes buffers a descriptor points into."""
+
+    def __init__(self):
+        self.items = []
+
+    def add(self, x):
+        self.items.append(x)
+        return x
+
+
+def gate_descriptor(opcode: int, arity: int, params=(0.0, 0.0, 0.0), matrix=None,
+                    name: str = "", keep: Optional[_Keep] = None,
+                    abi_version: int = ABI_VERSION) -> GateDescriptor:
+    keep = keep if keep is not None else _Keep()
+    g = GateDescriptor()
+    g.abi_version = abi_version
+    g.opcode = opcode
+    g.arity = arity
+    p = list(params) + [0.0] * (3 - len(params))
+    for i in range(3):
+        g.parameters[i] = float(p[i])
+    if matrix is not None:
+        m = keep.add(np.ascontiguousarray(np.asarray(matrix, dtype=np.complex128).ravel()))
+        g.matrix = m.ctypes.data
+        g.matrix_len = m.size
+    if name:
+        nb = keep.add(C.create_string_buffer(name.encode()))
+        g.name = C.addressof(nb)
+        g.name_len = len(name.encode())
+    return g
+
+
+def _op_descriptor(op: PlanOp, keep: _Keep) -> OperationDescriptor:
+    d = OperationDescriptor()
+    d.gate = gate_descriptor(op.opcode, len(op.qubits), op.params, op.matrix, op.name, keep)
+    q = keep.add((C.c_size_t * max(1, len(op.qubits)))(*op.qubits))
+    d.qubits = C.cast(q, C.POINTER(C.c_size_t))
+    d.qubits_len = len(op.qubits)
+    b = keep.add((ParameterBindingDescriptor * 3)())
+    for i, (slot, parent) in enumerate(op.bindings):
+        b[i].parameter_slot = slot
+        b[i].parent_index = parent
+    d.parameters = C.cast(b, C.POINTER(ParameterBindingDescriptor))
+    d.parameters_len = len(op.bindings)
+    return d
+
+
+def _state_ptr(a: np.ndarray):
+    if a.dtype != np.complex128 or not a.flags.c_contiguous:
+        raise TypeError("amplitudes must be a C-contiguous complex128 array")
+    return a.ctypes.data
+
+
+def _qubits(qubits: Sequence[int]):
+    return (C.c_size_t * max(1, len(qubits)))(*[int(q) for q in qubits])
+
+
+# ------------------------------------------------------------------ v1 (host buffers)
+
+
+def apply_gate(amplitudes: np.ndarray, num_qubits: int, gate: GateDescriptor,
+               qubits: Sequence[int]) -> None:
+    """arcqml_runtime_sys::apply_gate (lib.rs:137-153): in place."""
+    _status(load().arcqml_rt_v1_apply_gate(_state_ptr(amplitudes), amplitudes.size, num_qubits,
+                                          C.byref(gate), _qubits(qubits), len(qubits)))
+
+
+def apply_adjoint_gate(amplitudes: np.ndarray, num_qubits: int, gate: GateDescriptor,
+                       qubits: Sequence[int]) -> None:
+    """arcqml_runtime_sys::apply_adjoint_gate (lib.rs:155-171): in place."""
+    _status(load().arcqml_rt_v1_apply_adjoint_gate(_state_ptr(amplitudes), amplitudes.size,
+                                                  num_qubits, C.byref(gate), _qubits(qubits),
+                                                  len(qubits)))
+
+
+def parameter_derivative_into(inp: np.ndarray, out: np.ndarray, gate: GateDescriptor,
+                              qubits: Sequence[int], parameter_slot: int) -> None:
+    """arcqml_runtime_sys::parameter_derivative_into (lib.rs:173-192)."""
+    _status(load().arcqml_rt_v1_parameter_derivative_into(
+        _state_ptr(inp), inp.size, _state_ptr(out), out.size, C.byref(gate), _qubits(qubits),
+        len(qubits), parameter_slot))
+
+
+class DerivativeMatrix:
+    """arcqml_runtime_sys::DerivativeMatrix (lib.rs:194-232)."""
+
+    def __init__(self, gate: GateDescriptor, parameter_slot: int):
+        self.raw = DerivativeMatrixHandle()
+        _status(load().arcqml_rt_v1_derivative_matrix_create(C.byref(gate), parameter_slot,
+                                                           C.byref(self.raw)))
+
+    @classmethod
+    def create(cls, gate: GateDescriptor, parameter_slot: int) -> "DerivativeMatrix":
+        return cls(gate, parameter_slot)
+
+    def matrix(self) -> np.ndarray:
+        n = self.raw.len
+        dim = int(round(np.sqrt(n)))
+        flat = np.ctypeslib.as_array(C.cast(self.raw.data, C.POINTER(C.c_double)), shape=(2 * n,))
+        return (flat[0::2] + 1j * flat[1::2]).reshape(dim, dim).copy()
+
+    def apply(self, amplitudes: np.ndarray, qubits: Sequence[int]) -> None:
+        _status(load().arcqml_rt_v1_derivative_matrix_apply(
+            _state_ptr(amplitudes), amplitudes.size, C.byref(self.raw), _qubits(qubits),
+            len(qubits)))
+
+    def __del__(self):
+        if _lib is not None and getattr(self, "raw", None) is not None:
+            _lib.arcqml_rt_v1_derivative_matrix_destroy(C.byref(self.raw))
+
+
+class CircuitPlan:
+    """arcqml_runtime_sys::CircuitPlan (lib.rs:234-320)."""
+
+    def __init__(self, raw: CircuitPlanHandle):
+        self.raw = raw
+
+    @classmethod
+    def create(cls, operations: Sequence[PlanOp]) -> "CircuitPlan":
+        ensure_compatible()
+        keep = _Keep()
+        arr = (OperationDescriptor * max(1, len(operations)))()
+        for i, op in enumerate(operations):
+            arr[i] = _op_descriptor(op, keep)
+        raw = CircuitPlanHandle()
+        _status(load().arcqml_rt_v1_circuit_plan_create(arr, len(operations), C.byref(raw)))
+        return cls(raw)
+
+    @classmethod
+    def with_capacity(cls, operation_capacity: int) -> "CircuitPlan":
+        ensure_compatible()
+        raw = CircuitPlanHandle()
+        _status(load().arcqml_rt_v1_circuit_plan_create_empty(operation_capacity, C.byref(raw)))
+        return cls(raw)
+
+    @classmethod
+    def compile(cls, ops: Sequence[PlanOp]) -> "CircuitPlan":
+        """RuntimeCircuitPlan::compile: one push per operation, descriptors from temporaries."""
+        plan = cls.with_capacity(len(ops))
+        for op in ops:
+            plan.push(op)
+        return plan
+
+    def push(self, op: PlanOp) -> None:
+        keep = _Keep()
+        d = _op_descriptor(op, keep)
+        _status(load().arcqml_rt_v1_circuit_plan_push(C.byref(self.raw), C.byref(d)))
+        del keep  # the runtime deep-copied everything
+
+    def apply(self, amplitudes: np.ndarray, num_qubits: int) -> None:
+        _status(load().arcqml_rt_v1_circuit_plan_apply(C.byref(self.raw), _state_ptr(amplitudes),
+                                                      amplitudes.size, num_qubits))
+
+    def adjoint_backward(self, forward_state: np.ndarray, adjoint_state: np.ndarray,
+                         derivative_state: np.ndarray, num_qubits: int, upstream: float,
+                         parameter_requires_grad: np.ndarray, gradients: np.ndarray) -> None:
+        if not (forward_state.size == adjoint_state.size == derivative_state.size):
+            raise RuntimeError("adjoint buffers must have identical lengths")
+        req = np.ascontiguousarray(parameter_requires_grad, dtype=np.uint8)
+        if gradients.dtype != np.float64 or not gradients.flags.c_contiguous:
+            raise TypeError("gradients must be a C-contiguous float64 array")
+        _status(load().arcqml_rt_v1_adjoint_backward(
+            C.byref(self.raw), _state_ptr(forward_state), _state_ptr(adjoint_state),
+            forward_state.size, _state_ptr(derivative_state), num_qubits, float(upstream),
+            req.ctypes.data, req.size, gradients.ctypes.data, gradients.size))
+
+    # -- v2 extensions on the same plan -------------------------------------------
+    def set_parameters(self, parent_values: np.ndarray) -> None:
+        v = np.ascontiguousarray(parent_values, dtype=np.float64)
+        _status(load().arcqml_rt_v2_plan_set_parameters(C.byref(self.raw), v.ctypes.data, v.size))
+
+    def __len__(self) -> int:
+        return load().arcqml_rt_v2_plan_len(C.byref(self.raw))
+
+    def __del__(self):
+        if _lib is not None and getattr(self, "raw", None) is not None:
+            _lib.arcqml_rt_v1_circuit_plan_destroy(C.byref(self.raw))
+
+
+# ------------------------------------------------------------------ v2 (device states)
+
+
+def _stream_ptr(stream) -> Optional[int]:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return int(stream)
+
+
+def _dev_ptr(t) -> int:
+    import torch
+    if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.complex128
+            and t.is_contiguous()):
+        raise TypeError("device amplitudes must be a contiguous complex128 CUDA tensor")
+    return t.data_ptr()
+
+
+def _rows(t, num_qubits: int) -> int:
+    dim = 1 << num_qubits
+    if t.numel() % dim != 0 or t.numel() == 0:
+        raise RuntimeError(f"device state of {t.numel()} amplitudes is not [batch, {dim}]")
+    return t.numel() // dim
+
+
+class Observable:
+    """Compiled Pauli observable on the runtime (arcqml_rt_v2_observable_*)."""
+
+    def __init__(self, num_qubits: int, coefficients, flip_masks, phase_masks):
+        c = np.ascontiguousarray(coefficients, dtype=np.float64)
+        f = np.ascontiguousarray(flip_masks, dtype=np.uint64)
+        p = np.ascontiguousarray(phase_masks, dtype=np.uint64)
+        if not (c.size == f.size == p.size):
+            raise ValueError("term arrays differ in length")
+        self.num_qubits = num_qubits
+        self.raw = ObservableHandle()
+        _status(load().arcqml_rt_v2_observable_create(num_qubits, c.ctypes.data, f.ctypes.data,
+                                                      p.ctypes.data, c.size, C.byref(self.raw)))
+
+    @classmethod
+    def from_sparse_pauli_op(cls, op) -> "Observable":
+        c, f, p = op.masks()
+        return cls(op.num_qubits, c, f, p)
+
+    def expectation(self, state, num_qubits: int, stream=None) -> np.ndarray:
+        b = _rows(state, num_qubits)
+        out = np.zeros(b, dtype=np.float64)
+        _status(load().arcqml_rt_v2_expectation(C.byref(self.raw), _dev_ptr(state), b, num_qubits,
+                                                out.ctypes.data, _stream_ptr(stream)))
+        return out
+
+    def expectation_and_apply(self, state, out_state, num_qubits: int, stream=None) -> np.ndarray:
+        b = _rows(state, num_qubits)
+        vals = np.zeros(b, dtype=np.float64)
+        _status(load().arcqml_rt_v2_expectation_and_apply(
+            C.byref(self.raw), _dev_ptr(state), _dev_ptr(out_state), b, num_qubits,
+            vals.ctypes.data, _stream_ptr(stream)))
+        return vals
+
+    def __del__(self):
+        if _lib is not None and getattr(self, "raw", None) is not None:
+            _lib.arcqml_rt_v2_observable_destroy(C.byref(self.raw))
+
+
+def plan_apply_device(plan: CircuitPlan, state, num_qubits: int, stream=None) -> None:
+    b = _rows(state, num_qubits)
+    _status(load().arcqml_rt_v2_plan_apply(C.byref(plan.raw), _dev_ptr(state), b, num_qubits,
+                                           _stream_ptr(stream)))
+
+
+def apply_gate_device(state, num_qubits: int, gate: GateDescriptor, qubits, adjoint=False,
+                      stream=None) -> None:
+    b = _rows(state, num_qubits)
+    _status(load().arcqml_rt_v2_apply_gate(_dev_ptr(state), b, num_qubits, C.byref(gate),
+                                           _qubits(qubits), len(qubits), int(adjoint),
+                                           _stream_ptr(stream)))
+
+
+def parameter_derivative_device(inp, out, num_qubits: int, gate: GateDescriptor, qubits, slot,
+                                stream=None) -> None:
+    b = _rows(inp, num_qubits)
+    _status(load().arcqml_rt_v2_parameter_derivative(
+        _dev_ptr(inp), _dev_ptr(out), b, num_qubits, C.byref(gate), _qubits(qubits), len(qubits),
+        slot, _stream_ptr(stream)))
+
+
+def adjoint_backward_device(plan: CircuitPlan, psi, lam, num_qubits: int, upstream,
+                            requires_grad, num_gradients: int, stream=None) -> np.ndarray:
+    b = _rows(psi, num_qubits)
+    up = np.ascontiguousarray(np.broadcast_to(np.asarray(upstream, dtype=np.float64), (b,)))
+    req = np.ascontiguousarray(requires_grad, dtype=np.uint8)
+    grads = np.zeros(num_gradients, dtype=np.float64)
+    _status(load().arcqml_rt_v2_adjoint_backward(
+        C.byref(plan.raw), _dev_ptr(psi), _dev_ptr(lam), b, num_qubits, up.ctypes.data,
+        req.ctypes.data, req.size, grads.ctypes.data, grads.size, _stream_ptr(stream)))
+    return grads
+
+
+def norms_device(state, num_qubits: int, stream=None) -> np.ndarray:
+    b = _rows(state, num_qubits)
+    out = np.zeros(b, dtype=np.float64)
+    _status(load().arcqml_rt_v2_norms(_dev_ptr(state), b, num_qubits, out.ctypes.data,
+                                      _stream_ptr(stream)))
+    return out
+
+
+def set_basis_state_device(state, num_qubits: int, index: int = 0, stream=None) -> None:
+    b = _rows(state, num_qubits)
+    _status(load().arcqml_rt_v2_set_basis_state(_dev_ptr(state), b, num_qubits, index,
+                                                _stream_ptr(stream)))

@@ -1,0 +1,225 @@
+"""Device-resident statevector simulators over the sm_100a runtime.
+
+Mirrors ArcQML's ``StateVectorSimulator`` / ``BatchStateVectorSimulator`` run path
+(``crates/arcqml-sim/src/statevector/execution/adjoint/single.rs:29-163``, ``batch.rs:30-128``,
+``row_major.rs:18-307``): ``run`` compiles the plan with parent offset 1 (the initial state is
+parent 0), applies it, computes ``<H>`` and ``H|psi>`` in one pass, and returns a result whose
+``backward(upstream)`` runs the adjoint reverse sweep. Parameter gradients follow the
+reference's indexing (``gradients[1:]``); the initial-state gradient is ``2 * g * lambda_0``
+(``adjoint/single.rs:138-146``). States live in HBM as torch ``complex128`` CUDA tensors; only
+parameters, upstream factors, values and gradients cross PCIe.
+
+Unlike the reference, ``backward`` consumes the saved psi/lambda buffers in place (a 32-qubit
+state is 64 GiB; cloning them as the reference does would not fit). Pass ``retain=True`` to
+keep the context for a second backward.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+from . import runtime as rt
+from .circuit import Circuit
+from .observable import SparsePauliOp
+
+NORM_TOLERANCE = 1e-10  # docs/ArcQML技术手册.md:206-213
+
+
+class SimError(ValueError):
+    pass
+
+
+def _torch():
+    import torch
+    if not torch.cuda.is_available():
+        raise SimError("the B200 statevector runtime needs a CUDA device")
+    return torch
+
+
+def _new_state(num_qubits: int, batch: Optional[int], device):
+    torch = _torch()
+    shape = (1 << num_qubits,) if batch is None else (batch, 1 << num_qubits)
+    return torch.empty(shape, dtype=torch.complex128, device=device)
+
+
+@dataclass
+class _Context:
+    num_qubits: int
+    batch: Optional[int]
+    psi: object
+    lam: object
+    plan: rt.CircuitPlan
+    circuit: Circuit
+    initial_requires_grad: bool
+
+
+class RunResult:
+    """Output of ``run``: value(s) plus the adjoint context for ``backward``."""
+
+    def __init__(self, values: np.ndarray, ctx: Optional[_Context]):
+        self.values = values
+        self._ctx = ctx
+        self.initial_state_grad = None
+        self.parameter_grads = None
+
+    @property
+    def value(self) -> float:
+        return float(self.values[0])
+
+    @property
+    def requires_grad(self) -> bool:
+        return self._ctx is not None
+
+    def backward(self, upstream=1.0, retain: bool = False, stream=None):
+        """Adjoint reverse sweep with upstream g (scalar, or [batch] for batch runs).
+
+        Returns (parameter_grads, initial_state_grad). Parameter gradients are also
+        accumulated into ``circuit.parameters[i].grad``.
+        """
+        if self._ctx is None:
+            raise SimError("run was executed without gradient recording")
+        c = self._ctx
+        torch = _torch()
+        psi, lam = (c.psi.clone(), c.lam.clone()) if retain else (c.psi, c.lam)
+        req = c.circuit.requires_grad_mask(True, c.initial_requires_grad)
+        grads = rt.adjoint_backward_device(c.plan, psi, lam, c.num_qubits, upstream, req,
+                                           len(req), stream)
+        pgrads = grads[1:].copy()
+        for p, g in zip(c.circuit.parameters, pgrads):
+            if p.requires_grad:
+                g = float(np.float32(g)) if p.dtype == "f32" else float(g)
+                p.grad = g if getattr(p, "grad", None) is None else p.grad + g
+        self.parameter_grads = pgrads
+        self.initial_state_grad = (2.0 * lam) if c.initial_requires_grad else None
+        if not retain:
+            self._ctx = None
+        return pgrads, self.initial_state_grad
+
+
+class StateVectorSimulator:
+    """Single state of ``num_qubits`` qubits, resident on a CUDA device."""
+
+    def __init__(self, num_qubits: int, device=None):
+        if num_qubits < 0 or num_qubits >= 40:
+            raise SimError(f"state dimension overflow for {num_qubits} qubits")
+        self.num_qubits = num_qubits
+        self.device = device if device is not None else _torch().device("cuda", _torch().cuda.current_device())
+        self.state = _new_state(num_qubits, None, self.device)
+        self.initial_requires_grad = False
+        self.reset()
+
+    @classmethod
+    def from_amplitudes(cls, num_qubits: int, amplitudes, requires_grad: bool = False):
+        a = np.ascontiguousarray(amplitudes, dtype=np.complex128)
+        if a.shape != (1 << num_qubits,):
+            raise SimError(f"state must have shape [{1 << num_qubits}], got {list(a.shape)}")
+        norm = float(np.vdot(a, a).real)
+        if abs(norm - 1.0) > NORM_TOLERANCE:
+            raise SimError(f"state is not normalized: squared norm {norm}")
+        sim = cls(num_qubits)
+        sim.state.copy_(_torch().from_numpy(a))
+        sim.initial_requires_grad = requires_grad
+        return sim
+
+    def reset(self) -> None:
+        rt.set_basis_state_device(self.state, self.num_qubits, 0)
+
+    def amplitudes(self) -> np.ndarray:
+        return self.state.cpu().numpy()
+
+    def apply_circuit(self, circuit: Circuit) -> None:
+        self._check(circuit)
+        plan = rt.CircuitPlan.compile(circuit.compile_plan(0))
+        rt.plan_apply_device(plan, self.state, self.num_qubits)
+
+    def expectation(self, observable: SparsePauliOp) -> float:
+        obs = rt.Observable.from_sparse_pauli_op(observable)
+        return float(obs.expectation(self.state, self.num_qubits)[0])
+
+    def norm(self) -> float:
+        return float(rt.norms_device(self.state, self.num_qubits)[0])
+
+    def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True) -> RunResult:
+        self._check(circuit)
+        records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
+        psi = self.state.clone()
+        plan = rt.CircuitPlan.compile(circuit.compile_plan(1 if records else 0))
+        rt.plan_apply_device(plan, psi, self.num_qubits)
+        obs = rt.Observable.from_sparse_pauli_op(observable)
+        if observable.num_qubits != self.num_qubits:
+            raise SimError("observable and state qubit counts differ")
+        if not records:
+            return RunResult(obs.expectation(psi, self.num_qubits), None)
+        lam = _torch().empty_like(psi)
+        vals = obs.expectation_and_apply(psi, lam, self.num_qubits)
+        return RunResult(vals, _Context(self.num_qubits, None, psi, lam, plan, circuit,
+                                        self.initial_requires_grad))
+
+    def _check(self, circuit: Circuit):
+        if circuit.num_qubits != self.num_qubits:
+            raise SimError(f"circuit has {circuit.num_qubits} qubits, simulator has {self.num_qubits}")
+
+
+class BatchStateVectorSimulator:
+    """[batch, 2^n] independent states sharing one circuit and observable."""
+
+    def __init__(self, num_qubits: int, batch_size: int, device=None):
+        if batch_size <= 0:
+            raise SimError("batch size must be non-zero")
+        self.num_qubits = num_qubits
+        self.batch_size = batch_size
+        self.device = device if device is not None else _torch().device("cuda", _torch().cuda.current_device())
+        self.state = _new_state(num_qubits, batch_size, self.device)
+        self.initial_requires_grad = False
+        rt.set_basis_state_device(self.state, num_qubits, 0)
+
+    @classmethod
+    def from_amplitudes(cls, num_qubits: int, amplitudes, requires_grad: bool = False):
+        a = np.ascontiguousarray(amplitudes, dtype=np.complex128)
+        if a.ndim != 2 or a.shape[1] != (1 << num_qubits) or a.shape[0] == 0:
+            raise SimError(f"batch state must have shape [B, {1 << num_qubits}]")
+        norms = np.einsum("ij,ij->i", a.conj(), a).real
+        bad = np.nonzero(np.abs(norms - 1.0) > NORM_TOLERANCE)[0]
+        if bad.size:
+            raise SimError(f"batch row {int(bad[0])} is not normalized")
+        sim = cls(num_qubits, a.shape[0])
+        sim.state.copy_(_torch().from_numpy(a))
+        sim.initial_requires_grad = requires_grad
+        return sim
+
+    @classmethod
+    def from_device_state(cls, num_qubits: int, state, requires_grad: bool = False):
+        sim = cls.__new__(cls)
+        sim.num_qubits = num_qubits
+        sim.batch_size = state.shape[0]
+        sim.device = state.device
+        sim.state = state
+        sim.initial_requires_grad = requires_grad
+        return sim
+
+    def amplitudes(self) -> np.ndarray:
+        return self.state.cpu().numpy()
+
+    def apply_circuit(self, circuit: Circuit) -> None:
+        plan = rt.CircuitPlan.compile(circuit.compile_plan(0))
+        rt.plan_apply_device(plan, self.state, self.num_qubits)
+
+    def expectation(self, observable: SparsePauliOp) -> np.ndarray:
+        return rt.Observable.from_sparse_pauli_op(observable).expectation(self.state, self.num_qubits)
+
+    def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True) -> RunResult:
+        if circuit.num_qubits != self.num_qubits or observable.num_qubits != self.num_qubits:
+            raise SimError("circuit, observable and state qubit counts differ")
+        records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
+        psi = self.state.clone()
+        plan = rt.CircuitPlan.compile(circuit.compile_plan(1 if records else 0))
+        rt.plan_apply_device(plan, psi, self.num_qubits)
+        obs = rt.Observable.from_sparse_pauli_op(observable)
+        if not records:
+            return RunResult(obs.expectation(psi, self.num_qubits), None)
+        lam = _torch().empty_like(psi)
+        vals = obs.expectation_and_apply(psi, lam, self.num_qubits)
+        return RunResult(vals, _Context(self.num_qubits, self.batch_size, psi, lam, plan, circuit,
+                                        self.initial_requires_grad))

@@ -1,0 +1,101 @@
+/*
+ * arcqml_runtime_v2.h — device-resident extension of the ArcQML runtime C ABI (B200 build).
+ *
+ * The v1 entry points (arcqml_runtime.h) take host buffers and copy them to the GPU on every
+ * call, as the reference's callers hand over host `Vec<Complex64>` states. These additive
+ * `arcqml_rt_v2_*` entry points keep states in HBM across calls: amplitude pointers are
+ * DEVICE pointers on the calling thread's current CUDA device, laid out [batch, 2^n]
+ * row-major complex128, and `stream` is a cudaStream_t (NULL selects CUDA's legacy default
+ * stream). Small results (values, gradients, norms) are written to HOST arrays; calls that
+ * return them synchronize the stream before returning.
+ *
+ * Each entry point restates a step of the reference's `run` / backward path on device:
+ *   plan apply           crates/arcqml-runtime-sys/src/lib.rs:82-87 (circuit_plan_apply)
+ *   observable           crates/arcqml-observable/src/compiled_hamiltonian.rs:30-182
+ *   adjoint backward     crates/arcqml-runtime-sys/src/lib.rs:88-100 (adjoint_backward),
+ *                        batch rows as crates/arcqml-sim/src/statevector/execution/adjoint/
+ *                        row_major.rs:108-162 (per-row upstream, gradients summed over rows)
+ * Status and errors follow the v1 convention (0 = success, message via arcqml_rt_last_error).
+ */
+#ifndef ARCQML_RUNTIME_V2_H
+#define ARCQML_RUNTIME_V2_H
+
+#include "arcqml_runtime.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Compiled sparse Pauli observable (CompiledHamiltonian, compiled_hamiltonian.rs:13-26). */
+typedef struct ArcqmlObservableHandle {
+    void *opaque;
+} ArcqmlObservableHandle;
+
+/* Term k is coefficients[k] * i^{popcount(flip & phase) mod 4} * X^{flip} Z^{phase} applied as
+ * P|i> = i^y (-1)^{popcount(i & phase_masks[k])} |i ^ flip_masks[k]> (flip = X|Y bits,
+ * phase = Y|Z bits, compiled_hamiltonian.rs:37-62, :198-210). */
+int32_t arcqml_rt_v2_observable_create(size_t num_qubits, const double *coefficients,
+                                       const uint64_t *flip_masks, const uint64_t *phase_masks,
+                                       size_t num_terms, ArcqmlObservableHandle *output);
+void arcqml_rt_v2_observable_destroy(ArcqmlObservableHandle *observable);
+
+/* amplitudes[b] <- U_m ... U_1 amplitudes[b] for every row b. */
+int32_t arcqml_rt_v2_plan_apply(const CircuitPlanHandle *plan, arcqml_c128 *amplitudes,
+                                size_t batch, size_t num_qubits, void *stream);
+
+/* One gate (adjoint != 0 applies U^dagger) on every row. */
+int32_t arcqml_rt_v2_apply_gate(arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                const GateDescriptor *gate, const size_t *qubits,
+                                size_t qubits_len, int32_t adjoint, void *stream);
+
+/* output[b] <- (dU/dp_slot) input[b] (control-0 block of controlled gates is zero). */
+int32_t arcqml_rt_v2_parameter_derivative(const arcqml_c128 *input, arcqml_c128 *output,
+                                          size_t batch, size_t num_qubits,
+                                          const GateDescriptor *gate, const size_t *qubits,
+                                          size_t qubits_len, size_t parameter_slot,
+                                          void *stream);
+
+/* values[b] <- Re<psi_b|H|psi_b> (host array of batch doubles). */
+int32_t arcqml_rt_v2_expectation(const ArcqmlObservableHandle *observable,
+                                 const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                 double *values, void *stream);
+
+/* output[b] <- H psi_b and values[b] <- Re<psi_b|H psi_b> in one pass. */
+int32_t arcqml_rt_v2_expectation_and_apply(const ArcqmlObservableHandle *observable,
+                                           const arcqml_c128 *amplitudes, arcqml_c128 *output,
+                                           size_t batch, size_t num_qubits, double *values,
+                                           void *stream);
+
+/* Reverse sweep over device states. In: psi = psi_m, lambda = H psi_m (unscaled) per row,
+ * upstream[b] = g_b (host array). Out: psi = psi_0, lambda = g_b lambda_0, and
+ * gradients[parent] += sum_b 2 g_b Re<lambda_k| dU_k/dp |psi_{k-1}> over every bound slot whose
+ * parent has parameter_requires_grad[parent] != 0. No scratch state is needed. */
+int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
+                                      arcqml_c128 *adjoint_state, size_t batch,
+                                      size_t num_qubits, const double *upstream,
+                                      const uint8_t *parameter_requires_grad,
+                                      size_t parameter_requires_grad_len, double *gradients,
+                                      size_t gradients_len, void *stream);
+
+/* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
+int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                           double *norms, void *stream);
+
+/* Every row <- |index>. */
+int32_t arcqml_rt_v2_set_basis_state(arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                     uint64_t index, void *stream);
+
+/* Replaces the bound value of every (slot, parent) binding of the plan with
+ * parent_values[parent]; the plan's structure is unchanged. Lets a training loop update
+ * parameters without rebuilding the plan. */
+int32_t arcqml_rt_v2_plan_set_parameters(CircuitPlanHandle *plan, const double *parent_values,
+                                         size_t parent_values_len);
+
+/* Number of operations in the plan. */
+size_t arcqml_rt_v2_plan_len(const CircuitPlanHandle *plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ARCQML_RUNTIME_V2_H */

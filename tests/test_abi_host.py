@@ -1,0 +1,179 @@
+"""C-ABI checks that need no GPU: exports, struct layouts, validation, host-only entry points."""
+import ctypes as C
+import math
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from arcqml_b200 import circuit as cm
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INCLUDE = os.path.join(ROOT, "include")
+
+
+def declared_symbols():
+    names = set()
+    for f in os.listdir(INCLUDE):
+        if f.endswith(".h"):
+            text = open(os.path.join(INCLUDE, f)).read()
+            names |= set(re.findall(r"\b(arcqml_rt_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol(runtime):
+    out = subprocess.run(["nm", "-D", "--defined-only", runtime.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    missing = [s for s in declared_symbols() if s not in exported]
+    assert not missing, missing
+    # the 14 symbols arcqml-runtime-sys binds (crates/arcqml-runtime-sys/src/lib.rs:28-103)
+    assert set(runtime.V1_SYMBOLS) <= exported
+    assert len(runtime.V1_SYMBOLS) == 14
+
+
+def test_static_archive_holds_the_abi(runtime):
+    archive = runtime.LIB_PATH[:-3] + ".a"
+    out = subprocess.run(["nm", "--defined-only", archive], capture_output=True, text=True,
+                         check=True).stdout
+    for s in runtime.V1_SYMBOLS:
+        assert re.search(rf"\bT {s}\b", out), s
+
+
+LAYOUT_PROBE = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "arcqml_runtime.h"
+#define P(T, F) printf(#T "." #F " %zu\n", offsetof(T, F));
+int main(void) {
+  printf("GateDescriptor %zu\nOperationDescriptor %zu\nParameterBindingDescriptor %zu\n"
+         "DerivativeMatrixHandle %zu\nCircuitPlanHandle %zu\narcqml_c128 %zu\n",
+         sizeof(GateDescriptor), sizeof(OperationDescriptor), sizeof(ParameterBindingDescriptor),
+         sizeof(DerivativeMatrixHandle), sizeof(CircuitPlanHandle), sizeof(arcqml_c128));
+  P(GateDescriptor, opcode) P(GateDescriptor, arity) P(GateDescriptor, parameters)
+  P(GateDescriptor, matrix) P(GateDescriptor, matrix_len) P(GateDescriptor, name)
+  P(GateDescriptor, name_len) P(OperationDescriptor, qubits) P(OperationDescriptor, qubits_len)
+  P(OperationDescriptor, parameters) P(OperationDescriptor, parameters_len)
+  return 0;
+}
+"""
+
+
+def test_header_layouts_match_repr_c(tmp_path, runtime):
+    """repr(C) layouts of crates/arcqml-runtime-abi/src/lib.rs:13-110 on x86_64."""
+    src = tmp_path / "probe.c"
+    src.write_text(LAYOUT_PROBE)
+    exe = tmp_path / "probe"
+    subprocess.run(["/usr/bin/gcc", "-I", INCLUDE, str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True,
+                                                                text=True).stdout.splitlines())
+    got = {k: int(v) for k, v in got.items()}
+    expect = {"GateDescriptor": 72, "OperationDescriptor": 104, "ParameterBindingDescriptor": 16,
+              "DerivativeMatrixHandle": 24, "CircuitPlanHandle": 8, "arcqml_c128": 16,
+              "GateDescriptor.opcode": 4, "GateDescriptor.arity": 8,
+              "GateDescriptor.parameters": 16, "GateDescriptor.matrix": 40,
+              "GateDescriptor.matrix_len": 48, "GateDescriptor.name": 56,
+              "GateDescriptor.name_len": 64, "OperationDescriptor.qubits": 72,
+              "OperationDescriptor.qubits_len": 80, "OperationDescriptor.parameters": 88,
+              "OperationDescriptor.parameters_len": 96}
+    assert got == expect
+    # the ctypes mirror agrees
+    assert C.sizeof(runtime.GateDescriptor) == 72
+    assert C.sizeof(runtime.OperationDescriptor) == 104
+    assert C.sizeof(runtime.DerivativeMatrixHandle) == 24
+
+
+def test_abi_version(runtime):
+    assert runtime.load().arcqml_rt_abi_version() == 1
+    runtime.ensure_compatible()
+
+
+def test_plan_push_validation_messages(runtime):
+    plan = runtime.CircuitPlan.with_capacity(4)
+    with pytest.raises(runtime.RuntimeError, match="has arity 2, descriptor says 1"):
+        plan.push(cm.PlanOp(16, (0,), (0, 0, 0)))
+    with pytest.raises(runtime.RuntimeError, match="expects 2 qubits, got 1"):
+        runtime.apply_gate(np.zeros(4, np.complex128), 2, runtime.gate_descriptor(16, 2), [0])
+    with pytest.raises(runtime.RuntimeError, match="duplicate qubit"):
+        plan.push(cm.PlanOp(16, (1, 1), (0, 0, 0)))
+    with pytest.raises(runtime.RuntimeError, match="does not have parameter slot 1"):
+        plan.push(cm.PlanOp(11, (0,), (0.1, 0, 0), None, ((1, 1),)))
+    with pytest.raises(runtime.RuntimeError, match="unknown gate opcode 39"):
+        plan.push(cm.PlanOp(39, (0,), (0, 0, 0)))
+    with pytest.raises(runtime.RuntimeError, match="expects 16 matrix entries"):
+        plan.push(cm.PlanOp(38, (0, 1), (0, 0, 0), np.eye(2, dtype=np.complex128)))
+    plan.push(cm.PlanOp(11, (0,), (0.1, 0, 0), None, ((0, 1),)))
+    assert len(plan) == 1
+
+
+def test_descriptor_abi_version_rejected(runtime):
+    keep = []
+    g = runtime.gate_descriptor(1, 1, abi_version=2)
+    a = np.array([1, 0], np.complex128)
+    with pytest.raises(runtime.RuntimeError, match="ABI mismatch: expected 1, got 2"):
+        runtime.apply_gate(a, 1, g, [0])
+
+
+def test_state_length_errors_before_any_device_work(runtime):
+    """kernel_tests.rs:25-68: wrong lengths and unrepresentable dimensions are errors."""
+    a = np.array([1], np.complex128)
+    g = runtime.gate_descriptor(1, 1)
+    with pytest.raises(runtime.RuntimeError, match="expected 2, got 1"):
+        runtime.apply_gate(a, 1, g, [0])
+    with pytest.raises(runtime.RuntimeError, match="expected 2, got 1"):
+        runtime.apply_adjoint_gate(a, 1, g, [0])
+    with pytest.raises(runtime.RuntimeError, match="overflow"):
+        runtime.apply_gate(a, 64, g, [0])
+    with pytest.raises(runtime.RuntimeError, match="out of range"):
+        runtime.apply_gate(np.zeros(2, np.complex128), 1, g, [3])
+
+
+def test_last_error_protocol(runtime):
+    L = runtime.load()
+    plan = runtime.CircuitPlan.with_capacity(1)
+    with pytest.raises(runtime.RuntimeError):
+        plan.push(cm.PlanOp(16, (0,), (0, 0, 0)))
+    n = L.arcqml_rt_last_error(None, 0)
+    assert n > 0
+    buf = (C.c_uint8 * 4)()
+    assert L.arcqml_rt_last_error(buf, 4) == n  # truncated copy, full length returned
+
+
+def test_destroy_is_idempotent(runtime):
+    L = runtime.load()
+    h = runtime.CircuitPlanHandle()
+    L.arcqml_rt_v1_circuit_plan_destroy(C.byref(h))
+    L.arcqml_rt_v1_circuit_plan_destroy(None)
+    m = runtime.DerivativeMatrixHandle()
+    L.arcqml_rt_v1_derivative_matrix_destroy(C.byref(m))
+    L.arcqml_rt_v1_derivative_matrix_destroy(None)
+
+
+PARAM_OPS = [(11, 1), (12, 1), (13, 1), (14, 1), (15, 1), (22, 2), (23, 2), (24, 2), (25, 2),
+             (30, 2), (31, 2), (32, 2), (33, 2), (34, 2)]
+
+
+@pytest.mark.parametrize("opcode,arity", PARAM_OPS)
+def test_derivative_matrix_create_matches_oracle(runtime, oracle, opcode, arity):
+    """Host-built dU/dp (DerivativeMatrix::create) equals the oracle's for every slot."""
+    params = (0.37, -1.1, 0.52)
+    for slot in range(cm.slot_count(opcode)):
+        m = runtime.DerivativeMatrix.create(runtime.gate_descriptor(opcode, arity, params), slot).matrix()
+        ref = oracle.derivative_matrix(opcode, arity, params, slot)
+        assert np.max(np.abs(m - ref)) < 1e-14, (opcode, slot)
+
+
+def test_derivative_matrix_rejects_invalid_slot(runtime):
+    with pytest.raises(runtime.RuntimeError, match="does not have parameter slot"):
+        runtime.DerivativeMatrix.create(runtime.gate_descriptor(4, 1), 0)
+    with pytest.raises(runtime.RuntimeError, match="does not have parameter slot 3"):
+        runtime.DerivativeMatrix.create(runtime.gate_descriptor(15, 1, (0.1, 0.2, 0.3)), 3)
+
+
+def test_plan_parameters_update(runtime):
+    plan = runtime.CircuitPlan.compile([cm.PlanOp(11, (0,), (0.1, 0, 0), None, ((0, 1),))])
+    plan.set_parameters(np.array([0.0, 0.5]))
+    with pytest.raises(runtime.RuntimeError, match="out of range"):
+        plan.set_parameters(np.array([0.0]))

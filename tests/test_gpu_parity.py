@@ -1,0 +1,247 @@
+"""sm_100a runtime vs the CPU oracle, through the C ABI (needs a B200).
+
+Tolerances: amplitudes and matrices 1e-12 absolute on normalized states (the kernels use FMA,
+the oracle does not); expectations and gradients 1e-10 relative, the bar the reference's
+row_major_batch_tests.rs sets.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import reference_cases as rc
+from backends import OracleBackend, RuntimeBackend, op
+from arcqml_b200 import circuit as cm
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-10
+
+
+def rel_close(a, b, tol=RTOL):
+    a, b = np.asarray(a), np.asarray(b)
+    scale = max(1.0, float(np.max(np.abs(b))) if b.size else 1.0)
+    assert float(np.max(np.abs(a - b))) <= tol * scale, (a, b)
+
+
+@pytest.fixture(scope="module")
+def be(runtime):
+    return RuntimeBackend(runtime)
+
+
+@pytest.mark.parametrize("case", rc.ALL_CASES, ids=lambda f: f.__name__)
+def test_runtime_reference_case(be, case):
+    case(be)
+
+
+def test_runtime_h2_vqe_trajectory(be, oracle):
+    rc.case_h2_vqe_trajectory(be, oracle.adam_step)
+
+
+def random_state(g, n, batch=None):
+    shape = (1 << n,) if batch is None else (batch, 1 << n)
+    a = g.normal(size=shape) + 1j * g.normal(size=shape)
+    a /= np.linalg.norm(a, axis=-1, keepdims=True)
+    return np.ascontiguousarray(a)
+
+
+def random_unitary(g, k):
+    dim = 1 << k
+    z = g.normal(size=(dim, dim)) + 1j * g.normal(size=(dim, dim))
+    q, r = np.linalg.qr(z)
+    return q * (np.diag(r) / np.abs(np.diag(r)))
+
+
+def all_gate_ops(g, n):
+    """One op per opcode (and several MCX / custom arities) on random distinct qubits."""
+    ops = []
+    for code in range(37):
+        arity = 1 if code <= 15 else (2 if code <= 34 else 3)
+        if arity > n:
+            continue
+        q = [int(x) for x in g.choice(n, size=arity, replace=False)]
+        p = tuple(float(x) for x in g.uniform(-math.pi, math.pi, size=3))
+        ops.append(op(code, q, p))
+    for k in range(2, min(n, 6) + 1):
+        ops.append(op(cm.MCX, [int(x) for x in g.choice(n, size=k, replace=False)]))
+    for k in range(1, min(n, 4) + 1):
+        ops.append(op(cm.CUSTOM_UNITARY, [int(x) for x in g.choice(n, size=k, replace=False)],
+                      matrix=random_unitary(g, k)))
+    return ops
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 9, 13])
+def test_every_gate_forward_and_adjoint_matches_oracle(be, oracle, n):
+    g = np.random.Generator(np.random.PCG64(100 + n))
+    ob = OracleBackend(oracle)
+    for o in all_gate_ops(g, n):
+        a = random_state(g, n)
+        for adj in (False, True):
+            got = be.apply_gate(a, n, o, adjoint=adj)
+            want = ob.apply_gate(a, n, o, adjoint=adj)
+            assert np.max(np.abs(got - want)) < 1e-12, (o.opcode, o.qubits, adj)
+
+
+@pytest.mark.parametrize("n", [2, 4, 11])
+def test_every_parameter_derivative_matches_oracle(be, oracle, n):
+    g = np.random.Generator(np.random.PCG64(200 + n))
+    ob = OracleBackend(oracle)
+    for code in range(35):
+        slots = cm.slot_count(code)
+        arity = 1 if code <= 15 else 2
+        for slot in range(slots):
+            q = [int(x) for x in g.choice(n, size=arity, replace=False)]
+            o = op(code, q, tuple(float(x) for x in g.uniform(-3, 3, size=3)))
+            a = random_state(g, n)
+            got = be.parameter_derivative(a, n, o, slot)
+            want = ob.parameter_derivative(a, n, o, slot)
+            assert np.max(np.abs(got - want)) < 1e-12, (code, slot, q)
+
+
+def test_derivative_matrix_apply_matches_oracle(runtime, oracle):
+    g = np.random.Generator(np.random.PCG64(7))
+    n = 6
+    for code, arity in [(11, 1), (15, 1), (24, 2), (34, 2), (30, 2)]:
+        for slot in range(cm.slot_count(code)):
+            p = tuple(float(x) for x in g.uniform(-3, 3, size=3))
+            q = [int(x) for x in g.choice(n, size=arity, replace=False)]
+            dm = runtime.DerivativeMatrix.create(runtime.gate_descriptor(code, arity, p), slot)
+            a = random_state(g, n)
+            got = a.copy()
+            dm.apply(got, q)
+            want = oracle.parameter_derivative(a, n, op(code, q, p), slot)
+            assert np.max(np.abs(got - want)) < 1e-12
+
+
+def random_plan(g, n, num_ops, num_params):
+    """Random circuit over every parameterized opcode plus fixed gates; shared parameters."""
+    param_codes = [11, 12, 13, 14, 15, 22, 23, 24, 25, 30, 31, 32, 33, 34]
+    fixed_codes = [1, 2, 3, 4, 5, 9, 16, 18, 19, 26, 27, 28, 29, 35, 36]
+    values = g.uniform(-math.pi, math.pi, size=num_params)
+    ops = []
+    for _ in range(num_ops):
+        if g.uniform() < 0.65:
+            code = int(g.choice(param_codes))
+            arity = 1 if code <= 15 else 2
+            q = [int(x) for x in g.choice(n, size=arity, replace=False)]
+            slots = cm.slot_count(code)
+            params, binds = [0.0, 0.0, 0.0], []
+            for s in range(slots):
+                if g.uniform() < 0.8:
+                    pid = int(g.integers(0, num_params))
+                    params[s] = values[pid]
+                    binds.append((s, pid + 1))
+                else:
+                    params[s] = float(g.uniform(-3, 3))
+            ops.append(op(code, q, params, bindings=binds))
+        else:
+            code = int(g.choice(fixed_codes))
+            arity = 1 if code <= 15 else (2 if code <= 34 else 3)
+            if arity > n:
+                continue
+            ops.append(op(code, [int(x) for x in g.choice(n, size=arity, replace=False)]))
+    return ops
+
+
+def random_terms(g, n, count):
+    from arcqml_b200.workloads import random_pauli_sum
+    return random_pauli_sum(n, count, seed=int(g.integers(1 << 30))).compiled_terms()
+
+
+@pytest.mark.parametrize("n,num_ops", [(3, 40), (8, 120), (12, 200), (16, 120)])
+def test_run_and_adjoint_match_oracle(be, oracle, n, num_ops):
+    g = np.random.Generator(np.random.PCG64(300 + n))
+    ob = OracleBackend(oracle)
+    npar = 12
+    ops = random_plan(g, n, num_ops, npar)
+    terms = random_terms(g, n, 25)
+    init = random_state(g, n)
+    req = [1] + [int(x) for x in (g.uniform(size=npar) < 0.8)]
+    up = float(g.normal())
+    results = []
+    for b in (be, ob):
+        psi = b.plan_apply(ops, init, n)
+        v, lam = b.expectation_and_apply(terms, psi, n)
+        psi0, lam0, grads = b.adjoint_backward(ops, psi, lam, n, up, req, npar + 1)
+        results.append((psi, v, lam, psi0, lam0, grads))
+    (p1, v1, l1, a1, b1, g1), (p2, v2, l2, a2, b2, g2) = results
+    assert np.max(np.abs(p1 - p2)) < 1e-12
+    rel_close(v1, v2)
+    rel_close(l1, l2)
+    assert np.max(np.abs(a1 - init)) < 1e-10
+    rel_close(b1, b2)
+    rel_close(g1, g2)
+    assert g1[0] == 0.0  # the initial-state slot is never written
+
+
+def test_device_batch_api_matches_oracle(runtime, oracle):
+    import torch
+
+    g = np.random.Generator(np.random.PCG64(11))
+    n, batch, npar = 7, 6, 9
+    ops = random_plan(g, n, 80, npar)
+    terms = random_terms(g, n, 17)
+    init = random_state(g, n, batch)
+    up = g.normal(size=batch)
+    req = np.array([0] + [1] * npar, np.uint8)
+    plan = runtime.CircuitPlan.compile(ops)
+    psi = torch.from_numpy(init.copy()).cuda()
+    runtime.plan_apply_device(plan, psi, n)
+    c = np.array([t[0] for t in terms]); f = np.array([t[1] for t in terms], np.uint64)
+    p = np.array([t[2] for t in terms], np.uint64)
+    obs = runtime.Observable(n, c, f, p)
+    lam = torch.empty_like(psi)
+    vals = obs.expectation_and_apply(psi, lam, n)
+    vals2 = obs.expectation(psi, n)
+    grads = runtime.adjoint_backward_device(plan, psi, lam, n, up, req, npar + 1)
+    ref_psi = oracle.plan_apply(ops, init, n, batch=batch)
+    ref_vals = [oracle.expectation_and_apply(terms, r, n)[0] for r in ref_psi]
+    ref_lam = np.stack([oracle.expectation_and_apply(terms, r, n)[1] for r in ref_psi])
+    _, ref_lam0, ref_grads = oracle.adjoint_backward(ops, ref_psi, ref_lam, n, up, req,
+                                                    npar + 1, batch=batch)
+    rel_close(vals, ref_vals)
+    rel_close(vals2, ref_vals)
+    rel_close(grads, ref_grads)
+    rel_close(lam.cpu().numpy(), ref_lam0)
+    assert np.max(np.abs(psi.cpu().numpy() - init)) < 1e-10
+    norms = runtime.norms_device(psi, n)
+    assert np.max(np.abs(norms - 1.0)) < 1e-12
+
+
+def test_basis_state_and_errors(runtime):
+    import torch
+
+    s = torch.empty((3, 16), dtype=torch.complex128, device="cuda")
+    runtime.set_basis_state_device(s, 4, 5)
+    want = np.zeros((3, 16), np.complex128); want[:, 5] = 1
+    assert np.array_equal(s.cpu().numpy(), want)
+    with pytest.raises(runtime.RuntimeError, match="basis index out of range"):
+        runtime.set_basis_state_device(s, 4, 16)
+    plan = runtime.CircuitPlan.compile([op(16, [0, 5])])
+    with pytest.raises(runtime.RuntimeError, match="out of range for 4 qubits"):
+        runtime.plan_apply_device(plan, s, 4)
+
+
+def test_brickwork_20q_matches_oracle(runtime, oracle):
+    """A brickwork circuit and 200-term observable of the benchmark generators at 20 qubits."""
+    import torch
+    from arcqml_b200 import workloads
+
+    n = 20
+    c = workloads.brickwork(n, 6, seed=5)
+    obs = workloads.random_pauli_sum(n, 60, seed=6)
+    ops = c.compile_plan(1)
+    init = np.zeros(1 << n, np.complex128); init[0] = 1
+    plan = runtime.CircuitPlan.compile(ops)
+    psi = torch.from_numpy(init.copy()).cuda()
+    runtime.plan_apply_device(plan, psi, n)
+    robs = runtime.Observable.from_sparse_pauli_op(obs)
+    lam = torch.empty_like(psi)
+    v = robs.expectation_and_apply(psi, lam, n)[0]
+    req = c.requires_grad_mask(True)
+    grads = runtime.adjoint_backward_device(plan, psi, lam, n, 1.0, req, len(req))
+    ref_psi = oracle.plan_apply(ops, init, n)
+    rv, rlam = oracle.expectation_and_apply(obs.compiled_terms(), ref_psi, n)
+    _, _, rgrads = oracle.adjoint_backward(ops, ref_psi, rlam, n, 1.0, req, len(req))
+    rel_close(v, rv)
+    rel_close(grads, rgrads)
