@@ -8,10 +8,12 @@
 // (k_adjoint): 64 bytes of HBM traffic per touched amplitude, no derivative scratch state.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <sstream>
 #include <unordered_map>
 
 #include "launch.h"
+#include "planner.h"
 #include "rt_internal.h"
 
 namespace arcqml {
@@ -47,7 +49,7 @@ struct ContextSlot {
         int prev = -1;
         if (cudaGetDevice(&prev) != cudaSuccess) return;
         if (ctx.device >= 0 && cudaSetDevice(ctx.device) == cudaSuccess) {
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 5; ++i)
                 if (ctx.buf[i]) cudaFree(ctx.buf[i]);
             if (ctx.partials) cudaFree(ctx.partials);
             if (ctx.dgrads) cudaFree(ctx.dgrads);
@@ -160,9 +162,27 @@ void validate_plan_for_state(const Plan &plan, uint32_t n) {
     for (const auto &op : plan.ops) check_qubits_for_state(op, n);
 }
 
+// Fused passes are used from these state sizes up (a tile must fit in one state row).
+constexpr uint32_t kFusedForwardMinQubits = 12;
+constexpr uint32_t kFusedAdjointMinQubits = 11;
+
+// ARCQML_FUSE=0 selects the per-gate kernels everywhere (for A/B measurements).
+bool fusion_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_FUSE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 void plan_apply_device(Plan &plan, double2 *amps, size_t batch, uint32_t n, ThreadContext &ctx,
                        cudaStream_t s) {
     validate_plan_for_state(plan, n);
+    if (fusion_enabled() && n >= kFusedForwardMinQubits) {
+        Schedule sch = build_schedule(plan, n, false, nullptr, false, 12, 4);
+        run_schedule(sch, amps, nullptr, batch, n, nullptr, 0, ctx, s);
+        return;
+    }
     std::vector<std::vector<double2>> dense;
     std::vector<DevGate> gates;
     gates.reserve(plan.ops.size());
@@ -222,6 +242,31 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
         auto p = upload_tables(refs, ctx, s);
         launch_scale(lam, batch, n, reinterpret_cast<const double *>(p[0]), s);
         // The table buffer is reused below for dense matrices; keep the scale ordered first.
+    }
+
+    if (fusion_enabled() && n >= kFusedAdjointMinQubits) {
+        Schedule sch = build_schedule(plan, n, true, req, true, 11, 3);
+        const uint32_t stride = fused_grid_blocks(true);
+        double *partials = nullptr;
+        if (sch.total_acc) {
+            partials = ctx_partials(ctx, size_t(sch.total_acc) * stride);
+            check_cuda(cudaMemsetAsync(partials, 0, size_t(sch.total_acc) * stride * sizeof(double), s),
+                       "cudaMemsetAsync");
+        }
+        run_schedule(sch, psi, lam, batch, n, partials, stride, ctx, s);
+        if (sch.total_acc) {
+            double *sums = ctx_dgrads(ctx, sch.total_acc);
+            launch_reduce_rows(partials, sch.total_acc, stride, sums, s);
+            double *h = ctx_hvals(ctx, sch.total_acc);
+            check_cuda(cudaMemcpyAsync(h, sums, sch.total_acc * sizeof(double),
+                                       cudaMemcpyDeviceToHost, s),
+                       "cudaMemcpyAsync (gradients)");
+            check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+            size_t a = 0;
+            for (const auto &st : sch.steps)
+                for (size_t p : st.parents) grads_host[p] += 2.0 * h[a++];
+        }
+        return;
     }
 
     // Rows of partial sums, one per (op, binding) that needs a gradient, in sweep order.

@@ -1,0 +1,653 @@
+// fused.cu — fused multi-gate passes for sm_100a (layouts in fused.h, schedules in planner.cpp).
+//
+// One persistent launch per pass. Each CTA (256 threads) loops over tiles: it streams the
+// tile's 2^k amplitudes (psi, and lambda for the adjoint sweep) from HBM into swizzled shared
+// memory, runs the pass's sub-blocks — each thread gathers 2^RB amplitudes into registers,
+// applies the sub-block's gates there, scatters them back — and streams the tile out. HBM sees
+// one read and one write per amplitude per pass; the arithmetic runs from registers.
+//
+// Adjoint passes apply U^dagger to psi and lambda and accumulate, per bound parameter slot,
+// Re<lambda_k| dU/dp |psi_{k-1}> (for Pauli rotations as Im<lambda_k|P|psi_k> / 2): each warp
+// reduces its lanes with shuffles and adds into its own shared-memory column; columns are summed
+// per CTA at the end into partials[acc][block] (fixed order, deterministic).
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "fused.h"
+#include "launch.h"
+#include "planner.h"
+
+namespace arcqml {
+
+namespace {
+
+constexpr int kFThreads = 256;
+constexpr int kWarps = kFThreads / 32;
+
+__device__ __forceinline__ uint32_t phys(uint32_t j) {
+    return j ^ (((j >> 3) ^ (j >> 6) ^ (j >> 9)) & 7u);
+}
+
+__device__ __forceinline__ double2 cmul(double2 a, double2 b) {
+    return make_double2(fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x));
+}
+__device__ __forceinline__ double2 cfma(double2 a, double2 b, double2 c) {
+    return make_double2(fma(a.x, b.x, fma(-a.y, b.y, c.x)), fma(a.x, b.y, fma(a.y, b.x, c.y)));
+}
+// Re(conj(a) b) and Im(conj(a) b)
+__device__ __forceinline__ double rcm(double2 a, double2 b) { return fma(a.x, b.x, a.y * b.y); }
+__device__ __forceinline__ double icm(double2 a, double2 b) { return fma(a.x, b.y, -a.y * b.x); }
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ void load_op(const FOp *src, FOp &dst) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    uint4 *d = reinterpret_cast<uint4 *>(&dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] = __ldg(s + i);
+}
+
+struct OpEnv {
+    bool tile_ok;        // controls outside the tile satisfied
+    bool plain;          // no controls at all
+    uint32_t lcmask;
+    uint64_t gbase;      // global index bits outside the tile
+};
+
+template <int RB>
+__device__ __forceinline__ bool ctrl_ok(const OpEnv &E, const uint32_t (&Le)[1 << RB], int e) {
+    return E.plain || (E.tile_ok && ((Le[e] & E.lcmask) == E.lcmask));
+}
+
+// ---------------------------------------------------------------- 1-target gates on bit B
+
+template <int RB, int B>
+__device__ __forceinline__ void apply_1t(uint8_t kind, const double2 *mt, double2 (&v)[1 << RB],
+                                         const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    if (kind == FK_RX || kind == FK_RY) {
+        const double2 cs = __ldg(mt);
+        const double c = cs.x, s = cs.y;
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+            if (e & (1 << B)) continue;
+            const int f = e | (1 << B);
+            const double2 x0 = v[e], x1 = v[f];
+            double2 y0, y1;
+            if (kind == FK_RX) {
+                y0 = make_double2(fma(c, x0.x, s * x1.y), fma(c, x0.y, -s * x1.x));
+                y1 = make_double2(fma(c, x1.x, s * x0.y), fma(c, x1.y, -s * x0.x));
+            } else {
+                y0 = make_double2(fma(c, x0.x, -s * x1.x), fma(c, x0.y, -s * x1.y));
+                y1 = make_double2(fma(s, x0.x, c * x1.x), fma(s, x0.y, c * x1.y));
+            }
+            const bool ok = ctrl_ok<RB>(E, Le, e);
+            v[e] = ok ? y0 : x0;
+            v[f] = ok ? y1 : x1;
+        }
+    } else {  // FK_M2
+        const double2 m0 = __ldg(mt), m1 = __ldg(mt + 1), m2 = __ldg(mt + 2), m3 = __ldg(mt + 3);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+            if (e & (1 << B)) continue;
+            const int f = e | (1 << B);
+            const double2 x0 = v[e], x1 = v[f];
+            const double2 y0 = cfma(m0, x0, cmul(m1, x1));
+            const double2 y1 = cfma(m2, x0, cmul(m3, x1));
+            const bool ok = ctrl_ok<RB>(E, Le, e);
+            v[e] = ok ? y0 : x0;
+            v[f] = ok ? y1 : x1;
+        }
+    }
+}
+
+template <int RB>
+__device__ __forceinline__ void apply_1t_dispatch(int b, uint8_t kind, const double2 *mt,
+                                                  double2 (&v)[1 << RB],
+                                                  const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    switch (b) {
+    case 0: apply_1t<RB, 0>(kind, mt, v, Le, E); break;
+    case 1: apply_1t<RB, 1>(kind, mt, v, Le, E); break;
+    case 2: apply_1t<RB, 2>(kind, mt, v, Le, E); break;
+    default:
+        if constexpr (RB > 3) apply_1t<RB, 3>(kind, mt, v, Le, E);
+        break;
+    }
+}
+
+// ---------------------------------------------------------------- 2-target dense on (B0, B1)
+
+template <int RB, int B0, int B1>
+__device__ __forceinline__ void apply_m4(const double2 *mt, double2 (&v)[1 << RB],
+                                         const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        if (e & ((1 << B0) | (1 << B1))) continue;
+        const int idx[4] = {e, e | (1 << B0), e | (1 << B1), e | (1 << B0) | (1 << B1)};
+        double2 x[4], y[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = v[idx[j]];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            double2 acc = cmul(__ldg(mt + i * 4), x[0]);
+            acc = cfma(__ldg(mt + i * 4 + 1), x[1], acc);
+            acc = cfma(__ldg(mt + i * 4 + 2), x[2], acc);
+            acc = cfma(__ldg(mt + i * 4 + 3), x[3], acc);
+            y[i] = acc;
+        }
+        const bool ok = ctrl_ok<RB>(E, Le, e);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[idx[j]] = ok ? y[j] : x[j];
+    }
+}
+
+template <int RB, int B0>
+__device__ __forceinline__ void apply_m4_b1(int b1, const double2 *mt, double2 (&v)[1 << RB],
+                                            const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    switch (b1) {
+    case 0: if constexpr (B0 != 0) apply_m4<RB, B0, 0>(mt, v, Le, E); break;
+    case 1: if constexpr (B0 != 1) apply_m4<RB, B0, 1>(mt, v, Le, E); break;
+    case 2: if constexpr (B0 != 2) apply_m4<RB, B0, 2>(mt, v, Le, E); break;
+    default:
+        if constexpr (RB > 3 && B0 != 3) apply_m4<RB, B0, 3>(mt, v, Le, E);
+        break;
+    }
+}
+
+template <int RB>
+__device__ __forceinline__ void apply_m4_dispatch(int b0, int b1, const double2 *mt,
+                                                  double2 (&v)[1 << RB],
+                                                  const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    switch (b0) {
+    case 0: apply_m4_b1<RB, 0>(b1, mt, v, Le, E); break;
+    case 1: apply_m4_b1<RB, 1>(b1, mt, v, Le, E); break;
+    case 2: apply_m4_b1<RB, 2>(b1, mt, v, Le, E); break;
+    default:
+        if constexpr (RB > 3) apply_m4_b1<RB, 3>(b1, mt, v, Le, E);
+        break;
+    }
+}
+
+// ---------------------------------------------------------------- diagonal gates
+
+template <int RB>
+__device__ __forceinline__ uint32_t dbit(const FOp &o, int t, const uint32_t (&Le)[1 << RB], int e,
+                                         uint64_t gbase) {
+    return o.dq_in_tile[t] ? ((Le[e] >> o.dq_pos[t]) & 1u) : uint32_t((gbase >> o.dq_pos[t]) & 1u);
+}
+
+template <int RB>
+__device__ __forceinline__ void apply_diag(const FOp &o, const double2 *mt, double2 (&v)[1 << RB],
+                                           const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    if (o.kind == FK_D1) {
+        const double2 d0 = __ldg(mt), d1 = __ldg(mt + 1);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+            const double2 d = dbit<RB>(o, 0, Le, e, E.gbase) ? d1 : d0;
+            const double2 y = cmul(d, v[e]);
+            v[e] = ctrl_ok<RB>(E, Le, e) ? y : v[e];
+        }
+    } else {
+        const double2 d0 = __ldg(mt), d1 = __ldg(mt + 1), d2 = __ldg(mt + 2), d3 = __ldg(mt + 3);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+            const uint32_t b = dbit<RB>(o, 0, Le, e, E.gbase) | (dbit<RB>(o, 1, Le, e, E.gbase) << 1);
+            const double2 d = b == 0 ? d0 : (b == 1 ? d1 : (b == 2 ? d2 : d3));
+            const double2 y = cmul(d, v[e]);
+            v[e] = ctrl_ok<RB>(E, Le, e) ? y : v[e];
+        }
+    }
+}
+
+template <int RB>
+__device__ __forceinline__ void apply_op(const FOp &o, const double2 *mt, double2 (&v)[1 << RB],
+                                         const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    switch (o.kind) {
+    case FK_RX:
+    case FK_RY:
+    case FK_M2: apply_1t_dispatch<RB>(o.rb0, o.kind, mt, v, Le, E); break;
+    case FK_D1:
+    case FK_D2: apply_diag<RB>(o, mt, v, Le, E); break;
+    case FK_M4: apply_m4_dispatch<RB>(o.rb0, o.rb1, mt, v, Le, E); break;
+    default: break;
+    }
+}
+
+// ---------------------------------------------------------------- adjoint gradients
+
+// Im<lam|X|psi> or Im<lam|Y|psi> over pairs on register bit B (psi = psi_k, before U^dag).
+template <int RB, int B>
+__device__ __forceinline__ double grad_xy(bool is_y, const double2 (&v)[1 << RB],
+                                          const double2 (&w)[1 << RB],
+                                          const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        // X: Im(conj(l0) x1) + Im(conj(l1) x0);  Y: -Re(conj(l0) x1) + Re(conj(l1) x0)
+        const double t = is_y ? (rcm(w[f], v[e]) - rcm(w[e], v[f])) : (icm(w[e], v[f]) + icm(w[f], v[e]));
+        z += ctrl_ok<RB>(E, Le, e) ? t : 0.0;
+    }
+    return z;
+}
+
+template <int RB>
+__device__ __forceinline__ double grad_xy_dispatch(int b, bool is_y, const double2 (&v)[1 << RB],
+                                                   const double2 (&w)[1 << RB],
+                                                   const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    switch (b) {
+    case 0: return grad_xy<RB, 0>(is_y, v, w, Le, E);
+    case 1: return grad_xy<RB, 1>(is_y, v, w, Le, E);
+    case 2: return grad_xy<RB, 2>(is_y, v, w, Le, E);
+    default:
+        if constexpr (RB > 3) return grad_xy<RB, 3>(is_y, v, w, Le, E);
+        return 0.0;
+    }
+}
+
+// Im<lam|Z_q|psi> for the op's diagonal qubit q.
+template <int RB>
+__device__ __forceinline__ double grad_z(const FOp &o, const double2 (&v)[1 << RB],
+                                         const double2 (&w)[1 << RB], const uint32_t (&Le)[1 << RB],
+                                         const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        const double t = icm(w[e], v[e]);
+        const double st = dbit<RB>(o, 0, Le, e, E.gbase) ? -t : t;
+        z += ctrl_ok<RB>(E, Le, e) ? st : 0.0;
+    }
+    return z;
+}
+
+// Re<lam| D |psi'> for a small matrix D of the op's shape, psi' already U^dag psi.
+template <int RB, int B>
+__device__ __forceinline__ double grad_m2(const double2 *d, const double2 (&v)[1 << RB],
+                                          const double2 (&w)[1 << RB],
+                                          const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    const double2 m0 = __ldg(d), m1 = __ldg(d + 1), m2 = __ldg(d + 2), m3 = __ldg(d + 3);
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        const double2 y0 = cfma(m0, v[e], cmul(m1, v[f]));
+        const double2 y1 = cfma(m2, v[e], cmul(m3, v[f]));
+        const double t = rcm(w[e], y0) + rcm(w[f], y1);
+        z += ctrl_ok<RB>(E, Le, e) ? t : 0.0;
+    }
+    return z;
+}
+
+template <int RB, int B0, int B1>
+__device__ __forceinline__ double grad_m4(const double2 *d, const double2 (&v)[1 << RB],
+                                          const double2 (&w)[1 << RB],
+                                          const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        if (e & ((1 << B0) | (1 << B1))) continue;
+        const int idx[4] = {e, e | (1 << B0), e | (1 << B1), e | (1 << B0) | (1 << B1)};
+        double t = 0.0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            double2 acc = cmul(__ldg(d + i * 4), v[idx[0]]);
+            acc = cfma(__ldg(d + i * 4 + 1), v[idx[1]], acc);
+            acc = cfma(__ldg(d + i * 4 + 2), v[idx[2]], acc);
+            acc = cfma(__ldg(d + i * 4 + 3), v[idx[3]], acc);
+            t += rcm(w[idx[i]], acc);
+        }
+        z += ctrl_ok<RB>(E, Le, e) ? t : 0.0;
+    }
+    return z;
+}
+
+template <int RB, int B0>
+__device__ __forceinline__ double grad_m4_b1(int b1, const double2 *d, const double2 (&v)[1 << RB],
+                                             const double2 (&w)[1 << RB],
+                                             const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    switch (b1) {
+    case 0: if constexpr (B0 != 0) return grad_m4<RB, B0, 0>(d, v, w, Le, E); break;
+    case 1: if constexpr (B0 != 1) return grad_m4<RB, B0, 1>(d, v, w, Le, E); break;
+    case 2: if constexpr (B0 != 2) return grad_m4<RB, B0, 2>(d, v, w, Le, E); break;
+    default:
+        if constexpr (RB > 3 && B0 != 3) return grad_m4<RB, B0, 3>(d, v, w, Le, E);
+        break;
+    }
+    return 0.0;
+}
+
+template <int RB>
+__device__ __forceinline__ double grad_generic(const FOp &o, const double2 *d,
+                                               const double2 (&v)[1 << RB],
+                                               const double2 (&w)[1 << RB],
+                                               const uint32_t (&Le)[1 << RB], const OpEnv &E) {
+    constexpr int N = 1 << RB;
+    if (o.kind == FK_D1 || o.kind == FK_D2) {
+        double z = 0.0;
+        const bool two = o.kind == FK_D2;
+        const double2 d0 = __ldg(d), d1 = __ldg(d + 1);
+        const double2 d2 = two ? __ldg(d + 2) : d0, d3 = two ? __ldg(d + 3) : d1;
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+            uint32_t b = dbit<RB>(o, 0, Le, e, E.gbase);
+            if (two) b |= dbit<RB>(o, 1, Le, e, E.gbase) << 1;
+            const double2 dd = b == 0 ? d0 : (b == 1 ? d1 : (b == 2 ? d2 : d3));
+            const double t = rcm(w[e], cmul(dd, v[e]));
+            z += ctrl_ok<RB>(E, Le, e) ? t : 0.0;
+        }
+        return z;
+    }
+    if (o.kind == FK_M4) {
+        switch (o.rb0) {
+        case 0: return grad_m4_b1<RB, 0>(o.rb1, d, v, w, Le, E);
+        case 1: return grad_m4_b1<RB, 1>(o.rb1, d, v, w, Le, E);
+        case 2: return grad_m4_b1<RB, 2>(o.rb1, d, v, w, Le, E);
+        default:
+            if constexpr (RB > 3) return grad_m4_b1<RB, 3>(o.rb1, d, v, w, Le, E);
+            return 0.0;
+        }
+    }
+    switch (o.rb0) {
+    case 0: return grad_m2<RB, 0>(d, v, w, Le, E);
+    case 1: return grad_m2<RB, 1>(d, v, w, Le, E);
+    case 2: return grad_m2<RB, 2>(d, v, w, Le, E);
+    default:
+        if constexpr (RB > 3) return grad_m2<RB, 3>(d, v, w, Le, E);
+        return 0.0;
+    }
+}
+
+// Matrix entries of the op's U (to skip over to the derivative matrices) and of one dU.
+__device__ __forceinline__ int umat_len(uint8_t kind) {
+    switch (kind) {
+    case FK_RX: case FK_RY: return 1;
+    case FK_M2: return 4;
+    case FK_D1: return 2;
+    case FK_D2: return 4;
+    default: return 16;
+    }
+}
+__device__ __forceinline__ int dmat_len(uint8_t kind) {
+    switch (kind) {
+    case FK_D1: return 2;
+    case FK_D2: return 4;
+    case FK_M4: return 16;
+    default: return 4;
+    }
+}
+
+__device__ __forceinline__ void accumulate(double *sacc, uint32_t acc, double z) {
+    z = warp_sum(z);
+    if ((threadIdx.x & 31) == 0) sacc[acc * kWarps + (threadIdx.x >> 5)] += z;
+}
+
+// ---------------------------------------------------------------- the pass kernel
+
+template <int RB, bool ADJ>
+__global__ void __launch_bounds__(kFThreads, ADJ ? 2 : 1)
+    k_fused(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n, uint32_t tiles_log,
+            uint64_t total_tiles, const PassHeader *__restrict__ hdr,
+            const SubBlock *__restrict__ subs, const FOp *__restrict__ ops,
+            const double2 *__restrict__ mats, double *__restrict__ partials, uint32_t stride) {
+    constexpr int N = 1 << RB;
+    extern __shared__ double2 smem[];
+    __shared__ uint8_t sS[16];
+    __shared__ uint32_t sk, snsub, snacc, sacc_base;
+    if (threadIdx.x < 16) sS[threadIdx.x] = hdr->S[threadIdx.x];
+    if (threadIdx.x == 0) {
+        sk = hdr->k;
+        snsub = hdr->nsub;
+        snacc = hdr->nacc;
+        sacc_base = hdr->acc_base;
+    }
+    __syncthreads();
+    const uint32_t k = sk;
+    const uint32_t D = 1u << k;
+    const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
+    const uint32_t lowmask = (1u << L) - 1;
+    double2 *tp = smem;
+    double2 *tl = smem + (ADJ ? D : 0);
+    uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + (ADJ ? 2 * D : D));
+    double *sacc = reinterpret_cast<double *>(hioff + (1u << (k - L)));
+    for (uint32_t h = threadIdx.x; h < (1u << (k - L)); h += kFThreads) {
+        uint64_t off = 0;
+        for (uint32_t b = 0; b < k - L; ++b)
+            if ((h >> b) & 1) off |= uint64_t(1) << sS[L + b];
+        hioff[h] = off;
+    }
+    if (ADJ)
+        for (uint32_t a = threadIdx.x; a < snacc * kWarps; a += kFThreads) sacc[a] = 0.0;
+    __syncthreads();
+
+    const uint64_t tmask = (uint64_t(1) << tiles_log) - 1;
+    for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x) {
+        const uint64_t rowoff = (T >> tiles_log) << n;
+        // global bits of the tile: insert zeros at the (sorted) tile positions
+        uint64_t gbase = T & tmask;
+        for (uint32_t b = 0; b < k; ++b) {
+            const uint32_t p = sS[b];
+            gbase = ((gbase >> p) << (p + 1)) | (gbase & ((uint64_t(1) << p) - 1));
+        }
+        double2 *P = psi + rowoff + gbase;
+        double2 *Lm = ADJ ? lam + rowoff + gbase : nullptr;
+        for (uint32_t j = threadIdx.x; j < D; j += kFThreads) {
+            const uint64_t g = (j & lowmask) | hioff[j >> L];
+            tp[phys(j)] = P[g];
+            if (ADJ) tl[phys(j)] = Lm[g];
+        }
+        __syncthreads();
+        for (uint32_t sb = 0; sb < snsub; ++sb) {
+            SubBlock S;
+            {
+                const uint2 *s = reinterpret_cast<const uint2 *>(subs + sb);
+                uint2 *d = reinterpret_cast<uint2 *>(&S);
+#pragma unroll
+                for (int i = 0; i < 3; ++i) d[i] = __ldg(s + i);
+            }
+            uint32_t tb = 0;
+#pragma unroll
+            for (int i = 0; i < 12 - RB; ++i)
+                if (i < int(k) - RB && ((threadIdx.x >> i) & 1)) tb |= 1u << S.perm[i];
+            uint32_t rm[RB];
+#pragma unroll
+            for (int r = 0; r < RB; ++r) rm[r] = 1u << S.R[r];
+            uint32_t Le[N];
+            double2 v[N], w[N];
+#pragma unroll
+            for (int e = 0; e < N; ++e) {
+                uint32_t x = tb;
+#pragma unroll
+                for (int r = 0; r < RB; ++r)
+                    if ((e >> r) & 1) x |= rm[r];
+                Le[e] = x;
+                v[e] = tp[phys(x)];
+                if (ADJ) w[e] = tl[phys(x)];
+            }
+            for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
+                FOp o;
+                load_op(ops + oi, o);
+                OpEnv E;
+                E.lcmask = o.lcmask;
+                E.gbase = gbase;
+                E.tile_ok = (gbase & o.gcmask) == o.gcmask;
+                E.plain = (o.lcmask == 0) && (o.gcmask == 0);
+                const double2 *mt = mats + o.moff;
+                if (ADJ) {
+                    if (o.gkind == GK_PX || o.gkind == GK_PY) {
+                        const double z = grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
+                        accumulate(sacc, o.acc[0], 0.5 * z);
+                    } else if (o.gkind == GK_PZ) {
+                        accumulate(sacc, o.acc[0], 0.5 * grad_z<RB>(o, v, w, Le, E));
+                    }
+                }
+                apply_op<RB>(o, mt, v, Le, E);
+                if (ADJ) {
+                    if (o.gkind == GK_GENERIC) {
+                        const double2 *d = mt + umat_len(o.kind);
+                        const int dl = dmat_len(o.kind);
+                        for (int s = 0; s < int(o.nslots); ++s)
+                            accumulate(sacc, o.acc[s], grad_generic<RB>(o, d + s * dl, v, w, Le, E));
+                    }
+                    apply_op<RB>(o, mt, w, Le, E);
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < N; ++e) {
+                tp[phys(Le[e])] = v[e];
+                if (ADJ) tl[phys(Le[e])] = w[e];
+            }
+            __syncthreads();
+        }
+        for (uint32_t j = threadIdx.x; j < D; j += kFThreads) {
+            const uint64_t g = (j & lowmask) | hioff[j >> L];
+            P[g] = tp[phys(j)];
+            if (ADJ) Lm[g] = tl[phys(j)];
+        }
+        __syncthreads();
+    }
+    if (ADJ) {
+        for (uint32_t a = threadIdx.x; a < snacc; a += kFThreads) {
+            double s = 0.0;
+#pragma unroll
+            for (int wi = 0; wi < kWarps; ++wi) s += sacc[a * kWarps + wi];
+            partials[size_t(sacc_base + a) * stride + blockIdx.x] = s;
+        }
+    }
+}
+
+constexpr int kFwdRB = 4;   // forward: 16 amplitudes per thread, k = 12
+constexpr int kAdjRB = 3;   // adjoint: 8 + 8 amplitudes per thread, k = 11
+
+size_t fused_smem(bool adj, uint32_t k, uint32_t nacc) {
+    const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
+    size_t b = (adj ? 2 : 1) * (size_t(16) << k) + (size_t(8) << (k - L));
+    if (adj) b += size_t(nacc) * kWarps * 8;
+    return b;
+}
+
+int g_blocks_fwd = 0, g_blocks_adj = 0;
+
+}  // namespace
+
+uint32_t fused_grid_blocks(bool adjoint) {
+    int &cache = adjoint ? g_blocks_adj : g_blocks_fwd;
+    if (cache == 0) {
+        int dev = 0, sms = 0;
+        check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+        check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
+                   "cudaDeviceGetAttribute");
+        const size_t smem = adjoint ? fused_smem(true, 11, kMaxPassAcc) : fused_smem(false, 12, 0);
+        int per_sm = 0;
+        if (adjoint) {
+            check_cuda(cudaFuncSetAttribute(k_fused<kAdjRB, true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                       "cudaFuncSetAttribute");
+            check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused<kAdjRB, true>,
+                                                                     kFThreads, smem),
+                       "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        } else {
+            check_cuda(cudaFuncSetAttribute(k_fused<kFwdRB, false>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                       "cudaFuncSetAttribute");
+            check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused<kFwdRB, false>,
+                                                                     kFThreads, smem),
+                       "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        }
+        cache = sms * (per_sm < 1 ? 1 : per_sm);
+    }
+    return uint32_t(cache);
+}
+
+void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch, uint32_t n,
+                  double *partials, uint32_t partial_stride, ThreadContext &ctx, cudaStream_t s) {
+    const bool adj = lam != nullptr;
+    // Upload every pass's tables into one device blob (16-byte aligned sections).
+    struct Off {
+        size_t hdr, subs, ops, mats;
+    };
+    std::vector<Off> offs;
+    size_t total = 0;
+    auto align = [](size_t x) { return (x + 15) & ~size_t(15); };
+    for (const auto &st : sch.steps) {
+        Off o{0, 0, 0, 0};
+        if (st.is_pass) {
+            o.hdr = total;
+            total = align(total + sizeof(PassHeader));
+            o.subs = total;
+            total = align(total + st.subs.size() * sizeof(SubBlock));
+            o.ops = total;
+            total = align(total + st.ops.size() * sizeof(FOp));
+            o.mats = total;
+            total = align(total + st.mats.size() * sizeof(double2));
+        }
+        offs.push_back(o);
+    }
+    std::vector<char> blob(total);
+    for (size_t i = 0; i < sch.steps.size(); ++i) {
+        const auto &st = sch.steps[i];
+        if (!st.is_pass) continue;
+        std::memcpy(blob.data() + offs[i].hdr, &st.header, sizeof(PassHeader));
+        std::memcpy(blob.data() + offs[i].subs, st.subs.data(), st.subs.size() * sizeof(SubBlock));
+        std::memcpy(blob.data() + offs[i].ops, st.ops.data(), st.ops.size() * sizeof(FOp));
+        std::memcpy(blob.data() + offs[i].mats, st.mats.data(), st.mats.size() * sizeof(double2));
+    }
+    char *dev = nullptr;
+    if (total) {
+        dev = static_cast<char *>(ctx_buffer(ctx, 4, total));
+        check_cuda(cudaMemcpyAsync(dev, blob.data(), total, cudaMemcpyHostToDevice, s),
+                   "cudaMemcpyAsync (pass tables)");
+    }
+    const uint32_t blocks = fused_grid_blocks(adj);
+    for (size_t i = 0; i < sch.steps.size(); ++i) {
+        const auto &st = sch.steps[i];
+        if (!st.is_pass) {
+            const OpRecord &op = *st.dense_op;
+            std::vector<double2> m = op.custom;
+            if (adj) {
+                const size_t dim = size_t(1) << op.qubits.size();
+                for (size_t a = 0; a < dim; ++a)
+                    for (size_t b = 0; b < dim; ++b)
+                        m[b * dim + a] = make_double2(op.custom[a * dim + b].x, -op.custom[a * dim + b].y);
+            }
+            DevGate g = lower(op, LOWER_FORWARD, 0);
+            std::vector<const std::vector<double2> *> refs{&m};
+            g.dense = upload_tables(refs, ctx, s)[0];
+            launch_gate(psi, batch, n, g, s);
+            if (adj) launch_gate(lam, batch, n, g, s);
+            continue;
+        }
+        const uint32_t k = st.header.k;
+        const uint32_t tiles_log = n - k;
+        const uint64_t total_tiles = uint64_t(batch) << tiles_log;
+        const size_t smem = fused_smem(adj, k, st.header.nacc);
+        const auto *hdr = reinterpret_cast<const PassHeader *>(dev + offs[i].hdr);
+        const auto *sub = reinterpret_cast<const SubBlock *>(dev + offs[i].subs);
+        const auto *ops = reinterpret_cast<const FOp *>(dev + offs[i].ops);
+        const auto *mats = reinterpret_cast<const double2 *>(dev + offs[i].mats);
+        const unsigned grid = unsigned(total_tiles < blocks ? total_tiles : blocks);
+        if (adj)
+            k_fused<kAdjRB, true><<<grid, kFThreads, smem, s>>>(psi, lam, n, tiles_log, total_tiles,
+                                                               hdr, sub, ops, mats, partials,
+                                                               partial_stride);
+        else
+            k_fused<kFwdRB, false><<<grid, kFThreads, smem, s>>>(psi, nullptr, n, tiles_log,
+                                                                total_tiles, hdr, sub, ops, mats,
+                                                                nullptr, 0);
+        check_cuda(cudaGetLastError(), "fused pass launch");
+    }
+}
+
+}  // namespace arcqml

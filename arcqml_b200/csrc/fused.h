@@ -1,0 +1,80 @@
+// fused.h — fused multi-gate passes over shared-memory tiles (host + device layouts).
+//
+// A pass loads a tile of 2^k amplitudes whose tile-local index bit j is global qubit S[j]
+// (S sorted, S[0..L) = 0..L-1 so a tile is 2^(k-L) contiguous runs of 2^L amplitudes), applies a
+// sequence of gates whose non-diagonal targets lie in S, and writes the tile back: one HBM read
+// and write of the state for the whole sequence. Diagonal gates and controls may sit on any
+// qubit (their bits are known per tile). Inside the tile the gates are grouped in sub-blocks: each
+// thread holds 2^RB amplitudes in registers spanning RB "register bits" R of the tile, applies
+// every gate of the sub-block whose targets lie in R, and the tile round-trips through shared
+// memory only between sub-blocks.
+//
+// Shared-memory layout: tile element j lives at phys(j) = j ^ fold(j), where fold XORs the
+// 3-bit groups j[3:6], j[6:9], j[9:12] into the low 3 bits. A quarter-warp (8 lanes) whose
+// lane bits map to tile bits with distinct residues mod 3 touches 8 distinct 16-byte bank slots.
+#pragma once
+
+#include <stdint.h>
+
+namespace arcqml {
+
+constexpr int kTileMax = 12;       // tile qubits
+constexpr int kLowFixed = 4;       // S always holds qubits 0..kLowFixed-1 (256-byte runs)
+constexpr int kMaxPassOps = 512;   // fused ops per pass
+constexpr int kMaxPassAcc = 256;   // gradient accumulators per pass
+
+enum FusedKind : uint8_t {
+    FK_M2 = 0,  // dense 2x2 on register bit rb0; m = [m00 m01 m10 m11]
+    FK_RX = 1,  // m[0] = (c, s): [[c, -is], [-is, c]]
+    FK_RY = 2,  // m[0] = (c, s): [[c, -s], [s, c]]
+    FK_D1 = 3,  // diagonal (d0, d1) on one qubit anywhere
+    FK_D2 = 4,  // diagonal (d0..d3) on two qubits anywhere, index bit(q0) + 2 bit(q1)
+    FK_M4 = 5,  // dense 4x4 on register bits (rb0, rb1)
+};
+
+enum GradKind : uint8_t {
+    GK_NONE = 0,
+    GK_PX = 1,       // rotation about X on rb0: slot gradient = Im<lam|X|psi> (psi before U^dag)
+    GK_PY = 2,       // about Y
+    GK_PZ = 3,       // about Z on a diag qubit (dq 0)
+    GK_GENERIC = 4,  // per slot: Re<lam| dU_s |psi'> with psi' = U^dag psi (dU after U's matrix)
+};
+
+struct FOp {
+    uint8_t kind;
+    uint8_t rb0, rb1;        // register bits of the targets (FK_M2/RX/RY/M4)
+    uint8_t gkind;           // adjoint passes only
+    uint8_t dq_in_tile[2];   // FK_D1/FK_D2: qubit lies in the tile
+    uint8_t dq_pos[2];       // tile-local bit if in the tile, else global position
+    uint16_t lcmask;         // controls inside the tile (tile-local bits)
+    uint16_t nslots;         // GK_GENERIC: number of slots
+    uint32_t moff;           // offset of the op's matrices in the pass matrix table
+    uint32_t acc[3];         // pass-local accumulator index per slot
+    uint32_t pad0;
+    uint64_t gcmask;         // controls outside the tile (global positions)
+    uint32_t pad[6];
+};
+static_assert(sizeof(FOp) == 64, "FOp layout");
+
+struct SubBlock {
+    uint8_t R[4];            // register bits (tile-local), ascending; RB of them are used
+    uint8_t perm[12];        // thread bit i -> tile-local bit perm[i] (the bits not in R)
+    uint16_t op_begin, op_end;
+    uint32_t pad;
+};
+static_assert(sizeof(SubBlock) == 24, "SubBlock layout");
+
+struct PassHeader {
+    uint32_t k;              // tile bits
+    uint32_t nsub;
+    uint32_t nops;
+    uint32_t nmat;           // double2 entries
+    uint32_t nacc;           // accumulators used (adjoint)
+    uint32_t acc_base;       // first global accumulator row of this pass
+    uint32_t rb;             // register bits per thread (3 or 4)
+    uint32_t pad0;
+    uint8_t S[16];           // tile bit -> global qubit
+};
+static_assert(sizeof(PassHeader) == 48, "PassHeader layout");
+
+}  // namespace arcqml

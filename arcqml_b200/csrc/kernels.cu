@@ -199,7 +199,8 @@ __global__ void __launch_bounds__(kThreads) k_adjoint(double2 *__restrict__ psi,
                                                       double2 *__restrict__ lam, uint64_t total,
                                                       uint32_t n, uint32_t glog,
                                                       const __grid_constant__ AdjArgs A,
-                                                      double *__restrict__ partials) {
+                                                      double *__restrict__ partials,
+                                                      uint32_t partial_stride) {
     constexpr int D = 1 << NT;
     __shared__ double s_red[kThreads / 32];
     const uint64_t gmask = (uint64_t(1) << glog) - 1;
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(kThreads) k_adjoint(double2 *__restrict__ psi,
     }
     for (int s = 0; s < A.ns; ++s) {
         const double r = block_sum(acc[s], s_red);
-        if (threadIdx.x == 0) partials[size_t(s) * gridDim.x + blockIdx.x] = r;
+        if (threadIdx.x == 0) partials[size_t(s) * partial_stride + blockIdx.x] = r;
     }
 }
 
@@ -375,11 +376,6 @@ unsigned grid_for(uint64_t items) {
     return unsigned(need < 1 ? 1 : (need < cap ? need : cap));
 }
 
-uint32_t ilog2(uint64_t x) {
-    uint32_t r = 0;
-    while ((uint64_t(1) << r) < x) ++r;
-    return r;
-}
 
 }  // namespace
 
@@ -419,10 +415,12 @@ void launch_gate_out(const double2 *in, double2 *out, size_t batch, uint32_t n,
     check_cuda(cudaGetLastError(), "derivative kernel launch");
 }
 
-// Returns the number of blocks; partials receives [slot][block].
+// Returns the number of blocks; partials receives [slot][block] with a row stride of
+// adjoint_max_blocks() (the reduction reads whole rows; unused tail entries stay zero).
 unsigned launch_adjoint_raw(double2 *psi, double2 *lam, size_t batch, uint32_t n,
                             const DevGate &uadj, const double2 (*d)[16], int ns,
                             double *partials, cudaStream_t s) {
+    const uint32_t stride = uint32_t(num_sms()) * 8;
     AdjArgs A;
     std::memset(&A, 0, sizeof(A));
     A.u = uadj;
@@ -434,9 +432,9 @@ unsigned launch_adjoint_raw(double2 *psi, double2 *lam, size_t batch, uint32_t n
     const uint64_t total = uint64_t(batch) << glog;
     const unsigned blocks = grid_for(total);
     if (uadj.kind == KIND_1Q)
-        k_adjoint<1><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials);
+        k_adjoint<1><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials, stride);
     else if (uadj.kind == KIND_2Q)
-        k_adjoint<2><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials);
+        k_adjoint<2><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials, stride);
     else
         fail("internal: adjoint step needs a dense small form");
     check_cuda(cudaGetLastError(), "adjoint kernel launch");

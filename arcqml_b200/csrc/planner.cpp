@@ -1,0 +1,302 @@
+// planner.cpp — partitions a gate sequence into fused passes (see fused.h).
+//
+// Greedy, order-preserving: a pass picks its tile qubits S (qubits 0..L-1 plus the first
+// non-diagonal targets met in circuit order) and takes every gate it can, in order, whose
+// non-diagonal targets lie in S and that does not need to move past a gate it left behind
+// (a gate sharing a qubit with a skipped gate is skipped too, so the relative order of all gates
+// on any qubit is kept). Inside a pass, consecutive gates are grouped into sub-blocks whose
+// non-diagonal targets fit in RB register bits. Custom gates on more than two targets cannot be
+// fused and run as separate per-gate kernels between passes.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "fused.h"
+#include "planner.h"
+#include "rt_internal.h"
+
+namespace arcqml {
+
+namespace {
+
+bool is_diag(const std::vector<double2> &m, size_t dim) {
+    for (size_t i = 0; i < dim; ++i)
+        for (size_t j = 0; j < dim; ++j)
+            if (i != j && (m[i * dim + j].x != 0.0 || m[i * dim + j].y != 0.0)) return false;
+    return true;
+}
+
+bool eq(double2 a, double2 b) { return a.x == b.x && a.y == b.y; }
+
+// One gate in kernel-ready small form, with its planning footprint.
+struct PGate {
+    const OpRecord *op = nullptr;
+    bool dense_barrier = false;        // arity > 2 custom: per-gate kernel
+    std::vector<uint32_t> controls;
+    std::vector<uint32_t> targets;
+    std::vector<double2> m;            // (2^nt)^2, U or U^dagger
+    bool diag = false;
+    uint64_t touched = 0;              // every qubit of the gate
+    uint64_t needs = 0;                // non-diagonal targets (must be in the tile)
+    uint8_t gkind = GK_NONE;           // adjoint
+    std::vector<std::vector<double2>> dm;  // generic slots: dU in small form
+    std::vector<size_t> parents;           // per required slot
+};
+
+PGate make_pgate(const OpRecord &op, bool adjoint, const uint8_t *req, bool grads) {
+    PGate g;
+    g.op = &op;
+    for (uint32_t q : op.qubits) g.touched |= uint64_t(1) << q;
+    if (op.opcode == ARCQML_OP_CUSTOM_UNITARY && op.qubits.size() > 2) {
+        g.dense_barrier = true;
+        return g;
+    }
+    // allow_diag = false keeps the dense small form: positions = controls + targets.
+    DevGate u = lower(op, adjoint ? LOWER_ADJOINT : LOWER_FORWARD, 0, false);
+    for (int i = 0; i < u.nt; ++i) g.targets.push_back(uint32_t(u.t[i]));
+    for (uint32_t q = 0; q < 64; ++q)
+        if ((u.cmask >> q) & 1) g.controls.push_back(q);
+    const size_t dim = size_t(1) << u.nt;
+    g.m.assign(u.m, u.m + dim * dim);
+    g.diag = is_diag(g.m, dim);
+    if (!g.diag)
+        for (uint32_t t : g.targets) g.needs |= uint64_t(1) << t;
+    if (adjoint && grads) {
+        const uint32_t o = op.opcode;
+        std::vector<uint32_t> slots;
+        for (uint32_t b = 0; b < op.num_bindings; ++b)
+            if (req[op.parents[b]]) {
+                slots.push_back(uint32_t(op.slots[b]));
+                g.parents.push_back(op.parents[b]);
+            }
+        if (!slots.empty()) {
+            if (o == ARCQML_OP_RX || o == ARCQML_OP_CRX) g.gkind = GK_PX;
+            else if (o == ARCQML_OP_RY || o == ARCQML_OP_CRY) g.gkind = GK_PY;
+            else if (o == ARCQML_OP_RZ || o == ARCQML_OP_CRZ) g.gkind = GK_PZ;
+            else g.gkind = GK_GENERIC;
+            if (g.gkind == GK_GENERIC)
+                for (uint32_t s : slots) {
+                    DevGate d = lower(op, LOWER_DERIVATIVE, s, false);
+                    g.dm.emplace_back(d.m, d.m + dim * dim);
+                }
+            // X/Y gradients pair amplitudes across the target even when the angle makes the
+            // matrix diagonal (e.g. RX(0)): keep the target in registers.
+            if ((g.gkind == GK_PX || g.gkind == GK_PY) && g.diag) {
+                g.diag = false;
+                for (uint32_t t : g.targets) g.needs |= uint64_t(1) << t;
+            }
+        }
+    }
+    return g;
+}
+
+// Residue of a tile bit under the shared-memory swizzle (fold of 3-bit groups).
+inline int residue(int bit) { return bit % 3; }
+
+}  // namespace
+
+Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
+                        bool grads, uint32_t k, uint32_t rb) {
+    Schedule sch;
+    sch.k = k;
+    sch.rb = rb;
+    // Gates in execution order (reversed and daggered for the adjoint sweep).
+    std::vector<PGate> gates;
+    gates.reserve(plan.ops.size());
+    if (!adjoint) {
+        for (const auto &op : plan.ops) gates.push_back(make_pgate(op, false, req, false));
+    } else {
+        for (size_t i = plan.ops.size(); i-- > 0;)
+            gates.push_back(make_pgate(plan.ops[i], true, req, grads));
+    }
+    const uint32_t L = std::min<uint32_t>(kLowFixed, k);
+    const uint64_t low_mask = (uint64_t(1) << L) - 1;
+
+    std::vector<char> done(gates.size(), 0);
+    size_t first = 0;
+    uint32_t acc_total = 0;
+    while (true) {
+        while (first < gates.size() && done[first]) ++first;
+        if (first >= gates.size()) break;
+        if (gates[first].dense_barrier) {
+            Step st;
+            st.dense_op = gates[first].op;
+            st.is_pass = false;
+            sch.steps.push_back(std::move(st));
+            done[first] = 1;
+            continue;
+        }
+        // --- choose S and collect the pass's gates (first-come greedy)
+        uint64_t S = low_mask;
+        uint32_t free_slots = k - L;
+        uint64_t blocked = 0;
+        std::vector<size_t> members;
+        size_t pass_acc = 0;
+        for (size_t i = first; i < gates.size(); ++i) {
+            if (done[i]) continue;
+            const PGate &g = gates[i];
+            if (pass_acc + g.parents.size() > size_t(kMaxPassAcc)) break;
+            if (g.dense_barrier || (g.touched & blocked)) {
+                blocked |= g.touched;
+                continue;
+            }
+            const uint64_t extra = g.needs & ~S;
+            const uint32_t cnt = uint32_t(__builtin_popcountll(extra));
+            if (cnt <= free_slots) {
+                S |= extra;
+                free_slots -= cnt;
+                members.push_back(i);
+                pass_acc += g.parents.size();
+                if (members.size() >= size_t(kMaxPassOps)) break;
+            } else {
+                blocked |= g.touched;
+            }
+        }
+        // fill S up to k bits with the lowest unused qubits (keeps runs long)
+        for (uint32_t q = 0; q < n && uint32_t(__builtin_popcountll(S)) < k; ++q) S |= uint64_t(1) << q;
+
+        Step st;
+        st.is_pass = true;
+        PassHeader &h = st.header;
+        std::memset(&h, 0, sizeof(h));
+        h.k = k;
+        h.rb = rb;
+        int lpos[64];
+        for (int q = 0; q < 64; ++q) lpos[q] = -1;
+        {
+            uint32_t j = 0;
+            for (uint32_t q = 0; q < n; ++q)
+                if ((S >> q) & 1) {
+                    h.S[j] = uint8_t(q);
+                    lpos[q] = int(j);
+                    ++j;
+                }
+        }
+        // --- sub-blocks (consecutive members whose non-diagonal targets fit in rb bits)
+        std::vector<std::vector<size_t>> subs;
+        std::vector<uint32_t> sub_R;  // bitmask over tile bits
+        {
+            uint32_t R = 0;
+            std::vector<size_t> cur;
+            for (size_t i : members) {
+                uint32_t need = 0;
+                if (!gates[i].diag)
+                    for (uint32_t t : gates[i].targets) need |= 1u << lpos[t];
+                if (uint32_t(__builtin_popcount(R | need)) > rb) {
+                    subs.push_back(cur);
+                    sub_R.push_back(R);
+                    cur.clear();
+                    R = 0;
+                }
+                R |= need;
+                cur.push_back(i);
+            }
+            if (!cur.empty()) {
+                subs.push_back(cur);
+                sub_R.push_back(R);
+            }
+        }
+        // --- emit sub-blocks, ops and matrices
+        for (size_t sb = 0; sb < subs.size(); ++sb) {
+            uint32_t R = sub_R[sb];
+            for (int b = int(k) - 1; b >= 0 && uint32_t(__builtin_popcount(R)) < rb; --b)
+                R |= 1u << b;  // pad to exactly rb register bits
+            SubBlock s;
+            std::memset(&s, 0, sizeof(s));
+            int ri = 0;
+            for (uint32_t b = 0; b < k; ++b)
+                if ((R >> b) & 1) s.R[ri++] = uint8_t(b);
+            // thread bits: three lane bits with distinct swizzle residues first, then the rest
+            std::vector<int> rest;
+            for (uint32_t b = 0; b < k; ++b)
+                if (!((R >> b) & 1)) rest.push_back(int(b));
+            std::vector<int> order;
+            bool used_res[3] = {false, false, false};
+            for (int want = 0; want < 3; ++want)
+                for (size_t i = 0; i < rest.size(); ++i) {
+                    const int b = rest[i];
+                    if (b < 0 || used_res[residue(b)]) continue;
+                    used_res[residue(b)] = true;
+                    order.push_back(b);
+                    rest[i] = -1;
+                    break;
+                }
+            for (int b : rest)
+                if (b >= 0) order.push_back(b);
+            for (size_t i = 0; i < order.size(); ++i) s.perm[i] = uint8_t(order[i]);
+            s.op_begin = uint16_t(st.ops.size());
+            auto reg_of = [&](uint32_t q) -> uint8_t {
+                const int lp = lpos[q];
+                for (int r = 0; r < int(rb); ++r)
+                    if (s.R[r] == lp) return uint8_t(r);
+                return 0xFF;
+            };
+            for (size_t gi : subs[sb]) {
+                const PGate &g = gates[gi];
+                FOp o;
+                std::memset(&o, 0, sizeof(o));
+                for (uint32_t c : g.controls) {
+                    if (lpos[c] >= 0) o.lcmask |= uint16_t(1u << lpos[c]);
+                    else o.gcmask |= uint64_t(1) << c;
+                }
+                o.moff = uint32_t(st.mats.size());
+                const size_t nt = g.targets.size();
+                if (g.diag) {
+                    o.kind = nt == 1 ? FK_D1 : FK_D2;
+                    for (size_t t = 0; t < nt; ++t) {
+                        const uint32_t q = g.targets[t];
+                        o.dq_in_tile[t] = lpos[q] >= 0 ? 1 : 0;
+                        o.dq_pos[t] = uint8_t(lpos[q] >= 0 ? lpos[q] : int(q));
+                    }
+                    const size_t dim = size_t(1) << nt;
+                    for (size_t i = 0; i < dim; ++i) st.mats.push_back(g.m[i * dim + i]);
+                } else if (nt == 1) {
+                    o.rb0 = reg_of(g.targets[0]);
+                    const double2 *m = g.m.data();
+                    const bool same_diag = eq(m[0], m[3]) && m[0].y == 0.0;
+                    if (same_diag && m[1].x == 0.0 && eq(m[1], m[2])) {
+                        o.kind = FK_RX;  // [[c, -is], [-is, c]] with m01 = (0, -s)
+                        st.mats.push_back(make_double2(m[0].x, -m[1].y));
+                    } else if (same_diag && m[1].y == 0.0 && m[2].y == 0.0 && m[1].x == -m[2].x) {
+                        o.kind = FK_RY;  // [[c, -s], [s, c]]
+                        st.mats.push_back(make_double2(m[0].x, m[2].x));
+                    } else {
+                        o.kind = FK_M2;
+                        for (int i = 0; i < 4; ++i) st.mats.push_back(m[i]);
+                    }
+                } else {
+                    o.kind = FK_M4;
+                    o.rb0 = reg_of(g.targets[0]);
+                    o.rb1 = reg_of(g.targets[1]);
+                    for (int i = 0; i < 16; ++i) st.mats.push_back(g.m[i]);
+                }
+                o.gkind = g.gkind;
+                if (g.gkind != GK_NONE) {
+                    o.nslots = uint16_t(g.parents.size());
+                    if (g.gkind == GK_GENERIC)
+                        for (const auto &d : g.dm)
+                            for (const auto &x : d) st.mats.push_back(x);
+                    for (size_t s2 = 0; s2 < g.parents.size(); ++s2) {
+                        o.acc[s2] = uint32_t(st.parents.size());
+                        st.parents.push_back(g.parents[s2]);
+                    }
+                }
+                st.ops.push_back(o);
+            }
+            s.op_end = uint16_t(st.ops.size());
+            st.subs.push_back(s);
+        }
+        h.nsub = uint32_t(st.subs.size());
+        h.nops = uint32_t(st.ops.size());
+        h.nmat = uint32_t(st.mats.size());
+        h.nacc = uint32_t(st.parents.size());
+        h.acc_base = acc_total;
+        acc_total += h.nacc;
+        for (size_t i : members) done[i] = 1;
+        sch.steps.push_back(std::move(st));
+    }
+    sch.total_acc = acc_total;
+    return sch;
+}
+
+}  // namespace arcqml

@@ -1,0 +1,40 @@
+// planner.h — fused-pass schedules built from a plan (host side).
+#pragma once
+
+#include <vector>
+
+#include "fused.h"
+#include "rt_internal.h"
+
+namespace arcqml {
+
+struct Step {
+    bool is_pass = true;
+    const OpRecord *dense_op = nullptr;  // !is_pass: a custom gate on > 2 targets
+    PassHeader header{};
+    std::vector<SubBlock> subs;
+    std::vector<FOp> ops;
+    std::vector<double2> mats;
+    std::vector<size_t> parents;         // per accumulator of the pass (adjoint)
+};
+
+struct Schedule {
+    uint32_t k = 0, rb = 0;
+    std::vector<Step> steps;
+    uint32_t total_acc = 0;
+};
+
+// Forward (adjoint = false) or reverse-daggered (adjoint = true) schedule of the plan's gates
+// for an n-qubit state, with tiles of k qubits and rb register bits per thread. With grads,
+// every bound slot whose parent has req[parent] != 0 gets an accumulator.
+Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
+                        bool grads, uint32_t k, uint32_t rb);
+
+// Runs a schedule on device states (fused.cu). psi/lam are [batch, 2^n]; lam is null in
+// forward mode. Accumulator partials go to partials[acc * partial_stride + block].
+void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch, uint32_t n,
+                  double *partials, uint32_t partial_stride, ThreadContext &ctx, cudaStream_t s);
+// Persistent grid size of the fused kernels (resident CTAs on the current device).
+uint32_t fused_grid_blocks(bool adjoint);
+
+}  // namespace arcqml

@@ -121,8 +121,8 @@ struct Observable {
 struct ThreadContext {
     int device = -1;
     cudaStream_t stream = nullptr;
-    void *buf[4] = {nullptr, nullptr, nullptr, nullptr};  // 0-2: states, 3: tables
-    size_t cap[4] = {0, 0, 0, 0};
+    void *buf[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // 0-2: states, 3: tables,
+    size_t cap[5] = {0, 0, 0, 0, 0};                               // 4: fused-pass tables
     double *partials = nullptr;  // block partial sums
     size_t partials_cap = 0;     // in doubles
     double *dgrads = nullptr;    // gradient accumulators
