@@ -3,6 +3,7 @@
 //
 // Every entry point converts C++ failures into a non-zero status plus a thread-local
 // message; nothing throws or aborts across the boundary.
+#include <algorithm>
 #include <cmath>
 #include <new>
 #include <sstream>
@@ -10,6 +11,8 @@
 #include "../../include/arcqml_runtime.h"
 #include "../../include/arcqml_runtime_v2.h"
 #include "launch.h"
+#include "planner.h"
+#include "profile.h"
 #include "rt_internal.h"
 
 using namespace arcqml;
@@ -536,6 +539,52 @@ size_t arcqml_rt_v2_plan_len(const CircuitPlanHandle *plan) {
     if (!plan || !plan->opaque) return 0;
     return static_cast<const Plan *>(plan->opaque)->ops.size();
 }
+
+int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t num_qubits,
+                                         int32_t adjoint, uint64_t *passes, uint64_t *sub_blocks,
+                                         uint64_t *gates) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        state_dimension(num_qubits);
+        if (!passes || !sub_blocks || !gates) fail("output pointer is null");
+        validate_plan_for_state(*p, uint32_t(num_qubits));
+        const uint32_t need = adjoint ? 11 : 12;
+        if (num_qubits < need) {
+            *passes = p->ops.size();
+            *sub_blocks = p->ops.size();
+            *gates = p->ops.size();
+            return;
+        }
+        size_t parents = 1;
+        for (const auto &op : p->ops)
+            for (uint32_t b = 0; b < op.num_bindings; ++b)
+                parents = std::max(parents, op.parents[b] + 1);
+        std::vector<uint8_t> req(parents, 1);
+        Schedule sch = build_schedule(*p, uint32_t(num_qubits), adjoint != 0, req.data(),
+                                      adjoint != 0, adjoint ? 11 : 12, adjoint ? 3 : 4);
+        *passes = sch.steps.size();
+        uint64_t sb = 0, g = 0;
+        for (const auto &st : sch.steps) {
+            sb += st.is_pass ? st.subs.size() : 1;
+            g += st.is_pass ? st.ops.size() : 1;
+        }
+        *sub_blocks = sb;
+        *gates = g;
+    });
+}
+
+void arcqml_rt_v2_profile_enable(int32_t on) { prof_enable(on != 0); }
+
+int32_t arcqml_rt_v2_profile_read(uint32_t category, uint64_t *launches, double *total_ms,
+                                  double *algorithmic_bytes) {
+    return guarded([&] {
+        if (category >= uint32_t(kProfCategories)) fail("unknown profile category");
+        if (!launches || !total_ms || !algorithmic_bytes) fail("output pointer is null");
+        prof_read(int(category), launches, total_ms, algorithmic_bytes);
+    });
+}
+
+uint64_t arcqml_rt_v2_launch_count(void) { return prof_launch_count(); }
 
 }  // extern "C"
 #pragma GCC visibility pop

@@ -17,6 +17,7 @@
 #include "fused.h"
 #include "launch.h"
 #include "planner.h"
+#include "profile.h"
 
 namespace arcqml {
 
@@ -638,6 +639,9 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         const auto *ops = reinterpret_cast<const FOp *>(dev + offs[i].ops);
         const auto *mats = reinterpret_cast<const double2 *>(dev + offs[i].mats);
         const unsigned grid = unsigned(total_tiles < blocks ? total_tiles : blocks);
+        // algorithmic traffic: psi (and lambda) read and written once per pass
+        const double bytes = (adj ? 64.0 : 32.0) * double(uint64_t(batch) << n);
+        const ProfToken tok = prof_begin(adj ? PROF_FUSED_ADJ : PROF_FUSED_FWD, s);
         if (adj)
             k_fused<kAdjRB, true><<<grid, kFThreads, smem, s>>>(psi, lam, n, tiles_log, total_tiles,
                                                                hdr, sub, ops, mats, partials,
@@ -646,6 +650,7 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
             k_fused<kFwdRB, false><<<grid, kFThreads, smem, s>>>(psi, nullptr, n, tiles_log,
                                                                 total_tiles, hdr, sub, ops, mats,
                                                                 nullptr, 0);
+        prof_end(tok, s, bytes);
         check_cuda(cudaGetLastError(), "fused pass launch");
     }
 }

@@ -8,6 +8,7 @@
 // Batches [batch, 2^n] are one flat group range: row = counter >> (n - npos).
 #include <cuda_runtime.h>
 
+#include "profile.h"
 #include "rt_internal.h"
 
 namespace arcqml {
@@ -384,6 +385,9 @@ void launch_gate(double2 *amps, size_t batch, uint32_t n, const DevGate &g, cuda
     if (uint32_t(g.npos) > n) fail("internal: gate wider than the state");
     const uint32_t glog = n - uint32_t(g.npos);
     const uint64_t total = uint64_t(batch) << glog;
+    // algorithmic traffic: every touched amplitude is read and written once (16 + 16 bytes)
+    const int per_group = (g.kind == KIND_DIAG1 || g.kind == KIND_DIAG2) ? 1 : (1 << g.nt);
+    const ProfToken tok = prof_begin(PROF_GATE, s);
     switch (g.kind) {
     case KIND_1Q: k_gate_1q<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, glog, g); break;
     case KIND_2Q: k_gate_2q<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, glog, g); break;
@@ -402,6 +406,7 @@ void launch_gate(double2 *amps, size_t batch, uint32_t n, const DevGate &g, cuda
     }
     default: fail("internal: bad gate kind");
     }
+    prof_end(tok, s, 32.0 * double(total) * per_group);
     check_cuda(cudaGetLastError(), "gate kernel launch");
 }
 
@@ -411,7 +416,9 @@ void launch_gate_out(const double2 *in, double2 *out, size_t batch, uint32_t n,
     if (uint32_t(g.nt) > n) fail("internal: gate wider than the state");
     const uint32_t glog = n - uint32_t(g.nt);
     const uint64_t total = uint64_t(batch) << glog;
+    const ProfToken tok = prof_begin(PROF_GATE, s);
     k_gate_out<<<grid_for(total), kThreads, 0, s>>>(in, out, total, n, glog, g);
+    prof_end(tok, s, 32.0 * double(uint64_t(batch) << n));
     check_cuda(cudaGetLastError(), "derivative kernel launch");
 }
 
@@ -431,12 +438,14 @@ unsigned launch_adjoint_raw(double2 *psi, double2 *lam, size_t batch, uint32_t n
     const uint32_t glog = n - uint32_t(uadj.npos);
     const uint64_t total = uint64_t(batch) << glog;
     const unsigned blocks = grid_for(total);
+    if (uadj.kind != KIND_1Q && uadj.kind != KIND_2Q)
+        fail("internal: adjoint step needs a dense small form");
+    const ProfToken tok = prof_begin(PROF_ADJ_STEP, s);
     if (uadj.kind == KIND_1Q)
         k_adjoint<1><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials, stride);
-    else if (uadj.kind == KIND_2Q)
-        k_adjoint<2><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials, stride);
     else
-        fail("internal: adjoint step needs a dense small form");
+        k_adjoint<2><<<blocks, kThreads, 0, s>>>(psi, lam, total, n, glog, A, partials, stride);
+    prof_end(tok, s, 64.0 * double(total) * (1 << uadj.nt));
     check_cuda(cudaGetLastError(), "adjoint kernel launch");
     return blocks;
 }
@@ -446,6 +455,7 @@ unsigned adjoint_max_blocks() { return unsigned(num_sms()) * 8; }
 void launch_reduce_rows(const double *partials, uint32_t rows, uint32_t nblocks, double *sums,
                         cudaStream_t s) {
     if (rows == 0) return;
+    prof_count_launch();
     k_reduce_rows<<<rows, kThreads, 0, s>>>(partials, nblocks, sums);
     check_cuda(cudaGetLastError(), "reduce kernel launch");
 }
@@ -453,13 +463,17 @@ void launch_reduce_rows(const double *partials, uint32_t rows, uint32_t nblocks,
 void launch_scale(double2 *amps, size_t batch, uint32_t n, const double *row_scale_dev,
                   cudaStream_t s) {
     const uint64_t total = uint64_t(batch) << n;
+    const ProfToken tok = prof_begin(PROF_OTHER, s);
     k_scale_rows<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, row_scale_dev);
+    prof_end(tok, s, 32.0 * double(total));
     check_cuda(cudaGetLastError(), "scale kernel launch");
 }
 
 void launch_basis_state(double2 *amps, size_t batch, uint32_t n, uint64_t index, cudaStream_t s) {
     const uint64_t total = uint64_t(batch) << n;
+    const ProfToken tok = prof_begin(PROF_OTHER, s);
     k_basis_state<<<grid_for(total), kThreads, 0, s>>>(amps, total, n, index);
+    prof_end(tok, s, 16.0 * double(total));
     check_cuda(cudaGetLastError(), "basis-state kernel launch");
 }
 
@@ -470,7 +484,9 @@ unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *par
     unsigned bx = grid_for(dim);
     const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);
     if (bx > cap) bx = cap < 1 ? 1 : cap;
+    const ProfToken tok = prof_begin(PROF_OTHER, s);
     k_norms<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(amps, dim, partials);
+    prof_end(tok, s, 16.0 * double(dim) * double(batch));
     check_cuda(cudaGetLastError(), "norm kernel launch");
     return bx;
 }
@@ -484,7 +500,10 @@ unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n
     unsigned bx = grid_for(dim);
     const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);
     if (bx > cap) bx = cap < 1 ? 1 : cap;
+    // algorithmic traffic: read psi once, write H psi once (when requested)
+    const ProfToken tok = prof_begin(PROF_PAULI, s);
     k_pauli<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(psi, out, dim, P, partials);
+    prof_end(tok, s, (out ? 32.0 : 16.0) * double(dim) * double(batch));
     check_cuda(cudaGetLastError(), "observable kernel launch");
     return bx;
 }

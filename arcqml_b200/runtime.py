@@ -124,6 +124,10 @@ def load():
         "arcqml_rt_v2_set_basis_state": (I32, [P, S, S, C.c_uint64, P]),
         "arcqml_rt_v2_plan_set_parameters": (I32, [P, P, S]),
         "arcqml_rt_v2_plan_len": (S, [P]),
+        "arcqml_rt_v2_plan_schedule_stats": (I32, [P, S, I32, P, P, P]),
+        "arcqml_rt_v2_profile_enable": (None, [I32]),
+        "arcqml_rt_v2_profile_read": (I32, [C.c_uint32, P, P, P]),
+        "arcqml_rt_v2_launch_count": (C.c_uint64, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -330,6 +334,14 @@ class CircuitPlan:
     def __len__(self) -> int:
         return load().arcqml_rt_v2_plan_len(C.byref(self.raw))
 
+    def schedule_stats(self, num_qubits: int, adjoint: bool = False) -> dict:
+        """Fused-pass schedule size for an n-qubit state (host only)."""
+        a, b, c = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _status(load().arcqml_rt_v2_plan_schedule_stats(C.byref(self.raw), num_qubits,
+                                                        int(adjoint), C.byref(a), C.byref(b),
+                                                        C.byref(c)))
+        return {"passes": a.value, "sub_blocks": b.value, "gates": c.value}
+
     def __del__(self):
         if _lib is not None and getattr(self, "raw", None) is not None:
             _lib.arcqml_rt_v1_circuit_plan_destroy(C.byref(self.raw))
@@ -445,3 +457,30 @@ def set_basis_state_device(state, num_qubits: int, index: int = 0, stream=None) 
     b = _rows(state, num_qubits)
     _status(load().arcqml_rt_v2_set_basis_state(_dev_ptr(state), b, num_qubits, index,
                                                 _stream_ptr(stream)))
+
+
+# ------------------------------------------------------------------ kernel timing
+
+PROFILE_CATEGORIES = ("gate", "fused_forward", "fused_adjoint", "adjoint_step", "observable",
+                      "other")
+
+
+def profile_enable(on: bool = True) -> None:
+    """Bracket the runtime's kernel launches with CUDA events (resets the totals)."""
+    load().arcqml_rt_v2_profile_enable(int(on))
+
+
+def profile_read() -> dict:
+    """{category: (launches, total_ms, algorithmic_bytes)} since the last profile_enable."""
+    out = {}
+    for i, name in enumerate(PROFILE_CATEGORIES):
+        n = C.c_uint64()
+        ms = C.c_double()
+        by = C.c_double()
+        _status(load().arcqml_rt_v2_profile_read(i, C.byref(n), C.byref(ms), C.byref(by)))
+        out[name] = (int(n.value), float(ms.value), float(by.value))
+    return out
+
+
+def launch_count() -> int:
+    return int(load().arcqml_rt_v2_launch_count())

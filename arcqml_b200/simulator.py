@@ -99,16 +99,27 @@ class RunResult:
 
 
 class StateVectorSimulator:
-    """Single state of ``num_qubits`` qubits, resident on a CUDA device."""
+    """Single state of ``num_qubits`` qubits, resident on a CUDA device.
+
+    The simulator's own state buffer is created on first use: ``run`` on a fresh simulator
+    starts its working copy from |0...0> directly, so a 32-qubit run holds only psi and
+    lambda (2 x 64 GiB) in HBM.
+    """
 
     def __init__(self, num_qubits: int, device=None):
         if num_qubits < 0 or num_qubits >= 40:
             raise SimError(f"state dimension overflow for {num_qubits} qubits")
         self.num_qubits = num_qubits
         self.device = device if device is not None else _torch().device("cuda", _torch().cuda.current_device())
-        self.state = _new_state(num_qubits, None, self.device)
+        self._state = None  # None means |0...0>, not materialised
         self.initial_requires_grad = False
-        self.reset()
+
+    @property
+    def state(self):
+        if self._state is None:
+            self._state = _new_state(self.num_qubits, None, self.device)
+            rt.set_basis_state_device(self._state, self.num_qubits, 0)
+        return self._state
 
     @classmethod
     def from_amplitudes(cls, num_qubits: int, amplitudes, requires_grad: bool = False):
@@ -124,14 +135,14 @@ class StateVectorSimulator:
         return sim
 
     def reset(self) -> None:
-        rt.set_basis_state_device(self.state, self.num_qubits, 0)
+        self._state = None
 
     def amplitudes(self) -> np.ndarray:
         return self.state.cpu().numpy()
 
     def apply_circuit(self, circuit: Circuit) -> None:
         self._check(circuit)
-        plan = rt.CircuitPlan.compile(circuit.compile_plan(0))
+        plan = rt.CircuitPlan.create(circuit.compile_plan(0))
         rt.plan_apply_device(plan, self.state, self.num_qubits)
 
     def expectation(self, observable: SparsePauliOp) -> float:
@@ -141,18 +152,36 @@ class StateVectorSimulator:
     def norm(self) -> float:
         return float(rt.norms_device(self.state, self.num_qubits)[0])
 
-    def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True) -> RunResult:
+    def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True,
+            initial_state=None) -> RunResult:
+        """Expectation of ``observable`` after ``circuit``; ``backward`` gives the gradients.
+
+        ``initial_state`` (optional, a CPU torch tensor or numpy array of 2^n complex128,
+        ideally pinned) replaces the simulator's state as the input of this run; it is copied
+        to the device on the current stream.
+        """
         self._check(circuit)
-        records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
-        psi = self.state.clone()
-        plan = rt.CircuitPlan.compile(circuit.compile_plan(1 if records else 0))
-        rt.plan_apply_device(plan, psi, self.num_qubits)
-        obs = rt.Observable.from_sparse_pauli_op(observable)
         if observable.num_qubits != self.num_qubits:
             raise SimError("observable and state qubit counts differ")
+        torch = _torch()
+        records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
+        psi = _new_state(self.num_qubits, None, self.device)
+        if initial_state is not None:
+            src = initial_state if isinstance(initial_state, torch.Tensor) else torch.from_numpy(
+                np.ascontiguousarray(initial_state, dtype=np.complex128))
+            if src.shape != psi.shape or src.dtype != torch.complex128:
+                raise SimError(f"initial state must be complex128 of shape [{1 << self.num_qubits}]")
+            psi.copy_(src, non_blocking=True)
+        elif self._state is None:
+            rt.set_basis_state_device(psi, self.num_qubits, 0)
+        else:
+            psi.copy_(self._state)
+        plan = rt.CircuitPlan.create(circuit.compile_plan(1 if records else 0))
+        rt.plan_apply_device(plan, psi, self.num_qubits)
+        obs = rt.Observable.from_sparse_pauli_op(observable)
         if not records:
             return RunResult(obs.expectation(psi, self.num_qubits), None)
-        lam = _torch().empty_like(psi)
+        lam = torch.empty_like(psi)
         vals = obs.expectation_and_apply(psi, lam, self.num_qubits)
         return RunResult(vals, _Context(self.num_qubits, None, psi, lam, plan, circuit,
                                         self.initial_requires_grad))
@@ -203,7 +232,7 @@ class BatchStateVectorSimulator:
         return self.state.cpu().numpy()
 
     def apply_circuit(self, circuit: Circuit) -> None:
-        plan = rt.CircuitPlan.compile(circuit.compile_plan(0))
+        plan = rt.CircuitPlan.create(circuit.compile_plan(0))
         rt.plan_apply_device(plan, self.state, self.num_qubits)
 
     def expectation(self, observable: SparsePauliOp) -> np.ndarray:
@@ -214,7 +243,7 @@ class BatchStateVectorSimulator:
             raise SimError("circuit, observable and state qubit counts differ")
         records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
         psi = self.state.clone()
-        plan = rt.CircuitPlan.compile(circuit.compile_plan(1 if records else 0))
+        plan = rt.CircuitPlan.create(circuit.compile_plan(1 if records else 0))
         rt.plan_apply_device(plan, psi, self.num_qubits)
         obs = rt.Observable.from_sparse_pauli_op(observable)
         if not records:

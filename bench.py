@@ -1,0 +1,316 @@
+"""Benchmark: 32-qubit brickwork circuit, forward + <H> + full adjoint gradient on B200.
+
+Workload (one step): |0...0> on 32 qubits (complex128, 64 GiB per state); 20 brickwork layers
+(two random-axis rotations per qubit per layer, CZ on alternating neighbour pairs: 1280
+parameters, 1590 gates); a 200-term random Pauli observable; forward pass, expectation and
+H|psi> in one pass, then the adjoint reverse sweep producing all 1280 parameter gradients.
+Inputs are seeded synthetic data (no dataset). The state (64 GiB) is far larger than L2, so no
+L2 flush is needed between steps.
+
+Reported value: gate passes per second = (gates applied forward + gates un-applied in the
+adjoint sweep) x steps / device time. ``e2e`` times the same step through the public simulator
+API with the initial state copied from pinned host memory every step and the value and
+gradients read back to the host.
+
+``--impl reference`` times the CPU oracle (the f64 restatement of the reference's algorithm;
+the reference's own runtime is a closed Windows library) on the host cores with a bounded
+sample of the same workload (fewer qubits and layers), scaled to 32 qubits by state size.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "gate passes/s (32q 20-layer brickwork forward + adjoint gradient, 200-term <H>)"
+UNIT = "gate_passes/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--qubits", type=int, default=32)
+    ap.add_argument("--layers", type=int, default=20)
+    ap.add_argument("--terms", type=int, default=200)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def workload(n, layers, terms, seed):
+    from arcqml_b200 import workloads
+    c = workloads.brickwork(n, layers, seed=seed)
+    obs = workloads.random_pauli_sum(n, terms, seed=seed + 1)
+    return c, obs
+
+
+def config(args, c):
+    return {"workload": f"{args.qubits}q brickwork x{args.layers} fwd + adjoint, "
+                        f"{args.terms}-term Pauli sum",
+            "qubits": args.qubits, "layers": args.layers, "pauli_terms": args.terms,
+            "gates": len(c.operations), "parameters": c.num_parameters(),
+            "state_bytes": 16 << args.qubits,
+            "l2": "state (16 * 2^n bytes) larger than the 126 MB L2; no flush needed",
+            "parallelism": f"dp1" if args.gpus == 1 else f"replicas{args.gpus}"}
+
+
+# ------------------------------------------------------------------ CPU oracle sample
+
+
+def cpu_sample(args, max_qubits=22, layers=4):
+    """Times the oracle (all host threads) on a bounded sample; returns gate passes/s scaled to
+    args.qubits by state size, plus a description."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    O.build()
+    n = min(max_qubits, args.qubits)
+    layers = min(layers, args.layers)
+    c, obs = workload(n, layers, args.terms, args.seed)
+    ops = c.compile_plan(1)
+    terms = obs.compiled_terms()
+    init = np.zeros(1 << n, np.complex128)
+    init[0] = 1
+    req = c.requires_grad_mask(True)
+    t0 = time.perf_counter()
+    psi = O.plan_apply(ops, init, n)
+    _, lam = O.expectation_and_apply(terms, psi, n)
+    O.adjoint_backward(ops, psi, lam, n, 1.0, req, len(req))
+    dt = time.perf_counter() - t0
+    passes = 2 * len(ops)
+    rate = passes / dt * (2.0 ** (n - args.qubits))
+    sample = (f"oracle on {n} qubits, {layers} layers ({len(ops)} gates) + {args.terms}-term <H>, "
+              f"forward + adjoint in {dt:.1f} s; gate passes/s scaled by 2^({n}-{args.qubits})")
+    return rate, O.num_threads(), sample, dt
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except Exception:  # nvidia-smi missing
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        self.f.close()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": reasons}
+
+
+# ------------------------------------------------------------------ GPU arm
+
+
+def peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return {}
+
+
+def gpu_arm(args):
+    import torch
+    from arcqml_b200 import build, runtime as rt
+    from arcqml_b200.simulator import StateVectorSimulator
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    build.build()
+    rt.load()
+    n = args.qubits
+    c, obs = workload(n, args.layers, args.terms, args.seed)
+    sim = StateVectorSimulator(n)
+    gates = len(c.operations)
+
+    def step(initial=None):
+        res = sim.run(c, obs, initial_state=initial)
+        pgrads, _ = res.backward(1.0)
+        return res.value, pgrads
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    clocks = Clocks(local)
+    rt.profile_enable(True)
+    launches0 = rt.launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        value, grads = step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    launches = rt.launch_count() - launches0
+    prof = rt.profile_read()
+    rt.profile_enable(False)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    passes = 2 * gates
+    value_rate = world * passes * args.steps / (ms / 1e3)
+
+    # dominant kernel category and its roofline
+    dom = max(prof.items(), key=lambda kv: kv[1][1])
+    dname, (dl, dms, dbytes) = dom
+    pk = peaks()
+    hbm = pk.get("hbm_gbs")
+    achieved = (dbytes / dl) / (dms / dl * 1e-3) / 1e9 if dl else 0.0
+    roofline = {"kernel": f"k_fused ({dname})" if dname.startswith("fused") else dname,
+                "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": hbm if hbm else 6650.0, "unit": "GB/s",
+                "peak_source": "measured" if hbm else "fallback",
+                "frac": round(achieved / (hbm if hbm else 6650.0), 4),
+                "bytes_per_launch": dbytes / dl if dl else 0, "avg_launch_ms": dms / dl if dl else 0,
+                "traffic": None}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_arm(args, step, n, world, passes)
+
+    line = {"metric": METRIC, "value": round(value_rate, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "complex128 (f64)", "data": "synthetic (seeded brickwork + random Pauli sum)",
+            "config": config(args, c), "roofline": roofline,
+            "kernels": {k: {"launches": v[0], "ms": round(v[1], 3),
+                            "gbs": round(v[2] / (v[1] * 1e-3) / 1e9, 1) if v[1] else 0}
+                        for k, v in prof.items() if v[0]},
+            "gpu_launches": launches, "e2e": e2e, "clocks": clk,
+            "adjoint_grads_per_s": round(world * args.steps / (ms / 1e3), 5),
+            "param_grads_per_s": round(world * c.num_parameters() * args.steps / (ms / 1e3), 2),
+            "check": {"value": value, "grad_norm": float(np.linalg.norm(grads))}}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, cores, sample, _ = cpu_sample(args)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def e2e_arm(args, step, n, world, passes):
+    import torch
+    try:
+        host = torch.zeros(1 << n, dtype=torch.complex128, pin_memory=True)
+    except Exception as exc:  # pinned host memory unavailable
+        return {"value": None, "unit": UNIT, "unavailable": f"pinned host buffer: {exc}"}
+    host[0] = 1.0
+    step(host)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, grads = step(host)  # value and gradients come back to the host inside step
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([dt], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dt = float(t.item())
+    return {"value": round(world * passes * args.steps / dt, 3), "unit": UNIT,
+            "h2d_bytes_per_step": int(16 << n), "d2h_bytes_per_step": int(8 * (len(grads) + 2)),
+            "path": "StateVectorSimulator.run(initial_state=pinned host) + backward"}
+
+
+# ------------------------------------------------------------------ reference arm
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from arcqml_b200 import workloads  # noqa: F401 (generators only)
+    rates, samples = [], []
+    for _ in range(args.warmup):
+        cpu_sample(args)
+    for _ in range(args.steps):
+        rate, cores, sample, _ = cpu_sample(args)
+        rates.append(rate)
+    value = statistics.median(rates)
+    c, _ = workload(args.qubits, args.layers, args.terms, args.seed)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "complex128 (f64)", "data": "synthetic (seeded brickwork + random Pauli sum)",
+            "config": config(args, c),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference runtime ships only as a closed Windows static library; this arm "
+                    "times the f64 CPU oracle that restates its algorithm"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

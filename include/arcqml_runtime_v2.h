@@ -94,6 +94,28 @@ int32_t arcqml_rt_v2_plan_set_parameters(CircuitPlanHandle *plan, const double *
 /* Number of operations in the plan. */
 size_t arcqml_rt_v2_plan_len(const CircuitPlanHandle *plan);
 
+/* Fused-pass schedule of the plan for an n-qubit state (host only; no reference counterpart).
+ * adjoint != 0 plans the reverse sweep with every bound slot required. Writes the number of
+ * HBM passes, register sub-blocks and fused gates; states below the fused-path size report
+ * one pass per gate. */
+int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t num_qubits,
+                                         int32_t adjoint, uint64_t *passes, uint64_t *sub_blocks,
+                                         uint64_t *gates);
+
+/* Kernel timing (no reference counterpart; measurement support). While enabled, every kernel
+ * launch of the runtime in these categories is bracketed by CUDA events on its own stream:
+ * 0 per-gate kernels, 1 fused forward passes, 2 fused adjoint passes, 3 per-gate adjoint steps,
+ * 4 observable passes, 5 other (scaling, norms, basis states). Enabling (or disabling) resets
+ * the totals. */
+void arcqml_rt_v2_profile_enable(int32_t on);
+/* Totals of one category since the last enable: launches, summed device time (ms) and summed
+ * algorithmic HBM bytes (each touched amplitude read and written once). Waits for pending
+ * events. Returns non-zero for an unknown category. */
+int32_t arcqml_rt_v2_profile_read(uint32_t category, uint64_t *launches, double *total_ms,
+                                  double *algorithmic_bytes);
+/* Kernel launches issued by the runtime since the library was loaded (all categories). */
+uint64_t arcqml_rt_v2_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

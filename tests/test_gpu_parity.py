@@ -245,3 +245,71 @@ def test_brickwork_20q_matches_oracle(runtime, oracle):
     _, _, rgrads = oracle.adjoint_backward(ops, ref_psi, rlam, n, 1.0, req, len(req))
     rel_close(v, rv)
     rel_close(grads, rgrads)
+
+
+def with_bindings(g, ops, num_params):
+    """Binds every parameter slot of the parameterized ops to random parents 1..num_params."""
+    out = []
+    for o in ops:
+        slots = cm.slot_count(o.opcode)
+        binds = tuple((s, int(g.integers(1, num_params + 1))) for s in range(slots))
+        out.append(op(o.opcode, o.qubits, o.params, o.matrix, binds))
+    return out
+
+
+@pytest.mark.parametrize("n", [11, 12, 14])
+def test_fused_passes_with_every_gate_match_oracle(be, oracle, n):
+    """Every opcode, MCX and custom unitaries (3-4 qubit ones run between fused passes) on
+    random qubits, forward and adjoint, at sizes that take the fused-pass path."""
+    g = np.random.Generator(np.random.PCG64(400 + n))
+    ob = OracleBackend(oracle)
+    ops = all_gate_ops(g, n) + all_gate_ops(g, n)
+    g.shuffle(ops)
+    npar = 6
+    ops = with_bindings(g, ops, npar)
+    terms = random_terms(g, n, 30)
+    init = random_state(g, n)
+    req = [0] + [1] * npar
+    res = []
+    for b in (be, ob):
+        psi = b.plan_apply(ops, init, n)
+        v, lam = b.expectation_and_apply(terms, psi, n)
+        psi0, lam0, grads = b.adjoint_backward(ops, psi, lam, n, 0.7, req, npar + 1)
+        res.append((psi, v, lam0, psi0, grads))
+    (p1, v1, l1, a1, g1), (p2, v2, l2, a2, g2) = res
+    assert np.max(np.abs(p1 - p2)) < 1e-12
+    rel_close(v1, v2)
+    rel_close(l1, l2)
+    assert np.max(np.abs(a1 - init)) < 1e-10
+    rel_close(g1, g2)
+
+
+def test_fused_batch_rows_match_oracle(runtime, oracle):
+    """[batch, 2^n] rows through the fused forward and adjoint passes."""
+    import torch
+
+    g = np.random.Generator(np.random.PCG64(12))
+    n, batch, npar = 12, 3, 8
+    ops = random_plan(g, n, 150, npar)
+    terms = random_terms(g, n, 12)
+    init = random_state(g, n, batch)
+    up = g.normal(size=batch)
+    req = np.array([0] + [1] * npar, np.uint8)
+    plan = runtime.CircuitPlan.compile(ops)
+    psi = torch.from_numpy(init.copy()).cuda()
+    runtime.plan_apply_device(plan, psi, n)
+    c = np.array([t[0] for t in terms]); f = np.array([t[1] for t in terms], np.uint64)
+    p = np.array([t[2] for t in terms], np.uint64)
+    obs = runtime.Observable(n, c, f, p)
+    lam = torch.empty_like(psi)
+    vals = obs.expectation_and_apply(psi, lam, n)
+    grads = runtime.adjoint_backward_device(plan, psi, lam, n, up, req, npar + 1)
+    ref_psi = oracle.plan_apply(ops, init, n, batch=batch)
+    ref = [oracle.expectation_and_apply(terms, r, n) for r in ref_psi]
+    ref_lam = np.stack([x[1] for x in ref])
+    _, ref_lam0, ref_grads = oracle.adjoint_backward(ops, ref_psi, ref_lam, n, up, req, npar + 1,
+                                                    batch=batch)
+    rel_close(vals, [x[0] for x in ref])
+    rel_close(grads, ref_grads)
+    rel_close(lam.cpu().numpy(), ref_lam0)
+    assert np.max(np.abs(psi.cpu().numpy() - init)) < 1e-10
