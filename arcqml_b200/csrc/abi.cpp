@@ -548,8 +548,7 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
         state_dimension(num_qubits);
         if (!passes || !sub_blocks || !gates) fail("output pointer is null");
         validate_plan_for_state(*p, uint32_t(num_qubits));
-        const uint32_t need = adjoint ? 11 : 12;
-        if (num_qubits < need) {
+        if (num_qubits < kFusedMinQubits) {
             *passes = p->ops.size();
             *sub_blocks = p->ops.size();
             *gates = p->ops.size();
@@ -560,8 +559,9 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
             for (uint32_t b = 0; b < op.num_bindings; ++b)
                 parents = std::max(parents, op.parents[b] + 1);
         std::vector<uint8_t> req(parents, 1);
+        const uint32_t k = fused_k(uint32_t(num_qubits), adjoint != 0);
         Schedule sch = build_schedule(*p, uint32_t(num_qubits), adjoint != 0, req.data(),
-                                      adjoint != 0, adjoint ? 11 : 12, adjoint ? 3 : 4);
+                                      adjoint != 0, k, fused_rb(k, adjoint != 0));
         *passes = sch.steps.size();
         uint64_t sb = 0, g = 0;
         for (const auto &st : sch.steps) {

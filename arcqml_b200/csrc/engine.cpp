@@ -162,11 +162,8 @@ void validate_plan_for_state(const Plan &plan, uint32_t n) {
     for (const auto &op : plan.ops) check_qubits_for_state(op, n);
 }
 
-// Fused passes are used from these state sizes up (a tile must fit in one state row).
-constexpr uint32_t kFusedForwardMinQubits = 12;
-constexpr uint32_t kFusedAdjointMinQubits = 11;
-
-// ARCQML_FUSE=0 selects the per-gate kernels everywhere (for A/B measurements).
+// ARCQML_FUSE=0 selects the per-gate kernels everywhere (for A/B measurements);
+// ARCQML_FORWARD_RB=3 runs 12-qubit forward tiles with 8 instead of 16 amplitudes per thread.
 bool fusion_enabled() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FUSE");
@@ -175,11 +172,21 @@ bool fusion_enabled() {
     return on;
 }
 
+uint32_t forward_rb(uint32_t k) {
+    static const int forced = [] {
+        const char *e = std::getenv("ARCQML_FORWARD_RB");
+        return e ? std::atoi(e) : 0;
+    }();
+    if (k >= 12 && (forced == 3 || forced == 4)) return uint32_t(forced);
+    return fused_rb(k, false);
+}
+
 void plan_apply_device(Plan &plan, double2 *amps, size_t batch, uint32_t n, ThreadContext &ctx,
                        cudaStream_t s) {
     validate_plan_for_state(plan, n);
-    if (fusion_enabled() && n >= kFusedForwardMinQubits) {
-        Schedule sch = build_schedule(plan, n, false, nullptr, false, 12, 4);
+    if (fusion_enabled() && n >= kFusedMinQubits) {
+        const uint32_t k = fused_k(n, false);
+        Schedule sch = build_schedule(plan, n, false, nullptr, false, k, forward_rb(k));
         run_schedule(sch, amps, nullptr, batch, n, nullptr, 0, ctx, s);
         return;
     }
@@ -244,9 +251,11 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
         // The table buffer is reused below for dense matrices; keep the scale ordered first.
     }
 
-    if (fusion_enabled() && n >= kFusedAdjointMinQubits) {
-        Schedule sch = build_schedule(plan, n, true, req, true, 11, 3);
-        const uint32_t stride = fused_grid_blocks(true);
+    if (fusion_enabled() && n >= kFusedMinQubits) {
+        const uint32_t k = fused_k(n, true);
+        const uint32_t rb = fused_rb(k, true);
+        Schedule sch = build_schedule(plan, n, true, req, true, k, rb);
+        const uint32_t stride = fused_grid_blocks(true, k, rb);
         double *partials = nullptr;
         if (sch.total_acc) {
             partials = ctx_partials(ctx, size_t(sch.total_acc) * stride);

@@ -13,6 +13,8 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "fused.h"
 #include "launch.h"
@@ -23,8 +25,6 @@ namespace arcqml {
 
 namespace {
 
-constexpr int kFThreads = 256;
-constexpr int kWarps = kFThreads / 32;
 
 __device__ __forceinline__ uint32_t phys(uint32_t j) {
     return j ^ (((j >> 3) ^ (j >> 6) ^ (j >> 9)) & 7u);
@@ -50,7 +50,20 @@ __device__ __forceinline__ void load_op(const FOp *src, FOp &dst) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(&dst);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) d[i] = __ldg(s + i);
+    for (int i = 0; i < 4; ++i) d[i] = s[i];
+}
+
+__device__ __forceinline__ double2 ld(const double2 *p) { return *p; }
+
+// 16-byte asynchronous global -> shared copy (LDGSTS); completion via commit/wait groups.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 struct OpEnv {
@@ -72,7 +85,7 @@ __device__ __forceinline__ void apply_1t(uint8_t kind, const double2 *mt, double
                                          const uint32_t (&Le)[1 << RB], const OpEnv &E) {
     constexpr int N = 1 << RB;
     if (kind == FK_RX || kind == FK_RY) {
-        const double2 cs = __ldg(mt);
+        const double2 cs = ld(mt);
         const double c = cs.x, s = cs.y;
 #pragma unroll
         for (int e = 0; e < N; ++e) {
@@ -92,7 +105,7 @@ __device__ __forceinline__ void apply_1t(uint8_t kind, const double2 *mt, double
             v[f] = ok ? y1 : x1;
         }
     } else {  // FK_M2
-        const double2 m0 = __ldg(mt), m1 = __ldg(mt + 1), m2 = __ldg(mt + 2), m3 = __ldg(mt + 3);
+        const double2 m0 = ld(mt), m1 = ld(mt + 1), m2 = ld(mt + 2), m3 = ld(mt + 3);
 #pragma unroll
         for (int e = 0; e < N; ++e) {
             if (e & (1 << B)) continue;
@@ -136,10 +149,10 @@ __device__ __forceinline__ void apply_m4(const double2 *mt, double2 (&v)[1 << RB
         for (int j = 0; j < 4; ++j) x[j] = v[idx[j]];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            double2 acc = cmul(__ldg(mt + i * 4), x[0]);
-            acc = cfma(__ldg(mt + i * 4 + 1), x[1], acc);
-            acc = cfma(__ldg(mt + i * 4 + 2), x[2], acc);
-            acc = cfma(__ldg(mt + i * 4 + 3), x[3], acc);
+            double2 acc = cmul(ld(mt + i * 4), x[0]);
+            acc = cfma(ld(mt + i * 4 + 1), x[1], acc);
+            acc = cfma(ld(mt + i * 4 + 2), x[2], acc);
+            acc = cfma(ld(mt + i * 4 + 3), x[3], acc);
             y[i] = acc;
         }
         const bool ok = ctrl_ok<RB>(E, Le, e);
@@ -188,7 +201,7 @@ __device__ __forceinline__ void apply_diag(const FOp &o, const double2 *mt, doub
                                            const uint32_t (&Le)[1 << RB], const OpEnv &E) {
     constexpr int N = 1 << RB;
     if (o.kind == FK_D1) {
-        const double2 d0 = __ldg(mt), d1 = __ldg(mt + 1);
+        const double2 d0 = ld(mt), d1 = ld(mt + 1);
 #pragma unroll
         for (int e = 0; e < N; ++e) {
             const double2 d = dbit<RB>(o, 0, Le, e, E.gbase) ? d1 : d0;
@@ -196,7 +209,7 @@ __device__ __forceinline__ void apply_diag(const FOp &o, const double2 *mt, doub
             v[e] = ctrl_ok<RB>(E, Le, e) ? y : v[e];
         }
     } else {
-        const double2 d0 = __ldg(mt), d1 = __ldg(mt + 1), d2 = __ldg(mt + 2), d3 = __ldg(mt + 3);
+        const double2 d0 = ld(mt), d1 = ld(mt + 1), d2 = ld(mt + 2), d3 = ld(mt + 3);
 #pragma unroll
         for (int e = 0; e < N; ++e) {
             const uint32_t b = dbit<RB>(o, 0, Le, e, E.gbase) | (dbit<RB>(o, 1, Le, e, E.gbase) << 1);
@@ -277,7 +290,7 @@ __device__ __forceinline__ double grad_m2(const double2 *d, const double2 (&v)[1
                                           const double2 (&w)[1 << RB],
                                           const uint32_t (&Le)[1 << RB], const OpEnv &E) {
     constexpr int N = 1 << RB;
-    const double2 m0 = __ldg(d), m1 = __ldg(d + 1), m2 = __ldg(d + 2), m3 = __ldg(d + 3);
+    const double2 m0 = ld(d), m1 = ld(d + 1), m2 = ld(d + 2), m3 = ld(d + 3);
     double z = 0.0;
 #pragma unroll
     for (int e = 0; e < N; ++e) {
@@ -304,10 +317,10 @@ __device__ __forceinline__ double grad_m4(const double2 *d, const double2 (&v)[1
         double t = 0.0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            double2 acc = cmul(__ldg(d + i * 4), v[idx[0]]);
-            acc = cfma(__ldg(d + i * 4 + 1), v[idx[1]], acc);
-            acc = cfma(__ldg(d + i * 4 + 2), v[idx[2]], acc);
-            acc = cfma(__ldg(d + i * 4 + 3), v[idx[3]], acc);
+            double2 acc = cmul(ld(d + i * 4), v[idx[0]]);
+            acc = cfma(ld(d + i * 4 + 1), v[idx[1]], acc);
+            acc = cfma(ld(d + i * 4 + 2), v[idx[2]], acc);
+            acc = cfma(ld(d + i * 4 + 3), v[idx[3]], acc);
             t += rcm(w[idx[i]], acc);
         }
         z += ctrl_ok<RB>(E, Le, e) ? t : 0.0;
@@ -339,8 +352,8 @@ __device__ __forceinline__ double grad_generic(const FOp &o, const double2 *d,
     if (o.kind == FK_D1 || o.kind == FK_D2) {
         double z = 0.0;
         const bool two = o.kind == FK_D2;
-        const double2 d0 = __ldg(d), d1 = __ldg(d + 1);
-        const double2 d2 = two ? __ldg(d + 2) : d0, d3 = two ? __ldg(d + 3) : d1;
+        const double2 d0 = ld(d), d1 = ld(d + 1);
+        const double2 d2 = two ? ld(d + 2) : d0, d3 = two ? ld(d + 3) : d1;
 #pragma unroll
         for (int e = 0; e < N; ++e) {
             uint32_t b = dbit<RB>(o, 0, Le, e, E.gbase);
@@ -390,66 +403,124 @@ __device__ __forceinline__ int dmat_len(uint8_t kind) {
     }
 }
 
-__device__ __forceinline__ void accumulate(double *sacc, uint32_t acc, double z) {
+// Adds the warp's sum of z into its own column of accumulator row `row` (= acc * nwarps).
+__device__ __forceinline__ void accumulate(double *sacc, uint32_t row, double z) {
     z = warp_sum(z);
-    if ((threadIdx.x & 31) == 0) sacc[acc * kWarps + (threadIdx.x >> 5)] += z;
+    if ((threadIdx.x & 31) == 0) sacc[row + (threadIdx.x >> 5)] += z;
 }
 
 // ---------------------------------------------------------------- the pass kernel
 
+// Shared memory: [tile buffers: 2 x (psi [, lambda])][hioff][accumulators][ops][matrices].
+// While a CTA computes tile i from one buffer, cp.async streams tile i + gridDim into the other.
+struct SmemLayout {
+    uint32_t tile, hioff, sacc, ops, mats, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t nacc,
+                                                  uint32_t nops, uint32_t nmat, uint32_t nwarps) {
+    const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
+    SmemLayout m;
+    m.tile = 0;
+    uint32_t off = (adj ? 4u : 2u) * (16u << k);
+    m.hioff = off;
+    off += 8u << (k - L);
+    m.sacc = off;
+    off += adj ? nacc * nwarps * 8u : 0u;
+    off = (off + 15u) & ~15u;
+    m.ops = off;
+    off += nops * uint32_t(sizeof(FOp));
+    m.mats = off;
+    off += nmat * 16u;
+    m.total = off;
+    return m;
+}
+
 template <int RB, bool ADJ>
-__global__ void __launch_bounds__(kFThreads, ADJ ? 2 : 1)
+__global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
     k_fused(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n, uint32_t tiles_log,
             uint64_t total_tiles, const PassHeader *__restrict__ hdr,
-            const SubBlock *__restrict__ subs, const FOp *__restrict__ ops,
-            const double2 *__restrict__ mats, double *__restrict__ partials, uint32_t stride) {
+            const SubBlock *__restrict__ subs, const FOp *__restrict__ gops,
+            const double2 *__restrict__ gmats, double *__restrict__ partials, uint32_t stride) {
     constexpr int N = 1 << RB;
-    extern __shared__ double2 smem[];
+    extern __shared__ __align__(16) unsigned char smem[];
     __shared__ uint8_t sS[16];
-    __shared__ uint32_t sk, snsub, snacc, sacc_base;
+    __shared__ uint32_t sk, snsub, snacc, sacc_base, snops, snmat;
     if (threadIdx.x < 16) sS[threadIdx.x] = hdr->S[threadIdx.x];
     if (threadIdx.x == 0) {
         sk = hdr->k;
         snsub = hdr->nsub;
         snacc = hdr->nacc;
         sacc_base = hdr->acc_base;
+        snops = hdr->nops;
+        snmat = hdr->nmat;
     }
     __syncthreads();
     const uint32_t k = sk;
     const uint32_t D = 1u << k;
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     const uint32_t lowmask = (1u << L) - 1;
-    double2 *tp = smem;
-    double2 *tl = smem + (ADJ ? D : 0);
-    uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + (ADJ ? 2 * D : D));
-    double *sacc = reinterpret_cast<double *>(hioff + (1u << (k - L)));
-    for (uint32_t h = threadIdx.x; h < (1u << (k - L)); h += kFThreads) {
+    const uint32_t nwarps = blockDim.x >> 5;
+    const SmemLayout lay = smem_layout(ADJ, k, snacc, snops, snmat, nwarps);
+    double2 *bufs = reinterpret_cast<double2 *>(smem + lay.tile);
+    uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + lay.hioff);
+    double *sacc = reinterpret_cast<double *>(smem + lay.sacc);
+    FOp *ops = reinterpret_cast<FOp *>(smem + lay.ops);
+    double2 *mats = reinterpret_cast<double2 *>(smem + lay.mats);
+    // buffer b, state s (0 = psi, 1 = lambda)
+    auto tile_buf = [&](int b, int st) { return bufs + (size_t(b) * (ADJ ? 2 : 1) + st) * D; };
+
+    for (uint32_t h = threadIdx.x; h < (1u << (k - L)); h += blockDim.x) {
         uint64_t off = 0;
         for (uint32_t b = 0; b < k - L; ++b)
             if ((h >> b) & 1) off |= uint64_t(1) << sS[L + b];
         hioff[h] = off;
     }
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(gops);
+        uint4 *dst = reinterpret_cast<uint4 *>(ops);
+        for (uint32_t i = threadIdx.x; i < snops * 4; i += blockDim.x) dst[i] = src[i];
+        for (uint32_t i = threadIdx.x; i < snmat; i += blockDim.x) mats[i] = gmats[i];
+    }
     if (ADJ)
-        for (uint32_t a = threadIdx.x; a < snacc * kWarps; a += kFThreads) sacc[a] = 0.0;
+        for (uint32_t a = threadIdx.x; a < snacc * nwarps; a += blockDim.x) sacc[a] = 0.0;
     __syncthreads();
 
     const uint64_t tmask = (uint64_t(1) << tiles_log) - 1;
-    for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x) {
-        const uint64_t rowoff = (T >> tiles_log) << n;
-        // global bits of the tile: insert zeros at the (sorted) tile positions
-        uint64_t gbase = T & tmask;
+    auto tile_base = [&](uint64_t T) {
+        uint64_t g = T & tmask;
         for (uint32_t b = 0; b < k; ++b) {
             const uint32_t p = sS[b];
-            gbase = ((gbase >> p) << (p + 1)) | (gbase & ((uint64_t(1) << p) - 1));
+            g = ((g >> p) << (p + 1)) | (g & ((uint64_t(1) << p) - 1));
         }
-        double2 *P = psi + rowoff + gbase;
-        double2 *Lm = ADJ ? lam + rowoff + gbase : nullptr;
-        for (uint32_t j = threadIdx.x; j < D; j += kFThreads) {
+        return g;
+    };
+    auto issue_load = [&](uint64_t T, int b) {
+        const uint64_t off = ((T >> tiles_log) << n) + tile_base(T);
+        const double2 *P = psi + off;
+        const double2 *Lm = ADJ ? lam + off : nullptr;
+        double2 *tp = tile_buf(b, 0);
+        double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
+        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
             const uint64_t g = (j & lowmask) | hioff[j >> L];
-            tp[phys(j)] = P[g];
-            if (ADJ) tl[phys(j)] = Lm[g];
+            cp_async16(tp + phys(j), P + g);
+            if (ADJ) cp_async16(tl + phys(j), Lm + g);
         }
+        cp_async_commit();
+    };
+
+    if (uint64_t(blockIdx.x) < total_tiles) issue_load(blockIdx.x, 0);
+    else cp_async_commit();
+    int b = 0;
+    for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x, b ^= 1) {
+        const uint64_t Tn = T + gridDim.x;
+        if (Tn < total_tiles) issue_load(Tn, b ^ 1);
+        else cp_async_commit();
+        cp_async_wait<1>();
         __syncthreads();
+        const uint64_t gbase = tile_base(T);
+        double2 *tp = tile_buf(b, 0);
+        double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
         for (uint32_t sb = 0; sb < snsub; ++sb) {
             SubBlock S;
             {
@@ -489,9 +560,9 @@ __global__ void __launch_bounds__(kFThreads, ADJ ? 2 : 1)
                 if (ADJ) {
                     if (o.gkind == GK_PX || o.gkind == GK_PY) {
                         const double z = grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
-                        accumulate(sacc, o.acc[0], 0.5 * z);
+                        accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
                     } else if (o.gkind == GK_PZ) {
-                        accumulate(sacc, o.acc[0], 0.5 * grad_z<RB>(o, v, w, Le, E));
+                        accumulate(sacc, o.acc[0] * nwarps, 0.5 * grad_z<RB>(o, v, w, Le, E));
                     }
                 }
                 apply_op<RB>(o, mt, v, Le, E);
@@ -500,7 +571,8 @@ __global__ void __launch_bounds__(kFThreads, ADJ ? 2 : 1)
                         const double2 *d = mt + umat_len(o.kind);
                         const int dl = dmat_len(o.kind);
                         for (int s = 0; s < int(o.nslots); ++s)
-                            accumulate(sacc, o.acc[s], grad_generic<RB>(o, d + s * dl, v, w, Le, E));
+                            accumulate(sacc, o.acc[s] * nwarps,
+                                       grad_generic<RB>(o, d + s * dl, v, w, Le, E));
                     }
                     apply_op<RB>(o, mt, w, Le, E);
                 }
@@ -512,64 +584,79 @@ __global__ void __launch_bounds__(kFThreads, ADJ ? 2 : 1)
             }
             __syncthreads();
         }
-        for (uint32_t j = threadIdx.x; j < D; j += kFThreads) {
-            const uint64_t g = (j & lowmask) | hioff[j >> L];
-            P[g] = tp[phys(j)];
-            if (ADJ) Lm[g] = tl[phys(j)];
+        {
+            const uint64_t off = ((T >> tiles_log) << n) + gbase;
+            double2 *P = psi + off;
+            double2 *Lm = ADJ ? lam + off : nullptr;
+            for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
+                const uint64_t g = (j & lowmask) | hioff[j >> L];
+                P[g] = tp[phys(j)];
+                if (ADJ) Lm[g] = tl[phys(j)];
+            }
         }
         __syncthreads();
     }
+    cp_async_wait<0>();
     if (ADJ) {
-        for (uint32_t a = threadIdx.x; a < snacc; a += kFThreads) {
+        for (uint32_t a = threadIdx.x; a < snacc; a += blockDim.x) {
             double s = 0.0;
-#pragma unroll
-            for (int wi = 0; wi < kWarps; ++wi) s += sacc[a * kWarps + wi];
+            for (uint32_t wi = 0; wi < nwarps; ++wi) s += sacc[a * nwarps + wi];
             partials[size_t(sacc_base + a) * stride + blockIdx.x] = s;
         }
     }
 }
 
-constexpr int kFwdRB = 4;   // forward: 16 amplitudes per thread, k = 12
-constexpr int kAdjRB = 3;   // adjoint: 8 + 8 amplitudes per thread, k = 11
-
-size_t fused_smem(bool adj, uint32_t k, uint32_t nacc) {
-    const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
-    size_t b = (adj ? 2 : 1) * (size_t(16) << k) + (size_t(8) << (k - L));
-    if (adj) b += size_t(nacc) * kWarps * 8;
-    return b;
+size_t fused_smem(bool adj, uint32_t k, uint32_t nacc, uint32_t nops, uint32_t nmat,
+                  uint32_t threads) {
+    return smem_layout(adj, k, nacc, nops, nmat, threads / 32).total;
 }
 
-int g_blocks_fwd = 0, g_blocks_adj = 0;
+using FusedKernel = void (*)(double2 *, double2 *, uint32_t, uint32_t, uint64_t,
+                             const PassHeader *, const SubBlock *, const FOp *, const double2 *,
+                             double *, uint32_t);
+
+FusedKernel fused_kernel(bool adj, uint32_t rb) {
+    if (adj) return k_fused<3, true>;
+    return rb == 4 ? k_fused<4, false> : k_fused<3, false>;
+}
+
+// Resident CTAs per device for each (adjoint, k, rb) launch shape, computed once.
+struct GridKey {
+    int dev;
+    bool adj;
+    uint32_t k, rb;
+};
+std::mutex g_grid_mu;
+std::vector<std::pair<GridKey, uint32_t>> g_grid;
 
 }  // namespace
 
-uint32_t fused_grid_blocks(bool adjoint) {
-    int &cache = adjoint ? g_blocks_adj : g_blocks_fwd;
-    if (cache == 0) {
-        int dev = 0, sms = 0;
-        check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
-        check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
-                   "cudaDeviceGetAttribute");
-        const size_t smem = adjoint ? fused_smem(true, 11, kMaxPassAcc) : fused_smem(false, 12, 0);
-        int per_sm = 0;
-        if (adjoint) {
-            check_cuda(cudaFuncSetAttribute(k_fused<kAdjRB, true>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                       "cudaFuncSetAttribute");
-            check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused<kAdjRB, true>,
-                                                                     kFThreads, smem),
-                       "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-        } else {
-            check_cuda(cudaFuncSetAttribute(k_fused<kFwdRB, false>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                       "cudaFuncSetAttribute");
-            check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_fused<kFwdRB, false>,
-                                                                     kFThreads, smem),
-                       "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-        }
-        cache = sms * (per_sm < 1 ? 1 : per_sm);
-    }
-    return uint32_t(cache);
+uint32_t fused_threads(uint32_t k, uint32_t rb) { return 1u << (k - rb); }
+
+uint32_t fused_grid_blocks(bool adjoint, uint32_t k, uint32_t rb) {
+    int dev = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    std::lock_guard<std::mutex> lock(g_grid_mu);
+    for (const auto &e : g_grid)
+        if (e.first.dev == dev && e.first.adj == adjoint && e.first.k == k && e.first.rb == rb)
+            return e.second;
+    int sms = 0;
+    check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
+               "cudaDeviceGetAttribute");
+    // occupancy for the largest pass the planner emits (its tables are capped)
+    const size_t smem = fused_smem(adjoint, k, adjoint ? kMaxPassAcc : 0, kMaxPassOps, kMaxPassMats,
+                                   fused_threads(k, rb));
+    if (smem > 227 * 1024) fail("internal: fused pass shared memory exceeds 227 KB");
+    FusedKernel kern = fused_kernel(adjoint, rb);
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+               "cudaFuncSetAttribute");
+    int per_sm = 0;
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern,
+                                                             int(fused_threads(k, rb)), smem),
+               "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    const uint32_t blocks = uint32_t(sms * (per_sm < 1 ? 1 : per_sm));
+    g_grid.push_back({GridKey{dev, adjoint, k, rb}, blocks});
+    return blocks;
 }
 
 void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch, uint32_t n,
@@ -611,7 +698,6 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         check_cuda(cudaMemcpyAsync(dev, blob.data(), total, cudaMemcpyHostToDevice, s),
                    "cudaMemcpyAsync (pass tables)");
     }
-    const uint32_t blocks = fused_grid_blocks(adj);
     for (size_t i = 0; i < sch.steps.size(); ++i) {
         const auto &st = sch.steps[i];
         if (!st.is_pass) {
@@ -633,23 +719,21 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         const uint32_t k = st.header.k;
         const uint32_t tiles_log = n - k;
         const uint64_t total_tiles = uint64_t(batch) << tiles_log;
-        const size_t smem = fused_smem(adj, k, st.header.nacc);
+        const size_t smem = fused_smem(adj, k, st.header.nacc, st.header.nops, st.header.nmat,
+                                       fused_threads(k, st.header.rb));
         const auto *hdr = reinterpret_cast<const PassHeader *>(dev + offs[i].hdr);
         const auto *sub = reinterpret_cast<const SubBlock *>(dev + offs[i].subs);
         const auto *ops = reinterpret_cast<const FOp *>(dev + offs[i].ops);
         const auto *mats = reinterpret_cast<const double2 *>(dev + offs[i].mats);
+        const uint32_t blocks = fused_grid_blocks(adj, k, st.header.rb);
+        if (adj && blocks > partial_stride) fail("internal: accumulator stride below the grid size");
         const unsigned grid = unsigned(total_tiles < blocks ? total_tiles : blocks);
         // algorithmic traffic: psi (and lambda) read and written once per pass
         const double bytes = (adj ? 64.0 : 32.0) * double(uint64_t(batch) << n);
         const ProfToken tok = prof_begin(adj ? PROF_FUSED_ADJ : PROF_FUSED_FWD, s);
-        if (adj)
-            k_fused<kAdjRB, true><<<grid, kFThreads, smem, s>>>(psi, lam, n, tiles_log, total_tiles,
-                                                               hdr, sub, ops, mats, partials,
-                                                               partial_stride);
-        else
-            k_fused<kFwdRB, false><<<grid, kFThreads, smem, s>>>(psi, nullptr, n, tiles_log,
-                                                                total_tiles, hdr, sub, ops, mats,
-                                                                nullptr, 0);
+        fused_kernel(adj, st.header.rb)<<<grid, fused_threads(k, st.header.rb), smem, s>>>(
+            psi, adj ? lam : nullptr, n, tiles_log, total_tiles, hdr, sub, ops, mats,
+            adj ? partials : nullptr, adj ? partial_stride : 0);
         prof_end(tok, s, bytes);
         check_cuda(cudaGetLastError(), "fused pass launch");
     }

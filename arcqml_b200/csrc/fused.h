@@ -20,7 +20,8 @@ namespace arcqml {
 
 constexpr int kTileMax = 12;       // tile qubits
 constexpr int kLowFixed = 4;       // S always holds qubits 0..kLowFixed-1 (256-byte runs)
-constexpr int kMaxPassOps = 512;   // fused ops per pass
+constexpr int kMaxPassOps = 256;   // fused ops per pass (staged in shared memory)
+constexpr int kMaxPassMats = 1536; // matrix-table entries (double2) per pass
 constexpr int kMaxPassAcc = 256;   // gradient accumulators per pass
 
 enum FusedKind : uint8_t {

@@ -78,6 +78,12 @@ PGate make_pgate(const OpRecord &op, bool adjoint, const uint8_t *req, bool grad
                 for (uint32_t s : slots) {
                     DevGate d = lower(op, LOWER_DERIVATIVE, s, false);
                     g.dm.emplace_back(d.m, d.m + dim * dim);
+                    // U can be diagonal at particular angles (U3(0, f, l), fSim(0, f), RXX(0))
+                    // while its derivative is not: then the targets must sit in registers
+                    if (g.diag && !is_diag(g.dm.back(), dim)) {
+                        g.diag = false;
+                        for (uint32_t t : g.targets) g.needs |= uint64_t(1) << t;
+                    }
                 }
             // X/Y gradients pair amplitudes across the target even when the angle makes the
             // matrix diagonal (e.g. RX(0)): keep the target in registers.
@@ -88,6 +94,13 @@ PGate make_pgate(const OpRecord &op, bool adjoint, const uint8_t *req, bool grad
         }
     }
     return g;
+}
+
+// Upper bound of the matrix-table entries a gate adds to its pass.
+size_t mat_entries(const PGate &g) {
+    const size_t dim = size_t(1) << g.targets.size();
+    const size_t per = g.diag ? dim : dim * dim;
+    return per * (1 + g.dm.size());
 }
 
 // Residue of a tile bit under the shared-memory swizzle (fold of 3-bit groups).
@@ -132,10 +145,12 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         uint64_t blocked = 0;
         std::vector<size_t> members;
         size_t pass_acc = 0;
+        size_t pass_mats = 0;
         for (size_t i = first; i < gates.size(); ++i) {
             if (done[i]) continue;
             const PGate &g = gates[i];
             if (pass_acc + g.parents.size() > size_t(kMaxPassAcc)) break;
+            if (pass_mats + mat_entries(g) > size_t(kMaxPassMats)) break;
             if (g.dense_barrier || (g.touched & blocked)) {
                 blocked |= g.touched;
                 continue;
@@ -147,6 +162,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 free_slots -= cnt;
                 members.push_back(i);
                 pass_acc += g.parents.size();
+                pass_mats += mat_entries(g);
                 if (members.size() >= size_t(kMaxPassOps)) break;
             } else {
                 blocked |= g.touched;
@@ -273,9 +289,17 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 o.gkind = g.gkind;
                 if (g.gkind != GK_NONE) {
                     o.nslots = uint16_t(g.parents.size());
-                    if (g.gkind == GK_GENERIC)
-                        for (const auto &d : g.dm)
-                            for (const auto &x : d) st.mats.push_back(x);
+                    if (g.gkind == GK_GENERIC) {
+                        // a diagonal gate's derivative is diagonal: store its diagonal only,
+                        // in the same layout as the gate's own phases
+                        const size_t dim = size_t(1) << nt;
+                        for (const auto &d : g.dm) {
+                            if (g.diag)
+                                for (size_t i = 0; i < dim; ++i) st.mats.push_back(d[i * dim + i]);
+                            else
+                                for (const auto &x : d) st.mats.push_back(x);
+                        }
+                    }
                     for (size_t s2 = 0; s2 < g.parents.size(); ++s2) {
                         o.acc[s2] = uint32_t(st.parents.size());
                         st.parents.push_back(g.parents[s2]);

@@ -34,7 +34,18 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
 // forward mode. Accumulator partials go to partials[acc * partial_stride + block].
 void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch, uint32_t n,
                   double *partials, uint32_t partial_stride, ThreadContext &ctx, cudaStream_t s);
-// Persistent grid size of the fused kernels (resident CTAs on the current device).
-uint32_t fused_grid_blocks(bool adjoint);
+// Persistent grid size of the fused kernel for tiles of k qubits with rb register bits
+// (resident CTAs on the current device), and its block size 2^(k - rb).
+uint32_t fused_grid_blocks(bool adjoint, uint32_t k, uint32_t rb);
+uint32_t fused_threads(uint32_t k, uint32_t rb);
+
+// Tile shape the engine uses for an n-qubit state: forward k = min(n, 12) with 4 register bits
+// at k = 12 (3 below), adjoint k = min(n, 11) with 3. Fused passes need n >= 8 (a full warp).
+constexpr uint32_t kFusedMinQubits = 8;
+inline uint32_t fused_k(uint32_t n, bool adjoint) {
+    const uint32_t cap = adjoint ? 11u : 12u;
+    return n < cap ? n : cap;
+}
+inline uint32_t fused_rb(uint32_t k, bool adjoint) { return (!adjoint && k >= 12) ? 4u : 3u; }
 
 }  // namespace arcqml
