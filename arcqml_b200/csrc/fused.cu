@@ -409,6 +409,285 @@ __device__ __forceinline__ void accumulate(double *sacc, uint32_t row, double z)
     if ((threadIdx.x & 31) == 0) sacc[row + (threadIdx.x >> 5)] += z;
 }
 
+// ---------------------------------------------------------------- specialised fast paths
+//
+// Uncontrolled gates with compile-time register bits: pure FP64 arithmetic on the thread's
+// registers, no per-element index or control logic. Sign flips (CZ, Z) toggle the sign bit
+// of the high word with an integer XOR instead of using the FP64 pipe.
+
+__device__ __forceinline__ double flip(double x, uint32_t m) {
+    return __hiloint2double(__double2hiint(x) ^ int(m), __double2loint(x));
+}
+__device__ __forceinline__ double2 flip2(double2 a, uint32_t m) {
+    return make_double2(flip(a.x, m), flip(a.y, m));
+}
+
+template <int RB, int B>
+__device__ __forceinline__ void f_rx(double2 (&v)[1 << RB], double c, double s) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        const double2 x0 = v[e], x1 = v[f];
+        v[e] = make_double2(fma(c, x0.x, s * x1.y), fma(c, x0.y, -s * x1.x));
+        v[f] = make_double2(fma(c, x1.x, s * x0.y), fma(c, x1.y, -s * x0.x));
+    }
+}
+
+template <int RB, int B>
+__device__ __forceinline__ void f_ry(double2 (&v)[1 << RB], double c, double s) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        const double2 x0 = v[e], x1 = v[f];
+        v[e] = make_double2(fma(c, x0.x, -s * x1.x), fma(c, x0.y, -s * x1.y));
+        v[f] = make_double2(fma(s, x0.x, c * x1.x), fma(s, x0.y, c * x1.y));
+    }
+}
+
+template <int RB, int B>
+__device__ __forceinline__ void f_m2(double2 (&v)[1 << RB], const double2 *mt) {
+    const double2 m0 = mt[0], m1 = mt[1], m2 = mt[2], m3 = mt[3];
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        const double2 x0 = v[e], x1 = v[f];
+        v[e] = cfma(m0, x0, cmul(m1, x1));
+        v[f] = cfma(m2, x0, cmul(m3, x1));
+    }
+}
+
+template <int RB, int B>
+__device__ __forceinline__ void f_d1_reg(double2 (&v)[1 << RB], double2 d0, double2 d1) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) v[e] = cmul((e >> B) & 1 ? d1 : d0, v[e]);
+}
+
+template <int RB>
+__device__ __forceinline__ void f_d1_uni(double2 (&v)[1 << RB], double2 d) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) v[e] = cmul(d, v[e]);
+}
+
+template <int RB, int B0, int B1>
+__device__ __forceinline__ void f_sign_rr(double2 (&v)[1 << RB]) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e)
+        if (((e >> B0) & 1) && ((e >> B1) & 1)) v[e] = flip2(v[e], 0x80000000u);
+}
+
+template <int RB, int B>
+__device__ __forceinline__ void f_sign_rc(double2 (&v)[1 << RB], uint32_t m) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e)
+        if ((e >> B) & 1) v[e] = flip2(v[e], m);
+}
+
+template <int RB>
+__device__ __forceinline__ void f_sign_cc(double2 (&v)[1 << RB], uint32_t m) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) v[e] = flip2(v[e], m);
+}
+
+template <int RB, int B0, int B1>
+__device__ __forceinline__ void f_m4(double2 (&v)[1 << RB], const double2 *mt) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & ((1 << B0) | (1 << B1))) continue;
+        const int idx[4] = {e, e | (1 << B0), e | (1 << B1), e | (1 << B0) | (1 << B1)};
+        double2 x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = v[idx[j]];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            double2 acc = cmul(mt[i * 4], x[0]);
+            acc = cfma(mt[i * 4 + 1], x[1], acc);
+            acc = cfma(mt[i * 4 + 2], x[2], acc);
+            acc = cfma(mt[i * 4 + 3], x[3], acc);
+            v[idx[i]] = acc;
+        }
+    }
+}
+
+template <int RB, int B>
+__device__ __forceinline__ double g_x(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        z += icm(w[e], v[f]) + icm(w[f], v[e]);
+    }
+    return z;
+}
+
+template <int RB, int B>
+__device__ __forceinline__ double g_y(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        z += rcm(w[f], v[e]) - rcm(w[e], v[f]);
+    }
+    return z;
+}
+
+template <int RB, int B>
+__device__ __forceinline__ double g_z(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        const double t = icm(w[e], v[e]);
+        z += ((e >> B) & 1) ? -t : t;
+    }
+    return z;
+}
+
+template <int RB>
+__device__ __forceinline__ double g_z_uni(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
+    double z = 0.0;
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) z += icm(w[e], v[e]);
+    return z;
+}
+
+// Dispatch a template over a runtime register bit b (< RB).
+#define ARCQML_BITS(b, CALL)                          \
+    switch (b) {                                      \
+    case 0: CALL(0); break;                           \
+    case 1: CALL(1); break;                           \
+    case 2: CALL(2); break;                           \
+    default:                                          \
+        if constexpr (RB > 3) { CALL(3); }            \
+        break;                                        \
+    }
+
+// Per-thread value of a qubit that is not a register bit: a tile bit lives in the thread's
+// base index tb, a qubit outside the tile in the tile's global base.
+__device__ __forceinline__ uint32_t const_bit(const FOp &o, int slot, uint32_t tb, uint64_t gbase) {
+    return o.dq_in_tile[slot] ? ((tb >> o.dq_pos[slot]) & 1u) : uint32_t((gbase >> o.dq_pos[slot]) & 1u);
+}
+
+// Applies op o (U or U^dagger) to the registers through its fast path; false if the op
+// needs the generic path.
+template <int RB>
+__device__ __forceinline__ bool apply_fast(const FOp &o, const double2 *mt, double2 (&v)[1 << RB],
+                                           uint32_t tb, uint64_t gbase) {
+    switch (o.code) {
+    case FC_RX: {
+        const double2 cs = mt[0];
+#define C_(B) f_rx<RB, B>(v, cs.x, cs.y)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_RY: {
+        const double2 cs = mt[0];
+#define C_(B) f_ry<RB, B>(v, cs.x, cs.y)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_M2: {
+#define C_(B) f_m2<RB, B>(v, mt)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_D1_REG: {
+        const double2 d0 = mt[0], d1 = mt[1];
+#define C_(B) f_d1_reg<RB, B>(v, d0, d1)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_D1_UNI:
+        f_d1_uni<RB>(v, const_bit(o, 0, tb, gbase) ? mt[1] : mt[0]);
+        return true;
+    case FC_SIGN_RR: {
+#define C1_(B0, B1) f_sign_rr<RB, B0, B1>(v)
+#define C_(B1)                                 \
+    switch (o.rb0) {                           \
+    case 0: C1_(0, B1); break;                 \
+    case 1: C1_(1, B1); break;                 \
+    case 2: C1_(2, B1); break;                 \
+    default:                                   \
+        if constexpr (RB > 3) { C1_(3, B1); }  \
+        break;                                 \
+    }
+        ARCQML_BITS(o.rb1, C_)
+#undef C_
+#undef C1_
+        return true;
+    }
+    case FC_SIGN_RC: {
+        const uint32_t m = const_bit(o, 0, tb, gbase) ? 0x80000000u : 0u;
+#define C_(B) f_sign_rc<RB, B>(v, m)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_SIGN_CC:
+        f_sign_cc<RB>(v, (const_bit(o, 0, tb, gbase) & const_bit(o, 1, tb, gbase)) ? 0x80000000u : 0u);
+        return true;
+    case FC_M4: {
+#define C1_(B0, B1) f_m4<RB, B0, B1>(v, mt)
+#define C_(B1)                                                   \
+    switch (o.rb0) {                                             \
+    case 0: if constexpr (B1 != 0) { C1_(0, B1); } break;        \
+    case 1: if constexpr (B1 != 1) { C1_(1, B1); } break;        \
+    case 2: if constexpr (B1 != 2) { C1_(2, B1); } break;        \
+    default:                                                     \
+        if constexpr (RB > 3 && B1 != 3) { C1_(3, B1); }         \
+        break;                                                   \
+    }
+        ARCQML_BITS(o.rb1, C_)
+#undef C_
+#undef C1_
+        return true;
+    }
+    default:
+        return false;
+    }
+}
+
+// Fast Pauli-rotation gradients (half-gradient units: Im<lam|P|psi> / 2 with psi = psi_k).
+template <int RB>
+__device__ __forceinline__ bool grad_fast(const FOp &o, const double2 (&v)[1 << RB],
+                                          const double2 (&w)[1 << RB], uint32_t tb, uint64_t gbase,
+                                          double &z) {
+    switch (o.gcode) {
+    case GF_X: {
+#define C_(B) z = g_x<RB, B>(v, w)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case GF_Y: {
+#define C_(B) z = g_y<RB, B>(v, w)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case GF_Z_REG: {
+#define C_(B) z = g_z<RB, B>(v, w)
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case GF_Z_UNI: {
+        const double t = g_z_uni<RB>(v, w);
+        z = const_bit(o, 0, tb, gbase) ? -t : t;
+        return true;
+    }
+    default:
+        return false;
+    }
+}
+
 // ---------------------------------------------------------------- the pass kernel
 
 // Shared memory: [tile buffers: 2 x (psi [, lambda])][hioff][accumulators][ops][matrices].
@@ -557,15 +836,16 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                 E.tile_ok = (gbase & o.gcmask) == o.gcmask;
                 E.plain = (o.lcmask == 0) && (o.gcmask == 0);
                 const double2 *mt = mats + o.moff;
-                if (ADJ) {
-                    if (o.gkind == GK_PX || o.gkind == GK_PY) {
-                        const double z = grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
-                        accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
-                    } else if (o.gkind == GK_PZ) {
-                        accumulate(sacc, o.acc[0] * nwarps, 0.5 * grad_z<RB>(o, v, w, Le, E));
+                if (ADJ && o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
+                    double z = 0.0;
+                    if (!grad_fast<RB>(o, v, w, tb, gbase, z)) {
+                        if (o.gkind == GK_PZ) z = grad_z<RB>(o, v, w, Le, E);
+                        else z = grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
                     }
+                    accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
                 }
-                apply_op<RB>(o, mt, v, Le, E);
+                const bool fast = apply_fast<RB>(o, mt, v, tb, gbase);
+                if (!fast) apply_op<RB>(o, mt, v, Le, E);
                 if (ADJ) {
                     if (o.gkind == GK_GENERIC) {
                         const double2 *d = mt + umat_len(o.kind);
@@ -574,7 +854,8 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                             accumulate(sacc, o.acc[s] * nwarps,
                                        grad_generic<RB>(o, d + s * dl, v, w, Le, E));
                     }
-                    apply_op<RB>(o, mt, w, Le, E);
+                    if (fast) apply_fast<RB>(o, mt, w, tb, gbase);
+                    else apply_op<RB>(o, mt, w, Le, E);
                 }
             }
 #pragma unroll

@@ -41,6 +41,29 @@ enum GradKind : uint8_t {
     GK_GENERIC = 4,  // per slot: Re<lam| dU_s |psi'> with psi' = U^dag psi (dU after U's matrix)
 };
 
+// Specialised code paths the planner selects per op (the generic path handles every case;
+// the others are exact rewrites for common shapes without per-element control logic).
+enum FastCode : uint8_t {
+    FC_GENERIC = 0,  // kind + controls, evaluated per element
+    FC_RX = 1,       // uncontrolled RX-form on register bit rb0
+    FC_RY = 2,       // uncontrolled RY-form on register bit rb0
+    FC_M2 = 3,       // uncontrolled 2x2 on register bit rb0
+    FC_D1_REG = 4,   // uncontrolled diagonal on register bit rb0
+    FC_D1_UNI = 5,   // uncontrolled diagonal on a qubit constant per thread (dq 0)
+    FC_SIGN_RR = 6,  // -1 where register bits rb0 and rb1 are both set (CZ)
+    FC_SIGN_RC = 7,  // -1 where register bit rb0 and the per-thread bit dq 0 are set
+    FC_SIGN_CC = 8,  // -1 where the per-thread bits dq 0 and dq 1 are set
+    FC_M4 = 9,       // uncontrolled 4x4 on register bits (rb0, rb1)
+};
+
+enum GradFast : uint8_t {
+    GF_GENERIC = 0,  // gkind path with per-element control logic
+    GF_X = 1,        // uncontrolled Im<lam|X_rb0|psi>
+    GF_Y = 2,        // uncontrolled Im<lam|Y_rb0|psi>
+    GF_Z_REG = 3,    // uncontrolled Im<lam|Z_rb0|psi>
+    GF_Z_UNI = 4,    // uncontrolled Im<lam|Z|psi> on the per-thread bit dq 0
+};
+
 struct FOp {
     uint8_t kind;
     uint8_t rb0, rb1;        // register bits of the targets (FK_M2/RX/RY/M4)
@@ -51,7 +74,9 @@ struct FOp {
     uint16_t nslots;         // GK_GENERIC: number of slots
     uint32_t moff;           // offset of the op's matrices in the pass matrix table
     uint32_t acc[3];         // pass-local accumulator index per slot
-    uint32_t pad0;
+    uint8_t code;            // FastCode
+    uint8_t gcode;           // GradFast
+    uint8_t pad0[2];
     uint64_t gcmask;         // controls outside the tile (global positions)
     uint32_t pad[6];
 };

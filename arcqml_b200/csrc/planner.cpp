@@ -31,6 +31,7 @@ bool eq(double2 a, double2 b) { return a.x == b.x && a.y == b.y; }
 // One gate in kernel-ready small form, with its planning footprint.
 struct PGate {
     const OpRecord *op = nullptr;
+    bool noop = false;                 // identity gate
     bool dense_barrier = false;        // arity > 2 custom: per-gate kernel
     std::vector<uint32_t> controls;
     std::vector<uint32_t> targets;
@@ -53,6 +54,10 @@ PGate make_pgate(const OpRecord &op, bool adjoint, const uint8_t *req, bool grad
     }
     // allow_diag = false keeps the dense small form: positions = controls + targets.
     DevGate u = lower(op, adjoint ? LOWER_ADJOINT : LOWER_FORWARD, 0, false);
+    if (u.kind == KIND_NONE) {  // the identity gate: nothing to apply, nothing to differentiate
+        g.noop = true;
+        return g;
+    }
     for (int i = 0; i < u.nt; ++i) g.targets.push_back(uint32_t(u.t[i]));
     for (uint32_t q = 0; q < 64; ++q)
         if ((u.cmask >> q) & 1) g.controls.push_back(q);
@@ -103,6 +108,60 @@ size_t mat_entries(const PGate &g) {
     return per * (1 + g.dm.size());
 }
 
+// Chooses the op's specialised device path (fused.h FastCode). reg_of(q) is the register bit
+// of qubit q in the current sub-block (0xFF if none); lpos[q] its tile bit (-1 if outside).
+template <class RegOf>
+void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
+    const bool plain = o.lcmask == 0 && o.gcmask == 0;
+    const size_t nt = g.targets.size();
+    auto put = [&](int slot, uint32_t q) {
+        o.dq_in_tile[slot] = lpos[q] >= 0 ? 1 : 0;
+        o.dq_pos[slot] = uint8_t(lpos[q] >= 0 ? lpos[q] : int(q));
+    };
+    o.code = FC_GENERIC;
+    if (!g.diag) {
+        if (plain && nt == 1)
+            o.code = o.kind == FK_RX ? FC_RX : (o.kind == FK_RY ? FC_RY : FC_M2);
+        else if (plain && nt == 2)
+            o.code = FC_M4;
+        return;
+    }
+    if (nt != 1) return;
+    const uint32_t t = g.targets[0];
+    if (plain) {
+        const uint8_t r = reg_of(t);
+        if (r != 0xFF) {
+            o.code = FC_D1_REG;
+            o.rb0 = r;
+        } else {
+            o.code = FC_D1_UNI;
+        }
+        return;
+    }
+    const double2 d0 = g.m[0], d1 = g.m[3];
+    const bool sign = d0.x == 1.0 && d0.y == 0.0 && d1.x == -1.0 && d1.y == 0.0;
+    if (!sign || g.controls.size() != 1) return;
+    const uint32_t c = g.controls[0];  // CZ-like: -1 where both c and t are 1
+    const uint8_t rc = reg_of(c), rt = reg_of(t);
+    if (rc != 0xFF && rt != 0xFF) {
+        o.code = FC_SIGN_RR;
+        o.rb0 = rc;
+        o.rb1 = rt;
+    } else if (rt != 0xFF) {
+        o.code = FC_SIGN_RC;
+        o.rb0 = rt;
+        put(0, c);
+    } else if (rc != 0xFF) {
+        o.code = FC_SIGN_RC;
+        o.rb0 = rc;
+        put(0, t);
+    } else {
+        o.code = FC_SIGN_CC;
+        put(0, c);
+        put(1, t);
+    }
+}
+
 // Residue of a tile bit under the shared-memory swizzle (fold of 3-bit groups).
 inline int residue(int bit) { return bit % 3; }
 
@@ -126,6 +185,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
     const uint64_t low_mask = (uint64_t(1) << L) - 1;
 
     std::vector<char> done(gates.size(), 0);
+    for (size_t i = 0; i < gates.size(); ++i) done[i] = gates[i].noop ? 1 : 0;
     size_t first = 0;
     uint32_t acc_total = 0;
     while (true) {
@@ -286,8 +346,15 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                     o.rb1 = reg_of(g.targets[1]);
                     for (int i = 0; i < 16; ++i) st.mats.push_back(g.m[i]);
                 }
+                classify(o, g, reg_of, lpos);
                 o.gkind = g.gkind;
                 if (g.gkind != GK_NONE) {
+                    const bool plain = o.lcmask == 0 && o.gcmask == 0;
+                    o.gcode = GF_GENERIC;
+                    if (plain && g.gkind == GK_PX) o.gcode = GF_X;
+                    if (plain && g.gkind == GK_PY) o.gcode = GF_Y;
+                    if (plain && g.gkind == GK_PZ)
+                        o.gcode = o.code == FC_D1_REG ? GF_Z_REG : GF_Z_UNI;
                     o.nslots = uint16_t(g.parents.size());
                     if (g.gkind == GK_GENERIC) {
                         // a diagonal gate's derivative is diagonal: store its diagonal only,
