@@ -688,6 +688,55 @@ __device__ __forceinline__ bool grad_fast(const FOp &o, const double2 (&v)[1 << 
     }
 }
 
+// ---------------------------------------------------------------- generic path (out of line)
+//
+// Gates without a fast path (controlled gates other than CZ, two-qubit diagonals, controlled
+// rotations' gradients, ...) run through these non-inlined functions, so their per-element
+// index and control logic never mixes into the hot loop of the fast paths. The caller copies
+// the thread's registers into a local array around the call.
+
+template <int RB>
+__device__ __forceinline__ void rebuild(uint32_t tb, const uint32_t *rm, uint64_t gbase,
+                                        const FOp &o, uint32_t (&Le)[1 << RB], OpEnv &E) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        uint32_t x = tb;
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+            if ((e >> r) & 1) x |= rm[r];
+        Le[e] = x;
+    }
+    E.lcmask = o.lcmask;
+    E.gbase = gbase;
+    E.tile_ok = (gbase & o.gcmask) == o.gcmask;
+    E.plain = (o.lcmask == 0) && (o.gcmask == 0);
+}
+
+template <int RB>
+__device__ __noinline__ void slow_apply(const FOp &o, const double2 *mt, double2 *vp, uint32_t tb,
+                                        const uint32_t *rm, uint64_t gbase) {
+    uint32_t Le[1 << RB];
+    OpEnv E;
+    rebuild<RB>(tb, rm, gbase, o, Le, E);
+    apply_op<RB>(o, mt, *reinterpret_cast<double2(*)[1 << RB]>(vp), Le, E);
+}
+
+// d == nullptr: Pauli gradient (gkind X/Y/Z) before U^dag; else generic slot gradient with the
+// derivative matrix d after U^dag.
+template <int RB>
+__device__ __noinline__ double slow_grad(const FOp &o, const double2 *d, const double2 *vp,
+                                         const double2 *wp, uint32_t tb, const uint32_t *rm,
+                                         uint64_t gbase) {
+    uint32_t Le[1 << RB];
+    OpEnv E;
+    rebuild<RB>(tb, rm, gbase, o, Le, E);
+    const auto &v = *reinterpret_cast<const double2(*)[1 << RB]>(vp);
+    const auto &w = *reinterpret_cast<const double2(*)[1 << RB]>(wp);
+    if (d) return grad_generic<RB>(o, d, v, w, Le, E);
+    if (o.gkind == GK_PZ) return grad_z<RB>(o, v, w, Le, E);
+    return grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
+}
+
 // ---------------------------------------------------------------- the pass kernel
 
 // Shared memory: [tile buffers: 2 x (psi [, lambda])][hioff][accumulators][ops][matrices].
@@ -830,32 +879,53 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
             for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
                 FOp o;
                 load_op(ops + oi, o);
-                OpEnv E;
-                E.lcmask = o.lcmask;
-                E.gbase = gbase;
-                E.tile_ok = (gbase & o.gcmask) == o.gcmask;
-                E.plain = (o.lcmask == 0) && (o.gcmask == 0);
                 const double2 *mt = mats + o.moff;
                 if (ADJ && o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
                     double z = 0.0;
                     if (!grad_fast<RB>(o, v, w, tb, gbase, z)) {
-                        if (o.gkind == GK_PZ) z = grad_z<RB>(o, v, w, Le, E);
-                        else z = grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
+                        double2 tv[N], tw[N];
+#pragma unroll
+                        for (int e = 0; e < N; ++e) {
+                            tv[e] = v[e];
+                            tw[e] = w[e];
+                        }
+                        z = slow_grad<RB>(o, nullptr, tv, tw, tb, rm, gbase);
                     }
                     accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
                 }
                 const bool fast = apply_fast<RB>(o, mt, v, tb, gbase);
-                if (!fast) apply_op<RB>(o, mt, v, Le, E);
+                if (!fast) {
+                    double2 tv[N];
+#pragma unroll
+                    for (int e = 0; e < N; ++e) tv[e] = v[e];
+                    slow_apply<RB>(o, mt, tv, tb, rm, gbase);
+#pragma unroll
+                    for (int e = 0; e < N; ++e) v[e] = tv[e];
+                }
                 if (ADJ) {
                     if (o.gkind == GK_GENERIC) {
                         const double2 *d = mt + umat_len(o.kind);
                         const int dl = dmat_len(o.kind);
+                        double2 tv[N], tw[N];
+#pragma unroll
+                        for (int e = 0; e < N; ++e) {
+                            tv[e] = v[e];
+                            tw[e] = w[e];
+                        }
                         for (int s = 0; s < int(o.nslots); ++s)
                             accumulate(sacc, o.acc[s] * nwarps,
-                                       grad_generic<RB>(o, d + s * dl, v, w, Le, E));
+                                       slow_grad<RB>(o, d + s * dl, tv, tw, tb, rm, gbase));
                     }
-                    if (fast) apply_fast<RB>(o, mt, w, tb, gbase);
-                    else apply_op<RB>(o, mt, w, Le, E);
+                    if (fast) {
+                        apply_fast<RB>(o, mt, w, tb, gbase);
+                    } else {
+                        double2 tw[N];
+#pragma unroll
+                        for (int e = 0; e < N; ++e) tw[e] = w[e];
+                        slow_apply<RB>(o, mt, tw, tb, rm, gbase);
+#pragma unroll
+                        for (int e = 0; e < N; ++e) w[e] = tw[e];
+                    }
                 }
             }
 #pragma unroll

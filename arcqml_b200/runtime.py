@@ -21,7 +21,8 @@ from .circuit import PlanOp
 
 ABI_VERSION = 1
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libarcqml_runtime_private.so")
+# ARCQML_RUNTIME_LIB may name another build of the same C ABI (e.g. an instrumented one).
+LIB_PATH = os.environ.get("ARCQML_RUNTIME_LIB") or os.path.join(_HERE, "libarcqml_runtime_private.so")
 
 
 class RuntimeError(Exception):  # noqa: A001 - mirrors arcqml_runtime_sys::RuntimeError
