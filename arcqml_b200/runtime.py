@@ -122,6 +122,7 @@ def load():
         "arcqml_rt_v2_expectation_and_apply": (I32, [P, P, P, S, S, P, P]),
         "arcqml_rt_v2_adjoint_backward": (I32, [P, P, P, S, S, P, P, S, P, S, P]),
         "arcqml_rt_v2_norms": (I32, [P, S, S, P, P]),
+        "arcqml_rt_v2_norms_noalloc": (I32, [P, S, S, P, P]),
         "arcqml_rt_v2_set_basis_state": (I32, [P, S, S, C.c_uint64, P]),
         "arcqml_rt_v2_plan_set_parameters": (I32, [P, P, S]),
         "arcqml_rt_v2_plan_len": (S, [P]),
@@ -451,6 +452,15 @@ def norms_device(state, num_qubits: int, stream=None) -> np.ndarray:
     out = np.zeros(b, dtype=np.float64)
     _status(load().arcqml_rt_v2_norms(_dev_ptr(state), b, num_qubits, out.ctypes.data,
                                       _stream_ptr(stream)))
+    return out
+
+
+def norms_device_noalloc(state, num_qubits: int, stream=None) -> np.ndarray:
+    """Row norms through the entry point that allocates no device memory (see its header)."""
+    b = _rows(state, num_qubits)
+    out = np.zeros(b, dtype=np.float64)
+    _status(load().arcqml_rt_v2_norms_noalloc(_dev_ptr(state), b, num_qubits, out.ctypes.data,
+                                              _stream_ptr(stream)))
     return out
 
 

@@ -81,6 +81,17 @@ int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);
 
+/* Same result as arcqml_rt_v2_norms, for callers that cannot allocate device memory while they
+ * run (their memory is all handed to their own pool, or an allocation would synchronise the
+ * device at a point they cannot afford). No counterpart in the reference. It allocates nothing:
+ * its scratch is a static 192 KiB device array that every GPU loading the library keeps until
+ * exit. At most 8192 rows per call (larger batches are rejected with an error). The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture. All calls share the array: calls
+ * that overlap on the GPU race. */
+int32_t arcqml_rt_v2_norms_noalloc(const arcqml_c128 *amplitudes, size_t batch,
+                                   size_t num_qubits, double *norms, void *stream);
+
 /* Every row <- |index>. */
 int32_t arcqml_rt_v2_set_basis_state(arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                                      uint64_t index, void *stream);
