@@ -712,24 +712,39 @@ __device__ __forceinline__ void rebuild(uint32_t tb, const uint32_t *rm, uint64_
     E.plain = (o.lcmask == 0) && (o.gcmask == 0);
 }
 
+// The op is read from its shared-memory table entry and the register bits from the sub-block
+// descriptor, so the hot loop passes only pointers (nothing of it is spilled for these calls).
 template <int RB>
-__device__ __noinline__ void slow_apply(const FOp &o, const double2 *mt, double2 *vp, uint32_t tb,
-                                        const uint32_t *rm, uint64_t gbase) {
+__device__ __forceinline__ void slow_setup(const FOp *op, const SubBlock *sbp, uint32_t tb,
+                                           uint64_t gbase, FOp &o, uint32_t (&Le)[1 << RB],
+                                           OpEnv &E) {
+    load_op(op, o);
+    uint32_t rm[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) rm[r] = 1u << sbp->R[r];
+    rebuild<RB>(tb, rm, gbase, o, Le, E);
+}
+
+template <int RB>
+__device__ __noinline__ void slow_apply(const FOp *op, const double2 *mt, double2 *vp, uint32_t tb,
+                                        const SubBlock *sbp, uint64_t gbase) {
+    FOp o;
     uint32_t Le[1 << RB];
     OpEnv E;
-    rebuild<RB>(tb, rm, gbase, o, Le, E);
+    slow_setup<RB>(op, sbp, tb, gbase, o, Le, E);
     apply_op<RB>(o, mt, *reinterpret_cast<double2(*)[1 << RB]>(vp), Le, E);
 }
 
 // d == nullptr: Pauli gradient (gkind X/Y/Z) before U^dag; else generic slot gradient with the
 // derivative matrix d after U^dag.
 template <int RB>
-__device__ __noinline__ double slow_grad(const FOp &o, const double2 *d, const double2 *vp,
-                                         const double2 *wp, uint32_t tb, const uint32_t *rm,
+__device__ __noinline__ double slow_grad(const FOp *op, const double2 *d, const double2 *vp,
+                                         const double2 *wp, uint32_t tb, const SubBlock *sbp,
                                          uint64_t gbase) {
+    FOp o;
     uint32_t Le[1 << RB];
     OpEnv E;
-    rebuild<RB>(tb, rm, gbase, o, Le, E);
+    slow_setup<RB>(op, sbp, tb, gbase, o, Le, E);
     const auto &v = *reinterpret_cast<const double2(*)[1 << RB]>(vp);
     const auto &w = *reinterpret_cast<const double2(*)[1 << RB]>(wp);
     if (d) return grad_generic<RB>(o, d, v, w, Le, E);
@@ -889,7 +904,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                             tv[e] = v[e];
                             tw[e] = w[e];
                         }
-                        z = slow_grad<RB>(o, nullptr, tv, tw, tb, rm, gbase);
+                        z = slow_grad<RB>(ops + oi, nullptr, tv, tw, tb, subs + sb, gbase);
                     }
                     accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
                 }
@@ -898,7 +913,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                     double2 tv[N];
 #pragma unroll
                     for (int e = 0; e < N; ++e) tv[e] = v[e];
-                    slow_apply<RB>(o, mt, tv, tb, rm, gbase);
+                    slow_apply<RB>(ops + oi, mt, tv, tb, subs + sb, gbase);
 #pragma unroll
                     for (int e = 0; e < N; ++e) v[e] = tv[e];
                 }
@@ -914,7 +929,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                         }
                         for (int s = 0; s < int(o.nslots); ++s)
                             accumulate(sacc, o.acc[s] * nwarps,
-                                       slow_grad<RB>(o, d + s * dl, tv, tw, tb, rm, gbase));
+                                       slow_grad<RB>(ops + oi, d + s * dl, tv, tw, tb, subs + sb, gbase));
                     }
                     if (fast) {
                         apply_fast<RB>(o, mt, w, tb, gbase);
@@ -922,7 +937,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                         double2 tw[N];
 #pragma unroll
                         for (int e = 0; e < N; ++e) tw[e] = w[e];
-                        slow_apply<RB>(o, mt, tw, tb, rm, gbase);
+                        slow_apply<RB>(ops + oi, mt, tw, tb, subs + sb, gbase);
 #pragma unroll
                         for (int e = 0; e < N; ++e) w[e] = tw[e];
                     }

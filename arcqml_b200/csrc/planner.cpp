@@ -102,10 +102,37 @@ PGate make_pgate(const OpRecord &op, bool adjoint, const uint8_t *req, bool grad
 }
 
 // Upper bound of the matrix-table entries a gate adds to its pass.
+// (a forward single-qubit gate may be merged into a 2x2 of 4 entries: count it as 4)
 size_t mat_entries(const PGate &g) {
     const size_t dim = size_t(1) << g.targets.size();
-    const size_t per = g.diag ? dim : dim * dim;
+    const size_t per = (g.diag && dim > 2) ? dim : dim * dim;
     return per * (1 + g.dm.size());
+}
+
+// Full 2x2 of an emitted single-target op from its kind and matrix-table entries.
+void op_matrix2(const FOp &o, const std::vector<double2> &mats, double2 u[4]) {
+    const double2 *m = mats.data() + o.moff;
+    switch (o.kind) {
+    case FK_RX: u[0] = make_double2(m[0].x, 0); u[1] = make_double2(0, -m[0].y);
+                u[2] = u[1]; u[3] = u[0]; break;
+    case FK_RY: u[0] = make_double2(m[0].x, 0); u[1] = make_double2(-m[0].y, 0);
+                u[2] = make_double2(m[0].y, 0); u[3] = u[0]; break;
+    case FK_D1: u[0] = m[0]; u[1] = make_double2(0, 0); u[2] = u[1]; u[3] = m[1]; break;
+    default: for (int i = 0; i < 4; ++i) u[i] = m[i]; break;
+    }
+}
+
+void mul2(const double2 a[4], const double2 b[4], double2 out[4]) {  // out = a * b
+    for (int i = 0; i < 2; ++i)
+        for (int j = 0; j < 2; ++j) {
+            double re = 0, im = 0;
+            for (int k = 0; k < 2; ++k) {
+                const double2 x = a[i * 2 + k], y = b[k * 2 + j];
+                re += x.x * y.x - x.y * y.y;
+                im += x.x * y.y + x.y * y.x;
+            }
+            out[i * 2 + j] = make_double2(re, im);
+        }
 }
 
 // Chooses the op's specialised device path (fused.h FastCode). reg_of(q) is the register bit
@@ -307,8 +334,38 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                     if (s.R[r] == lp) return uint8_t(r);
                 return 0xFF;
             };
+            // Forward passes merge consecutive uncontrolled single-qubit gates on the same qubit
+            // (nothing else touching it in between) into one 2x2: same arithmetic, fewer ops.
+            int last1q[64];
+            for (int q = 0; q < 64; ++q) last1q[q] = -1;
             for (size_t gi : subs[sb]) {
                 const PGate &g = gates[gi];
+                const bool mergeable = !adjoint && g.controls.empty() && g.targets.size() == 1 &&
+                                       g.gkind == GK_NONE;
+                if (mergeable && last1q[g.targets[0]] >= 0) {
+                    FOp &e = st.ops[size_t(last1q[g.targets[0]])];
+                    double2 ue[4], un[4], p[4];
+                    op_matrix2(e, st.mats, ue);
+                    for (int i = 0; i < 4; ++i) un[i] = g.m[i];
+                    mul2(un, ue, p);  // the earlier gate acts first
+                    const bool pdiag = p[1].x == 0 && p[1].y == 0 && p[2].x == 0 && p[2].y == 0;
+                    e.moff = uint32_t(st.mats.size());
+                    if (pdiag && e.kind == FK_D1) {
+                        st.mats.push_back(p[0]);
+                        st.mats.push_back(p[3]);
+                    } else {
+                        const uint8_t r = reg_of(g.targets[0]);
+                        if (r == 0xFF) fail("internal: merged gate without a register target");
+                        e.kind = FK_M2;
+                        e.code = FC_M2;
+                        e.rb0 = r;
+                        for (int i = 0; i < 4; ++i) st.mats.push_back(p[i]);
+                    }
+                    continue;
+                }
+                for (uint32_t q = 0; q < 64; ++q)
+                    if ((g.touched >> q) & 1) last1q[q] = -1;
+                if (mergeable) last1q[g.targets[0]] = int(st.ops.size());
                 FOp o;
                 std::memset(&o, 0, sizeof(o));
                 for (uint32_t c : g.controls) {
