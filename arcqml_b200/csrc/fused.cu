@@ -752,6 +752,84 @@ __device__ __noinline__ double slow_grad(const FOp *op, const double2 *d, const 
     return grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
 }
 
+// Tile-local index of a thread's register element e in the current sub-block.
+template <int RB>
+__device__ __forceinline__ uint32_t sub_index(uint32_t tb, const uint32_t (&rm)[RB], int e) {
+    uint32_t x = tb;
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+        if ((e >> r) & 1) x |= rm[r];
+    return x;
+}
+
+// Adjoint step for the common uncontrolled gates in one dispatch: the Pauli-rotation gradient
+// (from psi_k, lambda_k), then U^dagger on psi and on lambda. Returns false when the op needs
+// the general sequence (controlled gates, generic gradients).
+template <int RB>
+__device__ __forceinline__ bool adj_fast(const FOp &o, const double2 *mt, double2 (&v)[1 << RB],
+                                         double2 (&w)[1 << RB], uint32_t tb, uint64_t gbase,
+                                         double &z) {
+    const bool none = o.gkind == GK_NONE;
+    switch (o.code) {
+    case FC_RX: {
+        if (!none && o.gcode != GF_X) return false;
+        const double2 cs = mt[0];
+#define C_(B)                                   \
+    {                                           \
+        if (!none) z = g_x<RB, B>(v, w);        \
+        f_rx<RB, B>(v, cs.x, cs.y);             \
+        f_rx<RB, B>(w, cs.x, cs.y);             \
+    }
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_RY: {
+        if (!none && o.gcode != GF_Y) return false;
+        const double2 cs = mt[0];
+#define C_(B)                                   \
+    {                                           \
+        if (!none) z = g_y<RB, B>(v, w);        \
+        f_ry<RB, B>(v, cs.x, cs.y);             \
+        f_ry<RB, B>(w, cs.x, cs.y);             \
+    }
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_D1_REG: {
+        if (!none && o.gcode != GF_Z_REG) return false;
+        const double2 d0 = mt[0], d1 = mt[1];
+#define C_(B)                                   \
+    {                                           \
+        if (!none) z = g_z<RB, B>(v, w);        \
+        f_d1_reg<RB, B>(v, d0, d1);             \
+        f_d1_reg<RB, B>(w, d0, d1);             \
+    }
+        ARCQML_BITS(o.rb0, C_)
+#undef C_
+        return true;
+    }
+    case FC_D1_UNI: {
+        if (!none && o.gcode != GF_Z_UNI) return false;
+        const bool bit = const_bit(o, 0, tb, gbase) != 0;
+        if (!none) {
+            const double t = g_z_uni<RB>(v, w);
+            z = bit ? -t : t;
+        }
+        const double2 d = bit ? mt[1] : mt[0];
+        f_d1_uni<RB>(v, d);
+        f_d1_uni<RB>(w, d);
+        return true;
+    }
+    default:
+        if (!none) return false;
+        if (!apply_fast<RB>(o, mt, v, tb, gbase)) return false;
+        apply_fast<RB>(o, mt, w, tb, gbase);
+        return true;
+    }
+}
+
 // ---------------------------------------------------------------- the pass kernel
 
 // Shared memory: [tile buffers: 2 x (psi [, lambda])][hioff][accumulators][ops][matrices].
@@ -879,15 +957,10 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
             uint32_t rm[RB];
 #pragma unroll
             for (int r = 0; r < RB; ++r) rm[r] = 1u << S.R[r];
-            uint32_t Le[N];
             double2 v[N], w[N];
 #pragma unroll
             for (int e = 0; e < N; ++e) {
-                uint32_t x = tb;
-#pragma unroll
-                for (int r = 0; r < RB; ++r)
-                    if ((e >> r) & 1) x |= rm[r];
-                Le[e] = x;
+                const uint32_t x = sub_index<RB>(tb, rm, e);
                 v[e] = tp[phys(x)];
                 if (ADJ) w[e] = tl[phys(x)];
             }
@@ -895,18 +968,25 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                 FOp o;
                 load_op(ops + oi, o);
                 const double2 *mt = mats + o.moff;
-                if (ADJ && o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
+                if constexpr (ADJ) {
+                    // one dispatch: Pauli gradient (if any), then U^dagger on psi and lambda
                     double z = 0.0;
-                    if (!grad_fast<RB>(o, v, w, tb, gbase, z)) {
-                        double2 tv[N], tw[N];
-#pragma unroll
-                        for (int e = 0; e < N; ++e) {
-                            tv[e] = v[e];
-                            tw[e] = w[e];
-                        }
-                        z = slow_grad<RB>(ops + oi, nullptr, tv, tw, tb, subs + sb, gbase);
+                    if (adj_fast<RB>(o, mt, v, w, tb, gbase, z)) {
+                        if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                        continue;
                     }
-                    accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                    if (o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
+                        if (!grad_fast<RB>(o, v, w, tb, gbase, z)) {
+                            double2 tv[N], tw[N];
+#pragma unroll
+                            for (int e = 0; e < N; ++e) {
+                                tv[e] = v[e];
+                                tw[e] = w[e];
+                            }
+                            z = slow_grad<RB>(ops + oi, nullptr, tv, tw, tb, subs + sb, gbase);
+                        }
+                        accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                    }
                 }
                 const bool fast = apply_fast<RB>(o, mt, v, tb, gbase);
                 if (!fast) {
@@ -917,7 +997,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
 #pragma unroll
                     for (int e = 0; e < N; ++e) v[e] = tv[e];
                 }
-                if (ADJ) {
+                if constexpr (ADJ) {
                     if (o.gkind == GK_GENERIC) {
                         const double2 *d = mt + umat_len(o.kind);
                         const int dl = dmat_len(o.kind);
@@ -945,8 +1025,9 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
             }
 #pragma unroll
             for (int e = 0; e < N; ++e) {
-                tp[phys(Le[e])] = v[e];
-                if (ADJ) tl[phys(Le[e])] = w[e];
+                const uint32_t x = sub_index<RB>(tb, rm, e);
+                tp[phys(x)] = v[e];
+                if (ADJ) tl[phys(x)] = w[e];
             }
             __syncthreads();
         }
