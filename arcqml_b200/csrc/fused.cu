@@ -830,6 +830,91 @@ __device__ __forceinline__ bool adj_fast(const FOp &o, const double2 *mt, double
     }
 }
 
+// A sub-block with at least one op on the generic path, out of line so that the fast loop
+// above keeps a register allocation of its own.
+template <int RB, bool ADJ>
+__device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, double2 *tp,
+                                              double2 *tl, const FOp *ops, const double2 *mats,
+                                              const SubBlock *subs, double *sacc,
+                                              uint32_t nwarps, uint32_t tb, uint64_t gbase) {
+    constexpr int N = 1 << RB;
+    uint32_t rm[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) rm[r] = 1u << S.R[r];
+    double2 v[N], w[N];
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        const uint32_t x = sub_index<RB>(tb, rm, e);
+        v[e] = tp[phys(x)];
+        if (ADJ) w[e] = tl[phys(x)];
+    }
+    for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
+        FOp o;
+        load_op(ops + oi, o);
+        const double2 *mt = mats + o.moff;
+        if constexpr (ADJ) {
+            // one dispatch: Pauli gradient (if any), then U^dagger on psi and lambda
+            double z = 0.0;
+            if (adj_fast<RB>(o, mt, v, w, tb, gbase, z)) {
+                if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                continue;
+            }
+            if (o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
+                if (!grad_fast<RB>(o, v, w, tb, gbase, z)) {
+                    double2 tv[N], tw[N];
+#pragma unroll
+                    for (int e = 0; e < N; ++e) {
+                        tv[e] = v[e];
+                        tw[e] = w[e];
+                    }
+                    z = slow_grad<RB>(ops + oi, nullptr, tv, tw, tb, subs + sb, gbase);
+                }
+                accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+            }
+        }
+        const bool fast = apply_fast<RB>(o, mt, v, tb, gbase);
+        if (!fast) {
+            double2 tv[N];
+#pragma unroll
+            for (int e = 0; e < N; ++e) tv[e] = v[e];
+            slow_apply<RB>(ops + oi, mt, tv, tb, subs + sb, gbase);
+#pragma unroll
+            for (int e = 0; e < N; ++e) v[e] = tv[e];
+        }
+        if constexpr (ADJ) {
+            if (o.gkind == GK_GENERIC) {
+                const double2 *d = mt + umat_len(o.kind);
+                const int dl = dmat_len(o.kind);
+                double2 tv[N], tw[N];
+#pragma unroll
+                for (int e = 0; e < N; ++e) {
+                    tv[e] = v[e];
+                    tw[e] = w[e];
+                }
+                for (int s = 0; s < int(o.nslots); ++s)
+                    accumulate(sacc, o.acc[s] * nwarps,
+                               slow_grad<RB>(ops + oi, d + s * dl, tv, tw, tb, subs + sb, gbase));
+            }
+            if (fast) {
+                apply_fast<RB>(o, mt, w, tb, gbase);
+            } else {
+                double2 tw[N];
+#pragma unroll
+                for (int e = 0; e < N; ++e) tw[e] = w[e];
+                slow_apply<RB>(ops + oi, mt, tw, tb, subs + sb, gbase);
+#pragma unroll
+                for (int e = 0; e < N; ++e) w[e] = tw[e];
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < N; ++e) {
+        const uint32_t x = sub_index<RB>(tb, rm, e);
+        tp[phys(x)] = v[e];
+        if (ADJ) tl[phys(x)] = w[e];
+    }
+}
+
 // ---------------------------------------------------------------- the pass kernel
 
 // Shared memory: [tile buffers: 2 x (psi [, lambda])][hioff][accumulators][ops][matrices].
@@ -957,77 +1042,34 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
             uint32_t rm[RB];
 #pragma unroll
             for (int r = 0; r < RB; ++r) rm[r] = 1u << S.R[r];
-            double2 v[N], w[N];
+            if (S.flags & SB_ALL_FAST) {
+                double2 v[N], w[N];
 #pragma unroll
-            for (int e = 0; e < N; ++e) {
-                const uint32_t x = sub_index<RB>(tb, rm, e);
-                v[e] = tp[phys(x)];
-                if (ADJ) w[e] = tl[phys(x)];
-            }
-            for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
-                FOp o;
-                load_op(ops + oi, o);
-                const double2 *mt = mats + o.moff;
-                if constexpr (ADJ) {
-                    // one dispatch: Pauli gradient (if any), then U^dagger on psi and lambda
-                    double z = 0.0;
-                    if (adj_fast<RB>(o, mt, v, w, tb, gbase, z)) {
+                for (int e = 0; e < N; ++e) {
+                    const uint32_t x = sub_index<RB>(tb, rm, e);
+                    v[e] = tp[phys(x)];
+                    if (ADJ) w[e] = tl[phys(x)];
+                }
+                for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
+                    FOp o;
+                    load_op(ops + oi, o);
+                    const double2 *mt = mats + o.moff;
+                    if constexpr (ADJ) {
+                        double z = 0.0;
+                        adj_fast<RB>(o, mt, v, w, tb, gbase, z);
                         if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
-                        continue;
-                    }
-                    if (o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
-                        if (!grad_fast<RB>(o, v, w, tb, gbase, z)) {
-                            double2 tv[N], tw[N];
-#pragma unroll
-                            for (int e = 0; e < N; ++e) {
-                                tv[e] = v[e];
-                                tw[e] = w[e];
-                            }
-                            z = slow_grad<RB>(ops + oi, nullptr, tv, tw, tb, subs + sb, gbase);
-                        }
-                        accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
-                    }
-                }
-                const bool fast = apply_fast<RB>(o, mt, v, tb, gbase);
-                if (!fast) {
-                    double2 tv[N];
-#pragma unroll
-                    for (int e = 0; e < N; ++e) tv[e] = v[e];
-                    slow_apply<RB>(ops + oi, mt, tv, tb, subs + sb, gbase);
-#pragma unroll
-                    for (int e = 0; e < N; ++e) v[e] = tv[e];
-                }
-                if constexpr (ADJ) {
-                    if (o.gkind == GK_GENERIC) {
-                        const double2 *d = mt + umat_len(o.kind);
-                        const int dl = dmat_len(o.kind);
-                        double2 tv[N], tw[N];
-#pragma unroll
-                        for (int e = 0; e < N; ++e) {
-                            tv[e] = v[e];
-                            tw[e] = w[e];
-                        }
-                        for (int s = 0; s < int(o.nslots); ++s)
-                            accumulate(sacc, o.acc[s] * nwarps,
-                                       slow_grad<RB>(ops + oi, d + s * dl, tv, tw, tb, subs + sb, gbase));
-                    }
-                    if (fast) {
-                        apply_fast<RB>(o, mt, w, tb, gbase);
                     } else {
-                        double2 tw[N];
-#pragma unroll
-                        for (int e = 0; e < N; ++e) tw[e] = w[e];
-                        slow_apply<RB>(ops + oi, mt, tw, tb, subs + sb, gbase);
-#pragma unroll
-                        for (int e = 0; e < N; ++e) w[e] = tw[e];
+                        apply_fast<RB>(o, mt, v, tb, gbase);
                     }
                 }
-            }
 #pragma unroll
-            for (int e = 0; e < N; ++e) {
-                const uint32_t x = sub_index<RB>(tb, rm, e);
-                tp[phys(x)] = v[e];
-                if (ADJ) tl[phys(x)] = w[e];
+                for (int e = 0; e < N; ++e) {
+                    const uint32_t x = sub_index<RB>(tb, rm, e);
+                    tp[phys(x)] = v[e];
+                    if (ADJ) tl[phys(x)] = w[e];
+                }
+            } else {
+                general_subblock<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nwarps, tb, gbase);
             }
             __syncthreads();
         }

@@ -86,8 +86,9 @@ struct SubBlock {
     uint8_t R[4];            // register bits (tile-local), ascending; RB of them are used
     uint8_t perm[12];        // thread bit i -> tile-local bit perm[i] (the bits not in R)
     uint16_t op_begin, op_end;
-    uint32_t pad;
+    uint32_t flags;          // SB_ALL_FAST: every op of the sub-block has a fast path
 };
+constexpr uint32_t SB_ALL_FAST = 1;
 static_assert(sizeof(SubBlock) == 24, "SubBlock layout");
 
 struct PassHeader {

@@ -189,6 +189,15 @@ void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
     }
 }
 
+// Whether the device runs op o without its generic (out-of-line) path: the forward pass needs
+// a fast apply; the adjoint pass also needs the gradient, if any, on the same fast path.
+bool has_fast_path(const FOp &o, bool adjoint) {
+    if (o.code == FC_GENERIC) return false;
+    if (!adjoint || o.gkind == GK_NONE) return true;
+    return (o.code == FC_RX && o.gcode == GF_X) || (o.code == FC_RY && o.gcode == GF_Y) ||
+           (o.code == FC_D1_REG && o.gcode == GF_Z_REG) || (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
+}
+
 // Residue of a tile bit under the shared-memory swizzle (fold of 3-bit groups).
 inline int residue(int bit) { return bit % 3; }
 
@@ -432,6 +441,9 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 st.ops.push_back(o);
             }
             s.op_end = uint16_t(st.ops.size());
+            s.flags = SB_ALL_FAST;
+            for (size_t oi = s.op_begin; oi < s.op_end; ++oi)
+                if (!has_fast_path(st.ops[oi], adjoint)) s.flags = 0;
             st.subs.push_back(s);
         }
         h.nsub = uint32_t(st.subs.size());
