@@ -458,6 +458,53 @@ int32_t arcqml_rt_v2_expectation_and_apply(const ArcqmlObservableHandle *observa
     });
 }
 
+int32_t arcqml_rt_v2_expectation_and_accumulate(const ArcqmlObservableHandle *observable,
+                                                const arcqml_c128 *amplitudes, arcqml_c128 *output,
+                                                size_t batch, size_t num_qubits, double *values,
+                                                void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (!values || !output) fail("output buffer is null");
+        ThreadContext &ctx = thread_context();
+        observable_device(*obs_of(observable), reinterpret_cast<const double2 *>(amplitudes),
+                          reinterpret_cast<double2 *>(output), batch, uint32_t(num_qubits), values,
+                          ctx, pick_stream(ctx, stream), true);
+    });
+}
+
+int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubits,
+                                  const uint32_t *positions, size_t num_positions,
+                                  uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip_value,
+                                  arcqml_c128 *staging, int32_t unpack, void *stream) {
+    return guarded([&] {
+        if (!amplitudes || !staging) fail("amplitude or staging buffer is null");
+        if (num_local_qubits >= 63) fail("shard qubit count must be below 63");
+        if (num_positions == 0 || num_positions > kMaxSliceBits)
+            fail("slice must have between 1 and 8 positions");
+        if (num_positions > num_local_qubits)
+            fail("slice has more positions than the shard has qubits");
+        if (!positions) fail("slice position list is null");
+        uint64_t seen = 0;
+        for (size_t i = 0; i < num_positions; ++i) {
+            if (positions[i] >= num_local_qubits) {
+                std::ostringstream m;
+                m << "slice position " << positions[i] << " is outside the " << num_local_qubits
+                  << "-qubit shard";
+                fail(m.str());
+            }
+            if ((seen >> positions[i]) & 1) fail("slice positions repeat");
+            seen |= uint64_t(1) << positions[i];
+        }
+        const uint64_t others = uint64_t(1) << (num_local_qubits - num_positions);
+        if (chunk_begin > others || chunk_len > others - chunk_begin)
+            fail("slice chunk exceeds the shard");
+        ThreadContext &ctx = thread_context();
+        launch_slices(reinterpret_cast<double2 *>(amplitudes), uint32_t(num_local_qubits),
+                      positions, uint32_t(num_positions), chunk_begin, chunk_len, skip_value,
+                      reinterpret_cast<double2 *>(staging), unpack != 0, pick_stream(ctx, stream));
+    });
+}
+
 int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
                                       arcqml_c128 *adjoint_state, size_t batch,
                                       size_t num_qubits, const double *upstream,

@@ -240,8 +240,10 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
     validate_plan_for_state(plan, n);
     check_bindings(plan, req_len, grads_len);
 
-    // lambda <- g lambda (per row)
-    {
+    // lambda <- g lambda (per row); factors of exactly 1 leave lambda unchanged
+    bool unit = true;
+    for (size_t b = 0; b < batch; ++b) unit = unit && upstream_host[b] == 1.0;
+    if (!unit) {
         // pack the per-row factors as doubles inside the table buffer
         std::vector<double2> packed((batch + 1) / 2);
         std::memcpy(packed.data(), upstream_host, batch * sizeof(double));
@@ -345,7 +347,8 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
 // ------------------------------------------------------------------ observables
 
 void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
-                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s) {
+                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
+                       bool accumulate) {
     if (obs.num_qubits != n) {
         std::ostringstream m;
         m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
@@ -395,7 +398,8 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         const unsigned bx_cap = adjoint_max_blocks();
         double *partials = ctx_partials(ctx, rows * size_t(bx_cap));
         const unsigned bx = launch_pauli(psi + b0 * dim, out ? out + b0 * dim : nullptr, rows, n,
-                                         dw, dz, dflip, dfirst, dcount, uint32_t(ng), partials, s);
+                                         dw, dz, dflip, dfirst, dcount, uint32_t(ng), partials,
+                                         accumulate, s);
         double *sums = ctx_dgrads(ctx, rows);
         launch_reduce_rows(partials, uint32_t(rows), bx, sums, s);
         double *h = ctx_hvals(ctx, rows);

@@ -326,7 +326,7 @@ struct PauliArgs {
 __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ psi,
                                                     double2 *__restrict__ out, uint64_t dim,
                                                     const __grid_constant__ PauliArgs P,
-                                                    double *__restrict__ partials) {
+                                                    double *__restrict__ partials, int accumulate) {
     __shared__ double s_red[kThreads / 32];
     const size_t roff = size_t(blockIdx.y) * dim;
     const double2 *r = psi + roff;
@@ -349,7 +349,14 @@ __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ 
             const double2 ps = f ? r[s] : pt;
             acc = cfma(w, ps, acc);
         }
-        if (out) out[roff + t] = acc;
+        if (out) {
+            if (accumulate) {
+                const double2 o = out[roff + t];
+                out[roff + t] = make_double2(o.x + acc.x, o.y + acc.y);
+            } else {
+                out[roff + t] = acc;
+            }
+        }
         ev += re_conj_mul(pt, acc);
     }
     const double tsum = block_sum(ev, s_red);
@@ -494,7 +501,7 @@ unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *par
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
                       const double2 *w, const uint64_t *z, const uint64_t *flip,
                       const uint32_t *first, const uint32_t *count, uint32_t ngroups,
-                      double *partials, cudaStream_t s) {
+                      double *partials, bool accumulate, cudaStream_t s) {
     PauliArgs P{w, z, flip, first, count, ngroups};
     const uint64_t dim = uint64_t(1) << n;
     unsigned bx = grid_for(dim);
@@ -502,8 +509,9 @@ unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n
     if (bx > cap) bx = cap < 1 ? 1 : cap;
     // algorithmic traffic: read psi once, write H psi once (when requested)
     const ProfToken tok = prof_begin(PROF_PAULI, s);
-    k_pauli<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(psi, out, dim, P, partials);
-    prof_end(tok, s, (out ? 32.0 : 16.0) * double(dim) * double(batch));
+    k_pauli<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(psi, out, dim, P, partials,
+                                                           accumulate ? 1 : 0);
+    prof_end(tok, s, (out ? (accumulate ? 48.0 : 32.0) : 16.0) * double(dim) * double(batch));
     check_cuda(cudaGetLastError(), "observable kernel launch");
     return bx;
 }

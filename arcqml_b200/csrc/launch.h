@@ -21,7 +21,14 @@ unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *par
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
                       const double2 *w, const uint64_t *z, const uint64_t *flip,
                       const uint32_t *first, const uint32_t *count, uint32_t ngroups,
-                      double *partials, cudaStream_t s);
+                      double *partials, bool accumulate, cudaStream_t s);
+
+// Moves the slices of a shard with slice value y != skip (bit i of y at positions[i]) between
+// the shard and staging blocks [block][chunk_len], for other-index o in [chunk_begin, +chunk_len).
+void launch_slices(double2 *amps, uint32_t n_local, const uint32_t *positions, uint32_t k,
+                   uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip, double2 *staging,
+                   bool unpack, cudaStream_t s);
+constexpr uint32_t kMaxSliceBits = 8;
 
 Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,
                             const uint64_t *phase, size_t num_terms);

@@ -13,8 +13,9 @@ enum ProfCategory {
     PROF_ADJ_STEP = 3,   // per-gate adjoint steps
     PROF_PAULI = 4,      // observable passes
     PROF_OTHER = 5,      // reductions, scaling, norms, basis states
+    PROF_SHARD = 6,      // shard slice packing for global-qubit swaps
 };
-constexpr int kProfCategories = 6;
+constexpr int kProfCategories = 7;
 
 struct ProfToken {
     int cat = -1;

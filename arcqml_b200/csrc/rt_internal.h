@@ -163,9 +163,11 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
                              const double *upstream_host, const uint8_t *req, size_t req_len,
                              double *grads_host, size_t grads_len, ThreadContext &ctx,
                              cudaStream_t s);
-// values_host[b] = <psi_b|H|psi_b>; when out != null also writes out = H psi.
+// values_host[b] = <psi_b|H|psi_b>; when out != null also writes out = H psi, or adds H psi
+// to out when `accumulate` is set.
 void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
-                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s);
+                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
+                       bool accumulate = false);
 
 // Copies host tables (dense matrices of custom gates) into the context's table buffer;
 // returns device pointers in the same order. Valid until the next call on this thread.

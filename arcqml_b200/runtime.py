@@ -120,6 +120,9 @@ def load():
         "arcqml_rt_v2_parameter_derivative": (I32, [P, P, S, S, P, P, S, S, P]),
         "arcqml_rt_v2_expectation": (I32, [P, P, S, S, P, P]),
         "arcqml_rt_v2_expectation_and_apply": (I32, [P, P, P, S, S, P, P]),
+        "arcqml_rt_v2_expectation_and_accumulate": (I32, [P, P, P, S, S, P, P]),
+        "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
+                                            I32, P]),
         "arcqml_rt_v2_adjoint_backward": (I32, [P, P, P, S, S, P, P, S, P, S, P]),
         "arcqml_rt_v2_norms": (I32, [P, S, S, P, P]),
         "arcqml_rt_v2_norms_noalloc": (I32, [P, S, S, P, P]),
@@ -408,6 +411,16 @@ class Observable:
             vals.ctypes.data, _stream_ptr(stream)))
         return vals
 
+    def expectation_and_accumulate(self, state, out_state, num_qubits: int,
+                                   stream=None) -> np.ndarray:
+        """out_state += H psi; returns <psi|H|psi> per row."""
+        b = _rows(state, num_qubits)
+        vals = np.zeros(b, dtype=np.float64)
+        _status(load().arcqml_rt_v2_expectation_and_accumulate(
+            C.byref(self.raw), _dev_ptr(state), _dev_ptr(out_state), b, num_qubits,
+            vals.ctypes.data, _stream_ptr(stream)))
+        return vals
+
     def __del__(self):
         if _lib is not None and getattr(self, "raw", None) is not None:
             _lib.arcqml_rt_v2_observable_destroy(C.byref(self.raw))
@@ -473,7 +486,17 @@ def set_basis_state_device(state, num_qubits: int, index: int = 0, stream=None) 
 # ------------------------------------------------------------------ kernel timing
 
 PROFILE_CATEGORIES = ("gate", "fused_forward", "fused_adjoint", "adjoint_step", "observable",
-                      "other")
+                      "other", "shard_slices")
+
+
+def shard_slices(shard, num_local_qubits: int, positions: Sequence[int], chunk_begin: int,
+                 chunk_len: int, skip_value: int, staging, unpack: bool, stream=None) -> None:
+    """Moves slices of a shard to (unpack=False) or from (unpack=True) contiguous staging
+    blocks, one block per slice value other than ``skip_value`` (see arcqml_rt_v2_shard_slices)."""
+    pos = (C.c_uint32 * len(positions))(*positions)
+    _status(load().arcqml_rt_v2_shard_slices(
+        _dev_ptr(shard), num_local_qubits, pos, len(positions), chunk_begin, chunk_len,
+        skip_value, _dev_ptr(staging), int(bool(unpack)), _stream_ptr(stream)))
 
 
 def profile_enable(on: bool = True) -> None:

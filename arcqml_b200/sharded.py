@@ -1,0 +1,616 @@
+"""One statevector sharded over the ranks of a process group on its highest ("global") qubits.
+
+With P = 2^g ranks, rank r holds the 2^(n-g) amplitudes whose physical index has r in its top g
+bits. A layout maps every logical qubit to a physical bit position; positions below
+``n_local = n - g`` are local (inside every shard), the top g are global (the rank's bits).
+
+* Gates run on the ranks' shards through the runtime's device entry points, with qubits renamed
+  to their physical positions. An op that touches a global qubit first triggers a swap: the
+  needed global qubits trade places with local qubits, chosen as those whose next use lies
+  farthest ahead (the layout planner below). The ops between swaps are scheduled as a list over
+  the circuit's dependency order (ops on disjoint qubits commute), so every op whose qubits are
+  all local runs before a swap is paid.
+* A swap of k qubits is an all-to-all among 2^k ranks: each rank packs the slices of its shard
+  that belong to the other ranks (``arcqml_rt_v2_shard_slices``), exchanges them with
+  point-to-point NCCL calls through ``torch.distributed``, and unpacks what it receives into the
+  slots it emptied. Chunks are double-buffered so packing overlaps the transfer.
+* The observable's terms are evaluated in groups, one per layout in which no flip bit (X/Y) of
+  the group lies on a global qubit; a Z on a global qubit becomes a per-rank sign on the
+  coefficient. ``H psi`` accumulates over the groups (``arcqml_rt_v2_expectation_and_accumulate``)
+  and moves with psi when the layout changes. The value is summed over ranks.
+* The adjoint sweep schedules the reversed op list from the observable's final layout, swaps psi
+  and lambda together, and sums the per-rank gradient partials over ranks at the end.
+
+Semantics follow the single-device path (``simulator.StateVectorSimulator``), i.e. the
+reference's run/backward (``crates/arcqml-sim/src/statevector/execution/adjoint/single.rs:29-163``)
+and observable (``crates/arcqml-observable/src/compiled_hamiltonian.rs:30-182``); results agree
+to rounding (ops that commute may run in a different order).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from .circuit import Circuit, PlanOp
+from .observable import SparsePauliOp
+
+INF = 1 << 62
+
+
+class ShardError(ValueError):
+    pass
+
+
+# ---------------------------------------------------------------------------- layout planning
+
+
+class Layout:
+    """Logical qubit -> physical bit position; positions >= n_local are global."""
+
+    def __init__(self, num_qubits: int, global_qubits: int):
+        if global_qubits < 0 or global_qubits >= num_qubits:
+            raise ShardError(f"cannot shard {num_qubits} qubits over 2^{global_qubits} ranks")
+        self.n = num_qubits
+        self.g = global_qubits
+        self.n_local = num_qubits - global_qubits
+        self.pos = list(range(num_qubits))
+        self.at = list(range(num_qubits))
+
+    def copy(self) -> "Layout":
+        c = Layout.__new__(Layout)
+        c.n, c.g, c.n_local = self.n, self.g, self.n_local
+        c.pos, c.at = list(self.pos), list(self.at)
+        return c
+
+    def is_local(self, q: int) -> bool:
+        return self.pos[q] < self.n_local
+
+    def global_qubits(self) -> List[int]:
+        return [self.at[p] for p in range(self.n_local, self.n)]
+
+    def apply_swap(self, pairs: Sequence[Tuple[int, int]]) -> None:
+        for pg, pl in pairs:
+            a, b = self.at[pg], self.at[pl]
+            self.at[pg], self.at[pl] = b, a
+            self.pos[a], self.pos[b] = pl, pg
+
+    def physical_mask(self, mask: int) -> int:
+        out = 0
+        q = 0
+        while mask:
+            if mask & 1:
+                out |= 1 << self.pos[q]
+            mask >>= 1
+            q += 1
+        return out
+
+
+@dataclass
+class SwapStep:
+    pairs: List[Tuple[int, int]]  # (global position, local position)
+
+
+@dataclass
+class OpsStep:
+    ops: List[PlanOp]                                 # qubits renamed to physical positions
+    indices: List[int] = field(default_factory=list)  # positions in the input op list
+
+
+@dataclass
+class TermsStep:
+    groups: List[int]  # indices into the flip-mask group list
+
+
+def _pair(layout: Layout, bring: Sequence[int], evict: Sequence[int]) -> List[Tuple[int, int]]:
+    gpos = sorted(layout.pos[q] for q in bring)
+    lpos = sorted(layout.pos[q] for q in evict)
+    return list(zip(gpos, lpos))
+
+
+def schedule_ops(ops: Sequence[PlanOp], layout: Layout) -> Tuple[list, Layout]:
+    """List-schedules ops (in dependency order) into OpsStep / SwapStep items.
+
+    Returns the steps and the layout after them; ``layout`` itself is not modified.
+    """
+    L = layout.copy()
+    n = L.n
+    m = len(ops)
+    for i, op in enumerate(ops):
+        if len(set(op.qubits)) > L.n_local:
+            raise ShardError(f"operation {i} acts on {len(op.qubits)} qubits, a shard holds "
+                             f"only {L.n_local} local qubits")
+        for q in op.qubits:
+            if not 0 <= q < n:
+                raise ShardError(f"operation {i} uses qubit {q} outside the {n}-qubit state")
+    queues: List[List[int]] = [[] for _ in range(n)]
+    for i, op in enumerate(ops):
+        for q in dict.fromkeys(op.qubits):
+            queues[q].append(i)
+    head = [0] * n
+
+    def is_ready(i):
+        return all(head[q] < len(queues[q]) and queues[q][head[q]] == i
+                   for q in dict.fromkeys(ops[i].qubits))
+
+    ready = set(i for i in range(m) if is_ready(i))
+    steps: list = []
+    cur_ops: List[PlanOp] = []
+    cur_idx: List[int] = []
+    done = 0
+
+    def emit(i):
+        op = ops[i]
+        cur_ops.append(PlanOp(op.opcode, tuple(L.pos[q] for q in op.qubits), op.params,
+                              op.matrix, op.bindings, op.name))
+        cur_idx.append(i)
+        ready.discard(i)
+        for q in dict.fromkeys(op.qubits):
+            head[q] += 1
+            if head[q] < len(queues[q]):
+                j = queues[q][head[q]]
+                if is_ready(j):
+                    ready.add(j)
+
+    while done < m:
+        progressed = True
+        while progressed:
+            progressed = False
+            for i in sorted(ready):
+                if i in ready and all(L.is_local(q) for q in ops[i].qubits):
+                    emit(i)
+                    done += 1
+                    progressed = True
+        if done == m:
+            break
+        if cur_ops:
+            steps.append(OpsStep(cur_ops, cur_idx))
+            cur_ops, cur_idx = [], []
+        # bring in the global qubits of as many blocked ops as fit, oldest first
+        bring: List[int] = []
+        protect: set = set()
+        for i in sorted(ready):
+            qs = list(dict.fromkeys(ops[i].qubits))
+            need = [q for q in qs if not L.is_local(q) and q not in bring]
+            prot = protect | {q for q in qs if L.is_local(q)}
+            free = [q for q in L.at[:L.n_local] if q not in prot]
+            if len(bring) + len(need) <= len(free):
+                bring += need
+                protect = prot
+        assert bring, "scheduler made no progress"
+        free = [q for q in L.at[:L.n_local] if q not in protect]
+
+        def next_use(q):
+            return queues[q][head[q]] if head[q] < len(queues[q]) else INF
+
+        # farthest next use first; among equals the higher position (longer contiguous runs)
+        free.sort(key=lambda q: (-next_use(q), -L.pos[q]))
+        evict = free[:len(bring)]
+        pairs = _pair(L, bring, evict)
+        steps.append(SwapStep(pairs))
+        L.apply_swap(pairs)
+    if cur_ops:
+        steps.append(OpsStep(cur_ops, cur_idx))
+    return steps, L
+
+
+def schedule_terms(flips: Sequence[int], layout: Layout) -> Tuple[list, Layout]:
+    """Splits flip-mask groups into TermsStep items, each evaluable with no flip bit on a global
+    qubit, separated by SwapStep items. Returns the steps and the final layout."""
+    L = layout.copy()
+    n = L.n
+    remaining = list(range(len(flips)))
+    steps: list = []
+    while remaining:
+        gmask = 0
+        for q in L.global_qubits():
+            gmask |= 1 << q
+        ok = [i for i in remaining if not (flips[i] & gmask)]
+        if ok:
+            steps.append(TermsStep(ok))
+            okset = set(ok)
+            remaining = [i for i in remaining if i not in okset]
+        if not remaining:
+            break
+        first = flips[remaining[0]]
+        cand = [q for q in range(n) if not (first >> q) & 1]
+        if len(cand) < L.g:
+            raise ShardError(f"a Pauli term flips {bin(first).count('1')} qubits; with "
+                             f"{L.g} global qubits at most {L.n_local} can be flipped")
+        count = [0] * n
+        for i in remaining:
+            f = flips[i]
+            for q in range(n):
+                if (f >> q) & 1:
+                    count[q] += 1
+        cand.sort(key=lambda q: (count[q], 0 if not L.is_local(q) else 1, -L.pos[q]))
+        chosen = set(cand[:L.g])
+        bring = [q for q in L.global_qubits() if q not in chosen]
+        evict = [q for q in chosen if L.is_local(q)]
+        pairs = _pair(L, bring, evict)
+        steps.append(SwapStep(pairs))
+        L.apply_swap(pairs)
+    return steps, L
+
+
+def flip_groups(terms) -> Tuple[List[int], List[List[int]]]:
+    """Distinct flip masks in first-appearance order and the term indices of each."""
+    flips: List[int] = []
+    members: Dict[int, List[int]] = {}
+    for k, (_, f, _, _) in enumerate(terms):
+        if f not in members:
+            members[f] = []
+            flips.append(f)
+        members[f].append(k)
+    return flips, [members[f] for f in flips]
+
+
+def local_terms(terms, member_lists, layout: Layout, rank: int):
+    """(coefficients, local flip masks, local phase masks) of the given term groups on `rank`:
+    masks renamed to physical positions; the phase bits on global positions (Z factors only,
+    as the groups flip no global qubit) become the sign (-1)^popcount(rank bits & phase)."""
+    coef, flip, phase = [], [], []
+    local_mask = (1 << layout.n_local) - 1
+    for ks in member_lists:
+        for k in ks:
+            c, f, p, _ = terms[k]
+            fp = layout.physical_mask(f)
+            pp = layout.physical_mask(p)
+            assert fp & ~local_mask == 0
+            sign = -1.0 if bin((pp >> layout.n_local) & rank).count("1") & 1 else 1.0
+            coef.append(sign * c)
+            flip.append(fp)
+            phase.append(pp & local_mask)
+    return (np.asarray(coef, dtype=np.float64), np.asarray(flip, dtype=np.uint64),
+            np.asarray(phase, dtype=np.uint64))
+
+
+# ---------------------------------------------------------------------------- communication
+
+
+class DistComm:
+    """Point-to-point exchange and sums over a torch.distributed process group."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+        self.nccl = dist.get_backend(group) == "nccl"
+
+    def _global(self, r: int) -> int:
+        if self.group is None:
+            return r
+        return self.dist.get_global_rank(self.group, r)
+
+    def exchange_start(self, sends: Dict[int, object], recvs: Dict[int, object]):
+        """Starts sends[peer] -> peer and recvs[peer] <- peer; returns a handle for wait()."""
+        import torch
+        ops = []
+        for peer in sorted(set(sends) | set(recvs)):
+            if peer in sends:
+                ops.append(self.dist.P2POp(self.dist.isend, torch.view_as_real(sends[peer]),
+                                           self._global(peer), self.group))
+            if peer in recvs:
+                ops.append(self.dist.P2POp(self.dist.irecv, torch.view_as_real(recvs[peer]),
+                                           self._global(peer), self.group))
+        return self.dist.batch_isend_irecv(ops) if ops else []
+
+    @staticmethod
+    def wait(handle) -> None:
+        for w in handle:
+            w.wait()
+
+    def allreduce_sum(self, values: np.ndarray) -> np.ndarray:
+        import torch
+        dev = torch.device("cuda", torch.cuda.current_device()) if self.nccl else torch.device("cpu")
+        t = torch.from_numpy(np.ascontiguousarray(values, dtype=np.float64)).to(dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
+        return t.cpu().numpy()
+
+    def allgather(self, shard):
+        import torch
+        parts = [torch.empty_like(shard) for _ in range(self.size)]
+        self.dist.all_gather([torch.view_as_real(p) for p in parts], torch.view_as_real(shard),
+                             group=self.group)
+        return parts
+
+
+# ---------------------------------------------------------------------------- device backend
+
+
+class RuntimeBackend:
+    """Local compute on this rank's GPU through the runtime's v2 entry points."""
+
+    def __init__(self, device=None):
+        import torch
+        from . import runtime as rt
+        if not torch.cuda.is_available():
+            raise ShardError("the sharded statevector runtime needs a CUDA device")
+        self.rt = rt
+        self.torch = torch
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+
+    def empty(self, numel: int):
+        return self.torch.empty(numel, dtype=self.torch.complex128, device=self.device)
+
+    def zeros(self, numel: int):
+        return self.torch.zeros(numel, dtype=self.torch.complex128, device=self.device)
+
+    def from_numpy(self, a: np.ndarray):
+        return self.torch.from_numpy(np.ascontiguousarray(a, dtype=np.complex128)).to(self.device)
+
+    def set_amplitude_one(self, shard, index: int) -> None:
+        """shard <- |index> (every other amplitude zero)."""
+        self.rt.set_basis_state_device(shard, int(shard.numel()).bit_length() - 1, index)
+
+    def apply(self, ops: Sequence[PlanOp], shard, n_local: int) -> None:
+        if not ops:
+            return
+        plan = self.rt.CircuitPlan.create(ops)
+        self.rt.plan_apply_device(plan, shard, n_local)
+
+    def adjoint(self, ops: Sequence[PlanOp], psi, lam, n_local: int, upstream: float, req,
+                grads: np.ndarray) -> None:
+        plan = self.rt.CircuitPlan.create(ops)
+        grads += self.rt.adjoint_backward_device(plan, psi, lam, n_local, float(upstream), req,
+                                                 len(grads))
+
+    def observable(self, coef, flip, phase, psi, out, n_local: int) -> float:
+        obs = self.rt.Observable(n_local, coef, flip, phase)
+        if out is None:
+            return float(obs.expectation(psi, n_local)[0])
+        return float(obs.expectation_and_accumulate(psi, out, n_local)[0])
+
+    def slices(self, shard, n_local, positions, chunk_begin, chunk_len, skip, staging,
+               unpack) -> None:
+        self.rt.shard_slices(shard, n_local, positions, chunk_begin, chunk_len, skip, staging,
+                             unpack)
+
+
+# ---------------------------------------------------------------------------- simulator
+
+
+@dataclass
+class SwapStats:
+    swaps: int = 0
+    qubits: int = 0
+    bytes_sent: int = 0
+
+
+class ShardedStateVectorSimulator:
+    """A single n-qubit state over all ranks of ``comm`` (a power-of-two count).
+
+    ``run(circuit, observable)`` returns ``(value, ctx)``-style results like
+    ``StateVectorSimulator.run``; ``backward(upstream)`` returns the parameter gradients summed
+    over ranks (same on every rank).
+    """
+
+    def __init__(self, num_qubits: int, comm=None, backend=None, chunk_amplitudes: int = 1 << 24):
+        self.comm = comm if comm is not None else DistComm()
+        self.backend = backend if backend is not None else RuntimeBackend()
+        size = self.comm.size
+        if size & (size - 1):
+            raise ShardError(f"world size {size} is not a power of two")
+        g = size.bit_length() - 1
+        if num_qubits - g < 1:
+            raise ShardError(f"{num_qubits} qubits cannot be sharded over {size} ranks")
+        self.num_qubits = num_qubits
+        self.layout = Layout(num_qubits, g)
+        self.rank = self.comm.rank
+        self.chunk = max(1, int(chunk_amplitudes))
+        self.stats = SwapStats()
+        self._events = None
+        self._staging = None
+        self.psi = None
+        self.lam = None
+        self._ctx = None
+
+    @property
+    def n_local(self) -> int:
+        return self.layout.n_local
+
+    # -- state ---------------------------------------------------------------------------
+    def reset(self) -> None:
+        """|0...0>: amplitude 1 at physical index 0, which rank 0 holds."""
+        self.layout = Layout(self.num_qubits, self.layout.g)
+        d = 1 << self.n_local
+        if self.psi is None or self.psi.numel() != d:
+            self.psi = self.backend.empty(d)
+        if self.rank == 0:
+            self.backend.set_amplitude_one(self.psi, 0)
+        else:
+            self.psi.zero_()
+
+    def load(self, full_amplitudes) -> None:
+        """Takes this rank's part of a full state given in logical order (tests, small n)."""
+        self.layout = Layout(self.num_qubits, self.layout.g)
+        a = np.ascontiguousarray(full_amplitudes, dtype=np.complex128).reshape(-1)
+        d = 1 << self.n_local
+        self.psi = self.backend.from_numpy(a[self.rank * d:(self.rank + 1) * d])
+
+    def amplitudes(self, which: str = "psi") -> np.ndarray:
+        """Full state in logical order on every rank (gathers all shards; tests, small n)."""
+        shard = self.psi if which == "psi" else self.lam
+        parts = self.comm.allgather(shard.contiguous())
+        full = np.concatenate([p.cpu().numpy() for p in parts])
+        n = self.num_qubits
+        idx = np.arange(1 << n, dtype=np.int64)
+        phys = np.zeros_like(idx)
+        for q in range(n):
+            phys |= ((idx >> q) & 1) << self.layout.pos[q]
+        return full[phys]
+
+    # -- swaps ---------------------------------------------------------------------------
+    def timing(self, on: bool):
+        """Starts (True) or stops (False) timing the swaps with CUDA events on the current
+        stream; stopping returns {swaps, qubits, bytes_sent, ms} since the start."""
+        import torch
+        if on:
+            self.stats = SwapStats()
+            self._events = []
+            return None
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in (self._events or []))
+        self._events = None
+        return dict(swaps=self.stats.swaps, qubits=self.stats.qubits,
+                    bytes_sent=self.stats.bytes_sent, ms=ms)
+
+    def _staging_for(self, numel: int):
+        if self._staging is None or self._staging[0][0].numel() < numel:
+            self._staging = [(self.backend.empty(numel), self.backend.empty(numel))
+                             for _ in range(2)]
+        return self._staging
+
+    def _swap(self, pairs: Sequence[Tuple[int, int]], tensors: Sequence) -> None:
+        L = self.layout
+        n_l = L.n_local
+        k = len(pairs)
+        gbits = [pg - n_l for pg, _ in pairs]
+        lpos = [pl for _, pl in pairs]
+        x = 0
+        for i, b in enumerate(gbits):
+            x |= ((self.rank >> b) & 1) << i
+        peers = {}
+        for y in range(1 << k):
+            if y == x:
+                continue
+            r = self.rank
+            for i, b in enumerate(gbits):
+                r = (r & ~(1 << b)) | (((y >> i) & 1) << b)
+            peers[y] = r
+        others = 1 << (n_l - k)
+        nblk = (1 << k) - 1
+        chunk = min(others, max(1, self.chunk // nblk))
+        chunk = 1 << (chunk.bit_length() - 1)
+        stage = self._staging_for(nblk * chunk)
+        be = self.backend
+        ev = None
+        if self._events is not None:
+            import torch
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+
+        def views(buf):
+            return {peers[y]: buf[(y - (1 if y > x else 0)) * chunk:
+                                  (y - (1 if y > x else 0) + 1) * chunk] for y in peers}
+
+        # Two staging sets: chunk j is packed and put on the wire while chunk j-1, already
+        # received, is unpacked.
+        jobs = [(t, c0) for t in tensors for c0 in range(0, others, chunk)]
+        pending = None  # (tensor, c0, recv buffer, handle)
+        for j, (t, c0) in enumerate(jobs):
+            send, recv = stage[j & 1]
+            be.slices(t, n_l, lpos, c0, chunk, x, send, False)
+            h = self.comm.exchange_start(views(send), views(recv))
+            if pending is not None:
+                pt, pc0, precv, ph = pending
+                self.comm.wait(ph)
+                be.slices(pt, n_l, lpos, pc0, chunk, x, precv, True)
+            pending = (t, c0, recv, h)
+        if pending is not None:
+            pt, pc0, precv, ph = pending
+            self.comm.wait(ph)
+            be.slices(pt, n_l, lpos, pc0, chunk, x, precv, True)
+        if ev is not None:
+            ev[1].record()
+            self._events.append(ev)
+        self.stats.swaps += 1
+        self.stats.qubits += k
+        self.stats.bytes_sent += len(tensors) * nblk * others * 16
+        L.apply_swap(pairs)
+
+    # -- forward / observable / adjoint on plan ops -------------------------------------------
+    def forward(self, ops: Sequence[PlanOp]) -> None:
+        """psi <- U_m ... U_1 psi for plan ops in logical qubits (starts from |0...0> if unset)."""
+        if self.psi is None:
+            self.reset()
+        steps, _ = schedule_ops(ops, self.layout)
+        for st in steps:
+            if isinstance(st, SwapStep):
+                self._swap(st.pairs, [self.psi])
+            else:
+                self.backend.apply(st.ops, self.psi, self.n_local)
+
+    def observe(self, terms, keep_lambda: bool) -> float:
+        """<psi|H|psi> summed over ranks for compiled terms (coef, flip, phase, y); with
+        keep_lambda the shards of H psi are kept (as lambda) for ``adjoint``."""
+        flips, members = flip_groups(terms)
+        if keep_lambda:
+            if self.lam is None or self.lam.numel() != self.psi.numel():
+                self.lam = self.backend.empty(self.psi.numel())
+            self.lam.zero_()
+        else:
+            self.lam = None
+        tsteps, _ = schedule_terms(flips, self.layout)
+        partial = 0.0
+        for st in tsteps:
+            if isinstance(st, SwapStep):
+                self._swap(st.pairs, [self.psi] + ([self.lam] if keep_lambda else []))
+            else:
+                coef, flip, phase = local_terms(terms, [members[i] for i in st.groups],
+                                                self.layout, self.rank)
+                partial += self.backend.observable(coef, flip, phase, self.psi, self.lam,
+                                                   self.n_local)
+        return float(self.comm.allreduce_sum(np.array([partial]))[0])
+
+    def adjoint(self, ops: Sequence[PlanOp], upstream: float, requires_grad) -> np.ndarray:
+        """Reverse sweep over ops from (psi, lambda = H psi): lambda <- g lambda, then per op
+        psi <- U^dag psi, grads[parent] += 2 Re<lambda|dU psi>, lambda <- U^dag lambda. Returns
+        the gradients summed over ranks (len(requires_grad) entries, index = parent)."""
+        if self.lam is None:
+            raise ShardError("adjoint needs lambda: call observe(..., keep_lambda=True) first")
+        req = list(requires_grad)
+        steps, _ = schedule_ops(list(reversed(ops)), self.layout)
+        grads = np.zeros(len(req), dtype=np.float64)
+        first = True
+        for st in steps:
+            if isinstance(st, SwapStep):
+                self._swap(st.pairs, [self.psi, self.lam])
+            else:
+                self.backend.adjoint(list(reversed(st.ops)), self.psi, self.lam, self.n_local,
+                                     upstream if first else 1.0, req, grads)
+                first = False
+        if first:
+            self.backend.adjoint([], self.psi, self.lam, self.n_local, upstream, req, grads)
+        return self.comm.allreduce_sum(grads)
+
+    # -- run / backward (circuit API) ----------------------------------------------------------
+    def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True,
+            initial_shard=None) -> float:
+        """Applies the circuit to |0...0> (or to ``initial_shard``: this rank's 2^n_local
+        amplitudes of the initial state in logical order, e.g. a pinned host tensor, copied on
+        the current stream) and returns <H>; keeps psi and H psi for ``backward``."""
+        if circuit.num_qubits != self.num_qubits or observable.num_qubits != self.num_qubits:
+            raise ShardError("circuit, observable and simulator qubit counts differ")
+        records = grad and any(p.requires_grad for p in circuit.parameters)
+        ops = circuit.compile_plan(1 if records else 0)
+        if initial_shard is None:
+            self.reset()
+        else:
+            if initial_shard.numel() != (1 << self.n_local):
+                raise ShardError(f"initial shard must hold 2^{self.n_local} amplitudes")
+            self.layout = Layout(self.num_qubits, self.layout.g)
+            if self.psi is None or self.psi.numel() != initial_shard.numel():
+                self.psi = self.backend.empty(initial_shard.numel())
+            self.psi.copy_(initial_shard.reshape(-1), non_blocking=True)
+        self.forward(ops)
+        value = self.observe(observable.compiled_terms(), records)
+        self._ctx = (ops, circuit) if records else None
+        return value
+
+    def backward(self, upstream: float = 1.0) -> np.ndarray:
+        """Adjoint sweep; returns the parameter gradients (index i = circuit parameter i)."""
+        if self._ctx is None:
+            raise ShardError("run was executed without gradient recording")
+        ops, circuit = self._ctx
+        grads = self.adjoint(ops, upstream, circuit.requires_grad_mask(True, False))
+        self._ctx = None
+        pgrads = grads[1:].copy()
+        for p, g in zip(circuit.parameters, pgrads):
+            if p.requires_grad:
+                g = float(np.float32(g)) if p.dtype == "f32" else float(g)
+                p.grad = g if getattr(p, "grad", None) is None else p.grad + g
+        return pgrads

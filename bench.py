@@ -12,6 +12,11 @@ adjoint sweep) x steps / device time. ``e2e`` times the same step through the pu
 API with the initial state copied from pinned host memory every step and the value and
 gradients read back to the host.
 
+With ``--gpus N`` (N > 1, one process per GPU under torchrun) the same 32-qubit state is sharded
+over the N GPUs on its top log2(N) qubits (``arcqml_b200.sharded``): strong scaling, the
+whole-job rate over the max-over-ranks device time. Global-qubit swaps go over NCCL; their
+count, bytes and time are reported under ``swaps``.
+
 ``--impl reference`` times the CPU oracle (the f64 restatement of the reference's algorithm;
 the reference's own runtime is a closed Windows library) on the host cores with a bounded
 sample of the same workload (fewer qubits and layers), scaled to 32 qubits by state size.
@@ -65,7 +70,8 @@ def config(args, c):
             "gates": len(c.operations), "parameters": c.num_parameters(),
             "state_bytes": 16 << args.qubits,
             "l2": "state (16 * 2^n bytes) larger than the 126 MB L2; no flush needed",
-            "parallelism": f"dp1" if args.gpus == 1 else f"replicas{args.gpus}"}
+            "parallelism": "1 GPU" if args.gpus == 1 else
+            f"state sharded over {args.gpus} GPUs on its top {args.gpus.bit_length() - 1} qubits"}
 
 
 # ------------------------------------------------------------------ CPU oracle sample
@@ -169,13 +175,21 @@ def gpu_arm(args):
     rt.load()
     n = args.qubits
     c, obs = workload(n, args.layers, args.terms, args.seed)
-    sim = StateVectorSimulator(n)
     gates = len(c.operations)
+    if world == 1:
+        sim = StateVectorSimulator(n)
 
-    def step(initial=None):
-        res = sim.run(c, obs, initial_state=initial)
-        pgrads, _ = res.backward(1.0)
-        return res.value, pgrads
+        def step(initial=None):
+            res = sim.run(c, obs, initial_state=initial)
+            pgrads, _ = res.backward(1.0)
+            return res.value, pgrads
+    else:
+        from arcqml_b200.sharded import ShardedStateVectorSimulator
+        sim = ShardedStateVectorSimulator(n)
+
+        def step(initial=None):
+            value = sim.run(c, obs, initial_shard=initial)
+            return value, sim.backward(1.0)
 
     for _ in range(args.warmup):
         step()
@@ -187,6 +201,8 @@ def gpu_arm(args):
 
     clocks = Clocks(local)
     rt.profile_enable(True)
+    if world > 1:
+        sim.timing(True)
     launches0 = rt.launch_count()
     barrier()
     torch.cuda.synchronize()
@@ -210,7 +226,18 @@ def gpu_arm(args):
         ms = float(t.item())
     ms_step = ms / args.steps
     passes = 2 * gates
-    value_rate = world * passes * args.steps / (ms / 1e3)
+    value_rate = passes * args.steps / (ms / 1e3)
+    swaps = None
+    if world > 1:
+        st = sim.timing(False)
+        link = 770.0  # NVLink peer copy measured on this GPU type, GB/s per direction
+        sent = st["bytes_sent"] / args.steps
+        swap_ms = st["ms"] / args.steps
+        swaps = {"per_step": st["swaps"] / args.steps, "qubits_per_step": st["qubits"] / args.steps,
+                 "bytes_sent_per_step": sent, "ms_per_step": round(swap_ms, 3),
+                 "achieved_gbs": round(sent / (swap_ms * 1e-3) / 1e9, 1) if swap_ms else None,
+                 "peak_gbs": link, "peak_source": "measured NVLink peer copy",
+                 "frac": round(sent / (swap_ms * 1e-3) / 1e9 / link, 4) if swap_ms else None}
 
     # dominant kernel category and its roofline
     dom = max(prof.items(), key=lambda kv: kv[1][1])
@@ -232,15 +259,15 @@ def gpu_arm(args):
 
     line = {"metric": METRIC, "value": round(value_rate, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "complex128 (f64)", "data": "synthetic (seeded brickwork + random Pauli sum)",
-            "config": config(args, c), "roofline": roofline,
+            "config": config(args, c), "roofline": roofline, "swaps": swaps,
             "kernels": {k: {"launches": v[0], "ms": round(v[1], 3),
                             "gbs": round(v[2] / (v[1] * 1e-3) / 1e9, 1) if v[1] else 0}
                         for k, v in prof.items() if v[0]},
             "gpu_launches": launches, "e2e": e2e, "clocks": clk,
-            "adjoint_grads_per_s": round(world * args.steps / (ms / 1e3), 5),
-            "param_grads_per_s": round(world * c.num_parameters() * args.steps / (ms / 1e3), 2),
+            "adjoint_grads_per_s": round(args.steps / (ms / 1e3), 5),
+            "param_grads_per_s": round(c.num_parameters() * args.steps / (ms / 1e3), 2),
             "check": {"value": value, "grad_norm": float(np.linalg.norm(grads))}}
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, cores, sample, _ = cpu_sample(args)
@@ -254,11 +281,14 @@ def gpu_arm(args):
 
 def e2e_arm(args, step, n, world, passes):
     import torch
+    g = world.bit_length() - 1
+    rank = int(os.environ.get("RANK", "0"))
     try:
-        host = torch.zeros(1 << n, dtype=torch.complex128, pin_memory=True)
+        host = torch.zeros(1 << (n - g), dtype=torch.complex128, pin_memory=True)
     except Exception as exc:  # pinned host memory unavailable
         return {"value": None, "unit": UNIT, "unavailable": f"pinned host buffer: {exc}"}
-    host[0] = 1.0
+    if rank == 0:
+        host[0] = 1.0
     step(host)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -270,9 +300,11 @@ def e2e_arm(args, step, n, world, passes):
         t = torch.tensor([dt], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         dt = float(t.item())
-    return {"value": round(world * passes * args.steps / dt, 3), "unit": UNIT,
+    return {"value": round(passes * args.steps / dt, 3), "unit": UNIT,
             "h2d_bytes_per_step": int(16 << n), "d2h_bytes_per_step": int(8 * (len(grads) + 2)),
-            "path": "StateVectorSimulator.run(initial_state=pinned host) + backward"}
+            "path": "StateVectorSimulator.run(initial_state=pinned host) + backward" if world == 1
+            else "ShardedStateVectorSimulator.run(initial_shard=pinned host) + backward, "
+                 "every rank its shard"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -293,7 +325,7 @@ def reference_arm(args):
     c, _ = workload(args.qubits, args.layers, args.terms, args.seed)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "complex128 (f64)", "data": "synthetic (seeded brickwork + random Pauli sum)",
             "config": config(args, c),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",

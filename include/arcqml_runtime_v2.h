@@ -77,6 +77,30 @@ int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128
                                       size_t parameter_requires_grad_len, double *gradients,
                                       size_t gradients_len, void *stream);
 
+/* Same as arcqml_rt_v2_expectation_and_apply but ADDS H psi to `output` (output += H psi) and
+ * returns this call's <psi|H|psi> in values. Lets a caller sum H psi over several observables
+ * that share one output buffer; a sharded state evaluates its terms in groups, one group per
+ * qubit layout (no reference counterpart: the reference's observables run in one piece,
+ * compiled_hamiltonian.rs:104-182). */
+int32_t arcqml_rt_v2_expectation_and_accumulate(const ArcqmlObservableHandle *observable,
+                                                const arcqml_c128 *amplitudes, arcqml_c128 *output,
+                                                size_t batch, size_t num_qubits, double *values,
+                                                void *stream);
+
+/* Global-qubit swap support for one state sharded over ranks on its highest qubits (no
+ * reference counterpart: the reference runs one process). The local index of a shard of
+ * num_local_qubits qubits splits into the slice bits at positions[0..num_positions) (bit i of a
+ * slice value y sits at positions[i]) and the other bits o, in ascending order. For every slice
+ * value y != skip_value and o in [chunk_begin, chunk_begin + chunk_len):
+ *   unpack == 0: staging[block(y) * chunk_len + o - chunk_begin] <- amplitudes[index(y, o)]
+ *   unpack != 0: amplitudes[index(y, o)] <- staging[block(y) * chunk_len + o - chunk_begin]
+ * where block(y) numbers the slice values in increasing order without skip_value (pass 2^k or
+ * more to keep every value). At most 8 positions; o must stay below 2^(num_local_qubits - k). */
+int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubits,
+                                  const uint32_t *positions, size_t num_positions,
+                                  uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip_value,
+                                  arcqml_c128 *staging, int32_t unpack, void *stream);
+
 /* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);
@@ -116,7 +140,8 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
 /* Kernel timing (no reference counterpart; measurement support). While enabled, every kernel
  * launch of the runtime in these categories is bracketed by CUDA events on its own stream:
  * 0 per-gate kernels, 1 fused forward passes, 2 fused adjoint passes, 3 per-gate adjoint steps,
- * 4 observable passes, 5 other (scaling, norms, basis states). Enabling (or disabling) resets
+ * 4 observable passes, 5 other (scaling, norms, basis states), 6 shard slice packing for
+ * global-qubit swaps. Enabling (or disabling) resets
  * the totals. */
 void arcqml_rt_v2_profile_enable(int32_t on);
 /* Totals of one category since the last enable: launches, summed device time (ms) and summed

@@ -1,0 +1,223 @@
+"""Test support for the sharded statevector: a CPU shard backend over the oracle, the slice
+packing rule in numpy, an in-process communicator for ranks run as threads, and the worker that
+the gloo tests start once per rank.
+
+Nothing here is used by the package: ``arcqml_b200.sharded`` runs its shards on the GPU runtime
+(``RuntimeBackend``) and exchanges them over ``torch.distributed``.
+"""
+from __future__ import annotations
+
+import os
+import threading
+
+import numpy as np
+
+
+def slice_index(o: np.ndarray, y: int, positions) -> np.ndarray:
+    """Local index of other-index o with slice value y (bit i of y at positions[i])."""
+    o = np.asarray(o, dtype=np.int64)
+    for p in sorted(positions):
+        o = ((o >> p) << (p + 1)) | (o & ((1 << p) - 1))
+    for i, p in enumerate(positions):
+        if (y >> i) & 1:
+            o = o | (1 << p)
+    return o
+
+
+def slices_numpy(shard: np.ndarray, positions, chunk_begin: int, chunk_len: int, skip: int,
+                 staging: np.ndarray, unpack: bool) -> None:
+    k = len(positions)
+    o = np.arange(chunk_begin, chunk_begin + chunk_len, dtype=np.int64)
+    blk = 0
+    for y in range(1 << k):
+        if y == skip:
+            continue
+        idx = slice_index(o, y, positions)
+        st = staging[blk * chunk_len:(blk + 1) * chunk_len]
+        if unpack:
+            shard[idx] = st
+        else:
+            st[:] = shard[idx]
+        blk += 1
+
+
+class OracleShardBackend:
+    """Shard compute on the CPU oracle (torch CPU tensors, numpy views)."""
+
+    def __init__(self, oracle_module):
+        import torch
+        self.O = oracle_module
+        self.torch = torch
+
+    def empty(self, numel):
+        return self.torch.empty(numel, dtype=self.torch.complex128)
+
+    def zeros(self, numel):
+        return self.torch.zeros(numel, dtype=self.torch.complex128)
+
+    def from_numpy(self, a):
+        return self.torch.from_numpy(np.ascontiguousarray(a, dtype=np.complex128).copy())
+
+    def set_amplitude_one(self, shard, index):
+        shard.zero_()
+        shard[index] = 1.0
+
+    def apply(self, ops, shard, n_local):
+        if ops:
+            shard.copy_(self.torch.from_numpy(self.O.plan_apply(ops, shard.numpy(), n_local)))
+
+    def adjoint(self, ops, psi, lam, n_local, upstream, req, grads):
+        p, l, g = self.O.adjoint_backward(ops, psi.numpy(), lam.numpy(), n_local, upstream, req,
+                                          len(grads))
+        psi.copy_(self.torch.from_numpy(p))
+        lam.copy_(self.torch.from_numpy(l))
+        grads += g
+
+    def observable(self, coef, flip, phase, psi, out, n_local):
+        terms = [(float(c), int(f), int(p), bin(int(f) & int(p)).count("1") % 4)
+                 for c, f, p in zip(coef, flip, phase)]
+        if out is None:
+            return float(self.O.expectation(terms, psi.numpy(), n_local))
+        v, h = self.O.expectation_and_apply(terms, psi.numpy(), n_local)
+        out += self.torch.from_numpy(h)
+        return float(v)
+
+    def slices(self, shard, n_local, positions, chunk_begin, chunk_len, skip, staging, unpack):
+        slices_numpy(shard.numpy(), positions, chunk_begin, chunk_len, skip, staging.numpy(),
+                     unpack)
+
+
+class ThreadHub:
+    def __init__(self, size):
+        self.size = size
+        self.barrier = threading.Barrier(size, timeout=600)
+        self.box = {}
+        self.lock = threading.Lock()
+
+
+class ThreadComm:
+    """Ranks as threads of one process: exchanges are copies between the threads' buffers."""
+
+    def __init__(self, hub: ThreadHub, rank: int):
+        self.hub = hub
+        self.rank = rank
+        self.size = hub.size
+
+    def _sync(self):
+        import torch
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+
+    def exchange_start(self, sends, recvs):
+        self._sync()
+        with self.hub.lock:
+            for peer, t in sends.items():
+                self.hub.box[(self.rank, peer)] = t
+        self.hub.barrier.wait()
+        for peer, buf in recvs.items():
+            buf.copy_(self.hub.box[(peer, self.rank)])
+        self._sync()
+        self.hub.barrier.wait()
+        with self.hub.lock:
+            for peer in sends:
+                del self.hub.box[(self.rank, peer)]
+        self.hub.barrier.wait()
+        return []
+
+    @staticmethod
+    def wait(handle):
+        pass
+
+    def _gather(self, value):
+        with self.hub.lock:
+            self.hub.box[("g", self.rank)] = value
+        self.hub.barrier.wait()
+        vals = [self.hub.box[("g", r)] for r in range(self.size)]
+        self.hub.barrier.wait()
+        with self.hub.lock:
+            del self.hub.box[("g", self.rank)]
+        self.hub.barrier.wait()
+        return vals
+
+    def allreduce_sum(self, values):
+        vals = self._gather(np.array(values, dtype=np.float64, copy=True))
+        out = np.zeros_like(vals[0])
+        for v in vals:
+            out = out + v
+        return out
+
+    def allgather(self, shard):
+        self._sync()
+        return [t.clone() for t in self._gather(shard)]
+
+
+def run_threads(size, fn):
+    """Runs fn(rank, comm) on `size` threads; returns the per-rank results (re-raises)."""
+    hub = ThreadHub(size)
+    out = [None] * size
+    errs = []
+
+    def body(r):
+        try:
+            out[r] = fn(r, ThreadComm(hub, r))
+        except BaseException as e:  # noqa: BLE001 - re-raised below
+            errs.append(e)
+            hub.barrier.abort()
+
+    ts = [threading.Thread(target=body, args=(r,)) for r in range(size)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    if errs:
+        raise errs[0]
+    return out
+
+
+# ---------------------------------------------------------------------------- gloo worker
+
+
+def sharded_case(sim, ops, terms, init, upstream, req):
+    """Forward, observable and adjoint on the sharded simulator; returns what the tests
+    compare: value, psi_m, H psi (logical order), gradients, psi_0, lambda_0."""
+    sim.load(init)
+    sim.forward(ops)
+    psi_m = sim.amplitudes("psi")
+    value = sim.observe(terms, True)
+    hpsi = sim.amplitudes("lam")
+    grads = sim.adjoint(ops, upstream, req)
+    return dict(value=value, psi_m=psi_m, hpsi=hpsi, grads=grads,
+                psi0=sim.amplitudes("psi"), lam0=sim.amplitudes("lam"),
+                swaps=sim.stats.swaps)
+
+
+def gloo_worker(rank, size, port, case, queue):
+    """One rank of a world on gloo (CPU): runs `case` through the sharded simulator."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "oracle"), here):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(size))
+    import datetime
+
+    import torch.distributed as dist
+
+    import oracle as O
+    from arcqml_b200.sharded import DistComm, ShardedStateVectorSimulator
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=size,
+                                timeout=datetime.timedelta(seconds=120))
+        sim = ShardedStateVectorSimulator(case["n"], comm=DistComm(),
+                                          backend=OracleShardBackend(O),
+                                          chunk_amplitudes=case.get("chunk", 1 << 24))
+        res = sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
+                           case["req"])
+        queue.put((rank, res))
+    except BaseException as e:  # noqa: BLE001 - reported to the parent
+        queue.put((rank, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()

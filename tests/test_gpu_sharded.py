@@ -1,0 +1,105 @@
+"""Sharded statevector on the GPU runtime (needs a B200).
+
+* the slice packing kernel against the numpy rule;
+* a whole sharded run with 4 and 8 ranks emulated as threads on one GPU (exchanges are device
+  copies), compared with the oracle at 1e-10 — this exercises every kernel of the sharded path;
+* with two or more GPUs, the same run over NCCL with one process per GPU (torchrun).
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from arcqml_b200.workloads import brickwork, random_pauli_sum
+from plans import random_plan, random_state, random_terms
+from shard_support import run_threads, sharded_case, slices_numpy
+from test_sharded_host import check_world, expected
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.mark.parametrize("positions,chunk_begin,chunk_len,skip", [
+    ([13], 0, 1 << 12, 0), ([0, 9], 256, 1 << 10, 2), ([11, 2, 7], 0, 1 << 11, 5),
+    ([3, 12, 8, 1], 64, 200, 16)])
+def test_shard_slices_kernel_matches_numpy(runtime, positions, chunk_begin, chunk_len, skip):
+    import torch
+    n_local = 14
+    rng = np.random.Generator(np.random.PCG64(sum(positions)))
+    host = rng.normal(size=1 << n_local) + 1j * rng.normal(size=1 << n_local)
+    k = len(positions)
+    nblk = (1 << k) - (1 if skip < (1 << k) else 0)
+    dev = torch.from_numpy(host).cuda()
+    staging = torch.zeros(nblk * chunk_len, dtype=torch.complex128, device="cuda")
+    runtime.shard_slices(dev, n_local, positions, chunk_begin, chunk_len, skip, staging, False)
+    ref = np.zeros(nblk * chunk_len, dtype=np.complex128)
+    slices_numpy(host, positions, chunk_begin, chunk_len, skip, ref, False)
+    assert np.array_equal(staging.cpu().numpy(), ref)
+    back = torch.zeros_like(dev)
+    runtime.shard_slices(back, n_local, positions, chunk_begin, chunk_len, skip, staging, True)
+    hb = np.zeros_like(host)
+    slices_numpy(hb, positions, chunk_begin, chunk_len, skip, ref, True)
+    assert np.array_equal(back.cpu().numpy(), hb)
+
+
+def test_shard_slices_rejects_bad_arguments(runtime):
+    import torch
+    dev = torch.zeros(1 << 6, dtype=torch.complex128, device="cuda")
+    st = torch.zeros(1 << 6, dtype=torch.complex128, device="cuda")
+    with pytest.raises(runtime.RuntimeError, match="outside the 6-qubit shard"):
+        runtime.shard_slices(dev, 6, [6], 0, 4, 0, st, False)
+    with pytest.raises(runtime.RuntimeError, match="repeat"):
+        runtime.shard_slices(dev, 6, [1, 1], 0, 4, 0, st, False)
+    with pytest.raises(runtime.RuntimeError, match="exceeds the shard"):
+        runtime.shard_slices(dev, 6, [1], 16, 32, 0, st, False)
+
+
+def thread_world(size, case):
+    from arcqml_b200.sharded import RuntimeBackend, ShardedStateVectorSimulator
+
+    def body(rank, comm):
+        sim = ShardedStateVectorSimulator(case["n"], comm=comm, backend=RuntimeBackend(),
+                                          chunk_amplitudes=case.get("chunk", 1 << 20))
+        return sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
+                            case["req"])
+
+    return dict(enumerate(run_threads(size, body)))
+
+
+@pytest.mark.parametrize("size,n", [(4, 12), (8, 13)])
+def test_emulated_ranks_random_plan_match_oracle(runtime, oracle, size, n):
+    rng = np.random.Generator(np.random.PCG64(900 + n))
+    npar = 12
+    case = dict(n=n, ops=random_plan(rng, n, 160, npar), terms=random_terms(rng, n, 40),
+                init=random_state(rng, n), upstream=float(rng.normal()),
+                req=[1] + [int(x) for x in (rng.uniform(size=npar) < 0.8)], chunk=1 << 9)
+    res = thread_world(size, case)
+    assert res[0]["swaps"] > 0
+    check_world(res, expected(oracle, case), size)
+
+
+def test_emulated_ranks_brickwork_match_oracle(runtime, oracle):
+    n, size = 16, 8
+    c = brickwork(n, 6, seed=21)
+    rng = np.random.Generator(np.random.PCG64(17))
+    case = dict(n=n, ops=c.compile_plan(1), terms=random_pauli_sum(n, 60, seed=8).compiled_terms(),
+                init=random_state(rng, n), upstream=-0.5, req=c.requires_grad_mask(True, False))
+    res = thread_world(size, case)
+    check_world(res, expected(oracle, case), size)
+
+
+@pytest.mark.skipif("not __import__('torch').cuda.is_available() or "
+                    "__import__('torch').cuda.device_count() < 2", reason="needs 2 GPUs")
+def test_nccl_ranks_match_oracle():
+    import torch
+    size = 4 if torch.cuda.device_count() >= 4 else 2
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes", "1", "--nproc-per-node", str(size), "--master-addr", "127.0.0.1",
+           "--master-port", "29571", os.path.join(HERE, "shard_nccl_worker.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=os.path.dirname(HERE))
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "sharded-nccl-ok" in r.stdout
