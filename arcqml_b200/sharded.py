@@ -352,17 +352,23 @@ class RuntimeBackend:
         plan = self.rt.CircuitPlan.create(ops)
         self.rt.plan_apply_device(plan, shard, n_local)
 
-    def adjoint(self, ops: Sequence[PlanOp], psi, lam, n_local: int, upstream: float, req,
+    def adjoint(self, ops: Sequence[PlanOp], psi, lam, n_local: int, upstream, req,
                 grads: np.ndarray) -> None:
+        """Reverse sweep over [rows, 2^n_local] psi/lambda; upstream is a scalar or one factor
+        per row; gradients (summed over rows) are added to grads."""
         plan = self.rt.CircuitPlan.create(ops)
-        grads += self.rt.adjoint_backward_device(plan, psi, lam, n_local, float(upstream), req,
+        grads += self.rt.adjoint_backward_device(plan, psi, lam, n_local, upstream, req,
                                                  len(grads))
 
     def observable(self, coef, flip, phase, psi, out, n_local: int) -> float:
+        return float(self.observable_rows(coef, flip, phase, psi, out, n_local)[0])
+
+    def observable_rows(self, coef, flip, phase, psi, out, n_local: int) -> np.ndarray:
+        """Per-row <psi|H|psi>; adds H psi to out when given."""
         obs = self.rt.Observable(n_local, coef, flip, phase)
         if out is None:
-            return float(obs.expectation(psi, n_local)[0])
-        return float(obs.expectation_and_accumulate(psi, out, n_local)[0])
+            return obs.expectation(psi, n_local)
+        return obs.expectation_and_accumulate(psi, out, n_local)
 
     def slices(self, shard, n_local, positions, chunk_begin, chunk_len, skip, staging,
                unpack) -> None:
@@ -607,6 +613,84 @@ class ShardedStateVectorSimulator:
             raise ShardError("run was executed without gradient recording")
         ops, circuit = self._ctx
         grads = self.adjoint(ops, upstream, circuit.requires_grad_mask(True, False))
+        self._ctx = None
+        pgrads = grads[1:].copy()
+        for p, g in zip(circuit.parameters, pgrads):
+            if p.requires_grad:
+                g = float(np.float32(g)) if p.dtype == "f32" else float(g)
+                p.grad = g if getattr(p, "grad", None) is None else p.grad + g
+        return pgrads
+
+
+# ---------------------------------------------------------------------------- batch rows
+
+
+class ShardedBatchSimulator:
+    """[batch, 2^n] rows split over the ranks of ``comm`` in contiguous blocks.
+
+    Mirrors ``BatchStateVectorSimulator`` (rows independent, per-row upstream factors, gradients
+    summed over rows: ``crates/arcqml-sim/src/statevector/execution/adjoint/row_major.rs:108-162``)
+    with the rows of each rank on its own GPU: ``run`` returns all B values (gathered), and
+    ``backward`` returns the gradients summed over every row of every rank.
+    """
+
+    def __init__(self, num_qubits: int, batch_size: int, comm=None, backend=None):
+        self.comm = comm if comm is not None else DistComm()
+        self.backend = backend if backend is not None else RuntimeBackend()
+        size = self.comm.size
+        if batch_size < size:
+            raise ShardError(f"batch of {batch_size} rows cannot be split over {size} ranks")
+        self.num_qubits = num_qubits
+        self.batch_size = batch_size
+        counts = [batch_size // size + (1 if r < batch_size % size else 0) for r in range(size)]
+        self.row_begin = sum(counts[:self.comm.rank])
+        self.rows = counts[self.comm.rank]
+        self.state = None
+        self._ctx = None
+
+    def load(self, full_rows) -> None:
+        """Takes this rank's rows of a [batch, 2^n] initial state."""
+        a = np.ascontiguousarray(full_rows, dtype=np.complex128).reshape(self.batch_size, -1)
+        if a.shape[1] != (1 << self.num_qubits):
+            raise ShardError(f"batch state must have shape [{self.batch_size}, {1 << self.num_qubits}]")
+        self.state = self.backend.from_numpy(a[self.row_begin:self.row_begin + self.rows])
+
+    def _gather_rows(self, local: np.ndarray) -> np.ndarray:
+        full = np.zeros(self.batch_size, dtype=np.float64)
+        full[self.row_begin:self.row_begin + self.rows] = local
+        return self.comm.allreduce_sum(full)
+
+    def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True) -> np.ndarray:
+        """Values of all B rows; keeps psi and H psi of this rank's rows for ``backward``."""
+        if circuit.num_qubits != self.num_qubits or observable.num_qubits != self.num_qubits:
+            raise ShardError("circuit, observable and state qubit counts differ")
+        if self.state is None:
+            raise ShardError("load the batch state first")
+        records = grad and any(p.requires_grad for p in circuit.parameters)
+        ops = circuit.compile_plan(1 if records else 0)
+        n = self.num_qubits
+        psi = self.state.clone()
+        self.backend.apply(ops, psi, n)
+        coef, flip, phase = (np.asarray(x) for x in observable.masks())
+        lam = None
+        if records:
+            lam = self.backend.zeros(psi.numel()).reshape(psi.shape)
+        vals = self.backend.observable_rows(coef, flip, phase, psi, lam, n)
+        self._ctx = (ops, circuit, psi, lam) if records else None
+        return self._gather_rows(np.asarray(vals, dtype=np.float64))
+
+    def backward(self, upstream) -> np.ndarray:
+        """Per-row upstream factors (length B, or a scalar); returns the parameter gradients
+        summed over all rows of all ranks."""
+        if self._ctx is None:
+            raise ShardError("run was executed without gradient recording")
+        ops, circuit, psi, lam = self._ctx
+        up = np.broadcast_to(np.asarray(upstream, dtype=np.float64), (self.batch_size,))
+        mine = np.ascontiguousarray(up[self.row_begin:self.row_begin + self.rows])
+        req = circuit.requires_grad_mask(True, False)
+        grads = np.zeros(len(req), dtype=np.float64)
+        self.backend.adjoint(ops, psi, lam, self.num_qubits, mine, req, grads)
+        grads = self.comm.allreduce_sum(grads)
         self._ctx = None
         pgrads = grads[1:].copy()
         for p, g in zip(circuit.parameters, pgrads):

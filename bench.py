@@ -37,6 +37,11 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+# DRAM bytes per amplitude of one fused pass from ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) on 26-qubit passes of this workload: forward 1.074 + 1.015 GB, adjoint
+# 2.148 + 2.090 GB per 2^26 amplitudes; a pass's traffic grows with the state it streams.
+NCU_DRAM_BYTES_PER_AMP = {"fused_forward": 2.089e9 / 2 ** 26, "fused_adjoint": 4.238e9 / 2 ** 26}
+
 METRIC = "gate passes/s (32q 20-layer brickwork forward + adjoint gradient, 200-term <H>)"
 UNIT = "gate_passes/s"
 
@@ -170,7 +175,8 @@ def gpu_arm(args):
     torch.cuda.set_device(local)
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
     build.build()
     rt.load()
     n = args.qubits
@@ -217,6 +223,10 @@ def gpu_arm(args):
     barrier()
     clk = clocks.stop()
     launches = rt.launch_count() - launches0
+    if world > 1:
+        t = torch.tensor([launches], device="cuda", dtype=torch.int64)
+        torch.distributed.all_reduce(t)
+        launches = int(t.item())
     prof = rt.profile_read()
     rt.profile_enable(False)
     ms = e0.elapsed_time(e1)
@@ -245,13 +255,22 @@ def gpu_arm(args):
     pk = peaks()
     hbm = pk.get("hbm_gbs")
     achieved = (dbytes / dl) / (dms / dl * 1e-3) / 1e9 if dl else 0.0
+    peak = hbm if hbm else 6650.0
+    local_amps = 2.0 ** (n - (world.bit_length() - 1))
+    traffic = NCU_DRAM_BYTES_PER_AMP.get(dname)
     roofline = {"kernel": f"k_fused ({dname})" if dname.startswith("fused") else dname,
                 "bound": "hbm", "achieved": round(achieved, 1),
-                "peak": hbm if hbm else 6650.0, "unit": "GB/s",
+                "peak": peak, "unit": "GB/s",
                 "peak_source": "measured" if hbm else "fallback",
-                "frac": round(achieved / (hbm if hbm else 6650.0), 4),
+                "frac": round(achieved / peak, 4),
                 "bytes_per_launch": dbytes / dl if dl else 0, "avg_launch_ms": dms / dl if dl else 0,
-                "traffic": None}
+                "traffic": traffic * local_amps if traffic else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                  "26-qubit pass of this kernel, scaled per amplitude"
+                                  if traffic else None}
+    # The rate per-gate kernels would reach at the HBM roofline: every gate one pass over the
+    # state (32 B per amplitude forward, 64 B adjoint), all GPUs streaming their shards.
+    unfused = 2 * gates * world * peak * 1e9 / (gates * 96.0 * 2.0 ** n)
 
     e2e = None
     if not args.no_e2e:
@@ -266,6 +285,8 @@ def gpu_arm(args):
                             "gbs": round(v[2] / (v[1] * 1e-3) / 1e9, 1) if v[1] else 0}
                         for k, v in prof.items() if v[0]},
             "gpu_launches": launches, "e2e": e2e, "clocks": clk,
+            "unfused_hbm_roofline_value": round(unfused, 3),
+            "vs_unfused_hbm_roofline": round(value_rate / unfused, 3),
             "adjoint_grads_per_s": round(args.steps / (ms / 1e3), 5),
             "param_grads_per_s": round(c.num_parameters() * args.steps / (ms / 1e3), 2),
             "check": {"value": value, "grad_norm": float(np.linalg.norm(grads))}}

@@ -64,23 +64,37 @@ class OracleShardBackend:
 
     def apply(self, ops, shard, n_local):
         if ops:
-            shard.copy_(self.torch.from_numpy(self.O.plan_apply(ops, shard.numpy(), n_local)))
+            rows = shard.numel() >> n_local
+            out = self.O.plan_apply(ops, shard.numpy().reshape(-1), n_local, rows)
+            shard.copy_(self.torch.from_numpy(out).reshape(shard.shape))
 
     def adjoint(self, ops, psi, lam, n_local, upstream, req, grads):
-        p, l, g = self.O.adjoint_backward(ops, psi.numpy(), lam.numpy(), n_local, upstream, req,
-                                          len(grads))
-        psi.copy_(self.torch.from_numpy(p))
-        lam.copy_(self.torch.from_numpy(l))
+        rows = psi.numel() >> n_local
+        up = np.broadcast_to(np.asarray(upstream, dtype=np.float64), (rows,))
+        up = float(up[0]) if rows == 1 else np.ascontiguousarray(up)
+        p, l, g = self.O.adjoint_backward(ops, psi.numpy().reshape(-1), lam.numpy().reshape(-1),
+                                          n_local, up, req, len(grads), rows)
+        psi.copy_(self.torch.from_numpy(p).reshape(psi.shape))
+        lam.copy_(self.torch.from_numpy(l).reshape(lam.shape))
         grads += g
 
-    def observable(self, coef, flip, phase, psi, out, n_local):
+    def observable_rows(self, coef, flip, phase, psi, out, n_local):
         terms = [(float(c), int(f), int(p), bin(int(f) & int(p)).count("1") % 4)
                  for c, f, p in zip(coef, flip, phase)]
-        if out is None:
-            return float(self.O.expectation(terms, psi.numpy(), n_local))
-        v, h = self.O.expectation_and_apply(terms, psi.numpy(), n_local)
-        out += self.torch.from_numpy(h)
-        return float(v)
+        rows = psi.numel() >> n_local
+        a = psi.numpy().reshape(rows, -1)
+        vals = np.zeros(rows)
+        for b in range(rows):
+            if out is None:
+                vals[b] = self.O.expectation(terms, a[b], n_local)
+            else:
+                v, h = self.O.expectation_and_apply(terms, a[b], n_local)
+                out.view(rows, -1)[b] += self.torch.from_numpy(h)
+                vals[b] = v
+        return vals
+
+    def observable(self, coef, flip, phase, psi, out, n_local):
+        return float(self.observable_rows(coef, flip, phase, psi, out, n_local)[0])
 
     def slices(self, shard, n_local, positions, chunk_begin, chunk_len, skip, staging, unpack):
         slices_numpy(shard.numpy(), positions, chunk_begin, chunk_len, skip, staging.numpy(),
@@ -216,6 +230,39 @@ def gloo_worker(rank, size, port, case, queue):
         res = sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
                            case["req"])
         queue.put((rank, res))
+    except BaseException as e:  # noqa: BLE001 - reported to the parent
+        queue.put((rank, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def gloo_batch_worker(rank, size, port, case, queue):
+    """One rank of a gloo world running the row-sharded batch simulator on the oracle."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "oracle"), here):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import torch.distributed as dist
+
+    import oracle as O
+    from arcqml_b200.sharded import DistComm, ShardedBatchSimulator
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=size, timeout=datetime.timedelta(seconds=120))
+        from arcqml_b200.workloads import qnn
+        circuit, obs, init, labels = qnn(case["n"], case["batch"], case["layers"], case["seed"])
+        sim = ShardedBatchSimulator(circuit.num_qubits, init.shape[0], comm=DistComm(),
+                                    backend=OracleShardBackend(O))
+        sim.load(init)
+        vals = sim.run(circuit, obs)
+        up = (vals - labels) / len(labels)
+        grads = sim.backward(up)
+        queue.put((rank, dict(values=vals, grads=grads)))
     except BaseException as e:  # noqa: BLE001 - reported to the parent
         queue.put((rank, repr(e)))
     finally:

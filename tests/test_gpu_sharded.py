@@ -103,3 +103,31 @@ def test_nccl_ranks_match_oracle():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=os.path.dirname(HERE))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "sharded-nccl-ok" in r.stdout
+
+
+def test_emulated_ranks_row_sharded_qnn_match_oracle(runtime, oracle):
+    """The batched QNN (10 qubits) with its rows split over 4 emulated ranks on one GPU."""
+    from arcqml_b200.sharded import RuntimeBackend, ShardedBatchSimulator
+    from arcqml_b200.workloads import half_mse_upstream, qnn
+    n, b = 10, 64
+    c, obs, init, labels = qnn(n, b, 4, seed=7)
+
+    def body(rank, comm):
+        sim = ShardedBatchSimulator(n, b, comm=comm, backend=RuntimeBackend())
+        sim.load(init)
+        vals = sim.run(c, obs)
+        _, up = half_mse_upstream(vals, labels)
+        return vals, sim.backward(up)
+
+    res = run_threads(4, body)
+    ops = c.compile_plan(1)
+    psi = oracle.plan_apply(ops, init.reshape(-1), n, b).reshape(b, -1)
+    terms = obs.compiled_terms()
+    vals = np.array([oracle.expectation(terms, psi[i], n) for i in range(b)])
+    lam = np.stack([oracle.expectation_and_apply(terms, psi[i], n)[1] for i in range(b)])
+    _, up = half_mse_upstream(vals, labels)
+    req = c.requires_grad_mask(True, False)
+    _, _, g = oracle.adjoint_backward(ops, psi.reshape(-1), lam.reshape(-1), n, up, req, len(req), b)
+    for v, gr in res:
+        np.testing.assert_allclose(v, vals, rtol=0, atol=1e-10)
+        np.testing.assert_allclose(gr, g[1:], rtol=0, atol=1e-10 * max(1.0, np.abs(g).max()))

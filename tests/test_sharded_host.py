@@ -203,3 +203,44 @@ def test_gloo_world_brickwork_matches_oracle(oracle):
                 req=c.requires_grad_mask(True, False))
     res = run_world(size, case)
     check_world(res, expected(oracle, case), size)
+
+
+def test_gloo_world_row_sharded_batch_matches_oracle(oracle):
+    """Batch rows split over 4 ranks: values of all rows and gradients summed over all rows
+    equal the oracle's batch path (crates/arcqml-sim/src/statevector/execution/adjoint/
+    row_major.rs:108-162 semantics: per-row upstream, row gradients summed)."""
+    from arcqml_b200.workloads import half_mse_upstream, qnn
+    from shard_support import gloo_batch_worker
+    case = dict(n=6, batch=14, layers=2, seed=3)
+    size = 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=gloo_batch_worker, args=(r, size, port, case, q))
+          for r in range(size)]
+    for p in ps:
+        p.start()
+    out = {}
+    try:
+        for _ in range(size):
+            r, res = q.get(timeout=300)
+            out[r] = res
+    finally:
+        for p in ps:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    c, obs, init, labels = qnn(case["n"], case["batch"], case["layers"], case["seed"])
+    n, b = case["n"], case["batch"]
+    ops = c.compile_plan(1)
+    psi = oracle.plan_apply(ops, init.reshape(-1), n, b).reshape(b, -1)
+    terms = obs.compiled_terms()
+    vals = np.array([oracle.expectation(terms, psi[i], n) for i in range(b)])
+    lam = np.stack([oracle.expectation_and_apply(terms, psi[i], n)[1] for i in range(b)])
+    _, up = half_mse_upstream(vals, labels)
+    req = c.requires_grad_mask(True, False)
+    _, _, g = oracle.adjoint_backward(ops, psi.reshape(-1), lam.reshape(-1), n, up, req, len(req), b)
+    for r in range(size):
+        assert not isinstance(out[r], str), out[r]
+        close(out[r]["values"], vals)
+        close(out[r]["grads"], g[1:])
