@@ -505,6 +505,35 @@ int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubi
     });
 }
 
+int32_t arcqml_rt_v2_sample(const arcqml_c128 *amplitudes, size_t num_qubits, uint64_t shots,
+                            uint64_t seed, uint64_t *indices, double *norm_sqr, void *stream) {
+    return guarded([&] {
+        if (shots == 0) fail("invalid shot count: shots must be greater than zero");
+        check_device_state(amplitudes, 1, num_qubits);
+        if (!indices) fail("index buffer is null");
+        const size_t dim = state_dimension(num_qubits);
+        ThreadContext &ctx = thread_context();
+        cudaStream_t s = pick_stream(ctx, stream);
+        // the v2 entry points never use the state slots 1 and 2 of the thread's buffers
+        auto *cum = static_cast<double *>(ctx_buffer(ctx, 1, dim * sizeof(double)));
+        auto *out = static_cast<uint64_t *>(ctx_buffer(ctx, 2, shots * sizeof(uint64_t)));
+        launch_sample(reinterpret_cast<const double2 *>(amplitudes), uint32_t(num_qubits), shots,
+                      seed, cum, out, s);
+        double total = 0.0;
+        check_cuda(cudaMemcpyAsync(&total, cum + dim - 1, sizeof(double), cudaMemcpyDeviceToHost, s),
+                   "cudaMemcpyAsync (norm)");
+        check_cuda(cudaMemcpyAsync(indices, out, shots * sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
+                   "cudaMemcpyAsync (indices)");
+        check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        if (norm_sqr) *norm_sqr = total;
+        if (!(std::fabs(total - 1.0) <= 1e-10)) {
+            std::ostringstream m;
+            m << "tensor state is not normalized: expected norm squared close to 1, got " << total;
+            fail(m.str());
+        }
+    });
+}
+
 int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
                                       arcqml_c128 *adjoint_state, size_t batch,
                                       size_t num_qubits, const double *upstream,

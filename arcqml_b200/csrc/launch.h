@@ -30,6 +30,11 @@ void launch_slices(double2 *amps, uint32_t n_local, const uint32_t *positions, u
                    bool unpack, cudaStream_t s);
 constexpr uint32_t kMaxSliceBits = 8;
 
+// cum[i] = sequential f64 sum of |amps[j]|^2 for j <= i (no FMA); out[s] = basis index of
+// shot s of StdRng::seed_from_u64(seed). cum holds 2^n doubles, out `shots` entries.
+void launch_sample(const double2 *amps, uint32_t n, uint64_t shots, uint64_t seed, double *cum,
+                   uint64_t *out, cudaStream_t s);
+
 Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,
                             const uint64_t *phase, size_t num_terms);
 const std::string &last_error();

@@ -121,6 +121,7 @@ def load():
         "arcqml_rt_v2_expectation": (I32, [P, P, S, S, P, P]),
         "arcqml_rt_v2_expectation_and_apply": (I32, [P, P, P, S, S, P, P]),
         "arcqml_rt_v2_expectation_and_accumulate": (I32, [P, P, P, S, S, P, P]),
+        "arcqml_rt_v2_sample": (I32, [P, S, C.c_uint64, C.c_uint64, P, P, P]),
         "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
                                             I32, P]),
         "arcqml_rt_v2_adjoint_backward": (I32, [P, P, P, S, S, P, P, S, P, S, P]),
@@ -487,6 +488,17 @@ def set_basis_state_device(state, num_qubits: int, index: int = 0, stream=None) 
 
 PROFILE_CATEGORIES = ("gate", "fused_forward", "fused_adjoint", "adjoint_step", "observable",
                       "other", "shard_slices")
+
+
+def sample_indices_device(state, num_qubits: int, shots: int, seed: int, stream=None):
+    """Basis index of every shot (numpy uint64) and the state's norm squared; see
+    arcqml_rt_v2_sample (bit-exact with the reference's sample_counts)."""
+    out = np.zeros(max(int(shots), 1), dtype=np.uint64)
+    norm = C.c_double()
+    _status(load().arcqml_rt_v2_sample(_dev_ptr(state), num_qubits, int(shots),
+                                       int(seed) & ((1 << 64) - 1), out.ctypes.data,
+                                       C.byref(norm), _stream_ptr(stream)))
+    return out[:int(shots)], float(norm.value)
 
 
 def shard_slices(shard, num_local_qubits: int, positions: Sequence[int], chunk_begin: int,

@@ -15,6 +15,7 @@ keep the context for a second backward.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -151,6 +152,23 @@ class StateVectorSimulator:
 
     def norm(self) -> float:
         return float(rt.norms_device(self.state, self.num_qubits)[0])
+
+    def sample_counts(self, shots: int, seed: Optional[int] = None) -> dict:
+        """Counts of ``shots`` full-register measurements of the current state, keyed by the
+        bitstring q[n-1]..q0 and sorted by it; the state is not collapsed. The same seed gives
+        the reference's counts bit for bit (StdRng::seed_from_u64, sequential running sum;
+        ``crates/arcqml-sim/src/statevector/api/measurement.rs:18-60``); ``None`` draws a seed."""
+        if shots <= 0:
+            raise SimError("invalid shot count: shots must be greater than zero")
+        if seed is None:
+            seed = int.from_bytes(os.urandom(8), "little")
+        try:
+            idx, _ = rt.sample_indices_device(self.state, self.num_qubits, shots, seed)
+        except rt.RuntimeError as e:
+            raise SimError(str(e)) from None
+        vals, cnt = np.unique(idx, return_counts=True)
+        n = self.num_qubits
+        return dict(sorted((format(int(v), f"0{n}b"), int(c)) for v, c in zip(vals, cnt)))
 
     def run(self, circuit: Circuit, observable: SparsePauliOp, grad: bool = True,
             initial_state=None) -> RunResult:

@@ -101,6 +101,17 @@ int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubi
                                   uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip_value,
                                   arcqml_c128 *staging, int32_t unpack, void *stream);
 
+/* Shot sampling from one device state, bit-exact with the reference's sample_counts
+ * (crates/arcqml-sim/src/statevector/api/measurement.rs:18-60): p_i = re^2 + im^2 (no fused
+ * multiply-add), a sequential f64 running sum, and per shot target = u * total with u the next
+ * f64 of StdRng::seed_from_u64(seed) (ChaCha12); indices[s] (host array of `shots` entries)
+ * receives the first basis index whose running sum exceeds target (the last index if none).
+ * norm_sqr (optional) receives the total. Fails, as the reference does, for shots == 0 and
+ * when |total - 1| > 1e-10 (state.rs:108-114). Uses 8 * 2^n bytes of device scratch; the running
+ * sum is one dependency chain (about 2-4 ns per amplitude). */
+int32_t arcqml_rt_v2_sample(const arcqml_c128 *amplitudes, size_t num_qubits, uint64_t shots,
+                            uint64_t seed, uint64_t *indices, double *norm_sqr, void *stream);
+
 /* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);

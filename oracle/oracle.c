@@ -599,3 +599,111 @@ double oracle_expectation_and_apply(const oracle_term *terms, size_t num_terms,
     oracle_apply_hamiltonian(terms, num_terms, amps, out, n);
     return re_inner(amps, out, (size_t)1 << n);
 }
+
+/* ---------------------------------------------------------------- sampling
+ *
+ * sample_counts, crates/arcqml-sim/src/statevector/api/measurement.rs:18-60: p_i = re^2 + im^2
+ * (two products and a sum, no fused multiply-add), a sequential f64 running sum, and per shot
+ * target = u * total with u the next f64 of StdRng::seed_from_u64(seed); the shot lands on the
+ * first index whose running sum exceeds target (the last index if none does).
+ *
+ * The generator comes from crates the reference pins but does not ship (rand 0.10.2,
+ * rand_core 0.10.1, chacha20 0.10.2, Cargo.lock:482-497, :201-204); this restates their
+ * published algorithms:
+ *   seed_from_u64  the 32-byte seed is eight outputs of PCG32 (XSH-RR) on a 64-bit state
+ *                  advanced as s = s * 6364136223846793005 + 11634580027462260723 before each
+ *                  output, each output stored little-endian;
+ *   StdRng         ChaCha with 12 rounds (6 double rounds): words 0-3 the "expand 32-byte k"
+ *                  constants, 4-11 the seed as little-endian words, 12-13 a 64-bit block
+ *                  counter from 0, 14-15 a zero stream id; the keystream is the blocks' output
+ *                  words in order;
+ *   next_u64       two consecutive keystream words, the first as the low half;
+ *   f64            (next_u64 >> 11) * 2^-53.
+ */
+
+static inline uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+#define QR(a, b, c, d)                 \
+    do {                               \
+        a += b; d ^= a; d = rotl32(d, 16); \
+        c += d; b ^= c; b = rotl32(b, 12); \
+        a += b; d ^= a; d = rotl32(d, 8);  \
+        c += d; b ^= c; b = rotl32(b, 7);  \
+    } while (0)
+
+void oracle_chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, int rounds,
+                         uint32_t out[16]) {
+    uint32_t s[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u};
+    for (int i = 0; i < 8; ++i) s[4 + i] = key[i];
+    s[12] = (uint32_t)counter;
+    s[13] = (uint32_t)(counter >> 32);
+    s[14] = (uint32_t)stream;
+    s[15] = (uint32_t)(stream >> 32);
+    uint32_t x[16];
+    memcpy(x, s, sizeof x);
+    for (int r = 0; r < rounds; r += 2) {
+        QR(x[0], x[4], x[8], x[12]);
+        QR(x[1], x[5], x[9], x[13]);
+        QR(x[2], x[6], x[10], x[14]);
+        QR(x[3], x[7], x[11], x[15]);
+        QR(x[0], x[5], x[10], x[15]);
+        QR(x[1], x[6], x[11], x[12]);
+        QR(x[2], x[7], x[8], x[13]);
+        QR(x[3], x[4], x[9], x[14]);
+    }
+    for (int i = 0; i < 16; ++i) out[i] = x[i] + s[i];
+}
+
+void oracle_stdrng_key(uint64_t seed, uint32_t key[8]) {
+    uint64_t st = seed;
+    for (int i = 0; i < 8; ++i) {
+        st = st * 6364136223846793005ull + 11634580027462260723ull;
+        const uint32_t xorshifted = (uint32_t)(((st >> 18) ^ st) >> 27);
+        const uint32_t rot = (uint32_t)(st >> 59);
+        key[i] = (xorshifted >> rot) | (xorshifted << ((32 - rot) & 31));
+    }
+}
+
+/* The k-th u64 of StdRng::seed_from_u64(seed) (k = 0 first). */
+uint64_t oracle_stdrng_u64(uint64_t seed, uint64_t k) {
+    uint32_t key[8], blk[16];
+    oracle_stdrng_key(seed, key);
+    oracle_chacha_block(key, k / 8, 0, 12, blk);
+    const int w = (int)(k % 8) * 2;
+    return (uint64_t)blk[w] | ((uint64_t)blk[w + 1] << 32);
+}
+
+int oracle_sample_indices(const oc128 *amps, uint32_t num_qubits, uint64_t shots, uint64_t seed,
+                          uint64_t *out) {
+    if (num_qubits >= 63 || shots == 0) return 1;
+    const size_t dim = (size_t)1 << num_qubits;
+    double *cum = (double *)malloc(dim * sizeof(double));
+    if (!cum) return 2;
+    double run = 0.0;
+    for (size_t i = 0; i < dim; ++i) {
+        const double re2 = amps[i].re * amps[i].re;
+        const double im2 = amps[i].im * amps[i].im;
+        run += re2 + im2;
+        cum[i] = run;
+    }
+    const double total = run;
+    uint32_t key[8], blk[16];
+    oracle_stdrng_key(seed, key);
+    for (uint64_t s = 0; s < shots; ++s) {
+        if (s % 8 == 0) oracle_chacha_block(key, s / 8, 0, 12, blk);
+        const int w = (int)(s % 8) * 2;
+        const uint64_t x = (uint64_t)blk[w] | ((uint64_t)blk[w + 1] << 32);
+        const double target = (double)(x >> 11) * (1.0 / 9007199254740992.0) * total;
+        /* first i with target < cum[i]: the running sum never decreases, so the linear scan
+         * of the reference and this bisection land on the same index */
+        size_t lo = 0, hi = dim;
+        while (lo < hi) {
+            const size_t mid = lo + (hi - lo) / 2;
+            if (target < cum[mid]) hi = mid;
+            else lo = mid + 1;
+        }
+        out[s] = lo < dim ? lo : dim - 1;
+    }
+    free(cum);
+    return 0;
+}

@@ -86,6 +86,14 @@ int oracle_batch_adjoint_backward(const oracle_op *ops, size_t num_ops, oc128 *p
                                   double *grads, size_t grads_len);
 
 /* Threads used by the OpenMP loops (1 when built without OpenMP). */
+/* Sampling (crates/arcqml-sim/src/statevector/api/measurement.rs:18-60): shot s's basis index
+ * in out[s]. The ChaCha block and the StdRng key/stream helpers are exported for tests. */
+int oracle_sample_indices(const oc128 *amps, uint32_t num_qubits, uint64_t shots, uint64_t seed,
+                          uint64_t *out);
+void oracle_chacha_block(const uint32_t key[8], uint64_t counter, uint64_t stream, int rounds,
+                         uint32_t out[16]);
+void oracle_stdrng_key(uint64_t seed, uint32_t key[8]);
+uint64_t oracle_stdrng_u64(uint64_t seed, uint64_t k);
 int oracle_num_threads(void);
 void oracle_set_num_threads(int n);
 

@@ -78,6 +78,11 @@ def lib():
         L.oracle_apply_hamiltonian.argtypes = [P, C.c_size_t, P, P, C.c_uint32]
         L.oracle_gate_matrix.argtypes = [C.c_uint32, C.c_uint32, P, P, P]
         L.oracle_derivative_matrix.argtypes = [C.c_uint32, C.c_uint32, P, C.c_size_t, P]
+        L.oracle_sample_indices.argtypes = [P, C.c_uint32, C.c_uint64, C.c_uint64, P]
+        L.oracle_chacha_block.argtypes = [P, C.c_uint64, C.c_uint64, C.c_int, P]
+        L.oracle_stdrng_key.argtypes = [C.c_uint64, P]
+        L.oracle_stdrng_u64.argtypes = [C.c_uint64, C.c_uint64]
+        L.oracle_stdrng_u64.restype = C.c_uint64
         L.oracle_num_threads.restype = C.c_int
         L.oracle_set_num_threads.argtypes = [C.c_int]
         _lib = L
@@ -236,6 +241,42 @@ def apply_hamiltonian(terms, amps, num_qubits):
     out = np.empty_like(a)
     lib().oracle_apply_hamiltonian(C.addressof(arr), nt, a.ctypes.data, out.ctypes.data, num_qubits)
     return out
+
+
+def sample_indices(amps, num_qubits, shots, seed):
+    """Basis index of every shot of sample_counts(shots, seed)
+    (crates/arcqml-sim/src/statevector/api/measurement.rs:18-60)."""
+    a = _state(amps)
+    out = np.zeros(int(shots), dtype=np.uint64)
+    if lib().oracle_sample_indices(a.ctypes.data, num_qubits, int(shots), int(seed),
+                                   out.ctypes.data) != 0:
+        raise ValueError("oracle: invalid sampling call")
+    return out
+
+
+def sample_counts(amps, num_qubits, shots, seed):
+    """{bitstring q[n-1]..q0: count} sorted by bitstring, as the reference's BTreeMap."""
+    idx = sample_indices(amps, num_qubits, shots, seed)
+    vals, cnt = np.unique(idx, return_counts=True)
+    d = {format(int(v), f"0{num_qubits}b"): int(c) for v, c in zip(vals, cnt)}
+    return dict(sorted(d.items()))
+
+
+def chacha_block(key, counter, stream=0, rounds=20):
+    k = (C.c_uint32 * 8)(*key)
+    out = (C.c_uint32 * 16)()
+    lib().oracle_chacha_block(k, counter, stream, rounds, out)
+    return list(out)
+
+
+def stdrng_key(seed):
+    k = (C.c_uint32 * 8)()
+    lib().oracle_stdrng_key(seed, k)
+    return list(k)
+
+
+def stdrng_u64(seed, k):
+    return int(lib().oracle_stdrng_u64(seed, k))
 
 
 def adam_step(values, grads, state, lr=0.05, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0):
