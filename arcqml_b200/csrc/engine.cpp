@@ -346,6 +346,41 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
 
 // ------------------------------------------------------------------ observables
 
+void pauli_traversal_tables(uint32_t n, const std::vector<uint64_t> &flips,
+                            std::vector<uint64_t> &tables, PauliTraversal &tr) {
+    constexpr uint32_t kCoset = 21;  // 2^21 amplitudes = 32 MB of psi per coset
+    tables.clear();
+    tr = PauliTraversal{};
+    if (n <= kCoset) return;
+    // qubits 0-5 always (coalesced 1 KB runs); then the qubits the most flip groups act on
+    std::vector<std::pair<uint32_t, uint32_t>> cnt;  // (-count, qubit) sorts by count desc
+    for (uint32_t q = 6; q < n; ++q) {
+        uint32_t c = 0;
+        for (uint64_t f : flips) c += uint32_t((f >> q) & 1u);
+        cnt.push_back({~c, q});
+    }
+    std::sort(cnt.begin(), cnt.end());
+    std::vector<uint32_t> in, out;
+    for (size_t i = 0; i < cnt.size(); ++i)
+        (i < kCoset - 6 ? in : out).push_back(cnt[i].second);
+    std::sort(in.begin(), in.end());
+    std::sort(out.begin(), out.end());
+    auto add = [&](const std::vector<uint32_t> &pos) {
+        uint32_t made = 0;
+        for (size_t j = 0; j < pos.size(); j += 8, ++made)
+            for (uint32_t v = 0; v < 256; ++v) {
+                uint64_t e = 0;
+                for (uint32_t i = 0; i < 8; ++i)
+                    if (j + i < pos.size() && ((v >> i) & 1u)) e |= uint64_t(1) << pos[j + i];
+                tables.push_back(e);
+            }
+        return made;
+    };
+    tr.nb = add(in);
+    tr.ntables = tr.nb + add(out);
+    tr.coset_bits = kCoset;
+}
+
 void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
                        uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
                        bool accumulate) {
@@ -358,9 +393,14 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
     const size_t ng = obs.groups.size();
     // Pack tables: w (double2 per term), z (u64 per term), flip (u64 per group),
     // first/count (u32 per group), all in one upload.
+    std::vector<uint64_t> gflips(ng), ptab;
+    for (size_t g = 0; g < ng; ++g) gflips[g] = obs.groups[g].flip;
+    PauliTraversal tr;
+    pauli_traversal_tables(n, gflips, ptab, tr);
     const size_t wz_bytes = nt * 16 + nt * 8;
     const size_t g_bytes = ng * 8 + ng * 8;
-    std::vector<double2> pack((wz_bytes + g_bytes + 15) / 16 + 1);
+    const size_t t_off = (wz_bytes + g_bytes + 15) & ~size_t(15);
+    std::vector<double2> pack((t_off + ptab.size() * 8 + 15) / 16 + 1);
     char *base = reinterpret_cast<char *>(pack.data());
     double2 *w = reinterpret_cast<double2 *>(base);
     uint64_t *z = reinterpret_cast<uint64_t *>(base + nt * 16);
@@ -382,9 +422,11 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         first[g] = obs.groups[g].first;
         count[g] = obs.groups[g].count;
     }
+    if (!ptab.empty()) std::memcpy(base + t_off, ptab.data(), ptab.size() * 8);
     std::vector<const std::vector<double2> *> refs{&pack};
     auto p = upload_tables(refs, ctx, s);
     const char *dbase = reinterpret_cast<const char *>(p[0]);
+    if (!ptab.empty()) tr.tables = reinterpret_cast<const uint64_t *>(dbase + t_off);
     const double2 *dw = reinterpret_cast<const double2 *>(dbase);
     const uint64_t *dz = reinterpret_cast<const uint64_t *>(dbase + nt * 16);
     const uint64_t *dflip = reinterpret_cast<const uint64_t *>(dbase + nt * 24);
@@ -398,8 +440,8 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         const unsigned bx_cap = adjoint_max_blocks();
         double *partials = ctx_partials(ctx, rows * size_t(bx_cap));
         const unsigned bx = launch_pauli(psi + b0 * dim, out ? out + b0 * dim : nullptr, rows, n,
-                                         dw, dz, dflip, dfirst, dcount, uint32_t(ng), partials,
-                                         accumulate, s);
+                                         dw, dz, dflip, dfirst, dcount, uint32_t(ng), tr,
+                                         partials, accumulate, s);
         double *sums = ctx_dgrads(ctx, rows);
         launch_reduce_rows(partials, uint32_t(rows), bx, sums, s);
         double *h = ctx_hvals(ctx, rows);

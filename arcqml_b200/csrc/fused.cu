@@ -14,6 +14,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "fused.h"
@@ -403,10 +404,10 @@ __device__ __forceinline__ int dmat_len(uint8_t kind) {
     }
 }
 
-// Adds the warp's sum of z into its own column of accumulator row `row` (= acc * nwarps).
+// Adds z into this thread's own column of accumulator row `row` (= acc * blockDim.x): no
+// cross-lane traffic per gate; the columns are summed once per pass at the end of the kernel.
 __device__ __forceinline__ void accumulate(double *sacc, uint32_t row, double z) {
-    z = warp_sum(z);
-    if ((threadIdx.x & 31) == 0) sacc[row + (threadIdx.x >> 5)] += z;
+    sacc[row + threadIdx.x] += z;
 }
 
 // ---------------------------------------------------------------- specialised fast paths
@@ -836,7 +837,7 @@ template <int RB, bool ADJ>
 __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, double2 *tp,
                                               double2 *tl, const FOp *ops, const double2 *mats,
                                               const SubBlock *subs, double *sacc,
-                                              uint32_t nwarps, uint32_t tb, uint64_t gbase) {
+                                              uint32_t nthreads, uint32_t tb, uint64_t gbase) {
     constexpr int N = 1 << RB;
     uint32_t rm[RB];
 #pragma unroll
@@ -856,7 +857,7 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
             // one dispatch: Pauli gradient (if any), then U^dagger on psi and lambda
             double z = 0.0;
             if (adj_fast<RB>(o, mt, v, w, tb, gbase, z)) {
-                if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nthreads, 0.5 * z);
                 continue;
             }
             if (o.gkind != GK_NONE && o.gkind != GK_GENERIC) {
@@ -869,7 +870,7 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
                     }
                     z = slow_grad<RB>(ops + oi, nullptr, tv, tw, tb, subs + sb, gbase);
                 }
-                accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                accumulate(sacc, o.acc[0] * nthreads, 0.5 * z);
             }
         }
         const bool fast = apply_fast<RB>(o, mt, v, tb, gbase);
@@ -892,7 +893,7 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
                     tw[e] = w[e];
                 }
                 for (int s = 0; s < int(o.nslots); ++s)
-                    accumulate(sacc, o.acc[s] * nwarps,
+                    accumulate(sacc, o.acc[s] * nthreads,
                                slow_grad<RB>(ops + oi, d + s * dl, tv, tw, tb, subs + sb, gbase));
             }
             if (fast) {
@@ -917,22 +918,25 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
 
 // ---------------------------------------------------------------- the pass kernel
 
-// Shared memory: [tile buffers: 2 x (psi [, lambda])][hioff][accumulators][ops][matrices].
-// While a CTA computes tile i from one buffer, cp.async streams tile i + gridDim into the other.
+// Shared memory: [tile buffers][hioff][accumulators][ops][matrices].
+// Forward: two psi buffers; while a CTA computes tile i from one, cp.async streams tile
+// i + gridDim into the other. Adjoint: one psi and one lambda buffer (the next tile is
+// prefetched into L2 instead) and one accumulator column per thread.
 struct SmemLayout {
     uint32_t tile, hioff, sacc, ops, mats, total;
 };
 
 __host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t nacc,
-                                                  uint32_t nops, uint32_t nmat, uint32_t nwarps) {
+                                                  uint32_t nops, uint32_t nmat, uint32_t nthreads) {
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     SmemLayout m;
     m.tile = 0;
-    uint32_t off = (adj ? 4u : 2u) * (16u << k);
+    uint32_t off = 2u * (16u << k);
     m.hioff = off;
     off += 8u << (k - L);
+    off = (off + 15u) & ~15u;
     m.sacc = off;
-    off += adj ? nacc * nwarps * 8u : 0u;
+    off += adj ? nacc * nthreads * 8u : 0u;
     off = (off + 15u) & ~15u;
     m.ops = off;
     off += nops * uint32_t(sizeof(FOp));
@@ -966,15 +970,15 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
     const uint32_t D = 1u << k;
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     const uint32_t lowmask = (1u << L) - 1;
-    const uint32_t nwarps = blockDim.x >> 5;
-    const SmemLayout lay = smem_layout(ADJ, k, snacc, snops, snmat, nwarps);
+    const uint32_t nthreads = blockDim.x;
+    const SmemLayout lay = smem_layout(ADJ, k, snacc, snops, snmat, nthreads);
     double2 *bufs = reinterpret_cast<double2 *>(smem + lay.tile);
     uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + lay.hioff);
     double *sacc = reinterpret_cast<double *>(smem + lay.sacc);
     FOp *ops = reinterpret_cast<FOp *>(smem + lay.ops);
     double2 *mats = reinterpret_cast<double2 *>(smem + lay.mats);
-    // buffer b, state s (0 = psi, 1 = lambda)
-    auto tile_buf = [&](int b, int st) { return bufs + (size_t(b) * (ADJ ? 2 : 1) + st) * D; };
+    // forward: buffer b; adjoint: state st (0 = psi, 1 = lambda) of the single buffer
+    auto tile_buf = [&](int b, int st) { return bufs + size_t(ADJ ? st : b) * D; };
 
     for (uint32_t h = threadIdx.x; h < (1u << (k - L)); h += blockDim.x) {
         uint64_t off = 0;
@@ -989,7 +993,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
         for (uint32_t i = threadIdx.x; i < snmat; i += blockDim.x) mats[i] = gmats[i];
     }
     if (ADJ)
-        for (uint32_t a = threadIdx.x; a < snacc * nwarps; a += blockDim.x) sacc[a] = 0.0;
+        for (uint32_t a = threadIdx.x; a < snacc * nthreads; a += blockDim.x) sacc[a] = 0.0;
     __syncthreads();
 
     const uint64_t tmask = (uint64_t(1) << tiles_log) - 1;
@@ -1015,25 +1019,18 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
         cp_async_commit();
     };
 
-    if (uint64_t(blockIdx.x) < total_tiles) issue_load(blockIdx.x, 0);
-    else cp_async_commit();
-    int b = 0;
-    for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x, b ^= 1) {
-        const uint64_t Tn = T + gridDim.x;
-        if (Tn < total_tiles) issue_load(Tn, b ^ 1);
-        else cp_async_commit();
-        cp_async_wait<1>();
-        __syncthreads();
+    // Applies every sub-block of the pass to the tile in buffer b and writes it back.
+    auto process_tile = [&](uint64_t T, int b) {
         const uint64_t gbase = tile_base(T);
         double2 *tp = tile_buf(b, 0);
         double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
         for (uint32_t sb = 0; sb < snsub; ++sb) {
             SubBlock S;
             {
-                const uint2 *s = reinterpret_cast<const uint2 *>(subs + sb);
+                const uint2 *src = reinterpret_cast<const uint2 *>(subs + sb);
                 uint2 *d = reinterpret_cast<uint2 *>(&S);
 #pragma unroll
-                for (int i = 0; i < 3; ++i) d[i] = __ldg(s + i);
+                for (int i = 0; i < 3; ++i) d[i] = __ldg(src + i);
             }
             uint32_t tb = 0;
 #pragma unroll
@@ -1057,7 +1054,7 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                     if constexpr (ADJ) {
                         double z = 0.0;
                         adj_fast<RB>(o, mt, v, w, tb, gbase, z);
-                        if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nwarps, 0.5 * z);
+                        if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nthreads, 0.5 * z);
                     } else {
                         apply_fast<RB>(o, mt, v, tb, gbase);
                     }
@@ -1069,35 +1066,78 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
                     if (ADJ) tl[phys(x)] = w[e];
                 }
             } else {
-                general_subblock<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nwarps, tb, gbase);
+                general_subblock<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nthreads, tb,
+                                          gbase);
             }
             __syncthreads();
         }
-        {
-            const uint64_t off = ((T >> tiles_log) << n) + gbase;
-            double2 *P = psi + off;
-            double2 *Lm = ADJ ? lam + off : nullptr;
-            for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
-                const uint64_t g = (j & lowmask) | hioff[j >> L];
-                P[g] = tp[phys(j)];
-                if (ADJ) Lm[g] = tl[phys(j)];
-            }
+        const uint64_t off = ((T >> tiles_log) << n) + gbase;
+        double2 *P = psi + off;
+        double2 *Lm = ADJ ? lam + off : nullptr;
+        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
+            const uint64_t g = (j & lowmask) | hioff[j >> L];
+            P[g] = tp[phys(j)];
+            if (ADJ) Lm[g] = tl[phys(j)];
         }
-        __syncthreads();
+    };
+
+    if constexpr (ADJ) {
+        // One buffer: load tile T, ask L2 for tile T + gridDim while T is computed.
+        const uint32_t run_bytes = 16u << L;
+        const uint32_t lines = run_bytes >= 128u ? run_bytes / 128u : 1u;
+        for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x) {
+            issue_load(T, 0);
+            const uint64_t Tn = T + gridDim.x;
+            if (Tn < total_tiles) {
+                const uint64_t off = ((Tn >> tiles_log) << n) + tile_base(Tn);
+                const char *P = reinterpret_cast<const char *>(psi + off);
+                const char *Lm = reinterpret_cast<const char *>(lam + off);
+                const uint32_t count = lines << (k - L);
+                for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) {
+                    const size_t o = size_t(hioff[i / lines]) * 16u + size_t(i % lines) * 128u;
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(P + o));
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(Lm + o));
+                }
+            }
+            cp_async_wait<0>();
+            __syncthreads();
+            process_tile(T, 0);
+            __syncthreads();
+        }
+    } else {
+        if (uint64_t(blockIdx.x) < total_tiles) issue_load(blockIdx.x, 0);
+        else cp_async_commit();
+        int b = 0;
+        for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x, b ^= 1) {
+            const uint64_t Tn = T + gridDim.x;
+            if (Tn < total_tiles) issue_load(Tn, b ^ 1);
+            else cp_async_commit();
+            cp_async_wait<1>();
+            __syncthreads();
+            process_tile(T, b);
+            __syncthreads();
+        }
     }
     cp_async_wait<0>();
     if (ADJ) {
+        // column sums in a fixed order (deterministic)
         for (uint32_t a = threadIdx.x; a < snacc; a += blockDim.x) {
-            double s = 0.0;
-            for (uint32_t wi = 0; wi < nwarps; ++wi) s += sacc[a * nwarps + wi];
-            partials[size_t(sacc_base + a) * stride + blockIdx.x] = s;
+            const double *row = sacc + size_t(a) * nthreads;
+            double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+            for (uint32_t t = 0; t < nthreads; t += 4) {
+                s0 += row[t];
+                s1 += row[t + 1];
+                s2 += row[t + 2];
+                s3 += row[t + 3];
+            }
+            partials[size_t(sacc_base + a) * stride + blockIdx.x] = (s0 + s1) + (s2 + s3);
         }
     }
 }
 
 size_t fused_smem(bool adj, uint32_t k, uint32_t nacc, uint32_t nops, uint32_t nmat,
                   uint32_t threads) {
-    return smem_layout(adj, k, nacc, nops, nmat, threads / 32).total;
+    return smem_layout(adj, k, nacc, nops, nmat, threads).total;
 }
 
 using FusedKernel = void (*)(double2 *, double2 *, uint32_t, uint32_t, uint64_t,
@@ -1117,6 +1157,9 @@ struct GridKey {
 };
 std::mutex g_grid_mu;
 std::vector<std::pair<GridKey, uint32_t>> g_grid;
+// Largest dynamic shared memory allowed so far per (device, kernel): the attribute belongs to
+// the kernel function, which serves several tile sizes, so it may only grow.
+std::vector<std::tuple<int, FusedKernel, size_t>> g_smem_max;
 
 }  // namespace
 
@@ -1137,8 +1180,21 @@ uint32_t fused_grid_blocks(bool adjoint, uint32_t k, uint32_t rb) {
                                    fused_threads(k, rb));
     if (smem > 227 * 1024) fail("internal: fused pass shared memory exceeds 227 KB");
     FusedKernel kern = fused_kernel(adjoint, rb);
-    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-               "cudaFuncSetAttribute");
+    size_t allowed = 0;
+    for (const auto &e : g_smem_max)
+        if (std::get<0>(e) == dev && std::get<1>(e) == kern) allowed = std::get<2>(e);
+    if (smem > allowed) {
+        check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        int(smem)),
+                   "cudaFuncSetAttribute");
+        bool found = false;
+        for (auto &e : g_smem_max)
+            if (std::get<0>(e) == dev && std::get<1>(e) == kern) {
+                std::get<2>(e) = smem;
+                found = true;
+            }
+        if (!found) g_smem_max.emplace_back(dev, kern, smem);
+    }
     int per_sm = 0;
     check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern,
                                                              int(fused_threads(k, rb)), smem),

@@ -22,7 +22,7 @@ constexpr int kTileMax = 12;       // tile qubits
 constexpr int kLowFixed = 4;       // S always holds qubits 0..kLowFixed-1 (256-byte runs)
 constexpr int kMaxPassOps = 256;   // fused ops per pass (staged in shared memory)
 constexpr int kMaxPassMats = 1536; // matrix-table entries (double2) per pass
-constexpr int kMaxPassAcc = 256;   // gradient accumulators per pass
+constexpr int kMaxPassAcc = 56;    // gradient accumulators per pass (one smem column per thread)
 
 enum FusedKind : uint8_t {
     FK_M2 = 0,  // dense 2x2 on register bit rb0; m = [m00 m01 m10 m11]

@@ -8,6 +8,7 @@
 // Batches [batch, 2^n] are one flat group range: row = counter >> (n - npos).
 #include <cuda_runtime.h>
 
+#include "launch.h"
 #include "profile.h"
 #include "rt_internal.h"
 
@@ -319,20 +320,45 @@ struct PauliArgs {
     const uint32_t *first; // per group: first term
     const uint32_t *count; // per group: number of terms
     uint32_t ngroups;
+    // Traversal order (perm == nullptr: index order). The loop counter's low 6 bits are index
+    // bits 0-5; its next (coset_bits - 6) bits are spread over the other qubits of the coset set
+    // by tables 0..nb-1, the remaining bits over the complement by tables nb..ntables-1 (256
+    // entries each, one per 8 counter bits).
+    const uint64_t *perm;
+    uint32_t coset_bits, nb, ntables;
 };
+constexpr uint32_t kMaxPermTables = 8;
 
 // out[t] = sum_groups sum_terms w_k (-1)^popc((t^f) & z_k) psi[t^f]   (= (H psi)[t])
 // partials[row, block] = sum_t Re(conj(psi[t]) out[t]).
+//
+// Every flip group reads psi once more (psi[t ^ f]). The amplitudes are visited coset by coset
+// of a qubit set B chosen on the host (the qubits most flips act on, plus 0-5 for coalescing,
+// 2^21 amplitudes = 32 MB per coset): a group whose flips all lie in B reads inside the coset
+// being visited, which stays in L2, so HBM serves such groups once per coset instead of once per
+// group.
 __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ psi,
                                                     double2 *__restrict__ out, uint64_t dim,
                                                     const __grid_constant__ PauliArgs P,
                                                     double *__restrict__ partials, int accumulate) {
     __shared__ double s_red[kThreads / 32];
+    __shared__ uint64_t s_perm[kMaxPermTables * 256];
+    if (P.perm) {
+        for (uint32_t i = threadIdx.x; i < P.ntables * 256; i += blockDim.x) s_perm[i] = P.perm[i];
+        __syncthreads();
+    }
     const size_t roff = size_t(blockIdx.y) * dim;
     const double2 *r = psi + roff;
     double ev = 0.0;
-    for (uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < dim;
-         t += uint64_t(gridDim.x) * blockDim.x) {
+    for (uint64_t c = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; c < dim;
+         c += uint64_t(gridDim.x) * blockDim.x) {
+        uint64_t t = c;
+        if (P.perm) {
+            t = c & 63u;
+            for (uint32_t j = 0; j < P.nb; ++j) t |= s_perm[j * 256 + ((c >> (6 + 8 * j)) & 255u)];
+            for (uint32_t j = P.nb; j < P.ntables; ++j)
+                t |= s_perm[j * 256 + ((c >> (P.coset_bits + 8 * (j - P.nb))) & 255u)];
+        }
         const double2 pt = r[t];
         double2 acc = make_double2(0.0, 0.0);
         for (uint32_t gi = 0; gi < P.ngroups; ++gi) {
@@ -501,8 +527,11 @@ unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *par
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
                       const double2 *w, const uint64_t *z, const uint64_t *flip,
                       const uint32_t *first, const uint32_t *count, uint32_t ngroups,
-                      double *partials, bool accumulate, cudaStream_t s) {
-    PauliArgs P{w, z, flip, first, count, ngroups};
+                      const PauliTraversal &tr, double *partials, bool accumulate,
+                      cudaStream_t s) {
+    if (tr.tables && (tr.ntables > kMaxPermTables || tr.coset_bits < 6 || tr.coset_bits > n))
+        fail("internal: observable traversal tables out of range");
+    PauliArgs P{w, z, flip, first, count, ngroups, tr.tables, tr.coset_bits, tr.nb, tr.ntables};
     const uint64_t dim = uint64_t(1) << n;
     unsigned bx = grid_for(dim);
     const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);

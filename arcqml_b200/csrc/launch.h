@@ -18,10 +18,20 @@ void launch_reduce_rows(const double *partials, uint32_t rows, uint32_t nblocks,
 void launch_basis_state(double2 *amps, size_t batch, uint32_t n, uint64_t index, cudaStream_t s);
 unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *partials,
                       cudaStream_t s);
+// Coset traversal of the observable pass (see k_pauli); tables == nullptr: index order.
+struct PauliTraversal {
+    const uint64_t *tables = nullptr;  // device, ntables x 256 entries
+    uint32_t coset_bits = 0, nb = 0, ntables = 0;
+};
+// Host-side choice of the coset qubits for an n-qubit state and the given group flip masks;
+// fills `tables` (host, ntables x 256) and the counts, or leaves it empty for index order.
+void pauli_traversal_tables(uint32_t n, const std::vector<uint64_t> &flips,
+                            std::vector<uint64_t> &tables, PauliTraversal &tr);
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
                       const double2 *w, const uint64_t *z, const uint64_t *flip,
                       const uint32_t *first, const uint32_t *count, uint32_t ngroups,
-                      double *partials, bool accumulate, cudaStream_t s);
+                      const PauliTraversal &tr, double *partials, bool accumulate,
+                      cudaStream_t s);
 
 // Moves the slices of a shard with slice value y != skip (bit i of y at positions[i]) between
 // the shard and staging blocks [block][chunk_len], for other-index o in [chunk_begin, +chunk_len).
