@@ -45,12 +45,29 @@ def headers():
     return hs
 
 
+JIT_INC = os.path.join(OBJ, "jit_source.inc")
+
+
+def write_jit_source() -> None:
+    """Embeds fused.h and fused_core.cuh as string literals for the run-time pass compiler."""
+    parts = []
+    for var, name in (("kJitFusedH", "fused.h"), ("kJitCore", "fused_core.cuh")):
+        text = open(os.path.join(CSRC, name)).read()
+        if ")ARCQMLSRC" in text:
+            raise RuntimeError(f"{name} contains the raw-string delimiter")
+        parts.append(f'static const char {var}[] = R"ARCQMLSRC({text})ARCQMLSRC";\n')
+    body = "".join(parts)
+    if not os.path.exists(JIT_INC) or open(JIT_INC).read() != body:
+        with open(JIT_INC, "w") as f:
+            f.write(body)
+
+
 def _compile(src: str, verbose: bool) -> str:
     obj = os.path.join(OBJ, os.path.basename(src) + ".o")
     newest_dep = max([os.path.getmtime(src)] + [os.path.getmtime(h) for h in headers()])
     if os.path.exists(obj) and os.path.getmtime(obj) >= newest_dep:
         return obj
-    cmd = [nvcc()] + NVCC_FLAGS + ["-x", "cu", "-c", src, "-o", obj]
+    cmd = [nvcc()] + NVCC_FLAGS + ["-I", OBJ, "-x", "cu", "-c", src, "-o", obj]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -66,6 +83,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     if force:
         for f in os.listdir(OBJ):
             os.remove(os.path.join(OBJ, f))
+    write_jit_source()
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), sources()))
     newest = max(os.path.getmtime(o) for o in objs)

@@ -5,11 +5,13 @@
 // message; nothing throws or aborts across the boundary.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <new>
 #include <sstream>
 
 #include "../../include/arcqml_runtime.h"
 #include "../../include/arcqml_runtime_v2.h"
+#include "jit.h"
 #include "launch.h"
 #include "planner.h"
 #include "profile.h"
@@ -532,6 +534,48 @@ int32_t arcqml_rt_v2_sample(const arcqml_c128 *amplitudes, size_t num_qubits, ui
             fail(m.str());
         }
     });
+}
+
+int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qubits,
+                                    int32_t adjoint, uint64_t *compiled, uint64_t *eligible,
+                                    char *message, size_t capacity) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        state_dimension(num_qubits);
+        const uint32_t n = uint32_t(num_qubits);
+        if (n < kFusedMinQubits) fail("plans below 8 qubits run no fused passes");
+        validate_plan_for_state(*p, n);
+        size_t parents = 1;
+        for (const auto &op : p->ops)
+            for (uint32_t b = 0; b < op.num_bindings; ++b)
+                parents = std::max(parents, op.parents[b] + 1);
+        std::vector<uint8_t> req(parents, 1);
+        const uint32_t k = fused_k(n, adjoint != 0);
+        Schedule sch = build_schedule(*p, n, adjoint != 0, req.data(), adjoint != 0, k,
+                                      fused_rb(k, adjoint != 0));
+        size_t el = 0;
+        std::string err;
+        const size_t ok = jit_compile_check(sch, adjoint != 0, &el, &err);
+        if (compiled) *compiled = ok;
+        if (eligible) *eligible = el;
+        if (message && capacity) {
+            const size_t m = std::min(capacity - 1, err.size());
+            std::memcpy(message, err.data(), m);
+            message[m] = '\0';
+        }
+    });
+}
+
+size_t arcqml_rt_v2_jit_info(uint64_t *kernels_compiled, uint64_t *launches, uint64_t *fallbacks,
+                             char *last_error, size_t capacity) {
+    std::string last;
+    jit_info(kernels_compiled, launches, fallbacks, &last);
+    if (last_error && capacity) {
+        const size_t n = std::min(capacity - 1, last.size());
+        std::memcpy(last_error, last.data(), n);
+        last_error[n] = '\0';
+    }
+    return last.size();
 }
 
 int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,

@@ -7,9 +7,13 @@
 // one read and one write per amplitude per pass; the arithmetic runs from registers.
 //
 // Adjoint passes apply U^dagger to psi and lambda and accumulate, per bound parameter slot,
-// Re<lambda_k| dU/dp |psi_{k-1}> (for Pauli rotations as Im<lambda_k|P|psi_k> / 2): each warp
-// reduces its lanes with shuffles and adds into its own shared-memory column; columns are summed
-// per CTA at the end into partials[acc][block] (fixed order, deterministic).
+// Re<lambda_k| dU/dp |psi_{k-1}> (for Pauli rotations as Im<lambda_k|P|psi_k> / 2) into the
+// thread's own shared-memory column; columns are summed per CTA at the end into
+// partials[acc][block] (fixed order, deterministic).
+//
+// The tile loop and the fast gate paths live in fused_core.cuh. The kernels here interpret the
+// pass's op table (one dispatch per op); jit.cpp compiles per-pass kernels in which the same
+// fast paths are inlined in the pass's op order.
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -18,6 +22,7 @@
 #include <vector>
 
 #include "fused.h"
+#include "jit.h"
 #include "launch.h"
 #include "planner.h"
 #include "profile.h"
@@ -26,20 +31,7 @@ namespace arcqml {
 
 namespace {
 
-
-__device__ __forceinline__ uint32_t phys(uint32_t j) {
-    return j ^ (((j >> 3) ^ (j >> 6) ^ (j >> 9)) & 7u);
-}
-
-__device__ __forceinline__ double2 cmul(double2 a, double2 b) {
-    return make_double2(fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x));
-}
-__device__ __forceinline__ double2 cfma(double2 a, double2 b, double2 c) {
-    return make_double2(fma(a.x, b.x, fma(-a.y, b.y, c.x)), fma(a.x, b.y, fma(a.y, b.x, c.y)));
-}
-// Re(conj(a) b) and Im(conj(a) b)
-__device__ __forceinline__ double rcm(double2 a, double2 b) { return fma(a.x, b.x, a.y * b.y); }
-__device__ __forceinline__ double icm(double2 a, double2 b) { return fma(a.x, b.y, -a.y * b.x); }
+#include "fused_core.cuh"
 
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
@@ -52,19 +44,6 @@ __device__ __forceinline__ void load_op(const FOp *src, FOp &dst) {
     uint4 *d = reinterpret_cast<uint4 *>(&dst);
 #pragma unroll
     for (int i = 0; i < 4; ++i) d[i] = s[i];
-}
-
-__device__ __forceinline__ double2 ld(const double2 *p) { return *p; }
-
-// 16-byte asynchronous global -> shared copy (LDGSTS); completion via commit/wait groups.
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
 struct OpEnv {
@@ -404,157 +383,6 @@ __device__ __forceinline__ int dmat_len(uint8_t kind) {
     }
 }
 
-// Adds z into this thread's own column of accumulator row `row` (= acc * blockDim.x): no
-// cross-lane traffic per gate; the columns are summed once per pass at the end of the kernel.
-__device__ __forceinline__ void accumulate(double *sacc, uint32_t row, double z) {
-    sacc[row + threadIdx.x] += z;
-}
-
-// ---------------------------------------------------------------- specialised fast paths
-//
-// Uncontrolled gates with compile-time register bits: pure FP64 arithmetic on the thread's
-// registers, no per-element index or control logic. Sign flips (CZ, Z) toggle the sign bit
-// of the high word with an integer XOR instead of using the FP64 pipe.
-
-__device__ __forceinline__ double flip(double x, uint32_t m) {
-    return __hiloint2double(__double2hiint(x) ^ int(m), __double2loint(x));
-}
-__device__ __forceinline__ double2 flip2(double2 a, uint32_t m) {
-    return make_double2(flip(a.x, m), flip(a.y, m));
-}
-
-template <int RB, int B>
-__device__ __forceinline__ void f_rx(double2 (&v)[1 << RB], double c, double s) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        if (e & (1 << B)) continue;
-        const int f = e | (1 << B);
-        const double2 x0 = v[e], x1 = v[f];
-        v[e] = make_double2(fma(c, x0.x, s * x1.y), fma(c, x0.y, -s * x1.x));
-        v[f] = make_double2(fma(c, x1.x, s * x0.y), fma(c, x1.y, -s * x0.x));
-    }
-}
-
-template <int RB, int B>
-__device__ __forceinline__ void f_ry(double2 (&v)[1 << RB], double c, double s) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        if (e & (1 << B)) continue;
-        const int f = e | (1 << B);
-        const double2 x0 = v[e], x1 = v[f];
-        v[e] = make_double2(fma(c, x0.x, -s * x1.x), fma(c, x0.y, -s * x1.y));
-        v[f] = make_double2(fma(s, x0.x, c * x1.x), fma(s, x0.y, c * x1.y));
-    }
-}
-
-template <int RB, int B>
-__device__ __forceinline__ void f_m2(double2 (&v)[1 << RB], const double2 *mt) {
-    const double2 m0 = mt[0], m1 = mt[1], m2 = mt[2], m3 = mt[3];
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        if (e & (1 << B)) continue;
-        const int f = e | (1 << B);
-        const double2 x0 = v[e], x1 = v[f];
-        v[e] = cfma(m0, x0, cmul(m1, x1));
-        v[f] = cfma(m2, x0, cmul(m3, x1));
-    }
-}
-
-template <int RB, int B>
-__device__ __forceinline__ void f_d1_reg(double2 (&v)[1 << RB], double2 d0, double2 d1) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) v[e] = cmul((e >> B) & 1 ? d1 : d0, v[e]);
-}
-
-template <int RB>
-__device__ __forceinline__ void f_d1_uni(double2 (&v)[1 << RB], double2 d) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) v[e] = cmul(d, v[e]);
-}
-
-template <int RB, int B0, int B1>
-__device__ __forceinline__ void f_sign_rr(double2 (&v)[1 << RB]) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e)
-        if (((e >> B0) & 1) && ((e >> B1) & 1)) v[e] = flip2(v[e], 0x80000000u);
-}
-
-template <int RB, int B>
-__device__ __forceinline__ void f_sign_rc(double2 (&v)[1 << RB], uint32_t m) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e)
-        if ((e >> B) & 1) v[e] = flip2(v[e], m);
-}
-
-template <int RB>
-__device__ __forceinline__ void f_sign_cc(double2 (&v)[1 << RB], uint32_t m) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) v[e] = flip2(v[e], m);
-}
-
-template <int RB, int B0, int B1>
-__device__ __forceinline__ void f_m4(double2 (&v)[1 << RB], const double2 *mt) {
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        if (e & ((1 << B0) | (1 << B1))) continue;
-        const int idx[4] = {e, e | (1 << B0), e | (1 << B1), e | (1 << B0) | (1 << B1)};
-        double2 x[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x[j] = v[idx[j]];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            double2 acc = cmul(mt[i * 4], x[0]);
-            acc = cfma(mt[i * 4 + 1], x[1], acc);
-            acc = cfma(mt[i * 4 + 2], x[2], acc);
-            acc = cfma(mt[i * 4 + 3], x[3], acc);
-            v[idx[i]] = acc;
-        }
-    }
-}
-
-template <int RB, int B>
-__device__ __forceinline__ double g_x(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        if (e & (1 << B)) continue;
-        const int f = e | (1 << B);
-        z += icm(w[e], v[f]) + icm(w[f], v[e]);
-    }
-    return z;
-}
-
-template <int RB, int B>
-__device__ __forceinline__ double g_y(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        if (e & (1 << B)) continue;
-        const int f = e | (1 << B);
-        z += rcm(w[f], v[e]) - rcm(w[e], v[f]);
-    }
-    return z;
-}
-
-template <int RB, int B>
-__device__ __forceinline__ double g_z(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) {
-        const double t = icm(w[e], v[e]);
-        z += ((e >> B) & 1) ? -t : t;
-    }
-    return z;
-}
-
-template <int RB>
-__device__ __forceinline__ double g_z_uni(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
-#pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) z += icm(w[e], v[e]);
-    return z;
-}
-
 // Dispatch a template over a runtime register bit b (< RB).
 #define ARCQML_BITS(b, CALL)                          \
     switch (b) {                                      \
@@ -566,11 +394,6 @@ __device__ __forceinline__ double g_z_uni(const double2 (&v)[1 << RB], const dou
         break;                                        \
     }
 
-// Per-thread value of a qubit that is not a register bit: a tile bit lives in the thread's
-// base index tb, a qubit outside the tile in the tile's global base.
-__device__ __forceinline__ uint32_t const_bit(const FOp &o, int slot, uint32_t tb, uint64_t gbase) {
-    return o.dq_in_tile[slot] ? ((tb >> o.dq_pos[slot]) & 1u) : uint32_t((gbase >> o.dq_pos[slot]) & 1u);
-}
 
 // Applies op o (U or U^dagger) to the registers through its fast path; false if the op
 // needs the generic path.
@@ -753,15 +576,6 @@ __device__ __noinline__ double slow_grad(const FOp *op, const double2 *d, const 
     return grad_xy_dispatch<RB>(o.rb0, o.gkind == GK_PY, v, w, Le, E);
 }
 
-// Tile-local index of a thread's register element e in the current sub-block.
-template <int RB>
-__device__ __forceinline__ uint32_t sub_index(uint32_t tb, const uint32_t (&rm)[RB], int e) {
-    uint32_t x = tb;
-#pragma unroll
-    for (int r = 0; r < RB; ++r)
-        if ((e >> r) & 1) x |= rm[r];
-    return x;
-}
 
 // Adjoint step for the common uncontrolled gates in one dispatch: the Pauli-rotation gradient
 // (from psi_k, lambda_k), then U^dagger on psi and on lambda. Returns false when the op needs
@@ -918,33 +732,39 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
 
 // ---------------------------------------------------------------- the pass kernel
 
-// Shared memory: [tile buffers][hioff][accumulators][ops][matrices].
-// Forward: two psi buffers; while a CTA computes tile i from one, cp.async streams tile
-// i + gridDim into the other. Adjoint: one psi and one lambda buffer (the next tile is
-// prefetched into L2 instead) and one accumulator column per thread.
-struct SmemLayout {
-    uint32_t tile, hioff, sacc, ops, mats, total;
-};
 
-__host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t nacc,
-                                                  uint32_t nops, uint32_t nmat, uint32_t nthreads) {
-    const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
-    SmemLayout m;
-    m.tile = 0;
-    uint32_t off = 2u * (16u << k);
-    m.hioff = off;
-    off += 8u << (k - L);
-    off = (off + 15u) & ~15u;
-    m.sacc = off;
-    off += adj ? nacc * nthreads * 8u : 0u;
-    off = (off + 15u) & ~15u;
-    m.ops = off;
-    off += nops * uint32_t(sizeof(FOp));
-    m.mats = off;
-    off += nmat * 16u;
-    m.total = off;
-    return m;
-}
+
+// ---------------------------------------------------------------- the precompiled pass kernel
+
+// Applies sub-block sb by interpreting its op table: sub-blocks whose ops all have fast paths
+// run an inline loop with one dispatch per op, the others the out-of-line general routine.
+struct TableRunner {
+    template <int RB, bool ADJ>
+    __device__ static __forceinline__ void run(const SubBlock &S, uint32_t sb, double2 *tp,
+                                               double2 *tl, const FOp *ops, const double2 *mats,
+                                               const SubBlock *subs, double *sacc,
+                                               uint32_t nthreads, uint32_t tb, uint64_t gbase) {
+        if (!(S.flags & SB_ALL_FAST)) {
+            general_subblock<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nthreads, tb, gbase);
+            return;
+        }
+        double2 v[1 << RB], w[1 << RB];
+        load_regs<RB, ADJ>(S, tb, tp, tl, v, w);
+        for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
+            FOp o;
+            load_op(ops + oi, o);
+            const double2 *mt = mats + o.moff;
+            if constexpr (ADJ) {
+                double z = 0.0;
+                adj_fast<RB>(o, mt, v, w, tb, gbase, z);
+                if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nthreads, 0.5 * z);
+            } else {
+                apply_fast<RB>(o, mt, v, tb, gbase);
+            }
+        }
+        store_regs<RB, ADJ>(S, tb, tp, tl, v, w);
+    }
+};
 
 template <int RB, bool ADJ>
 __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
@@ -952,187 +772,8 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
             uint64_t total_tiles, const PassHeader *__restrict__ hdr,
             const SubBlock *__restrict__ subs, const FOp *__restrict__ gops,
             const double2 *__restrict__ gmats, double *__restrict__ partials, uint32_t stride) {
-    constexpr int N = 1 << RB;
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ uint8_t sS[16];
-    __shared__ uint32_t sk, snsub, snacc, sacc_base, snops, snmat;
-    if (threadIdx.x < 16) sS[threadIdx.x] = hdr->S[threadIdx.x];
-    if (threadIdx.x == 0) {
-        sk = hdr->k;
-        snsub = hdr->nsub;
-        snacc = hdr->nacc;
-        sacc_base = hdr->acc_base;
-        snops = hdr->nops;
-        snmat = hdr->nmat;
-    }
-    __syncthreads();
-    const uint32_t k = sk;
-    const uint32_t D = 1u << k;
-    const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
-    const uint32_t lowmask = (1u << L) - 1;
-    const uint32_t nthreads = blockDim.x;
-    const SmemLayout lay = smem_layout(ADJ, k, snacc, snops, snmat, nthreads);
-    double2 *bufs = reinterpret_cast<double2 *>(smem + lay.tile);
-    uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + lay.hioff);
-    double *sacc = reinterpret_cast<double *>(smem + lay.sacc);
-    FOp *ops = reinterpret_cast<FOp *>(smem + lay.ops);
-    double2 *mats = reinterpret_cast<double2 *>(smem + lay.mats);
-    // forward: buffer b; adjoint: state st (0 = psi, 1 = lambda) of the single buffer
-    auto tile_buf = [&](int b, int st) { return bufs + size_t(ADJ ? st : b) * D; };
-
-    for (uint32_t h = threadIdx.x; h < (1u << (k - L)); h += blockDim.x) {
-        uint64_t off = 0;
-        for (uint32_t b = 0; b < k - L; ++b)
-            if ((h >> b) & 1) off |= uint64_t(1) << sS[L + b];
-        hioff[h] = off;
-    }
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(gops);
-        uint4 *dst = reinterpret_cast<uint4 *>(ops);
-        for (uint32_t i = threadIdx.x; i < snops * 4; i += blockDim.x) dst[i] = src[i];
-        for (uint32_t i = threadIdx.x; i < snmat; i += blockDim.x) mats[i] = gmats[i];
-    }
-    if (ADJ)
-        for (uint32_t a = threadIdx.x; a < snacc * nthreads; a += blockDim.x) sacc[a] = 0.0;
-    __syncthreads();
-
-    const uint64_t tmask = (uint64_t(1) << tiles_log) - 1;
-    auto tile_base = [&](uint64_t T) {
-        uint64_t g = T & tmask;
-        for (uint32_t b = 0; b < k; ++b) {
-            const uint32_t p = sS[b];
-            g = ((g >> p) << (p + 1)) | (g & ((uint64_t(1) << p) - 1));
-        }
-        return g;
-    };
-    auto issue_load = [&](uint64_t T, int b) {
-        const uint64_t off = ((T >> tiles_log) << n) + tile_base(T);
-        const double2 *P = psi + off;
-        const double2 *Lm = ADJ ? lam + off : nullptr;
-        double2 *tp = tile_buf(b, 0);
-        double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
-        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
-            const uint64_t g = (j & lowmask) | hioff[j >> L];
-            cp_async16(tp + phys(j), P + g);
-            if (ADJ) cp_async16(tl + phys(j), Lm + g);
-        }
-        cp_async_commit();
-    };
-
-    // Applies every sub-block of the pass to the tile in buffer b and writes it back.
-    auto process_tile = [&](uint64_t T, int b) {
-        const uint64_t gbase = tile_base(T);
-        double2 *tp = tile_buf(b, 0);
-        double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
-        for (uint32_t sb = 0; sb < snsub; ++sb) {
-            SubBlock S;
-            {
-                const uint2 *src = reinterpret_cast<const uint2 *>(subs + sb);
-                uint2 *d = reinterpret_cast<uint2 *>(&S);
-#pragma unroll
-                for (int i = 0; i < 3; ++i) d[i] = __ldg(src + i);
-            }
-            uint32_t tb = 0;
-#pragma unroll
-            for (int i = 0; i < 12 - RB; ++i)
-                if (i < int(k) - RB && ((threadIdx.x >> i) & 1)) tb |= 1u << S.perm[i];
-            uint32_t rm[RB];
-#pragma unroll
-            for (int r = 0; r < RB; ++r) rm[r] = 1u << S.R[r];
-            if (S.flags & SB_ALL_FAST) {
-                double2 v[N], w[N];
-#pragma unroll
-                for (int e = 0; e < N; ++e) {
-                    const uint32_t x = sub_index<RB>(tb, rm, e);
-                    v[e] = tp[phys(x)];
-                    if (ADJ) w[e] = tl[phys(x)];
-                }
-                for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
-                    FOp o;
-                    load_op(ops + oi, o);
-                    const double2 *mt = mats + o.moff;
-                    if constexpr (ADJ) {
-                        double z = 0.0;
-                        adj_fast<RB>(o, mt, v, w, tb, gbase, z);
-                        if (o.gkind != GK_NONE) accumulate(sacc, o.acc[0] * nthreads, 0.5 * z);
-                    } else {
-                        apply_fast<RB>(o, mt, v, tb, gbase);
-                    }
-                }
-#pragma unroll
-                for (int e = 0; e < N; ++e) {
-                    const uint32_t x = sub_index<RB>(tb, rm, e);
-                    tp[phys(x)] = v[e];
-                    if (ADJ) tl[phys(x)] = w[e];
-                }
-            } else {
-                general_subblock<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nthreads, tb,
-                                          gbase);
-            }
-            __syncthreads();
-        }
-        const uint64_t off = ((T >> tiles_log) << n) + gbase;
-        double2 *P = psi + off;
-        double2 *Lm = ADJ ? lam + off : nullptr;
-        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
-            const uint64_t g = (j & lowmask) | hioff[j >> L];
-            P[g] = tp[phys(j)];
-            if (ADJ) Lm[g] = tl[phys(j)];
-        }
-    };
-
-    if constexpr (ADJ) {
-        // One buffer: load tile T, ask L2 for tile T + gridDim while T is computed.
-        const uint32_t run_bytes = 16u << L;
-        const uint32_t lines = run_bytes >= 128u ? run_bytes / 128u : 1u;
-        for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x) {
-            issue_load(T, 0);
-            const uint64_t Tn = T + gridDim.x;
-            if (Tn < total_tiles) {
-                const uint64_t off = ((Tn >> tiles_log) << n) + tile_base(Tn);
-                const char *P = reinterpret_cast<const char *>(psi + off);
-                const char *Lm = reinterpret_cast<const char *>(lam + off);
-                const uint32_t count = lines << (k - L);
-                for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) {
-                    const size_t o = size_t(hioff[i / lines]) * 16u + size_t(i % lines) * 128u;
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(P + o));
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(Lm + o));
-                }
-            }
-            cp_async_wait<0>();
-            __syncthreads();
-            process_tile(T, 0);
-            __syncthreads();
-        }
-    } else {
-        if (uint64_t(blockIdx.x) < total_tiles) issue_load(blockIdx.x, 0);
-        else cp_async_commit();
-        int b = 0;
-        for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x, b ^= 1) {
-            const uint64_t Tn = T + gridDim.x;
-            if (Tn < total_tiles) issue_load(Tn, b ^ 1);
-            else cp_async_commit();
-            cp_async_wait<1>();
-            __syncthreads();
-            process_tile(T, b);
-            __syncthreads();
-        }
-    }
-    cp_async_wait<0>();
-    if (ADJ) {
-        // column sums in a fixed order (deterministic)
-        for (uint32_t a = threadIdx.x; a < snacc; a += blockDim.x) {
-            const double *row = sacc + size_t(a) * nthreads;
-            double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-            for (uint32_t t = 0; t < nthreads; t += 4) {
-                s0 += row[t];
-                s1 += row[t + 1];
-                s2 += row[t + 2];
-                s3 += row[t + 3];
-            }
-            partials[size_t(sacc_base + a) * stride + blockIdx.x] = (s0 + s1) + (s2 + s3);
-        }
-    }
+    fused_body<RB, ADJ, TableRunner>(psi, lam, n, tiles_log, total_tiles, hdr, subs, gops, gmats,
+                                     partials, stride);
 }
 
 size_t fused_smem(bool adj, uint32_t k, uint32_t nacc, uint32_t nops, uint32_t nmat,
@@ -1207,6 +848,8 @@ uint32_t fused_grid_blocks(bool adjoint, uint32_t k, uint32_t rb) {
 void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch, uint32_t n,
                   double *partials, uint32_t partial_stride, ThreadContext &ctx, cudaStream_t s) {
     const bool adj = lam != nullptr;
+    // Compiled kernels of the passes that have one (compiled once per circuit structure).
+    const std::vector<void *> jit = jit_kernels(sch, adj);
     // Upload every pass's tables into one device blob (16-byte aligned sections).
     struct Off {
         size_t hdr, subs, ops, mats;
@@ -1276,9 +919,23 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         // algorithmic traffic: psi (and lambda) read and written once per pass
         const double bytes = (adj ? 64.0 : 32.0) * double(uint64_t(batch) << n);
         const ProfToken tok = prof_begin(adj ? PROF_FUSED_ADJ : PROF_FUSED_FWD, s);
-        fused_kernel(adj, st.header.rb)<<<grid, fused_threads(k, st.header.rb), smem, s>>>(
-            psi, adj ? lam : nullptr, n, tiles_log, total_tiles, hdr, sub, ops, mats,
-            adj ? partials : nullptr, adj ? partial_stride : 0);
+        if (jit[i]) {
+            double2 *a_psi = psi, *a_lam = adj ? lam : nullptr;
+            uint32_t a_n = n, a_tl = tiles_log, a_stride = adj ? partial_stride : 0;
+            uint64_t a_tt = total_tiles;
+            const PassHeader *a_h = hdr;
+            const SubBlock *a_sub = sub;
+            const FOp *a_ops = ops;
+            const double2 *a_mats = mats;
+            double *a_part = adj ? partials : nullptr;
+            void *args[] = {&a_psi, &a_lam, &a_n, &a_tl, &a_tt, &a_h, &a_sub, &a_ops, &a_mats,
+                            &a_part, &a_stride};
+            jit_launch(jit[i], grid, fused_threads(k, st.header.rb), smem, s, args);
+        } else {
+            fused_kernel(adj, st.header.rb)<<<grid, fused_threads(k, st.header.rb), smem, s>>>(
+                psi, adj ? lam : nullptr, n, tiles_log, total_tiles, hdr, sub, ops, mats,
+                adj ? partials : nullptr, adj ? partial_stride : 0);
+        }
         prof_end(tok, s, bytes);
         check_cuda(cudaGetLastError(), "fused pass launch");
     }

@@ -14,7 +14,9 @@
 // lane bits map to tile bits with distinct residues mod 3 touches 8 distinct 16-byte bank slots.
 #pragma once
 
+#ifndef __CUDACC_RTC__
 #include <stdint.h>
+#endif
 
 namespace arcqml {
 

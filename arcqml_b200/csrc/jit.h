@@ -1,0 +1,28 @@
+// jit.h — per-pass fused kernels compiled at run time (jit.cpp).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "planner.h"
+
+namespace arcqml {
+
+// False when ARCQML_JIT=0.
+bool jit_enabled();
+// Per step of the schedule: its compiled kernel, or nullptr where the step has no compiled form
+// (a dense barrier, an op without a fast path, or a failed compile) and the precompiled pass
+// kernel runs instead. Kernels are compiled once per circuit structure and device.
+std::vector<void *> jit_kernels(const Schedule &sch, bool adjoint);
+// Launches a compiled pass kernel with the precompiled kernel's argument list.
+void jit_launch(void *fn, unsigned grid, unsigned threads, size_t smem, cudaStream_t s,
+                void **args);
+// Compiles the schedule's passes with NVRTC only (no device needed); returns how many compiled,
+// with the number that have a compiled form in *eligible and the first error in *err.
+size_t jit_compile_check(const Schedule &sch, bool adjoint, size_t *eligible, std::string *err);
+void jit_info(uint64_t *compiled, uint64_t *launches, uint64_t *fallbacks, std::string *last);
+
+}  // namespace arcqml

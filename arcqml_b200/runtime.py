@@ -134,6 +134,8 @@ def load():
         "arcqml_rt_v2_profile_enable": (None, [I32]),
         "arcqml_rt_v2_profile_read": (I32, [C.c_uint32, P, P, P]),
         "arcqml_rt_v2_launch_count": (C.c_uint64, []),
+        "arcqml_rt_v2_jit_info": (S, [P, P, P, P, S]),
+        "arcqml_rt_v2_plan_jit_check": (I32, [P, S, I32, P, P, P, S]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -337,6 +339,16 @@ class CircuitPlan:
         v = np.ascontiguousarray(parent_values, dtype=np.float64)
         _status(load().arcqml_rt_v2_plan_set_parameters(C.byref(self.raw), v.ctypes.data, v.size))
 
+    def jit_check(self, num_qubits: int, adjoint: bool = False) -> dict:
+        """Compiles the run-time kernels of this plan's fused passes (NVRTC only, no GPU):
+        {compiled, eligible, message}."""
+        c, e = C.c_uint64(), C.c_uint64()
+        buf = C.create_string_buffer(4096)
+        _status(load().arcqml_rt_v2_plan_jit_check(C.byref(self.raw), num_qubits, int(adjoint),
+                                                   C.byref(c), C.byref(e), buf, 4096))
+        return {"compiled": int(c.value), "eligible": int(e.value),
+                "message": buf.value.decode("utf-8", errors="replace")}
+
     def __len__(self) -> int:
         return load().arcqml_rt_v2_plan_len(C.byref(self.raw))
 
@@ -530,3 +542,12 @@ def profile_read() -> dict:
 
 def launch_count() -> int:
     return int(load().arcqml_rt_v2_launch_count())
+
+
+def jit_info() -> dict:
+    """Run-time compiled pass kernels: {compiled, launches, fallbacks, last_error}."""
+    c, l, f = C.c_uint64(), C.c_uint64(), C.c_uint64()
+    buf = C.create_string_buffer(4096)
+    load().arcqml_rt_v2_jit_info(C.byref(c), C.byref(l), C.byref(f), buf, 4096)
+    return {"compiled": int(c.value), "launches": int(l.value), "fallbacks": int(f.value),
+            "last_error": buf.value.decode("utf-8", errors="replace")}

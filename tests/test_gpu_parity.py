@@ -290,3 +290,62 @@ def test_observable_coset_traversal_matches_oracle(runtime, oracle, n):
     rel_close(vals2[0], v_ref)
     got = acc.cpu().numpy() - base.cpu().numpy()
     assert float(np.max(np.abs(got - h_ref))) <= 1e-11 * max(1.0, np.abs(h_ref).max())
+
+
+def test_compiled_pass_kernels_run_and_match_oracle(runtime, oracle):
+    """Brickwork passes run as run-time compiled kernels (no fallback) and match the oracle."""
+    import torch
+    from arcqml_b200.workloads import brickwork, random_pauli_sum
+    n = 14
+    c = brickwork(n, 5, seed=77)
+    obs = random_pauli_sum(n, 30, seed=78)
+    before = runtime.jit_info()
+    ops = c.compile_plan(1)
+    req = c.requires_grad_mask(True)
+    plan = runtime.CircuitPlan.create(ops)
+    psi = torch.zeros(1 << n, dtype=torch.complex128, device="cuda")
+    runtime.set_basis_state_device(psi, n, 0)
+    runtime.plan_apply_device(plan, psi, n)
+    lam = torch.empty_like(psi)
+    ro = runtime.Observable.from_sparse_pauli_op(obs)
+    value = ro.expectation_and_apply(psi, lam, n)[0]
+    grads = runtime.adjoint_backward_device(plan, psi, lam, n, 0.5, req, len(req))
+    after = runtime.jit_info()
+    assert after["launches"] > before["launches"], after
+    assert after["fallbacks"] == before["fallbacks"], after["last_error"]
+    init = np.zeros(1 << n, np.complex128)
+    init[0] = 1
+    ref_psi = oracle.plan_apply(ops, init, n)
+    ref_v, ref_lam = oracle.expectation_and_apply(obs.compiled_terms(), ref_psi, n)
+    _, _, ref_g = oracle.adjoint_backward(ops, ref_psi, ref_lam, n, 0.5, req, len(req))
+    rel_close(value, ref_v)
+    rel_close(grads, ref_g)
+
+
+def test_precompiled_pass_kernels_match_oracle_without_jit(runtime):
+    """With ARCQML_JIT=0 every pass runs the precompiled table-driven kernel (subprocess)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys; sys.path[:0]=[%r, %r]\n"
+        "import numpy as np, torch, oracle as O\n"
+        "from arcqml_b200 import runtime as rt, workloads as W\n"
+        "n=14; c=W.brickwork(n,5,seed=77); obs=W.random_pauli_sum(n,30,seed=78)\n"
+        "ops=c.compile_plan(1); req=c.requires_grad_mask(True); plan=rt.CircuitPlan.create(ops)\n"
+        "psi=torch.zeros(1<<n,dtype=torch.complex128,device='cuda'); rt.set_basis_state_device(psi,n,0)\n"
+        "rt.plan_apply_device(plan,psi,n); lam=torch.empty_like(psi)\n"
+        "v=rt.Observable.from_sparse_pauli_op(obs).expectation_and_apply(psi,lam,n)[0]\n"
+        "g=rt.adjoint_backward_device(plan,psi,lam,n,0.5,req,len(req))\n"
+        "init=np.zeros(1<<n,np.complex128); init[0]=1; rp=O.plan_apply(ops,init,n)\n"
+        "rv,rl=O.expectation_and_apply(obs.compiled_terms(),rp,n)\n"
+        "_,_,rg=O.adjoint_backward(ops,rp,rl,n,0.5,req,len(req))\n"
+        "assert abs(v-rv)<=1e-10*max(1,abs(rv)), (v,rv)\n"
+        "assert np.max(np.abs(g-rg))<=1e-10*max(1,np.max(np.abs(rg)))\n"
+        "assert rt.jit_info()['launches']==0\n"
+        "print('aot-ok')\n") % (root, os.path.join(root, "oracle"))
+    env = dict(os.environ, ARCQML_JIT="0")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=600)
+    assert r.returncode == 0 and "aot-ok" in r.stdout, r.stdout + r.stderr
