@@ -391,47 +391,50 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
     }
     const size_t nt = obs.coef.size();
     const size_t ng = obs.groups.size();
-    // Pack tables: w (double2 per term), z (u64 per term), flip (u64 per group),
-    // first/count (u32 per group), all in one upload.
+    // Pack tables in one upload: w' (double2 per term), z (u64 per term), flip (u64 per group),
+    // term ranges (u32 per group + 1), then the traversal tables (16-byte aligned).
     std::vector<uint64_t> gflips(ng), ptab;
     for (size_t g = 0; g < ng; ++g) gflips[g] = obs.groups[g].flip;
     PauliTraversal tr;
     pauli_traversal_tables(n, gflips, ptab, tr);
-    const size_t wz_bytes = nt * 16 + nt * 8;
-    const size_t g_bytes = ng * 8 + ng * 8;
-    const size_t t_off = (wz_bytes + g_bytes + 15) & ~size_t(15);
-    std::vector<double2> pack((t_off + ptab.size() * 8 + 15) / 16 + 1);
+    const size_t tab_bytes = (nt * 24 + ng * 8 + (ng + 1) * 4 + 15) & ~size_t(15);
+    std::vector<double2> pack((tab_bytes + ptab.size() * 8 + 15) / 16 + 1);
     char *base = reinterpret_cast<char *>(pack.data());
     double2 *w = reinterpret_cast<double2 *>(base);
     uint64_t *z = reinterpret_cast<uint64_t *>(base + nt * 16);
     uint64_t *flip = reinterpret_cast<uint64_t *>(base + nt * 24);
-    uint32_t *first = reinterpret_cast<uint32_t *>(base + nt * 24 + ng * 8);
-    uint32_t *count = first + ng;
-    for (size_t k = 0; k < nt; ++k) {
-        const double c = obs.coef[k];
-        switch (obs.ymod4[k] & 3u) {
-        case 0: w[k] = make_double2(c, 0.0); break;
-        case 1: w[k] = make_double2(0.0, c); break;
-        case 2: w[k] = make_double2(-c, 0.0); break;
-        default: w[k] = make_double2(0.0, -c); break;
-        }
-        z[k] = obs.zmask[k];
-    }
+    uint32_t *ends = reinterpret_cast<uint32_t *>(base + nt * 24 + ng * 8);
     for (size_t g = 0; g < ng; ++g) {
-        flip[g] = obs.groups[g].flip;
-        first[g] = obs.groups[g].first;
-        count[g] = obs.groups[g].count;
+        const auto &grp = obs.groups[g];
+        flip[g] = grp.flip;
+        ends[g] = grp.first;
+        for (uint32_t k = grp.first; k < grp.first + grp.count; ++k) {
+            // (-1)^popc((t ^ f) & z) = (-1)^popc(f & z) (-1)^popc(t & z): fold the first factor
+            const double c = (__builtin_popcountll(grp.flip & obs.zmask[k]) & 1) ? -obs.coef[k]
+                                                                                 : obs.coef[k];
+            switch (obs.ymod4[k] & 3u) {
+            case 0: w[k] = make_double2(c, 0.0); break;
+            case 1: w[k] = make_double2(0.0, c); break;
+            case 2: w[k] = make_double2(-c, 0.0); break;
+            default: w[k] = make_double2(0.0, -c); break;
+            }
+            z[k] = obs.zmask[k];
+        }
     }
-    if (!ptab.empty()) std::memcpy(base + t_off, ptab.data(), ptab.size() * 8);
+    ends[ng] = uint32_t(nt);
+    if (!ptab.empty()) std::memcpy(base + tab_bytes, ptab.data(), ptab.size() * 8);
     std::vector<const std::vector<double2> *> refs{&pack};
     auto p = upload_tables(refs, ctx, s);
     const char *dbase = reinterpret_cast<const char *>(p[0]);
-    if (!ptab.empty()) tr.tables = reinterpret_cast<const uint64_t *>(dbase + t_off);
-    const double2 *dw = reinterpret_cast<const double2 *>(dbase);
-    const uint64_t *dz = reinterpret_cast<const uint64_t *>(dbase + nt * 16);
-    const uint64_t *dflip = reinterpret_cast<const uint64_t *>(dbase + nt * 24);
-    const uint32_t *dfirst = reinterpret_cast<const uint32_t *>(dbase + nt * 24 + ng * 8);
-    const uint32_t *dcount = dfirst + ng;
+    if (!ptab.empty()) tr.tables = reinterpret_cast<const uint64_t *>(dbase + tab_bytes);
+    PauliTables tab;
+    tab.w = reinterpret_cast<const double2 *>(dbase);
+    tab.z = reinterpret_cast<const uint64_t *>(dbase + nt * 16);
+    tab.flip = reinterpret_cast<const uint64_t *>(dbase + nt * 24);
+    tab.end = reinterpret_cast<const uint32_t *>(dbase + nt * 24 + ng * 8);
+    tab.nterms = uint32_t(nt);
+    tab.ngroups = uint32_t(ng);
+    tab.bytes = tab_bytes;
 
     const size_t dim = size_t(1) << n;
     const size_t chunk = 65535;  // grid.y limit
@@ -440,8 +443,7 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         const unsigned bx_cap = adjoint_max_blocks();
         double *partials = ctx_partials(ctx, rows * size_t(bx_cap));
         const unsigned bx = launch_pauli(psi + b0 * dim, out ? out + b0 * dim : nullptr, rows, n,
-                                         dw, dz, dflip, dfirst, dcount, uint32_t(ng), tr,
-                                         partials, accumulate, s);
+                                         tab, tr, partials, accumulate, s);
         double *sums = ctx_dgrads(ctx, rows);
         launch_reduce_rows(partials, uint32_t(rows), bx, sums, s);
         double *h = ctx_hvals(ctx, rows);

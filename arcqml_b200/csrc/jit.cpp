@@ -60,6 +60,7 @@ struct Driver {
     CUresult (*load)(CUmodule *, const void *) = nullptr;
     CUresult (*get)(CUfunction *, CUmodule, const char *) = nullptr;
     CUresult (*set_attr)(CUfunction, CUfunction_attribute, int) = nullptr;
+    CUresult (*get_attr)(int *, CUfunction_attribute, CUfunction) = nullptr;
     CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
                        unsigned, CUstream, void **, void **) = nullptr;
 };
@@ -110,6 +111,7 @@ bool load_driver() {
     g_drv.tried = true;
     g_drv.ok = entry("cuModuleLoadData", g_drv.load) && entry("cuModuleGetFunction", g_drv.get) &&
                entry("cuFuncSetAttribute", g_drv.set_attr) &&
+               entry("cuFuncGetAttribute", g_drv.get_attr) &&
                entry("cuLaunchKernel", g_drv.launch);
     if (!g_drv.ok) g_drv.why = "driver entry points unavailable";
     return g_drv.ok;
@@ -289,6 +291,7 @@ Compiled compile(const std::string &src) {
     return out;
 }
 
+// Per device: source -> kernel (nullptr: the source failed to compile or load; not retried).
 std::unordered_map<int, std::unordered_map<std::string, CUfunction>> g_cache;
 std::atomic<uint64_t> g_compiled{0}, g_jit_launches{0}, g_fallbacks{0};
 std::string g_last_error;
@@ -320,8 +323,10 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
     for (size_t i = 0; i < srcs.size(); ++i) {
         if (srcs[i].empty()) continue;
         auto it = cache.find(srcs[i]);
-        if (it != cache.end()) fns[i] = it->second;
-        else {
+        if (it != cache.end()) {
+            fns[i] = it->second;
+            if (!fns[i]) ++g_fallbacks;
+        } else {
             bool dup = false;
             for (size_t j : todo) dup = dup || srcs[j] == srcs[i];
             if (!dup) todo.push_back(i);
@@ -347,6 +352,7 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
         check_cuda(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
                    "cudaDeviceGetAttribute");
         for (size_t j = 0; j < todo.size(); ++j) {
+            cache[srcs[todo[j]]] = nullptr;
             if (!out[j].error.empty()) {
                 g_last_error = out[j].error;
                 ++g_fallbacks;
@@ -354,11 +360,27 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
             }
             CUmodule mod = nullptr;
             CUfunction fn = nullptr;
-            if (g_drv.load(&mod, out[j].cubin.data()) != CUDA_SUCCESS ||
-                g_drv.get(&fn, mod, "arcqml_pass") != CUDA_SUCCESS ||
-                g_drv.set_attr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, optin) !=
-                    CUDA_SUCCESS) {
-                g_last_error = "loading a compiled pass kernel failed";
+            int static_smem = 0;
+            CUresult r = g_drv.load(&mod, out[j].cubin.data());
+            const char *what = "cuModuleLoadData";
+            if (r == CUDA_SUCCESS) {
+                r = g_drv.get(&fn, mod, "arcqml_pass");
+                what = "cuModuleGetFunction";
+            }
+            if (r == CUDA_SUCCESS) {
+                r = g_drv.get_attr(&static_smem, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, fn);
+                what = "cuFuncGetAttribute";
+            }
+            if (r == CUDA_SUCCESS) {
+                // dynamic shared memory may use what the static part leaves of the opt-in limit
+                r = g_drv.set_attr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                   optin - static_smem);
+                what = "cuFuncSetAttribute";
+            }
+            if (r != CUDA_SUCCESS) {
+                std::ostringstream m;
+                m << "loading a compiled pass kernel failed: " << what << " returned " << int(r);
+                g_last_error = m.str();
                 ++g_fallbacks;
                 continue;
             }

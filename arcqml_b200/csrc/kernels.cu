@@ -314,12 +314,16 @@ __global__ void __launch_bounds__(kThreads) k_norms(const double2 *__restrict__ 
 // ---------------------------------------------------------------- Pauli observable
 
 struct PauliArgs {
-    const double2 *w;      // per term: coefficient * i^(y mod 4)
-    const uint64_t *z;     // per term: phase mask
-    const uint64_t *flip;  // per group: flip mask
-    const uint32_t *first; // per group: first term
-    const uint32_t *count; // per group: number of terms
-    uint32_t ngroups;
+    // Term and group tables, contiguous in this order (staged in shared memory when
+    // table_bytes > 0): per term w'_k (double2: coefficient * i^(y mod 4) * (-1)^popc(f & z_k),
+    // the sign folding the group's flip into the phase) and z_k (phase mask), per group its flip
+    // mask f and, with one extra entry, the index of its first term (group g's terms are
+    // [end[g], end[g+1])).
+    const double2 *w;
+    const uint64_t *z;
+    const uint64_t *flip;
+    const uint32_t *end;
+    uint32_t nterms, ngroups, table_bytes;
     // Traversal order (perm == nullptr: index order). The loop counter's low 6 bits are index
     // bits 0-5; its next (coset_bits - 6) bits are spread over the other qubits of the coset set
     // by tables 0..nb-1, the remaining bits over the complement by tables nb..ntables-1 (256
@@ -328,25 +332,55 @@ struct PauliArgs {
     uint32_t coset_bits, nb, ntables;
 };
 constexpr uint32_t kMaxPermTables = 8;
+constexpr uint32_t kPauliSmemTables = 30 * 1024;  // larger tables are read from global memory
+
+constexpr int kPauliBatch = 4;
+
+// sum over group g's terms of w'_k (-1)^popc(t & z_k)  (= sum w_k (-1)^popc((t ^ f) & z_k))
+__device__ __forceinline__ double2 group_weight(const double2 *W, const uint64_t *Z,
+                                                const uint32_t *E, uint32_t g, uint64_t t) {
+    const uint32_t k0 = E[g], k1 = E[g + 1];
+    double2 w = make_double2(0.0, 0.0);
+    for (uint32_t k = k0; k < k1; ++k) {
+        const double2 wk = W[k];
+        const bool neg = __popcll(t & Z[k]) & 1;
+        w.x += neg ? -wk.x : wk.x;
+        w.y += neg ? -wk.y : wk.y;
+    }
+    return w;
+}
 
 // out[t] = sum_groups sum_terms w_k (-1)^popc((t^f) & z_k) psi[t^f]   (= (H psi)[t])
 // partials[row, block] = sum_t Re(conj(psi[t]) out[t]).
 //
-// Every flip group reads psi once more (psi[t ^ f]). The amplitudes are visited coset by coset
-// of a qubit set B chosen on the host (the qubits most flips act on, plus 0-5 for coalescing,
-// 2^21 amplitudes = 32 MB per coset): a group whose flips all lie in B reads inside the coset
-// being visited, which stays in L2, so HBM serves such groups once per coset instead of once per
-// group.
+// Every flip group reads psi once more (psi[t ^ f]); groups go in batches of kPauliBatch whose
+// gathers are all issued before any is consumed (accumulation stays in group order). The
+// amplitudes are visited coset by coset of a qubit set B chosen on the host (the qubits most
+// flips act on, plus 0-5 for coalescing, 2^21 amplitudes = 32 MB per coset): a group whose flips
+// all lie in B reads inside the coset being visited, which stays in L2.
 __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ psi,
                                                     double2 *__restrict__ out, uint64_t dim,
                                                     const __grid_constant__ PauliArgs P,
                                                     double *__restrict__ partials, int accumulate) {
     __shared__ double s_red[kThreads / 32];
     __shared__ uint64_t s_perm[kMaxPermTables * 256];
-    if (P.perm) {
+    extern __shared__ __align__(16) unsigned char s_tab[];
+    if (P.perm)
         for (uint32_t i = threadIdx.x; i < P.ntables * 256; i += blockDim.x) s_perm[i] = P.perm[i];
-        __syncthreads();
+    const double2 *W = P.w;
+    const uint64_t *Z = P.z, *F = P.flip;
+    const uint32_t *E = P.end;
+    if (P.table_bytes) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(P.w);
+        uint4 *dst = reinterpret_cast<uint4 *>(s_tab);
+        for (uint32_t i = threadIdx.x; i < P.table_bytes / 16; i += blockDim.x) dst[i] = src[i];
+        const unsigned char *g = reinterpret_cast<const unsigned char *>(P.w);
+        W = reinterpret_cast<const double2 *>(s_tab);
+        Z = reinterpret_cast<const uint64_t *>(s_tab + (reinterpret_cast<const unsigned char *>(P.z) - g));
+        F = reinterpret_cast<const uint64_t *>(s_tab + (reinterpret_cast<const unsigned char *>(P.flip) - g));
+        E = reinterpret_cast<const uint32_t *>(s_tab + (reinterpret_cast<const unsigned char *>(P.end) - g));
     }
+    __syncthreads();
     const size_t roff = size_t(blockIdx.y) * dim;
     const double2 *r = psi + roff;
     double ev = 0.0;
@@ -361,19 +395,20 @@ __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ 
         }
         const double2 pt = r[t];
         double2 acc = make_double2(0.0, 0.0);
-        for (uint32_t gi = 0; gi < P.ngroups; ++gi) {
-            const uint64_t f = __ldg(&P.flip[gi]);
-            const uint64_t s = t ^ f;
-            const uint32_t k0 = __ldg(&P.first[gi]), k1 = k0 + __ldg(&P.count[gi]);
-            double2 w = make_double2(0.0, 0.0);
-            for (uint32_t k = k0; k < k1; ++k) {
-                const double2 wk = __ldg(&P.w[k]);
-                const bool neg = __popcll(s & __ldg(&P.z[k])) & 1;
-                w.x += neg ? -wk.x : wk.x;
-                w.y += neg ? -wk.y : wk.y;
+        uint32_t gi = 0;
+        for (; gi + kPauliBatch <= P.ngroups; gi += kPauliBatch) {
+            double2 ps[kPauliBatch];
+#pragma unroll
+            for (int j = 0; j < kPauliBatch; ++j) {
+                const uint64_t f = F[gi + j];
+                ps[j] = f ? r[t ^ f] : pt;
             }
-            const double2 ps = f ? r[s] : pt;
-            acc = cfma(w, ps, acc);
+#pragma unroll
+            for (int j = 0; j < kPauliBatch; ++j) acc = cfma(group_weight(W, Z, E, gi + j, t), ps[j], acc);
+        }
+        for (; gi < P.ngroups; ++gi) {
+            const uint64_t f = F[gi];
+            acc = cfma(group_weight(W, Z, E, gi, t), f ? r[t ^ f] : pt, acc);
         }
         if (out) {
             if (accumulate) {
@@ -525,21 +560,21 @@ unsigned launch_norms(const double2 *amps, size_t batch, uint32_t n, double *par
 }
 
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
-                      const double2 *w, const uint64_t *z, const uint64_t *flip,
-                      const uint32_t *first, const uint32_t *count, uint32_t ngroups,
-                      const PauliTraversal &tr, double *partials, bool accumulate,
-                      cudaStream_t s) {
+                      const PauliTables &tab, const PauliTraversal &tr, double *partials,
+                      bool accumulate, cudaStream_t s) {
     if (tr.tables && (tr.ntables > kMaxPermTables || tr.coset_bits < 6 || tr.coset_bits > n))
         fail("internal: observable traversal tables out of range");
-    PauliArgs P{w, z, flip, first, count, ngroups, tr.tables, tr.coset_bits, tr.nb, tr.ntables};
+    const uint32_t bytes = tab.bytes <= kPauliSmemTables ? uint32_t(tab.bytes) : 0u;
+    PauliArgs P{tab.w,   tab.z,         tab.flip, tab.end,       tab.nterms, tab.ngroups,
+                bytes,   tr.tables,     tr.coset_bits, tr.nb,    tr.ntables};
     const uint64_t dim = uint64_t(1) << n;
     unsigned bx = grid_for(dim);
     const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);
     if (bx > cap) bx = cap < 1 ? 1 : cap;
     // algorithmic traffic: read psi once, write H psi once (when requested)
     const ProfToken tok = prof_begin(PROF_PAULI, s);
-    k_pauli<<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(psi, out, dim, P, partials,
-                                                           accumulate ? 1 : 0);
+    k_pauli<<<dim3(bx, unsigned(batch)), kThreads, bytes, s>>>(psi, out, dim, P, partials,
+                                                               accumulate ? 1 : 0);
     prof_end(tok, s, (out ? (accumulate ? 48.0 : 32.0) : 16.0) * double(dim) * double(batch));
     check_cuda(cudaGetLastError(), "observable kernel launch");
     return bx;

@@ -27,11 +27,19 @@ struct PauliTraversal {
 // fills `tables` (host, ntables x 256) and the counts, or leaves it empty for index order.
 void pauli_traversal_tables(uint32_t n, const std::vector<uint64_t> &flips,
                             std::vector<uint64_t> &tables, PauliTraversal &tr);
+// Device tables of an observable, contiguous from w (16-byte aligned, `bytes` long): per term
+// w'_k = coefficient * i^(y mod 4) * (-1)^popc(f_g & z_k) and z_k, per group its flip mask and
+// the first-term index, plus one final end index.
+struct PauliTables {
+    const double2 *w = nullptr;
+    const uint64_t *z = nullptr, *flip = nullptr;
+    const uint32_t *end = nullptr;
+    uint32_t nterms = 0, ngroups = 0;
+    size_t bytes = 0;
+};
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
-                      const double2 *w, const uint64_t *z, const uint64_t *flip,
-                      const uint32_t *first, const uint32_t *count, uint32_t ngroups,
-                      const PauliTraversal &tr, double *partials, bool accumulate,
-                      cudaStream_t s);
+                      const PauliTables &tab, const PauliTraversal &tr, double *partials,
+                      bool accumulate, cudaStream_t s);
 
 // Moves the slices of a shard with slice value y != skip (bit i of y at positions[i]) between
 // the shard and staging blocks [block][chunk_len], for other-index o in [chunk_begin, +chunk_len).
