@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--forward-only", action="store_true",
+                    help="forward + <H> without the adjoint sweep (the 35-qubit sharded config)")
     return ap.parse_args()
 
 
@@ -69,7 +71,8 @@ def workload(n, layers, terms, seed):
 
 
 def config(args, c):
-    return {"workload": f"{args.qubits}q brickwork x{args.layers} fwd + adjoint, "
+    what = "fwd + <H>" if args.forward_only else "fwd + adjoint"
+    return {"workload": f"{args.qubits}q brickwork x{args.layers} {what}, "
                         f"{args.terms}-term Pauli sum",
             "qubits": args.qubits, "layers": args.layers, "pauli_terms": args.terms,
             "gates": len(c.operations), "parameters": c.num_parameters(),
@@ -186,7 +189,9 @@ def gpu_arm(args):
         sim = StateVectorSimulator(n)
 
         def step(initial=None):
-            res = sim.run(c, obs, initial_state=initial)
+            res = sim.run(c, obs, grad=not args.forward_only, initial_state=initial)
+            if args.forward_only:
+                return res.value, np.zeros(0)
             pgrads, _ = res.backward(1.0)
             return res.value, pgrads
     else:
@@ -194,8 +199,8 @@ def gpu_arm(args):
         sim = ShardedStateVectorSimulator(n)
 
         def step(initial=None):
-            value = sim.run(c, obs, initial_shard=initial)
-            return value, sim.backward(1.0)
+            value = sim.run(c, obs, grad=not args.forward_only, initial_shard=initial)
+            return value, (np.zeros(0) if args.forward_only else sim.backward(1.0))
 
     for _ in range(args.warmup):
         step()
@@ -235,7 +240,7 @@ def gpu_arm(args):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    passes = 2 * gates
+    passes = (1 if args.forward_only else 2) * gates
     value_rate = passes * args.steps / (ms / 1e3)
     swaps = None
     if world > 1:
@@ -270,7 +275,8 @@ def gpu_arm(args):
                                   if traffic else None}
     # The rate per-gate kernels would reach at the HBM roofline: every gate one pass over the
     # state (32 B per amplitude forward, 64 B adjoint), all GPUs streaming their shards.
-    unfused = 2 * gates * world * peak * 1e9 / (gates * 96.0 * 2.0 ** n)
+    step_bytes = gates * (32.0 if args.forward_only else 96.0) * 2.0 ** n
+    unfused = passes * world * peak * 1e9 / step_bytes
 
     e2e = None
     if not args.no_e2e:
