@@ -257,7 +257,8 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
         const uint32_t k = fused_k(n, true);
         const uint32_t rb = fused_rb(k, true);
         Schedule sch = build_schedule(plan, n, true, req, true, k, rb);
-        const uint32_t stride = fused_grid_blocks(true, k, rb);
+        // room for two resident CTAs per SM (run-time compiled adjoint kernels may have them)
+        const uint32_t stride = 2 * fused_grid_blocks(true, k, rb);
         double *partials = nullptr;
         if (sch.total_acc) {
             partials = ctx_partials(ctx, size_t(sch.total_acc) * stride);
@@ -391,50 +392,76 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
     }
     const size_t nt = obs.coef.size();
     const size_t ng = obs.groups.size();
-    // Pack tables in one upload: w' (double2 per term), z (u64 per term), flip (u64 per group),
-    // term ranges (u32 per group + 1), then the traversal tables (16-byte aligned).
+    // Pack the tables in one upload (layout in PauliTables), then the traversal tables.
     std::vector<uint64_t> gflips(ng), ptab;
     for (size_t g = 0; g < ng; ++g) gflips[g] = obs.groups[g].flip;
     PauliTraversal tr;
     pauli_traversal_tables(n, gflips, ptab, tr);
-    const size_t tab_bytes = (nt * 24 + ng * 8 + (ng + 1) * 4 + 15) & ~size_t(15);
-    std::vector<double2> pack((tab_bytes + ptab.size() * 8 + 15) / 16 + 1);
-    char *base = reinterpret_cast<char *>(pack.data());
-    double2 *w = reinterpret_cast<double2 *>(base);
-    uint64_t *z = reinterpret_cast<uint64_t *>(base + nt * 16);
-    uint64_t *flip = reinterpret_cast<uint64_t *>(base + nt * 24);
-    uint32_t *ends = reinterpret_cast<uint32_t *>(base + nt * 24 + ng * 8);
+    auto weight = [&](const PauliGroup &grp, uint32_t k) {
+        // (-1)^popc((t ^ f) & z) = (-1)^popc(f & z) (-1)^popc(t & z): fold the first factor
+        const double c = (__builtin_popcountll(grp.flip & obs.zmask[k]) & 1) ? -obs.coef[k]
+                                                                             : obs.coef[k];
+        switch (obs.ymod4[k] & 3u) {
+        case 0: return make_double2(c, 0.0);
+        case 1: return make_double2(0.0, c);
+        case 2: return make_double2(-c, 0.0);
+        default: return make_double2(0.0, -c);
+        }
+    };
+    std::vector<double2> sw, mw;
+    std::vector<uint64_t> sf, sz, mz, mf;
+    std::vector<uint32_t> me;
     for (size_t g = 0; g < ng; ++g) {
         const auto &grp = obs.groups[g];
-        flip[g] = grp.flip;
-        ends[g] = grp.first;
-        for (uint32_t k = grp.first; k < grp.first + grp.count; ++k) {
-            // (-1)^popc((t ^ f) & z) = (-1)^popc(f & z) (-1)^popc(t & z): fold the first factor
-            const double c = (__builtin_popcountll(grp.flip & obs.zmask[k]) & 1) ? -obs.coef[k]
-                                                                                 : obs.coef[k];
-            switch (obs.ymod4[k] & 3u) {
-            case 0: w[k] = make_double2(c, 0.0); break;
-            case 1: w[k] = make_double2(0.0, c); break;
-            case 2: w[k] = make_double2(-c, 0.0); break;
-            default: w[k] = make_double2(0.0, -c); break;
+        if (grp.count == 1) {
+            sw.push_back(weight(grp, grp.first));
+            sf.push_back(grp.flip);
+            sz.push_back(obs.zmask[grp.first]);
+        } else {
+            mf.push_back(grp.flip);
+            me.push_back(uint32_t(mw.size()));
+            for (uint32_t k = grp.first; k < grp.first + grp.count; ++k) {
+                mw.push_back(weight(grp, k));
+                mz.push_back(obs.zmask[k]);
             }
-            z[k] = obs.zmask[k];
         }
     }
-    ends[ng] = uint32_t(nt);
-    if (!ptab.empty()) std::memcpy(base + tab_bytes, ptab.data(), ptab.size() * 8);
+    me.push_back(uint32_t(mw.size()));
+    PauliTables tab;
+    size_t off = 0;
+    auto place = [&](size_t bytes) {
+        const size_t at = off;
+        off = (off + bytes + 15) & ~size_t(15);
+        return uint32_t(at);
+    };
+    tab.s_w = place(sw.size() * 16);
+    tab.s_f = place(sf.size() * 8);
+    tab.s_z = place(sz.size() * 8);
+    tab.m_w = place(mw.size() * 16);
+    tab.m_z = place(mz.size() * 8);
+    tab.m_f = place(mf.size() * 8);
+    tab.m_e = place(me.size() * 4);
+    tab.bytes = off;
+    tab.ns = uint32_t(sw.size());
+    tab.nm = uint32_t(mf.size());
+    std::vector<double2> pack((off + ptab.size() * 8 + 15) / 16 + 1);
+    char *base = reinterpret_cast<char *>(pack.data());
+    auto put = [&](uint32_t at, const void *src, size_t bytes) {
+        if (bytes) std::memcpy(base + at, src, bytes);
+    };
+    put(tab.s_w, sw.data(), sw.size() * 16);
+    put(tab.s_f, sf.data(), sf.size() * 8);
+    put(tab.s_z, sz.data(), sz.size() * 8);
+    put(tab.m_w, mw.data(), mw.size() * 16);
+    put(tab.m_z, mz.data(), mz.size() * 8);
+    put(tab.m_f, mf.data(), mf.size() * 8);
+    put(tab.m_e, me.data(), me.size() * 4);
+    if (!ptab.empty()) std::memcpy(base + off, ptab.data(), ptab.size() * 8);
     std::vector<const std::vector<double2> *> refs{&pack};
     auto p = upload_tables(refs, ctx, s);
     const char *dbase = reinterpret_cast<const char *>(p[0]);
-    if (!ptab.empty()) tr.tables = reinterpret_cast<const uint64_t *>(dbase + tab_bytes);
-    PauliTables tab;
-    tab.w = reinterpret_cast<const double2 *>(dbase);
-    tab.z = reinterpret_cast<const uint64_t *>(dbase + nt * 16);
-    tab.flip = reinterpret_cast<const uint64_t *>(dbase + nt * 24);
-    tab.end = reinterpret_cast<const uint32_t *>(dbase + nt * 24 + ng * 8);
-    tab.nterms = uint32_t(nt);
-    tab.ngroups = uint32_t(ng);
-    tab.bytes = tab_bytes;
+    if (!ptab.empty()) tr.tables = reinterpret_cast<const uint64_t *>(dbase + off);
+    tab.base = reinterpret_cast<const unsigned char *>(dbase);
 
     const size_t dim = size_t(1) << n;
     const size_t chunk = 65535;  // grid.y limit

@@ -739,6 +739,7 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
 // Applies sub-block sb by interpreting its op table: sub-blocks whose ops all have fast paths
 // run an inline loop with one dispatch per op, the others the out-of-line general routine.
 struct TableRunner {
+    static constexpr bool kAccPerWarp = false;
     template <int RB, bool ADJ>
     __device__ static __forceinline__ void run(const SubBlock &S, uint32_t sb, double2 *tp,
                                                double2 *tl, const FOp *ops, const double2 *mats,
@@ -777,8 +778,8 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
 }
 
 size_t fused_smem(bool adj, uint32_t k, uint32_t nacc, uint32_t nops, uint32_t nmat,
-                  uint32_t threads) {
-    return smem_layout(adj, k, nacc, nops, nmat, threads).total;
+                  uint32_t acc_cols) {
+    return smem_layout(adj, k, nacc, nops, nmat, acc_cols).total;
 }
 
 using FusedKernel = void (*)(double2 *, double2 *, uint32_t, uint32_t, uint64_t,
@@ -913,8 +914,15 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         const auto *sub = reinterpret_cast<const SubBlock *>(dev + offs[i].subs);
         const auto *ops = reinterpret_cast<const FOp *>(dev + offs[i].ops);
         const auto *mats = reinterpret_cast<const double2 *>(dev + offs[i].mats);
-        const uint32_t blocks = fused_grid_blocks(adj, k, st.header.rb);
-        if (adj && blocks > partial_stride) fail("internal: accumulator stride below the grid size");
+        const uint32_t threads = fused_threads(k, st.header.rb);
+        uint32_t blocks = fused_grid_blocks(adj, k, st.header.rb);
+        size_t launch_smem = smem;
+        if (jit[i]) {
+            const uint32_t cols = (adj && jit_adjoint_per_warp()) ? threads / 32u : threads;
+            launch_smem = fused_smem(adj, k, st.header.nacc, st.header.nops, st.header.nmat, cols);
+            blocks = jit_grid_blocks(jit[i], threads, launch_smem);
+        }
+        if (adj && blocks > partial_stride) blocks = partial_stride;
         const unsigned grid = unsigned(total_tiles < blocks ? total_tiles : blocks);
         // algorithmic traffic: psi (and lambda) read and written once per pass
         const double bytes = (adj ? 64.0 : 32.0) * double(uint64_t(batch) << n);
@@ -930,7 +938,7 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
             double *a_part = adj ? partials : nullptr;
             void *args[] = {&a_psi, &a_lam, &a_n, &a_tl, &a_tt, &a_h, &a_sub, &a_ops, &a_mats,
                             &a_part, &a_stride};
-            jit_launch(jit[i], grid, fused_threads(k, st.header.rb), smem, s, args);
+            jit_launch(jit[i], grid, threads, launch_smem, s, args);
         } else {
             fused_kernel(adj, st.header.rb)<<<grid, fused_threads(k, st.header.rb), smem, s>>>(
                 psi, adj ? lam : nullptr, n, tiles_log, total_tiles, hdr, sub, ops, mats,

@@ -34,6 +34,13 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 
+// Adds the warp's sum of z into its own column of accumulator row `row` (= acc * warps).
+__device__ __forceinline__ void accumulate_warp(double *sacc, uint32_t row, double z) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    if ((threadIdx.x & 31u) == 0) sacc[row + (threadIdx.x >> 5)] += z;
+}
+
 // Adds z into this thread's own column of accumulator row `row` (= acc * blockDim.x): no
 // cross-lane traffic per gate; the columns are summed once per pass at the end of the kernel.
 __device__ __forceinline__ void accumulate(double *sacc, uint32_t row, double z) {
@@ -210,8 +217,9 @@ struct SmemLayout {
     uint32_t tile, hioff, sacc, ops, mats, total;
 };
 
+// acc_cols: accumulator columns per row (one per thread, or one per warp).
 __host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t nacc,
-                                                  uint32_t nops, uint32_t nmat, uint32_t nthreads) {
+                                                  uint32_t nops, uint32_t nmat, uint32_t acc_cols) {
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     SmemLayout m;
     m.tile = 0;
@@ -220,7 +228,7 @@ __host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t
     off += 8u << (k - L);
     off = (off + 15u) & ~15u;
     m.sacc = off;
-    off += adj ? nacc * nthreads * 8u : 0u;
+    off += adj ? nacc * acc_cols * 8u : 0u;
     off = (off + 15u) & ~15u;
     m.ops = off;
     off += nops * uint32_t(sizeof(FOp));
@@ -288,7 +296,8 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     const uint32_t D = 1u << k;
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     const uint32_t lowmask = (1u << L) - 1;
-    const uint32_t nthreads = blockDim.x;
+    // accumulator row stride: one column per thread, or per warp (Runner::kAccPerWarp)
+    const uint32_t nthreads = Runner::kAccPerWarp ? blockDim.x / 32u : blockDim.x;
     const SmemLayout lay = smem_layout(ADJ, k, snacc, snops, snmat, nthreads);
     double2 *bufs = reinterpret_cast<double2 *>(smem + lay.tile);
     uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + lay.hioff);
@@ -410,12 +419,14 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         for (uint32_t a = threadIdx.x; a < snacc; a += blockDim.x) {
             const double *row = sacc + size_t(a) * nthreads;
             double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-            for (uint32_t t = 0; t < nthreads; t += 4) {
+            uint32_t t = 0;
+            for (; t + 4 <= nthreads; t += 4) {
                 s0 += row[t];
                 s1 += row[t + 1];
                 s2 += row[t + 2];
                 s3 += row[t + 3];
             }
+            for (; t < nthreads; ++t) s0 += row[t];
             partials[size_t(sacc_base + a) * stride + blockIdx.x] = (s0 + s1) + (s2 + s3);
         }
     }

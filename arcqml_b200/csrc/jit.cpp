@@ -61,6 +61,7 @@ struct Driver {
     CUresult (*get)(CUfunction *, CUmodule, const char *) = nullptr;
     CUresult (*set_attr)(CUfunction, CUfunction_attribute, int) = nullptr;
     CUresult (*get_attr)(int *, CUfunction_attribute, CUfunction) = nullptr;
+    CUresult (*occupancy)(int *, CUfunction, int, size_t) = nullptr;
     CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
                        unsigned, CUstream, void **, void **) = nullptr;
 };
@@ -112,12 +113,23 @@ bool load_driver() {
     g_drv.ok = entry("cuModuleLoadData", g_drv.load) && entry("cuModuleGetFunction", g_drv.get) &&
                entry("cuFuncSetAttribute", g_drv.set_attr) &&
                entry("cuFuncGetAttribute", g_drv.get_attr) &&
+               entry("cuOccupancyMaxActiveBlocksPerMultiprocessor", g_drv.occupancy) &&
                entry("cuLaunchKernel", g_drv.launch);
     if (!g_drv.ok) g_drv.why = "driver entry points unavailable";
     return g_drv.ok;
 }
 
 // ---------------------------------------------------------------- code generation
+
+// ARCQML_JIT_ADJ_WARP=1: adjoint kernels reduce each gradient over the warp (one accumulator
+// column per warp instead of per thread) and ask for two resident CTAs per SM.
+bool adjoint_per_warp() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_JIT_ADJ_WARP");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
 
 // Per-thread value of the op's qubit `slot` when it is not a register bit (fast paths D1_UNI and
 // the sign flips): a tile bit of the thread's base index, or a bit of the tile's global base.
@@ -186,7 +198,8 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb) {
     if (!emit_apply(c, o, "v", rb)) return false;
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb)) return false;
-    c << "\n        accumulate(sacc, " << o.acc[0] << "u * nthreads, 0.5 * z); }";
+    c << "\n        " << (adjoint_per_warp() ? "accumulate_warp" : "accumulate") << "(sacc, "
+      << o.acc[0] << "u * nthreads, 0.5 * z); }";
     return true;
 }
 
@@ -194,6 +207,8 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb) {
 std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     std::ostringstream c;
     c << "struct PassOps {\n"
+         "    static constexpr bool kAccPerWarp = " << (adj && adjoint_per_warp() ? "true" : "false")
+      << ";\n"
          "    template <int RB, bool ADJ>\n"
          "    __device__ static __forceinline__ void run(const SubBlock &S, uint32_t sb, double2 *tp,\n"
          "            double2 *tl, const FOp *, const double2 *M, const SubBlock *, double *sacc,\n"
@@ -218,7 +233,8 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "    }\n"
          "};\n";
     const int threads = (adj || rb == 4) ? 256 : 512;
-    c << "extern \"C\" __global__ void __launch_bounds__(" << threads << ")\n"
+    const int min_blocks = (adj && adjoint_per_warp()) ? 2 : 1;
+    c << "extern \"C\" __global__ void __launch_bounds__(" << threads << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"
          "            const SubBlock *__restrict__ subs, const FOp *__restrict__ gops,\n"
@@ -394,6 +410,19 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
             }
     }
     return fns;
+}
+
+bool jit_adjoint_per_warp() { return adjoint_per_warp(); }
+
+uint32_t jit_grid_blocks(void *fn, uint32_t threads, size_t smem) {
+    int per_sm = 0, dev = 0, sms = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
+               "cudaDeviceGetAttribute");
+    if (g_drv.occupancy(&per_sm, static_cast<CUfunction>(fn), int(threads), smem) != CUDA_SUCCESS ||
+        per_sm < 1)
+        per_sm = 1;
+    return uint32_t(sms * per_sm);
 }
 
 void jit_launch(void *fn, unsigned grid, unsigned threads, size_t smem, cudaStream_t s,

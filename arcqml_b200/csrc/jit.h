@@ -17,6 +17,10 @@ bool jit_enabled();
 // (a dense barrier, an op without a fast path, or a failed compile) and the precompiled pass
 // kernel runs instead. Kernels are compiled once per circuit structure and device.
 std::vector<void *> jit_kernels(const Schedule &sch, bool adjoint);
+// True when adjoint kernels reduce gradients per warp (ARCQML_JIT_ADJ_WARP=1).
+bool jit_adjoint_per_warp();
+// Persistent grid of a compiled kernel: resident CTAs per SM x SMs for this launch shape.
+uint32_t jit_grid_blocks(void *fn, uint32_t threads, size_t smem);
 // Launches a compiled pass kernel with the precompiled kernel's argument list.
 void jit_launch(void *fn, unsigned grid, unsigned threads, size_t smem, cudaStream_t s,
                 void **args);

@@ -314,16 +314,16 @@ __global__ void __launch_bounds__(kThreads) k_norms(const double2 *__restrict__ 
 // ---------------------------------------------------------------- Pauli observable
 
 struct PauliArgs {
-    // Term and group tables, contiguous in this order (staged in shared memory when
-    // table_bytes > 0): per term w'_k (double2: coefficient * i^(y mod 4) * (-1)^popc(f & z_k),
-    // the sign folding the group's flip into the phase) and z_k (phase mask), per group its flip
-    // mask f and, with one extra entry, the index of its first term (group g's terms are
-    // [end[g], end[g+1])).
-    const double2 *w;
-    const uint64_t *z;
-    const uint64_t *flip;
-    const uint32_t *end;
-    uint32_t nterms, ngroups, table_bytes;
+    // Observable tables, one contiguous block (copied to shared memory when table_bytes > 0),
+    // offsets in bytes from its start. Weights fold the group's flip into the phase:
+    // w'_k = coefficient * i^(y mod 4) * (-1)^popc(f & z_k), so term k contributes
+    // w'_k (-1)^popc(t & z_k) psi[t ^ f] to (H psi)[t].
+    //   groups with one term ("singles", ns of them): w' (double2), f (u64), z (u64) arrays;
+    //   the other groups (nm of them, ntm terms): w' and z per term, f per group, and the first
+    //   term of each group plus one final end index.
+    const unsigned char *tables;
+    uint32_t s_w, s_f, s_z, m_w, m_z, m_f, m_e;
+    uint32_t ns, nm, table_bytes;
     // Traversal order (perm == nullptr: index order). The loop counter's low 6 bits are index
     // bits 0-5; its next (coset_bits - 6) bits are spread over the other qubits of the coset set
     // by tables 0..nb-1, the remaining bits over the complement by tables nb..ntables-1 (256
@@ -333,31 +333,22 @@ struct PauliArgs {
 };
 constexpr uint32_t kMaxPermTables = 8;
 constexpr uint32_t kPauliSmemTables = 30 * 1024;  // larger tables are read from global memory
-
 constexpr int kPauliBatch = 4;
 
-// sum over group g's terms of w'_k (-1)^popc(t & z_k)  (= sum w_k (-1)^popc((t ^ f) & z_k))
-__device__ __forceinline__ double2 group_weight(const double2 *W, const uint64_t *Z,
-                                                const uint32_t *E, uint32_t g, uint64_t t) {
-    const uint32_t k0 = E[g], k1 = E[g + 1];
-    double2 w = make_double2(0.0, 0.0);
-    for (uint32_t k = k0; k < k1; ++k) {
-        const double2 wk = W[k];
-        const bool neg = __popcll(t & Z[k]) & 1;
-        w.x += neg ? -wk.x : wk.x;
-        w.y += neg ? -wk.y : wk.y;
-    }
-    return w;
+__device__ __forceinline__ double flip_sign(double x, uint32_t m) {
+    return __hiloint2double(__double2hiint(x) ^ int(m), __double2loint(x));
 }
 
 // out[t] = sum_groups sum_terms w_k (-1)^popc((t^f) & z_k) psi[t^f]   (= (H psi)[t])
 // partials[row, block] = sum_t Re(conj(psi[t]) out[t]).
 //
 // Every flip group reads psi once more (psi[t ^ f]); groups go in batches of kPauliBatch whose
-// gathers are all issued before any is consumed (accumulation stays in group order). The
-// amplitudes are visited coset by coset of a qubit set B chosen on the host (the qubits most
-// flips act on, plus 0-5 for coalescing, 2^21 amplitudes = 32 MB per coset): a group whose flips
-// all lie in B reads inside the coset being visited, which stays in L2.
+// gathers are all issued before any is consumed. Single-term groups (most of a random Pauli sum)
+// take a branch-free path: the term's sign is an XOR on the weight's sign bits. The amplitudes
+// are visited coset by coset of a qubit set B chosen on the host (the qubits most flips act on,
+// plus 0-5 for coalescing, 2^21 amplitudes = 32 MB per coset): a group whose flips all lie in B
+// reads inside the coset being visited, which stays in L2.
+template <bool SMEM>
 __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ psi,
                                                     double2 *__restrict__ out, uint64_t dim,
                                                     const __grid_constant__ PauliArgs P,
@@ -367,20 +358,20 @@ __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ 
     extern __shared__ __align__(16) unsigned char s_tab[];
     if (P.perm)
         for (uint32_t i = threadIdx.x; i < P.ntables * 256; i += blockDim.x) s_perm[i] = P.perm[i];
-    const double2 *W = P.w;
-    const uint64_t *Z = P.z, *F = P.flip;
-    const uint32_t *E = P.end;
-    if (P.table_bytes) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(P.w);
+    if (SMEM) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(P.tables);
         uint4 *dst = reinterpret_cast<uint4 *>(s_tab);
         for (uint32_t i = threadIdx.x; i < P.table_bytes / 16; i += blockDim.x) dst[i] = src[i];
-        const unsigned char *g = reinterpret_cast<const unsigned char *>(P.w);
-        W = reinterpret_cast<const double2 *>(s_tab);
-        Z = reinterpret_cast<const uint64_t *>(s_tab + (reinterpret_cast<const unsigned char *>(P.z) - g));
-        F = reinterpret_cast<const uint64_t *>(s_tab + (reinterpret_cast<const unsigned char *>(P.flip) - g));
-        E = reinterpret_cast<const uint32_t *>(s_tab + (reinterpret_cast<const unsigned char *>(P.end) - g));
     }
     __syncthreads();
+    const unsigned char *tb = SMEM ? s_tab : P.tables;
+    const double2 *sW = reinterpret_cast<const double2 *>(tb + P.s_w);
+    const uint64_t *sF = reinterpret_cast<const uint64_t *>(tb + P.s_f);
+    const uint64_t *sZ = reinterpret_cast<const uint64_t *>(tb + P.s_z);
+    const double2 *mW = reinterpret_cast<const double2 *>(tb + P.m_w);
+    const uint64_t *mZ = reinterpret_cast<const uint64_t *>(tb + P.m_z);
+    const uint64_t *mF = reinterpret_cast<const uint64_t *>(tb + P.m_f);
+    const uint32_t *mE = reinterpret_cast<const uint32_t *>(tb + P.m_e);
     const size_t roff = size_t(blockIdx.y) * dim;
     const double2 *r = psi + roff;
     double ev = 0.0;
@@ -395,20 +386,34 @@ __global__ void __launch_bounds__(kThreads) k_pauli(const double2 *__restrict__ 
         }
         const double2 pt = r[t];
         double2 acc = make_double2(0.0, 0.0);
-        uint32_t gi = 0;
-        for (; gi + kPauliBatch <= P.ngroups; gi += kPauliBatch) {
+        uint32_t i = 0;
+        for (; i + kPauliBatch <= P.ns; i += kPauliBatch) {
             double2 ps[kPauliBatch];
 #pragma unroll
-            for (int j = 0; j < kPauliBatch; ++j) {
-                const uint64_t f = F[gi + j];
-                ps[j] = f ? r[t ^ f] : pt;
-            }
+            for (int j = 0; j < kPauliBatch; ++j) ps[j] = r[t ^ sF[i + j]];
 #pragma unroll
-            for (int j = 0; j < kPauliBatch; ++j) acc = cfma(group_weight(W, Z, E, gi + j, t), ps[j], acc);
+            for (int j = 0; j < kPauliBatch; ++j) {
+                const uint32_t neg = uint32_t(__popcll(t & sZ[i + j]) & 1) << 31;
+                const double2 w = sW[i + j];
+                acc = cfma(make_double2(flip_sign(w.x, neg), flip_sign(w.y, neg)), ps[j], acc);
+            }
         }
-        for (; gi < P.ngroups; ++gi) {
-            const uint64_t f = F[gi];
-            acc = cfma(group_weight(W, Z, E, gi, t), f ? r[t ^ f] : pt, acc);
+        for (; i < P.ns; ++i) {
+            const uint32_t neg = uint32_t(__popcll(t & sZ[i]) & 1) << 31;
+            const double2 w = sW[i];
+            acc = cfma(make_double2(flip_sign(w.x, neg), flip_sign(w.y, neg)), r[t ^ sF[i]], acc);
+        }
+        for (uint32_t g = 0; g < P.nm; ++g) {
+            const uint64_t f = mF[g];
+            const double2 ps = f ? r[t ^ f] : pt;
+            double2 w = make_double2(0.0, 0.0);
+            for (uint32_t k = mE[g]; k < mE[g + 1]; ++k) {
+                const uint32_t neg = uint32_t(__popcll(t & mZ[k]) & 1) << 31;
+                const double2 wk = mW[k];
+                w.x += flip_sign(wk.x, neg);
+                w.y += flip_sign(wk.y, neg);
+            }
+            acc = cfma(w, ps, acc);
         }
         if (out) {
             if (accumulate) {
@@ -564,17 +569,35 @@ unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n
                       bool accumulate, cudaStream_t s) {
     if (tr.tables && (tr.ntables > kMaxPermTables || tr.coset_bits < 6 || tr.coset_bits > n))
         fail("internal: observable traversal tables out of range");
-    const uint32_t bytes = tab.bytes <= kPauliSmemTables ? uint32_t(tab.bytes) : 0u;
-    PauliArgs P{tab.w,   tab.z,         tab.flip, tab.end,       tab.nterms, tab.ngroups,
-                bytes,   tr.tables,     tr.coset_bits, tr.nb,    tr.ntables};
+    const bool smem = tab.bytes <= kPauliSmemTables;
+    PauliArgs P{};
+    P.tables = tab.base;
+    P.s_w = tab.s_w;
+    P.s_f = tab.s_f;
+    P.s_z = tab.s_z;
+    P.m_w = tab.m_w;
+    P.m_z = tab.m_z;
+    P.m_f = tab.m_f;
+    P.m_e = tab.m_e;
+    P.ns = tab.ns;
+    P.nm = tab.nm;
+    P.table_bytes = smem ? uint32_t(tab.bytes) : 0u;
+    P.perm = tr.tables;
+    P.coset_bits = tr.coset_bits;
+    P.nb = tr.nb;
+    P.ntables = tr.ntables;
     const uint64_t dim = uint64_t(1) << n;
     unsigned bx = grid_for(dim);
     const unsigned cap = unsigned((uint64_t(num_sms()) * 8 + batch - 1) / batch);
     if (bx > cap) bx = cap < 1 ? 1 : cap;
     // algorithmic traffic: read psi once, write H psi once (when requested)
     const ProfToken tok = prof_begin(PROF_PAULI, s);
-    k_pauli<<<dim3(bx, unsigned(batch)), kThreads, bytes, s>>>(psi, out, dim, P, partials,
-                                                               accumulate ? 1 : 0);
+    if (smem)
+        k_pauli<true><<<dim3(bx, unsigned(batch)), kThreads, P.table_bytes, s>>>(
+            psi, out, dim, P, partials, accumulate ? 1 : 0);
+    else
+        k_pauli<false><<<dim3(bx, unsigned(batch)), kThreads, 0, s>>>(psi, out, dim, P, partials,
+                                                                     accumulate ? 1 : 0);
     prof_end(tok, s, (out ? (accumulate ? 48.0 : 32.0) : 16.0) * double(dim) * double(batch));
     check_cuda(cudaGetLastError(), "observable kernel launch");
     return bx;

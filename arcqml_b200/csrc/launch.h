@@ -27,14 +27,14 @@ struct PauliTraversal {
 // fills `tables` (host, ntables x 256) and the counts, or leaves it empty for index order.
 void pauli_traversal_tables(uint32_t n, const std::vector<uint64_t> &flips,
                             std::vector<uint64_t> &tables, PauliTraversal &tr);
-// Device tables of an observable, contiguous from w (16-byte aligned, `bytes` long): per term
-// w'_k = coefficient * i^(y mod 4) * (-1)^popc(f_g & z_k) and z_k, per group its flip mask and
-// the first-term index, plus one final end index.
+// Device tables of an observable in one block at `base` (`bytes` long, 16-byte aligned), byte
+// offsets of each array: single-term groups (s_*: weight, flip, phase mask per group) and the
+// other groups (m_*: weight and phase mask per term, flip per group, first term per group plus
+// an end index). Weights are coefficient * i^(y mod 4) * (-1)^popc(flip & phase).
 struct PauliTables {
-    const double2 *w = nullptr;
-    const uint64_t *z = nullptr, *flip = nullptr;
-    const uint32_t *end = nullptr;
-    uint32_t nterms = 0, ngroups = 0;
+    const unsigned char *base = nullptr;
+    uint32_t s_w = 0, s_f = 0, s_z = 0, m_w = 0, m_z = 0, m_f = 0, m_e = 0;
+    uint32_t ns = 0, nm = 0;
     size_t bytes = 0;
 };
 unsigned launch_pauli(const double2 *psi, double2 *out, size_t batch, uint32_t n,
