@@ -550,9 +550,10 @@ int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qu
             for (uint32_t b = 0; b < op.num_bindings; ++b)
                 parents = std::max(parents, op.parents[b] + 1);
         std::vector<uint8_t> req(parents, 1);
-        const uint32_t k = fused_k(n, adjoint != 0);
+        const bool wide = adjoint && adjoint_wide_tiles() && n >= 12;
+        const uint32_t k = wide ? 12u : fused_k(n, adjoint != 0);
         Schedule sch = build_schedule(*p, n, adjoint != 0, req.data(), adjoint != 0, k,
-                                      fused_rb(k, adjoint != 0));
+                                      wide ? 4u : fused_rb(k, adjoint != 0));
         size_t el = 0;
         std::string err;
         const size_t ok = jit_compile_check(sch, adjoint != 0, &el, &err);

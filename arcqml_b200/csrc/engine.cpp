@@ -12,6 +12,7 @@
 #include <sstream>
 #include <unordered_map>
 
+#include "jit.h"
 #include "launch.h"
 #include "planner.h"
 #include "rt_internal.h"
@@ -254,9 +255,19 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
     }
 
     if (fusion_enabled() && n >= kFusedMinQubits) {
-        const uint32_t k = fused_k(n, true);
-        const uint32_t rb = fused_rb(k, true);
-        Schedule sch = build_schedule(plan, n, true, req, true, k, rb);
+        uint32_t k = fused_k(n, true);
+        uint32_t rb = fused_rb(k, true);
+        Schedule sch;
+        bool wide = false;
+        if (adjoint_wide_tiles() && n >= 12) {
+            sch = build_schedule(plan, n, true, req, true, 12, 4);
+            wide = jit_schedule_compiles(sch, true);
+            if (wide) {
+                k = 12;
+                rb = 4;
+            }
+        }
+        if (!wide) sch = build_schedule(plan, n, true, req, true, k, rb);
         // room for two resident CTAs per SM (run-time compiled adjoint kernels may have them)
         const uint32_t stride = 2 * fused_grid_blocks(true, k, rb);
         double *partials = nullptr;

@@ -818,8 +818,10 @@ uint32_t fused_grid_blocks(bool adjoint, uint32_t k, uint32_t rb) {
     check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
                "cudaDeviceGetAttribute");
     // occupancy for the largest pass the planner emits (its tables are capped)
+    const uint32_t threads = fused_threads(k, rb);
+    const uint32_t cols = (adjoint && rb == 4) ? threads / 32u : threads;
     const size_t smem = fused_smem(adjoint, k, adjoint ? kMaxPassAcc : 0, kMaxPassOps, kMaxPassMats,
-                                   fused_threads(k, rb));
+                                   cols);
     if (smem > 227 * 1024) fail("internal: fused pass shared memory exceeds 227 KB");
     FusedKernel kern = fused_kernel(adjoint, rb);
     size_t allowed = 0;
@@ -918,10 +920,12 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         uint32_t blocks = fused_grid_blocks(adj, k, st.header.rb);
         size_t launch_smem = smem;
         if (jit[i]) {
-            const uint32_t cols = (adj && jit_adjoint_per_warp()) ? threads / 32u : threads;
+            const uint32_t cols = jit_acc_per_warp(adj, st.header.rb) ? threads / 32u : threads;
             launch_smem = fused_smem(adj, k, st.header.nacc, st.header.nops, st.header.nmat, cols);
             blocks = jit_grid_blocks(jit[i], threads, launch_smem);
         }
+        if (!jit[i] && adj && st.header.rb == 4)
+            fail("internal: adjoint pass with 4 register bits has no compiled kernel");
         if (adj && blocks > partial_stride) blocks = partial_stride;
         const unsigned grid = unsigned(total_tiles < blocks ? total_tiles : blocks);
         // algorithmic traffic: psi (and lambda) read and written once per pass

@@ -121,6 +121,11 @@ bool load_driver() {
 
 // ---------------------------------------------------------------- code generation
 
+bool adjoint_per_warp();
+// Adjoint kernels with 4 register bits (tiles of 12 qubits) keep one accumulator column per warp
+// so that psi, lambda and the accumulators fit one CTA's shared memory.
+bool acc_per_warp(bool adj, uint32_t rb) { return adj && (adjoint_per_warp() || rb == 4); }
+
 // ARCQML_JIT_ADJ_WARP=1: adjoint kernels reduce each gradient over the warp (one accumulator
 // column per warp instead of per thread) and ask for two resident CTAs per SM.
 bool adjoint_per_warp() {
@@ -198,7 +203,7 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb) {
     if (!emit_apply(c, o, "v", rb)) return false;
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb)) return false;
-    c << "\n        " << (adjoint_per_warp() ? "accumulate_warp" : "accumulate") << "(sacc, "
+    c << "\n        " << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
       << o.acc[0] << "u * nthreads, 0.5 * z); }";
     return true;
 }
@@ -207,7 +212,7 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb) {
 std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     std::ostringstream c;
     c << "struct PassOps {\n"
-         "    static constexpr bool kAccPerWarp = " << (adj && adjoint_per_warp() ? "true" : "false")
+         "    static constexpr bool kAccPerWarp = " << (acc_per_warp(adj, rb) ? "true" : "false")
       << ";\n"
          "    template <int RB, bool ADJ>\n"
          "    __device__ static __forceinline__ void run(const SubBlock &S, uint32_t sb, double2 *tp,\n"
@@ -233,7 +238,7 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "    }\n"
          "};\n";
     const int threads = (adj || rb == 4) ? 256 : 512;
-    const int min_blocks = (adj && adjoint_per_warp()) ? 2 : 1;
+    const int min_blocks = (adj && adjoint_per_warp() && rb == 3) ? 2 : 1;
     c << "extern \"C\" __global__ void __launch_bounds__(" << threads << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"
@@ -412,7 +417,22 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
     return fns;
 }
 
-bool jit_adjoint_per_warp() { return adjoint_per_warp(); }
+bool jit_acc_per_warp(bool adjoint, uint32_t rb) { return acc_per_warp(adjoint, rb); }
+
+bool jit_schedule_compiles(const Schedule &sch, bool adjoint) {
+    const std::vector<void *> fns = jit_kernels(sch, adjoint);
+    for (size_t i = 0; i < sch.steps.size(); ++i)
+        if (sch.steps[i].is_pass && !fns[i]) return false;
+    return true;
+}
+
+bool adjoint_wide_tiles() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_ADJ_WIDE");
+        return e && e[0] == '1';
+    }();
+    return on && jit_enabled();
+}
 
 uint32_t jit_grid_blocks(void *fn, uint32_t threads, size_t smem) {
     int per_sm = 0, dev = 0, sms = 0;

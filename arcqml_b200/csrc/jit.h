@@ -17,8 +17,13 @@ bool jit_enabled();
 // (a dense barrier, an op without a fast path, or a failed compile) and the precompiled pass
 // kernel runs instead. Kernels are compiled once per circuit structure and device.
 std::vector<void *> jit_kernels(const Schedule &sch, bool adjoint);
-// True when adjoint kernels reduce gradients per warp (ARCQML_JIT_ADJ_WARP=1).
-bool jit_adjoint_per_warp();
+// True when the compiled kernel of an (adjoint, rb) pass keeps one accumulator column per warp.
+bool jit_acc_per_warp(bool adjoint, uint32_t rb);
+// Compiles the schedule's passes; true if every pass has a compiled kernel.
+bool jit_schedule_compiles(const Schedule &sch, bool adjoint);
+// ARCQML_ADJ_WIDE=1 (with the run-time compiler on): adjoint sweeps use 12-qubit tiles with 4
+// register bits when every pass compiles.
+bool adjoint_wide_tiles();
 // Persistent grid of a compiled kernel: resident CTAs per SM x SMs for this launch shape.
 uint32_t jit_grid_blocks(void *fn, uint32_t threads, size_t smem);
 // Launches a compiled pass kernel with the precompiled kernel's argument list.
