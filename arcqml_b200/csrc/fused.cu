@@ -741,10 +741,12 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
 struct TableRunner {
     static constexpr bool kAccPerWarp = false;
     template <int RB, bool ADJ>
-    __device__ static __forceinline__ void run(const SubBlock &S, uint32_t sb, double2 *tp,
-                                               double2 *tl, const FOp *ops, const double2 *mats,
+    __device__ static __forceinline__ void run(uint32_t sb, uint32_t k, double2 *tp, double2 *tl,
+                                               const FOp *ops, const double2 *mats,
                                                const SubBlock *subs, double *sacc,
-                                               uint32_t nthreads, uint32_t tb, uint64_t gbase) {
+                                               uint32_t nthreads, uint64_t gbase) {
+        const SubBlock S = load_subblock(subs, sb);
+        const uint32_t tb = thread_base<RB>(S, k);
         if (!(S.flags & SB_ALL_FAST)) {
             general_subblock<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nthreads, tb, gbase);
             return;

@@ -269,8 +269,28 @@ __device__ __forceinline__ void store_regs(const SubBlock &S, uint32_t tb, doubl
     }
 }
 
-// One pass over all tiles; Runner::run<RB, ADJ>(...) applies sub-block sb of the pass to the
-// tile (it gathers the thread's registers, applies the gates and scatters them back).
+// Thread base index of sub-block S: thread bit i goes to tile bit S.perm[i].
+template <int RB>
+__device__ __forceinline__ uint32_t thread_base(const SubBlock &S, uint32_t k) {
+    uint32_t tb = 0;
+#pragma unroll
+    for (int i = 0; i < 12 - RB; ++i)
+        if (i < int(k) - RB && ((threadIdx.x >> i) & 1)) tb |= 1u << S.perm[i];
+    return tb;
+}
+
+// Sub-block sb of the pass table, read through the read-only cache.
+__device__ __forceinline__ SubBlock load_subblock(const SubBlock *subs, uint32_t sb) {
+    SubBlock S;
+    const uint2 *src = reinterpret_cast<const uint2 *>(subs + sb);
+    uint2 *d = reinterpret_cast<uint2 *>(&S);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) d[i] = __ldg(src + i);
+    return S;
+}
+
+// One pass over all tiles; Runner::run<RB, ADJ>(sb, ...) applies sub-block sb of the pass to
+// the tile (it gathers the thread's registers, applies the gates and scatters them back).
 template <int RB, bool ADJ, class Runner>
 __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *__restrict__ lam,
                                            uint32_t n, uint32_t tiles_log, uint64_t total_tiles,
@@ -352,18 +372,7 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         double2 *tp = tile_buf(b, 0);
         double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
         for (uint32_t sb = 0; sb < snsub; ++sb) {
-            SubBlock S;
-            {
-                const uint2 *src = reinterpret_cast<const uint2 *>(subs + sb);
-                uint2 *d = reinterpret_cast<uint2 *>(&S);
-#pragma unroll
-                for (int i = 0; i < 3; ++i) d[i] = __ldg(src + i);
-            }
-            uint32_t tb = 0;
-#pragma unroll
-            for (int i = 0; i < 12 - RB; ++i)
-                if (i < int(k) - RB && ((threadIdx.x >> i) & 1)) tb |= 1u << S.perm[i];
-            Runner::template run<RB, ADJ>(S, sb, tp, tl, ops, mats, subs, sacc, nthreads, tb, gbase);
+            Runner::template run<RB, ADJ>(sb, k, tp, tl, ops, mats, subs, sacc, nthreads, gbase);
             __syncthreads();
         }
         const uint64_t off = ((T >> tiles_log) << n) + gbase;

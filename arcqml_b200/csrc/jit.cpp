@@ -136,19 +136,34 @@ bool adjoint_per_warp() {
     return on;
 }
 
+// Host copy of the shared-memory swizzle of fused_core.cuh (phys): j ^ fold of its 3-bit groups.
+uint32_t swizzle(uint32_t j) { return j ^ (((j >> 3) ^ (j >> 6) ^ (j >> 9)) & 7u); }
+
 // Per-thread value of the op's qubit `slot` when it is not a register bit (fast paths D1_UNI and
 // the sign flips): a tile bit of the thread's base index, or a bit of the tile's global base.
-std::string const_bit(const FOp &o, int slot) {
+std::string const_bit(const FOp &o, int slot, const SubBlock &S, uint32_t thread_bits) {
     std::ostringstream e;
-    if (o.dq_in_tile[slot]) e << "((tb >> " << int(o.dq_pos[slot]) << ") & 1u)";
-    else e << "uint32_t((gbase >> " << int(o.dq_pos[slot]) << ") & 1ull)";
+    if (o.dq_in_tile[slot]) {
+        int bit = -1;
+        for (uint32_t i = 0; i < thread_bits; ++i)
+            if (S.perm[i] == o.dq_pos[slot]) bit = int(i);
+        if (bit < 0) return std::string();
+        e << "((tid >> " << bit << ") & 1u)";
+    } else {
+        e << "uint32_t((gbase >> " << int(o.dq_pos[slot]) << ") & 1ull)";
+    }
     return e.str();
 }
 
 // The fast path of op o on the register array `r` (U in forward passes, U^dagger in adjoint
 // passes: the planner stores the daggered matrices). False for a combination without one.
-bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb) {
+bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
+                const SubBlock &S, uint32_t tbits) {
     const int b0 = o.rb0, b1 = o.rb1;
+    const std::string bit0 = (o.code == FC_D1_UNI || o.code == FC_SIGN_RC || o.code == FC_SIGN_CC)
+                                 ? const_bit(o, 0, S, tbits) : std::string("0u");
+    const std::string bit1 = o.code == FC_SIGN_CC ? const_bit(o, 1, S, tbits) : std::string("0u");
+    if (bit0.empty() || bit1.empty()) return false;
     const uint32_t m = o.moff;
     const bool uses_b0 = o.code != FC_D1_UNI && o.code != FC_SIGN_CC;
     const bool uses_b1 = o.code == FC_SIGN_RR || o.code == FC_M4;
@@ -165,16 +180,16 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb)
         c << "f_d1_reg<RB, " << b0 << ">(" << r << ", M[" << m << "], M[" << m + 1 << "]);";
         break;
     case FC_D1_UNI:
-        c << "f_d1_uni<RB>(" << r << ", " << const_bit(o, 0) << " ? M[" << m + 1 << "] : M[" << m
+        c << "f_d1_uni<RB>(" << r << ", " << bit0 << " ? M[" << m + 1 << "] : M[" << m
           << "]);";
         break;
     case FC_SIGN_RR: c << "f_sign_rr<RB, " << b0 << ", " << b1 << ">(" << r << ");"; break;
     case FC_SIGN_RC:
-        c << "f_sign_rc<RB, " << b0 << ">(" << r << ", " << const_bit(o, 0)
+        c << "f_sign_rc<RB, " << b0 << ">(" << r << ", " << bit0
           << " ? 0x80000000u : 0u);";
         break;
     case FC_SIGN_CC:
-        c << "f_sign_cc<RB>(" << r << ", (" << const_bit(o, 0) << " & " << const_bit(o, 1)
+        c << "f_sign_cc<RB>(" << r << ", (" << bit0 << " & " << bit1
           << ") ? 0x80000000u : 0u);";
         break;
     case FC_M4: c << "f_m4<RB, " << b0 << ", " << b1 << ">(" << r << ", M + " << m << ");"; break;
@@ -184,11 +199,12 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb)
 }
 
 // Gradient then U^dagger on psi and lambda, as adj_fast does it.
-bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb) {
+bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
+                  uint32_t tbits) {
     if (o.gkind == GK_NONE) {
-        if (!emit_apply(c, o, "v", rb)) return false;
+        if (!emit_apply(c, o, "v", rb, S, tbits)) return false;
         c << "\n        ";
-        return emit_apply(c, o, "w", rb);
+        return emit_apply(c, o, "w", rb, S, tbits);
     }
     const int b0 = o.rb0;
     if (b0 >= int(rb) && o.code != FC_D1_UNI) return false;
@@ -196,13 +212,17 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb) {
     if (o.code == FC_RX && o.gcode == GF_X) c << "z = g_x<RB, " << b0 << ">(v, w);";
     else if (o.code == FC_RY && o.gcode == GF_Y) c << "z = g_y<RB, " << b0 << ">(v, w);";
     else if (o.code == FC_D1_REG && o.gcode == GF_Z_REG) c << "z = g_z<RB, " << b0 << ">(v, w);";
-    else if (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI)
-        c << "z = g_z_uni<RB>(v, w); if (" << const_bit(o, 0) << ") z = -z;";
-    else return false;
+    else if (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI) {
+        const std::string bit = const_bit(o, 0, S, tbits);
+        if (bit.empty()) return false;
+        c << "z = g_z_uni<RB>(v, w); if (" << bit << ") z = -z;";
+    } else {
+        return false;
+    }
     c << "\n        ";
-    if (!emit_apply(c, o, "v", rb)) return false;
+    if (!emit_apply(c, o, "v", rb, S, tbits)) return false;
     c << "\n        ";
-    if (!emit_apply(c, o, "w", rb)) return false;
+    if (!emit_apply(c, o, "w", rb, S, tbits)) return false;
     c << "\n        " << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
       << o.acc[0] << "u * nthreads, 0.5 * z); }";
     return true;
@@ -215,26 +235,52 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "    static constexpr bool kAccPerWarp = " << (acc_per_warp(adj, rb) ? "true" : "false")
       << ";\n"
          "    template <int RB, bool ADJ>\n"
-         "    __device__ static __forceinline__ void run(const SubBlock &S, uint32_t sb, double2 *tp,\n"
+         "    __device__ static __forceinline__ void run(uint32_t sb, uint32_t, double2 *tp,\n"
          "            double2 *tl, const FOp *, const double2 *M, const SubBlock *, double *sacc,\n"
-         "            uint32_t nthreads, uint32_t tb, uint64_t gbase) {\n"
+         "            uint32_t nthreads, uint64_t gbase) {\n"
          "        double2 v[1 << RB], w[1 << RB];\n"
-         "        load_regs<RB, ADJ>(S, tb, tp, tl, v, w);\n"
+         "        const uint32_t tid = threadIdx.x;\n"
+         "        uint32_t p;\n"
          "        switch (sb) {\n";
     for (size_t sb = 0; sb < st.subs.size(); ++sb) {
         const SubBlock &S = st.subs[sb];
         if (!(S.flags & SB_ALL_FAST)) return std::string();
+        // Swizzled shared-memory slot of register element e: phys is linear over XOR and tb
+        // shares no bit with the element's register bits, so slot = phys(tb) ^ phys(bits of e).
+        std::vector<uint32_t> slot(size_t(1) << rb);
+        for (uint32_t e = 0; e < slot.size(); ++e) {
+            uint32_t x = 0;
+            for (uint32_t r = 0; r < rb; ++r)
+                if ((e >> r) & 1u) x |= 1u << S.R[r];
+            slot[e] = swizzle(x);
+        }
         c << "        case " << sb << ":\n";
+        // the thread's swizzled base: thread bit i is tile bit S.perm[i]
+        const uint32_t kb = st.header.k - rb;
+        c << "        p = 0u";
+        for (uint32_t i = 0; i < kb; ++i)
+            c << " ^ (((tid >> " << i << ") & 1u) * " << swizzle(1u << S.perm[i]) << "u)";
+        c << ";\n";
+        for (uint32_t e = 0; e < slot.size(); ++e) {
+            c << "        v[" << e << "] = tp[p ^ " << slot[e] << "u];";
+            if (adj) c << " w[" << e << "] = tl[p ^ " << slot[e] << "u];";
+            c << "\n";
+        }
         for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
             c << "        ";
-            const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb) : emit_apply(c, st.ops[oi], "v", rb);
+            const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb, S, kb)
+                                : emit_apply(c, st.ops[oi], "v", rb, S, kb);
             if (!ok) return std::string();
+            c << "\n";
+        }
+        for (uint32_t e = 0; e < slot.size(); ++e) {
+            c << "        tp[p ^ " << slot[e] << "u] = v[" << e << "];";
+            if (adj) c << " tl[p ^ " << slot[e] << "u] = w[" << e << "];";
             c << "\n";
         }
         c << "        break;\n";
     }
     c << "        }\n"
-         "        store_regs<RB, ADJ>(S, tb, tp, tl, v, w);\n"
          "    }\n"
          "};\n";
     const int threads = (adj || rb == 4) ? 256 : 512;
