@@ -263,7 +263,10 @@ def gpu_arm(args):
     peak = hbm if hbm else 6650.0
     local_amps = 2.0 ** (n - (world.bit_length() - 1))
     traffic = NCU_DRAM_BYTES_PER_AMP.get(dname)
-    roofline = {"kernel": f"k_fused ({dname})" if dname.startswith("fused") else dname,
+    label = {"fused_adjoint": "arcqml_pass (fused adjoint passes, run-time compiled)",
+             "fused_forward": "arcqml_pass (fused forward passes, run-time compiled)",
+             "observable": "k_pauli (observable)"}.get(dname, dname)
+    roofline = {"kernel": label,
                 "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s",
                 "peak_source": "measured" if hbm else "fallback",
