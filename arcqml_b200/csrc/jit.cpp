@@ -224,13 +224,15 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb, S, tbits)) return false;
     c << "\n        " << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
-      << o.acc[0] << "u * nthreads, 0.5 * z); }";
+      << o.acc[0] << "u * kCols, 0.5 * z); }";
     return true;
 }
 
 // Source of the kernel `arcqml_pass` for one pass; empty when some op has no fast path.
 std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     std::ostringstream c;
+    const uint32_t threads = 1u << (st.header.k - rb);
+    const uint32_t cols = acc_per_warp(adj, rb) ? threads / 32u : threads;
     c << "struct PassOps {\n"
          "    static constexpr bool kAccPerWarp = " << (acc_per_warp(adj, rb) ? "true" : "false")
       << ";\n"
@@ -239,6 +241,7 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "            double2 *tl, const FOp *, const double2 *M, const SubBlock *, double *sacc,\n"
          "            uint32_t nthreads, uint64_t gbase) {\n"
          "        double2 v[1 << RB], w[1 << RB];\n"
+         "        constexpr uint32_t kCols = " << cols << "u;  // accumulator row stride\n"
          "        const uint32_t tid = threadIdx.x;\n"
          "        uint32_t p;\n"
          "        switch (sb) {\n";
@@ -283,9 +286,9 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     c << "        }\n"
          "    }\n"
          "};\n";
-    const int threads = (adj || rb == 4) ? 256 : 512;
+    const int bound = (adj || rb == 4) ? 256 : 512;
     const int min_blocks = (adj && adjoint_per_warp() && rb == 3) ? 2 : 1;
-    c << "extern \"C\" __global__ void __launch_bounds__(" << threads << ", " << min_blocks << ")\n"
+    c << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"
          "            const SubBlock *__restrict__ subs, const FOp *__restrict__ gops,\n"
