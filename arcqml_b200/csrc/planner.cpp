@@ -9,6 +9,7 @@
 // fused and run as separate per-gate kernels between passes.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "fused.h"
@@ -203,6 +204,16 @@ inline int residue(int bit) { return bit % 3; }
 
 }  // namespace
 
+// Gates per pass: kMaxPassOps, or fewer with ARCQML_PASS_OPS=<count> (smaller compiled kernels).
+size_t pass_op_cap() {
+    static const size_t cap = [] {
+        const char *e = std::getenv("ARCQML_PASS_OPS");
+        const long v = e ? std::strtol(e, nullptr, 10) : 0;
+        return (v > 0 && v < kMaxPassOps) ? size_t(v) : size_t(kMaxPassOps);
+    }();
+    return cap;
+}
+
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb) {
     Schedule sch;
@@ -259,7 +270,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 members.push_back(i);
                 pass_acc += g.parents.size();
                 pass_mats += mat_entries(g);
-                if (members.size() >= size_t(kMaxPassOps)) break;
+                if (members.size() >= pass_op_cap()) break;
             } else {
                 blocked |= g.touched;
             }
