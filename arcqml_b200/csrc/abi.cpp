@@ -460,6 +460,31 @@ int32_t arcqml_rt_v2_expectation_and_apply(const ArcqmlObservableHandle *observa
     });
 }
 
+// Shared validation of the slice entry points.
+static void check_slices(const void *amplitudes, size_t num_local_qubits, const uint32_t *positions,
+                         size_t num_positions, uint64_t chunk_begin, uint64_t chunk_len) {
+    if (!amplitudes) fail("amplitude buffer is null");
+    if (num_local_qubits >= 63) fail("shard qubit count must be below 63");
+    if (num_positions == 0 || num_positions > kMaxSliceBits)
+        fail("slice must have between 1 and 8 positions");
+    if (num_positions > num_local_qubits) fail("slice has more positions than the shard has qubits");
+    if (!positions) fail("slice position list is null");
+    uint64_t seen = 0;
+    for (size_t i = 0; i < num_positions; ++i) {
+        if (positions[i] >= num_local_qubits) {
+            std::ostringstream m;
+            m << "slice position " << positions[i] << " is outside the " << num_local_qubits
+              << "-qubit shard";
+            fail(m.str());
+        }
+        if ((seen >> positions[i]) & 1) fail("slice positions repeat");
+        seen |= uint64_t(1) << positions[i];
+    }
+    const uint64_t others = uint64_t(1) << (num_local_qubits - num_positions);
+    if (chunk_begin > others || chunk_len > others - chunk_begin)
+        fail("slice chunk exceeds the shard");
+}
+
 int32_t arcqml_rt_v2_expectation_and_accumulate(const ArcqmlObservableHandle *observable,
                                                 const arcqml_c128 *amplitudes, arcqml_c128 *output,
                                                 size_t batch, size_t num_qubits, double *values,
@@ -480,26 +505,8 @@ int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubi
                                   arcqml_c128 *staging, int32_t unpack, void *stream) {
     return guarded([&] {
         if (!amplitudes || !staging) fail("amplitude or staging buffer is null");
-        if (num_local_qubits >= 63) fail("shard qubit count must be below 63");
-        if (num_positions == 0 || num_positions > kMaxSliceBits)
-            fail("slice must have between 1 and 8 positions");
-        if (num_positions > num_local_qubits)
-            fail("slice has more positions than the shard has qubits");
-        if (!positions) fail("slice position list is null");
-        uint64_t seen = 0;
-        for (size_t i = 0; i < num_positions; ++i) {
-            if (positions[i] >= num_local_qubits) {
-                std::ostringstream m;
-                m << "slice position " << positions[i] << " is outside the " << num_local_qubits
-                  << "-qubit shard";
-                fail(m.str());
-            }
-            if ((seen >> positions[i]) & 1) fail("slice positions repeat");
-            seen |= uint64_t(1) << positions[i];
-        }
-        const uint64_t others = uint64_t(1) << (num_local_qubits - num_positions);
-        if (chunk_begin > others || chunk_len > others - chunk_begin)
-            fail("slice chunk exceeds the shard");
+        check_slices(amplitudes, num_local_qubits, positions, num_positions, chunk_begin,
+                     chunk_len);
         ThreadContext &ctx = thread_context();
         launch_slices(reinterpret_cast<double2 *>(amplitudes), uint32_t(num_local_qubits),
                       positions, uint32_t(num_positions), chunk_begin, chunk_len, skip_value,
@@ -577,6 +584,64 @@ size_t arcqml_rt_v2_jit_info(uint64_t *kernels_compiled, uint64_t *launches, uin
         last_error[n] = '\0';
     }
     return last.size();
+}
+
+int32_t arcqml_rt_v2_shard_slices_from(arcqml_c128 *amplitudes, size_t num_local_qubits,
+                                       const uint32_t *positions, size_t num_positions,
+                                       uint64_t chunk_begin, uint64_t chunk_len,
+                                       const arcqml_c128 *const *sources, void *stream) {
+    return guarded([&] {
+        check_slices(amplitudes, num_local_qubits, positions, num_positions, chunk_begin,
+                     chunk_len);
+        if (!sources) fail("slice source list is null");
+        ThreadContext &ctx = thread_context();
+        launch_slices_from(reinterpret_cast<double2 *>(amplitudes), positions,
+                           uint32_t(num_positions), chunk_begin, chunk_len,
+                           reinterpret_cast<const double2 *const *>(sources),
+                           pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_peer_buffer_create(size_t bytes, void **device_ptr, uint8_t *handle) {
+    return guarded([&] {
+        if (!device_ptr || !handle) fail("output pointer is null");
+        if (bytes == 0) fail("peer buffer size must be non-zero");
+        void *p = nullptr;
+        check_cuda(cudaMalloc(&p, bytes), "cudaMalloc (peer buffer)");
+        cudaIpcMemHandle_t h;
+        const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            check_cuda(e, "cudaIpcGetMemHandle");
+        }
+        static_assert(sizeof(h) == 64, "IPC handle size");
+        std::memcpy(handle, &h, sizeof(h));
+        *device_ptr = p;
+    });
+}
+
+int32_t arcqml_rt_v2_peer_buffer_open(const uint8_t *handle, void **device_ptr) {
+    return guarded([&] {
+        if (!device_ptr || !handle) fail("handle or output pointer is null");
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle, sizeof(h));
+        void *p = nullptr;
+        check_cuda(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess),
+                   "cudaIpcOpenMemHandle");
+        *device_ptr = p;
+    });
+}
+
+int32_t arcqml_rt_v2_peer_buffer_close(void *device_ptr) {
+    return guarded([&] {
+        if (device_ptr) check_cuda(cudaIpcCloseMemHandle(device_ptr), "cudaIpcCloseMemHandle");
+    });
+}
+
+int32_t arcqml_rt_v2_peer_buffer_destroy(void *device_ptr) {
+    return guarded([&] {
+        if (device_ptr) check_cuda(cudaFree(device_ptr), "cudaFree (peer buffer)");
+    });
 }
 
 int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,

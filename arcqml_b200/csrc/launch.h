@@ -47,6 +47,11 @@ void launch_slices(double2 *amps, uint32_t n_local, const uint32_t *positions, u
                    uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip, double2 *staging,
                    bool unpack, cudaStream_t s);
 constexpr uint32_t kMaxSliceBits = 8;
+// amps[index(y, o)] <- sources[y][o - chunk_begin] for every slice value y whose source is
+// non-null (sources may be peer mappings of other GPUs' buffers).
+void launch_slices_from(double2 *amps, const uint32_t *positions, uint32_t k,
+                        uint64_t chunk_begin, uint64_t chunk_len, const double2 *const *sources,
+                        cudaStream_t s);
 
 // cum[i] = sequential f64 sum of |amps[j]|^2 for j <= i (no FMA); out[s] = basis index of
 // shot s of StdRng::seed_from_u64(seed). cum holds 2^n doubles, out `shots` entries.

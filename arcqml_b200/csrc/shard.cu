@@ -50,9 +50,60 @@ __global__ void __launch_bounds__(kSliceThreads)
     }
 }
 
+// grid.y = slice value y; sources[y] (nullptr: skip) holds the chunk's amplitudes of value y,
+// possibly in another GPU's memory (a peer mapping): plain loads over NVLink, local stores.
+struct SliceSources {
+    const double2 *src[1u << kMaxSliceBits];
+};
+
+__global__ void __launch_bounds__(kSliceThreads)
+    k_shard_slices_from(double2 *__restrict__ amps, uint64_t chunk_begin, uint64_t chunk_len,
+                        const __grid_constant__ SliceArgs A,
+                        const __grid_constant__ SliceSources S) {
+    const uint64_t y = blockIdx.y;
+    const double2 *src = S.src[y];
+    if (!src) return;
+    for (uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < chunk_len;
+         j += uint64_t(gridDim.x) * blockDim.x)
+        amps[slice_index(chunk_begin + j, y, A)] = src[j];
+}
+
 int g_sms = 0;
 
 }  // namespace
+
+void launch_slices_from(double2 *amps, const uint32_t *positions, uint32_t k,
+                        uint64_t chunk_begin, uint64_t chunk_len, const double2 *const *sources,
+                        cudaStream_t s) {
+    SliceArgs A{};
+    A.k = k;
+    for (uint32_t i = 0; i < k; ++i) {
+        A.sorted[i] = positions[i];
+        A.ybit[i] = uint64_t(1) << positions[i];
+    }
+    std::sort(A.sorted, A.sorted + k);
+    SliceSources S{};
+    uint32_t active = 0;
+    for (uint32_t y = 0; y < (1u << k); ++y) {
+        S.src[y] = reinterpret_cast<const double2 *>(sources[y]);
+        active += sources[y] ? 1u : 0u;
+    }
+    if (!active || !chunk_len) return;
+    if (g_sms == 0) {
+        int dev = 0;
+        check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+        check_cuda(cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev),
+                   "cudaDeviceGetAttribute");
+    }
+    const uint64_t want = (uint64_t(g_sms) * 8 + active - 1) / active;
+    const uint64_t need = (chunk_len + kSliceThreads - 1) / kSliceThreads;
+    const unsigned bx = unsigned(std::max<uint64_t>(1, std::min(want, need)));
+    const ProfToken tok = prof_begin(PROF_SHARD, s);
+    k_shard_slices_from<<<dim3(bx, 1u << k), kSliceThreads, 0, s>>>(amps, chunk_begin, chunk_len,
+                                                                      A, S);
+    prof_end(tok, s, 32.0 * double(chunk_len) * double(active));
+    check_cuda(cudaGetLastError(), "shard slice gather kernel launch");
+}
 
 void launch_slices(double2 *amps, uint32_t n_local, const uint32_t *positions, uint32_t k,
                    uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip, double2 *staging,

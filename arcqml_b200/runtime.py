@@ -124,6 +124,11 @@ def load():
         "arcqml_rt_v2_sample": (I32, [P, S, C.c_uint64, C.c_uint64, P, P, P]),
         "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
                                             I32, P]),
+        "arcqml_rt_v2_shard_slices_from": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, P, P]),
+        "arcqml_rt_v2_peer_buffer_create": (I32, [S, P, P]),
+        "arcqml_rt_v2_peer_buffer_open": (I32, [P, P]),
+        "arcqml_rt_v2_peer_buffer_close": (I32, [P]),
+        "arcqml_rt_v2_peer_buffer_destroy": (I32, [P]),
         "arcqml_rt_v2_adjoint_backward": (I32, [P, P, P, S, S, P, P, S, P, S, P]),
         "arcqml_rt_v2_norms": (I32, [P, S, S, P, P]),
         "arcqml_rt_v2_norms_noalloc": (I32, [P, S, S, P, P]),
@@ -521,6 +526,57 @@ def shard_slices(shard, num_local_qubits: int, positions: Sequence[int], chunk_b
     _status(load().arcqml_rt_v2_shard_slices(
         _dev_ptr(shard), num_local_qubits, pos, len(positions), chunk_begin, chunk_len,
         skip_value, _dev_ptr(staging), int(bool(unpack)), _stream_ptr(stream)))
+
+
+def shard_slices_from(shard, num_local_qubits: int, positions: Sequence[int], chunk_begin: int,
+                      chunk_len: int, sources: Sequence[Optional[int]], stream=None) -> None:
+    """Gathers slice value y of a chunk from device address sources[y] (None: skip) into the
+    shard (see arcqml_rt_v2_shard_slices_from)."""
+    pos = (C.c_uint32 * len(positions))(*positions)
+    src = (C.c_void_p * len(sources))(*[s if s else None for s in sources])
+    _status(load().arcqml_rt_v2_shard_slices_from(
+        _dev_ptr(shard), num_local_qubits, pos, len(positions), chunk_begin, chunk_len, src,
+        _stream_ptr(stream)))
+
+
+def shard_slices_ptr(shard, num_local_qubits: int, positions: Sequence[int], chunk_begin: int,
+                     chunk_len: int, skip_value: int, staging_address: int, unpack: bool,
+                     stream=None) -> None:
+    """shard_slices with the staging buffer given as a raw device address."""
+    pos = (C.c_uint32 * len(positions))(*positions)
+    _status(load().arcqml_rt_v2_shard_slices(
+        _dev_ptr(shard), num_local_qubits, pos, len(positions), chunk_begin, chunk_len,
+        skip_value, C.c_void_p(staging_address), int(bool(unpack)), _stream_ptr(stream)))
+
+
+class PeerBuffer:
+    """A device buffer other processes of the node can map (CUDA IPC)."""
+
+    def __init__(self, nbytes: int):
+        ptr = C.c_void_p()
+        self.handle = (C.c_uint8 * 64)()
+        _status(load().arcqml_rt_v2_peer_buffer_create(nbytes, C.byref(ptr), self.handle))
+        self.address = int(ptr.value)
+        self.nbytes = nbytes
+
+    def handle_bytes(self) -> bytes:
+        return bytes(self.handle)
+
+    @staticmethod
+    def open(handle: bytes) -> int:
+        ptr = C.c_void_p()
+        h = (C.c_uint8 * 64)(*handle)
+        _status(load().arcqml_rt_v2_peer_buffer_open(h, C.byref(ptr)))
+        return int(ptr.value)
+
+    @staticmethod
+    def close(address: int) -> None:
+        _status(load().arcqml_rt_v2_peer_buffer_close(C.c_void_p(address)))
+
+    def destroy(self) -> None:
+        if self.address:
+            _status(load().arcqml_rt_v2_peer_buffer_destroy(C.c_void_p(self.address)))
+            self.address = 0
 
 
 def profile_enable(on: bool = True) -> None:

@@ -310,6 +310,35 @@ class DistComm:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM, group=self.group)
         return t.cpu().numpy()
 
+    def barrier(self) -> None:
+        """Waits for this rank's device work, then for every rank."""
+        import torch
+        torch.cuda.synchronize()
+        if self.nccl:
+            self.dist.barrier(group=self.group, device_ids=[torch.cuda.current_device()])
+        else:
+            self.dist.barrier(group=self.group)
+
+    def same_node(self) -> bool:
+        import socket
+        names = [None] * self.size
+        self.dist.all_gather_object(names, socket.gethostname(), group=self.group)
+        return len(set(names)) == 1
+
+    def share_buffer(self, buf) -> Dict[int, int]:
+        """Every rank's exported buffer as a device address usable here (IPC mappings)."""
+        handles = [None] * self.size
+        self.dist.all_gather_object(handles, buf.handle_bytes(), group=self.group)
+        from . import runtime as rt
+        return {r: (buf.address if r == self.rank else rt.PeerBuffer.open(handles[r]))
+                for r in range(self.size)}
+
+    def unshare_buffers(self, addresses: Dict[int, int]) -> None:
+        from . import runtime as rt
+        for r, a in addresses.items():
+            if r != self.rank:
+                rt.PeerBuffer.close(a)
+
     def allgather(self, shard):
         import torch
         parts = [torch.empty_like(shard) for _ in range(self.size)]
@@ -375,6 +404,17 @@ class RuntimeBackend:
         self.rt.shard_slices(shard, n_local, positions, chunk_begin, chunk_len, skip, staging,
                              unpack)
 
+    # -- peer transport (device addresses) --
+    def peer_buffer(self, nbytes: int):
+        return self.rt.PeerBuffer(nbytes)
+
+    def pack_to(self, shard, n_local, positions, chunk_begin, chunk_len, skip, address) -> None:
+        self.rt.shard_slices_ptr(shard, n_local, positions, chunk_begin, chunk_len, skip, address,
+                                 False)
+
+    def gather_from(self, shard, n_local, positions, chunk_begin, chunk_len, sources) -> None:
+        self.rt.shard_slices_from(shard, n_local, positions, chunk_begin, chunk_len, sources)
+
 
 # ---------------------------------------------------------------------------- simulator
 
@@ -394,7 +434,8 @@ class ShardedStateVectorSimulator:
     over ranks (same on every rank).
     """
 
-    def __init__(self, num_qubits: int, comm=None, backend=None, chunk_amplitudes: int = 1 << 24):
+    def __init__(self, num_qubits: int, comm=None, backend=None, chunk_amplitudes: int = 1 << 24,
+                 transport: Optional[str] = None, peer_bytes: int = 2 << 30):
         self.comm = comm if comm is not None else DistComm()
         self.backend = backend if backend is not None else RuntimeBackend()
         size = self.comm.size
@@ -410,6 +451,22 @@ class ShardedStateVectorSimulator:
         self.stats = SwapStats()
         self._events = None
         self._staging = None
+        # Swap transport: "peer" (each rank gathers its slices from the peers' packed buffers
+        # over NVLink with its own kernel) when every rank can map the others' memory, else
+        # "p2p" (point-to-point sends through the communicator). ARCQML_SWAP overrides.
+        import os
+        want = transport or os.environ.get("ARCQML_SWAP") or "auto"
+        if want not in ("auto", "peer", "p2p"):
+            raise ShardError(f"unknown swap transport {want!r}")
+        can_peer = (size > 1 and hasattr(self.comm, "share_buffer") and
+                    hasattr(self.backend, "gather_from"))
+        if want == "auto":
+            want = "peer" if can_peer and self.comm.same_node() else "p2p"
+        if want == "peer" and not can_peer:
+            raise ShardError("the peer swap transport needs share_buffer and gather_from")
+        self.transport = want
+        self._peer_bytes = int(peer_bytes)
+        self._peer = None  # (buffer, {rank: address})
         self.psi = None
         self.lam = None
         self._ctx = None
@@ -470,6 +527,47 @@ class ShardedStateVectorSimulator:
                              for _ in range(2)]
         return self._staging
 
+    def close(self) -> None:
+        """Releases the peer mappings and buffer (collective: every rank calls it)."""
+        if self._peer is not None:
+            buf, addrs = self._peer
+            self.comm.barrier()
+            self.comm.unshare_buffers(addrs)
+            self.comm.barrier()
+            buf.destroy()
+            self._peer = None
+
+    def _peer_swap(self, t, n_l, lpos, x, peers, others) -> int:
+        """Moves one tensor's slices through the peers' buffers; returns the chunk length."""
+        if self._peer is None:
+            buf = self.backend.peer_buffer(self._peer_bytes)
+            self._peer = (buf, self.comm.share_buffer(buf))
+        buf, addrs = self._peer
+        half = self._peer_bytes // 2
+        chunk = min(others, max(1, half // (16 * ((1 << self.layout.g) - 1))))
+        chunk = 1 << (chunk.bit_length() - 1)
+        starts = list(range(0, others, chunk))
+        be = self.backend
+
+        def region(rank, c):  # buffer half of chunk c in `rank`'s buffer
+            return addrs[rank] + (c & 1) * half
+
+        # Pack chunk c into half c % 2 of this rank's buffer (block order: slice values but
+        # this rank's own); after a barrier every rank gathers chunk c from the peers' halves
+        # while packing chunk c + 1 into its other half; one barrier per chunk.
+        be.pack_to(t, n_l, lpos, starts[0], chunk, x, region(self.rank, 0))
+        self.comm.barrier()
+        for c, c0 in enumerate(starts):
+            if c + 1 < len(starts):
+                be.pack_to(t, n_l, lpos, starts[c + 1], chunk, x, region(self.rank, c + 1))
+            sources = [None] * (1 << len(lpos))
+            for y, r in peers.items():
+                blk = x - (1 if x > y else 0)  # rank r skipped its own value y when packing
+                sources[y] = region(r, c) + blk * chunk * 16
+            be.gather_from(t, n_l, lpos, c0, chunk, sources)
+            self.comm.barrier()
+        return chunk
+
     def _swap(self, pairs: Sequence[Tuple[int, int]], tensors: Sequence) -> None:
         L = self.layout
         n_l = L.n_local
@@ -489,15 +587,26 @@ class ShardedStateVectorSimulator:
             peers[y] = r
         others = 1 << (n_l - k)
         nblk = (1 << k) - 1
-        chunk = min(others, max(1, self.chunk // nblk))
-        chunk = 1 << (chunk.bit_length() - 1)
-        stage = self._staging_for(nblk * chunk)
         be = self.backend
         ev = None
         if self._events is not None:
             import torch
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
+        if self.transport == "peer":
+            for t in tensors:
+                self._peer_swap(t, n_l, lpos, x, peers, others)
+            if ev is not None:
+                ev[1].record()
+                self._events.append(ev)
+            self.stats.swaps += 1
+            self.stats.qubits += k
+            self.stats.bytes_sent += len(tensors) * nblk * others * 16
+            L.apply_swap(pairs)
+            return
+        chunk = min(others, max(1, self.chunk // nblk))
+        chunk = 1 << (chunk.bit_length() - 1)
+        stage = self._staging_for(nblk * chunk)
 
         def views(buf):
             return {peers[y]: buf[(y - (1 if y > x else 0)) * chunk:

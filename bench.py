@@ -248,7 +248,8 @@ def gpu_arm(args):
         link = 770.0  # NVLink peer copy measured on this GPU type, GB/s per direction
         sent = st["bytes_sent"] / args.steps
         swap_ms = st["ms"] / args.steps
-        swaps = {"per_step": st["swaps"] / args.steps, "qubits_per_step": st["qubits"] / args.steps,
+        swaps = {"transport": sim.transport,
+                 "per_step": st["swaps"] / args.steps, "qubits_per_step": st["qubits"] / args.steps,
                  "bytes_sent_per_step": sent, "ms_per_step": round(swap_ms, 3),
                  "achieved_gbs": round(sent / (swap_ms * 1e-3) / 1e9, 1) if swap_ms else None,
                  "peak_gbs": link, "peak_source": "measured NVLink peer copy",
@@ -306,6 +307,7 @@ def gpu_arm(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        sim.close()
         torch.distributed.destroy_process_group()
 
 

@@ -112,6 +112,25 @@ int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubi
 int32_t arcqml_rt_v2_sample(const arcqml_c128 *amplitudes, size_t num_qubits, uint64_t shots,
                             uint64_t seed, uint64_t *indices, double *norm_sqr, void *stream);
 
+/* Same slice layout as arcqml_rt_v2_shard_slices, gathering into the shard: for every slice
+ * value y with sources[y] != NULL (sources has 2^num_positions entries) and o in
+ * [chunk_begin, chunk_begin + chunk_len): amplitudes[index(y, o)] <- sources[y][o - chunk_begin].
+ * A source may be another GPU's buffer mapped with arcqml_rt_v2_peer_buffer_open: the swap of a
+ * sharded state then reads each peer's packed slices over NVLink with plain loads. */
+int32_t arcqml_rt_v2_shard_slices_from(arcqml_c128 *amplitudes, size_t num_local_qubits,
+                                       const uint32_t *positions, size_t num_positions,
+                                       uint64_t chunk_begin, uint64_t chunk_len,
+                                       const arcqml_c128 *const *sources, void *stream);
+
+/* Device buffers shared between the processes of one node (CUDA IPC; no reference counterpart).
+ * create: cudaMalloc of `bytes` on the current device, its 64-byte IPC handle in handle[64];
+ * open: maps another process's buffer from its handle (peer access enabled on demand); close
+ * unmaps an opened buffer; destroy frees a created one. */
+int32_t arcqml_rt_v2_peer_buffer_create(size_t bytes, void **device_ptr, uint8_t *handle);
+int32_t arcqml_rt_v2_peer_buffer_open(const uint8_t *handle, void **device_ptr);
+int32_t arcqml_rt_v2_peer_buffer_close(void *device_ptr);
+int32_t arcqml_rt_v2_peer_buffer_destroy(void *device_ptr);
+
 /* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);

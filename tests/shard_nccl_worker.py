@@ -48,16 +48,19 @@ def main():
                       req=c.requires_grad_mask(True, False)))
     ok = True
     for case in cases:
-        sim = ShardedStateVectorSimulator(case["n"], comm=DistComm(), backend=RuntimeBackend(),
-                                          chunk_amplitudes=case.get("chunk", 1 << 20))
-        res = sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
-                           case["req"])
-        if rank == 0:
-            try:
-                check_world({0: res}, expected(O, case), 1)
-            except AssertionError as e:
-                print("mismatch", e, flush=True)
-                ok = False
+        for transport in ("p2p", "peer"):
+            sim = ShardedStateVectorSimulator(case["n"], comm=DistComm(), backend=RuntimeBackend(),
+                                              chunk_amplitudes=case.get("chunk", 1 << 20),
+                                              transport=transport, peer_bytes=1 << 20)
+            res = sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
+                               case["req"])
+            sim.close()
+            if rank == 0:
+                try:
+                    check_world({0: res}, expected(O, case), 1)
+                except AssertionError as e:
+                    print("mismatch", transport, e, flush=True)
+                    ok = False
     flag = torch.tensor([0 if ok else 1], device="cuda")
     dist.all_reduce(flag)
     dist.destroy_process_group()

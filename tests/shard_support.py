@@ -164,6 +164,20 @@ class ThreadComm:
         self._sync()
         return [t.clone() for t in self._gather(shard)]
 
+    # peer transport: the threads share one device, so buffers are used by address directly
+    def barrier(self):
+        self._sync()
+        self.hub.barrier.wait()
+
+    def same_node(self):
+        return True
+
+    def share_buffer(self, buf):
+        return dict(enumerate(self._gather(buf.address)))
+
+    def unshare_buffers(self, addresses):
+        pass
+
 
 def run_threads(size, fn):
     """Runs fn(rank, comm) on `size` threads; returns the per-rank results (re-raises)."""

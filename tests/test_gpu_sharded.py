@@ -57,26 +57,33 @@ def test_shard_slices_rejects_bad_arguments(runtime):
         runtime.shard_slices(dev, 6, [1], 16, 32, 0, st, False)
 
 
-def thread_world(size, case):
+def thread_world(size, case, transport="p2p"):
     from arcqml_b200.sharded import RuntimeBackend, ShardedStateVectorSimulator
 
     def body(rank, comm):
         sim = ShardedStateVectorSimulator(case["n"], comm=comm, backend=RuntimeBackend(),
-                                          chunk_amplitudes=case.get("chunk", 1 << 20))
-        return sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
-                            case["req"])
+                                          chunk_amplitudes=case.get("chunk", 1 << 20),
+                                          transport=transport,
+                                          peer_bytes=case.get("peer_bytes", 1 << 20))
+        try:
+            return sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
+                                case["req"])
+        finally:
+            sim.close()
 
     return dict(enumerate(run_threads(size, body)))
 
 
-@pytest.mark.parametrize("size,n", [(4, 12), (8, 13)])
-def test_emulated_ranks_random_plan_match_oracle(runtime, oracle, size, n):
+@pytest.mark.parametrize("size,n,transport", [(4, 12, "p2p"), (8, 13, "p2p"), (4, 12, "peer"),
+                                              (8, 13, "peer")])
+def test_emulated_ranks_random_plan_match_oracle(runtime, oracle, size, n, transport):
     rng = np.random.Generator(np.random.PCG64(900 + n))
     npar = 12
     case = dict(n=n, ops=random_plan(rng, n, 160, npar), terms=random_terms(rng, n, 40),
                 init=random_state(rng, n), upstream=float(rng.normal()),
-                req=[1] + [int(x) for x in (rng.uniform(size=npar) < 0.8)], chunk=1 << 9)
-    res = thread_world(size, case)
+                req=[1] + [int(x) for x in (rng.uniform(size=npar) < 0.8)], chunk=1 << 9,
+                peer_bytes=1 << 16)
+    res = thread_world(size, case, transport)
     assert res[0]["swaps"] > 0
     check_world(res, expected(oracle, case), size)
 
