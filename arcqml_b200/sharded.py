@@ -325,19 +325,10 @@ class DistComm:
         self.dist.all_gather_object(names, socket.gethostname(), group=self.group)
         return len(set(names)) == 1
 
-    def share_buffer(self, buf) -> Dict[int, int]:
-        """Every rank's exported buffer as a device address usable here (IPC mappings)."""
-        handles = [None] * self.size
-        self.dist.all_gather_object(handles, buf.handle_bytes(), group=self.group)
-        from . import runtime as rt
-        return {r: (buf.address if r == self.rank else rt.PeerBuffer.open(handles[r]))
-                for r in range(self.size)}
-
-    def unshare_buffers(self, addresses: Dict[int, int]) -> None:
-        from . import runtime as rt
-        for r, a in addresses.items():
-            if r != self.rank:
-                rt.PeerBuffer.close(a)
+    def allgather_object(self, obj) -> list:
+        out = [None] * self.size
+        self.dist.all_gather_object(out, obj, group=self.group)
+        return out
 
     def allgather(self, shard):
         import torch
@@ -415,6 +406,12 @@ class RuntimeBackend:
     def gather_from(self, shard, n_local, positions, chunk_begin, chunk_len, sources) -> None:
         self.rt.shard_slices_from(shard, n_local, positions, chunk_begin, chunk_len, sources)
 
+    def peer_open(self, handle: bytes) -> int:
+        return self.rt.PeerBuffer.open(handle)
+
+    def peer_close(self, address: int) -> None:
+        self.rt.PeerBuffer.close(address)
+
 
 # ---------------------------------------------------------------------------- simulator
 
@@ -458,12 +455,12 @@ class ShardedStateVectorSimulator:
         want = transport or os.environ.get("ARCQML_SWAP") or "auto"
         if want not in ("auto", "peer", "p2p"):
             raise ShardError(f"unknown swap transport {want!r}")
-        can_peer = (size > 1 and hasattr(self.comm, "share_buffer") and
+        can_peer = (size > 1 and hasattr(self.comm, "allgather_object") and
                     hasattr(self.backend, "gather_from"))
         if want == "auto":
             want = "peer" if can_peer and self.comm.same_node() else "p2p"
         if want == "peer" and not can_peer:
-            raise ShardError("the peer swap transport needs share_buffer and gather_from")
+            raise ShardError("the peer swap transport needs allgather_object and gather_from")
         self.transport = want
         self._peer_bytes = int(peer_bytes)
         self._peer = None  # (buffer, {rank: address})
@@ -532,16 +529,46 @@ class ShardedStateVectorSimulator:
         if self._peer is not None:
             buf, addrs = self._peer
             self.comm.barrier()
-            self.comm.unshare_buffers(addrs)
+            if not getattr(self.comm, "same_process", False):
+                for r, a in addrs.items():
+                    if r != self.rank:
+                        self.backend.peer_close(a)
             self.comm.barrier()
             buf.destroy()
             self._peer = None
 
+    def _share_peer_buffer(self):
+        """Creates this rank's peer buffer and maps every other rank's (collective); None on
+        every rank if any rank failed, after undoing what succeeded."""
+        same = getattr(self.comm, "same_process", False)
+        buf, handle = None, None
+        try:
+            buf = self.backend.peer_buffer(self._peer_bytes)
+            handle = buf.address if same else buf.handle_bytes()
+        except Exception:  # noqa: BLE001 - reported to the other ranks below
+            handle = None
+        handles = self.comm.allgather_object(handle)
+        addrs, ok = {}, all(h is not None for h in handles)
+        if ok:
+            try:
+                for r, h in enumerate(handles):
+                    addrs[r] = buf.address if r == self.rank else (h if same else
+                                                                    self.backend.peer_open(h))
+            except Exception:  # noqa: BLE001 - reported to the other ranks below
+                ok = False
+        failed = float(self.comm.allreduce_sum(np.array([0.0 if ok else 1.0]))[0])
+        if failed == 0.0:
+            return buf, addrs
+        if not same:
+            for r, a in addrs.items():
+                if r != self.rank:
+                    self.backend.peer_close(a)
+        if buf is not None:
+            buf.destroy()
+        return None
+
     def _peer_swap(self, t, n_l, lpos, x, peers, others) -> int:
         """Moves one tensor's slices through the peers' buffers; returns the chunk length."""
-        if self._peer is None:
-            buf = self.backend.peer_buffer(self._peer_bytes)
-            self._peer = (buf, self.comm.share_buffer(buf))
         buf, addrs = self._peer
         half = self._peer_bytes // 2
         chunk = min(others, max(1, half // (16 * ((1 << self.layout.g) - 1))))
@@ -593,6 +620,10 @@ class ShardedStateVectorSimulator:
             import torch
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
+        if self.transport == "peer" and self._peer is None:
+            self._peer = self._share_peer_buffer()
+            if self._peer is None:
+                self.transport = "p2p"
         if self.transport == "peer":
             for t in tensors:
                 self._peer_swap(t, n_l, lpos, x, peers, others)

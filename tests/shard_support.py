@@ -169,14 +169,13 @@ class ThreadComm:
         self._sync()
         self.hub.barrier.wait()
 
+    same_process = True
+
     def same_node(self):
         return True
 
-    def share_buffer(self, buf):
-        return dict(enumerate(self._gather(buf.address)))
-
-    def unshare_buffers(self, addresses):
-        pass
+    def allgather_object(self, obj):
+        return list(self._gather(obj))
 
 
 def run_threads(size, fn):
@@ -277,6 +276,63 @@ def gloo_batch_worker(rank, size, port, case, queue):
         up = (vals - labels) / len(labels)
         grads = sim.backward(up)
         queue.put((rank, dict(values=vals, grads=grads)))
+    except BaseException as e:  # noqa: BLE001 - reported to the parent
+        queue.put((rank, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+class _FakePeerBuffer:
+    address = 0
+
+    def handle_bytes(self):
+        return bytes(64)
+
+    def destroy(self):
+        pass
+
+
+class FailingPeerBackend(OracleShardBackend):
+    """Offers the peer transport, but rank `fail_rank` cannot create its peer buffer."""
+
+    def __init__(self, oracle_module, rank, fail_rank):
+        super().__init__(oracle_module)
+        self.rank, self.fail_rank = rank, fail_rank
+
+    def peer_buffer(self, nbytes):
+        if self.rank == self.fail_rank:
+            raise RuntimeError("no peer buffer on this rank")
+        return _FakePeerBuffer()
+
+    def gather_from(self, *args):
+        raise AssertionError("the peer transport must not run after a failed setup")
+
+
+def gloo_fallback_worker(rank, size, port, case, queue):
+    """One rank of a gloo world whose peer-transport setup fails on rank 1."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "oracle"), here):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import torch.distributed as dist
+
+    import oracle as O
+    from arcqml_b200.sharded import DistComm, ShardedStateVectorSimulator
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=size, timeout=datetime.timedelta(seconds=120))
+        sim = ShardedStateVectorSimulator(case["n"], comm=DistComm(),
+                                          backend=FailingPeerBackend(O, rank, 1),
+                                          chunk_amplitudes=8, transport="peer")
+        res = sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
+                           case["req"])
+        res["transport"] = sim.transport
+        queue.put((rank, res))
     except BaseException as e:  # noqa: BLE001 - reported to the parent
         queue.put((rank, repr(e)))
     finally:

@@ -244,3 +244,35 @@ def test_gloo_world_row_sharded_batch_matches_oracle(oracle):
         assert not isinstance(out[r], str), out[r]
         close(out[r]["values"], vals)
         close(out[r]["grads"], g[1:])
+
+
+def test_gloo_world_falls_back_when_a_rank_cannot_share_its_buffer(oracle):
+    """Peer-transport setup is collective: one rank failing makes every rank use the
+    point-to-point transport, and the run still matches the oracle."""
+    from shard_support import gloo_fallback_worker
+    n, size = 6, 2
+    rng = np.random.Generator(np.random.PCG64(31))
+    case = dict(n=n, ops=random_plan(rng, n, 60, 6), terms=random_terms(rng, n, 20),
+                init=random_state(rng, n), upstream=0.5,
+                req=[1] + [1] * 6)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=gloo_fallback_worker, args=(r, size, port, case, q))
+          for r in range(size)]
+    for p in ps:
+        p.start()
+    out = {}
+    try:
+        for _ in range(size):
+            r, res = q.get(timeout=300)
+            out[r] = res
+    finally:
+        for p in ps:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(size):
+        assert not isinstance(out[r], str), out[r]
+        assert out[r]["transport"] == "p2p"
+    check_world(out, expected(oracle, case), size)
