@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--forward-only", action="store_true",
                     help="forward + <H> without the adjoint sweep (the 35-qubit sharded config)")
+    ap.add_argument("--workload", default="brickwork", choices=["brickwork", "vqe4", "qnn"],
+                    help="vqe4: the 4-qubit VQE's 100 Adam steps; qnn: the batched QNN gradient")
     return ap.parse_args()
 
 
@@ -368,10 +370,109 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ small configurations
+
+
+def small_arm(args):
+    """One GPU: the 4-qubit VQE (steps of run -> backward -> Adam, lr 0.05, 100 per timed
+    repetition) or the batched QNN (full-batch gradient of 1024 rows x 10 qubits), with the
+    oracle timed on the same work beside it. Device time with CUDA events; these include the
+    host round trips every step makes (values and gradients come back each step)."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from arcqml_b200 import build, runtime as rt, workloads
+    from arcqml_b200.simulator import BatchStateVectorSimulator, StateVectorSimulator
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    build.build()
+    O.build()
+    rt.load()
+    if args.workload == "vqe4":
+        c, obs = workloads.vqe4(seed=1)
+        sim = StateVectorSimulator(4)
+        theta0 = c.parameter_values().astype(np.float64)
+
+        def unit():  # 100 Adam steps
+            theta, st = theta0.copy(), {}
+            for _ in range(100):
+                c.set_parameter_values(theta)
+                res = sim.run(c, obs)
+                g, _ = res.backward(1.0)
+                theta = O.adam_step(theta, np.asarray(g), st, lr=0.05)
+            return res.value
+
+        per_unit, unit_name, metric = 100, "steps/s", "4-qubit VQE Adam steps/s (15-term H)"
+        terms, ops_n = obs.compiled_terms(), 4
+
+        def cpu_unit():
+            theta, st = theta0.copy(), {}
+            init = np.zeros(16, np.complex128)
+            init[0] = 1
+            for _ in range(100):
+                c.set_parameter_values(theta)
+                ops = c.compile_plan(1)
+                psi = O.plan_apply(ops, init, 4)
+                _, lam = O.expectation_and_apply(terms, psi, 4)
+                req = c.requires_grad_mask(True)
+                _, _, g = O.adjoint_backward(ops, psi, lam, 4, 1.0, req, len(req))
+                theta = O.adam_step(theta, g[1:], st, lr=0.05)
+    else:
+        c, obs, init, labels = workloads.qnn(10, 1024, 4, seed=7)
+        sim = BatchStateVectorSimulator.from_amplitudes(10, init)
+
+        def unit():  # one full-batch gradient
+            res = sim.run(c, obs)
+            _, up = workloads.half_mse_upstream(res.values, labels)
+            g, _ = res.backward(up)
+            return float(np.sum(g))
+
+        per_unit, unit_name = 1, "gradients/s"
+        metric = "batched QNN full-batch gradients/s (1024 rows x 10 qubits, 80 parameters)"
+        ops = c.compile_plan(1)
+        terms = obs.compiled_terms()
+        req = c.requires_grad_mask(True, False)
+
+        def cpu_unit():
+            psi = O.plan_apply(ops, init.reshape(-1), 10, 1024).reshape(1024, -1)
+            vals = np.array([O.expectation(terms, psi[i], 10) for i in range(1024)])
+            lam = np.stack([O.expectation_and_apply(terms, psi[i], 10)[1] for i in range(1024)])
+            _, up = workloads.half_mse_upstream(vals, labels)
+            O.adjoint_backward(ops, psi.reshape(-1), lam.reshape(-1), 10, up, req, len(req), 1024)
+    for _ in range(args.warmup):
+        unit()
+    torch.cuda.synchronize()
+    launches0 = rt.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        check = unit()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    launches = rt.launch_count() - launches0
+    if args.workload == "vqe4":
+        O.set_num_threads(1)  # 16 amplitudes: threads only add overhead
+    t0 = time.perf_counter()
+    cpu_unit()
+    cpu_dt = time.perf_counter() - t0
+    line = {"metric": metric, "value": round(per_unit * args.steps / (ms / 1e3), 3),
+            "unit": unit_name, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "complex128 (f64)",
+            "data": "synthetic (seeded workload generator)", "config": {"workload": args.workload},
+            "gpu_launches": launches, "check": check,
+            "cpu_baseline": {"value": round(per_unit / cpu_dt, 3), "unit": unit_name,
+                             "cores": O.num_threads(), "kind": "port",
+                             "sample": f"one unit of the same work on the oracle in {cpu_dt:.3f} s"}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.workload != "brickwork":
+        small_arm(args)
     else:
         gpu_arm(args)
 
