@@ -644,6 +644,29 @@ int32_t arcqml_rt_v2_peer_buffer_destroy(void *device_ptr) {
     });
 }
 
+int32_t arcqml_rt_v2_small_run(const CircuitPlanHandle *plan,
+                               const ArcqmlObservableHandle *observable,
+                               const arcqml_c128 *initial_state, size_t num_qubits,
+                               const uint8_t *parameter_requires_grad,
+                               size_t parameter_requires_grad_len, double *gradients,
+                               size_t gradients_len, double *value, arcqml_c128 *lambda0,
+                               void *stream) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        state_dimension(num_qubits);
+        if (!value) fail("value pointer is null");
+        if (parameter_requires_grad_len && !parameter_requires_grad)
+            fail("requires-grad list is null");
+        if (gradients_len && !gradients) fail("gradient buffer is null");
+        ThreadContext &ctx = thread_context();
+        small_step_device(*p, *obs_of(observable),
+                          reinterpret_cast<const double2 *>(initial_state), uint32_t(num_qubits),
+                          parameter_requires_grad, parameter_requires_grad_len, gradients,
+                          gradients_len, value, reinterpret_cast<double2 *>(lambda0), ctx,
+                          pick_stream(ctx, stream));
+    });
+}
+
 int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
                                       arcqml_c128 *adjoint_state, size_t batch,
                                       size_t num_qubits, const double *upstream,

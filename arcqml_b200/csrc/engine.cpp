@@ -393,20 +393,14 @@ void pauli_traversal_tables(uint32_t n, const std::vector<uint64_t> &flips,
     tr.coset_bits = kCoset;
 }
 
-void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
-                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
-                       bool accumulate) {
-    if (obs.num_qubits != n) {
-        std::ostringstream m;
-        m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
-        fail(m.str());
-    }
-    const size_t nt = obs.coef.size();
+// Observable tables for k_pauli / the one-kernel step in one host block (layout in PauliTables;
+// tab.base left null), followed at `*perm_off` by the traversal tables of an n-qubit state.
+std::vector<double2> pack_pauli(const Observable &obs, uint32_t n, PauliTables &tab,
+                                PauliTraversal &tr, size_t *perm_off) {
     const size_t ng = obs.groups.size();
-    // Pack the tables in one upload (layout in PauliTables), then the traversal tables.
     std::vector<uint64_t> gflips(ng), ptab;
     for (size_t g = 0; g < ng; ++g) gflips[g] = obs.groups[g].flip;
-    PauliTraversal tr;
+    tr = PauliTraversal{};
     pauli_traversal_tables(n, gflips, ptab, tr);
     auto weight = [&](const PauliGroup &grp, uint32_t k) {
         // (-1)^popc((t ^ f) & z) = (-1)^popc(f & z) (-1)^popc(t & z): fold the first factor
@@ -438,7 +432,7 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         }
     }
     me.push_back(uint32_t(mw.size()));
-    PauliTables tab;
+    tab = PauliTables{};
     size_t off = 0;
     auto place = [&](size_t bytes) {
         const size_t at = off;
@@ -468,10 +462,26 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
     put(tab.m_f, mf.data(), mf.size() * 8);
     put(tab.m_e, me.data(), me.size() * 4);
     if (!ptab.empty()) std::memcpy(base + off, ptab.data(), ptab.size() * 8);
+    *perm_off = off;
+    return pack;
+}
+
+void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
+                       uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
+                       bool accumulate) {
+    if (obs.num_qubits != n) {
+        std::ostringstream m;
+        m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
+        fail(m.str());
+    }
+    PauliTables tab;
+    PauliTraversal tr;
+    size_t off = 0;
+    std::vector<double2> pack = pack_pauli(obs, n, tab, tr, &off);
     std::vector<const std::vector<double2> *> refs{&pack};
     auto p = upload_tables(refs, ctx, s);
     const char *dbase = reinterpret_cast<const char *>(p[0]);
-    if (!ptab.empty()) tr.tables = reinterpret_cast<const uint64_t *>(dbase + off);
+    if (tr.ntables) tr.tables = reinterpret_cast<const uint64_t *>(dbase + off);
     tab.base = reinterpret_cast<const unsigned char *>(dbase);
 
     const size_t dim = size_t(1) << n;
@@ -490,6 +500,90 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
         std::memcpy(values_host + b0, h, rows * sizeof(double));
     }
+}
+
+void small_step_device(Plan &plan, Observable &obs, const double2 *init, uint32_t n,
+                       const uint8_t *req, size_t req_len, double *grads_host, size_t grads_len,
+                       double *value_host, double2 *lam0, ThreadContext &ctx, cudaStream_t s) {
+    validate_plan_for_state(plan, n);
+    check_bindings(plan, req_len, grads_len);
+    if (n > kSmallMaxQubits) {
+        std::ostringstream m;
+        m << "the one-kernel step takes states of at most " << kSmallMaxQubits << " qubits";
+        fail(m.str());
+    }
+    if (obs.num_qubits != n) {
+        std::ostringstream m;
+        m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
+        fail(m.str());
+    }
+    // per op: U, U^dagger (dense small form when a slot needs its gradient) and dU/dp per slot
+    std::vector<SmallOp> ops(plan.ops.size());
+    std::vector<std::vector<double2>> dense;  // matrices of custom gates, forward then dagger
+    std::vector<std::pair<size_t, int>> dense_use;  // (op, 0 = u / 1 = ua)
+    std::vector<size_t> parents;  // per output row, in reverse-sweep order
+    for (size_t k = 0; k < plan.ops.size(); ++k) {
+        const OpRecord &op = plan.ops[k];
+        SmallOp &so = ops[k];
+        std::memset(&so, 0, sizeof(so));
+        so.u = lower(op, LOWER_FORWARD, 0);
+        if (so.u.kind == KIND_DENSE) {
+            if (op.qubits.size() > 4) fail("the one-kernel step takes custom gates on at most 4 qubits");
+            dense.push_back(op.custom);
+            dense_use.push_back({k, 0});
+        }
+        int ns = 0;
+        for (uint32_t b = 0; b < op.num_bindings; ++b) {
+            if (!req[op.parents[b]]) continue;
+            DevGate dg = lower(op, LOWER_DERIVATIVE, uint32_t(op.slots[b]), false);
+            for (int i = 0; i < 16; ++i) so.d[ns][i] = dg.m[i];
+            ++ns;
+        }
+        so.ns = ns;
+        so.ua = lower(op, LOWER_ADJOINT, 0, ns == 0);
+        if (so.ua.kind == KIND_DENSE) {
+            dense.push_back(dagger(op.custom, size_t(1) << op.qubits.size()));
+            dense_use.push_back({k, 1});
+        }
+        if (ns > 0 && so.ua.kind != KIND_1Q && so.ua.kind != KIND_2Q)
+            fail("internal: adjoint step needs a dense small form");
+    }
+    for (size_t k = plan.ops.size(); k-- > 0;) {
+        const OpRecord &op = plan.ops[k];
+        for (uint32_t b = 0; b < op.num_bindings; ++b)
+            if (req[op.parents[b]]) parents.push_back(op.parents[b]);
+    }
+    PauliTables tab;
+    PauliTraversal tr;
+    size_t off = 0;
+    std::vector<double2> pauli = pack_pauli(obs, n, tab, tr, &off);
+    // one upload: the op table, the custom matrices, the observable tables
+    std::vector<double2> optab((ops.size() * sizeof(SmallOp) + 15) / 16 + 1);
+    if (!ops.empty()) std::memcpy(optab.data(), ops.data(), ops.size() * sizeof(SmallOp));
+    std::vector<const std::vector<double2> *> refs{&optab, &pauli};
+    for (auto &d : dense) refs.push_back(&d);
+    auto ptrs = upload_tables(refs, ctx, s);
+    if (!dense.empty()) {
+        // patch the device matrix pointers into the op table on the device copy
+        for (size_t j = 0; j < dense.size(); ++j) {
+            SmallOp &so = ops[dense_use[j].first];
+            (dense_use[j].second == 0 ? so.u : so.ua).dense = ptrs[2 + j];
+        }
+        check_cuda(cudaMemcpyAsync(const_cast<double2 *>(ptrs[0]), ops.data(),
+                                   ops.size() * sizeof(SmallOp), cudaMemcpyHostToDevice, s),
+                   "cudaMemcpyAsync (step table)");
+    }
+    tab.base = reinterpret_cast<const unsigned char *>(ptrs[1]);
+    double *out = ctx_dgrads(ctx, 1 + parents.size());
+    launch_small_step(init, n, reinterpret_cast<const SmallOp *>(ptrs[0]),
+                      uint32_t(ops.size()), tab, out, lam0, s);
+    double *h = ctx_hvals(ctx, 1 + parents.size());
+    check_cuda(cudaMemcpyAsync(h, out, (1 + parents.size()) * sizeof(double),
+                               cudaMemcpyDeviceToHost, s),
+               "cudaMemcpyAsync (step results)");
+    check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (value_host) *value_host = h[0];
+    for (size_t j = 0; j < parents.size(); ++j) grads_host[parents[j]] += 2.0 * h[1 + j];
 }
 
 Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,

@@ -58,6 +58,21 @@ void launch_slices_from(double2 *amps, const uint32_t *positions, uint32_t k,
 void launch_sample(const double2 *amps, uint32_t n, uint64_t shots, uint64_t seed, double *cum,
                    uint64_t *out, cudaStream_t s);
 
+// One op of the one-kernel small-state step: U for the forward sweep, U^dagger (a dense small
+// form when slots need gradients) with dU/dp per such slot for the reverse sweep.
+struct SmallOp {
+    DevGate u;
+    DevGate ua;
+    int32_t ns;
+    int32_t pad;
+    double2 d[3][16];
+};
+constexpr uint32_t kSmallMaxQubits = 10;
+// One CTA: psi <- plan |init>, lam <- H psi, out[0] = <H>, then the reverse sweep with
+// out[1 + j] = sum Re<lam| dU/dp |psi> for the j-th (op, slot); lam0 (may be null) <- lambda_0.
+void launch_small_step(const double2 *init, uint32_t n, const SmallOp *ops, uint32_t nops,
+                       const PauliTables &tab, double *out, double2 *lam0, cudaStream_t s);
+
 Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,
                             const uint64_t *phase, size_t num_terms);
 const std::string &last_error();

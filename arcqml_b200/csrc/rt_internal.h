@@ -169,6 +169,13 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
                        uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
                        bool accumulate = false);
 
+// One-kernel run + backward of a small single state (small.cu): value <- <H> after the plan
+// applied to init (null: |0...0>), grads[parent] += 2 Re<lambda| dU/dp |psi> with lambda = H psi,
+// lam0 (may be null) <- lambda_0.
+void small_step_device(Plan &plan, Observable &obs, const double2 *init, uint32_t n,
+                       const uint8_t *req, size_t req_len, double *grads_host, size_t grads_len,
+                       double *value_host, double2 *lam0, ThreadContext &ctx, cudaStream_t s);
+
 // Copies host tables (dense matrices of custom gates) into the context's table buffer;
 // returns device pointers in the same order. Valid until the next call on this thread.
 std::vector<const double2 *> upload_tables(const std::vector<const std::vector<double2> *> &ms,

@@ -124,6 +124,7 @@ def load():
         "arcqml_rt_v2_sample": (I32, [P, S, C.c_uint64, C.c_uint64, P, P, P]),
         "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
                                             I32, P]),
+        "arcqml_rt_v2_small_run": (I32, [P, P, P, S, P, S, P, S, P, P, P]),
         "arcqml_rt_v2_shard_slices_from": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, P, P]),
         "arcqml_rt_v2_peer_buffer_create": (I32, [S, P, P]),
         "arcqml_rt_v2_peer_buffer_open": (I32, [P, P]),
@@ -476,6 +477,25 @@ def adjoint_backward_device(plan: CircuitPlan, psi, lam, num_qubits: int, upstre
         C.byref(plan.raw), _dev_ptr(psi), _dev_ptr(lam), b, num_qubits, up.ctypes.data,
         req.ctypes.data, req.size, grads.ctypes.data, grads.size, _stream_ptr(stream)))
     return grads
+
+
+SMALL_MAX_QUBITS = 10
+
+
+def small_run_device(plan: CircuitPlan, observable: "Observable", initial_state, num_qubits: int,
+                     requires_grad, num_gradients: int, lambda0=None, stream=None):
+    """One-kernel forward + <H> + adjoint (upstream 1) of a small single state; returns
+    (value, gradients). initial_state: device tensor or None for |0...0>; lambda0: optional
+    device tensor receiving lambda at the start of the circuit."""
+    req = np.ascontiguousarray(requires_grad, dtype=np.uint8)
+    grads = np.zeros(num_gradients, dtype=np.float64)
+    value = C.c_double()
+    _status(load().arcqml_rt_v2_small_run(
+        C.byref(plan.raw), C.byref(observable.raw),
+        None if initial_state is None else _dev_ptr(initial_state), num_qubits,
+        req.ctypes.data, req.size, grads.ctypes.data, grads.size, C.byref(value),
+        None if lambda0 is None else _dev_ptr(lambda0), _stream_ptr(stream)))
+    return float(value.value), grads
 
 
 def norms_device(state, num_qubits: int, stream=None) -> np.ndarray:

@@ -56,6 +56,19 @@ class _Context:
     initial_requires_grad: bool
 
 
+@dataclass
+class _SmallContext:
+    """Result of the one-kernel step: gradients for upstream 1 (the sweep is linear in it)."""
+    grads: np.ndarray
+    lam0: object
+    circuit: Circuit
+    initial_requires_grad: bool
+
+
+def _small_enabled() -> bool:
+    return os.environ.get("ARCQML_SMALL", "1") != "0"
+
+
 class RunResult:
     """Output of ``run``: value(s) plus the adjoint context for ``backward``."""
 
@@ -82,11 +95,15 @@ class RunResult:
         if self._ctx is None:
             raise SimError("run was executed without gradient recording")
         c = self._ctx
-        torch = _torch()
-        psi, lam = (c.psi.clone(), c.lam.clone()) if retain else (c.psi, c.lam)
-        req = c.circuit.requires_grad_mask(True, c.initial_requires_grad)
-        grads = rt.adjoint_backward_device(c.plan, psi, lam, c.num_qubits, upstream, req,
-                                           len(req), stream)
+        if isinstance(c, _SmallContext):
+            g = float(np.asarray(upstream, dtype=np.float64).reshape(-1)[0])
+            grads = g * c.grads
+            lam = None if c.lam0 is None else g * c.lam0
+        else:
+            psi, lam = (c.psi.clone(), c.lam.clone()) if retain else (c.psi, c.lam)
+            req = c.circuit.requires_grad_mask(True, c.initial_requires_grad)
+            grads = rt.adjoint_backward_device(c.plan, psi, lam, c.num_qubits, upstream, req,
+                                               len(req), stream)
         pgrads = grads[1:].copy()
         for p, g in zip(c.circuit.parameters, pgrads):
             if p.requires_grad:
@@ -183,6 +200,8 @@ class StateVectorSimulator:
             raise SimError("observable and state qubit counts differ")
         torch = _torch()
         records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
+        if records and self.num_qubits <= rt.SMALL_MAX_QUBITS and _small_enabled():
+            return self._run_small(circuit, observable, initial_state)
         psi = _new_state(self.num_qubits, None, self.device)
         if initial_state is not None:
             src = initial_state if isinstance(initial_state, torch.Tensor) else torch.from_numpy(
@@ -203,6 +222,60 @@ class StateVectorSimulator:
         vals = obs.expectation_and_apply(psi, lam, self.num_qubits)
         return RunResult(vals, _Context(self.num_qubits, None, psi, lam, plan, circuit,
                                         self.initial_requires_grad))
+
+    # -- small states: one kernel for forward, <H> and the adjoint sweep ----------------------
+    def _small_plan(self, circuit: Circuit):
+        """A plan for the circuit's structure, reused across runs with its bound parameter
+        values replaced (plan creation costs more host time than the step itself)."""
+        ops = circuit.compile_plan(1)
+        key = []
+        for o in ops:
+            bound = {slot for slot, _ in o.bindings}
+            fixed = tuple(v for i, v in enumerate(o.params) if i not in bound)
+            mat = None if o.matrix is None else np.asarray(o.matrix, dtype=np.complex128).tobytes()
+            key.append((o.opcode, tuple(o.qubits), tuple(o.bindings), fixed, mat))
+        key = tuple(key)
+        plans = self.__dict__.setdefault("_plans", {})
+        plan = plans.get(key)
+        if plan is None:
+            if len(plans) > 64:
+                plans.clear()
+            plan = rt.CircuitPlan.create(ops)
+            plans[key] = plan
+        else:
+            plan.set_parameters(np.array([0.0] + [p.f64() for p in circuit.parameters]))
+        return plan
+
+    def _small_observable(self, observable: SparsePauliOp):
+        key = tuple(observable.terms)
+        cache = self.__dict__.setdefault("_observables", {})
+        obs = cache.get(key)
+        if obs is None:
+            if len(cache) > 16:
+                cache.clear()
+            obs = rt.Observable.from_sparse_pauli_op(observable)
+            cache[key] = obs
+        return obs
+
+    def _run_small(self, circuit: Circuit, observable: SparsePauliOp, initial_state) -> RunResult:
+        torch = _torch()
+        init = None
+        if initial_state is not None:
+            src = initial_state if isinstance(initial_state, torch.Tensor) else torch.from_numpy(
+                np.ascontiguousarray(initial_state, dtype=np.complex128))
+            if src.numel() != (1 << self.num_qubits) or src.dtype != torch.complex128:
+                raise SimError(f"initial state must be complex128 of shape [{1 << self.num_qubits}]")
+            init = src.reshape(-1).to(self.device, non_blocking=True)
+        elif self._state is not None:
+            init = self._state
+        lam0 = torch.empty(1 << self.num_qubits, dtype=torch.complex128, device=self.device) \
+            if self.initial_requires_grad else None
+        req = circuit.requires_grad_mask(True, self.initial_requires_grad)
+        value, grads = rt.small_run_device(self._small_plan(circuit),
+                                           self._small_observable(observable), init,
+                                           self.num_qubits, req, len(req), lam0)
+        return RunResult(np.array([value]), _SmallContext(grads, lam0, circuit,
+                                                          self.initial_requires_grad))
 
     def _check(self, circuit: Circuit):
         if circuit.num_qubits != self.num_qubits:

@@ -131,6 +131,22 @@ int32_t arcqml_rt_v2_peer_buffer_open(const uint8_t *handle, void **device_ptr);
 int32_t arcqml_rt_v2_peer_buffer_close(void *device_ptr);
 int32_t arcqml_rt_v2_peer_buffer_destroy(void *device_ptr);
 
+/* One-kernel run + backward for a small single state (num_qubits <= 10; no reference
+ * counterpart: it fuses plan apply, expectation_and_apply and adjoint_backward with upstream 1
+ * into one launch and one read-back). psi = plan |initial_state> (device, or NULL for |0...0>),
+ * *value = <psi|H|psi>, gradients[parent] += 2 Re<lambda| dU/dp |psi> over the reverse sweep with
+ * lambda = H psi (as arcqml_rt_v2_adjoint_backward with upstream 1; scale by an upstream factor
+ * afterwards, the sweep is linear in it), and lambda0 (device, may be NULL) <- lambda at the
+ * start of the circuit (the initial state's gradient is 2 * upstream * lambda0). Custom gates
+ * must act on at most 4 qubits. */
+int32_t arcqml_rt_v2_small_run(const CircuitPlanHandle *plan,
+                               const ArcqmlObservableHandle *observable,
+                               const arcqml_c128 *initial_state, size_t num_qubits,
+                               const uint8_t *parameter_requires_grad,
+                               size_t parameter_requires_grad_len, double *gradients,
+                               size_t gradients_len, double *value, arcqml_c128 *lambda0,
+                               void *stream);
+
 /* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);

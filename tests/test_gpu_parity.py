@@ -349,3 +349,37 @@ def test_precompiled_pass_kernels_match_oracle_without_jit(runtime):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
                        timeout=600)
     assert r.returncode == 0 and "aot-ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("n", [2, 3, 6, 10])
+def test_one_kernel_small_step_matches_oracle(runtime, oracle, n):
+    """arcqml_rt_v2_small_run (forward, <H>, adjoint in one launch) against the oracle, with an
+    initial state, controlled and custom gates, shared parameters and lambda_0."""
+    import torch
+    g = np.random.Generator(np.random.PCG64(4000 + n))
+    npar = 7
+    ops = random_plan(g, n, 60, npar)
+    if n >= 3:
+        ops.append(op(38, (0, 2, 1), matrix=random_unitary(g, 3)))
+    if n >= 6:
+        ops.append(op(38, (5, 1, 3, 0), matrix=random_unitary(g, 4)))
+    terms_obj = __import__("arcqml_b200.workloads", fromlist=["x"]).random_pauli_sum(
+        n, 12, seed=n + 40)
+    init = random_state(g, n)
+    req = [1] + [int(x) for x in (g.uniform(size=npar) < 0.8)]
+    plan = runtime.CircuitPlan.create(ops)
+    obs = runtime.Observable.from_sparse_pauli_op(terms_obj)
+    dev = torch.from_numpy(init).cuda()
+    lam0 = torch.empty_like(dev)
+    value, grads = runtime.small_run_device(plan, obs, dev, n, req, len(req), lam0)
+    ref_psi = oracle.plan_apply(ops, init, n)
+    ref_v, ref_lam = oracle.expectation_and_apply(terms_obj.compiled_terms(), ref_psi, n)
+    _, ref_lam0, ref_g = oracle.adjoint_backward(ops, ref_psi, ref_lam, n, 1.0, req, len(req))
+    rel_close(value, ref_v)
+    rel_close(grads, ref_g)
+    rel_close(lam0.cpu().numpy(), ref_lam0)
+    # |0...0> when no initial state is given
+    v0, _ = runtime.small_run_device(plan, obs, None, n, req, len(req))
+    z = np.zeros(1 << n, np.complex128)
+    z[0] = 1
+    rel_close(v0, oracle.expectation(terms_obj.compiled_terms(), oracle.plan_apply(ops, z, n), n))
