@@ -14,7 +14,6 @@ C ABI:
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 from typing import Optional, Sequence, Tuple, Union
 

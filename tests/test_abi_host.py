@@ -1,6 +1,5 @@
 """C-ABI checks that need no GPU: exports, struct layouts, validation, host-only entry points."""
 import ctypes as C
-import math
 import os
 import re
 import subprocess

@@ -1,6 +1,5 @@
 """Device sampling (arcqml_rt_v2_sample) against the oracle: shot indices and the running
 total bit for bit (needs a B200)."""
-import math
 
 import numpy as np
 import pytest

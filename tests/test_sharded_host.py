@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from arcqml_b200.circuit import PlanOp
-from arcqml_b200.sharded import (Layout, OpsStep, ShardError, SwapStep, TermsStep, flip_groups,
+from arcqml_b200.sharded import (Layout, ShardError, SwapStep, TermsStep, flip_groups,
                                  local_terms, schedule_ops, schedule_terms)
 from arcqml_b200.workloads import brickwork, random_pauli_sum
 from plans import random_plan, random_state, random_terms
