@@ -1,7 +1,8 @@
 """The oracle's sampling restatement (crates/arcqml-sim/src/statevector/api/measurement.rs:18-60).
 
 Pins: the ChaCha block function against RFC 7539's test vectors (section 2.3.2 and appendix
-A.1 #1, ChaCha20); the reference's own sampling tests (Bell state, 1000 shots, seed 42: only
+A.1 #1, ChaCha20) and against OpenSSL's ChaCha20 for random keys and 64-bit counter and stream
+words; the reference's own sampling tests (Bell state, 1000 shots, seed 42: only
 "00" and "11", counts summing to 1000 — run_tests.rs:280-295, python/tests/api/single.rs:140-166);
 and the oracle's bisection against a literal restatement of the reference's per-shot linear scan.
 StdRng's seed expansion and stream layout come from crates the reference does not ship
@@ -23,6 +24,23 @@ def test_chacha20_rfc7539_vectors(oracle):
     blk = oracle.chacha_block(key, 1 | (0x09000000 << 32), 0x4A000000, 20)
     out = b"".join(x.to_bytes(4, "little") for x in blk)
     assert out.hex()[:64] == "10f1e7e4d13b5915500fdd1fa32071c4c7d1f4c733c068030422aa9ac3d46c4e"
+
+
+def test_chacha20_matches_openssl_for_random_keys_and_64_bit_words(oracle):
+    """An independent ChaCha20 (OpenSSL through the cryptography package, whose 16-byte IV is
+    state words 12-15) agrees block for block, with counter and stream words above 2^32."""
+    import struct
+
+    import pytest
+    algs = pytest.importorskip("cryptography.hazmat.primitives.ciphers")
+    rng = np.random.Generator(np.random.PCG64(77))
+    for _ in range(64):
+        key = [int(x) for x in rng.integers(0, 2**32, 8, dtype=np.uint64)]
+        ctr, stream = (int(x) for x in rng.integers(0, 2**63, 2, dtype=np.uint64))
+        iv = struct.pack("<4I", ctr & 0xFFFFFFFF, ctr >> 32, stream & 0xFFFFFFFF, stream >> 32)
+        enc = algs.Cipher(algs.algorithms.ChaCha20(struct.pack("<8I", *key), iv), mode=None)
+        words = list(struct.unpack("<16I", enc.encryptor().update(bytes(64))))
+        assert words == oracle.chacha_block(key, ctr, stream, 20)
 
 
 def test_bell_state_counts_like_reference_test(oracle):
