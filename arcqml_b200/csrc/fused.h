@@ -78,9 +78,11 @@ struct FOp {
     uint32_t acc[3];         // pass-local accumulator index per slot
     uint8_t code;            // FastCode
     uint8_t gcode;           // GradFast
-    uint8_t pad0[2];
+    uint8_t sform;           // compiled passes: apply the unit-diagonal form of mats[soff]
+    uint8_t sgrad;           // compiled passes: gradient factor in mats[soff].y
     uint64_t gcmask;         // controls outside the tile (global positions)
-    uint32_t pad[6];
+    uint32_t soff;           // scaled-pass entry: (tau, 0.5 |sigma|^2 before the op)
+    uint32_t pad[5];
 };
 static_assert(sizeof(FOp) == 64, "FOp layout");
 

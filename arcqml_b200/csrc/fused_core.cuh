@@ -149,47 +149,121 @@ __device__ __forceinline__ void f_m4(double2 (&v)[1 << RB], const double2 *mt) {
     }
 }
 
+// Scaled unit-diagonal forms (compiled scaled passes; the factor the planner took out of each
+// op is carried by the pass as one scalar): one FMA per component.
+// RX-form c [[1, -it], [-it, 1]]
 template <int RB, int B>
-__device__ __forceinline__ double g_x(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
+__device__ __forceinline__ void fs_rx(double2 (&v)[1 << RB], double t) {
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
         if (e & (1 << B)) continue;
         const int f = e | (1 << B);
-        z += icm(w[e], v[f]) + icm(w[f], v[e]);
+        const double2 x0 = v[e], x1 = v[f];
+        v[e] = make_double2(fma(t, x1.y, x0.x), fma(-t, x1.x, x0.y));
+        v[f] = make_double2(fma(t, x0.y, x1.x), fma(-t, x0.x, x1.y));
     }
-    return z;
+}
+
+// RY-form c [[1, -t], [t, 1]]
+template <int RB, int B>
+__device__ __forceinline__ void fs_ry(double2 (&v)[1 << RB], double t) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        const double2 x0 = v[e], x1 = v[f];
+        v[e] = make_double2(fma(-t, x1.x, x0.x), fma(-t, x1.y, x0.y));
+        v[f] = make_double2(fma(t, x0.x, x1.x), fma(t, x0.y, x1.y));
+    }
+}
+
+// x (1 + i t)
+__device__ __forceinline__ double2 one_plus_it(double2 x, double t) {
+    return make_double2(fma(-t, x.y, x.x), fma(t, x.x, x.y));
+}
+
+// diag(1 - i tau, 1 + i tau) on register bit B
+template <int RB, int B>
+__device__ __forceinline__ void fs_d1_reg(double2 (&v)[1 << RB], double tau) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) v[e] = one_plus_it(v[e], ((e >> B) & 1) ? tau : -tau);
+}
+
+// (1 + i t) on every element (t = +-tau by the thread's bit of the qubit)
+template <int RB>
+__device__ __forceinline__ void fs_d1_uni(double2 (&v)[1 << RB], double t) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) v[e] = one_plus_it(v[e], t);
+}
+
+// The pass's factor sigma, multiplied in once before the tile is written back.
+template <int RB>
+__device__ __forceinline__ void fs_scale(double2 (&v)[1 << RB], double2 sigma) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) v[e] = cmul(sigma, v[e]);
+}
+
+// Gradient sums Im<lam|P|psi> and Re-forms over the thread's elements: one FMA per product
+// term (2 FP64 instructions per amplitude), four partial sums for independent chains.
+template <int RB, int B>
+__device__ __forceinline__ double g_x(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
+    double z[4] = {0.0, 0.0, 0.0, 0.0};
+    int k = 0;
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const int f = e | (1 << B);
+        double &a = z[(k & 1) * 2], &b = z[(k & 1) * 2 + 1];
+        a = fma(w[e].x, v[f].y, a);
+        a = fma(-w[e].y, v[f].x, a);
+        b = fma(w[f].x, v[e].y, b);
+        b = fma(-w[f].y, v[e].x, b);
+        ++k;
+    }
+    return (z[0] + z[1]) + (z[2] + z[3]);
 }
 
 template <int RB, int B>
 __device__ __forceinline__ double g_y(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
+    double z[4] = {0.0, 0.0, 0.0, 0.0};
+    int k = 0;
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
         if (e & (1 << B)) continue;
         const int f = e | (1 << B);
-        z += rcm(w[f], v[e]) - rcm(w[e], v[f]);
+        double &a = z[(k & 1) * 2], &b = z[(k & 1) * 2 + 1];
+        a = fma(w[f].x, v[e].x, a);
+        a = fma(w[f].y, v[e].y, a);
+        b = fma(-w[e].x, v[f].x, b);
+        b = fma(-w[e].y, v[f].y, b);
+        ++k;
     }
-    return z;
+    return (z[0] + z[1]) + (z[2] + z[3]);
 }
 
 template <int RB, int B>
 __device__ __forceinline__ double g_z(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
+    double z[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
-        const double t = icm(w[e], v[e]);
-        z += ((e >> B) & 1) ? -t : t;
+        const bool neg = (e >> B) & 1;  // compile-time: folds into the FMA operands
+        double &a = z[e & 3];
+        a = fma(neg ? -w[e].x : w[e].x, v[e].y, a);
+        a = fma(neg ? w[e].y : -w[e].y, v[e].x, a);
     }
-    return z;
+    return (z[0] + z[1]) + (z[2] + z[3]);
 }
 
 template <int RB>
 __device__ __forceinline__ double g_z_uni(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z = 0.0;
+    double z[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-    for (int e = 0; e < (1 << RB); ++e) z += icm(w[e], v[e]);
-    return z;
+    for (int e = 0; e < (1 << RB); ++e) {
+        double &a = z[e & 3];
+        a = fma(w[e].x, v[e].y, a);
+        a = fma(-w[e].y, v[e].x, a);
+    }
+    return (z[0] + z[1]) + (z[2] + z[3]);
 }
 
 

@@ -168,6 +168,21 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
     const bool uses_b0 = o.code != FC_D1_UNI && o.code != FC_SIGN_CC;
     const bool uses_b1 = o.code == FC_SIGN_RR || o.code == FC_M4;
     if ((uses_b0 && b0 >= int(rb)) || (uses_b1 && b1 >= int(rb))) return false;
+    const uint32_t so = o.soff;
+    if (o.sform) {  // scaled unit-diagonal form (mats[soff].x = t or tau)
+        switch (o.code) {
+        case FC_RX: c << "fs_rx<RB, " << b0 << ">(" << r << ", M[" << so << "].x);"; return true;
+        case FC_RY: c << "fs_ry<RB, " << b0 << ">(" << r << ", M[" << so << "].x);"; return true;
+        case FC_D1_REG:
+            c << "fs_d1_reg<RB, " << b0 << ">(" << r << ", M[" << so << "].x);";
+            return true;
+        case FC_D1_UNI:
+            c << "fs_d1_uni<RB>(" << r << ", " << bit0 << " ? M[" << so << "].x : -M[" << so
+              << "].x);";
+            return true;
+        default: return false;
+        }
+    }
     switch (o.code) {
     case FC_RX:
         c << "f_rx<RB, " << b0 << ">(" << r << ", M[" << m << "].x, M[" << m << "].y);";
@@ -223,8 +238,11 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
     if (!emit_apply(c, o, "v", rb, S, tbits)) return false;
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb, S, tbits)) return false;
+    // 0.5 * z, times |sigma|^2 in a scaled pass
     c << "\n        " << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
-      << o.acc[0] << "u * kCols, 0.5 * z); }";
+      << o.acc[0] << "u * kCols, ";
+    if (o.sgrad) c << "M[" << o.soff << "].y * z); }";
+    else c << "0.5 * z); }";
     return true;
 }
 
@@ -274,6 +292,11 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
             const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb, S, kb)
                                 : emit_apply(c, st.ops[oi], "v", rb, S, kb);
             if (!ok) return std::string();
+            c << "\n";
+        }
+        if (st.scaled && sb + 1 == st.subs.size()) {
+            c << "        fs_scale<RB>(v, M[" << st.sfin << "]);";
+            if (adj) c << " fs_scale<RB>(w, M[" << st.sfin << "]);";
             c << "\n";
         }
         for (uint32_t e = 0; e < slot.size(); ++e) {

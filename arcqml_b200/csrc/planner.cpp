@@ -136,6 +136,96 @@ void mul2(const double2 a[4], const double2 b[4], double2 out[4]) {  // out = a 
         }
 }
 
+// FK_RX or FK_RY when a 2x2 (row-major) is [[c, -is], [-is, c]] or [[c, -s], [s, c]] with real
+// c and s (the patterns the op emitter stores as (c, s)), else 0.
+int rotation_form(const double2 m[4]) {
+    const bool same_diag = eq(m[0], m[3]) && m[0].y == 0.0;
+    if (same_diag && m[1].x == 0.0 && eq(m[1], m[2])) return FK_RX;
+    if (same_diag && m[1].y == 0.0 && m[2].y == 0.0 && m[1].x == -m[2].x) return FK_RY;
+    return 0;
+}
+
+// Whether a 2x2 (row-major) has a scaled unit-diagonal form: an RX- or RY-form rotation or a
+// diagonal with |d0| = |d1| (what scale_pass below rewrites).
+bool scalable_1q(const double2 m[4]) {
+    if (rotation_form(m) != 0) return true;
+    if (m[1].x != 0.0 || m[1].y != 0.0 || m[2].x != 0.0 || m[2].y != 0.0) return false;
+    const double a0 = std::hypot(m[0].x, m[0].y), a3 = std::hypot(m[3].x, m[3].y);
+    return a0 > 0.0 && std::fabs(a0 - a3) <= 1e-14 * a0;
+}
+
+double2 cmulh(double2 a, double2 b) {
+    return make_double2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+
+// Scaled pass (compiled kernels; FOp::sform/sgrad/soff, Step::scaled/sfin). A Pauli rotation or
+// a unitary one-qubit diagonal is f * M with M's diagonal 1 (RY: c [[1, -t], [t, 1]], t = s/c;
+// RX: c [[1, -it], [-it, 1]]; diag(d0, d1) = f diag(1 - i tau, 1 + i tau) with
+// tau = tan(arg(d1/d0) / 2), f = d0 cos(g) e^{ig}), so applying M costs one FMA per component
+// (2 FP64 instructions per amplitude instead of 4) and the factors f collect in one scalar sigma
+// per pass: true state = sigma * stored state. psi and lambda of an adjoint pass get the same
+// daggered ops, so they carry the same sigma and <lam|P|psi> = |sigma|^2 <lam~|P|psi~>: each
+// gradient is multiplied by 0.5 |sigma|^2 at its op instead of 0.5. Ops without such a form run
+// as they are (a scalar commutes with every linear op). The growth of 1/|sigma| is capped at
+// 2^300 per pass (and 2^30 per op), far from the f64 range even for the squared factor.
+void scale_pass(Step &st, bool adjoint) {
+    if (!scaled_passes()) return;
+    for (const SubBlock &sb : st.subs)
+        if (!(sb.flags & SB_ALL_FAST)) return;  // runs on the table-driven kernel
+    const size_t base = st.mats.size();
+    std::vector<double2> extra;
+    double2 sigma = make_double2(1.0, 0.0);
+    double growth = 0.0;  // log2(1 / |sigma|)
+    bool any = false;
+    for (FOp &o : st.ops) {
+        const double2 *m = st.mats.data() + o.moff;
+        bool sc = false;
+        double tau = 0.0;
+        double2 f = make_double2(1.0, 0.0);
+        if ((o.code == FC_RX || o.code == FC_RY) && m[0].x != 0.0) {
+            tau = m[0].y / m[0].x;
+            f = make_double2(m[0].x, 0.0);
+            sc = true;
+        } else if (o.code == FC_D1_REG || o.code == FC_D1_UNI) {
+            const double a0 = std::hypot(m[0].x, m[0].y), a1 = std::hypot(m[1].x, m[1].y);
+            if (a0 > 0.0 && std::fabs(a0 - a1) <= 1e-14 * a0) {
+                // r = d1 / d0 = e^{2ig}
+                const double2 r = make_double2((m[1].x * m[0].x + m[1].y * m[0].y) / (a0 * a0),
+                                               (m[1].y * m[0].x - m[1].x * m[0].y) / (a0 * a0));
+                const double g = 0.5 * std::atan2(r.y, r.x);
+                tau = std::tan(g);
+                f = cmulh(m[0], make_double2(std::cos(g) * std::cos(g), std::cos(g) * std::sin(g)));
+                sc = true;
+            }
+        }
+        if (sc) {
+            const double gr = -std::log2(std::hypot(f.x, f.y));
+            if (!std::isfinite(tau) || !(gr <= 30.0) || growth + gr > 300.0) sc = false;
+            else growth += gr;
+        }
+        const bool grad = adjoint && o.gkind != GK_NONE;
+        o.sform = sc ? 1 : 0;
+        o.sgrad = grad ? 1 : 0;
+        o.soff = 0;
+        if (sc || grad) {
+            o.soff = uint32_t(base + extra.size());
+            extra.push_back(make_double2(tau, 0.5 * (sigma.x * sigma.x + sigma.y * sigma.y)));
+        }
+        if (sc) {
+            sigma = cmulh(sigma, f);
+            any = true;
+        }
+    }
+    if (!any || base + extra.size() + 1 > size_t(kMaxPassMats)) {
+        for (FOp &o : st.ops) o.sform = o.sgrad = 0, o.soff = 0;
+        return;
+    }
+    st.sfin = uint32_t(base + extra.size());
+    extra.push_back(sigma);
+    st.mats.insert(st.mats.end(), extra.begin(), extra.end());
+    st.scaled = true;
+}
+
 // Chooses the op's specialised device path (fused.h FastCode). reg_of(q) is the register bit
 // of qubit q in the current sub-block (0xFF if none); lpos[q] its tile bit (-1 if outside).
 template <class RegOf>
@@ -203,6 +293,14 @@ bool has_fast_path(const FOp &o, bool adjoint) {
 inline int residue(int bit) { return bit % 3; }
 
 }  // namespace
+
+bool scaled_passes() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_SCALED");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
 
 // Gates per pass: kMaxPassOps, or fewer with ARCQML_PASS_OPS=<count> (smaller compiled kernels).
 size_t pass_op_cap() {
@@ -355,24 +453,42 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 return 0xFF;
             };
             // Forward passes merge consecutive uncontrolled single-qubit gates on the same qubit
-            // (nothing else touching it in between) into one 2x2: same arithmetic, fewer ops.
+            // (nothing else touching it in between) into one 2x2: same arithmetic, fewer ops —
+            // except two rotation-like gates in scaled passes (2 + 2 FP64 instructions per
+            // amplitude apart, 8 as one dense 2x2) unless they make a diagonal.
             int last1q[64];
             for (int q = 0; q < 64; ++q) last1q[q] = -1;
             for (size_t gi : subs[sb]) {
                 const PGate &g = gates[gi];
                 const bool mergeable = !adjoint && g.controls.empty() && g.targets.size() == 1 &&
                                        g.gkind == GK_NONE;
-                if (mergeable && last1q[g.targets[0]] >= 0) {
-                    FOp &e = st.ops[size_t(last1q[g.targets[0]])];
-                    double2 ue[4], un[4], p[4];
-                    op_matrix2(e, st.mats, ue);
+                bool merge = mergeable && last1q[g.targets[0]] >= 0;
+                double2 ue[4], un[4], p[4];
+                bool pdiag = false;
+                if (merge) {
+                    op_matrix2(st.ops[size_t(last1q[g.targets[0]])], st.mats, ue);
                     for (int i = 0; i < 4; ++i) un[i] = g.m[i];
                     mul2(un, ue, p);  // the earlier gate acts first
-                    const bool pdiag = p[1].x == 0 && p[1].y == 0 && p[2].x == 0 && p[2].y == 0;
+                    pdiag = p[1].x == 0 && p[1].y == 0 && p[2].x == 0 && p[2].y == 0;
+                    const bool to_diag = pdiag &&
+                                         st.ops[size_t(last1q[g.targets[0]])].kind == FK_D1;
+                    if (scaled_passes() && !to_diag && rotation_form(p) == 0 &&
+                        scalable_1q(ue) && scalable_1q(un))
+                        merge = false;
+                }
+                if (merge) {
+                    FOp &e = st.ops[size_t(last1q[g.targets[0]])];
                     e.moff = uint32_t(st.mats.size());
+                    const int rot = e.kind == FK_D1 ? 0 : rotation_form(p);
                     if (pdiag && e.kind == FK_D1) {
                         st.mats.push_back(p[0]);
                         st.mats.push_back(p[3]);
+                    } else if (rot != 0) {  // RX(a) RX(b), RY(a) RY(b): one rotation again
+                        e.kind = uint8_t(rot);
+                        e.code = rot == FK_RX ? FC_RX : FC_RY;
+                        e.rb0 = reg_of(g.targets[0]);
+                        if (e.rb0 == 0xFF) fail("internal: merged gate without a register target");
+                        st.mats.push_back(make_double2(p[0].x, rot == FK_RX ? -p[1].y : p[2].x));
                     } else {
                         const uint8_t r = reg_of(g.targets[0]);
                         if (r == 0xFF) fail("internal: merged gate without a register target");
@@ -457,6 +573,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 if (!has_fast_path(st.ops[oi], adjoint)) s.flags = 0;
             st.subs.push_back(s);
         }
+        scale_pass(st, adjoint);
         h.nsub = uint32_t(st.subs.size());
         h.nops = uint32_t(st.ops.size());
         h.nmat = uint32_t(st.mats.size());

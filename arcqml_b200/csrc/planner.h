@@ -16,6 +16,10 @@ struct Step {
     std::vector<FOp> ops;
     std::vector<double2> mats;
     std::vector<size_t> parents;         // per accumulator of the pass (adjoint)
+    // Scaled pass (compiled kernels only): the state in the tile carries a common factor sigma,
+    // true = sigma * stored, multiplied in once at the end from mats[sfin].
+    bool scaled = false;
+    uint32_t sfin = 0;
 };
 
 struct Schedule {
@@ -29,6 +33,10 @@ struct Schedule {
 // every bound slot whose parent has req[parent] != 0 gets an accumulator.
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb);
+
+// Whether compiled passes run Pauli rotations and unitary one-qubit diagonals in their scaled
+// unit-diagonal forms (ARCQML_SCALED=0 turns it off).
+bool scaled_passes();
 
 // Runs a schedule on device states (fused.cu). psi/lam are [batch, 2^n]; lam is null in
 // forward mode. Accumulator partials go to partials[acc * partial_stride + block].

@@ -322,6 +322,66 @@ def test_compiled_pass_kernels_run_and_match_oracle(runtime, oracle):
     rel_close(grads, ref_g)
 
 
+EDGE_ANGLES = (math.pi, -math.pi, math.pi * (1 - 1e-9), 3 * math.pi, math.pi / 2, 0.0, 1e-300,
+               -2.9999, 2.9999)
+
+
+def test_scaled_passes_with_edge_angles_match_oracle(runtime, oracle):
+    """Compiled passes carry a per-pass factor for rotations in unit-diagonal form: angles at
+    and near pi (forms refused, cos(theta/2) ~ 1e-17), long runs of near-pi rotations (the
+    2^300 growth cap), same-axis pairs merged in forward passes, fixed phase gates (S, T, Z)
+    and rotation-diagonal products, forward and adjoint against the oracle."""
+    import torch
+    n = 14
+    g = np.random.Generator(np.random.PCG64(31))
+    c = cm.Circuit(n)
+    for layer in range(12):
+        for q in range(n):
+            for _ in range(2):
+                axis = ("rx", "ry", "rz")[int(g.integers(0, 3))]
+                a = EDGE_ANGLES[int(g.integers(0, len(EDGE_ANGLES)))] if g.uniform() < 0.6 \
+                    else float(g.uniform(-math.pi, math.pi))
+                c.rot(axis, a, q)
+            if g.uniform() < 0.3:
+                c.append(("s", "t", "z", "sdg")[int(g.integers(0, 4))], (q,))
+            if g.uniform() < 0.2:
+                c.append("phase", (q,), float(EDGE_ANGLES[int(g.integers(0, len(EDGE_ANGLES)))]))
+        for a in range(layer % 2, n - 1, 2):
+            c.append("cz", (a, a + 1))
+    # a long run of rotations on one qubit at pi (1 - 1e-9): growth ~30 bits each
+    for _ in range(40):
+        c.rot("ry", math.pi * (1 - 1e-9), 3)
+    obs = cm_random_sum(n, 25, seed=32)
+    ops = c.compile_plan(1)
+    req = c.requires_grad_mask(True)
+    init = random_state(g, n)
+    before = runtime.jit_info()
+    plan = runtime.CircuitPlan.create(ops)
+    psi = torch.from_numpy(init.copy()).cuda()
+    runtime.plan_apply_device(plan, psi, n)
+    lam = torch.empty_like(psi)
+    ro = runtime.Observable.from_sparse_pauli_op(obs)
+    value = ro.expectation_and_apply(psi, lam, n)[0]
+    fwd = psi.cpu().numpy()
+    grads = runtime.adjoint_backward_device(plan, psi, lam, n, -1.5, req, len(req))
+    after = runtime.jit_info()
+    assert after["launches"] > before["launches"], after
+    ref_psi = oracle.plan_apply(ops, init, n)
+    ref_v, ref_lam = oracle.expectation_and_apply(obs.compiled_terms(), ref_psi, n)
+    ref_psi0, ref_lam0, ref_g = oracle.adjoint_backward(ops, ref_psi, ref_lam, n, -1.5, req,
+                                                        len(req))
+    assert float(np.max(np.abs(fwd - ref_psi))) < 1e-12
+    rel_close(value, ref_v)
+    rel_close(grads, ref_g)
+    rel_close(lam.cpu().numpy(), ref_lam0)
+    assert float(np.max(np.abs(psi.cpu().numpy() - init))) < 1e-10
+
+
+def cm_random_sum(n, terms, seed):
+    from arcqml_b200.workloads import random_pauli_sum
+    return random_pauli_sum(n, terms, seed=seed)
+
+
 def test_precompiled_pass_kernels_match_oracle_without_jit(runtime):
     """With ARCQML_JIT=0 every pass runs the precompiled table-driven kernel (subprocess)."""
     import os
