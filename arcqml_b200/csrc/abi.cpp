@@ -667,6 +667,29 @@ int32_t arcqml_rt_v2_small_run(const CircuitPlanHandle *plan,
     });
 }
 
+int32_t arcqml_rt_v2_small_adam(const CircuitPlanHandle *plan,
+                                const ArcqmlObservableHandle *observable,
+                                const arcqml_c128 *initial_state, size_t num_qubits,
+                                const uint8_t *parameter_requires_grad, double *parameters,
+                                size_t num_parameters, double *adam_m, double *adam_v,
+                                uint64_t steps_taken, size_t steps, double learning_rate,
+                                double beta1, double beta2, double epsilon, double weight_decay,
+                                double *energies, void *stream) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        state_dimension(num_qubits);
+        SmallAdam h{learning_rate, beta1, beta2, epsilon, weight_decay};
+        Observable &obs = *obs_of(observable);
+        validate_small_adam(*p, obs, uint32_t(num_qubits), parameter_requires_grad,
+                            num_parameters, parameters, steps, h, energies);
+        ThreadContext &ctx = thread_context();
+        small_adam_device(*p, obs, reinterpret_cast<const double2 *>(initial_state),
+                          uint32_t(num_qubits), parameter_requires_grad, num_parameters,
+                          parameters, adam_m, adam_v, steps_taken, steps, h, energies, ctx,
+                          pick_stream(ctx, stream));
+    });
+}
+
 int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128 *forward_state,
                                       arcqml_c128 *adjoint_state, size_t batch,
                                       size_t num_qubits, const double *upstream,

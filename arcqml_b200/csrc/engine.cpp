@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <sstream>
 #include <unordered_map>
 
@@ -584,6 +585,212 @@ void small_step_device(Plan &plan, Observable &obs, const double2 *init, uint32_
     check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
     if (value_host) *value_host = h[0];
     for (size_t j = 0; j < parents.size(); ++j) grads_host[parents[j]] += 2.0 * h[1 + j];
+}
+
+namespace {
+
+// Opcodes whose one parameter the device optimizer loop rebuilds on the device: the Pauli
+// rotations U = cos(t/2) a1 + sin(t/2) a2 and the phase gates U = a0 + cos(t) a1 + sin(t) a2.
+bool loop_rotation(uint32_t opcode) {
+    return (opcode >= 11 && opcode <= 13) || (opcode >= 23 && opcode <= 25) ||
+           (opcode >= 30 && opcode <= 33);
+}
+bool loop_phase(uint32_t opcode) { return opcode == 14 || opcode == 22; }
+
+}  // namespace
+
+std::vector<OpRecord> validate_small_adam(const Plan &plan, const Observable &obs, uint32_t n,
+                                          const uint8_t *req, size_t req_len,
+                                          const double *params, size_t steps, const SmallAdam &h,
+                                          const double *energies) {
+    validate_plan_for_state(plan, n);
+    check_bindings(plan, req_len, req_len);
+    if (n > kSmallMaxQubits) {
+        std::ostringstream m;
+        m << "the optimizer loop takes states of at most " << kSmallMaxQubits << " qubits";
+        fail(m.str());
+    }
+    if (obs.num_qubits != n) {
+        std::ostringstream m;
+        m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
+        fail(m.str());
+    }
+    if (req_len == 0 || !req || !params) fail("parameter arrays are empty or null");
+    if (req_len > (size_t(1) << 20)) fail("too many parameters for the optimizer loop");
+    if (steps == 0 || steps > (size_t(1) << 24)) fail("step count must be in 1..2^24");
+    if (!energies) fail("energy buffer is null");
+    if (!std::isfinite(h.lr) || !(h.beta1 >= 0.0 && h.beta1 < 1.0) ||
+        !(h.beta2 >= 0.0 && h.beta2 < 1.0) || !std::isfinite(h.eps) || h.eps < 0.0 ||
+        !std::isfinite(h.weight_decay))
+        fail("invalid Adam hyperparameters (finite lr and weight decay, 0 <= beta < 1, eps >= 0)");
+    for (size_t p = 0; p < req_len; ++p)
+        if (!std::isfinite(params[p])) fail("parameter values must be finite");
+    // the plan's ops with every bound slot set from params (the plan itself stays as it is)
+    std::vector<OpRecord> rec(plan.ops);
+    for (auto &op : rec)
+        for (uint32_t b = 0; b < op.num_bindings; ++b) op.params[op.slots[b]] = params[op.parents[b]];
+    for (const auto &op : rec) {
+        bool trained = false;
+        for (uint32_t b = 0; b < op.num_bindings; ++b) trained = trained || req[op.parents[b]];
+        if (!trained) continue;
+        if (!(loop_rotation(op.opcode) || loop_phase(op.opcode)) || op.num_bindings != 1) {
+            std::ostringstream m;
+            m << "the optimizer loop rebuilds only one-parameter rotation and phase gates on the "
+                 "device; op with opcode "
+              << op.opcode << " has a trained parameter";
+            fail(m.str());
+        }
+    }
+    return rec;
+}
+
+void small_adam_device(const Plan &plan, Observable &obs, const double2 *init, uint32_t n,
+                       const uint8_t *req, size_t req_len, double *params, double *adam_m,
+                       double *adam_v, uint64_t t0, size_t steps, const SmallAdam &h,
+                       double *energies, ThreadContext &ctx, cudaStream_t s) {
+    const std::vector<OpRecord> rec =
+        validate_small_adam(plan, obs, n, req, req_len, params, steps, h, energies);
+
+    // --- tables: ops (trained ones as dense small forms), their parameter forms, rows
+    std::vector<SmallOp> ops(rec.size());
+    std::vector<SmallParamOp> pops;
+    std::vector<std::vector<double2>> dense;
+    std::vector<std::pair<size_t, int>> dense_use;
+    for (size_t k = 0; k < rec.size(); ++k) {
+        const OpRecord &op = rec[k];
+        SmallOp &so = ops[k];
+        std::memset(&so, 0, sizeof(so));
+        const bool trained = op.num_bindings == 1 && req[op.parents[0]];
+        so.u = lower(op, LOWER_FORWARD, 0, !trained);
+        if (so.u.kind == KIND_DENSE) {
+            if (op.qubits.size() > 4) fail("the optimizer loop takes custom gates on at most 4 qubits");
+            dense.push_back(op.custom);
+            dense_use.push_back({k, 0});
+        }
+        so.ns = trained ? 1 : 0;
+        so.ua = lower(op, LOWER_ADJOINT, 0, !trained);
+        if (so.ua.kind == KIND_DENSE) {
+            dense.push_back(dagger(op.custom, size_t(1) << op.qubits.size()));
+            dense_use.push_back({k, 1});
+        }
+        if (!trained) continue;
+        if (so.u.kind != KIND_1Q && so.u.kind != KIND_2Q) fail("internal: loop op without a dense form");
+        const DevGate dg = lower(op, LOWER_DERIVATIVE, uint32_t(op.slots[0]), false);
+        for (int i = 0; i < 16; ++i) so.d[0][i] = dg.m[i];
+        SmallParamOp P;
+        std::memset(&P, 0, sizeof(P));
+        P.op = uint32_t(k);
+        P.parent = uint32_t(op.parents[0]);
+        P.slot_row = 0;
+        P.dim = so.u.kind == KIND_2Q ? 4 : 2;
+        OpRecord zero = op;
+        zero.params[op.slots[0]] = 0.0;
+        const DevGate u0 = lower(zero, LOWER_FORWARD, 0, false);
+        const DevGate d0 = lower(zero, LOWER_DERIVATIVE, uint32_t(op.slots[0]), false);
+        const int dd = P.dim * P.dim;
+        if (loop_rotation(op.opcode)) {  // U(0) = a1, dU/dt(0) = a2 / 2
+            P.alpha = 0.5;
+            for (int i = 0; i < dd; ++i) {
+                P.a1[i] = u0.m[i];
+                P.a2[i] = make_double2(2.0 * d0.m[i].x, 2.0 * d0.m[i].y);
+            }
+        } else {  // diag(1, e^{it}): a2 = dU/dt(0), a1 = U(0) where a2 is non-zero, a0 the rest
+            P.alpha = 1.0;
+            for (int i = 0; i < dd; ++i) {
+                P.a2[i] = d0.m[i];
+                const bool on = d0.m[i].x != 0.0 || d0.m[i].y != 0.0;
+                P.a1[i] = on ? u0.m[i] : make_double2(0.0, 0.0);
+                P.a0[i] = on ? make_double2(0.0, 0.0) : u0.m[i];
+            }
+        }
+        // the forms must reproduce the host's own matrices at the current value
+        const double t = op.params[op.slots[0]];
+        const double c = std::cos(P.alpha * t), sn = std::sin(P.alpha * t);
+        for (int i = 0; i < dd; ++i) {
+            const double rx = P.a0[i].x + c * P.a1[i].x + sn * P.a2[i].x;
+            const double ry = P.a0[i].y + c * P.a1[i].y + sn * P.a2[i].y;
+            if (std::fabs(rx - so.u.m[i].x) > 1e-14 || std::fabs(ry - so.u.m[i].y) > 1e-14)
+                fail("internal: optimizer-loop matrix form does not reproduce the gate");
+        }
+        pops.push_back(P);
+    }
+    std::vector<uint32_t> row_parent, trained;
+    for (size_t k = rec.size(); k-- > 0;)
+        if (ops[k].ns) row_parent.push_back(uint32_t(rec[k].parents[0]));
+    for (size_t p = 1; p < req_len; ++p)
+        if (req[p]) trained.push_back(uint32_t(p));
+    const uint32_t np = uint32_t(req_len);
+    const size_t smem = small_adam_smem(n, uint32_t(ops.size()), np);
+    int dev = 0, optin = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    check_cuda(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
+               "cudaDeviceGetAttribute");
+    if (smem + 1024 > size_t(optin)) {
+        std::ostringstream m;
+        m << "the optimizer loop keeps the state, the op table and the parameters in shared "
+             "memory: "
+          << rec.size() << " ops and " << req_len << " parameters need " << smem
+          << " bytes, the device allows " << optin;
+        fail(m.str());
+    }
+
+    // --- one upload: op table, parameter forms, index lists, bias corrections, observable,
+    // custom matrices, theta / m / v
+    auto words = [](const void *src, size_t bytes) {
+        std::vector<double2> v((bytes + 15) / 16 + 1);
+        if (bytes) std::memcpy(v.data(), src, bytes);
+        return v;
+    };
+    std::vector<double2> optab = words(ops.data(), ops.size() * sizeof(SmallOp));
+    std::vector<double2> ptab = words(pops.data(), pops.size() * sizeof(SmallParamOp));
+    std::vector<uint32_t> idx(row_parent);
+    idx.insert(idx.end(), trained.begin(), trained.end());
+    std::vector<double2> itab = words(idx.data(), idx.size() * sizeof(uint32_t));
+    std::vector<double2> bc(steps);
+    for (size_t i = 0; i < steps; ++i) {
+        const double t = double(t0 + i + 1);
+        bc[i] = make_double2(1.0 - std::pow(h.beta1, t), 1.0 - std::pow(h.beta2, t));
+    }
+    std::vector<double> st(3 * size_t(np), 0.0);
+    std::memcpy(st.data(), params, np * sizeof(double));
+    if (adam_m) std::memcpy(st.data() + np, adam_m, np * sizeof(double));
+    if (adam_v) std::memcpy(st.data() + 2 * size_t(np), adam_v, np * sizeof(double));
+    std::vector<double2> stab = words(st.data(), st.size() * sizeof(double));
+    PauliTables tab;
+    PauliTraversal tr;
+    size_t off = 0;
+    std::vector<double2> pauli = pack_pauli(obs, n, tab, tr, &off);
+    std::vector<const std::vector<double2> *> refs{&optab, &ptab, &itab, &bc, &pauli, &stab};
+    for (auto &d : dense) refs.push_back(&d);
+    auto ptrs = upload_tables(refs, ctx, s);
+    if (!dense.empty()) {
+        for (size_t j = 0; j < dense.size(); ++j) {
+            SmallOp &so = ops[dense_use[j].first];
+            (dense_use[j].second == 0 ? so.u : so.ua).dense = ptrs[6 + j];
+        }
+        check_cuda(cudaMemcpyAsync(const_cast<double2 *>(ptrs[0]), ops.data(),
+                                   ops.size() * sizeof(SmallOp), cudaMemcpyHostToDevice, s),
+                   "cudaMemcpyAsync (loop table)");
+    }
+    tab.base = reinterpret_cast<const unsigned char *>(ptrs[4]);
+    const uint32_t *ip = reinterpret_cast<const uint32_t *>(ptrs[2]);
+    double *state = reinterpret_cast<double *>(const_cast<double2 *>(ptrs[5]));
+    double *dev_e = ctx_dgrads(ctx, steps);
+    launch_small_adam(init, n, reinterpret_cast<const SmallOp *>(ptrs[0]), uint32_t(ops.size()),
+                      reinterpret_cast<const SmallParamOp *>(ptrs[1]), uint32_t(pops.size()), ip,
+                      ip + row_parent.size(), uint32_t(trained.size()), np, tab, h,
+                      reinterpret_cast<const double *>(ptrs[3]), uint32_t(steps), state, dev_e, s);
+    double *hb = ctx_hvals(ctx, steps + 3 * size_t(np));
+    check_cuda(cudaMemcpyAsync(hb, dev_e, steps * sizeof(double), cudaMemcpyDeviceToHost, s),
+               "cudaMemcpyAsync (energies)");
+    check_cuda(cudaMemcpyAsync(hb + steps, state, 3 * size_t(np) * sizeof(double),
+                               cudaMemcpyDeviceToHost, s),
+               "cudaMemcpyAsync (parameters)");
+    check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    std::memcpy(energies, hb, steps * sizeof(double));
+    std::memcpy(params, hb + steps, np * sizeof(double));
+    if (adam_m) std::memcpy(adam_m, hb + steps + np, np * sizeof(double));
+    if (adam_v) std::memcpy(adam_v, hb + steps + 2 * size_t(np), np * sizeof(double));
 }
 
 Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,

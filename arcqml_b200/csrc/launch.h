@@ -73,6 +73,31 @@ constexpr uint32_t kSmallMaxQubits = 10;
 void launch_small_step(const double2 *init, uint32_t n, const SmallOp *ops, uint32_t nops,
                        const PauliTables &tab, double *out, double2 *lam0, cudaStream_t s);
 
+// A trained op of the device optimizer loop: its one bound slot's parameter is `parent` and its
+// dense small form (D = dim) is U(t) = a0 + cos(alpha t) a1 + sin(alpha t) a2 (rotations:
+// alpha = 1/2, a0 = 0; phase gates: alpha = 1); dU/dt goes to d[slot_row] of the op.
+struct SmallParamOp {
+    uint32_t op, parent;
+    int32_t slot_row, dim;
+    double alpha, pad;
+    double2 a0[16], a1[16], a2[16];
+};
+struct SmallAdam {
+    double lr, beta1, beta2, eps, weight_decay;
+};
+// Dynamic shared memory of the loop: psi, lambda, the op table, theta / m / v / grad per parent.
+size_t small_adam_smem(uint32_t n, uint32_t nops, uint32_t nparents);
+// `steps` steps of: U, U^dagger and dU/dp of the trained ops from the parameters; forward, <H>,
+// reverse sweep (as launch_small_step); grad[parent] = sum 2 x rows (row_parent[j] per row);
+// energies[step] = <H>; Adam on the parents in `trained` with bias corrections
+// bc[2 step] = 1 - beta1^t, bc[2 step + 1] = 1 - beta2^t. state = theta, m, v per parent
+// (nparents each), read at the start and written at the end.
+void launch_small_adam(const double2 *init, uint32_t n, const SmallOp *ops, uint32_t nops,
+                       const SmallParamOp *pops, uint32_t npops, const uint32_t *row_parent,
+                       const uint32_t *trained, uint32_t ntrained, uint32_t nparents,
+                       const PauliTables &tab, const SmallAdam &h, const double *bc,
+                       uint32_t steps, double *state, double *energies, cudaStream_t s);
+
 Observable *make_observable(size_t num_qubits, const double *coef, const uint64_t *flip,
                             const uint64_t *phase, size_t num_terms);
 const std::string &last_error();

@@ -176,6 +176,22 @@ void small_step_device(Plan &plan, Observable &obs, const double2 *init, uint32_
                        const uint8_t *req, size_t req_len, double *grads_host, size_t grads_len,
                        double *value_host, double2 *lam0, ThreadContext &ctx, cudaStream_t s);
 
+// Device optimizer loop (small.cu): `steps` Adam steps of <H> over the parameters (parent
+// indexed, params[0..req_len) in and out; req[p] != 0 marks a trained parameter, p >= 1), each
+// step forward + <H> + adjoint + Adam in one CTA; energies[i] = <H> before update i. adam_m /
+// adam_v (may be null: zero) continue an optimizer that has taken t0 steps.
+struct SmallAdam;
+// Argument checks of small_adam_device (host only, no CUDA call); returns the plan's ops with
+// their bound slots set from params.
+std::vector<OpRecord> validate_small_adam(const Plan &plan, const Observable &obs, uint32_t n,
+                                          const uint8_t *req, size_t req_len,
+                                          const double *params, size_t steps, const SmallAdam &h,
+                                          const double *energies);
+void small_adam_device(const Plan &plan, Observable &obs, const double2 *init, uint32_t n,
+                       const uint8_t *req, size_t req_len, double *params, double *adam_m,
+                       double *adam_v, uint64_t t0, size_t steps, const SmallAdam &h,
+                       double *energies, ThreadContext &ctx, cudaStream_t s);
+
 // Copies host tables (dense matrices of custom gates) into the context's table buffer;
 // returns device pointers in the same order. Valid until the next call on this thread.
 std::vector<const double2 *> upload_tables(const std::vector<const std::vector<double2> *> &ms,

@@ -1,4 +1,5 @@
-// small.cu — one-kernel run + backward for small single states (n <= kSmallMaxQubits).
+// small.cu — one-kernel run + backward for small single states (n <= kSmallMaxQubits), and the
+// device optimizer loop built on it.
 //
 // A 16-amplitude VQE state is bound by launches and host round trips, not by arithmetic: the
 // per-gate path issues ~40 launches and two synchronisations per step. Here one CTA holds psi
@@ -128,26 +129,22 @@ __device__ double s_observable(const double2 *psi, double2 *lam, uint32_t n, con
     return s_block_sum(ev, red);
 }
 
-// out[0] = <H>; out[1 + j] = sum over the state of Re<lambda| dU/dp |psi> for the j-th
-// (op, slot) of the reverse sweep; lam0 (optional) receives lambda at the start of the circuit.
-__global__ void __launch_bounds__(kSmallThreads)
-    k_small_step(const double2 *__restrict__ init, uint32_t n, const SmallOp *__restrict__ ops,
-                 uint32_t nops, const __grid_constant__ PauliTables T, double *__restrict__ out,
-                 double2 *__restrict__ lam0) {
-    extern __shared__ __align__(16) double2 s_state[];
-    __shared__ double red[kSmallThreads / 32];
+// The step on psi and lambda in shared memory: psi <- plan |init> (null: |0...0>), lambda <- H psi,
+// then the reverse sweep; rows(j, sum) is called in every thread with the block sum of
+// Re<lambda| dU/dp |psi> for the j-th (op, slot) of the sweep. Returns <H> (in every thread).
+template <class Rows>
+__device__ double small_body(double2 *psi, double2 *lam, const double2 *init, uint32_t n,
+                             const SmallOp *ops, uint32_t nops, const PauliTables &T, double *red,
+                             Rows rows) {
     const uint32_t dim = 1u << n;
-    double2 *psi = s_state;
-    double2 *lam = s_state + dim;
     for (uint32_t t = threadIdx.x; t < dim; t += blockDim.x)
-        psi[t] = init ? init[t] : make_double2(t == 0 ? 1.0 : 0.0, 0.0);  // null: |0...0>
+        psi[t] = init ? init[t] : make_double2(t == 0 ? 1.0 : 0.0, 0.0);
     __syncthreads();
     for (uint32_t k = 0; k < nops; ++k) {
         s_apply(psi, n, ops[k].u);
         __syncthreads();
     }
     const double value = s_observable(psi, lam, n, T, red);
-    if (threadIdx.x == 0) out[0] = value;
     __syncthreads();
     uint32_t row = 0;
     for (uint32_t k = nops; k-- > 0;) {
@@ -199,26 +196,150 @@ __global__ void __launch_bounds__(kSmallThreads)
             }
         }
         __syncthreads();
-        for (int sl = 0; sl < o.ns; ++sl) {
-            const double sum = s_block_sum(acc[sl], red);
-            if (threadIdx.x == 0) out[1 + row] = sum;
-            ++row;
-        }
+        for (int sl = 0; sl < o.ns; ++sl) rows(row++, s_block_sum(acc[sl], red));
     }
+    return value;
+}
+
+// out[0] = <H>; out[1 + j] = sum over the state of Re<lambda| dU/dp |psi> for the j-th
+// (op, slot) of the reverse sweep; lam0 (optional) receives lambda at the start of the circuit.
+__global__ void __launch_bounds__(kSmallThreads)
+    k_small_step(const double2 *__restrict__ init, uint32_t n, const SmallOp *__restrict__ ops,
+                 uint32_t nops, const __grid_constant__ PauliTables T, double *__restrict__ out,
+                 double2 *__restrict__ lam0) {
+    extern __shared__ __align__(16) double2 s_state[];
+    __shared__ double red[kSmallThreads / 32];
+    const uint32_t dim = 1u << n;
+    double2 *psi = s_state;
+    double2 *lam = s_state + dim;
+    const double value = small_body(psi, lam, init, n, ops, nops, T, red,
+                                    [&](uint32_t row, double sum) {
+                                        if (threadIdx.x == 0) out[1 + row] = sum;
+                                    });
+    if (threadIdx.x == 0) out[0] = value;
     if (lam0)
         for (uint32_t t = threadIdx.x; t < dim; t += blockDim.x) lam0[t] = lam[t];
 }
 
+// Adam's update of one parameter, each operation rounded on its own (no contraction), in the
+// order of the f64 Adam of crates/arcqml-optim/src/adam.rs:190-240 (coupled L2 weight decay,
+// bias-corrected moments): bc1 = 1 - beta1^t, bc2 = 1 - beta2^t come from the host.
+__device__ __forceinline__ void adam_update(double &theta, double &m, double &v, double g,
+                                            const SmallAdam &h, double bc1, double bc2) {
+    const double adj = __dadd_rn(g, __dmul_rn(h.weight_decay, theta));
+    m = __dadd_rn(__dmul_rn(h.beta1, m), __dmul_rn(__dsub_rn(1.0, h.beta1), adj));
+    v = __dadd_rn(__dmul_rn(h.beta2, v), __dmul_rn(__dmul_rn(__dsub_rn(1.0, h.beta2), adj), adj));
+    const double mh = __ddiv_rn(m, bc1), vh = __ddiv_rn(v, bc2);
+    theta = __dsub_rn(theta, __ddiv_rn(__dmul_rn(h.lr, mh), __dadd_rn(__dsqrt_rn(vh), h.eps)));
+}
+
+// `steps` optimizer steps in one CTA: per step the trained ops' U, U^dagger and dU/dp from the
+// current parameters (U = a0 + cos(alpha t) a1 + sin(alpha t) a2), the step of small_body, the
+// gradient of every parent summed over its rows (x 2, reverse-sweep order), energies[step] = <H>
+// and Adam on the trained parents. theta / adam_m / adam_v are indexed by parent (in and out).
+__global__ void __launch_bounds__(kSmallThreads)
+    k_small_adam(const double2 *__restrict__ init, uint32_t n, const SmallOp *__restrict__ ops_g,
+                 uint32_t nops, const SmallParamOp *__restrict__ pops, uint32_t npops,
+                 const uint32_t *__restrict__ row_parent, const uint32_t *__restrict__ trained,
+                 uint32_t ntrained, uint32_t nparents, const __grid_constant__ PauliTables T,
+                 SmallAdam h, const double *__restrict__ bc, uint32_t steps,
+                 double *__restrict__ state, double *__restrict__ energies) {
+    extern __shared__ __align__(16) double2 s_state[];
+    __shared__ double red[kSmallThreads / 32];
+    const uint32_t dim = 1u << n;
+    double2 *psi = s_state;
+    double2 *lam = s_state + dim;
+    SmallOp *ops = reinterpret_cast<SmallOp *>(lam + dim);
+    double *th = reinterpret_cast<double *>(ops + nops);  // theta, m, v, grad per parent
+    double *am = th + nparents, *av = am + nparents, *gr = av + nparents;
+    {
+        const uint32_t words = nops * uint32_t(sizeof(SmallOp) / sizeof(double2));
+        const double2 *src = reinterpret_cast<const double2 *>(ops_g);
+        double2 *dst = reinterpret_cast<double2 *>(ops);
+        for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+        for (uint32_t i = threadIdx.x; i < 3 * nparents; i += blockDim.x) th[i] = state[i];
+    }
+    __syncthreads();
+    for (uint32_t step = 0; step < steps; ++step) {
+        for (uint32_t j = threadIdx.x; j < npops; j += blockDim.x) {
+            const SmallParamOp &P = pops[j];
+            SmallOp &o = ops[P.op];
+            double sn, cs;
+            sincos(P.alpha * th[P.parent], &sn, &cs);
+            const int D = P.dim;
+            for (int i = 0; i < D * D; ++i) {
+                const double2 a0 = P.a0[i], a1 = P.a1[i], a2 = P.a2[i];
+                o.u.m[i] = make_double2(fma(sn, a2.x, fma(cs, a1.x, a0.x)),
+                                        fma(sn, a2.y, fma(cs, a1.y, a0.y)));
+                o.d[P.slot_row][i] = make_double2(P.alpha * fma(cs, a2.x, -sn * a1.x),
+                                                  P.alpha * fma(cs, a2.y, -sn * a1.y));
+            }
+            for (int r = 0; r < D; ++r)  // U^dagger[r][c] = conj(U[c][r])
+                for (int c = 0; c < D; ++c) {
+                    const double2 x = o.u.m[c * D + r];
+                    o.ua.m[r * D + c] = make_double2(x.x, -x.y);
+                }
+        }
+        for (uint32_t i = threadIdx.x; i < nparents; i += blockDim.x) gr[i] = 0.0;
+        __syncthreads();
+        const double value = small_body(psi, lam, init, n, ops, nops, T, red,
+                                        [&](uint32_t row, double sum) {
+                                            if (threadIdx.x == 0)
+                                                gr[row_parent[row]] += 2.0 * sum;
+                                        });
+        if (threadIdx.x == 0) {
+            energies[step] = value;
+            for (uint32_t i = 0; i < ntrained; ++i) {
+                const uint32_t p = trained[i];
+                adam_update(th[p], am[p], av[p], gr[p], h, bc[2 * step], bc[2 * step + 1]);
+            }
+        }
+        __syncthreads();
+    }
+    for (uint32_t i = threadIdx.x; i < 3 * nparents; i += blockDim.x) state[i] = th[i];
+}
+
 }  // namespace
+
+// One warp up to 64 amplitudes (half of the groups of a one-qubit gate per thread), then up to
+// kSmallThreads threads.
+static uint32_t small_threads(uint32_t n) {
+    const uint32_t half = n >= 1 ? 1u << (n - 1) : 1u;
+    return half < 32u ? 32u : (half > uint32_t(kSmallThreads) ? uint32_t(kSmallThreads) : half);
+}
 
 void launch_small_step(const double2 *init, uint32_t n, const SmallOp *ops, uint32_t nops,
                        const PauliTables &tab, double *out, double2 *lam0, cudaStream_t s) {
     if (n > kSmallMaxQubits) fail("internal: state too large for the one-kernel step");
     const size_t smem = size_t(2) * (size_t(1) << n) * sizeof(double2);
     const ProfToken tok = prof_begin(PROF_OTHER, s);
-    k_small_step<<<1, kSmallThreads, smem, s>>>(init, n, ops, nops, tab, out, lam0);
+    k_small_step<<<1, small_threads(n), smem, s>>>(init, n, ops, nops, tab, out, lam0);
     prof_end(tok, s, 16.0 * double(size_t(1) << n));
     check_cuda(cudaGetLastError(), "one-kernel step launch");
+}
+
+size_t small_adam_smem(uint32_t n, uint32_t nops, uint32_t nparents) {
+    return size_t(2) * (size_t(1) << n) * sizeof(double2) + size_t(nops) * sizeof(SmallOp) +
+           size_t(4) * nparents * sizeof(double);
+}
+
+void launch_small_adam(const double2 *init, uint32_t n, const SmallOp *ops, uint32_t nops,
+                       const SmallParamOp *pops, uint32_t npops, const uint32_t *row_parent,
+                       const uint32_t *trained, uint32_t ntrained, uint32_t nparents,
+                       const PauliTables &tab, const SmallAdam &h, const double *bc,
+                       uint32_t steps, double *state, double *energies, cudaStream_t s) {
+    if (n > kSmallMaxQubits) fail("internal: state too large for the one-kernel step");
+    const size_t smem = small_adam_smem(n, nops, nparents);
+    static_assert(sizeof(SmallOp) % sizeof(double2) == 0, "SmallOp copies as double2 words");
+    check_cuda(cudaFuncSetAttribute(k_small_adam, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)),
+               "cudaFuncSetAttribute (optimizer loop)");
+    const ProfToken tok = prof_begin(PROF_OTHER, s);
+    k_small_adam<<<1, small_threads(n), smem, s>>>(init, n, ops, nops, pops, npops, row_parent,
+                                                   trained, ntrained, nparents, tab, h, bc, steps,
+                                                   state, energies);
+    prof_end(tok, s, 16.0 * double(size_t(1) << n) * double(steps));
+    check_cuda(cudaGetLastError(), "optimizer loop launch");
 }
 
 }  // namespace arcqml

@@ -125,6 +125,8 @@ def load():
         "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
                                             I32, P]),
         "arcqml_rt_v2_small_run": (I32, [P, P, P, S, P, S, P, S, P, P, P]),
+        "arcqml_rt_v2_small_adam": (I32, [P, P, P, S, P, P, S, P, P, C.c_uint64, S, D, D, D, D,
+                                          D, P, P]),
         "arcqml_rt_v2_shard_slices_from": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, P, P]),
         "arcqml_rt_v2_peer_buffer_create": (I32, [S, P, P]),
         "arcqml_rt_v2_peer_buffer_open": (I32, [P, P]),
@@ -496,6 +498,44 @@ def small_run_device(plan: CircuitPlan, observable: "Observable", initial_state,
         req.ctypes.data, req.size, grads.ctypes.data, grads.size, C.byref(value),
         None if lambda0 is None else _dev_ptr(lambda0), _stream_ptr(stream)))
     return float(value.value), grads
+
+
+class AdamState:
+    """Moments of the device optimizer loop (per parent index) and the steps taken so far."""
+
+    def __init__(self, num_parameters: int):
+        self.m = np.zeros(num_parameters, dtype=np.float64)
+        self.v = np.zeros(num_parameters, dtype=np.float64)
+        self.step = 0
+
+
+def small_adam_device(plan: CircuitPlan, observable: "Observable", num_qubits: int, parameters,
+                      requires_grad, steps: int, lr: float = 0.05,
+                      betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
+                      initial_state=None, state: "AdamState" = None, stream=None):
+    """`steps` Adam steps of <H> in one launch (arcqml_rt_v2_small_adam): per step forward, <H>,
+    adjoint gradient and the f64 Adam update on the device. parameters and requires_grad are
+    indexed by parent (entry 0: the initial-state slot). Returns (energies before each update,
+    parameters after the last one); `state` (AdamState) is advanced in place when given."""
+    req = np.ascontiguousarray(requires_grad, dtype=np.uint8)
+    params = np.array(parameters, dtype=np.float64, copy=True)
+    if params.shape != req.shape:
+        raise ValueError("parameters and requires_grad must have the same length")
+    energies = np.zeros(max(int(steps), 0), dtype=np.float64)
+    if state is not None and (state.m.size != params.size or state.v.size != params.size):
+        raise ValueError("AdamState size does not match the parameters")
+    _status(load().arcqml_rt_v2_small_adam(
+        C.byref(plan.raw), C.byref(observable.raw),
+        None if initial_state is None else _dev_ptr(initial_state), num_qubits,
+        req.ctypes.data, params.ctypes.data, params.size,
+        None if state is None else state.m.ctypes.data,
+        None if state is None else state.v.ctypes.data,
+        0 if state is None else int(state.step), int(steps), float(lr), float(betas[0]),
+        float(betas[1]), float(eps), float(weight_decay),
+        energies.ctypes.data if energies.size else None, _stream_ptr(stream)))
+    if state is not None:
+        state.step += int(steps)
+    return energies, params
 
 
 def norms_device(state, num_qubits: int, stream=None) -> np.ndarray:

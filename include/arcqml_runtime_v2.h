@@ -147,6 +147,28 @@ int32_t arcqml_rt_v2_small_run(const CircuitPlanHandle *plan,
                                size_t gradients_len, double *value, arcqml_c128 *lambda0,
                                void *stream);
 
+/* Device optimizer loop for a small single state (num_qubits <= 10; no reference counterpart:
+ * it runs `steps` iterations of the loop a caller writes around arcqml_rt_v2_small_run — run,
+ * backward with upstream 1, then the f64 Adam step of crates/arcqml-optim/src/adam.rs:190-240 —
+ * in one launch). parameters[num_parameters] is indexed by parent (as the requires-grad list;
+ * entry 0 is the initial-state slot and is never updated): read as the starting values, written
+ * with the values after the last step. Parameters with parameter_requires_grad[p] != 0 (p >= 1)
+ * are trained; every op with such a parameter must be a one-parameter rotation (RX, RY, RZ,
+ * CRX, CRY, CRZ, RXX, RYY, RZZ, RZX) or phase gate (PHASE, CPHASE). energies[i] = <H> before
+ * update i (host, `steps` entries). adam_m / adam_v (host, num_parameters each, may be NULL for
+ * zero moments and then not written) carry the moments of an optimizer that has taken
+ * steps_taken steps (bias corrections use t = steps_taken + i + 1). initial_state: device, or
+ * NULL for |0...0>. The op table, state and parameters must fit in one CTA's shared memory
+ * (an error names the sizes). */
+int32_t arcqml_rt_v2_small_adam(const CircuitPlanHandle *plan,
+                                const ArcqmlObservableHandle *observable,
+                                const arcqml_c128 *initial_state, size_t num_qubits,
+                                const uint8_t *parameter_requires_grad, double *parameters,
+                                size_t num_parameters, double *adam_m, double *adam_v,
+                                uint64_t steps_taken, size_t steps, double learning_rate,
+                                double beta1, double beta2, double epsilon, double weight_decay,
+                                double *energies, void *stream);
+
 /* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);
