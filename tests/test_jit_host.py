@@ -21,3 +21,41 @@ def test_jit_check_rejects_small_states(runtime):
     plan = runtime.CircuitPlan.create(c.compile_plan(1))
     with pytest.raises(runtime.RuntimeError, match="below 8 qubits"):
         plan.jit_check(4, False)
+
+
+def test_scaled_and_plain_rotation_forms_compile(runtime):
+    """Passes mixing scaled rotation forms with the plain forms kept for angles at pi (and
+    past the per-pass growth cap) compile, forward and adjoint; ARCQML_SCALED=0 (subprocess)
+    compiles the all-plain sources."""
+    import math
+    import os
+    import subprocess
+    import sys
+
+    from arcqml_b200 import circuit as cm
+    c = cm.Circuit(12)
+    for layer in range(6):
+        for q in range(12):
+            c.rot(("rx", "ry", "rz")[(q + layer) % 3], math.pi if q % 4 == 0 else 0.3 * q, q)
+            c.append("phase", (q,), math.pi * (1 - 1e-9))  # fixed: no gradient slot
+        for a in range(layer % 2, 11, 2):
+            c.append("cz", (a, a + 1))
+    for _ in range(30):
+        c.rot("ry", math.pi * (1 - 1e-9), 5)
+    plan = runtime.CircuitPlan.create(c.compile_plan(1))
+    for adjoint in (False, True):
+        r = plan.jit_check(12, adjoint)
+        if r["eligible"] == 0 and "not found" in r["message"]:
+            pytest.skip("NVRTC is not available: " + r["message"])
+        assert r["eligible"] >= 1 and r["compiled"] == r["eligible"], r["message"]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from arcqml_b200 import runtime as rt, workloads as W\n"
+            "p = rt.CircuitPlan.create(W.brickwork(10, 3, seed=5).compile_plan(1))\n"
+            "for adj in (False, True):\n"
+            "    r = p.jit_check(10, adj)\n"
+            "    assert r['compiled'] == r['eligible'] >= 1, r\n"
+            "print('plain-ok')\n") % root
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_SCALED="0"), timeout=600)
+    assert r.returncode == 0 and "plain-ok" in r.stdout, r.stdout + r.stderr
