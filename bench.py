@@ -29,6 +29,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -124,7 +125,9 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # samples go to ARCQML_CLOCKS_DIR when set (to keep them), else the temp directory
+        out_dir = os.environ.get("ARCQML_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
