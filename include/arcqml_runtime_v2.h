@@ -205,12 +205,6 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
                                          int32_t adjoint, uint64_t *passes, uint64_t *sub_blocks,
                                          uint64_t *gates);
 
-/* Run-time compiled pass kernels (no reference counterpart). Fused passes whose gates all have
- * fast paths run as kernels compiled for the circuit's structure (NVRTC, sm_100a) and cached per
- * device; ARCQML_JIT=0 in the environment keeps every pass on the precompiled kernel. Reports the
- * kernels compiled, the launches of compiled kernels and the passes that fell back to the
- * precompiled kernel since the library was loaded, and copies the last compile or load error
- * (NUL-terminated, at most capacity - 1 bytes); returns that message's length. */
 /* Generates the run-time kernels of the plan's fused passes for an n-qubit state (forward, or
  * the adjoint sweep when adjoint != 0) and compiles them with NVRTC without loading them: needs
  * no GPU. compiled / eligible receive the passes that compiled and the passes that have a
@@ -218,6 +212,12 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
 int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qubits,
                                     int32_t adjoint, uint64_t *compiled, uint64_t *eligible,
                                     char *message, size_t capacity);
+/* Run-time compiled pass kernels (no reference counterpart). Fused passes whose gates all have
+ * fast paths run as kernels compiled for the circuit's structure (NVRTC, sm_100a) and cached per
+ * device; ARCQML_JIT=0 in the environment keeps every pass on the precompiled kernel. Reports the
+ * kernels compiled, the launches of compiled kernels and the passes that fell back to the
+ * precompiled kernel since the library was loaded, and copies the last compile or load error
+ * (NUL-terminated, at most capacity - 1 bytes); returns that message's length. */
 size_t arcqml_rt_v2_jit_info(uint64_t *kernels_compiled, uint64_t *launches, uint64_t *fallbacks,
                              char *last_error, size_t capacity);
 
