@@ -707,3 +707,83 @@ int oracle_sample_indices(const oc128 *amps, uint32_t num_qubits, uint64_t shots
     free(cum);
     return 0;
 }
+
+/* ---------------------------------------------------------------- analysis
+ * crates/arcqml-analysis/src/statevector/{probabilities,marginal,bloch,fidelity}.rs. */
+
+/* probabilities.rs:22-25: square(abs(amplitude)); abs of a Complex64 is re.hypot(im). */
+void oracle_probabilities(const oc128 *amps, uint32_t num_qubits, double *out) {
+    const size_t dim = (size_t)1 << num_qubits;
+    for (size_t i = 0; i < dim; ++i) {
+        const double h = hypot(amps[i].re, amps[i].im);
+        out[i] = h * h;
+    }
+}
+
+/* marginal.rs:17-32 and :62-67: display order = selected qubits descending; output index bit j
+ * (counted from the most significant) is the basis index's bit display[j]; segment sums in
+ * basis-index order. Returns non-zero for an empty, duplicate or out-of-range selection. */
+int oracle_marginal_probabilities(const oc128 *amps, uint32_t num_qubits, const uint32_t *qubits,
+                                  size_t num_selected, double *out) {
+    if (num_selected == 0 || num_selected > num_qubits) return 1;
+    uint32_t disp[64];
+    for (size_t j = 0; j < num_selected; ++j) {
+        if (qubits[j] >= num_qubits) return 2;
+        for (size_t m = 0; m < j; ++m)
+            if (qubits[m] == qubits[j]) return 3;
+        disp[j] = qubits[j];
+    }
+    for (size_t a = 0; a < num_selected; ++a)  /* descending */
+        for (size_t b = a + 1; b < num_selected; ++b)
+            if (disp[b] > disp[a]) {
+                const uint32_t t = disp[a];
+                disp[a] = disp[b];
+                disp[b] = t;
+            }
+    const size_t dim = (size_t)1 << num_qubits, bins = (size_t)1 << num_selected;
+    for (size_t m = 0; m < bins; ++m) out[m] = 0.0;
+    for (size_t i = 0; i < dim; ++i) {
+        size_t m = 0;
+        for (size_t j = 0; j < num_selected; ++j) m = (m << 1) | ((i >> disp[j]) & 1u);
+        const double h = hypot(amps[i].re, amps[i].im);
+        out[m] += h * h;
+    }
+    return 0;
+}
+
+/* bloch.rs:23-56: x += 2 Re(conj(a0) a1), y += 2 Im(conj(a0) a1), z += |a0|^2 - |a1|^2 over the
+ * index pairs (a0, a1) of the qubit, in index order. */
+int oracle_bloch_vector(const oc128 *amps, uint32_t num_qubits, uint32_t qubit, double xyz[3]) {
+    if (qubit >= num_qubits) return 1;
+    const size_t dim = (size_t)1 << num_qubits, mask = (size_t)1 << qubit;
+    double x = 0.0, y = 0.0, z = 0.0;
+    for (size_t i = 0; i < dim; ++i) {
+        if (i & mask) continue;
+        const oc128 a0 = amps[i], a1 = amps[i | mask];
+        const double cre = a0.re * a1.re + a0.im * a1.im;
+        const double cim = a0.re * a1.im - a0.im * a1.re;
+        x += 2.0 * cre;
+        y += 2.0 * cim;
+        z += (a0.re * a0.re + a0.im * a0.im) - (a1.re * a1.re + a1.im * a1.im);
+    }
+    xyz[0] = x;
+    xyz[1] = y;
+    xyz[2] = z;
+    return 0;
+}
+
+/* fidelity.rs:14-30: overlap = sum(conj(lhs) * rhs) in index order; fidelity = square(abs(.)),
+ * returned in out[2] after the overlap's real and imaginary parts in out[0], out[1]. */
+void oracle_overlap_fidelity(const oc128 *lhs, const oc128 *rhs, uint32_t num_qubits,
+                             double out[3]) {
+    const size_t dim = (size_t)1 << num_qubits;
+    double re = 0.0, im = 0.0;
+    for (size_t i = 0; i < dim; ++i) {
+        re += lhs[i].re * rhs[i].re + lhs[i].im * rhs[i].im;
+        im += lhs[i].re * rhs[i].im - lhs[i].im * rhs[i].re;
+    }
+    const double h = hypot(re, im);
+    out[0] = re;
+    out[1] = im;
+    out[2] = h * h;
+}

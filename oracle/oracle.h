@@ -97,6 +97,17 @@ uint64_t oracle_stdrng_u64(uint64_t seed, uint64_t k);
 int oracle_num_threads(void);
 void oracle_set_num_threads(int n);
 
+/* Analysis of a state (crates/arcqml-analysis/src/statevector): probabilities (2^n), marginal
+ * probabilities of a qubit selection (2^k, selected qubits in descending order from the most
+ * significant output bit; non-zero return for an empty, out-of-range or duplicate selection),
+ * the Bloch vector of one qubit, and <lhs|rhs> with the fidelity |<lhs|rhs>|^2. */
+void oracle_probabilities(const oc128 *amps, uint32_t num_qubits, double *out);
+int oracle_marginal_probabilities(const oc128 *amps, uint32_t num_qubits, const uint32_t *qubits,
+                                  size_t num_selected, double *out);
+int oracle_bloch_vector(const oc128 *amps, uint32_t num_qubits, uint32_t qubit, double xyz[3]);
+void oracle_overlap_fidelity(const oc128 *lhs, const oc128 *rhs, uint32_t num_qubits,
+                             double out[3]);
+
 #ifdef __cplusplus
 }
 #endif

@@ -83,6 +83,10 @@ def lib():
         L.oracle_stdrng_key.argtypes = [C.c_uint64, P]
         L.oracle_stdrng_u64.argtypes = [C.c_uint64, C.c_uint64]
         L.oracle_stdrng_u64.restype = C.c_uint64
+        L.oracle_probabilities.argtypes = [P, C.c_uint32, P]
+        L.oracle_marginal_probabilities.argtypes = [P, C.c_uint32, P, C.c_size_t, P]
+        L.oracle_bloch_vector.argtypes = [P, C.c_uint32, C.c_uint32, P]
+        L.oracle_overlap_fidelity.argtypes = [P, P, C.c_uint32, P]
         L.oracle_num_threads.restype = C.c_int
         L.oracle_set_num_threads.argtypes = [C.c_int]
         _lib = L
@@ -296,3 +300,45 @@ def adam_step(values, grads, state, lr=0.05, beta1=0.9, beta2=0.999, eps=1e-8, w
         second_hat = second[i] / b2c
         out[i] -= lr * first_hat / (np.sqrt(second_hat) + eps)
     return out
+
+
+# ---------------------------------------------------------------- analysis
+# crates/arcqml-analysis/src/statevector/{probabilities,marginal,bloch,fidelity}.rs
+
+
+def probabilities(amps, num_qubits):
+    """|psi_i|^2 as square(abs(psi_i)) (probabilities.rs:22-25)."""
+    a = _state(amps)
+    out = np.zeros(1 << num_qubits, dtype=np.float64)
+    lib().oracle_probabilities(a.ctypes.data, num_qubits, out.ctypes.data)
+    return out
+
+
+def marginal_probabilities(amps, num_qubits, qubits):
+    """Segment sums of the probabilities over the selected qubits, output bits in descending
+    qubit order (marginal.rs:17-67); ValueError for an invalid selection."""
+    a = _state(amps)
+    q = np.ascontiguousarray(qubits, dtype=np.uint32)
+    out = np.zeros(1 << max(len(q), 0), dtype=np.float64)
+    rc = lib().oracle_marginal_probabilities(a.ctypes.data, num_qubits, q.ctypes.data, q.size,
+                                            out.ctypes.data)
+    if rc:
+        raise ValueError("oracle: invalid qubit selection")
+    return out
+
+
+def bloch_vector(amps, num_qubits, qubit):
+    """(<X>, <Y>, <Z>) of one qubit (bloch.rs:23-56)."""
+    a = _state(amps)
+    out = np.zeros(3, dtype=np.float64)
+    if lib().oracle_bloch_vector(a.ctypes.data, num_qubits, int(qubit), out.ctypes.data):
+        raise ValueError("oracle: qubit out of range")
+    return out
+
+
+def overlap_fidelity(lhs, rhs, num_qubits):
+    """(<lhs|rhs>, |<lhs|rhs>|^2) (fidelity.rs:14-30)."""
+    a, b = _state(lhs), _state(rhs)
+    out = np.zeros(3, dtype=np.float64)
+    lib().oracle_overlap_fidelity(a.ctypes.data, b.ctypes.data, num_qubits, out.ctypes.data)
+    return complex(out[0], out[1]), float(out[2])
