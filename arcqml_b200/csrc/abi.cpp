@@ -11,6 +11,7 @@
 
 #include "../../include/arcqml_runtime.h"
 #include "../../include/arcqml_runtime_v2.h"
+#include "analysis.h"
 #include "jit.h"
 #include "launch.h"
 #include "planner.h"
@@ -710,6 +711,125 @@ int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128
                                 uint32_t(num_qubits), upstream, parameter_requires_grad,
                                 parameter_requires_grad_len, gradients, gradients_len, ctx,
                                 pick_stream(ctx, stream));
+    });
+}
+
+// ---------------------------------------------------------------- state analysis
+
+// The qubit selection of crates/arcqml-analysis/src/statevector/marginal.rs:38-59 (same errors
+// and messages as AnalysisError); qubits == NULL with num_selected == 0 selects every qubit when
+// allow_all is set.
+static Selection analysis_selection(size_t num_qubits, const size_t *qubits, size_t num_selected,
+                                    bool allow_all) {
+    std::vector<uint32_t> q;
+    if (!qubits && num_selected == 0 && allow_all) {
+        for (size_t i = num_qubits; i-- > 0;) q.push_back(uint32_t(i));
+        return make_selection(uint32_t(num_qubits), q);
+    }
+    if (num_selected == 0) fail("at least one qubit must be selected");
+    if (!qubits) fail("qubit list is null");
+    for (size_t j = 0; j < num_selected; ++j) {
+        if (qubits[j] >= num_qubits) {
+            std::ostringstream m;
+            m << "qubit index out of range: simulator has " << num_qubits << " qubits, got "
+              << qubits[j];
+            fail(m.str());
+        }
+        for (size_t i = 0; i < j; ++i)
+            if (qubits[i] == qubits[j]) {
+                std::ostringstream m;
+                m << "duplicate qubit in selection: " << qubits[j];
+                fail(m.str());
+            }
+        q.push_back(uint32_t(qubits[j]));
+    }
+    return make_selection(uint32_t(num_qubits), q);
+}
+
+int32_t arcqml_rt_v2_probabilities(const arcqml_c128 *amplitudes, size_t batch,
+                                   size_t num_qubits, double *probabilities, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (!probabilities) fail("probability buffer is null");
+        ThreadContext &ctx = thread_context();
+        probabilities_device(reinterpret_cast<const double2 *>(amplitudes), batch,
+                             uint32_t(num_qubits), probabilities, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_marginal_probabilities(const arcqml_c128 *amplitudes, size_t batch,
+                                            size_t num_qubits, const size_t *qubits,
+                                            size_t num_selected, double *marginals,
+                                            void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        const Selection S = analysis_selection(num_qubits, qubits, num_selected, false);
+        if (!marginals) fail("marginal buffer is null");
+        ThreadContext &ctx = thread_context();
+        marginal_device(reinterpret_cast<const double2 *>(amplitudes), batch,
+                        uint32_t(num_qubits), S, marginals, ctx, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_bloch_vector(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                  size_t qubit, double *xyz, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        if (qubit >= num_qubits) {
+            std::ostringstream m;
+            m << "qubit index out of range: simulator has " << num_qubits << " qubits, got "
+              << qubit;
+            fail(m.str());
+        }
+        if (!xyz) fail("Bloch vector buffer is null");
+        ThreadContext &ctx = thread_context();
+        bloch_device(reinterpret_cast<const double2 *>(amplitudes), batch, uint32_t(num_qubits),
+                     uint32_t(qubit), xyz, ctx, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_overlap(const arcqml_c128 *lhs, const arcqml_c128 *rhs, size_t batch,
+                             size_t num_qubits, double *overlaps, void *stream) {
+    return guarded([&] {
+        check_device_state(lhs, batch, num_qubits);
+        check_device_state(rhs, batch, num_qubits);
+        if (!overlaps) fail("overlap buffer is null");
+        ThreadContext &ctx = thread_context();
+        overlap_device(reinterpret_cast<const double2 *>(lhs),
+                       reinterpret_cast<const double2 *>(rhs), batch, uint32_t(num_qubits),
+                       overlaps, ctx, pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_probability_cotangent(const arcqml_c128 *amplitudes, size_t batch,
+                                           size_t num_qubits, const size_t *qubits,
+                                           size_t num_selected, const double *upstream,
+                                           arcqml_c128 *cotangent, void *stream) {
+    return guarded([&] {
+        check_device_state(amplitudes, batch, num_qubits);
+        const Selection S = analysis_selection(num_qubits, qubits, num_selected, true);
+        if (!upstream) fail("upstream buffer is null");
+        if (!cotangent) fail("cotangent buffer is null");
+        ThreadContext &ctx = thread_context();
+        probability_cotangent_device(reinterpret_cast<const double2 *>(amplitudes), batch,
+                                     uint32_t(num_qubits), S, upstream,
+                                     reinterpret_cast<double2 *>(cotangent),
+                                     pick_stream(ctx, stream));
+    });
+}
+
+int32_t arcqml_rt_v2_scaled_copy(const arcqml_c128 *input, size_t batch, size_t num_qubits,
+                                 const double *factors, arcqml_c128 *output, void *stream) {
+    return guarded([&] {
+        check_device_state(input, batch, num_qubits);
+        if (!factors) fail("factor list is null");
+        if (!output) fail("output buffer is null");
+        for (size_t r = 0; r < 2 * batch; ++r)
+            if (!std::isfinite(factors[r])) fail("factors must be finite");
+        ThreadContext &ctx = thread_context();
+        scaled_copy_device(reinterpret_cast<const double2 *>(input), batch, uint32_t(num_qubits),
+                           factors, reinterpret_cast<double2 *>(output), ctx,
+                           pick_stream(ctx, stream));
     });
 }
 

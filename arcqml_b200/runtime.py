@@ -125,6 +125,12 @@ def load():
         "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
                                             I32, P]),
         "arcqml_rt_v2_small_run": (I32, [P, P, P, S, P, S, P, S, P, P, P]),
+        "arcqml_rt_v2_probabilities": (I32, [P, S, S, P, P]),
+        "arcqml_rt_v2_marginal_probabilities": (I32, [P, S, S, P, S, P, P]),
+        "arcqml_rt_v2_bloch_vector": (I32, [P, S, S, S, P, P]),
+        "arcqml_rt_v2_overlap": (I32, [P, P, S, S, P, P]),
+        "arcqml_rt_v2_probability_cotangent": (I32, [P, S, S, P, S, P, P, P]),
+        "arcqml_rt_v2_scaled_copy": (I32, [P, S, S, P, P, P]),
         "arcqml_rt_v2_small_adam": (I32, [P, P, P, S, P, P, S, P, P, C.c_uint64, S, D, D, D, D,
                                           D, P, P]),
         "arcqml_rt_v2_shard_slices_from": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, P, P]),
@@ -388,6 +394,14 @@ def _dev_ptr(t) -> int:
     if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.complex128
             and t.is_contiguous()):
         raise TypeError("device amplitudes must be a contiguous complex128 CUDA tensor")
+    return t.data_ptr()
+
+
+def _dev_ptr_f64(t) -> int:
+    import torch
+    if not (isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float64
+            and t.is_contiguous()):
+        raise TypeError("device values must be a contiguous float64 CUDA tensor")
     return t.data_ptr()
 
 
@@ -667,3 +681,102 @@ def jit_info() -> dict:
     load().arcqml_rt_v2_jit_info(C.byref(c), C.byref(l), C.byref(f), buf, 4096)
     return {"compiled": int(c.value), "launches": int(l.value), "fallbacks": int(f.value),
             "last_error": buf.value.decode("utf-8", errors="replace")}
+
+
+# ---------------------------------------------------------------- state analysis
+
+
+def _selection(qubits):
+    q = np.ascontiguousarray([int(x) for x in qubits], dtype=np.uintp)
+    return q, (q.ctypes.data if q.size else None)
+
+
+def probabilities_device(state, num_qubits: int, out=None, stream=None):
+    """|psi_i|^2 of every row (arcqml_rt_v2_probabilities): a float64 CUDA tensor shaped like
+    the state."""
+    import torch
+    b = _rows(state, num_qubits)
+    if out is None:
+        out = torch.empty(state.shape, dtype=torch.float64, device=state.device)
+    _status(load().arcqml_rt_v2_probabilities(_dev_ptr(state), b, num_qubits, _dev_ptr_f64(out),
+                                              _stream_ptr(stream)))
+    return out
+
+
+def marginal_probabilities_device(state, num_qubits: int, qubits, out=None, stream=None):
+    """Marginal probabilities of the selected qubits (highest selected qubit as the most
+    significant output bit) for every row: float64 CUDA tensor [2^k] or [batch, 2^k]."""
+    import torch
+    b = _rows(state, num_qubits)
+    q, qp = _selection(qubits)
+    if qp is None:  # empty selection: rejected by the runtime with the reference's message
+        q = np.zeros(1, dtype=np.uintp)
+        qp = q.ctypes.data
+        q = q[:0]
+    if out is None:
+        shape = (1 << q.size,) if state.dim() == 1 else (b, 1 << q.size)
+        out = torch.empty(shape, dtype=torch.float64, device=state.device)
+    _status(load().arcqml_rt_v2_marginal_probabilities(
+        _dev_ptr(state), b, num_qubits, qp, q.size, _dev_ptr_f64(out), _stream_ptr(stream)))
+    return out
+
+
+def bloch_vector_device(state, num_qubits: int, qubit: int, stream=None) -> np.ndarray:
+    """(<X>, <Y>, <Z>) of one qubit per row: numpy [3] or [batch, 3]."""
+    b = _rows(state, num_qubits)
+    out = np.zeros((b, 3), dtype=np.float64)
+    _status(load().arcqml_rt_v2_bloch_vector(_dev_ptr(state), b, num_qubits, int(qubit),
+                                             out.ctypes.data, _stream_ptr(stream)))
+    return out[0] if state.dim() == 1 else out
+
+
+def overlap_device(lhs, rhs, num_qubits: int, stream=None):
+    """<lhs|rhs> per row: a complex (1-D states) or a numpy complex array [batch]."""
+    b = _rows(lhs, num_qubits)
+    if rhs.shape != lhs.shape:
+        raise RuntimeError("overlap of states with different shapes")
+    out = np.zeros((b, 2), dtype=np.float64)
+    _status(load().arcqml_rt_v2_overlap(_dev_ptr(lhs), _dev_ptr(rhs), b, num_qubits,
+                                        out.ctypes.data, _stream_ptr(stream)))
+    z = out[:, 0] + 1j * out[:, 1]
+    return complex(z[0]) if lhs.dim() == 1 else z
+
+
+def probability_cotangent_device(state, num_qubits: int, upstream, qubits=None, out=None,
+                                 stream=None):
+    """lambda_i = upstream[bin(i)] psi_i per row (arcqml_rt_v2_probability_cotangent): the
+    adjoint sweep's lambda for an upstream gradient of the (marginal) probabilities; qubits=None
+    for the full probability vector. upstream: float64 CUDA tensor [batch, 2^k] (or [2^k])."""
+    import torch
+    b = _rows(state, num_qubits)
+    if qubits is None:
+        q, qp, k = None, None, num_qubits
+    else:
+        # an explicit empty selection keeps a non-null pointer: the runtime rejects it
+        q = np.ascontiguousarray([int(x) for x in qubits] or [0], dtype=np.uintp)
+        qp, k = q.ctypes.data, len(list(qubits))
+    if upstream.numel() != b << k:
+        raise RuntimeError(f"upstream has {upstream.numel()} values, expected {b << k}")
+    if out is None:
+        out = torch.empty_like(state)
+    _status(load().arcqml_rt_v2_probability_cotangent(
+        _dev_ptr(state), b, num_qubits, qp, 0 if qubits is None else k, _dev_ptr_f64(upstream),
+        _dev_ptr(out), _stream_ptr(stream)))
+    return out
+
+
+def scaled_copy_device(state, num_qubits: int, factors, out=None, stream=None):
+    """out[row] = factors[row] * state[row] with complex factors (arcqml_rt_v2_scaled_copy)."""
+    import torch
+    b = _rows(state, num_qubits)
+    f = np.asarray(factors, dtype=np.complex128).reshape(-1)
+    if f.size == 1 and b > 1:
+        f = np.full(b, f[0])
+    if f.size != b:
+        raise RuntimeError(f"{f.size} factors for {b} rows")
+    fr = np.ascontiguousarray(np.stack([f.real, f.imag], axis=1).reshape(-1))
+    if out is None:
+        out = torch.empty_like(state)
+    _status(load().arcqml_rt_v2_scaled_copy(_dev_ptr(state), b, num_qubits, fr.ctypes.data,
+                                            _dev_ptr(out), _stream_ptr(stream)))
+    return out

@@ -167,6 +167,28 @@ class StateVectorSimulator:
         obs = rt.Observable.from_sparse_pauli_op(observable)
         return float(obs.expectation(self.state, self.num_qubits)[0])
 
+    def gradient(self, circuit: Circuit, cotangent, stream=None):
+        """Parameter gradients of a loss of this simulator's state, given the loss's cotangent
+        (the lambda of ``arcqml_b200.analysis``'s ``*_cotangent`` helpers, a complex128 CUDA
+        tensor): the adjoint sweep of ``circuit`` adds 2 Re<lambda| dU/dp |psi> per bound slot.
+        The state must be ``circuit`` applied to this simulator's initial state; it is copied
+        (the sweep runs it back to the start), so the simulator keeps it. Returns the gradients
+        indexed like ``circuit.parameters`` and accumulates them into each parameter's
+        ``grad``, as ``RunResult.backward`` does."""
+        self._check(circuit)
+        plan = rt.CircuitPlan.create(circuit.compile_plan(1))
+        psi = self.state.clone()
+        lam = cotangent.clone()
+        req = circuit.requires_grad_mask(True, False)
+        grads = rt.adjoint_backward_device(plan, psi, lam, self.num_qubits, 1.0, req, len(req),
+                                           stream)
+        pgrads = grads[1:].copy()
+        for p, g in zip(circuit.parameters, pgrads):
+            if p.requires_grad:
+                g = float(np.float32(g)) if p.dtype == "f32" else float(g)
+                p.grad = g if getattr(p, "grad", None) is None else p.grad + g
+        return pgrads
+
     def norm(self) -> float:
         return float(rt.norms_device(self.state, self.num_qubits)[0])
 

@@ -169,6 +169,44 @@ int32_t arcqml_rt_v2_small_adam(const CircuitPlanHandle *plan,
                                 double beta1, double beta2, double epsilon, double weight_decay,
                                 double *energies, void *stream);
 
+/* State analysis (crates/arcqml-analysis/src/statevector), on every row of a device state.
+ * probabilities: probabilities[row][i] = |psi_row[i]|^2 (device, [batch, 2^n];
+ *   probabilities.rs:22-25).
+ * marginal_probabilities: marginals[row][m] = summed probabilities over the basis indices whose
+ *   selected qubits read m, the selected qubits taken in descending order with the highest as
+ *   the most significant bit of m (device, [batch, 2^num_selected]; marginal.rs:17-67). An empty
+ *   selection, a qubit >= num_qubits or a repeated qubit fails with the reference's message.
+ * bloch_vector: xyz[3 row + 0..2] = <X_q>, <Y_q>, <Z_q> (host, 3 per row; bloch.rs:23-56).
+ * overlap: overlaps[2 row], [2 row + 1] = real and imaginary part of <lhs_row|rhs_row> (host,
+ *   2 per row); the fidelity of fidelity.rs:14-30 is its squared modulus.
+ * Reductions are deterministic (fixed summation order on the device). */
+int32_t arcqml_rt_v2_probabilities(const arcqml_c128 *amplitudes, size_t batch,
+                                   size_t num_qubits, double *probabilities, void *stream);
+int32_t arcqml_rt_v2_marginal_probabilities(const arcqml_c128 *amplitudes, size_t batch,
+                                            size_t num_qubits, const size_t *qubits,
+                                            size_t num_selected, double *marginals,
+                                            void *stream);
+int32_t arcqml_rt_v2_bloch_vector(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
+                                  size_t qubit, double *xyz, void *stream);
+int32_t arcqml_rt_v2_overlap(const arcqml_c128 *lhs, const arcqml_c128 *rhs, size_t batch,
+                             size_t num_qubits, double *overlaps, void *stream);
+
+/* Cotangents for arcqml_rt_v2_adjoint_backward (its lambda; gradients += 2 Re<lambda|dU|psi>)
+ * of the analysis outputs, so that losses built on them train through the reverse sweep as the
+ * reference's autograd does (statevector_analysis.rs:109-181).
+ * probability_cotangent: cotangent[row][i] = upstream[row][bin(i)] psi_row[i] for upstream
+ *   gradients of marginal probabilities (device, [batch, 2^num_selected]); qubits = NULL with
+ *   num_selected = 0 means the full probability vector (bin(i) = i).
+ * scaled_copy: output[row] = factor[row] input[row] with a complex factor (host, re and im per
+ *   row): lambda = <a|psi> a for the fidelity |<a|psi>|^2, lambda = upstream / 2 for a complex
+ *   upstream gradient of the amplitudes. */
+int32_t arcqml_rt_v2_probability_cotangent(const arcqml_c128 *amplitudes, size_t batch,
+                                           size_t num_qubits, const size_t *qubits,
+                                           size_t num_selected, const double *upstream,
+                                           arcqml_c128 *cotangent, void *stream);
+int32_t arcqml_rt_v2_scaled_copy(const arcqml_c128 *input, size_t batch, size_t num_qubits,
+                                 const double *factors, arcqml_c128 *output, void *stream);
+
 /* norms[b] <- sum_i |psi_b[i]|^2 (host array). */
 int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,
                            double *norms, void *stream);
