@@ -60,7 +60,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--forward-only", action="store_true",
                     help="forward + <H> without the adjoint sweep (the 35-qubit sharded config)")
-    ap.add_argument("--workload", default="brickwork", choices=["brickwork", "vqe4", "qnn"],
+    ap.add_argument("--workload", default="brickwork",
+                    choices=["brickwork", "vqe4", "qnn", "analysis"],
                     help="vqe4: the 4-qubit VQE's 100 Adam steps; qnn: the batched QNN gradient")
     return ap.parse_args()
 
@@ -496,10 +497,70 @@ def small_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def analysis_arm(args):
+    """One GPU: the state-analysis kernels on random states of min(--qubits, 28) qubits (4 GiB,
+    beyond L2), each timed over --steps calls with CUDA events after --warmup calls; GB/s of
+    algorithmic bytes (every amplitude read once, outputs written once) against the measured
+    HBM copy rate. Bloch vector and overlap calls include their 16-24-byte read-back."""
+    import torch
+    from arcqml_b200 import build, runtime as rt
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    build.build()
+    rt.load()
+    n = min(args.qubits, 28)
+    dim = 1 << n
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    a = torch.randn(dim, dtype=torch.complex128, device="cuda", generator=gen)
+    a /= torch.linalg.vector_norm(a)
+    b = torch.randn(dim, dtype=torch.complex128, device="cuda", generator=gen)
+    b /= torch.linalg.vector_norm(b)
+    probs = torch.empty(dim, dtype=torch.float64, device="cuda")
+    lam = torch.empty_like(a)
+    up = torch.randn(dim, dtype=torch.float64, device="cuda", generator=gen)
+    ops = {
+        "probabilities": (lambda: rt.probabilities_device(a, n, out=probs), 24.0),
+        "marginal_top3": (lambda: rt.marginal_probabilities_device(a, n, [n - 1, n - 2, n - 3]),
+                          16.0),
+        "marginal_low2": (lambda: rt.marginal_probabilities_device(a, n, [0, 1]), 16.0),
+        "bloch_vector": (lambda: rt.bloch_vector_device(a, n, n // 2), 16.0),
+        "overlap": (lambda: rt.overlap_device(a, b, n), 32.0),
+        "probability_cotangent": (lambda: rt.probability_cotangent_device(a, n, up, out=lam),
+                                  40.0),
+    }
+    hbm = peaks().get("hbm_gbs") or 6650.0
+    launches0 = rt.launch_count()
+    out = {}
+    for name, (fn, per_amp) in ops.items():
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        gbs = per_amp * dim / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                     "bytes_per_amplitude": per_amp}
+    line = {"metric": f"state-analysis kernels, HBM GB/s ({n} qubits)",
+            "value": out["probabilities"]["gbs"], "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "complex128 (f64)",
+            "data": "synthetic (random normalised states)",
+            "config": {"workload": "analysis", "qubits": n, "l2": "inputs larger than L2"},
+            "peak": hbm, "peak_source": "measured" if peaks().get("hbm_gbs") else "fallback",
+            "kernels": out, "gpu_launches": rt.launch_count() - launches0}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.workload == "analysis":
+        analysis_arm(args)
     elif args.workload != "brickwork":
         small_arm(args)
     else:
