@@ -396,6 +396,18 @@ class RuntimeBackend:
                              unpack)
 
     # -- peer transport (device addresses) --
+    def marginal(self, shard, n_local: int, positions) -> np.ndarray:
+        return rt.marginal_probabilities_device(shard, n_local, list(positions)).cpu().numpy()
+
+    def bloch(self, shard, n_local: int, position: int) -> np.ndarray:
+        return rt.bloch_vector_device(shard, n_local, position)
+
+    def overlap(self, a, b, n_local: int) -> complex:
+        return rt.overlap_device(a, b, n_local)
+
+    def norm(self, shard, n_local: int) -> float:
+        return float(rt.norms_device(shard, n_local)[0])
+
     def peer_buffer(self, nbytes: int):
         return self.rt.PeerBuffer(nbytes)
 
@@ -760,6 +772,84 @@ class ShardedStateVectorSimulator:
                 g = float(np.float32(g)) if p.dtype == "f32" else float(g)
                 p.grad = g if getattr(p, "grad", None) is None else p.grad + g
         return pgrads
+
+
+    # -- analysis (crates/arcqml-analysis/src/statevector on the sharded state) -----------
+    def _check_qubit(self, q: int) -> None:
+        if not 0 <= q < self.num_qubits:
+            raise ShardError(f"qubit index out of range: simulator has {self.num_qubits} "
+                             f"qubits, got {q}")
+
+    def marginal_probabilities(self, qubits) -> np.ndarray:
+        """Marginal probabilities of logical qubits, the highest selected qubit as the most
+        significant output bit (marginal.rs:9-32), on every rank. Each rank sums its shard over
+        the selected local qubits at their physical positions; a selected global qubit reads the
+        rank's own bit; one all-reduce of the 2^k bins. No amplitude moves between ranks."""
+        qubits = [int(q) for q in qubits]
+        if not qubits:
+            raise ShardError("at least one qubit must be selected")
+        seen = set()
+        for q in qubits:
+            self._check_qubit(q)
+            if q in seen:
+                raise ShardError(f"duplicate qubit in selection: {q}")
+            seen.add(q)
+        if self.psi is None:
+            self.reset()
+        L = self.layout
+        disp = sorted(qubits, reverse=True)
+        lphys = sorted((L.pos[q] for q in disp if L.is_local(q)), reverse=True)
+        if lphys:
+            part = np.asarray(self.backend.marginal(self.psi, self.n_local, lphys))
+        else:
+            part = np.array([self.backend.norm(self.psi, self.n_local)])
+        out = np.zeros(1 << len(disp))
+        mm = np.arange(part.size)
+        m = np.zeros(part.size, dtype=np.int64)
+        for q in disp:  # logical bin of every local bin
+            if L.is_local(q):
+                bit = (mm >> (len(lphys) - 1 - lphys.index(L.pos[q]))) & 1
+            else:
+                bit = np.full(part.size, (self.rank >> (L.pos[q] - self.n_local)) & 1)
+            m = (m << 1) | bit
+        np.add.at(out, m, part)
+        return self.comm.allreduce_sum(out)
+
+    def bloch_vector(self, qubit: int) -> np.ndarray:
+        """(<X>, <Y>, <Z>) of a logical qubit (bloch.rs:23-56), on every rank. A global qubit
+        is first swapped with the highest local position (psi and a kept lambda together), since
+        its X and Y parts pair amplitudes of different ranks."""
+        q = int(qubit)
+        self._check_qubit(q)
+        if self.psi is None:
+            self.reset()
+        if not self.layout.is_local(q):
+            tensors = [self.psi] + ([self.lam] if self.lam is not None else [])
+            self._swap([(self.layout.pos[q], self.n_local - 1)], tensors)
+        v = np.asarray(self.backend.bloch(self.psi, self.n_local, self.layout.pos[q]), float)
+        return self.comm.allreduce_sum(v)
+
+    def overlap(self, other: "ShardedStateVectorSimulator") -> complex:
+        """<self|other> over all ranks; both states must be in the same qubit layout (two states
+        from circuits of the same structure, or freshly loaded ones are)."""
+        if other.num_qubits != self.num_qubits:
+            raise ShardError("cannot compare states with different qubit counts: "
+                             f"{self.num_qubits} and {other.num_qubits}")
+        if other.layout.pos != self.layout.pos:
+            raise ShardError("overlap needs both states in the same qubit layout")
+        if self.psi is None:
+            self.reset()
+        if other.psi is None:
+            other.reset()
+        s = self.backend.overlap(self.psi, other.psi, self.n_local)
+        v = self.comm.allreduce_sum(np.array([s.real, s.imag]))
+        return complex(v[0], v[1])
+
+    def fidelity(self, other: "ShardedStateVectorSimulator") -> float:
+        """|<self|other>|^2 (fidelity.rs:14-30)."""
+        s = self.overlap(other)
+        h = float(np.hypot(s.real, s.imag))
+        return h * h
 
 
 # ---------------------------------------------------------------------------- batch rows

@@ -96,6 +96,19 @@ class OracleShardBackend:
     def observable(self, coef, flip, phase, psi, out, n_local):
         return float(self.observable_rows(coef, flip, phase, psi, out, n_local)[0])
 
+    def marginal(self, shard, n_local, positions):
+        return self.O.marginal_probabilities(shard.numpy(), n_local, list(positions))
+
+    def bloch(self, shard, n_local, position):
+        return self.O.bloch_vector(shard.numpy(), n_local, position)
+
+    def overlap(self, a, b, n_local):
+        return self.O.overlap_fidelity(a.numpy(), b.numpy(), n_local)[0]
+
+    def norm(self, shard, n_local):
+        a = shard.numpy()
+        return float(np.vdot(a, a).real)
+
     def slices(self, shard, n_local, positions, chunk_begin, chunk_len, skip, staging, unpack):
         slices_numpy(shard.numpy(), positions, chunk_begin, chunk_len, skip, staging.numpy(),
                      unpack)
