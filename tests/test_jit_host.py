@@ -59,3 +59,45 @@ def test_scaled_and_plain_rotation_forms_compile(runtime):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, ARCQML_SCALED="0"), timeout=600)
     assert r.returncode == 0 and "plain-ok" in r.stdout, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("n,seed", [(8, 1), (11, 2), (14, 3)])
+def test_random_fast_path_circuits_compile(runtime, n, seed):
+    """Every pass of random circuits built from fast-path gates (rotations at random and edge
+    angles, fixed phases, H / SX / S / T / Z, U3 as a dense 2x2, RXX / RYY as dense 4x4s, CZ
+    between any qubits) has a compiled form that compiles, forward and adjoint."""
+    import math
+
+    import numpy as np
+
+    from arcqml_b200 import circuit as cm
+    g = np.random.Generator(np.random.PCG64(seed))
+    c = cm.Circuit(n)
+    edge = (math.pi, -math.pi, 0.0, 3 * math.pi, math.pi * (1 - 1e-9))
+    for _ in range(4):
+        for q in range(n):
+            r = g.uniform()
+            a = float(edge[int(g.integers(0, len(edge)))] if g.uniform() < 0.3
+                      else g.uniform(-3, 3))
+            if r < 0.45:
+                c.rot(("rx", "ry", "rz")[int(g.integers(0, 3))], a, q)
+            elif r < 0.6:
+                c.append(("h", "sx", "s", "t", "z")[int(g.integers(0, 5))], (q,))
+            elif r < 0.7:
+                c.append("phase", (q,), a)
+            elif r < 0.8:
+                c.append("u3", (q,), a, float(g.uniform(-3, 3)), float(g.uniform(-3, 3)))
+        for _ in range(n // 2):
+            a, b = (int(x) for x in g.choice(n, size=2, replace=False))
+            if g.uniform() < 0.7:
+                c.append("cz", (a, b))
+            elif abs(a - b) == 1:
+                c.append(("rxx", "ryy")[int(g.integers(0, 2))], (a, b), float(g.uniform(-3, 3)))
+    plan = runtime.CircuitPlan.create(c.compile_plan(1))
+    for adjoint in (False, True):
+        r = plan.jit_check(n, adjoint)
+        if r["eligible"] == 0 and "not found" in r["message"]:
+            pytest.skip("NVRTC is not available: " + r["message"])
+        assert r["compiled"] == r["eligible"], r["message"]
+        if not adjoint:
+            assert r["eligible"] >= 1
