@@ -714,6 +714,28 @@ int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128
     });
 }
 
+int32_t arcqml_rt_v2_plan_emulate(const CircuitPlanHandle *plan, arcqml_c128 *state,
+                                  size_t num_qubits, int32_t adjoint, arcqml_c128 *lambda,
+                                  const uint8_t *parameter_requires_grad,
+                                  size_t parameter_requires_grad_len, double *gradients,
+                                  size_t gradients_len) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        state_dimension(num_qubits);
+        if (!state) fail("state buffer is null");
+        if (adjoint) {
+            if (!lambda) fail("adjoint state buffer is null");
+            if (parameter_requires_grad_len && !parameter_requires_grad)
+                fail("requires-grad list is null");
+            if (gradients_len && !gradients) fail("gradient buffer is null");
+        }
+        emulate_schedule(*p, uint32_t(num_qubits), adjoint != 0,
+                         reinterpret_cast<double2 *>(state), reinterpret_cast<double2 *>(lambda),
+                         parameter_requires_grad, parameter_requires_grad_len, gradients,
+                         gradients_len);
+    });
+}
+
 // ---------------------------------------------------------------- state analysis
 
 // The qubit selection of crates/arcqml-analysis/src/statevector/marginal.rs:38-59 (same errors

@@ -34,6 +34,15 @@ struct Schedule {
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb);
 
+// Register bits of forward passes on tiles of k qubits (ARCQML_FORWARD_RB may force 3 or 4).
+uint32_t forward_rb(uint32_t k);
+
+// Runs the engine's schedule of the plan on a host state (emulate.cpp; diagnostic, no CUDA):
+// psi forward, or the adjoint sweep over psi and lam (lam already scaled by the upstream
+// factor) adding 2 Re<lam| dU |psi> per required slot into grads[parent].
+void emulate_schedule(const Plan &plan, uint32_t n, bool adjoint, double2 *psi, double2 *lam,
+                      const uint8_t *req, size_t req_len, double *grads, size_t grads_len);
+
 // Whether compiled passes run Pauli rotations and unitary one-qubit diagonals in their scaled
 // unit-diagonal forms (ARCQML_SCALED=0 turns it off).
 bool scaled_passes();

@@ -125,6 +125,7 @@ def load():
         "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
                                             I32, P]),
         "arcqml_rt_v2_small_run": (I32, [P, P, P, S, P, S, P, S, P, P, P]),
+        "arcqml_rt_v2_plan_emulate": (I32, [P, P, S, I32, P, P, S, P, S]),
         "arcqml_rt_v2_probabilities": (I32, [P, S, S, P, P]),
         "arcqml_rt_v2_marginal_probabilities": (I32, [P, S, S, P, S, P, P]),
         "arcqml_rt_v2_bloch_vector": (I32, [P, S, S, S, P, P]),
@@ -681,6 +682,24 @@ def jit_info() -> dict:
     load().arcqml_rt_v2_jit_info(C.byref(c), C.byref(l), C.byref(f), buf, 4096)
     return {"compiled": int(c.value), "launches": int(l.value), "fallbacks": int(f.value),
             "last_error": buf.value.decode("utf-8", errors="replace")}
+
+
+def plan_emulate(plan: CircuitPlan, state, num_qubits: int, adjoint: bool = False, lam=None,
+                 requires_grad=None, num_gradients: int = 0):
+    """The engine's fused-pass schedule run on the CPU (arcqml_rt_v2_plan_emulate): returns the
+    new state, or (psi, lambda, gradients) for the adjoint sweep. numpy complex128 inputs."""
+    a = np.ascontiguousarray(state, dtype=np.complex128).copy()
+    if not adjoint:
+        _status(load().arcqml_rt_v2_plan_emulate(C.byref(plan.raw), a.ctypes.data, num_qubits, 0,
+                                                 None, None, 0, None, 0))
+        return a
+    lm = np.ascontiguousarray(lam, dtype=np.complex128).copy()
+    req = np.ascontiguousarray(requires_grad, dtype=np.uint8)
+    grads = np.zeros(num_gradients, dtype=np.float64)
+    _status(load().arcqml_rt_v2_plan_emulate(C.byref(plan.raw), a.ctypes.data, num_qubits, 1,
+                                             lm.ctypes.data, req.ctypes.data, req.size,
+                                             grads.ctypes.data, grads.size))
+    return a, lm, grads
 
 
 # ---------------------------------------------------------------- state analysis

@@ -250,6 +250,19 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
 int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qubits,
                                     int32_t adjoint, uint64_t *compiled, uint64_t *eligible,
                                     char *message, size_t capacity);
+/* Runs the fused-pass schedule the engine builds for the plan on a host state, on the CPU
+ * (diagnostic and test support; no reference counterpart, no CUDA call): the same passes, tile
+ * mapping, encoded ops, scaled forms and gradient factors as the device kernels, so the
+ * planner can be checked against a CPU reference without a GPU. adjoint == 0: state <- plan
+ * state. adjoint != 0: the reverse sweep over state (psi) and lambda (already scaled by the
+ * upstream factor), gradients[parent] += 2 Re<lambda| dU |psi> per required slot. 8 to 22
+ * qubits. */
+int32_t arcqml_rt_v2_plan_emulate(const CircuitPlanHandle *plan, arcqml_c128 *state,
+                                  size_t num_qubits, int32_t adjoint, arcqml_c128 *lambda,
+                                  const uint8_t *parameter_requires_grad,
+                                  size_t parameter_requires_grad_len, double *gradients,
+                                  size_t gradients_len);
+
 /* Run-time compiled pass kernels (no reference counterpart). Fused passes whose gates all have
  * fast paths run as kernels compiled for the circuit's structure (NVRTC, sm_100a) and cached per
  * device; ARCQML_JIT=0 in the environment keeps every pass on the precompiled kernel. Reports the

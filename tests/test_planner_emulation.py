@@ -1,0 +1,75 @@
+"""The engine's fused-pass schedules run on the CPU (arcqml_rt_v2_plan_emulate) against the
+oracle: pass partitioning, tile mapping, op encoding, forward merges, scaled rotation forms and
+gradient bookkeeping, checked without a GPU (forward 1e-12, gradients 1e-10)."""
+import math
+
+import numpy as np
+import pytest
+
+from arcqml_b200 import circuit as cm
+from arcqml_b200 import workloads
+from plans import random_plan, random_state, random_terms
+
+
+def check(runtime, oracle, ops, n, terms, init, req, up):
+    plan = runtime.CircuitPlan.create(ops)
+    psi = runtime.plan_emulate(plan, init, n)
+    ref = oracle.plan_apply(ops, init, n)
+    assert float(np.max(np.abs(psi - ref))) < 1e-12
+    _, lam = oracle.expectation_and_apply(terms, ref, n)
+    p0, l0, g = runtime.plan_emulate(plan, psi, n, adjoint=True, lam=up * lam,
+                                     requires_grad=req, num_gradients=len(req))
+    rp0, rl0, rg = oracle.adjoint_backward(ops, ref, lam, n, up, req, len(req))
+    assert float(np.max(np.abs(p0 - init))) < 1e-10
+    assert float(np.max(np.abs(l0 - rl0))) <= 1e-10 * max(1.0, float(np.max(np.abs(rl0))))
+    assert float(np.max(np.abs(g - rg))) <= 1e-10 * max(1.0, float(np.max(np.abs(rg))))
+
+
+@pytest.mark.parametrize("n,num_ops", [(8, 150), (10, 200), (13, 160)])
+def test_random_plans_over_every_opcode(runtime, oracle, n, num_ops):
+    g = np.random.Generator(np.random.PCG64(1000 + n))
+    npar = 10
+    ops = random_plan(g, n, num_ops, npar)
+    req = [0] + [int(x) for x in (g.uniform(size=npar) < 0.8)]
+    check(runtime, oracle, ops, n, random_terms(g, n, 20), random_state(g, n), req,
+          float(g.normal()))
+
+
+@pytest.mark.parametrize("n", [9, 12])
+def test_brickwork_and_edge_angles(runtime, oracle, n):
+    g = np.random.Generator(np.random.PCG64(n))
+    c = workloads.brickwork(n, 5, seed=n)
+    for q in range(n):  # rotations at and near pi: forms refused or growth capped
+        c.rot("ry", math.pi * (1 - 1e-9), q)
+        c.rot("rx", math.pi, q)
+        c.append("phase", (q,), 3 * math.pi)
+    for _ in range(30):
+        c.rot("rz", math.pi * (1 - 1e-9), 1)
+    ops = c.compile_plan(1)
+    req = list(c.requires_grad_mask(True))
+    check(runtime, oracle, ops, n, workloads.random_pauli_sum(n, 25, seed=n).compiled_terms(),
+          random_state(g, n), req, -0.7)
+
+
+def test_emulator_rejects_small_states_and_bad_buffers(runtime):
+    plan = runtime.CircuitPlan.create(cm.Circuit(4).append("h", (0,)).compile_plan(1))
+    with pytest.raises(runtime.RuntimeError, match="below 8 qubits"):
+        runtime.plan_emulate(plan, np.zeros(16, np.complex128), 4)
+
+
+def test_plain_form_schedules_with_scaling_off():
+    """ARCQML_SCALED=0 (subprocess): the plain rotation forms and their forward merges into
+    dense 2x2s, emulated against the oracle."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import oracle, test_planner_emulation as T\n"
+            "from arcqml_b200 import runtime\n"
+            "T.test_brickwork_and_edge_angles(runtime, oracle, 10)\n"
+            "print('plain-ok')\n") % (root, here, os.path.join(root, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_SCALED="0"), timeout=600)
+    assert r.returncode == 0 and "plain-ok" in r.stdout, r.stdout + r.stderr
