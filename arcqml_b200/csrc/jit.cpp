@@ -531,22 +531,34 @@ void jit_launch(void *fn, unsigned grid, unsigned threads, size_t smem, cudaStre
 
 size_t jit_compile_check(const Schedule &sch, bool adj, size_t *eligible, std::string *err) {
     std::lock_guard<std::mutex> lock(g_mu);
-    size_t ok = 0, cand = 0;
     if (!load_nvrtc()) {
         if (err) *err = g_nvrtc.why;
         if (eligible) *eligible = 0;
         return 0;
     }
+    std::vector<std::string> srcs;
     for (const auto &st : sch.steps) {
         if (!st.is_pass) continue;
         const std::string pass = pass_source(st, adj, st.header.rb);
-        if (pass.empty()) continue;
-        ++cand;
-        const Compiled c = compile(full_source(pass));
+        if (!pass.empty()) srcs.push_back(full_source(pass));
+    }
+    // compiled on parallel host threads, as jit_kernels does
+    std::vector<Compiled> out(srcs.size());
+    std::atomic<size_t> next{0};
+    const unsigned hw = std::thread::hardware_concurrency();
+    const size_t nthreads = std::min<size_t>(srcs.size(), hw ? std::min(hw, 16u) : 4u);
+    std::vector<std::thread> pool;
+    for (size_t t = 0; t < nthreads; ++t)
+        pool.emplace_back([&] {
+            for (size_t j; (j = next++) < srcs.size();) out[j] = compile(srcs[j]);
+        });
+    for (auto &th : pool) th.join();
+    size_t ok = 0;
+    for (const Compiled &c : out) {
         if (c.error.empty() && !c.cubin.empty()) ++ok;
         else if (err && err->empty()) *err = c.error;
     }
-    if (eligible) *eligible = cand;
+    if (eligible) *eligible = srcs.size();
     return ok;
 }
 

@@ -101,3 +101,16 @@ def test_random_fast_path_circuits_compile(runtime, n, seed):
         assert r["compiled"] == r["eligible"], r["message"]
         if not adjoint:
             assert r["eligible"] >= 1
+
+
+def test_benchmark_schedule_compiles_completely(runtime):
+    """Every pass of the 32-qubit 20-layer brickwork (the bench's step), forward and adjoint,
+    has a compiled form that compiles: none falls back to the table-driven kernel."""
+    c = workloads.brickwork(32, 20, seed=1234)
+    plan = runtime.CircuitPlan.create(c.compile_plan(1))
+    for adjoint in (False, True):
+        r = plan.jit_check(32, adjoint)
+        if r["eligible"] == 0 and "not found" in r["message"]:
+            pytest.skip("NVRTC is not available: " + r["message"])
+        assert r["eligible"] >= 20 and r["compiled"] == r["eligible"], r
+        assert plan.schedule_stats(32, adjoint)["passes"] == r["eligible"]
