@@ -312,6 +312,75 @@ size_t pass_op_cap() {
     return cap;
 }
 
+namespace {
+
+// Sub-blocks of a pass's members with commuting gates reordered (ARCQML_SUBBLOCK_REORDER=1).
+// Two gates commute when every qubit they share is acted on diagonally by both (a diagonal
+// gate, or a control): then no shared qubit is a non-diagonal target (`needs`) of either. Each
+// sub-block first takes every ready gate (all non-commuting earlier gates placed) whose
+// non-diagonal targets already are register bits, and grows its register bits by the first
+// ready gate that fits only when none is left, so the tile goes through shared memory fewer
+// times than in circuit order.
+void pack_subblocks(const std::vector<PGate> &gates, const std::vector<size_t> &members,
+                    const int *lpos, uint32_t rb, std::vector<std::vector<size_t>> &subs,
+                    std::vector<uint32_t> &sub_R) {
+    const size_t m = members.size();
+    std::vector<uint32_t> need(m, 0);
+    std::vector<std::vector<uint32_t>> deps(m);
+    for (size_t b = 0; b < m; ++b) {
+        const PGate &B = gates[members[b]];
+        if (!B.diag)
+            for (uint32_t t : B.targets) need[b] |= 1u << lpos[t];
+        for (size_t a = 0; a < b; ++a) {
+            const PGate &A = gates[members[a]];
+            if ((A.touched & B.touched) & (A.needs | B.needs)) deps[b].push_back(uint32_t(a));
+        }
+    }
+    std::vector<char> placed(m, 0);
+    auto ready = [&](size_t b) {
+        for (uint32_t a : deps[b])
+            if (!placed[a]) return false;
+        return true;
+    };
+    size_t left = m;
+    while (left) {
+        uint32_t R = 0;
+        std::vector<size_t> cur;
+        while (true) {
+            bool took = false;
+            for (size_t b = 0; b < m; ++b)
+                if (!placed[b] && (need[b] & ~R) == 0 && ready(b)) {
+                    cur.push_back(members[b]);
+                    placed[b] = 1;
+                    --left;
+                    took = true;
+                }
+            if (took) continue;
+            for (size_t b = 0; b < m && !took; ++b)
+                if (!placed[b] && uint32_t(__builtin_popcount(R | need[b])) <= rb && ready(b)) {
+                    R |= need[b];
+                    cur.push_back(members[b]);
+                    placed[b] = 1;
+                    --left;
+                    took = true;
+                }
+            if (!took) break;
+        }
+        subs.push_back(cur);
+        sub_R.push_back(R);
+    }
+}
+
+}  // namespace
+
+bool subblock_reorder() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_SUBBLOCK_REORDER");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb) {
     Schedule sch;
@@ -396,7 +465,9 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         // --- sub-blocks (consecutive members whose non-diagonal targets fit in rb bits)
         std::vector<std::vector<size_t>> subs;
         std::vector<uint32_t> sub_R;  // bitmask over tile bits
-        {
+        if (subblock_reorder()) {
+            pack_subblocks(gates, members, lpos, rb, subs, sub_R);
+        } else {
             uint32_t R = 0;
             std::vector<size_t> cur;
             for (size_t i : members) {

@@ -34,6 +34,10 @@ struct Schedule {
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb);
 
+// Whether passes pack commuting gates into fewer register sub-blocks than circuit order gives
+// (ARCQML_SUBBLOCK_REORDER=1; off by default).
+bool subblock_reorder();
+
 // Register bits of forward passes on tiles of k qubits (ARCQML_FORWARD_RB may force 3 or 4).
 uint32_t forward_rb(uint32_t k);
 

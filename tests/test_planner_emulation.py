@@ -73,3 +73,36 @@ def test_plain_form_schedules_with_scaling_off():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, ARCQML_SCALED="0"), timeout=600)
     assert r.returncode == 0 and "plain-ok" in r.stdout, r.stdout + r.stderr
+
+
+def test_reordered_subblocks_emulate_correctly_and_pack_tighter():
+    """ARCQML_SUBBLOCK_REORDER=1 (subprocess): commuting gates packed into fewer register
+    sub-blocks; the emulated schedules still match the oracle, and the 32-qubit benchmark
+    circuit needs fewer sub-blocks than in circuit order."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import oracle, test_planner_emulation as T\n"
+            "from arcqml_b200 import runtime, workloads\n"
+            "for n, m in ((8, 150), (10, 200), (13, 160)):\n"
+            "    T.test_random_plans_over_every_opcode(runtime, oracle, n, m)\n"
+            "for n in (9, 12):\n"
+            "    T.test_brickwork_and_edge_angles(runtime, oracle, n)\n"
+            "c = workloads.brickwork(32, 20, seed=1234)\n"
+            "p = runtime.CircuitPlan.create(c.compile_plan(1))\n"
+            "print('blocks', p.schedule_stats(32, False)['sub_blocks'],"
+            " p.schedule_stats(32, True)['sub_blocks'])\n") % (
+        root, here, os.path.join(root, "oracle"))
+    env = dict(os.environ, ARCQML_SUBBLOCK_REORDER="1")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    fwd, adj = (int(x) for x in r.stdout.split("blocks")[1].split())
+    from arcqml_b200 import runtime, workloads
+    c = workloads.brickwork(32, 20, seed=1234)
+    p = runtime.CircuitPlan.create(c.compile_plan(1))
+    assert fwd < p.schedule_stats(32, False)["sub_blocks"]
+    assert adj < p.schedule_stats(32, True)["sub_blocks"]
