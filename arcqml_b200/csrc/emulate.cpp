@@ -63,9 +63,22 @@ bool sign_shape(const Step &st, const SubBlock &sb, const FOp &o, Shape &s) {
     return true;
 }
 
+// X and CNOT fast paths (FC_X / FC_CX_*): the target is register bit rb0; the control (if any)
+// is register bit rb1 or the diagonal slot 0, and the control masks are not read.
+bool x_shape(const Step &st, const SubBlock &sb, const FOp &o, Shape &s) {
+    if (o.code != FC_X && o.code != FC_CX_RR && o.code != FC_CX_CR) return false;
+    s.q = {reg_qubit(st, sb, o.rb0)};
+    s.diag = false;
+    s.ctrl = 0;
+    if (o.code == FC_CX_RR) s.ctrl = uint64_t(1) << reg_qubit(st, sb, o.rb1);
+    if (o.code == FC_CX_CR) s.ctrl = uint64_t(1) << diag_qubit(st, o, 0);
+    return true;
+}
+
 Shape shape_of(const Step &st, const SubBlock &sb, const FOp &o) {
     Shape s;
     if (sign_shape(st, sb, o, s)) return s;
+    if (x_shape(st, sb, o, s)) return s;
     s.ctrl = control_mask(st, o);
     switch (o.kind) {
     case FK_D1: s.q = {diag_qubit(st, o, 0)}; s.diag = true; break;
@@ -192,9 +205,11 @@ void run_step(const Step &st, bool adjoint, Emu &E, const uint8_t *req, double *
             const Shape s = shape_of(st, sb, o);
             const bool sc = st.scaled && o.sform;
             const bool sign = o.code == FC_SIGN_RR || o.code == FC_SIGN_RC || o.code == FC_SIGN_CC;
+            const bool xop = o.code == FC_X || o.code == FC_CX_RR || o.code == FC_CX_CR;
             const std::vector<cplx> u =
                 sign ? std::vector<cplx>{1.0, 1.0, 1.0, -1.0}
-                     : (sc ? scaled_matrix(o, st.mats[o.soff].x) : plain_matrix(o, m));
+                     : xop ? std::vector<cplx>{0.0, 1.0, 1.0, 0.0}
+                           : (sc ? scaled_matrix(o, st.mats[o.soff].x) : plain_matrix(o, m));
             Shape su = s;
             if (sc && o.kind == FK_D1) su.diag = true;
             if (adjoint && (o.gkind == GK_PX || o.gkind == GK_PY || o.gkind == GK_PZ)) {

@@ -56,6 +56,9 @@ enum FastCode : uint8_t {
     FC_SIGN_RC = 7,  // -1 where register bit rb0 and the per-thread bit dq 0 are set
     FC_SIGN_CC = 8,  // -1 where the per-thread bits dq 0 and dq 1 are set
     FC_M4 = 9,       // uncontrolled 4x4 on register bits (rb0, rb1)
+    FC_X = 10,       // uncontrolled X on register bit rb0 (register renaming)
+    FC_CX_RR = 11,   // X on register bit rb0 where register bit rb1 (the control) is 1
+    FC_CX_CR = 12,   // X on register bit rb0 where the per-thread bit dq 0 (the control) is 1
 };
 
 enum GradFast : uint8_t {

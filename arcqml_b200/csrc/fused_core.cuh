@@ -129,6 +129,36 @@ __device__ __forceinline__ void f_sign_cc(double2 (&v)[1 << RB], uint32_t m) {
     for (int e = 0; e < (1 << RB); ++e) v[e] = flip2(v[e], m);
 }
 
+// X on register bit B: the pairs exchange registers (no arithmetic once unrolled).
+template <int RB, int B>
+__device__ __forceinline__ void f_x(double2 (&v)[1 << RB]) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if (e & (1 << B)) continue;
+        const double2 t = v[e];
+        v[e] = v[e | (1 << B)];
+        v[e | (1 << B)] = t;
+    }
+}
+
+// CNOT with control register bit BC and target register bit BT.
+template <int RB, int BC, int BT>
+__device__ __forceinline__ void f_cx_rr(double2 (&v)[1 << RB]) {
+#pragma unroll
+    for (int e = 0; e < (1 << RB); ++e) {
+        if ((e & (1 << BT)) || !(e & (1 << BC))) continue;
+        const double2 t = v[e];
+        v[e] = v[e | (1 << BT)];
+        v[e | (1 << BT)] = t;
+    }
+}
+
+// CNOT whose control is the same for all of the thread's elements (a thread or tile bit).
+template <int RB, int B>
+__device__ __forceinline__ void f_cx_cr(double2 (&v)[1 << RB], uint32_t on) {
+    if (on) f_x<RB, B>(v);
+}
+
 template <int RB, int B0, int B1>
 __device__ __forceinline__ void f_m4(double2 (&v)[1 << RB], const double2 *mt) {
 #pragma unroll

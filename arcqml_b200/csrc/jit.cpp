@@ -160,13 +160,14 @@ std::string const_bit(const FOp &o, int slot, const SubBlock &S, uint32_t thread
 bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
                 const SubBlock &S, uint32_t tbits) {
     const int b0 = o.rb0, b1 = o.rb1;
-    const std::string bit0 = (o.code == FC_D1_UNI || o.code == FC_SIGN_RC || o.code == FC_SIGN_CC)
+    const std::string bit0 = (o.code == FC_D1_UNI || o.code == FC_SIGN_RC || o.code == FC_SIGN_CC ||
+                              o.code == FC_CX_CR)
                                  ? const_bit(o, 0, S, tbits) : std::string("0u");
     const std::string bit1 = o.code == FC_SIGN_CC ? const_bit(o, 1, S, tbits) : std::string("0u");
     if (bit0.empty() || bit1.empty()) return false;
     const uint32_t m = o.moff;
     const bool uses_b0 = o.code != FC_D1_UNI && o.code != FC_SIGN_CC;
-    const bool uses_b1 = o.code == FC_SIGN_RR || o.code == FC_M4;
+    const bool uses_b1 = o.code == FC_SIGN_RR || o.code == FC_M4 || o.code == FC_CX_RR;
     if ((uses_b0 && b0 >= int(rb)) || (uses_b1 && b1 >= int(rb))) return false;
     const uint32_t so = o.soff;
     if (o.sform) {  // scaled unit-diagonal form (mats[soff].x = t or tau)
@@ -208,6 +209,9 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
           << ") ? 0x80000000u : 0u);";
         break;
     case FC_M4: c << "f_m4<RB, " << b0 << ", " << b1 << ">(" << r << ", M + " << m << ");"; break;
+    case FC_X: c << "f_x<RB, " << b0 << ">(" << r << ");"; break;
+    case FC_CX_RR: c << "f_cx_rr<RB, " << b1 << ", " << b0 << ">(" << r << ");"; break;
+    case FC_CX_CR: c << "f_cx_cr<RB, " << b0 << ">(" << r << ", " << bit0 << ");"; break;
     default: return false;
     }
     return true;

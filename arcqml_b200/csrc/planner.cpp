@@ -226,6 +226,11 @@ void scale_pass(Step &st, bool adjoint) {
     st.scaled = true;
 }
 
+bool is_x(const std::vector<double2> &m) {
+    return m.size() == 4 && m[0].x == 0 && m[0].y == 0 && m[1].x == 1 && m[1].y == 0 &&
+           m[2].x == 1 && m[2].y == 0 && m[3].x == 0 && m[3].y == 0;
+}
+
 // Chooses the op's specialised device path (fused.h FastCode). reg_of(q) is the register bit
 // of qubit q in the current sub-block (0xFF if none); lpos[q] its tile bit (-1 if outside).
 template <class RegOf>
@@ -237,6 +242,24 @@ void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
         o.dq_pos[slot] = uint8_t(lpos[q] >= 0 ? lpos[q] : int(q));
     };
     o.code = FC_GENERIC;
+    if (!g.diag && fast_cnot() && nt == 1 && is_x(g.m)) {
+        if (plain) {
+            o.code = FC_X;
+            return;
+        }
+        if (g.controls.size() == 1) {
+            const uint32_t c = g.controls[0];
+            const uint8_t rc = reg_of(c);
+            if (rc != 0xFF) {
+                o.code = FC_CX_RR;
+                o.rb1 = rc;
+            } else {
+                o.code = FC_CX_CR;
+                put(0, c);
+            }
+            return;
+        }
+    }
     if (!g.diag) {
         if (plain && nt == 1)
             o.code = o.kind == FK_RX ? FC_RX : (o.kind == FK_RY ? FC_RY : FC_M2);
@@ -372,6 +395,14 @@ void pack_subblocks(const std::vector<PGate> &gates, const std::vector<size_t> &
 }
 
 }  // namespace
+
+bool fast_cnot() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_FAST_CNOT");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
 
 bool subblock_reorder() {
     static const bool on = [] {
@@ -545,6 +576,10 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                                          st.ops[size_t(last1q[g.targets[0]])].kind == FK_D1;
                     if (scaled_passes() && !to_diag && rotation_form(p) == 0 &&
                         scalable_1q(ue) && scalable_1q(un))
+                        merge = false;
+                    // an X on the fast path is a register exchange: keep it out of a dense 2x2
+                    if (fast_cnot() && (is_x(std::vector<double2>(ue, ue + 4)) ||
+                                        is_x(std::vector<double2>(un, un + 4))))
                         merge = false;
                 }
                 if (merge) {

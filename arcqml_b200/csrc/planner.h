@@ -34,6 +34,10 @@ struct Schedule {
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb);
 
+// Whether X and single-control CNOT gates on register bits use their register-exchange fast
+// paths (ARCQML_FAST_CNOT=1; off by default) instead of a dense 2x2 / the generic path.
+bool fast_cnot();
+
 // Whether passes pack commuting gates into fewer register sub-blocks than circuit order gives
 // (ARCQML_SUBBLOCK_REORDER=1; off by default).
 bool subblock_reorder();

@@ -96,13 +96,63 @@ def test_reordered_subblocks_emulate_correctly_and_pack_tighter():
             "print('blocks', p.schedule_stats(32, False)['sub_blocks'],"
             " p.schedule_stats(32, True)['sub_blocks'])\n") % (
         root, here, os.path.join(root, "oracle"))
-    env = dict(os.environ, ARCQML_SUBBLOCK_REORDER="1")
-    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
-                       timeout=600)
-    assert r.returncode == 0, r.stdout + r.stderr
-    fwd, adj = (int(x) for x in r.stdout.split("blocks")[1].split())
-    from arcqml_b200 import runtime, workloads
-    c = workloads.brickwork(32, 20, seed=1234)
-    p = runtime.CircuitPlan.create(c.compile_plan(1))
-    assert fwd < p.schedule_stats(32, False)["sub_blocks"]
-    assert adj < p.schedule_stats(32, True)["sub_blocks"]
+    counts = {}
+    for on in ("0", "1"):
+        env = dict(os.environ, ARCQML_SUBBLOCK_REORDER=on)
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                           env=env, timeout=600)
+        assert r.returncode == 0, r.stdout + r.stderr
+        counts[on] = [int(x) for x in r.stdout.split("blocks")[1].split()]
+    assert counts["1"][0] < counts["0"][0] and counts["1"][1] < counts["0"][1], counts
+
+
+def qnn_like(n, seed):
+    """RY / RZ layers, a CNOT ring (controls in registers, thread bits and outside the tile)
+    and X gates."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    c = cm.Circuit(n)
+    for _ in range(4):
+        for q in range(n):
+            c.rot("ry", float(g.uniform(-3, 3)), q)
+            c.rot("rz", float(g.uniform(-3, 3)), q)
+        for q in range(n):
+            c.append("cnot", (q, (q + 1) % n))
+        c.append("x", (int(g.integers(0, n)),))
+    return c
+
+
+def check_qnn_like(runtime, oracle):
+    for n in (10, 14):
+        c = qnn_like(n, n)
+        g = np.random.Generator(np.random.PCG64(n + 1))
+        check(runtime, oracle, c.compile_plan(1), n, random_terms(g, n, 10),
+              random_state(g, n), list(c.requires_grad_mask(True)), 0.9)
+
+
+def test_fast_cnot_paths_emulate_correctly_and_compile():
+    """ARCQML_FAST_CNOT=1 (subprocess): X and CNOT as register exchanges; random plans and
+    CNOT-ring circuits match the oracle through the emulator, and the 10-qubit CNOT-ring
+    circuit's passes all have compiled forms that compile."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import oracle, test_planner_emulation as T\n"
+            "from arcqml_b200 import runtime\n"
+            "for n, m in ((8, 150), (10, 200), (13, 160)):\n"
+            "    T.test_random_plans_over_every_opcode(runtime, oracle, n, m)\n"
+            "T.check_qnn_like(runtime, oracle)\n"
+            "p = runtime.CircuitPlan.create(T.qnn_like(10, 3).compile_plan(1))\n"
+            "for adj in (False, True):\n"
+            "    r = p.jit_check(10, adj)\n"
+            "    assert r['eligible'] >= 1 and r['compiled'] == r['eligible'], r\n"
+            "print('cnot-ok')\n") % (root, here, os.path.join(root, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_FAST_CNOT="1"), timeout=600)
+    assert r.returncode == 0 and "cnot-ok" in r.stdout, r.stdout + r.stderr
+
+
+def test_cnot_ring_circuits_in_the_default_configuration(runtime, oracle):
+    check_qnn_like(runtime, oracle)
