@@ -457,35 +457,6 @@ __device__ __forceinline__ bool apply_fast(const FOp &o, const double2 *mt, doub
     case FC_SIGN_CC:
         f_sign_cc<RB>(v, (const_bit(o, 0, tb, gbase) & const_bit(o, 1, tb, gbase)) ? 0x80000000u : 0u);
         return true;
-    case FC_X: {
-#define C_(B) f_x<RB, B>(v)
-        ARCQML_BITS(o.rb0, C_)
-#undef C_
-        return true;
-    }
-    case FC_CX_RR: {
-#define C1_(BC, BT) f_cx_rr<RB, BC, BT>(v)
-#define C_(BT)                                                   \
-    switch (o.rb1) {                                             \
-    case 0: if constexpr (BT != 0) { C1_(0, BT); } break;        \
-    case 1: if constexpr (BT != 1) { C1_(1, BT); } break;        \
-    case 2: if constexpr (BT != 2) { C1_(2, BT); } break;        \
-    default:                                                     \
-        if constexpr (RB > 3 && BT != 3) { C1_(3, BT); }         \
-        break;                                                   \
-    }
-        ARCQML_BITS(o.rb0, C_)
-#undef C_
-#undef C1_
-        return true;
-    }
-    case FC_CX_CR: {
-        const uint32_t on = const_bit(o, 0, tb, gbase);
-#define C_(B) f_cx_cr<RB, B>(v, on)
-        ARCQML_BITS(o.rb0, C_)
-#undef C_
-        return true;
-    }
     case FC_M4: {
 #define C1_(B0, B1) f_m4<RB, B0, B1>(v, mt)
 #define C_(B1)                                                   \

@@ -95,7 +95,8 @@ struct SubBlock {
     uint16_t op_begin, op_end;
     uint32_t flags;          // SB_ALL_FAST: every op of the sub-block has a fast path
 };
-constexpr uint32_t SB_ALL_FAST = 1;
+constexpr uint32_t SB_ALL_FAST = 1;  // the table-driven kernel has a fast path for every op
+constexpr uint32_t SB_JIT_FAST = 2;  // the run-time compiled kernels have one for every op
 static_assert(sizeof(SubBlock) == 24, "SubBlock layout");
 
 struct PassHeader {

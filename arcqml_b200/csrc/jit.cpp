@@ -269,7 +269,7 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "        switch (sb) {\n";
     for (size_t sb = 0; sb < st.subs.size(); ++sb) {
         const SubBlock &S = st.subs[sb];
-        if (!(S.flags & SB_ALL_FAST)) return std::string();
+        if (!(S.flags & SB_JIT_FAST)) return std::string();
         // Swizzled shared-memory slot of register element e: phys is linear over XOR and tb
         // shares no bit with the element's register bits, so slot = phys(tb) ^ phys(bits of e).
         std::vector<uint32_t> slot(size_t(1) << rb);

@@ -171,7 +171,7 @@ double2 cmulh(double2 a, double2 b) {
 void scale_pass(Step &st, bool adjoint) {
     if (!scaled_passes()) return;
     for (const SubBlock &sb : st.subs)
-        if (!(sb.flags & SB_ALL_FAST)) return;  // runs on the table-driven kernel
+        if (!(sb.flags & SB_JIT_FAST)) return;  // runs on the table-driven kernel
     const size_t base = st.mats.size();
     std::vector<double2> extra;
     double2 sigma = make_double2(1.0, 0.0);
@@ -307,9 +307,17 @@ void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
 // a fast apply; the adjoint pass also needs the gradient, if any, on the same fast path.
 bool has_fast_path(const FOp &o, bool adjoint) {
     if (o.code == FC_GENERIC) return false;
+    if (o.code == FC_X || o.code == FC_CX_RR || o.code == FC_CX_CR) return false;
     if (!adjoint || o.gkind == GK_NONE) return true;
     return (o.code == FC_RX && o.gcode == GF_X) || (o.code == FC_RY && o.gcode == GF_Y) ||
            (o.code == FC_D1_REG && o.gcode == GF_Z_REG) || (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
+}
+
+// The run-time compiled kernels also have fast paths for X and CNOT on register bits
+// (register exchanges); the table-driven kernel runs those through its generic path.
+bool has_jit_fast_path(const FOp &o, bool adjoint) {
+    if (o.code == FC_X || o.code == FC_CX_RR || o.code == FC_CX_CR) return o.gkind == GK_NONE;
+    return has_fast_path(o, adjoint);
 }
 
 // Residue of a tile bit under the shared-memory swizzle (fold of 3-bit groups).
@@ -674,9 +682,11 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 st.ops.push_back(o);
             }
             s.op_end = uint16_t(st.ops.size());
-            s.flags = SB_ALL_FAST;
-            for (size_t oi = s.op_begin; oi < s.op_end; ++oi)
-                if (!has_fast_path(st.ops[oi], adjoint)) s.flags = 0;
+            s.flags = SB_ALL_FAST | SB_JIT_FAST;
+            for (size_t oi = s.op_begin; oi < s.op_end; ++oi) {
+                if (!has_fast_path(st.ops[oi], adjoint)) s.flags &= ~SB_ALL_FAST;
+                if (!has_jit_fast_path(st.ops[oi], adjoint)) s.flags &= ~SB_JIT_FAST;
+            }
             st.subs.push_back(s);
         }
         scale_pass(st, adjoint);
