@@ -156,3 +156,16 @@ def test_fast_cnot_paths_emulate_correctly_and_compile():
 
 def test_cnot_ring_circuits_in_the_default_configuration(runtime, oracle):
     check_qnn_like(runtime, oracle)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_random_plan_sweep(runtime, oracle, seed):
+    """Random plans over every opcode on 8-16 qubits (every tile size the fused path uses,
+    3 and 4 forward register bits), forward and adjoint through the emulated schedules."""
+    g = np.random.Generator(np.random.PCG64(9000 + seed))
+    n = (8, 9, 11, 12, 14, 16)[seed]
+    npar = int(g.integers(3, 12))
+    ops = random_plan(g, n, int(g.integers(80, 260)), npar)
+    req = [int(g.uniform() < 0.3)] + [int(x) for x in (g.uniform(size=npar) < 0.8)]
+    check(runtime, oracle, ops, n, random_terms(g, n, int(g.integers(5, 30))),
+          random_state(g, n), req, float(g.normal()))
