@@ -714,6 +714,61 @@ int32_t arcqml_rt_v2_adjoint_backward(const CircuitPlanHandle *plan, arcqml_c128
     });
 }
 
+int32_t arcqml_rt_v2_plan_schedule_export(const CircuitPlanHandle *plan, size_t num_qubits,
+                                          int32_t adjoint, const uint8_t *parameter_requires_grad,
+                                          size_t parameter_requires_grad_len, uint8_t *buffer,
+                                          size_t capacity, size_t *size) {
+    return guarded([&] {
+        Plan *p = plan_of(plan);
+        state_dimension(num_qubits);
+        if (!size) fail("size pointer is null");
+        const uint32_t n = uint32_t(num_qubits);
+        if (n < kFusedMinQubits) fail("plans below 8 qubits run no fused passes");
+        validate_plan_for_state(*p, n);
+        std::vector<uint8_t> req(parameter_requires_grad,
+                                 parameter_requires_grad + parameter_requires_grad_len);
+        if (adjoint) check_bindings(*p, req.size(), req.size());
+        const uint32_t k = fused_k(n, adjoint != 0);
+        const uint32_t rb = adjoint ? fused_rb(k, true) : forward_rb(k);
+        const Schedule sch = build_schedule(*p, n, adjoint != 0, req.empty() ? nullptr : req.data(),
+                                            adjoint != 0, k, rb);
+        std::vector<uint8_t> out;
+        auto put = [&](const void *src, size_t bytes) {
+            const uint8_t *b = static_cast<const uint8_t *>(src);
+            out.insert(out.end(), b, b + bytes);
+        };
+        auto put32 = [&](uint64_t v) {
+            const uint32_t x = uint32_t(v);
+            put(&x, 4);
+        };
+        put32(sch.steps.size());
+        for (const Step &st : sch.steps) {
+            put32(st.is_pass ? 1 : 0);
+            if (!st.is_pass) {
+                put32(uint64_t(st.dense_op - p->ops.data()));
+                continue;
+            }
+            put(&st.header, sizeof(PassHeader));
+            put32(st.subs.size());
+            put(st.subs.data(), st.subs.size() * sizeof(SubBlock));
+            put32(st.ops.size());
+            put(st.ops.data(), st.ops.size() * sizeof(FOp));
+            put32(st.mats.size());
+            put(st.mats.data(), st.mats.size() * sizeof(double2));
+            put32(st.parents.size());
+            for (size_t pa : st.parents) {
+                const uint64_t x = pa;
+                put(&x, 8);
+            }
+            const std::string code = jit_pass_code(st, adjoint != 0);
+            put32(code.size());
+            put(code.data(), code.size());
+        }
+        *size = out.size();
+        if (buffer && capacity >= out.size()) std::memcpy(buffer, out.data(), out.size());
+    });
+}
+
 int32_t arcqml_rt_v2_plan_emulate(const CircuitPlanHandle *plan, arcqml_c128 *state,
                                   size_t num_qubits, int32_t adjoint, arcqml_c128 *lambda,
                                   const uint8_t *parameter_requires_grad,

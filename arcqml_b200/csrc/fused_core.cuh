@@ -2,7 +2,9 @@
 // per-pass kernels compiled at run time (jit.cpp embeds this file's text).
 //
 // Included inside namespace arcqml after fused.h. Compiles under nvcc and NVRTC alike: it uses
-// no standard headers.
+// no standard headers. With ARCQML_HOST_RUN defined, the parts that only a GPU can run
+// (asynchronous copies, warp shuffles, the tile loop) are left out, so that a host build of a
+// compiled pass's code can be executed on the CPU by a test.
 #pragma once
 
 __device__ __forceinline__ uint32_t phys(uint32_t j) {
@@ -22,6 +24,7 @@ __device__ __forceinline__ double icm(double2 a, double2 b) { return fma(a.x, b.
 
 __device__ __forceinline__ double2 ld(const double2 *p) { return *p; }
 
+#ifndef ARCQML_HOST_RUN  // device-only: not in host builds of the pass code (tests)
 // 16-byte asynchronous global -> shared copy (LDGSTS); completion via commit/wait groups.
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
@@ -40,6 +43,7 @@ __device__ __forceinline__ void accumulate_warp(double *sacc, uint32_t row, doub
     for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
     if ((threadIdx.x & 31u) == 0) sacc[row + (threadIdx.x >> 5)] += z;
 }
+#endif
 
 // Adds z into this thread's own column of accumulator row `row` (= acc * blockDim.x): no
 // cross-lane traffic per gate; the columns are summed once per pass at the end of the kernel.
@@ -383,6 +387,7 @@ __device__ __forceinline__ uint32_t thread_base(const SubBlock &S, uint32_t k) {
     return tb;
 }
 
+#ifndef ARCQML_HOST_RUN
 // Sub-block sb of the pass table, read through the read-only cache.
 __device__ __forceinline__ SubBlock load_subblock(const SubBlock *subs, uint32_t sb) {
     SubBlock S;
@@ -544,3 +549,4 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         }
     }
 }
+#endif  // ARCQML_HOST_RUN

@@ -395,6 +395,10 @@ std::string g_last_error;
 
 }  // namespace
 
+std::string jit_pass_code(const Step &st, bool adjoint) {
+    return st.is_pass ? pass_source(st, adjoint, st.header.rb) : std::string();
+}
+
 bool jit_enabled() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_JIT");

@@ -13,6 +13,9 @@ namespace arcqml {
 
 // False when ARCQML_JIT=0.
 bool jit_enabled();
+// The `struct PassOps` source the run-time compiler generates for a pass (empty when the pass
+// has no compiled form); a test builds it as host code (ARCQML_HOST_RUN) and runs it.
+std::string jit_pass_code(const Step &st, bool adjoint);
 // Per step of the schedule: its compiled kernel, or nullptr where the step has no compiled form
 // (a dense barrier, an op without a fast path, or a failed compile) and the precompiled pass
 // kernel runs instead. Kernels are compiled once per circuit structure and device.

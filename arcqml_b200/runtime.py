@@ -126,6 +126,7 @@ def load():
                                             I32, P]),
         "arcqml_rt_v2_small_run": (I32, [P, P, P, S, P, S, P, S, P, P, P]),
         "arcqml_rt_v2_plan_emulate": (I32, [P, P, S, I32, P, P, S, P, S]),
+        "arcqml_rt_v2_plan_schedule_export": (I32, [P, S, I32, P, S, P, S, P]),
         "arcqml_rt_v2_probabilities": (I32, [P, S, S, P, P]),
         "arcqml_rt_v2_marginal_probabilities": (I32, [P, S, S, P, S, P, P]),
         "arcqml_rt_v2_bloch_vector": (I32, [P, S, S, S, P, P]),
@@ -700,6 +701,20 @@ def plan_emulate(plan: CircuitPlan, state, num_qubits: int, adjoint: bool = Fals
                                              lm.ctypes.data, req.ctypes.data, req.size,
                                              grads.ctypes.data, grads.size))
     return a, lm, grads
+
+
+def plan_schedule_export(plan: CircuitPlan, num_qubits: int, adjoint: bool = False,
+                         requires_grad=None) -> bytes:
+    """The engine's fused-pass schedule for the plan, serialised (arcqml_rt_v2_plan_schedule_export)."""
+    req = np.ascontiguousarray([] if requires_grad is None else requires_grad, dtype=np.uint8)
+    rp = req.ctypes.data if req.size else None
+    size = C.c_size_t()
+    _status(load().arcqml_rt_v2_plan_schedule_export(C.byref(plan.raw), num_qubits, int(adjoint),
+                                                     rp, req.size, None, 0, C.byref(size)))
+    buf = (C.c_uint8 * max(1, size.value))()
+    _status(load().arcqml_rt_v2_plan_schedule_export(C.byref(plan.raw), num_qubits, int(adjoint),
+                                                     rp, req.size, buf, size.value, C.byref(size)))
+    return bytes(buf)[:size.value]
 
 
 # ---------------------------------------------------------------- state analysis

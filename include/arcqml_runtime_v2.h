@@ -250,6 +250,18 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
 int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qubits,
                                     int32_t adjoint, uint64_t *compiled, uint64_t *eligible,
                                     char *message, size_t capacity);
+/* The fused-pass schedule the engine builds for the plan (diagnostic and test support; no
+ * reference counterpart, no CUDA call), serialised into buffer when capacity allows; *size
+ * receives the byte count (call with buffer NULL to size it). Little-endian: u32 steps; per step
+ * u32 is_pass, then for a custom gate u32 op index, else the PassHeader, u32 count + SubBlocks,
+ * u32 count + FOps, u32 count + matrix entries (two doubles each), u32 count + u64 gradient
+ * parents, u32 length + the `struct PassOps` source of the pass's run-time compiled kernel
+ * (empty without one). The layouts are those of arcqml_b200/csrc/fused.h. */
+int32_t arcqml_rt_v2_plan_schedule_export(const CircuitPlanHandle *plan, size_t num_qubits,
+                                          int32_t adjoint, const uint8_t *parameter_requires_grad,
+                                          size_t parameter_requires_grad_len, uint8_t *buffer,
+                                          size_t capacity, size_t *size);
+
 /* Runs the fused-pass schedule the engine builds for the plan on a host state, on the CPU
  * (diagnostic and test support; no reference counterpart, no CUDA call): the same passes, tile
  * mapping, encoded ops, scaled forms and gradient factors as the device kernels, so the
