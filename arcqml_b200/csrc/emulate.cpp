@@ -220,6 +220,9 @@ void run_step(const Step &st, bool adjoint, Emu &E, const uint8_t *req, double *
             }
             apply(E.psi, n, su, u);
             if (adjoint && o.gkind == GK_GENERIC) {
+                // the op keeps its plain form, so psi and lambda both carry the pass factor
+                // sigma from before it: the stored sum times |sigma|^2 = 2 * mats[soff].y
+                const double f = (st.scaled && o.sgrad) ? 2.0 * st.mats[o.soff].y : 1.0;
                 static const int ulen[6] = {4, 1, 1, 2, 4, 16};
                 const int dl = o.kind == FK_D1 ? 2 : (o.kind == FK_D2 ? 4 : (o.kind == FK_M4 ? 16 : 4));
                 for (uint32_t sl = 0; sl < o.nslots; ++sl) {
@@ -228,7 +231,7 @@ void run_step(const Step &st, bool adjoint, Emu &E, const uint8_t *req, double *
                     for (int i = 0; i < dl; ++i) dm[i] = cx(d[i]);
                     Shape ds = s;
                     ds.diag = (o.kind == FK_D1 || o.kind == FK_D2);
-                    acc[o.acc[sl]] += re_inner(*E.lam, E.psi, n, ds, dm);
+                    acc[o.acc[sl]] += f * re_inner(*E.lam, E.psi, n, ds, dm);
                 }
             }
             if (adjoint) apply(*E.lam, n, su, u);

@@ -59,6 +59,11 @@ enum FastCode : uint8_t {
     FC_X = 10,       // uncontrolled X on register bit rb0 (register renaming)
     FC_CX_RR = 11,   // X on register bit rb0 where register bit rb1 (the control) is 1
     FC_CX_CR = 12,   // X on register bit rb0 where the per-thread bit dq 0 (the control) is 1
+    // Run-time compiled kernels only (ARCQML_FAST_DIAG=1): each qubit of the op (diagonal
+    // slots, controls) is a register bit or a per-thread value, resolved when the code is
+    // generated; the table-driven kernel runs these codes through its generic path.
+    FC_DIAG = 13,    // diagonal (FK_D1 / FK_D2) with any controls
+    FC_CM2 = 14,     // one-target gate (FK_RX / FK_RY / FK_M2) on rb0 with controls
 };
 
 enum GradFast : uint8_t {

@@ -300,6 +300,52 @@ __device__ __forceinline__ double g_z_uni(const double2 (&v)[1 << RB], const dou
     return (z[0] + z[1]) + (z[2] + z[3]);
 }
 
+// One-target gates and gradient terms on one register pair (x0 / v0 / w0: target bit 0), for
+// controlled gates in compiled passes, whose code lists the pairs with every control set.
+__device__ __forceinline__ void p_rx(double2 &x0, double2 &x1, double c, double s) {
+    const double2 a = x0, b = x1;
+    x0 = make_double2(fma(c, a.x, s * b.y), fma(c, a.y, -s * b.x));
+    x1 = make_double2(fma(c, b.x, s * a.y), fma(c, b.y, -s * a.x));
+}
+__device__ __forceinline__ void p_ry(double2 &x0, double2 &x1, double c, double s) {
+    const double2 a = x0, b = x1;
+    x0 = make_double2(fma(c, a.x, -s * b.x), fma(c, a.y, -s * b.y));
+    x1 = make_double2(fma(s, a.x, c * b.x), fma(s, a.y, c * b.y));
+}
+__device__ __forceinline__ void p_m2(double2 &x0, double2 &x1, const double2 *mt) {
+    const double2 a = x0, b = x1;
+    x0 = cfma(mt[0], a, cmul(mt[1], b));
+    x1 = cfma(mt[2], a, cmul(mt[3], b));
+}
+// Im<lam|X|psi> and Im<lam|Y|psi> over one pair (psi v, lambda w)
+__device__ __forceinline__ double p_gx(double2 v0, double2 v1, double2 w0, double2 w1) {
+    return icm(w0, v1) + icm(w1, v0);
+}
+__device__ __forceinline__ double p_gy(double2 v0, double2 v1, double2 w0, double2 w1) {
+    return rcm(w1, v0) - rcm(w0, v1);
+}
+// Re<lam| D |psi> over one pair for a dense 2x2 D
+__device__ __forceinline__ double p_gm2(const double2 *d, double2 v0, double2 v1, double2 w0,
+                                        double2 w1) {
+    return rcm(w0, cfma(d[0], v0, cmul(d[1], v1))) + rcm(w1, cfma(d[2], v0, cmul(d[3], v1)));
+}
+// Re<lam| D |psi> over one group of four for a dense 4x4 D (group index bit 0: rb0, bit 1: rb1)
+__device__ __forceinline__ double q_gm4(const double2 *d, double2 v0, double2 v1, double2 v2,
+                                        double2 v3, double2 w0, double2 w1, double2 w2,
+                                        double2 w3) {
+    const double2 x[4] = {v0, v1, v2, v3}, l[4] = {w0, w1, w2, w3};
+    double t = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        double2 acc = cmul(d[i * 4], x[0]);
+        acc = cfma(d[i * 4 + 1], x[1], acc);
+        acc = cfma(d[i * 4 + 2], x[2], acc);
+        acc = cfma(d[i * 4 + 3], x[3], acc);
+        t += rcm(l[i], acc);
+    }
+    return t;
+}
+
 
 // Per-thread value of a qubit that is not a register bit: a tile bit lives in the thread's
 // base index tb, a qubit outside the tile in the tile's global base.

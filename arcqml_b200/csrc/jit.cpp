@@ -155,10 +155,136 @@ std::string const_bit(const FOp &o, int slot, const SubBlock &S, uint32_t thread
     return e.str();
 }
 
+// ---------------------------------------------------------------- ops on general bit positions
+//
+// ARCQML_FAST_DIAG=1 (FC_DIAG, FC_CM2 and the generic gradients): every qubit of the op — a
+// diagonal index bit or a control — is a register bit of the sub-block, known per register
+// element when the code is generated, or a per-thread 0/1 value (a thread bit of the tile, or
+// a bit of the tile's global base). Register controls select the elements the code lists;
+// per-thread controls become one condition around them.
+
+struct BitPos {
+    int reg = -1;     // register bit, or -1
+    std::string val;  // otherwise the per-thread value ("" if the bit is neither)
+};
+
+BitPos tile_bit_pos(uint32_t lb, const SubBlock &S, uint32_t rb, uint32_t tbits) {
+    BitPos p;
+    for (uint32_t r = 0; r < rb; ++r)
+        if (S.R[r] == lb) {
+            p.reg = int(r);
+            return p;
+        }
+    for (uint32_t i = 0; i < tbits; ++i)
+        if (S.perm[i] == lb) {
+            p.val = "((tid >> " + std::to_string(i) + ") & 1u)";
+            return p;
+        }
+    return p;
+}
+
+BitPos global_bit_pos(uint32_t q) {
+    BitPos p;
+    p.val = "uint32_t((gbase >> " + std::to_string(q) + ") & 1ull)";
+    return p;
+}
+
+struct OpBits {
+    bool ok = true;
+    uint32_t creg = 0;  // register bits every control of which must be 1
+    std::string cond;   // per-thread control condition ("" if none)
+    int nslot = 0;      // diagonal ops: entry index = sum over slots s of bit(s) << s
+    BitPos slot[2];
+    std::string uval;   // per-thread part of the entry index ("" if none)
+
+    bool active(uint32_t e) const { return (e & creg) == creg; }
+    uint32_t entry(uint32_t e) const {  // register part of element e's entry index
+        uint32_t x = 0;
+        for (int s = 0; s < nslot; ++s)
+            if (slot[s].reg >= 0) x |= ((e >> slot[s].reg) & 1u) << s;
+        return x;
+    }
+    std::string open() const { return cond.empty() ? "{ " : "if (" + cond + ") { "; }
+    // matrix-table element of entry x (its per-thread part in `u`)
+    std::string at(uint32_t base, uint32_t x) const {
+        std::ostringstream e;
+        if (uval.empty()) e << "M[" << base + x << "]";
+        else e << "M[" << base << "u + (u | " << x << "u)]";
+        return e.str();
+    }
+    std::string decl_u() const { return uval.empty() ? "" : "const uint32_t u = " + uval + "; "; }
+};
+
+OpBits op_bits(const FOp &o, const SubBlock &S, uint32_t rb, uint32_t tbits) {
+    OpBits b;
+    std::vector<std::string> conds;
+    for (uint32_t t = 0; t < 16; ++t) {
+        if (!((o.lcmask >> t) & 1u)) continue;
+        const BitPos p = tile_bit_pos(t, S, rb, tbits);
+        if (p.reg >= 0) b.creg |= 1u << p.reg;
+        else if (!p.val.empty()) conds.push_back(p.val);
+        else b.ok = false;
+    }
+    for (uint32_t q = 0; q < 64; ++q)
+        if ((o.gcmask >> q) & 1u) conds.push_back(global_bit_pos(q).val);
+    for (size_t i = 0; i < conds.size(); ++i) b.cond += (i ? " & " : "") + conds[i];
+    if (o.kind == FK_D1 || o.kind == FK_D2) {
+        b.nslot = o.kind == FK_D1 ? 1 : 2;
+        for (int s = 0; s < b.nslot; ++s) {
+            b.slot[s] = o.dq_in_tile[s] ? tile_bit_pos(o.dq_pos[s], S, rb, tbits)
+                                        : global_bit_pos(o.dq_pos[s]);
+            const BitPos &p = b.slot[s];
+            if (p.reg >= 0) continue;
+            if (p.val.empty()) b.ok = false;
+            if (!b.uval.empty()) b.uval += " | ";
+            b.uval += s ? "(" + p.val + " << 1)" : p.val;
+        }
+    }
+    return b;
+}
+
+// U (or U^dagger) of an FC_DIAG or FC_CM2 op on the register array `r`.
+bool emit_general_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
+                        const SubBlock &S, uint32_t tbits) {
+    const OpBits b = op_bits(o, S, rb, tbits);
+    if (!b.ok) return false;
+    const uint32_t N = 1u << rb, m = o.moff;
+    if (o.code == FC_DIAG) {
+        if (b.nslot == 0) return false;
+        c << "{ " << b.decl_u() << b.open();
+        bool need[4] = {false, false, false, false};
+        for (uint32_t e = 0; e < N; ++e)
+            if (b.active(e)) need[b.entry(e)] = true;
+        for (uint32_t x = 0; x < 4; ++x)
+            if (need[x]) c << "const double2 d" << x << " = " << b.at(m, x) << "; ";
+        for (uint32_t e = 0; e < N; ++e)
+            if (b.active(e))
+                c << r << "[" << e << "] = cmul(d" << b.entry(e) << ", " << r << "[" << e << "]); ";
+        c << "} }";
+        return true;
+    }
+    if (o.code != FC_CM2) return false;
+    const uint32_t t = 1u << o.rb0;
+    if (o.rb0 >= rb || (b.creg & t)) return false;
+    c << "{ " << b.open();
+    for (uint32_t e = 0; e < N; ++e) {
+        if ((e & t) || !b.active(e)) continue;
+        const std::string x0 = std::string(r) + "[" + std::to_string(e) + "]";
+        const std::string x1 = std::string(r) + "[" + std::to_string(e | t) + "]";
+        if (o.kind == FK_RX) c << "p_rx(" << x0 << ", " << x1 << ", M[" << m << "].x, M[" << m << "].y); ";
+        else if (o.kind == FK_RY) c << "p_ry(" << x0 << ", " << x1 << ", M[" << m << "].x, M[" << m << "].y); ";
+        else if (o.kind == FK_M2) c << "p_m2(" << x0 << ", " << x1 << ", M + " << m << "); ";
+        else return false;
+    }
+    c << "} }";
+    return true;
+}
+
 // The fast path of op o on the register array `r` (U in forward passes, U^dagger in adjoint
 // passes: the planner stores the daggered matrices). False for a combination without one.
 bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
                 const SubBlock &S, uint32_t tbits) {
+    if (o.code == FC_DIAG || o.code == FC_CM2) return emit_general_apply(c, o, r, rb, S, tbits);
     const int b0 = o.rb0, b1 = o.rb1;
     const std::string bit0 = (o.code == FC_D1_UNI || o.code == FC_SIGN_RC || o.code == FC_SIGN_CC ||
                               o.code == FC_CX_CR)
@@ -217,6 +343,118 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
     return true;
 }
 
+// Gradients on general bit positions (ARCQML_FAST_DIAG=1), in the order of the table-driven
+// kernel: a Pauli-rotation gradient Im<lam|P|psi> on psi before U^dagger (X / Y over the
+// target pairs whose controls are set, Z with the sign of the target bit), then U^dagger on
+// psi, then each generic slot gradient Re<lam| dU_s |U^dagger psi>, then U^dagger on lambda.
+// In a scaled pass psi and lambda carry the pass factor sigma from before the op (which keeps
+// its plain form), so each sum is multiplied by |sigma|^2 = 2 * mats[soff].y.
+bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
+                          uint32_t tbits) {
+    const OpBits b = op_bits(o, S, rb, tbits);
+    if (!b.ok) return false;
+    const bool diag = o.kind == FK_D1 || o.kind == FK_D2;
+    const bool one = o.kind == FK_RX || o.kind == FK_RY || o.kind == FK_M2;
+    const bool four = o.kind == FK_M4;
+    const uint32_t N = 1u << rb, t0 = 1u << o.rb0, t1 = 1u << o.rb1;
+    if ((one || four) && (o.rb0 >= rb || (b.creg & t0))) return false;
+    if (four && (o.rb1 >= rb || o.rb1 == o.rb0 || b.creg || !b.cond.empty())) return false;
+    const std::string so = std::to_string(o.soff);
+    auto put_acc = [&](uint32_t slot, bool pauli) {
+        c << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
+          << o.acc[slot] << "u * kCols, ";
+        if (pauli) c << (o.sgrad ? "M[" + so + "].y * z); " : "0.5 * z); ");
+        else c << (o.sgrad ? "2.0 * M[" + so + "].y * z); " : "z); ");
+    };
+    auto apply_to = [&](const char *r) {
+        c << "\n        ";
+        if (!emit_apply(c, o, r, rb, S, tbits)) return false;
+        c << "\n        ";
+        return true;
+    };
+    auto apply_both = [&]() { return apply_to("v") && apply_to("w"); };
+    auto reg = [](const char *a, uint32_t e) { return std::string(a) + "[" + std::to_string(e) + "]"; };
+    if (o.gkind == GK_PX || o.gkind == GK_PY) {
+        if (!one) return false;
+        c << "{ double z = 0.0; " << b.open();
+        for (uint32_t e = 0; e < N; ++e) {
+            if ((e & t0) || !b.active(e)) continue;
+            const uint32_t f = e | t0;
+            c << "z += " << (o.gkind == GK_PX ? "p_gx(" : "p_gy(") << reg("v", e) << ", "
+              << reg("v", f) << ", " << reg("w", e) << ", " << reg("w", f) << "); ";
+        }
+        c << "}";
+        if (!apply_both()) return false;
+        put_acc(0, true);
+        c << "}";
+        return true;
+    }
+    if (o.gkind == GK_PZ) {
+        if (o.kind != FK_D1) return false;
+        const BitPos &q = b.slot[0];
+        c << "{ double z = 0.0; " << b.open();
+        for (uint32_t e = 0; e < N; ++e) {
+            if (!b.active(e)) continue;
+            const bool neg = q.reg >= 0 && ((e >> q.reg) & 1u);
+            c << "z " << (neg ? "-" : "+") << "= icm(" << reg("w", e) << ", " << reg("v", e) << "); ";
+        }
+        c << "} ";
+        if (q.reg < 0) c << "if (" << q.val << ") z = -z;";
+        if (!apply_both()) return false;
+        put_acc(0, true);
+        c << "}";
+        return true;
+    }
+    if (o.gkind != GK_GENERIC) return false;
+    // U's entries, then nslots derivative blocks of the same shape (diagonals: their diagonal)
+    const uint32_t ulen = o.kind == FK_RX || o.kind == FK_RY ? 1u
+                          : o.kind == FK_M2 ? 4u : o.kind == FK_D1 ? 2u : o.kind == FK_D2 ? 4u : 16u;
+    const uint32_t dlen = o.kind == FK_D1 ? 2u : o.kind == FK_M4 ? 16u : 4u;
+    if (o.nslots < 1 || o.nslots > 3) return false;
+    c << "{";
+    if (!apply_to("v")) return false;
+    for (uint32_t s = 0; s < o.nslots; ++s) {
+        const uint32_t d = o.moff + ulen + s * dlen;
+        c << "{ double z = 0.0; ";
+        if (diag) {
+            c << b.decl_u() << b.open();
+            bool need[4] = {false, false, false, false};
+            for (uint32_t e = 0; e < N; ++e)
+                if (b.active(e)) need[b.entry(e)] = true;
+            for (uint32_t x = 0; x < 4; ++x)
+                if (need[x]) c << "const double2 g" << x << " = " << b.at(d, x) << "; ";
+            for (uint32_t e = 0; e < N; ++e)
+                if (b.active(e))
+                    c << "z += rcm(" << reg("w", e) << ", cmul(g" << b.entry(e) << ", "
+                      << reg("v", e) << ")); ";
+        } else if (one) {
+            c << b.open();
+            for (uint32_t e = 0; e < N; ++e) {
+                if ((e & t0) || !b.active(e)) continue;
+                const uint32_t f = e | t0;
+                c << "z += p_gm2(M + " << d << ", " << reg("v", e) << ", " << reg("v", f) << ", "
+                  << reg("w", e) << ", " << reg("w", f) << "); ";
+            }
+        } else {
+            c << "{ ";
+            for (uint32_t e = 0; e < N; ++e) {
+                if (e & (t0 | t1)) continue;
+                const uint32_t i[4] = {e, e | t0, e | t1, e | t0 | t1};
+                c << "z += q_gm4(M + " << d;
+                for (const char *a : {"v", "w"})
+                    for (uint32_t j : i) c << ", " << reg(a, j);
+                c << "); ";
+            }
+        }
+        c << "} ";
+        put_acc(s, false);
+        c << "}";
+    }
+    if (!apply_to("w")) return false;
+    c << "}";
+    return true;
+}
+
 // Gradient then U^dagger on psi and lambda, as adj_fast does it.
 bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
                   uint32_t tbits) {
@@ -225,6 +463,11 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
         c << "\n        ";
         return emit_apply(c, o, "w", rb, S, tbits);
     }
+    const bool pauli_fast = (o.code == FC_RX && o.gcode == GF_X) ||
+                            (o.code == FC_RY && o.gcode == GF_Y) ||
+                            (o.code == FC_D1_REG && o.gcode == GF_Z_REG) ||
+                            (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
+    if (!pauli_fast) return fast_diag() && emit_adjoint_general(c, o, rb, S, tbits);
     const int b0 = o.rb0;
     if (b0 >= int(rb) && o.code != FC_D1_UNI) return false;
     c << "{ double z; ";

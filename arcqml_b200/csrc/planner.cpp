@@ -182,11 +182,13 @@ void scale_pass(Step &st, bool adjoint) {
         bool sc = false;
         double tau = 0.0;
         double2 f = make_double2(1.0, 0.0);
-        if ((o.code == FC_RX || o.code == FC_RY) && m[0].x != 0.0) {
+        // a generic slot gradient is taken on U^dagger psi: its op keeps the plain form
+        const bool keep = o.gkind == GK_GENERIC;
+        if (!keep && (o.code == FC_RX || o.code == FC_RY) && m[0].x != 0.0) {
             tau = m[0].y / m[0].x;
             f = make_double2(m[0].x, 0.0);
             sc = true;
-        } else if (o.code == FC_D1_REG || o.code == FC_D1_UNI) {
+        } else if (!keep && (o.code == FC_D1_REG || o.code == FC_D1_UNI)) {
             const double a0 = std::hypot(m[0].x, m[0].y), a1 = std::hypot(m[1].x, m[1].y);
             if (a0 > 0.0 && std::fabs(a0 - a1) <= 1e-14 * a0) {
                 // r = d1 / d0 = e^{2ig}
@@ -265,9 +267,14 @@ void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
             o.code = o.kind == FK_RX ? FC_RX : (o.kind == FK_RY ? FC_RY : FC_M2);
         else if (plain && nt == 2)
             o.code = FC_M4;
+        else if (fast_diag() && nt == 1)
+            o.code = FC_CM2;
         return;
     }
-    if (nt != 1) return;
+    if (nt != 1) {
+        if (fast_diag()) o.code = FC_DIAG;
+        return;
+    }
     const uint32_t t = g.targets[0];
     if (plain) {
         const uint8_t r = reg_of(t);
@@ -281,7 +288,10 @@ void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
     }
     const double2 d0 = g.m[0], d1 = g.m[3];
     const bool sign = d0.x == 1.0 && d0.y == 0.0 && d1.x == -1.0 && d1.y == 0.0;
-    if (!sign || g.controls.size() != 1) return;
+    if (!sign || g.controls.size() != 1) {
+        if (fast_diag()) o.code = FC_DIAG;
+        return;
+    }
     const uint32_t c = g.controls[0];  // CZ-like: -1 where both c and t are 1
     const uint8_t rc = reg_of(c), rt = reg_of(t);
     if (rc != 0xFF && rt != 0xFF) {
@@ -308,15 +318,37 @@ void classify(FOp &o, const PGate &g, const RegOf &reg_of, const int *lpos) {
 bool has_fast_path(const FOp &o, bool adjoint) {
     if (o.code == FC_GENERIC) return false;
     if (o.code == FC_X || o.code == FC_CX_RR || o.code == FC_CX_CR) return false;
+    if (o.code == FC_DIAG || o.code == FC_CM2) return false;
     if (!adjoint || o.gkind == GK_NONE) return true;
     return (o.code == FC_RX && o.gcode == GF_X) || (o.code == FC_RY && o.gcode == GF_Y) ||
            (o.code == FC_D1_REG && o.gcode == GF_Z_REG) || (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
+}
+
+// With ARCQML_FAST_DIAG=1 the run-time compiled kernels also run diagonal gates with controls,
+// two-qubit diagonals and controlled one-target gates (FC_DIAG / FC_CM2), Pauli-rotation
+// gradients with controls or on dense 2x2 forms, and every generic slot gradient of a one- or
+// two-qubit diagonal, a one-target gate or an uncontrolled 4x4 (jit.cpp writes each as its
+// register arithmetic).
+bool has_jit_general_path(const FOp &o, bool adjoint) {
+    const bool diag = o.kind == FK_D1 || o.kind == FK_D2;
+    const bool one = o.kind == FK_RX || o.kind == FK_RY || o.kind == FK_M2;
+    switch (o.code) {
+    case FC_DIAG: if (!diag) return false; break;
+    case FC_CM2: if (!one) return false; break;
+    case FC_D1_REG: case FC_D1_UNI: case FC_RX: case FC_RY: case FC_M2: case FC_M4: break;
+    default: return false;
+    }
+    if (!adjoint || o.gkind == GK_NONE) return true;
+    if (o.gkind == GK_GENERIC) return true;
+    if (o.gkind == GK_PZ) return o.kind == FK_D1;
+    return one && (o.gkind == GK_PX || o.gkind == GK_PY);
 }
 
 // The run-time compiled kernels also have fast paths for X and CNOT on register bits
 // (register exchanges); the table-driven kernel runs those through its generic path.
 bool has_jit_fast_path(const FOp &o, bool adjoint) {
     if (o.code == FC_X || o.code == FC_CX_RR || o.code == FC_CX_CR) return o.gkind == GK_NONE;
+    if (fast_diag() && has_jit_general_path(o, adjoint)) return true;
     return has_fast_path(o, adjoint);
 }
 
@@ -407,6 +439,14 @@ void pack_subblocks(const std::vector<PGate> &gates, const std::vector<size_t> &
 bool fast_cnot() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FAST_CNOT");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
+bool fast_diag() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_FAST_DIAG");
         return e && e[0] == '1';
     }();
     return on;

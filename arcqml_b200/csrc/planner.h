@@ -38,6 +38,10 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
 // paths (ARCQML_FAST_CNOT=1; off by default) instead of a dense 2x2 / the generic path.
 bool fast_cnot();
 
+// Whether the run-time compiled kernels run diagonal gates with controls, two-qubit diagonals,
+// controlled one-target gates and generic slot gradients (ARCQML_FAST_DIAG=1; off by default).
+bool fast_diag();
+
 // Whether passes pack commuting gates into fewer register sub-blocks than circuit order gives
 // (ARCQML_SUBBLOCK_REORDER=1; off by default).
 bool subblock_reorder();

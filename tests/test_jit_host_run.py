@@ -93,6 +93,53 @@ def cnot_ring(n, seed):
     return c
 
 
+def general_shapes(n, seed):
+    """Gates that only ARCQML_FAST_DIAG=1 compiles: diagonals with controls (CPHASE, CRZ, CS,
+    CT), two-qubit diagonals (RZZ), controlled one-target gates (CRX, CRY, CH, CY, Toffoli,
+    3-control X), trained PHASE / U3 / RXX / RYY / RZX / fSim (generic slot gradients), with
+    qubits in registers, thread bits and outside the tile, and parameters shared across gates;
+    Pauli rotations keep the scaled passes mixed."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    c = cm.Circuit(n)
+    shared = c.add_parameter(float(g.uniform(-3, 3)))
+
+    def angle():
+        if g.uniform() < 0.2:
+            return shared
+        return c.add_parameter(float(g.uniform(-3, 3))) if g.uniform() < 0.8 else float(g.uniform(-3, 3))
+
+    def qubits(k):
+        return [int(x) for x in g.choice(n, size=k, replace=False)]
+    for _ in range(4):
+        for q in range(n):
+            if g.uniform() < 0.5:
+                c.rot(("rx", "ry", "rz")[int(g.integers(0, 3))], float(g.uniform(-3, 3)), q)
+        for _ in range(n):
+            r = int(g.integers(0, 16))
+            if r == 0:
+                c.append("phase", qubits(1), angle())
+            elif r == 1:
+                c.append("u3", qubits(1), angle(), angle(), angle())
+            elif r in (2, 3, 4, 5, 6):
+                c.append(("cphase", "crz", "crx", "cry", "rzz")[r - 2], qubits(2), angle())
+            elif r in (7, 8, 9):
+                a, b = qubits(2)
+                if g.uniform() < 0.6:  # neighbours: both targets in the tile more often
+                    a, b = a, (a + 1) % n
+                c.append(("rxx", "ryy", "rzx")[r - 7], (a, b), angle())
+            elif r == 10:
+                c.append("fsim", qubits(2), angle(), angle())
+            elif r in (11, 12, 13, 14):
+                c.append(("cs", "ct", "ch", "cy")[r - 11], qubits(2))
+            else:
+                qs = qubits(4)
+                if g.uniform() < 0.5:
+                    c.append("toffoli", qs[:3])
+                else:
+                    c.mcx(qs[:3], qs[3])
+    return c
+
+
 @pytest.mark.parametrize("env", ["ARCQML_SUBBLOCK_REORDER", "ARCQML_FAST_CNOT"])
 def test_switches_run_their_compiled_code_on_host(env):
     here = os.path.dirname(os.path.abspath(__file__))
@@ -109,3 +156,26 @@ def test_switches_run_their_compiled_code_on_host(env):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, **{env: "1"}), timeout=900)
     assert r.returncode == 0 and "host-run-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_general_bit_positions_run_their_compiled_code_on_host():
+    """ARCQML_FAST_DIAG=1 (subprocess): controlled diagonals, two-qubit diagonals, controlled
+    one-target gates and generic slot gradients as compiled pass code, run on the CPU against
+    the oracle; every pass of these circuits has a compiled form, and it compiles for sm_100a."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import oracle, test_jit_host_run as T\n"
+            "from arcqml_b200 import runtime\n"
+            "for n, seed in ((9, 1), (12, 2), (13, 3)):\n"
+            "    T.check(runtime, oracle, T.general_shapes(n, seed), n, seed=seed, terms=20)\n"
+            "T.check(runtime, oracle, T.brickwork_edges(10, 3), 10, seed=3)\n"
+            "T.check(runtime, oracle, T.fast_shapes(12, 4), 12, seed=4)\n"
+            "p = runtime.CircuitPlan.create(T.general_shapes(13, 5).compile_plan(1))\n"
+            "for adj in (False, True):\n"
+            "    r = p.jit_check(13, adj)\n"
+            "    assert r['eligible'] >= 1 and r['compiled'] == r['eligible'], r\n"
+            "print('general-ok')\n") % (root, here, os.path.join(root, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_FAST_DIAG="1"), timeout=1200)
+    assert r.returncode == 0 and "general-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

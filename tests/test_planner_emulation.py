@@ -169,3 +169,30 @@ def test_random_plan_sweep(runtime, oracle, seed):
     req = [int(g.uniform() < 0.3)] + [int(x) for x in (g.uniform(size=npar) < 0.8)]
     check(runtime, oracle, ops, n, random_terms(g, n, int(g.integers(5, 30))),
           random_state(g, n), req, float(g.normal()))
+
+
+def test_general_bit_position_schedules_emulate_correctly():
+    """ARCQML_FAST_DIAG=1 (subprocess): controlled diagonals, two-qubit diagonals and controlled
+    one-target gates get their compiled-kernel codes, and generic-gradient ops keep their plain
+    forms in scaled passes; random plans over every opcode and the general-shape circuits
+    match the oracle through the emulated schedules."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import numpy as np, oracle, test_planner_emulation as T, test_jit_host_run as H\n"
+            "from plans import random_state, random_terms\n"
+            "from arcqml_b200 import runtime\n"
+            "for n, m in ((8, 150), (10, 200), (13, 160)):\n"
+            "    T.test_random_plans_over_every_opcode(runtime, oracle, n, m)\n"
+            "for n, seed in ((9, 11), (13, 12), (16, 13)):\n"
+            "    c = H.general_shapes(n, seed)\n"
+            "    g = np.random.Generator(np.random.PCG64(seed))\n"
+            "    T.check(runtime, oracle, c.compile_plan(1), n, random_terms(g, n, 15),\n"
+            "            random_state(g, n), list(c.requires_grad_mask(True)), -1.3)\n"
+            "print('general-ok')\n") % (root, here, os.path.join(root, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_FAST_DIAG="1"), timeout=900)
+    assert r.returncode == 0 and "general-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
