@@ -140,6 +140,43 @@ def test_last_error_protocol(runtime):
     assert L.arcqml_rt_last_error(buf, 4) == n  # truncated copy, full length returned
 
 
+def test_last_error_is_per_thread(runtime):
+    """The status message is thread-local (callers fail concurrently from worker threads,
+    row_major.rs:116-130): each thread fails, waits until every thread has failed, then reads
+    its own message."""
+    import threading
+    L = runtime.load()
+    g = runtime.gate_descriptor(1, 1)
+    nthreads = 8
+    barrier = threading.Barrier(nthreads, timeout=60)
+    got = [None] * nthreads
+
+    def read():
+        n = L.arcqml_rt_last_error(None, 0)
+        buf = (C.c_uint8 * (n + 1))()
+        L.arcqml_rt_last_error(buf, n + 1)
+        return bytes(buf[:n]).decode()
+
+    def body(t):
+        a = np.zeros(t + 3, np.complex128)  # length t + 3 is never 2^1
+        q = (C.c_size_t * 1)(0)
+        for _ in range(50):
+            assert L.arcqml_rt_v1_apply_gate(a.ctypes.data, a.size, 1, C.byref(g), q, 1) != 0
+            barrier.wait()
+            msg = read()
+            if got[t] is None or f"got {t + 3}" in got[t]:
+                got[t] = msg  # keeps the first wrong message
+            barrier.wait()
+
+    threads = [threading.Thread(target=body, args=(t,)) for t in range(nthreads)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    for t in range(nthreads):
+        assert f"expected 2, got {t + 3}" in got[t], got
+
+
 def test_destroy_is_idempotent(runtime):
     L = runtime.load()
     h = runtime.CircuitPlanHandle()
