@@ -397,16 +397,16 @@ class RuntimeBackend:
 
     # -- peer transport (device addresses) --
     def marginal(self, shard, n_local: int, positions) -> np.ndarray:
-        return rt.marginal_probabilities_device(shard, n_local, list(positions)).cpu().numpy()
+        return self.rt.marginal_probabilities_device(shard, n_local, list(positions)).cpu().numpy()
 
     def bloch(self, shard, n_local: int, position: int) -> np.ndarray:
-        return rt.bloch_vector_device(shard, n_local, position)
+        return self.rt.bloch_vector_device(shard, n_local, position)
 
     def overlap(self, a, b, n_local: int) -> complex:
-        return rt.overlap_device(a, b, n_local)
+        return self.rt.overlap_device(a, b, n_local)
 
     def norm(self, shard, n_local: int) -> float:
-        return float(rt.norms_device(shard, n_local)[0])
+        return float(self.rt.norms_device(shard, n_local)[0])
 
     def peer_buffer(self, nbytes: int):
         return self.rt.PeerBuffer(nbytes)
