@@ -12,9 +12,9 @@ from shard_support import OracleShardBackend, run_threads
 TOL = 1e-12
 
 
-def close(a, b):
+def close(a, b, tol=TOL):
     a, b = np.asarray(a), np.asarray(b)
-    assert float(np.max(np.abs(a - b))) <= TOL * max(1.0, float(np.max(np.abs(b)))), (a, b)
+    assert float(np.max(np.abs(a - b))) <= tol * max(1.0, float(np.max(np.abs(b)))), (a, b)
 
 
 def sim_for(n, comm):
@@ -22,9 +22,9 @@ def sim_for(n, comm):
                                        chunk_amplitudes=1 << 3, transport="p2p")
 
 
-@pytest.mark.parametrize("size", [2, 4, 8])
-def test_marginals_bloch_and_overlap_of_sharded_states(size):
-    n = 7
+def analysis_world(size, n, sim_for, tol=TOL):
+    """Marginals, Bloch vectors, overlaps and fidelities of sharded states after a random plan,
+    on `size` thread ranks with simulators from sim_for(n, comm), against the oracle."""
     g = np.random.Generator(np.random.PCG64(size))
     a, b = random_state(g, n), random_state(g, n)
     ops = random_plan(g, n, 60, 4)
@@ -57,19 +57,28 @@ def test_marginals_bloch_and_overlap_of_sharded_states(size):
         return moved, marg, bloch, same, ov, err, s.fidelity(s) if same else None
 
     res = run_threads(size, body)
+    check_analysis(res, n, selections, want, want_b, tol)
+
+
+def check_analysis(res, n, selections, want, want_b, tol):
     assert any(r[0] for r in res)  # the plan's swaps permuted the layout
     assert all(r[3] for r in res) and any(r[5] is not None for r in res)
     for moved, marg, bloch, same, ov, err, fid in res:
         for m, q in zip(marg, selections):
-            close(m, O.marginal_probabilities(want, n, q))
+            close(m, O.marginal_probabilities(want, n, q), tol)
         for q in range(n):
-            close(bloch[q], O.bloch_vector(want, n, q))
+            close(bloch[q], O.bloch_vector(want, n, q), tol)
         if same:
             rs, _ = O.overlap_fidelity(want, want_b, n)
-            close([ov.real, ov.imag], [rs.real, rs.imag])
+            close([ov.real, ov.imag], [rs.real, rs.imag], tol)
             assert abs(fid - 1.0) < 1e-10
         if err is not None:
             assert "same qubit layout" in err
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_marginals_bloch_and_overlap_of_sharded_states(size):
+    analysis_world(size, 7, sim_for)
 
 
 def test_sharded_selection_errors():
