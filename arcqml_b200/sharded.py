@@ -17,7 +17,9 @@ bits. A layout maps every logical qubit to a physical bit position; positions be
 * The observable's terms are evaluated in groups, one per layout in which no flip bit (X/Y) of
   the group lies on a global qubit; a Z on a global qubit becomes a per-rank sign on the
   coefficient. ``H psi`` accumulates over the groups (``arcqml_rt_v2_expectation_and_accumulate``)
-  and moves with psi when the layout changes. The value is summed over ranks.
+  and moves with psi when the layout changes. The value is summed over ranks. A group that flips
+  more qubits than a shard holds (a global qubit is flipped in every layout) is evaluated against
+  the partner rank's shard instead, exchanged chunk by chunk (``_partner_terms``).
 * The adjoint sweep schedules the reversed op list from the observable's final layout, swaps psi
   and lambda together, and sums the per-rank gradient partials over ranks at the end.
 
@@ -101,6 +103,11 @@ class OpsStep:
 @dataclass
 class TermsStep:
     groups: List[int]  # indices into the flip-mask group list
+
+
+@dataclass
+class PartnerStep:
+    group: int  # a flip group that flips a global qubit in every layout (see _partner_terms)
 
 
 def _pair(layout: Layout, bring: Sequence[int], evict: Sequence[int]) -> List[Tuple[int, int]]:
@@ -197,7 +204,8 @@ def schedule_ops(ops: Sequence[PlanOp], layout: Layout) -> Tuple[list, Layout]:
 
 def schedule_terms(flips: Sequence[int], layout: Layout) -> Tuple[list, Layout]:
     """Splits flip-mask groups into TermsStep items, each evaluable with no flip bit on a global
-    qubit, separated by SwapStep items. Returns the steps and the final layout."""
+    qubit, separated by SwapStep items; a group that flips more qubits than a shard holds
+    becomes a PartnerStep. Returns the steps and the final layout."""
     L = layout.copy()
     n = L.n
     remaining = list(range(len(flips)))
@@ -215,9 +223,10 @@ def schedule_terms(flips: Sequence[int], layout: Layout) -> Tuple[list, Layout]:
             break
         first = flips[remaining[0]]
         cand = [q for q in range(n) if not (first >> q) & 1]
-        if len(cand) < L.g:
-            raise ShardError(f"a Pauli term flips {bin(first).count('1')} qubits; with "
-                             f"{L.g} global qubits at most {L.n_local} can be flipped")
+        if len(cand) < L.g:  # no layout keeps its flips local
+            steps.append(PartnerStep(remaining[0]))
+            remaining = remaining[1:]
+            continue
         count = [0] * n
         for i in remaining:
             f = flips[i]
@@ -382,6 +391,10 @@ class RuntimeBackend:
 
     def observable(self, coef, flip, phase, psi, out, n_local: int) -> float:
         return float(self.observable_rows(coef, flip, phase, psi, out, n_local)[0])
+
+    def scale(self, x, factor: complex, out, n_local: int) -> None:
+        """out <- factor * x."""
+        self.rt.scaled_copy_device(x, n_local, [factor], out=out)
 
     def observable_rows(self, coef, flip, phase, psi, out, n_local: int) -> np.ndarray:
         """Per-row <psi|H|psi>; adds H psi to out when given."""
@@ -707,12 +720,77 @@ class ShardedStateVectorSimulator:
         for st in tsteps:
             if isinstance(st, SwapStep):
                 self._swap(st.pairs, [self.psi] + ([self.lam] if keep_lambda else []))
+            elif isinstance(st, PartnerStep):
+                partial += self._partner_terms(terms, members[st.group], flips[st.group],
+                                               keep_lambda)
             else:
                 coef, flip, phase = local_terms(terms, [members[i] for i in st.groups],
                                                 self.layout, self.rank)
                 partial += self.backend.observable(coef, flip, phase, self.psi, self.lam,
                                                    self.n_local)
         return float(self.comm.allreduce_sum(np.array([partial]))[0])
+
+    def _partner_terms(self, terms, ks, flip: int, keep_lambda: bool) -> float:
+        """This rank's part of <psi|H_g|psi> (and H_g psi into lambda) for the terms ks of one
+        flip group whose flips cover a global qubit in every layout.
+
+        With physical masks split into the rank bits (fg, pg), the chunk bits above the low
+        n_c local bits (ftop, ptop) and the low bits (flow, plow), a Pauli string P with
+        y = popcount(f & p) acts on index t = (R, c, j) as
+        (P psi)[t] = i^y (-1)^popcount((t ^ f) & p) psi[t ^ f], and t ^ f = (R ^ fg, c ^ ftop,
+        j ^ flow) lies on the partner rank R' = R ^ fg. So chunk c of (P psi) on this rank is
+        alpha * P_low b, where b is chunk c ^ ftop of the partner's shard, P_low the string with
+        masks (flow, plow) on n_c qubits (the runtime's observable, with its own i^y) and
+        alpha = i^(popcount(fg & pg) + popcount(ftop & ptop)) (-1)^popcount(R' & pg)
+        (-1)^popcount((c ^ ftop) & ptop). Terms are grouped by the power of i: for each power
+        the received chunk is multiplied by it (exact) and the real-coefficient sum is applied
+        once into lambda and once into a zeroed chunk x, whose overlap with this rank's chunk c
+        of psi gives the value. The partner computes the complex conjugate contributions, so
+        each rank adds the real part. Every rank sends its chunk c ^ ftop to its partner while
+        receiving the partner's, chunk by chunk, in the same order on every rank."""
+        L = self.layout
+        n_l = L.n_local
+        be = self.backend
+        fp = L.physical_mask(flip)
+        fg, fl = fp >> n_l, fp & ((1 << n_l) - 1)
+        partner = self.rank ^ fg
+        n_c = min(n_l, max(0, self.chunk.bit_length() - 1))
+        cs = 1 << n_c
+        ftop, flow = fl >> n_c, fl & (cs - 1)
+        # per term: coefficient, rank-bit phase mask, chunk-bit phase mask, low phase mask, i power
+        rows = []
+        for k in ks:
+            c, _, p, _ = terms[k]
+            pp = L.physical_mask(p)
+            pg, pl = pp >> n_l, pp & ((1 << n_l) - 1)
+            ptop, plow = pl >> n_c, pl & (cs - 1)
+            m = (bin(fg & pg).count("1") + bin(ftop & ptop).count("1")) % 4
+            sign = -1.0 if bin(partner & pg).count("1") & 1 else 1.0
+            rows.append((sign * float(c), ptop, plow, m))
+        powers = sorted({r[3] for r in rows})
+        unit = [1.0, 1j, -1.0, -1j]
+        b = be.empty(cs)
+        b2 = be.empty(cs)
+        x = be.empty(cs)
+        value = 0.0
+        for c in range(1 << (n_l - n_c)):
+            src = c ^ ftop
+            h = self.comm.exchange_start({partner: self.psi[src * cs:(src + 1) * cs]},
+                                         {partner: b})
+            self.comm.wait(h)
+            for m in powers:
+                sel = [r for r in rows if r[3] == m]
+                coef = np.array([r[0] * (-1.0 if bin(src & r[1]).count("1") & 1 else 1.0)
+                                 for r in sel], dtype=np.float64)
+                fmask = np.full(len(sel), flow, dtype=np.uint64)
+                pmask = np.array([r[2] for r in sel], dtype=np.uint64)
+                be.scale(b, unit[m], b2, n_c)
+                if keep_lambda:
+                    be.observable(coef, fmask, pmask, b2, self.lam[c * cs:(c + 1) * cs], n_c)
+                x.zero_()
+                be.observable(coef, fmask, pmask, b2, x, n_c)
+                value += be.overlap(self.psi[c * cs:(c + 1) * cs], x, n_c).real
+        return value
 
     def adjoint(self, ops: Sequence[PlanOp], upstream: float, requires_grad) -> np.ndarray:
         """Reverse sweep over ops from (psi, lambda = H psi): lambda <- g lambda, then per op

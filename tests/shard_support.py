@@ -96,6 +96,9 @@ class OracleShardBackend:
     def observable(self, coef, flip, phase, psi, out, n_local):
         return float(self.observable_rows(coef, flip, phase, psi, out, n_local)[0])
 
+    def scale(self, x, factor, out, n_local):
+        out.copy_(x * complex(factor))
+
     def marginal(self, shard, n_local, positions):
         return self.O.marginal_probabilities(shard.numpy(), n_local, list(positions))
 

@@ -8,8 +8,8 @@ import numpy as np
 import pytest
 
 from arcqml_b200.circuit import PlanOp
-from arcqml_b200.sharded import (Layout, ShardError, SwapStep, TermsStep, flip_groups,
-                                 local_terms, schedule_ops, schedule_terms)
+from arcqml_b200.sharded import (Layout, PartnerStep, ShardError, SwapStep, TermsStep,
+                                 flip_groups, local_terms, schedule_ops, schedule_terms)
 from arcqml_b200.workloads import brickwork, random_pauli_sum
 from plans import random_plan, random_state, random_terms
 from shard_support import gloo_worker, slice_index, slices_numpy
@@ -93,11 +93,62 @@ def test_schedule_terms_covers_every_group_without_global_flips(n, g):
     assert sorted(seen) == list(range(len(flips)))
 
 
-def test_schedule_terms_rejects_terms_flipping_too_many_qubits():
-    terms = [(1.0, 0b1111, 0, 0)]
+def test_schedule_terms_sends_groups_that_flip_every_layout_to_the_partner():
+    terms = [(1.0, 0b1111, 0, 0), (0.5, 0b0001, 0, 0), (2.0, 0b0111, 0b1000, 0)]
     flips, _ = flip_groups(terms)
-    with pytest.raises(ShardError, match="flips 4 qubits"):
-        schedule_terms(flips, Layout(4, 1))
+    steps, _ = schedule_terms(flips, Layout(4, 2))
+    partner = sorted(st.group for st in steps if isinstance(st, PartnerStep))
+    assert partner == [0, 2]  # 4 and 3 flipped qubits: fewer than 2 left for the rank bits
+    local = [gi for st in steps if isinstance(st, TermsStep) for gi in st.groups]
+    assert local == [1]
+
+
+def partner_terms(n, rng, count):
+    """Pauli terms (coefficient, flip, phase, Y count mod 4) that flip most qubits: X, Y and Z
+    on every qubit or all but one, so that every power of i occurs on the rank bits."""
+    full = (1 << n) - 1
+    out = []
+    for _ in range(count):
+        flip = full if rng.uniform() < 0.5 else full & ~(1 << int(rng.integers(0, n)))
+        y = int(rng.integers(0, 1 << n)) & flip  # Y where flip and phase meet
+        z = int(rng.integers(0, 1 << n)) & ~flip
+        phase = y | z
+        out.append((float(rng.normal()), flip, phase, bin(flip & phase).count("1") % 4))
+    return out
+
+
+@pytest.mark.parametrize("size,n,chunk", [(2, 6, 4), (4, 6, 2), (8, 7, 4), (4, 8, 1 << 10)])
+def test_thread_world_partner_terms_match_oracle(oracle, size, n, chunk):
+    """Terms flipping more qubits than a shard holds, mixed with ordinary ones, over thread
+    ranks: value, H psi and the adjoint sweep's gradients against the oracle."""
+    from arcqml_b200.sharded import ShardedStateVectorSimulator
+    from shard_support import OracleShardBackend, run_threads, sharded_case
+    rng = np.random.Generator(np.random.PCG64(300 + size + n))
+    npar = 6
+    terms = partner_terms(n, rng, 12) + random_terms(rng, n, 10)
+    terms.append(terms[0][:1] + terms[0][1:])  # a repeated flip mask: one group, two terms
+    case = dict(n=n, ops=random_plan(rng, n, 60, npar), terms=terms, init=random_state(rng, n),
+                upstream=float(rng.normal()),
+                req=[1] + [int(x) for x in (rng.uniform(size=npar) < 0.8)])
+
+    def body(rank, comm):
+        sim = ShardedStateVectorSimulator(n, comm=comm, backend=OracleShardBackend(oracle),
+                                          chunk_amplitudes=chunk, transport="p2p")
+        return sharded_case(sim, case["ops"], case["terms"], case["init"], case["upstream"],
+                            case["req"])
+
+    res = dict(enumerate(run_threads(size, body)))
+    check_world(res, expected(oracle, case), size)
+
+
+def test_gloo_world_partner_terms_match_oracle(oracle):
+    n, size = 6, 4
+    rng = np.random.Generator(np.random.PCG64(77))
+    case = dict(n=n, ops=random_plan(rng, n, 50, 5),
+                terms=partner_terms(n, rng, 8) + random_terms(rng, n, 8),
+                init=random_state(rng, n), upstream=-0.4, req=[0] + [1] * 5, chunk=4)
+    res = run_world(size, case)
+    check_world(res, expected(oracle, case), size)
 
 
 # ---------------------------------------------------------------------------- slice packing
