@@ -138,3 +138,17 @@ def test_emulated_ranks_row_sharded_qnn_match_oracle(runtime, oracle):
     for v, gr in res:
         np.testing.assert_allclose(v, vals, rtol=0, atol=1e-10)
         np.testing.assert_allclose(gr, g[1:], rtol=0, atol=1e-10 * max(1.0, np.abs(g).max()))
+
+
+def test_emulated_ranks_partner_terms_match_oracle(runtime, oracle):
+    """Terms that flip more qubits than a shard holds (evaluated against the partner rank's
+    shard, chunk by chunk) on 4 emulated ranks through the device backend."""
+    from test_sharded_host import partner_terms
+    n, size = 12, 4
+    rng = np.random.Generator(np.random.PCG64(1212))
+    npar = 8
+    case = dict(n=n, ops=random_plan(rng, n, 80, npar),
+                terms=partner_terms(n, rng, 10) + random_terms(rng, n, 20),
+                init=random_state(rng, n), upstream=0.6, req=[1] * (npar + 1), chunk=1 << 7)
+    res = thread_world(size, case)
+    check_world(res, expected(oracle, case), size)
