@@ -158,11 +158,13 @@ class ThreadComm:
     def wait(handle):
         pass
 
-    def _gather(self, value):
+    def _gather(self, value, take=lambda v: v):
+        """Every rank's value, each passed through take() while no rank can change it."""
         with self.hub.lock:
             self.hub.box[("g", self.rank)] = value
         self.hub.barrier.wait()
-        vals = [self.hub.box[("g", r)] for r in range(self.size)]
+        vals = [take(self.hub.box[("g", r)]) for r in range(self.size)]
+        self._sync()  # device copies done before any rank goes on
         self.hub.barrier.wait()
         with self.hub.lock:
             del self.hub.box[("g", self.rank)]
@@ -178,7 +180,7 @@ class ThreadComm:
 
     def allgather(self, shard):
         self._sync()
-        return [t.clone() for t in self._gather(shard)]
+        return self._gather(shard, lambda t: t.clone())
 
     # peer transport: the threads share one device, so buffers are used by address directly
     def barrier(self):
