@@ -40,3 +40,26 @@ def undefined_globals(path):
 @pytest.mark.parametrize("path", FILES, ids=[os.path.relpath(p, ROOT) for p in FILES])
 def test_no_undefined_globals(path):
     assert undefined_globals(path) == []
+
+
+def test_runtime_binding_attributes_exist():
+    """Every attribute read from the ctypes binding (``rt.X``, ``self.rt.X``, ``runtime.X``) in
+    the package, the benchmark and the tests is defined by ``arcqml_b200.runtime``."""
+    import ast
+
+    from arcqml_b200 import runtime
+    files = FILES + sorted(glob.glob(os.path.join(ROOT, "tests", "*.py")))
+    bad = []
+    for path in files:
+        with open(path) as f:
+            tree = ast.parse(f.read())
+        for node in ast.walk(tree):
+            if not isinstance(node, ast.Attribute):
+                continue
+            v = node.value
+            on_rt = isinstance(v, ast.Name) and v.id in ("rt", "runtime")
+            on_rt = on_rt or (isinstance(v, ast.Attribute) and v.attr == "rt" and
+                              isinstance(v.value, ast.Name) and v.value.id == "self")
+            if on_rt and not hasattr(runtime, node.attr):
+                bad.append(f"{os.path.relpath(path, ROOT)}:{node.lineno}: {node.attr}")
+    assert bad == []
