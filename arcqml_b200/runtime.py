@@ -84,6 +84,64 @@ V1_SYMBOLS = (
     "arcqml_rt_v1_adjoint_backward", "arcqml_rt_v1_circuit_plan_destroy", "arcqml_rt_last_error",
 )
 
+_P, _S, _I32, _D = C.c_void_p, C.c_size_t, C.c_int32, C.c_double
+# (result type, argument types) of every entry point the binding calls
+SIGNATURES = {
+    "arcqml_rt_abi_version": (C.c_uint32, []),
+    "arcqml_rt_v1_apply_gate": (_I32, [_P, _S, _S, _P, _P, _S]),
+    "arcqml_rt_v1_apply_adjoint_gate": (_I32, [_P, _S, _S, _P, _P, _S]),
+    "arcqml_rt_v1_parameter_derivative_into": (_I32, [_P, _S, _P, _S, _P, _P, _S, _S]),
+    "arcqml_rt_v1_derivative_matrix_create": (_I32, [_P, _S, _P]),
+    "arcqml_rt_v1_derivative_matrix_apply": (_I32, [_P, _S, _P, _P, _S]),
+    "arcqml_rt_v1_derivative_matrix_destroy": (None, [_P]),
+    "arcqml_rt_v1_circuit_plan_create": (_I32, [_P, _S, _P]),
+    "arcqml_rt_v1_circuit_plan_create_empty": (_I32, [_S, _P]),
+    "arcqml_rt_v1_circuit_plan_push": (_I32, [_P, _P]),
+    "arcqml_rt_v1_circuit_plan_apply": (_I32, [_P, _P, _S, _S]),
+    "arcqml_rt_v1_adjoint_backward": (_I32, [_P, _P, _P, _S, _P, _S, _D, _P, _S, _P, _S]),
+    "arcqml_rt_v1_circuit_plan_destroy": (None, [_P]),
+    "arcqml_rt_last_error": (_S, [_P, _S]),
+    "arcqml_rt_v2_observable_create": (_I32, [_S, _P, _P, _P, _S, _P]),
+    "arcqml_rt_v2_observable_destroy": (None, [_P]),
+    "arcqml_rt_v2_plan_apply": (_I32, [_P, _P, _S, _S, _P]),
+    "arcqml_rt_v2_apply_gate": (_I32, [_P, _S, _S, _P, _P, _S, _I32, _P]),
+    "arcqml_rt_v2_parameter_derivative": (_I32, [_P, _P, _S, _S, _P, _P, _S, _S, _P]),
+    "arcqml_rt_v2_expectation": (_I32, [_P, _P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_expectation_and_apply": (_I32, [_P, _P, _P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_expectation_and_accumulate": (_I32, [_P, _P, _P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_sample": (_I32, [_P, _S, C.c_uint64, C.c_uint64, _P, _P, _P]),
+    "arcqml_rt_v2_shard_slices": (_I32, [_P, _S, _P, _S, C.c_uint64, C.c_uint64, C.c_uint64, _P,
+                                        _I32, _P]),
+    "arcqml_rt_v2_small_run": (_I32, [_P, _P, _P, _S, _P, _S, _P, _S, _P, _P, _P]),
+    "arcqml_rt_v2_plan_emulate": (_I32, [_P, _P, _S, _I32, _P, _P, _S, _P, _S]),
+    "arcqml_rt_v2_plan_schedule_export": (_I32, [_P, _S, _I32, _P, _S, _P, _S, _P]),
+    "arcqml_rt_v2_probabilities": (_I32, [_P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_marginal_probabilities": (_I32, [_P, _S, _S, _P, _S, _P, _P]),
+    "arcqml_rt_v2_bloch_vector": (_I32, [_P, _S, _S, _S, _P, _P]),
+    "arcqml_rt_v2_overlap": (_I32, [_P, _P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_probability_cotangent": (_I32, [_P, _S, _S, _P, _S, _P, _P, _P]),
+    "arcqml_rt_v2_scaled_copy": (_I32, [_P, _S, _S, _P, _P, _P]),
+    "arcqml_rt_v2_small_adam": (_I32, [_P, _P, _P, _S, _P, _P, _S, _P, _P, C.c_uint64, _S, _D,
+                                      _D, _D, _D, _D, _P, _P]),
+    "arcqml_rt_v2_shard_slices_from": (_I32, [_P, _S, _P, _S, C.c_uint64, C.c_uint64, _P, _P]),
+    "arcqml_rt_v2_peer_buffer_create": (_I32, [_S, _P, _P]),
+    "arcqml_rt_v2_peer_buffer_open": (_I32, [_P, _P]),
+    "arcqml_rt_v2_peer_buffer_close": (_I32, [_P]),
+    "arcqml_rt_v2_peer_buffer_destroy": (_I32, [_P]),
+    "arcqml_rt_v2_adjoint_backward": (_I32, [_P, _P, _P, _S, _S, _P, _P, _S, _P, _S, _P]),
+    "arcqml_rt_v2_norms": (_I32, [_P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_norms_noalloc": (_I32, [_P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_set_basis_state": (_I32, [_P, _S, _S, C.c_uint64, _P]),
+    "arcqml_rt_v2_plan_set_parameters": (_I32, [_P, _P, _S]),
+    "arcqml_rt_v2_plan_len": (_S, [_P]),
+    "arcqml_rt_v2_plan_schedule_stats": (_I32, [_P, _S, _I32, _P, _P, _P]),
+    "arcqml_rt_v2_profile_enable": (None, [_I32]),
+    "arcqml_rt_v2_profile_read": (_I32, [C.c_uint32, _P, _P, _P]),
+    "arcqml_rt_v2_launch_count": (C.c_uint64, []),
+    "arcqml_rt_v2_jit_info": (_S, [_P, _P, _P, _P, _S]),
+    "arcqml_rt_v2_plan_jit_check": (_I32, [_P, _S, _I32, _P, _P, _P, _S]),
+}
+
 _lib = None
 
 
@@ -97,63 +155,7 @@ def load():
             f"{LIB_PATH} is missing: build it with `python -m arcqml_b200.build` "
             "(the statevector path has no CPU fallback)")
     L = C.CDLL(LIB_PATH)
-    P, S, I32, D = C.c_void_p, C.c_size_t, C.c_int32, C.c_double
-    sig = {
-        "arcqml_rt_abi_version": (C.c_uint32, []),
-        "arcqml_rt_v1_apply_gate": (I32, [P, S, S, P, P, S]),
-        "arcqml_rt_v1_apply_adjoint_gate": (I32, [P, S, S, P, P, S]),
-        "arcqml_rt_v1_parameter_derivative_into": (I32, [P, S, P, S, P, P, S, S]),
-        "arcqml_rt_v1_derivative_matrix_create": (I32, [P, S, P]),
-        "arcqml_rt_v1_derivative_matrix_apply": (I32, [P, S, P, P, S]),
-        "arcqml_rt_v1_derivative_matrix_destroy": (None, [P]),
-        "arcqml_rt_v1_circuit_plan_create": (I32, [P, S, P]),
-        "arcqml_rt_v1_circuit_plan_create_empty": (I32, [S, P]),
-        "arcqml_rt_v1_circuit_plan_push": (I32, [P, P]),
-        "arcqml_rt_v1_circuit_plan_apply": (I32, [P, P, S, S]),
-        "arcqml_rt_v1_adjoint_backward": (I32, [P, P, P, S, P, S, D, P, S, P, S]),
-        "arcqml_rt_v1_circuit_plan_destroy": (None, [P]),
-        "arcqml_rt_last_error": (S, [P, S]),
-        "arcqml_rt_v2_observable_create": (I32, [S, P, P, P, S, P]),
-        "arcqml_rt_v2_observable_destroy": (None, [P]),
-        "arcqml_rt_v2_plan_apply": (I32, [P, P, S, S, P]),
-        "arcqml_rt_v2_apply_gate": (I32, [P, S, S, P, P, S, I32, P]),
-        "arcqml_rt_v2_parameter_derivative": (I32, [P, P, S, S, P, P, S, S, P]),
-        "arcqml_rt_v2_expectation": (I32, [P, P, S, S, P, P]),
-        "arcqml_rt_v2_expectation_and_apply": (I32, [P, P, P, S, S, P, P]),
-        "arcqml_rt_v2_expectation_and_accumulate": (I32, [P, P, P, S, S, P, P]),
-        "arcqml_rt_v2_sample": (I32, [P, S, C.c_uint64, C.c_uint64, P, P, P]),
-        "arcqml_rt_v2_shard_slices": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, C.c_uint64, P,
-                                            I32, P]),
-        "arcqml_rt_v2_small_run": (I32, [P, P, P, S, P, S, P, S, P, P, P]),
-        "arcqml_rt_v2_plan_emulate": (I32, [P, P, S, I32, P, P, S, P, S]),
-        "arcqml_rt_v2_plan_schedule_export": (I32, [P, S, I32, P, S, P, S, P]),
-        "arcqml_rt_v2_probabilities": (I32, [P, S, S, P, P]),
-        "arcqml_rt_v2_marginal_probabilities": (I32, [P, S, S, P, S, P, P]),
-        "arcqml_rt_v2_bloch_vector": (I32, [P, S, S, S, P, P]),
-        "arcqml_rt_v2_overlap": (I32, [P, P, S, S, P, P]),
-        "arcqml_rt_v2_probability_cotangent": (I32, [P, S, S, P, S, P, P, P]),
-        "arcqml_rt_v2_scaled_copy": (I32, [P, S, S, P, P, P]),
-        "arcqml_rt_v2_small_adam": (I32, [P, P, P, S, P, P, S, P, P, C.c_uint64, S, D, D, D, D,
-                                          D, P, P]),
-        "arcqml_rt_v2_shard_slices_from": (I32, [P, S, P, S, C.c_uint64, C.c_uint64, P, P]),
-        "arcqml_rt_v2_peer_buffer_create": (I32, [S, P, P]),
-        "arcqml_rt_v2_peer_buffer_open": (I32, [P, P]),
-        "arcqml_rt_v2_peer_buffer_close": (I32, [P]),
-        "arcqml_rt_v2_peer_buffer_destroy": (I32, [P]),
-        "arcqml_rt_v2_adjoint_backward": (I32, [P, P, P, S, S, P, P, S, P, S, P]),
-        "arcqml_rt_v2_norms": (I32, [P, S, S, P, P]),
-        "arcqml_rt_v2_norms_noalloc": (I32, [P, S, S, P, P]),
-        "arcqml_rt_v2_set_basis_state": (I32, [P, S, S, C.c_uint64, P]),
-        "arcqml_rt_v2_plan_set_parameters": (I32, [P, P, S]),
-        "arcqml_rt_v2_plan_len": (S, [P]),
-        "arcqml_rt_v2_plan_schedule_stats": (I32, [P, S, I32, P, P, P]),
-        "arcqml_rt_v2_profile_enable": (None, [I32]),
-        "arcqml_rt_v2_profile_read": (I32, [C.c_uint32, P, P, P]),
-        "arcqml_rt_v2_launch_count": (C.c_uint64, []),
-        "arcqml_rt_v2_jit_info": (S, [P, P, P, P, S]),
-        "arcqml_rt_v2_plan_jit_check": (I32, [P, S, I32, P, P, P, S]),
-    }
-    for name, (res, args) in sig.items():
+    for name, (res, args) in SIGNATURES.items():
         f = getattr(L, name)
         f.restype = res
         f.argtypes = args

@@ -213,3 +213,48 @@ def test_plan_parameters_update(runtime):
     plan.set_parameters(np.array([0.0, 0.5]))
     with pytest.raises(runtime.RuntimeError, match="out of range"):
         plan.set_parameters(np.array([0.0]))
+
+
+def header_declarations():
+    """{name: (result, [parameter types])} of every arcqml_rt_* function in include/*.h."""
+    decls = {}
+    for f in sorted(os.listdir(INCLUDE)):
+        if not f.endswith(".h"):
+            continue
+        text = re.sub(r"/\*.*?\*/|//[^\n]*", " ", open(os.path.join(INCLUDE, f)).read(),
+                      flags=re.S)
+        for m in re.finditer(r"([A-Za-z_][\w \*]*?)\b(arcqml_rt_\w+)\s*\(([^)]*)\)\s*;", text):
+            params = [p.strip() for p in m.group(3).split(",") if p.strip() not in ("", "void")]
+            decls[m.group(2)] = (m.group(1).strip(), params)
+    return decls
+
+
+C_KINDS = {"size_t": "u64", "uint64_t": "u64", "int32_t": "i32", "uint32_t": "u32",
+           "double": "f64"}
+
+
+def c_kind(decl: str) -> str:
+    """Argument class of a C declaration: a pointer, or the width and kind of a scalar."""
+    if "*" in decl or "[" in decl:
+        return "ptr"
+    for t, k in C_KINDS.items():
+        if re.search(rf"\b{t}\b", decl):
+            return k
+    raise AssertionError(f"unclassified C type: {decl}")
+
+
+def test_binding_signatures_match_the_headers(runtime):
+    """The ctypes argument and result types of every bound entry point agree with the C
+    declarations in include/*.h (count, pointer or integer width, double)."""
+    import ctypes as C
+    kinds = {C.c_void_p: "ptr", C.c_size_t: "u64", C.c_uint64: "u64", C.c_int32: "i32",
+             C.c_uint32: "u32", C.c_double: "f64", None: "void"}
+    assert C.sizeof(C.c_size_t) == 8
+    decls = header_declarations()
+    assert set(runtime.SIGNATURES) <= set(decls), set(runtime.SIGNATURES) - set(decls)
+    for name, (res, args) in runtime.SIGNATURES.items():
+        cres, cparams = decls[name]
+        want = [c_kind(p) for p in cparams]
+        got = [kinds[a] for a in args]
+        assert got == want, (name, got, want)
+        assert kinds[res] == ("void" if cres == "void" else c_kind(cres)), (name, res, cres)
