@@ -196,3 +196,39 @@ def test_general_bit_position_schedules_emulate_correctly():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, ARCQML_FAST_DIAG="1"), timeout=900)
     assert r.returncode == 0 and "general-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_one_plan_from_many_threads(runtime, oracle):
+    """A plan is read-only after it is built (CircuitPlan is Send + Sync in
+    crates/arcqml-runtime-sys/src/lib.rs:199-200): eight threads emulate its forward and adjoint
+    schedules at the same time, each on its own state, and every result matches the oracle."""
+    import threading
+    n = 11
+    g = np.random.Generator(np.random.PCG64(4242))
+    npar = 8
+    ops = random_plan(g, n, 180, npar)
+    req = [0] + [1] * npar
+    plan = runtime.CircuitPlan.create(ops)
+    inits = [random_state(g, n) for _ in range(8)]
+    terms = random_terms(g, n, 12)
+    out = [None] * 8
+
+    def body(t):
+        psi = runtime.plan_emulate(plan, inits[t], n)
+        _, lam = oracle.expectation_and_apply(terms, psi, n)
+        out[t] = (psi, runtime.plan_emulate(plan, psi, n, adjoint=True, lam=lam,
+                                            requires_grad=req, num_gradients=len(req)))
+
+    threads = [threading.Thread(target=body, args=(t,)) for t in range(8)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    for t in range(8):
+        ref = oracle.plan_apply(ops, inits[t], n)
+        psi, (p0, l0, gr) = out[t]
+        assert float(np.max(np.abs(psi - ref))) < 1e-12
+        _, lam = oracle.expectation_and_apply(terms, ref, n)
+        _, rl0, rg = oracle.adjoint_backward(ops, ref, lam, n, 1.0, req, len(req))
+        assert float(np.max(np.abs(p0 - inits[t]))) < 1e-10
+        assert float(np.max(np.abs(gr - rg))) <= 1e-10 * max(1.0, float(np.max(np.abs(rg))))
