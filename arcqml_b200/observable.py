@@ -25,6 +25,10 @@ class SparsePauliOp:
     num_qubits: int
     terms: List[Tuple[float, Tuple[Tuple[int, str], ...]]] = field(default_factory=list)
 
+    def __post_init__(self):
+        if int(self.num_qubits) <= 0:  # EmptyQubitError (sparse_pauli_op.rs:107-110)
+            raise ObservableError("a Pauli operator acts on at least one qubit")
+
     @classmethod
     def constant(cls, num_qubits: int, value: float) -> "SparsePauliOp":
         return cls(num_qubits, [(float(value), ())])
@@ -37,10 +41,22 @@ class SparsePauliOp:
 
     @classmethod
     def from_json(cls, text: str) -> "SparsePauliOp":
-        d = json.loads(text)
-        op = cls(int(d["num_qubits"]))
-        for t in d["terms"]:
-            op.add_term(float(t["coefficient"]), [(int(p["qubit"]), p["pauli"]) for p in t["paulis"]])
+        """The reference's JSON form (``sparse_pauli_op.rs:180-240``): Pauli names X, Y or Z
+        only (an identity factor is left out, not written as "I")."""
+        try:
+            d = json.loads(text)
+            n = int(d["num_qubits"])
+            terms = [(float(t["coefficient"]), [(int(p["qubit"]), p["pauli"]) for p in t["paulis"]])
+                     for t in d["terms"]]
+        except (ValueError, KeyError, TypeError) as e:
+            raise ObservableError(f"invalid observable JSON: {e}") from None
+        op = cls(n)
+        for i, (c, ps) in enumerate(terms):
+            for j, (_, name) in enumerate(ps):
+                if name not in ("X", "Y", "Z"):
+                    raise ObservableError(f"terms[{i}].paulis[{j}].pauli must be X, Y or Z, "
+                                          f"got {name}")
+            op.add_term(c, ps)
         return op
 
     def to_json(self) -> str:
