@@ -232,3 +232,27 @@ def test_one_plan_from_many_threads(runtime, oracle):
         _, rl0, rg = oracle.adjoint_backward(ops, ref, lam, n, 1.0, req, len(req))
         assert float(np.max(np.abs(p0 - inits[t]))) < 1e-10
         assert float(np.max(np.abs(gr - rg))) <= 1e-10 * max(1.0, float(np.max(np.abs(rg))))
+
+
+def test_custom_unitaries_through_the_circuit_api(runtime, oracle):
+    """Circuit.custom_unitary on 1, 2 and 3 qubits (the last runs between fused passes as a
+    dense step) inside a trained circuit, through the emulated schedules against the oracle;
+    a non-unitary or mis-sized matrix is rejected when appended."""
+    from plans import random_unitary
+    n = 10
+    g = np.random.Generator(np.random.PCG64(515))
+    c = cm.Circuit(n)
+    for layer in range(3):
+        for q in range(n):
+            c.rot(("rx", "ry", "rz")[(q + layer) % 3], float(g.uniform(-3, 3)), q)
+        c.custom_unitary("u1", random_unitary(g, 1), [int(g.integers(0, n))])
+        a, b = (int(x) for x in g.choice(n, size=2, replace=False))
+        c.custom_unitary("u2", random_unitary(g, 2), [a, b])
+        c.custom_unitary("u3", random_unitary(g, 3), [int(x) for x in g.choice(n, 3, False)])
+        c.append("cz", (layer, layer + 1))
+    check(runtime, oracle, c.compile_plan(1), n, random_terms(g, n, 10), random_state(g, n),
+          list(c.requires_grad_mask(True)), 0.8)
+    with pytest.raises(cm.CircuitError, match="not unitary"):
+        c.custom_unitary("bad", np.eye(2) * 1.1, [0])
+    with pytest.raises(cm.CircuitError, match="expected 16 entries"):
+        c.custom_unitary("bad", np.eye(2), [0, 1])
