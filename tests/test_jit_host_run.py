@@ -179,3 +179,27 @@ def test_general_bit_positions_run_their_compiled_code_on_host():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, ARCQML_FAST_DIAG="1"), timeout=1200)
     assert r.returncode == 0 and "general-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_all_switches_together_run_their_compiled_code_on_host():
+    """ARCQML_SUBBLOCK_REORDER=1, ARCQML_FAST_CNOT=1 and ARCQML_FAST_DIAG=1 at once
+    (subprocess): reordered sub-blocks holding CNOT exchanges, controlled gates and generic
+    gradients, run on the CPU against the oracle."""
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import oracle, test_jit_host_run as T\n"
+            "from arcqml_b200 import runtime\n"
+            "for n, seed in ((10, 21), (13, 22)):\n"
+            "    c = T.general_shapes(n, seed)\n"
+            "    for q in range(n):\n"
+            "        c.append('cnot', (q, (q + 3) %% n))\n"
+            "    T.check(runtime, oracle, c, n, seed=seed, terms=15)\n"
+            "    T.check(runtime, oracle, T.cnot_ring(n, seed), n, seed=seed)\n"
+            "T.check(runtime, oracle, T.brickwork_edges(12, 5), 12, seed=5)\n"
+            "print('all-ok')\n") % (root, here, os.path.join(root, "oracle"))
+    env = dict(os.environ, ARCQML_SUBBLOCK_REORDER="1", ARCQML_FAST_CNOT="1",
+               ARCQML_FAST_DIAG="1")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=1200)
+    assert r.returncode == 0 and "all-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
