@@ -7,7 +7,8 @@ built-ins, and driven by a host tile loop that mirrors fused_body: tile T's elem
 index tile_base(T) | scatter(j over the tile qubits S), held in the tile buffer at phys(j); each
 sub-block runs thread by thread (threads never share registers within a sub-block, so running
 them one after another equals running them together), and the accumulator columns are summed
-at the end. The generated code itself, not a restatement of it, is what runs.
+at the end. The generated code itself, not a restatement of it, is what runs. Reads past the
+matrix table meet NaN entries and writes past the accumulator rows hit a checked guard region.
 """
 import ctypes as C
 import os
@@ -20,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(os.path.dirname(HERE), "arcqml_b200", "csrc")
 HEADER_BYTES, SUB_BYTES, OP_BYTES = 48, 24, 64
+GUARD = 256  # NaN matrix-table entries after the end
 
 PRELUDE = r"""
 #include <cmath>
@@ -51,13 +53,16 @@ using std::fma;
 namespace arcqml {
 #include "fused_core.cuh"
 
+// Returns 0, or 1 when the pass code wrote past its accumulator rows (a guard region).
 template <int RB, bool ADJ, class Ops>
-void drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const double2 *mats,
-           double *acc) {
+int drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const double2 *mats,
+          double *acc) {
     const uint32_t k = h->k, D = 1u << k, threads = 1u << (k - RB);
     const uint64_t tiles = uint64_t(1) << (n - k);
     std::vector<double2> tp(D), tl(D);
-    std::vector<double> sacc(size_t(h->nacc) * threads + 1, 0.0);
+    const size_t rows = size_t(h->nacc) * threads, guard = 64;
+    std::vector<double> sacc(rows + guard, 0.0);
+    for (size_t i = rows; i < rows + guard; ++i) sacc[i] = 12345.0;
     blockDim.x = threads;
     for (uint64_t T = 0; T < tiles; ++T) {
         uint64_t g = T;
@@ -91,6 +96,9 @@ void drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const do
         for (uint32_t t = 0; t < threads; ++t) s += sacc[size_t(a) * threads + t];
         acc[a] = s;
     }
+    for (size_t i = rows; i < rows + guard; ++i)
+        if (sacc[i] != 12345.0) return 1;
+    return 0;
 }
 """
 
@@ -144,9 +152,9 @@ def build(steps, adjoint: bool, workdir: str):
         body = p.code.split('extern "C"')[0]
         src.append(f"namespace pass_{i} {{\n{body}\n}}  // namespace pass_{i}\n")
         src.append(
-            f'extern "C" void run_pass_{i}(uint32_t n, double2 *psi, double2 *lam, '
+            f'extern "C" int run_pass_{i}(uint32_t n, double2 *psi, double2 *lam, '
             f"const PassHeader *h, const double2 *mats, double *acc) {{\n"
-            f"    drive<{p.rb}, {'true' if adjoint else 'false'}, pass_{i}::PassOps>"
+            f"    return drive<{p.rb}, {'true' if adjoint else 'false'}, pass_{i}::PassOps>"
             f"(n, psi, lam, h, mats, acc);\n}}\n")
     src.append("}  // namespace arcqml\n")
     cpp = os.path.join(workdir, "passes.cpp")
@@ -173,9 +181,13 @@ def run(runtime, plan, n, state, adjoint=False, lam=None, requires_grad=None):
             hdr = C.create_string_buffer(p.header, len(p.header))
             acc = np.zeros(max(1, p.nacc))
             fn = getattr(lib, f"run_pass_{i}")
-            fn(C.c_uint32(n), C.c_void_p(psi.ctypes.data),
-               C.c_void_p(lm.ctypes.data if lm is not None else 0), hdr,
-               C.c_void_p(p.mats.ctypes.data), C.c_void_p(acc.ctypes.data))
+            fn.restype = C.c_int
+            # the matrix table followed by NaN entries: a read past its end poisons the result
+            mats = np.concatenate([p.mats, np.full(GUARD, np.nan, dtype=np.complex128)])
+            status = fn(C.c_uint32(n), C.c_void_p(psi.ctypes.data),
+                        C.c_void_p(lm.ctypes.data if lm is not None else 0), hdr,
+                        C.c_void_p(mats.ctypes.data), C.c_void_p(acc.ctypes.data))
+            assert status == 0, f"pass {i} wrote past its accumulator rows"
             for a, parent in enumerate(p.parents):
                 grads[parent] += 2.0 * acc[a]
     return psi if not adjoint else (psi, lm, grads)
