@@ -114,3 +114,17 @@ def test_benchmark_schedule_compiles_completely(runtime):
             pytest.skip("NVRTC is not available: " + r["message"])
         assert r["eligible"] >= 20 and r["compiled"] == r["eligible"], r
         assert plan.schedule_stats(32, adjoint)["passes"] == r["eligible"]
+
+
+def test_default_pass_code_is_pinned():
+    """The compiled pass code of the default configuration equals the pinned digests
+    (tests/golden/pass_code_pins.json, last run on a B200): a planner or code-generator change
+    shows up here first and needs the GPU parity tests before the pins are regenerated."""
+    import json
+    import os
+    if any(k.startswith("ARCQML_") for k in os.environ):
+        pytest.skip("an ARCQML_* switch is set")
+    from golden import pass_code_pins
+    with open(pass_code_pins.PINS) as f:
+        pinned = json.load(f)
+    assert pass_code_pins.digests() == pinned
