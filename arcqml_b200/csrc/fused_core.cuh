@@ -324,6 +324,10 @@ __device__ __forceinline__ double p_gx(double2 v0, double2 v1, double2 w0, doubl
 __device__ __forceinline__ double p_gy(double2 v0, double2 v1, double2 w0, double2 w1) {
     return rcm(w1, v0) - rcm(w0, v1);
 }
+// s += conj(w) v (two FMAs per component): sums that a diagonal's entries multiply afterwards
+__device__ __forceinline__ void acc_cw(double2 &s, double2 w, double2 v) {
+    s = make_double2(fma(w.x, v.x, fma(w.y, v.y, s.x)), fma(w.x, v.y, fma(-w.y, v.x, s.y)));
+}
 // Re<lam| D |psi> over one pair for a dense 2x2 D
 __device__ __forceinline__ double p_gm2(const double2 *d, double2 v0, double2 v1, double2 w0,
                                         double2 w1) {

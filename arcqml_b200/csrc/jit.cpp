@@ -413,21 +413,39 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
     if (o.nslots < 1 || o.nslots > 3) return false;
     c << "{";
     if (!apply_to("v")) return false;
+    if (diag) {
+        // s_x = sum of conj(lambda) psi over the elements on diagonal entry x (once for all
+        // slots), then each slot's sum is Re(sum_x d_s[x] s_x)
+        bool need[4] = {false, false, false, false};
+        for (uint32_t e = 0; e < N; ++e)
+            if (b.active(e)) need[b.entry(e)] = true;
+        c << "{ " << b.decl_u();
+        for (uint32_t x = 0; x < 4; ++x)
+            if (need[x]) c << "double2 s" << x << " = make_double2(0.0, 0.0); ";
+        c << b.open();
+        for (uint32_t e = 0; e < N; ++e)
+            if (b.active(e))
+                c << "acc_cw(s" << b.entry(e) << ", " << reg("w", e) << ", " << reg("v", e) << "); ";
+        c << "}";
+        for (uint32_t s = 0; s < o.nslots; ++s) {
+            const uint32_t d = o.moff + ulen + s * dlen;
+            c << "\n        { double z = 0.0; ";
+            for (uint32_t x = 0; x < 4; ++x)
+                if (need[x])
+                    c << "{ const double2 g = " << b.at(d, x) << "; z = fma(g.x, s" << x
+                      << ".x, fma(-g.y, s" << x << ".y, z)); } ";
+            put_acc(s, false);
+            c << "}";
+        }
+        c << " }";
+        if (!apply_to("w")) return false;
+        c << "}";
+        return true;
+    }
     for (uint32_t s = 0; s < o.nslots; ++s) {
         const uint32_t d = o.moff + ulen + s * dlen;
         c << "{ double z = 0.0; ";
-        if (diag) {
-            c << b.decl_u() << b.open();
-            bool need[4] = {false, false, false, false};
-            for (uint32_t e = 0; e < N; ++e)
-                if (b.active(e)) need[b.entry(e)] = true;
-            for (uint32_t x = 0; x < 4; ++x)
-                if (need[x]) c << "const double2 g" << x << " = " << b.at(d, x) << "; ";
-            for (uint32_t e = 0; e < N; ++e)
-                if (b.active(e))
-                    c << "z += rcm(" << reg("w", e) << ", cmul(g" << b.entry(e) << ", "
-                      << reg("v", e) << ")); ";
-        } else if (one) {
+        if (one) {
             c << b.open();
             for (uint32_t e = 0; e < N; ++e) {
                 if ((e & t0) || !b.active(e)) continue;
