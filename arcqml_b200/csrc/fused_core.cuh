@@ -328,11 +328,6 @@ __device__ __forceinline__ double p_gy(double2 v0, double2 v1, double2 w0, doubl
 __device__ __forceinline__ void acc_cw(double2 &s, double2 w, double2 v) {
     s = make_double2(fma(w.x, v.x, fma(w.y, v.y, s.x)), fma(w.x, v.y, fma(-w.y, v.x, s.y)));
 }
-// Re<lam| D |psi> over one pair for a dense 2x2 D
-__device__ __forceinline__ double p_gm2(const double2 *d, double2 v0, double2 v1, double2 w0,
-                                        double2 w1) {
-    return rcm(w0, cfma(d[0], v0, cmul(d[1], v1))) + rcm(w1, cfma(d[2], v0, cmul(d[3], v1)));
-}
 // Re<lam| D |psi> over one group of four for a dense 4x4 D (group index bit 0: rb0, bit 1: rb1)
 __device__ __forceinline__ double q_gm4(const double2 *d, double2 v0, double2 v1, double2 v2,
                                         double2 v3, double2 w0, double2 w1, double2 w2,

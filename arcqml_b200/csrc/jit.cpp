@@ -442,29 +442,47 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
         c << "}";
         return true;
     }
+    if (one) {
+        // s_ij = sum over the target pairs of conj(lambda_i) psi_j (once for all slots), then
+        // each slot's sum is Re(sum_ij dU_s[i][j] s_ij)
+        c << "{ double2 s00 = make_double2(0.0, 0.0), s01 = s00, s10 = s00, s11 = s00; "
+          << b.open();
+        for (uint32_t e = 0; e < N; ++e) {
+            if ((e & t0) || !b.active(e)) continue;
+            const std::string v0 = reg("v", e), v1 = reg("v", e | t0);
+            const std::string w0 = reg("w", e), w1 = reg("w", e | t0);
+            c << "acc_cw(s00, " << w0 << ", " << v0 << "); acc_cw(s01, " << w0 << ", " << v1
+              << "); acc_cw(s10, " << w1 << ", " << v0 << "); acc_cw(s11, " << w1 << ", " << v1
+              << "); ";
+        }
+        c << "}";
+        for (uint32_t s = 0; s < o.nslots; ++s) {
+            const uint32_t d = o.moff + ulen + s * dlen;
+            c << "\n        { const double2 *g = M + " << d << "; double z = 0.0; ";
+            const char *sij[4] = {"s00", "s01", "s10", "s11"};
+            for (int i = 0; i < 4; ++i)
+                c << "z = fma(g[" << i << "].x, " << sij[i] << ".x, fma(-g[" << i << "].y, "
+                  << sij[i] << ".y, z)); ";
+            put_acc(s, false);
+            c << "}";
+        }
+        c << " }";
+        if (!apply_to("w")) return false;
+        c << "}";
+        return true;
+    }
+    // an uncontrolled dense 4x4: Re<lam| dU_s |psi> group by group
     for (uint32_t s = 0; s < o.nslots; ++s) {
         const uint32_t d = o.moff + ulen + s * dlen;
         c << "{ double z = 0.0; ";
-        if (one) {
-            c << b.open();
-            for (uint32_t e = 0; e < N; ++e) {
-                if ((e & t0) || !b.active(e)) continue;
-                const uint32_t f = e | t0;
-                c << "z += p_gm2(M + " << d << ", " << reg("v", e) << ", " << reg("v", f) << ", "
-                  << reg("w", e) << ", " << reg("w", f) << "); ";
-            }
-        } else {
-            c << "{ ";
-            for (uint32_t e = 0; e < N; ++e) {
-                if (e & (t0 | t1)) continue;
-                const uint32_t i[4] = {e, e | t0, e | t1, e | t0 | t1};
-                c << "z += q_gm4(M + " << d;
-                for (const char *a : {"v", "w"})
-                    for (uint32_t j : i) c << ", " << reg(a, j);
-                c << "); ";
-            }
+        for (uint32_t e = 0; e < N; ++e) {
+            if (e & (t0 | t1)) continue;
+            const uint32_t i[4] = {e, e | t0, e | t1, e | t0 | t1};
+            c << "z += q_gm4(M + " << d;
+            for (const char *a : {"v", "w"})
+                for (uint32_t j : i) c << ", " << reg(a, j);
+            c << "); ";
         }
-        c << "} ";
         put_acc(s, false);
         c << "}";
     }
