@@ -85,6 +85,25 @@ class SparsePauliOp:
     def __len__(self) -> int:
         return len(self.terms)
 
+    def scale(self, factor: float) -> "SparsePauliOp":
+        """Every coefficient times factor (``sparse_pauli_op.rs:339-356``)."""
+        if not np.isfinite(factor):
+            raise ObservableError("coefficient must be finite")
+        return SparsePauliOp(self.num_qubits, [(c * float(factor), ps) for c, ps in self.terms])
+
+    def simplify(self, tolerance: float = 1e-12) -> "SparsePauliOp":
+        """Equal Pauli strings merged (coefficients summed in term order), terms with
+        |coefficient| <= tolerance dropped, strings in canonical order
+        (``sparse_pauli_op.rs:358-387``)."""
+        if not (np.isfinite(tolerance) and tolerance >= 0.0):
+            raise ObservableError(f"invalid simplify tolerance {tolerance}")
+        sums = {}
+        for c, ps in self.terms:
+            key = tuple(sorted((q, p) for q, p in ps if p != "I"))
+            sums[key] = sums.get(key, 0.0) + c
+        return SparsePauliOp(self.num_qubits,
+                             [(c, k) for k, c in sorted(sums.items()) if abs(c) > tolerance])
+
     def compiled_terms(self):
         """[(coefficient, flip_mask, phase_mask, y_count_mod_four)] in insertion order."""
         out = []

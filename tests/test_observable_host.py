@@ -50,3 +50,21 @@ def test_compiled_masks_count_y_factors():
                                    (2.0, 0b0111, 0b0111, 3)]
     c, f, p = op.masks()
     assert list(c) == [0.3, -1.0, 2.0] and list(f) == [11, 2, 7] and list(p) == [13, 2, 7]
+
+
+def test_add_scale_and_simplify():
+    # observable_tests.rs:213-249
+    op = SparsePauliOp(2).add_term(1.0, [(0, "Z")]).add_term(2.0, [(0, "Z")])
+    assert len(op) == 2
+    s = op.simplify(1e-12)
+    assert len(s) == 1 and s.terms[0][0] == 3.0
+    assert s.scale(0.5).terms[0][0] == 1.5
+    assert len(SparsePauliOp(2).add_term(1e-13, [(0, "Z")]).simplify(1e-12)) == 0
+    mixed = SparsePauliOp(3).add_term(0.5, [(2, "X"), (0, "Y")]).add_term(0.25, [(0, "Y"), (2, "X")])
+    mixed.add_term(-1.0, [(1, "I"), (0, "Z")]).add_term(1.0, [(0, "Z")])
+    t = mixed.simplify()
+    assert t.compiled_terms() == [(0.75, 0b101, 0b001, 1)]
+    with pytest.raises(ObservableError, match="tolerance"):
+        op.simplify(-1.0)
+    with pytest.raises(ObservableError, match="finite"):
+        op.scale(float("inf"))
