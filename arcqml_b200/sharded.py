@@ -754,7 +754,7 @@ class ShardedStateVectorSimulator:
         fp = L.physical_mask(flip)
         fg, fl = fp >> n_l, fp & ((1 << n_l) - 1)
         partner = self.rank ^ fg
-        n_c = min(n_l, max(0, self.chunk.bit_length() - 1))
+        n_c = min(n_l, max(1, self.chunk.bit_length() - 1))  # chunks of at least one qubit
         cs = 1 << n_c
         ftop, flow = fl >> n_c, fl & (cs - 1)
         # per term: coefficient, rank-bit phase mask, chunk-bit phase mask, low phase mask, i power
