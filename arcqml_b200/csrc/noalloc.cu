@@ -10,7 +10,8 @@
 // The array is a file-scope __device__ variable: every GPU that loads the library holds it
 // (192 KiB) until the process exits. Host code cannot use its name as a device address; the
 // address is fetched once per device with cudaGetSymbolAddress (on the first call made with that
-// device current) and passed to the kernels. All calls share the array, so calls that overlap
+// device current) and passed to the kernels; it is kept for the life of the process, so a
+// cudaDeviceReset between calls (which would invalidate it) is not supported. All calls share the array, so calls that overlap
 // on the GPU (different streams or threads at the same time) race on it.
 #include <cuda_runtime.h>
 

@@ -526,6 +526,24 @@ class AdamState:
         self.v = np.zeros(num_parameters, dtype=np.float64)
         self.step = 0
 
+    def update(self, values, grads, lr: float = 0.05, betas=(0.9, 0.999), eps: float = 1e-8,
+               weight_decay: float = 0.0) -> np.ndarray:
+        """One f64 Adam step on the host (crates/arcqml-optim/src/adam.rs:190-240: coupled L2
+        weight decay, bias-corrected moments); advances the moments in place and returns the
+        new values. The same update the device loop (`small_adam_device`) applies per step."""
+        x = np.asarray(values, dtype=np.float64)
+        g = np.asarray(grads, dtype=np.float64)
+        if x.shape != self.m.shape or g.shape != self.m.shape:
+            raise ValueError("values and grads must match the AdamState size")
+        self.step += 1
+        b1, b2 = float(betas[0]), float(betas[1])
+        a = g + weight_decay * x
+        self.m = b1 * self.m + (1.0 - b1) * a
+        self.v = b2 * self.v + (1.0 - b2) * (a * a)
+        m_hat = self.m / (1.0 - b1 ** self.step)
+        v_hat = self.v / (1.0 - b2 ** self.step)
+        return x - lr * m_hat / (np.sqrt(v_hat) + eps)
+
 
 def small_adam_device(plan: CircuitPlan, observable: "Observable", num_qubits: int, parameters,
                       requires_grad, steps: int, lr: float = 0.05,

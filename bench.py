@@ -406,12 +406,12 @@ def small_arm(args):
             return float(e[-1])
 
         def host_unit():  # the same 100 steps, one run + backward per step, Adam on the host
-            theta, st = theta0.copy(), {}
+            theta, st = theta0.copy(), rt.AdamState(theta0.size)
             for _ in range(100):
                 c.set_parameter_values(theta)
                 res = sim.run(c, obs)
                 g, _ = res.backward(1.0)
-                theta = O.adam_step(theta, np.asarray(g), st, lr=0.05)
+                theta = st.update(theta, g, lr=0.05)
             c.set_parameter_values(theta0)
             return res.value
 

@@ -217,8 +217,12 @@ int32_t arcqml_rt_v2_norms(const arcqml_c128 *amplitudes, size_t batch, size_t n
  * its scratch is a static 192 KiB device array that every GPU loading the library keeps until
  * exit. At most 8192 rows per call (larger batches are rejected with an error). The first call
  * on a device looks up the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture. All calls share the array: calls
- * that overlap on the GPU race. */
+ * current; make that first call before any stream capture. That first call may also load the
+ * library's kernels onto the device (lazy module loading), which can allocate: a caller that
+ * needs every later call to allocate nothing makes one call ahead of time. Every call waits for
+ * its stream (the norms are copied to the host array before it returns). The address is kept
+ * for the life of the process: cudaDeviceReset is not supported between calls. All calls share
+ * the array: calls that overlap on the GPU race. */
 int32_t arcqml_rt_v2_norms_noalloc(const arcqml_c128 *amplitudes, size_t batch,
                                    size_t num_qubits, double *norms, void *stream);
 

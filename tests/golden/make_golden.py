@@ -1,8 +1,9 @@
 """Regenerates the golden fixtures in this folder from the ArcQML reference checkout.
 
-Run in a container that has the reference mounted (default ``/root/reference``):
+Run in a container that has the reference checkout, naming its root as the argument or in
+``ARCQML_REFERENCE_ROOT``:
 
-    python tests/golden/make_golden.py [reference_root]
+    python tests/golden/make_golden.py <reference_root>
 
 It reads, as text, the reference's own fixtures and known-answer values for the statevector
 path and writes them to JSON, with the source file and line of each value:
@@ -102,4 +103,7 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ARCQML_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <reference_root> (or set ARCQML_REFERENCE_ROOT)")
+    main(root)

@@ -8,10 +8,7 @@ import pytest
 from backends import op
 from plans import random_state
 
-# Written when no GPU time was left to run it: a failure is reported (xfail) without stopping
-# a -x run before the files that follow; the mark goes once it has passed on a B200.
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.xfail(reason="not yet run on a GPU", strict=False)]
+pytestmark = pytest.mark.gpu
 
 SLOTS = {11: 1, 12: 1, 13: 1, 14: 1, 15: 3, 22: 1, 23: 1, 24: 1, 25: 1, 30: 1, 31: 1, 32: 1,
          33: 1, 34: 2}

@@ -140,9 +140,6 @@ def test_emulated_ranks_row_sharded_qnn_match_oracle(runtime, oracle):
         np.testing.assert_allclose(gr, g[1:], rtol=0, atol=1e-10 * max(1.0, np.abs(g).max()))
 
 
-# Written when no GPU time was left to run it: a failure is reported (xfail) without stopping
-# a -x run before the tests that follow; the mark goes once it has passed on a B200.
-@pytest.mark.xfail(reason="not yet run on a GPU", strict=False)
 def test_emulated_ranks_partner_terms_match_oracle(runtime, oracle):
     """Terms that flip more qubits than a shard holds (evaluated against the partner rank's
     shard, chunk by chunk) on 4 emulated ranks through the device backend."""

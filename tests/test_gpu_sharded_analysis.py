@@ -5,10 +5,7 @@ import pytest
 
 from test_sharded_analysis_host import analysis_world
 
-# Written when no GPU time was left to run it: a failure is reported (xfail) without stopping
-# a -x run before the files that follow; the mark goes once it has passed on a B200.
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.xfail(reason="not yet run on a GPU", strict=False)]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("size,n", [(4, 9), (8, 10)])

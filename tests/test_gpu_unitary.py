@@ -11,10 +11,7 @@ from arcqml_b200 import circuit as cm
 from arcqml_b200 import unitary as U
 from unitary_support import OracleUnitaryBackend
 
-# Written when no GPU time was left to run it: a failure is reported (xfail) without stopping
-# a -x run before the files that follow; the mark goes once it has passed on a B200.
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.xfail(reason="not yet run on a GPU", strict=False)]
+pytestmark = pytest.mark.gpu
 
 
 def random_circuit(g, n, layers, trained=True):

@@ -69,3 +69,21 @@ def test_rejects_bad_parameter_arrays(runtime):
         c5 = cm.Circuit(5)
         c5.rot("ry", 0.2, 0)
         call(runtime, c5, obs, 5)
+
+
+def test_host_adam_update_matches_oracle(oracle):
+    """AdamState.update (the host loop's optimizer) against the oracle's f64 Adam over 50
+    steps, with and without weight decay."""
+    from arcqml_b200.runtime import AdamState
+    rng = np.random.default_rng(5)
+    for wd in (0.0, 0.01):
+        x = rng.uniform(-np.pi, np.pi, 9)
+        y, st, ost = x.copy(), AdamState(9), {}
+        for _ in range(50):
+            g = rng.normal(size=9)
+            x = st.update(x, g, lr=0.05, weight_decay=wd)
+            y = oracle.adam_step(y, g, ost, lr=0.05, weight_decay=wd)
+            np.testing.assert_allclose(x, y, rtol=1e-14, atol=1e-15)
+        assert st.step == 50
+    with pytest.raises(ValueError):
+        AdamState(3).update(np.zeros(4), np.zeros(4))

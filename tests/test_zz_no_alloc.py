@@ -39,3 +39,32 @@ def test_noalloc_norms_reject_batches_over_the_limit(runtime):
     a = torch.zeros((8193, 2), dtype=torch.complex128, device="cuda")
     with pytest.raises(runtime.RuntimeError, match="8192-row limit"):
         runtime.norms_device_noalloc(a, 1)
+
+
+def test_noalloc_norms_leave_device_memory_unchanged(runtime):
+    """Its one promise: a call allocates no device memory. The first call on the device (symbol
+    lookup, module load) is made beforehand; the measured call then runs on a new host thread,
+    whose per-thread workspace is empty, so any use of that workspace would cudaMalloc and show
+    up in the device's free memory."""
+    import threading
+
+    import torch
+
+    a = torch.from_numpy(_states(3, 64, 14)).cuda()
+    runtime.norms_device_noalloc(a, 14)
+    torch.cuda.synchronize()
+    out = {}
+
+    def worker():
+        torch.cuda.set_device(a.device)
+        free0, _ = torch.cuda.mem_get_info()
+        out["norms"] = runtime.norms_device_noalloc(a, 14, stream=0)
+        torch.cuda.synchronize()
+        free1, _ = torch.cuda.mem_get_info()
+        out["delta"] = free0 - free1
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert out["delta"] == 0
+    np.testing.assert_allclose(out["norms"], runtime.norms_device(a, 14), rtol=1e-12, atol=0)
