@@ -59,7 +59,7 @@ enum FastCode : uint8_t {
     FC_X = 10,       // uncontrolled X on register bit rb0 (register renaming)
     FC_CX_RR = 11,   // X on register bit rb0 where register bit rb1 (the control) is 1
     FC_CX_CR = 12,   // X on register bit rb0 where the per-thread bit dq 0 (the control) is 1
-    // Run-time compiled kernels only (ARCQML_FAST_DIAG=1): each qubit of the op (diagonal
+    // Run-time compiled kernels only (on unless ARCQML_FAST_DIAG=0): each qubit of the op (diagonal
     // slots, controls) is a register bit or a per-thread value, resolved when the code is
     // generated; the table-driven kernel runs these codes through its generic path.
     FC_DIAG = 13,    // diagonal (FK_D1 / FK_D2) with any controls

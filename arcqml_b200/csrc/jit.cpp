@@ -157,7 +157,7 @@ std::string const_bit(const FOp &o, int slot, const SubBlock &S, uint32_t thread
 
 // ---------------------------------------------------------------- ops on general bit positions
 //
-// ARCQML_FAST_DIAG=1 (FC_DIAG, FC_CM2 and the generic gradients): every qubit of the op — a
+// On unless ARCQML_FAST_DIAG=0 (FC_DIAG, FC_CM2 and the generic gradients): every qubit of the op — a
 // diagonal index bit or a control — is a register bit of the sub-block, known per register
 // element when the code is generated, or a per-thread 0/1 value (a thread bit of the tile, or
 // a bit of the tile's global base). Register controls select the elements the code lists;
@@ -343,7 +343,7 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
     return true;
 }
 
-// Gradients on general bit positions (ARCQML_FAST_DIAG=1), in the order of the table-driven
+// Gradients on general bit positions (on unless ARCQML_FAST_DIAG=0), in the order of the table-driven
 // kernel: a Pauli-rotation gradient Im<lam|P|psi> on psi before U^dagger (X / Y over the
 // target pairs whose controls are set, Z with the sign of the target bit), then U^dagger on
 // psi, then each generic slot gradient Re<lam| dU_s |U^dagger psi>, then U^dagger on lambda.

@@ -324,7 +324,7 @@ bool has_fast_path(const FOp &o, bool adjoint) {
            (o.code == FC_D1_REG && o.gcode == GF_Z_REG) || (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
 }
 
-// With ARCQML_FAST_DIAG=1 the run-time compiled kernels also run diagonal gates with controls,
+// Unless ARCQML_FAST_DIAG=0, the run-time compiled kernels also run diagonal gates with controls,
 // two-qubit diagonals and controlled one-target gates (FC_DIAG / FC_CM2), Pauli-rotation
 // gradients with controls or on dense 2x2 forms, and every generic slot gradient of a one- or
 // two-qubit diagonal, a one-target gate or an uncontrolled 4x4 (jit.cpp writes each as its
@@ -377,7 +377,7 @@ size_t pass_op_cap() {
 
 namespace {
 
-// Sub-blocks of a pass's members with commuting gates reordered (ARCQML_SUBBLOCK_REORDER=1).
+// Sub-blocks of a pass's members with commuting gates reordered (on unless ARCQML_SUBBLOCK_REORDER=0).
 // Two gates commute when every qubit they share is acted on diagonally by both (a diagonal
 // gate, or a control): then no shared qubit is a non-diagonal target (`needs`) of either. Each
 // sub-block first takes every ready gate (all non-commuting earlier gates placed) whose
@@ -439,7 +439,7 @@ void pack_subblocks(const std::vector<PGate> &gates, const std::vector<size_t> &
 bool fast_cnot() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FAST_CNOT");
-        return e && e[0] == '1';
+        return !(e && e[0] == '0');
     }();
     return on;
 }
@@ -447,7 +447,7 @@ bool fast_cnot() {
 bool fast_diag() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FAST_DIAG");
-        return e && e[0] == '1';
+        return !(e && e[0] == '0');
     }();
     return on;
 }
@@ -455,7 +455,7 @@ bool fast_diag() {
 bool subblock_reorder() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_SUBBLOCK_REORDER");
-        return e && e[0] == '1';
+        return !(e && e[0] == '0');
     }();
     return on;
 }

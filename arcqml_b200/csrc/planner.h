@@ -35,15 +35,15 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                         bool grads, uint32_t k, uint32_t rb);
 
 // Whether X and single-control CNOT gates on register bits use their register-exchange fast
-// paths (ARCQML_FAST_CNOT=1; off by default) instead of a dense 2x2 / the generic path.
+// paths (on unless ARCQML_FAST_CNOT=0) instead of a dense 2x2 / the generic path.
 bool fast_cnot();
 
 // Whether the run-time compiled kernels run diagonal gates with controls, two-qubit diagonals,
-// controlled one-target gates and generic slot gradients (ARCQML_FAST_DIAG=1; off by default).
+// controlled one-target gates and generic slot gradients (on unless ARCQML_FAST_DIAG=0).
 bool fast_diag();
 
 // Whether passes pack commuting gates into fewer register sub-blocks than circuit order gives
-// (ARCQML_SUBBLOCK_REORDER=1; off by default).
+// (on unless ARCQML_SUBBLOCK_REORDER=0).
 bool subblock_reorder();
 
 // Register bits of forward passes on tiles of k qubits (ARCQML_FORWARD_RB may force 3 or 4).

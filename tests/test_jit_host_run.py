@@ -1,6 +1,7 @@
 """The run-time compiled pass code, built as host code and run on the CPU (jit_host_run.py),
 against the oracle: the generated sources and the fused_core.cuh helpers they call, for the
-default configuration and for ARCQML_SUBBLOCK_REORDER=1 / ARCQML_FAST_CNOT=1 (subprocesses)."""
+default configuration and with ARCQML_SUBBLOCK_REORDER=0 / ARCQML_FAST_CNOT=0 /
+ARCQML_FAST_DIAG=0 (subprocesses)."""
 import math
 import os
 import shutil
@@ -94,7 +95,7 @@ def cnot_ring(n, seed):
 
 
 def general_shapes(n, seed):
-    """Gates that only ARCQML_FAST_DIAG=1 compiles: diagonals with controls (CPHASE, CRZ, CS,
+    """Gates that only the FAST_DIAG paths (on unless ARCQML_FAST_DIAG=0) compile: diagonals with controls (CPHASE, CRZ, CS,
     CT), two-qubit diagonals (RZZ), controlled one-target gates (CRX, CRY, CH, CY, Toffoli,
     3-control X), trained PHASE / U3 / RXX / RYY / RZX / fSim (generic slot gradients), with
     qubits in registers, thread bits and outside the tile, and parameters shared across gates;
@@ -140,28 +141,36 @@ def general_shapes(n, seed):
     return c
 
 
-@pytest.mark.parametrize("env", ["ARCQML_SUBBLOCK_REORDER", "ARCQML_FAST_CNOT"])
-def test_switches_run_their_compiled_code_on_host(env):
+SWITCHES = ("ARCQML_SUBBLOCK_REORDER", "ARCQML_FAST_CNOT", "ARCQML_FAST_DIAG")
+
+
+@pytest.mark.parametrize("env", SWITCHES + ("all",))
+def test_switches_off_run_their_compiled_code_on_host(env):
+    """Each switch turned off alone, and all three off (subprocesses): the brickwork and
+    fast-path circuits, and the CNOT rings while one of FAST_CNOT / FAST_DIAG still gives them
+    compiled code."""
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
+    rings = env != "all"
     code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
             "import oracle, test_jit_host_run as T\n"
             "from arcqml_b200 import runtime\n"
             "T.check(runtime, oracle, T.brickwork_edges(10, 3), 10, seed=3)\n"
             "T.check(runtime, oracle, T.fast_shapes(12, 4), 12, seed=4)\n"
-            "if %r == 'ARCQML_FAST_CNOT':\n"
-            "    for n in (10, 13):\n"
-            "        T.check(runtime, oracle, T.cnot_ring(n, n), n, seed=n)\n"
-            "print('host-run-ok')\n") % (root, here, os.path.join(root, "oracle"), env)
+            "for n in ((10, 13) if %r else ()):\n"
+            "    T.check(runtime, oracle, T.cnot_ring(n, n), n, seed=n)\n"
+            "print('host-run-ok')\n") % (root, here, os.path.join(root, "oracle"), rings)
+    off = SWITCHES if env == "all" else (env,)
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                       env=dict(os.environ, **{env: "1"}), timeout=900)
+                       env=dict(os.environ, **{k: "0" for k in off}), timeout=900)
     assert r.returncode == 0 and "host-run-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
 
 
 def test_general_bit_positions_run_their_compiled_code_on_host():
-    """ARCQML_FAST_DIAG=1 (subprocess): controlled diagonals, two-qubit diagonals, controlled
-    one-target gates and generic slot gradients as compiled pass code, run on the CPU against
-    the oracle; every pass of these circuits has a compiled form, and it compiles for sm_100a."""
+    """Default configuration (subprocess, FAST_DIAG on): controlled diagonals, two-qubit
+    diagonals, controlled one-target gates and generic slot gradients as compiled pass code, run
+    on the CPU against the oracle; every pass of these circuits has a compiled form, and it
+    compiles for sm_100a."""
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
@@ -177,14 +186,15 @@ def test_general_bit_positions_run_their_compiled_code_on_host():
             "    assert r['eligible'] >= 1 and r['compiled'] == r['eligible'], r\n"
             "print('general-ok')\n") % (root, here, os.path.join(root, "oracle"))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                       env=dict(os.environ, ARCQML_FAST_DIAG="1"), timeout=1200)
+                       env={k: v for k, v in os.environ.items() if not k.startswith("ARCQML_")},
+                       timeout=1200)
     assert r.returncode == 0 and "general-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
 
 
 def test_all_switches_together_run_their_compiled_code_on_host():
-    """ARCQML_SUBBLOCK_REORDER=1, ARCQML_FAST_CNOT=1 and ARCQML_FAST_DIAG=1 at once
-    (subprocess): reordered sub-blocks holding CNOT exchanges, controlled gates and generic
-    gradients, run on the CPU against the oracle."""
+    """The default configuration (all three switches on; subprocess with none set): reordered
+    sub-blocks holding CNOT exchanges, controlled gates and generic gradients, run on the CPU
+    against the oracle."""
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
@@ -198,8 +208,7 @@ def test_all_switches_together_run_their_compiled_code_on_host():
             "    T.check(runtime, oracle, T.cnot_ring(n, seed), n, seed=seed)\n"
             "T.check(runtime, oracle, T.brickwork_edges(12, 5), 12, seed=5)\n"
             "print('all-ok')\n") % (root, here, os.path.join(root, "oracle"))
-    env = dict(os.environ, ARCQML_SUBBLOCK_REORDER="1", ARCQML_FAST_CNOT="1",
-               ARCQML_FAST_DIAG="1")
+    env = {k: v for k, v in os.environ.items() if not k.startswith("ARCQML_")}
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
                        timeout=1200)
     assert r.returncode == 0 and "all-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

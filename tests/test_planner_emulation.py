@@ -130,9 +130,10 @@ def check_qnn_like(runtime, oracle):
 
 
 def test_fast_cnot_paths_emulate_correctly_and_compile():
-    """ARCQML_FAST_CNOT=1 (subprocess): X and CNOT as register exchanges; random plans and
-    CNOT-ring circuits match the oracle through the emulator, and the 10-qubit CNOT-ring
-    circuit's passes all have compiled forms that compile."""
+    """ARCQML_FAST_CNOT=0 (subprocess; on by default, so the default configuration covers
+    X and CNOT as register exchanges): random plans and CNOT-ring circuits match the oracle
+    through the emulator, and the 10-qubit CNOT-ring circuit's passes still all have compiled
+    forms (through the controlled one-target code) that compile."""
     import os
     import subprocess
     import sys
@@ -150,7 +151,7 @@ def test_fast_cnot_paths_emulate_correctly_and_compile():
             "    assert r['eligible'] >= 1 and r['compiled'] == r['eligible'], r\n"
             "print('cnot-ok')\n") % (root, here, os.path.join(root, "oracle"))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                       env=dict(os.environ, ARCQML_FAST_CNOT="1"), timeout=600)
+                       env=dict(os.environ, ARCQML_FAST_CNOT="0"), timeout=600)
     assert r.returncode == 0 and "cnot-ok" in r.stdout, r.stdout + r.stderr
 
 
@@ -172,10 +173,10 @@ def test_random_plan_sweep(runtime, oracle, seed):
 
 
 def test_general_bit_position_schedules_emulate_correctly():
-    """ARCQML_FAST_DIAG=1 (subprocess): controlled diagonals, two-qubit diagonals and controlled
-    one-target gates get their compiled-kernel codes, and generic-gradient ops keep their plain
-    forms in scaled passes; random plans over every opcode and the general-shape circuits
-    match the oracle through the emulated schedules."""
+    """ARCQML_FAST_DIAG=0 (subprocess; on by default, where controlled diagonals, two-qubit
+    diagonals and controlled one-target gates get their compiled-kernel codes and
+    generic-gradient ops keep their plain forms in scaled passes): random plans over every
+    opcode and the general-shape circuits match the oracle through the emulated schedules."""
     import os
     import subprocess
     import sys
@@ -194,7 +195,7 @@ def test_general_bit_position_schedules_emulate_correctly():
             "            random_state(g, n), list(c.requires_grad_mask(True)), -1.3)\n"
             "print('general-ok')\n") % (root, here, os.path.join(root, "oracle"))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                       env=dict(os.environ, ARCQML_FAST_DIAG="1"), timeout=900)
+                       env=dict(os.environ, ARCQML_FAST_DIAG="0"), timeout=900)
     assert r.returncode == 0 and "general-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
 
 
