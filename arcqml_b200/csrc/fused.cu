@@ -740,6 +740,8 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
 // run an inline loop with one dispatch per op, the others the out-of-line general routine.
 struct TableRunner {
     static constexpr bool kAccPerWarp = false;
+    static constexpr bool kSingleBuffer = false;
+    static constexpr bool kOpsInSmem = true;
     template <int RB, bool ADJ>
     __device__ static __forceinline__ void run(uint32_t sb, uint32_t k, double2 *tp, double2 *tl,
                                                const FOp *ops, const double2 *mats,
@@ -780,8 +782,8 @@ __global__ void __launch_bounds__((ADJ || RB == 4) ? 256 : 512)
 }
 
 size_t fused_smem(bool adj, uint32_t k, uint32_t nacc, uint32_t nops, uint32_t nmat,
-                  uint32_t acc_cols) {
-    return smem_layout(adj, k, nacc, nops, nmat, acc_cols).total;
+                  uint32_t acc_cols, bool single = false) {
+    return smem_layout(adj, k, nacc, nops, nmat, acc_cols, single).total;
 }
 
 using FusedKernel = void (*)(double2 *, double2 *, uint32_t, uint32_t, uint64_t,
@@ -922,8 +924,10 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         uint32_t blocks = fused_grid_blocks(adj, k, st.header.rb);
         size_t launch_smem = smem;
         if (jit[i]) {
+            // compiled kernels: the op table is inlined (none in shared memory)
             const uint32_t cols = jit_acc_per_warp(adj, st.header.rb) ? threads / 32u : threads;
-            launch_smem = fused_smem(adj, k, st.header.nacc, st.header.nops, st.header.nmat, cols);
+            launch_smem = fused_smem(adj, k, st.header.nacc, 0, st.header.nmat, cols,
+                                     !adj && jit_forward_single());
             blocks = jit_grid_blocks(jit[i], threads, launch_smem);
         }
         if (!jit[i] && adj && st.header.rb == 4)

@@ -364,19 +364,23 @@ __device__ __forceinline__ uint32_t sub_index(uint32_t tb, const uint32_t (&rm)[
 
 // Shared memory: [tile buffers][hioff][accumulators][ops][matrices].
 // Forward: two psi buffers; while a CTA computes tile i from one, cp.async streams tile
-// i + gridDim into the other. Adjoint: one psi and one lambda buffer (the next tile is
-// prefetched into L2 instead) and one accumulator column per thread.
+// i + gridDim into the other. Forward single-buffered (`single`, the compiled kernels that run
+// two CTAs per SM): one psi buffer, the next tile prefetched into L2, the other CTA on the SM
+// computing while this one loads. Adjoint: one psi and one lambda buffer (the next tile is
+// prefetched into L2 instead) and one accumulator column per thread. Kernels that do not read
+// the op table from shared memory pass nops = 0.
 struct SmemLayout {
     uint32_t tile, hioff, sacc, ops, mats, total;
 };
 
 // acc_cols: accumulator columns per row (one per thread, or one per warp).
 __host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t nacc,
-                                                  uint32_t nops, uint32_t nmat, uint32_t acc_cols) {
+                                                  uint32_t nops, uint32_t nmat, uint32_t acc_cols,
+                                                  bool single = false) {
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     SmemLayout m;
     m.tile = 0;
-    uint32_t off = 2u * (16u << k);
+    uint32_t off = ((adj || !single) ? 2u : 1u) * (16u << k);
     m.hioff = off;
     off += 8u << (k - L);
     off = (off + 15u) & ~15u;
@@ -445,6 +449,9 @@ __device__ __forceinline__ SubBlock load_subblock(const SubBlock *subs, uint32_t
 
 // One pass over all tiles; Runner::run<RB, ADJ>(sb, ...) applies sub-block sb of the pass to
 // the tile (it gathers the thread's registers, applies the gates and scatters them back).
+// Runner::kSingleBuffer: a forward pass keeps one tile buffer (load, compute, write back, with
+// the next tile prefetched into L2), as the adjoint does. Runner::kOpsInSmem: the runner reads
+// the op table from shared memory (the table-driven kernel; compiled kernels have it inlined).
 template <int RB, bool ADJ, class Runner>
 __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *__restrict__ lam,
                                            uint32_t n, uint32_t tiles_log, uint64_t total_tiles,
@@ -472,13 +479,16 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     const uint32_t lowmask = (1u << L) - 1;
     // accumulator row stride: one column per thread, or per warp (Runner::kAccPerWarp)
     const uint32_t nthreads = Runner::kAccPerWarp ? blockDim.x / 32u : blockDim.x;
-    const SmemLayout lay = smem_layout(ADJ, k, snacc, snops, snmat, nthreads);
+    constexpr bool kSingle = ADJ || Runner::kSingleBuffer;
+    const uint32_t nops_smem = Runner::kOpsInSmem ? snops : 0u;
+    const SmemLayout lay =
+        smem_layout(ADJ, k, snacc, nops_smem, snmat, nthreads, Runner::kSingleBuffer);
     double2 *bufs = reinterpret_cast<double2 *>(smem + lay.tile);
     uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + lay.hioff);
     double *sacc = reinterpret_cast<double *>(smem + lay.sacc);
     FOp *ops = reinterpret_cast<FOp *>(smem + lay.ops);
     double2 *mats = reinterpret_cast<double2 *>(smem + lay.mats);
-    // forward: buffer b; adjoint: state st (0 = psi, 1 = lambda) of the single buffer
+    // forward: buffer b (always 0 single-buffered); adjoint: state st (0 = psi, 1 = lambda)
     auto tile_buf = [&](int b, int st) { return bufs + size_t(ADJ ? st : b) * D; };
 
     for (uint32_t h = threadIdx.x; h < (1u << (k - L)); h += blockDim.x) {
@@ -490,7 +500,7 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     {
         const uint4 *src = reinterpret_cast<const uint4 *>(gops);
         uint4 *dst = reinterpret_cast<uint4 *>(ops);
-        for (uint32_t i = threadIdx.x; i < snops * 4; i += blockDim.x) dst[i] = src[i];
+        for (uint32_t i = threadIdx.x; i < nops_smem * 4; i += blockDim.x) dst[i] = src[i];
         for (uint32_t i = threadIdx.x; i < snmat; i += blockDim.x) mats[i] = gmats[i];
     }
     if (ADJ)
@@ -539,7 +549,7 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         }
     };
 
-    if constexpr (ADJ) {
+    if constexpr (kSingle) {
         // One buffer: load tile T, ask L2 for tile T + gridDim while T is computed.
         const uint32_t run_bytes = 16u << L;
         const uint32_t lines = run_bytes >= 128u ? run_bytes / 128u : 1u;
@@ -549,12 +559,12 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
             if (Tn < total_tiles) {
                 const uint64_t off = ((Tn >> tiles_log) << n) + tile_base(Tn);
                 const char *P = reinterpret_cast<const char *>(psi + off);
-                const char *Lm = reinterpret_cast<const char *>(lam + off);
+                const char *Lm = ADJ ? reinterpret_cast<const char *>(lam + off) : nullptr;
                 const uint32_t count = lines << (k - L);
                 for (uint32_t i = threadIdx.x; i < count; i += blockDim.x) {
                     const size_t o = size_t(hioff[i / lines]) * 16u + size_t(i % lines) * 128u;
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(P + o));
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(Lm + o));
+                    if (ADJ) asm volatile("prefetch.global.L2 [%0];" ::"l"(Lm + o));
                 }
             }
             cp_async_wait<0>();

@@ -136,6 +136,21 @@ bool adjoint_per_warp() {
     return on;
 }
 
+}  // namespace
+
+// ARCQML_FWD_SINGLE=1: compiled forward kernels keep one tile buffer (the next tile prefetched
+// into L2) and ask for two resident CTAs per SM, so that one CTA's loads and shared-memory
+// exchanges overlap the other's arithmetic.
+bool jit_forward_single() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_FWD_SINGLE");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
+namespace {
+
 // Host copy of the shared-memory swizzle of fused_core.cuh (phys): j ^ fold of its 3-bit groups.
 uint32_t swizzle(uint32_t j) { return j ^ (((j >> 3) ^ (j >> 6) ^ (j >> 9)) & 7u); }
 
@@ -534,9 +549,12 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     std::ostringstream c;
     const uint32_t threads = 1u << (st.header.k - rb);
     const uint32_t cols = acc_per_warp(adj, rb) ? threads / 32u : threads;
+    const bool single = !adj && jit_forward_single();
     c << "struct PassOps {\n"
          "    static constexpr bool kAccPerWarp = " << (acc_per_warp(adj, rb) ? "true" : "false")
       << ";\n"
+         "    static constexpr bool kSingleBuffer = " << (single ? "true" : "false") << ";\n"
+         "    static constexpr bool kOpsInSmem = false;\n"
          "    template <int RB, bool ADJ>\n"
          "    __device__ static __forceinline__ void run(uint32_t sb, uint32_t, double2 *tp,\n"
          "            double2 *tl, const FOp *, const double2 *M, const SubBlock *, double *sacc,\n"
@@ -593,7 +611,8 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "    }\n"
          "};\n";
     const int bound = (adj || rb == 4) ? 256 : 512;
-    const int min_blocks = (adj && adjoint_per_warp() && rb == 3) ? 2 : 1;
+    const int min_blocks =
+        ((adj && adjoint_per_warp() && rb == 3) || (single && threads <= 256)) ? 2 : 1;
     c << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"

@@ -22,6 +22,8 @@ std::string jit_pass_code(const Step &st, bool adjoint);
 std::vector<void *> jit_kernels(const Schedule &sch, bool adjoint);
 // True when the compiled kernel of an (adjoint, rb) pass keeps one accumulator column per warp.
 bool jit_acc_per_warp(bool adjoint, uint32_t rb);
+// Whether compiled forward kernels are single-buffered at two CTAs per SM (ARCQML_FWD_SINGLE=1).
+bool jit_forward_single();
 // Compiles the schedule's passes; true if every pass has a compiled kernel.
 bool jit_schedule_compiles(const Schedule &sch, bool adjoint);
 // ARCQML_ADJ_WIDE=1 (with the run-time compiler on): adjoint sweeps use 12-qubit tiles with 4

@@ -528,6 +528,29 @@ class ShardedStateVectorSimulator:
             phys |= ((idx >> q) & 1) << self.layout.pos[q]
         return full[phys]
 
+    def amplitudes_at(self, indices, which: str = "psi") -> np.ndarray:
+        """Amplitudes at the given logical basis indices, on every rank (collective): each rank
+        reads the ones its shard holds, and one all-reduce assembles them. For checks of
+        states too large to gather whole."""
+        shard = self.psi if which == "psi" else self.lam
+        idx = np.asarray(indices, dtype=np.int64).reshape(-1)
+        if idx.size and (idx.min() < 0 or idx.max() >= (1 << self.num_qubits)):
+            raise ShardError("basis index outside the state")
+        phys = np.zeros_like(idx)
+        for q in range(self.num_qubits):
+            phys |= ((idx >> q) & 1) << self.layout.pos[q]
+        n_local = self.n_local
+        mine = (phys >> n_local) == self.rank
+        out = np.zeros(2 * idx.size, dtype=np.float64)
+        if mine.any():
+            import torch
+            local = torch.from_numpy(phys[mine] & ((1 << n_local) - 1)).to(shard.device)
+            vals = shard.index_select(0, local).cpu().numpy()
+            out[0::2][mine] = vals.real
+            out[1::2][mine] = vals.imag
+        tot = self.comm.allreduce_sum(out)
+        return tot[0::2] + 1j * tot[1::2]
+
     # -- swaps ---------------------------------------------------------------------------
     def timing(self, on: bool):
         """Starts (True) or stops (False) timing the swaps with CUDA events on the current

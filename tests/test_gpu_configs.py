@@ -4,9 +4,18 @@
   every energy and the final parameters at 1e-10;
 * batched QNN: 1024 rows of 10 qubits, 80 parameters, half-MSE upstream, values and the
   row-summed gradient at 1e-10 through BatchStateVectorSimulator;
-* 28 qubits: the fused forward pass against the per-gate kernels on the full-size state (two
-  independent GPU paths), plus norm preservation and <H> against the same state.
+* 28 qubits (config 3 at its stated size): the 20-layer brickwork and the 200-term sum, forward
+  and H|psi>, against the oracle's outputs for the same seeded workload
+  (tests/golden/config_28q_brickwork20.npz, made by tests/golden/make_config_fixtures.py):
+  <H> at 1e-10 relative, sampled amplitudes of psi and H|psi>;
+* 32 qubits (config 4 at its stated size, 64 GiB per state): the full forward + adjoint step;
+  eight gradients against the parameter-shift rule (exact for Pauli rotations), the norm of
+  the final state, and psi back at |0...0> after the reverse sweep un-applied every gate;
+* 30 qubits with the 35-qubit configuration's generator (10 layers, 50 terms) on 8 ranks
+  emulated as threads on one GPU (every kernel and swap of the sharded path) against the
+  oracle's outputs (tests/golden/config_30q_brickwork10.npz).
 """
+import os
 import numpy as np
 import pytest
 
@@ -71,30 +80,129 @@ def test_config2_batched_qnn_matches_oracle(runtime, oracle):
     assert rel_err(grads, g[1:]) <= 1e-10
 
 
-def test_config3_28q_fused_pass_equals_per_gate_kernels(runtime):
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def free_gib():
+    import torch
+    torch.cuda.empty_cache()
+    return torch.cuda.mem_get_info()[0] / 2 ** 30
+
+
+def check_samples(got, want, what):
+    """Sampled amplitudes: largest difference at most 1e-12, and the difference's norm at most
+    1e-10 of the sample's norm."""
+    diff = np.abs(got - want)
+    assert float(diff.max()) <= 1e-12, (what, float(diff.max()))
+    assert float(np.linalg.norm(got - want)) <= 1e-10 * float(np.linalg.norm(want)), what
+
+
+def test_config3_28q_full_workload_matches_oracle(runtime):
     import torch
     from arcqml_b200.workloads import brickwork, random_pauli_sum
-    n = 28
-    c = brickwork(n, 4, seed=1234)
-    ops = c.compile_plan(0)
-    a = torch.zeros(1 << n, dtype=torch.complex128, device="cuda")
-    runtime.set_basis_state_device(a, n, 0)
-    runtime.plan_apply_device(runtime.CircuitPlan.create(ops), a, n)
-    b = torch.zeros_like(a)
-    runtime.set_basis_state_device(b, n, 0)
-    for o in ops:
-        g = runtime.gate_descriptor(o.opcode, len(o.qubits), o.params, o.matrix)
-        runtime.apply_gate_device(b, n, g, o.qubits)
-    diff = float((a - b).abs().max().item())
-    scale = float(b.abs().max().item())
-    assert diff <= 1e-12 * max(scale, 1e-300) + 1e-15, (diff, scale)
-    del b
+    fx = np.load(os.path.join(GOLDEN, "config_28q_brickwork20.npz"))
+    n, layers, terms = int(fx["qubits"]), int(fx["layers"]), int(fx["terms"])
+    assert (n, layers, terms) == (28, 20, 200)
+    c = brickwork(n, layers, seed=1234)
+    obs = runtime.Observable.from_sparse_pauli_op(random_pauli_sum(n, terms, seed=1235))
+    psi = torch.zeros(1 << n, dtype=torch.complex128, device="cuda")
+    runtime.set_basis_state_device(psi, n, 0)
+    runtime.plan_apply_device(runtime.CircuitPlan.create(c.compile_plan(1)), psi, n)
+    hpsi = torch.empty_like(psi)
+    value = float(obs.expectation_and_apply(psi, hpsi, n)[0])
+    ref = float(fx["value"])
+    assert abs(value - ref) <= 1e-10 * max(1.0, abs(ref)), (value, ref)
+    assert abs(float(runtime.norms_device(psi, n)[0]) - float(fx["norm"])) <= 1e-12
+    idx = torch.from_numpy(fx["indices"]).cuda()
+    check_samples(psi.index_select(0, idx).cpu().numpy(), fx["psi"], "psi")
+    check_samples(hpsi.index_select(0, idx).cpu().numpy(), fx["hpsi"], "H psi")
+    del psi, hpsi
     torch.cuda.empty_cache()
-    norm = float(runtime.norms_device(a, n)[0])
-    assert abs(norm - 1.0) <= 1e-10
+
+
+def test_config4_32q_gradients_norm_and_reverse_sweep(runtime):
+    import torch
+    from arcqml_b200.workloads import brickwork, random_pauli_sum
+    n = 32
+    if free_gib() < 130:
+        pytest.skip("the 32-qubit step needs 128 GiB of free device memory")
+    c = brickwork(n, 20, seed=1234)
     obs = runtime.Observable.from_sparse_pauli_op(random_pauli_sum(n, 200, seed=1235))
-    v1 = obs.expectation(a, n)[0]
-    out = torch.empty_like(a)
-    v2 = obs.expectation_and_apply(a, out, n)[0]
-    assert abs(v1 - v2) <= 1e-12
-    assert abs(v1) <= 200 * 4.0
+    ops = c.compile_plan(1)
+    plan = runtime.CircuitPlan.create(ops)
+    values = np.array([0.0] + [p.f64() for p in c.parameters])
+    psi = torch.empty(1 << n, dtype=torch.complex128, device="cuda")
+
+    def energy(v):
+        plan.set_parameters(v)
+        runtime.set_basis_state_device(psi, n, 0)
+        runtime.plan_apply_device(plan, psi, n)
+        return float(obs.expectation(psi, n)[0])
+
+    g = np.random.Generator(np.random.PCG64(32))
+    picks = sorted(int(x) for x in g.choice(len(c.parameters), size=8, replace=False))
+    shift = {}
+    for p in picks:
+        up, dn = values.copy(), values.copy()
+        up[p + 1] += np.pi / 2
+        dn[p + 1] -= np.pi / 2
+        shift[p] = 0.5 * (energy(up) - energy(dn))
+    plan.set_parameters(values)
+    runtime.set_basis_state_device(psi, n, 0)
+    runtime.plan_apply_device(plan, psi, n)
+    assert abs(float(runtime.norms_device(psi, n)[0]) - 1.0) <= 1e-12
+    lam = torch.empty_like(psi)
+    value = float(obs.expectation_and_apply(psi, lam, n)[0])
+    assert abs(value - energy_check(obs, psi, n)) <= 1e-12 * max(1.0, abs(value))
+    req = c.requires_grad_mask(True)
+    grads = runtime.adjoint_backward_device(plan, psi, lam, n, 1.0, req, len(req))
+    del lam
+    scale = max(1.0, float(np.max(np.abs(grads))))
+    for p in picks:
+        assert abs(grads[p + 1] - shift[p]) <= 1e-10 * scale, (p, grads[p + 1], shift[p])
+    # the reverse sweep un-applied every gate: psi is |0...0> again
+    head = psi[:4].cpu().numpy()
+    assert abs(head[0] - 1.0) <= 1e-10 and float(np.max(np.abs(head[1:]))) <= 1e-10
+    assert abs(float(runtime.norms_device(psi, n)[0]) - 1.0) <= 1e-10
+    del psi
+    torch.cuda.empty_cache()
+
+
+def energy_check(obs, psi, n):
+    return float(obs.expectation(psi, n)[0])
+
+
+def test_config5_generator_30q_on_8_emulated_ranks_matches_oracle(runtime):
+    import torch
+    from arcqml_b200.sharded import RuntimeBackend, ShardedStateVectorSimulator
+    from arcqml_b200.workloads import brickwork, random_pauli_sum
+    from shard_support import run_threads
+    fx = np.load(os.path.join(GOLDEN, "config_30q_brickwork10.npz"))
+    n, layers, nterms = int(fx["qubits"]), int(fx["layers"]), int(fx["terms"])
+    assert (n, layers, nterms) == (30, 10, 50)
+    if free_gib() < 40:
+        pytest.skip("needs 40 GiB of free device memory")
+    c = brickwork(n, layers, seed=1234)
+    ops = c.compile_plan(0)
+    terms = random_pauli_sum(n, nterms, seed=1235).compiled_terms()
+
+    def body(rank, comm):
+        sim = ShardedStateVectorSimulator(n, comm=comm, backend=RuntimeBackend(),
+                                          transport="p2p")
+        try:
+            sim.reset()
+            sim.forward(ops)
+            value = sim.observe(terms, True)
+            return (value, sim.amplitudes_at(fx["indices"]),
+                    sim.amplitudes_at(fx["indices"], "lam"), sim.stats.swaps)
+        finally:
+            sim.close()
+
+    res = run_threads(8, body)
+    ref = float(fx["value"])
+    for value, amps, hamps, swaps in res:
+        assert swaps > 0
+        assert abs(value - ref) <= 1e-10 * max(1.0, abs(ref)), (value, ref)
+        check_samples(amps, fx["psi"], "psi")
+        check_samples(hamps, fx["hpsi"], "H psi")
+    torch.cuda.empty_cache()

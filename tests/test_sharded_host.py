@@ -327,3 +327,33 @@ def test_gloo_world_falls_back_when_a_rank_cannot_share_its_buffer(oracle):
         assert not isinstance(out[r], str), out[r]
         assert out[r]["transport"] == "p2p"
     check_world(out, expected(oracle, case), size)
+
+
+@pytest.mark.parametrize("size,n", [(2, 7), (4, 9), (8, 10)])
+def test_thread_world_amplitudes_at_match_oracle(oracle, size, n):
+    """amplitudes_at after a forward sweep whose swaps permuted the layout: the amplitudes at
+    seeded logical indices, on every rank, equal the oracle's state there."""
+    from arcqml_b200.sharded import ShardError, ShardedStateVectorSimulator
+    from shard_support import OracleShardBackend, run_threads
+    rng = np.random.Generator(np.random.PCG64(700 + n))
+    ops = random_plan(rng, n, 80, 5)
+    init = random_state(rng, n)
+    idx = rng.integers(0, 1 << n, size=57)
+    want = oracle.plan_apply(ops, init, n)[idx]
+
+    def body(rank, comm):
+        sim = ShardedStateVectorSimulator(n, comm=comm, backend=OracleShardBackend(oracle),
+                                          transport="p2p")
+        sim.load(init)
+        sim.forward(ops)
+        got = sim.amplitudes_at(idx)
+        try:
+            sim.amplitudes_at([1 << n])
+        except ShardError:
+            pass
+        else:
+            raise AssertionError("an index outside the state was accepted")
+        return got, sim.stats.swaps
+
+    for got, swaps in run_threads(size, body):
+        np.testing.assert_allclose(got, want, rtol=0, atol=1e-12)
