@@ -742,6 +742,7 @@ struct TableRunner {
     static constexpr bool kAccPerWarp = false;
     static constexpr bool kSingleBuffer = false;
     static constexpr bool kOpsInSmem = true;
+    static constexpr bool kMatsInSmem = true;
     template <int RB, bool ADJ>
     __device__ static __forceinline__ void run(uint32_t sb, uint32_t k, double2 *tp, double2 *tl,
                                                const FOp *ops, const double2 *mats,
@@ -926,7 +927,8 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         if (jit[i]) {
             // compiled kernels: the op table is inlined (none in shared memory)
             const uint32_t cols = jit_acc_per_warp(adj, st.header.rb) ? threads / 32u : threads;
-            launch_smem = fused_smem(adj, k, st.header.nacc, 0, st.header.nmat, cols,
+            launch_smem = fused_smem(adj, k, st.header.nacc, 0,
+                                     jit_mats_in_params() ? 0 : st.header.nmat, cols,
                                      !adj && jit_forward_single());
             blocks = jit_grid_blocks(jit[i], threads, launch_smem);
         }
@@ -946,7 +948,12 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
             const FOp *a_ops = ops;
             const double2 *a_mats = mats;
             double *a_part = adj ? partials : nullptr;
-            void *args[] = {&a_psi, &a_lam, &a_n, &a_tl, &a_tt, &a_h, &a_sub, &a_ops, &a_mats,
+            // by value: the pass's matrix table itself is the kernel parameter (copied at launch)
+            static const double2 kNoMats[1] = {};
+            void *mats_arg = jit_mats_in_params()
+                                 ? const_cast<double2 *>(st.mats.empty() ? kNoMats : st.mats.data())
+                                 : static_cast<void *>(&a_mats);
+            void *args[] = {&a_psi, &a_lam, &a_n, &a_tl, &a_tt, &a_h, &a_sub, &a_ops, mats_arg,
                             &a_part, &a_stride};
             jit_launch(jit[i], grid, threads, launch_smem, s, args);
         } else {

@@ -24,6 +24,12 @@ __device__ __forceinline__ double icm(double2 a, double2 b) { return fma(a.x, b.
 
 __device__ __forceinline__ double2 ld(const double2 *p) { return *p; }
 
+// The matrix table a compiled pass indexes as M[...]: a pointer (shared memory, or a host buffer
+// in host runs of the pass code), or the m member of the kernel's by-value parameter struct.
+__device__ __forceinline__ const double2 *mats_of(const double2 *p) { return p; }
+template <class T>
+__device__ __forceinline__ const auto &mats_of(const T &params) { return params.m; }
+
 #ifndef ARCQML_HOST_RUN  // device-only: not in host builds of the pass code (tests)
 // 16-byte asynchronous global -> shared copy (LDGSTS); completion via commit/wait groups.
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -452,13 +458,37 @@ __device__ __forceinline__ SubBlock load_subblock(const SubBlock *subs, uint32_t
 // Runner::kSingleBuffer: a forward pass keeps one tile buffer (load, compute, write back, with
 // the next tile prefetched into L2), as the adjoint does. Runner::kOpsInSmem: the runner reads
 // the op table from shared memory (the table-driven kernel; compiled kernels have it inlined).
-template <int RB, bool ADJ, class Runner>
+// Runner::kMatsInSmem: the matrix table `gmats` (a pointer) is staged in shared memory;
+// otherwise `gmats` is the kernel's by-value parameter struct holding the table (member m), which
+// the runner indexes directly, so that its entries are constant-bank operands of the arithmetic
+// and need no loads or registers of their own.
+// fn(j, phys(j)) for every tile element j the calling thread copies between the state and the
+// tile: with KT > 0 (blockDim.x = 2^(KT - RB)) 2^RB unrolled accesses whose slots differ from
+// phys(threadIdx.x) = ptid by compile-time constants (phys is linear over XOR).
+template <int RB, int KT, class F>
+__device__ __forceinline__ void tile_elements(uint32_t D, uint32_t ptid, const F &fn) {
+    if constexpr (KT > 0) {
+#pragma unroll
+        for (uint32_t i = 0; i < (1u << RB); ++i) {
+            const uint32_t hi = i << (KT - RB);
+            fn(threadIdx.x | hi, ptid ^ phys(hi));
+        }
+    } else {
+        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) fn(j, phys(j));
+    }
+}
+
+// KT > 0: the tile has KT qubits (the compiled kernels know it), so the copies between the
+// state and the tile unroll into 2^RB accesses per thread whose shared-memory slots differ from
+// the thread's own by compile-time constants (phys is linear over XOR); KT = 0 reads k from the
+// pass header.
+template <int RB, bool ADJ, class Runner, int KT = 0, class GM = const double2 *>
 __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *__restrict__ lam,
                                            uint32_t n, uint32_t tiles_log, uint64_t total_tiles,
                                            const PassHeader *__restrict__ hdr,
                                            const SubBlock *__restrict__ subs,
                                            const FOp *__restrict__ gops,
-                                           const double2 *__restrict__ gmats,
+                                           const GM &gmats,
                                            double *__restrict__ partials, uint32_t stride) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ uint8_t sS[16];
@@ -473,7 +503,7 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         snmat = hdr->nmat;
     }
     __syncthreads();
-    const uint32_t k = sk;
+    const uint32_t k = KT > 0 ? uint32_t(KT) : sk;
     const uint32_t D = 1u << k;
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     const uint32_t lowmask = (1u << L) - 1;
@@ -481,13 +511,14 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     const uint32_t nthreads = Runner::kAccPerWarp ? blockDim.x / 32u : blockDim.x;
     constexpr bool kSingle = ADJ || Runner::kSingleBuffer;
     const uint32_t nops_smem = Runner::kOpsInSmem ? snops : 0u;
+    const uint32_t nmat_smem = Runner::kMatsInSmem ? snmat : 0u;
     const SmemLayout lay =
-        smem_layout(ADJ, k, snacc, nops_smem, snmat, nthreads, Runner::kSingleBuffer);
+        smem_layout(ADJ, k, snacc, nops_smem, nmat_smem, nthreads, Runner::kSingleBuffer);
     double2 *bufs = reinterpret_cast<double2 *>(smem + lay.tile);
     uint64_t *hioff = reinterpret_cast<uint64_t *>(smem + lay.hioff);
     double *sacc = reinterpret_cast<double *>(smem + lay.sacc);
     FOp *ops = reinterpret_cast<FOp *>(smem + lay.ops);
-    double2 *mats = reinterpret_cast<double2 *>(smem + lay.mats);
+    const double2 *smats = reinterpret_cast<const double2 *>(smem + lay.mats);
     // forward: buffer b (always 0 single-buffered); adjoint: state st (0 = psi, 1 = lambda)
     auto tile_buf = [&](int b, int st) { return bufs + size_t(ADJ ? st : b) * D; };
 
@@ -501,11 +532,16 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         const uint4 *src = reinterpret_cast<const uint4 *>(gops);
         uint4 *dst = reinterpret_cast<uint4 *>(ops);
         for (uint32_t i = threadIdx.x; i < nops_smem * 4; i += blockDim.x) dst[i] = src[i];
-        for (uint32_t i = threadIdx.x; i < snmat; i += blockDim.x) mats[i] = gmats[i];
+        if constexpr (Runner::kMatsInSmem) {
+            double2 *dst_m = reinterpret_cast<double2 *>(smem + lay.mats);
+            for (uint32_t i = threadIdx.x; i < nmat_smem; i += blockDim.x) dst_m[i] = gmats[i];
+        }
     }
     if (ADJ)
         for (uint32_t a = threadIdx.x; a < snacc * nthreads; a += blockDim.x) sacc[a] = 0.0;
     __syncthreads();
+
+    const uint32_t ptid = phys(threadIdx.x);
 
     const uint64_t tmask = (uint64_t(1) << tiles_log) - 1;
     auto tile_base = [&](uint64_t T) {
@@ -522,11 +558,11 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         const double2 *Lm = ADJ ? lam + off : nullptr;
         double2 *tp = tile_buf(b, 0);
         double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
-        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
+        tile_elements<RB, KT>(D, ptid, [&](uint32_t j, uint32_t pj) {
             const uint64_t g = (j & lowmask) | hioff[j >> L];
-            cp_async16(tp + phys(j), P + g);
-            if (ADJ) cp_async16(tl + phys(j), Lm + g);
-        }
+            cp_async16(tp + pj, P + g);
+            if (ADJ) cp_async16(tl + pj, Lm + g);
+        });
         cp_async_commit();
     };
 
@@ -536,17 +572,22 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
         double2 *tp = tile_buf(b, 0);
         double2 *tl = ADJ ? tile_buf(b, 1) : nullptr;
         for (uint32_t sb = 0; sb < snsub; ++sb) {
-            Runner::template run<RB, ADJ>(sb, k, tp, tl, ops, mats, subs, sacc, nthreads, gbase);
+            if constexpr (Runner::kMatsInSmem)
+                Runner::template run<RB, ADJ>(sb, k, tp, tl, ops, smats, subs, sacc, nthreads,
+                                              gbase);
+            else
+                Runner::template run<RB, ADJ>(sb, k, tp, tl, ops, gmats, subs, sacc, nthreads,
+                                              gbase);
             __syncthreads();
         }
         const uint64_t off = ((T >> tiles_log) << n) + gbase;
         double2 *P = psi + off;
         double2 *Lm = ADJ ? lam + off : nullptr;
-        for (uint32_t j = threadIdx.x; j < D; j += blockDim.x) {
+        tile_elements<RB, KT>(D, ptid, [&](uint32_t j, uint32_t pj) {
             const uint64_t g = (j & lowmask) | hioff[j >> L];
-            P[g] = tp[phys(j)];
-            if (ADJ) Lm[g] = tl[phys(j)];
-        }
+            P[g] = tp[pj];
+            if (ADJ) Lm[g] = tl[pj];
+        });
     };
 
     if constexpr (kSingle) {

@@ -39,6 +39,10 @@
 namespace arcqml {
 namespace {
 
+// Largest matrix table passed by value: kernel parameters may total 32764 bytes (sm_70 and
+// later, CUDA 12.1 and later); the other arguments take under 100.
+constexpr size_t kJitMaxParamMats = 32000;
+
 // ---------------------------------------------------------------- NVRTC and driver entry points
 
 struct Nvrtc {
@@ -145,6 +149,14 @@ bool jit_forward_single() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FWD_SINGLE");
         return e && e[0] == '1';
+    }();
+    return on;
+}
+
+bool jit_mats_in_params() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_JIT_MATS_SMEM");
+        return !(e && e[0] == '1');
     }();
     return on;
 }
@@ -550,15 +562,22 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     const uint32_t threads = 1u << (st.header.k - rb);
     const uint32_t cols = acc_per_warp(adj, rb) ? threads / 32u : threads;
     const bool single = !adj && jit_forward_single();
+    const bool params = jit_mats_in_params();
+    // the pass's matrix table as one by-value kernel parameter (constant-bank operands)
+    const size_t nmats = st.mats.empty() ? 1 : st.mats.size();
+    if (params && nmats * sizeof(double2) > kJitMaxParamMats) return std::string();
+    if (params) c << "struct PassMats { double2 m[" << nmats << "]; };\n";
     c << "struct PassOps {\n"
          "    static constexpr bool kAccPerWarp = " << (acc_per_warp(adj, rb) ? "true" : "false")
       << ";\n"
          "    static constexpr bool kSingleBuffer = " << (single ? "true" : "false") << ";\n"
          "    static constexpr bool kOpsInSmem = false;\n"
-         "    template <int RB, bool ADJ>\n"
+         "    static constexpr bool kMatsInSmem = " << (params ? "false" : "true") << ";\n"
+         "    template <int RB, bool ADJ, class MT>\n"
          "    __device__ static __forceinline__ void run(uint32_t sb, uint32_t, double2 *tp,\n"
-         "            double2 *tl, const FOp *, const double2 *M, const SubBlock *, double *sacc,\n"
+         "            double2 *tl, const FOp *, const MT &MS, const SubBlock *, double *sacc,\n"
          "            uint32_t nthreads, uint64_t gbase) {\n"
+         "        const auto &M = mats_of(MS);\n"
          "        double2 v[1 << RB], w[1 << RB];\n"
          "        constexpr uint32_t kCols = " << cols << "u;  // accumulator row stride\n"
          "        const uint32_t tid = threadIdx.x;\n"
@@ -617,11 +636,13 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"
          "            const SubBlock *__restrict__ subs, const FOp *__restrict__ gops,\n"
-         "            const double2 *__restrict__ gmats, double *__restrict__ partials,\n"
+      << (params ? "            const __grid_constant__ PassMats pm,"
+                 : "            const double2 *__restrict__ gmats,")
+      << " double *__restrict__ partials,\n"
          "            uint32_t stride) {\n"
          "    fused_body<" << rb << ", " << (adj ? "true" : "false")
-      << ", PassOps>(psi, lam, n, tiles_log, total_tiles, hdr, subs, gops, gmats, partials,"
-         " stride);\n}\n";
+      << ", PassOps, " << st.header.k << ">(psi, lam, n, tiles_log, total_tiles, hdr, subs, gops, "
+      << (params ? "pm" : "gmats") << ", partials, stride);\n}\n";
     return c.str();
 }
 

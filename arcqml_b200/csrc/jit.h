@@ -24,6 +24,9 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adjoint);
 bool jit_acc_per_warp(bool adjoint, uint32_t rb);
 // Whether compiled forward kernels are single-buffered at two CTAs per SM (ARCQML_FWD_SINGLE=1).
 bool jit_forward_single();
+// Whether compiled kernels take their pass's matrix table as a by-value kernel parameter (on
+// unless ARCQML_JIT_MATS_SMEM=1, which stages it in shared memory as the table-driven kernel does).
+bool jit_mats_in_params();
 // Compiles the schedule's passes; true if every pass has a compiled kernel.
 bool jit_schedule_compiles(const Schedule &sch, bool adjoint);
 // ARCQML_ADJ_WIDE=1 (with the run-time compiler on): adjoint sweeps use 12-qubit tiles with 4
