@@ -739,7 +739,7 @@ __device__ __noinline__ void general_subblock(const SubBlock &S, uint32_t sb, do
 // Applies sub-block sb by interpreting its op table: sub-blocks whose ops all have fast paths
 // run an inline loop with one dispatch per op, the others the out-of-line general routine.
 struct TableRunner {
-    static constexpr bool kAccPerWarp = false;
+    static constexpr int kAccLanes = 1;
     static constexpr bool kSingleBuffer = false;
     static constexpr bool kOpsInSmem = true;
     static constexpr bool kMatsInSmem = true;
@@ -926,9 +926,9 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         size_t launch_smem = smem;
         if (jit[i]) {
             // compiled kernels: the op table is inlined (none in shared memory)
-            const uint32_t cols = jit_acc_per_warp(adj, st.header.rb) ? threads / 32u : threads;
+            const uint32_t cols = threads / jit_acc_lanes(adj, st.header.rb);
             launch_smem = fused_smem(adj, k, st.header.nacc, 0,
-                                     jit_mats_in_params() ? 0 : st.header.nmat, cols,
+                                     jit_mats_in_params(adj) ? 0 : st.header.nmat, cols,
                                      !adj && jit_forward_single());
             blocks = jit_grid_blocks(jit[i], threads, launch_smem);
         }
@@ -950,7 +950,7 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
             double *a_part = adj ? partials : nullptr;
             // by value: the pass's matrix table itself is the kernel parameter (copied at launch)
             static const double2 kNoMats[1] = {};
-            void *mats_arg = jit_mats_in_params()
+            void *mats_arg = jit_mats_in_params(adj)
                                  ? const_cast<double2 *>(st.mats.empty() ? kNoMats : st.mats.data())
                                  : static_cast<void *>(&a_mats);
             void *args[] = {&a_psi, &a_lam, &a_n, &a_tl, &a_tt, &a_h, &a_sub, &a_ops, mats_arg,

@@ -49,6 +49,20 @@ __device__ __forceinline__ void accumulate_warp(double *sacc, uint32_t row, doub
     for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
     if ((threadIdx.x & 31u) == 0) sacc[row + (threadIdx.x >> 5)] += z;
 }
+
+// Adds the sum of z over each group of four lanes into that group's column of accumulator row
+// `row` (= acc * blockDim.x / 4): a quarter of the per-thread columns' shared memory, for kernels
+// that run two CTAs per SM. Every lane of the warp calls it.
+__device__ __forceinline__ void accumulate_quad(double *sacc, uint32_t row, double z) {
+    z += __shfl_xor_sync(0xffffffffu, z, 1);
+    z += __shfl_xor_sync(0xffffffffu, z, 2);
+    if ((threadIdx.x & 3u) == 0) sacc[row + (threadIdx.x >> 2)] += z;
+}
+#else
+// Host runs execute the threads one after another: the group's column takes each lane's z.
+__device__ __forceinline__ void accumulate_quad(double *sacc, uint32_t row, double z) {
+    sacc[row + (threadIdx.x >> 2)] += z;
+}
 #endif
 
 // Adds z into this thread's own column of accumulator row `row` (= acc * blockDim.x): no
@@ -507,8 +521,8 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     const uint32_t D = 1u << k;
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     const uint32_t lowmask = (1u << L) - 1;
-    // accumulator row stride: one column per thread, or per warp (Runner::kAccPerWarp)
-    const uint32_t nthreads = Runner::kAccPerWarp ? blockDim.x / 32u : blockDim.x;
+    // accumulator row stride: one column per Runner::kAccLanes threads (1, 4 or a warp)
+    const uint32_t nthreads = blockDim.x / uint32_t(Runner::kAccLanes);
     constexpr bool kSingle = ADJ || Runner::kSingleBuffer;
     const uint32_t nops_smem = Runner::kOpsInSmem ? snops : 0u;
     const uint32_t nmat_smem = Runner::kMatsInSmem ? snmat : 0u;

@@ -130,6 +130,27 @@ bool adjoint_per_warp();
 // so that psi, lambda and the accumulators fit one CTA's shared memory.
 bool acc_per_warp(bool adj, uint32_t rb) { return adj && (adjoint_per_warp() || rb == 4); }
 
+bool adjoint_two_ctas();
+// Adjoint kernels on 3 register bits at two CTAs per SM (ARCQML_ADJ_2CTA=1) keep one
+// accumulator column per four lanes, so that two CTAs' tiles and columns fit one SM.
+uint32_t acc_lanes(bool adj, uint32_t rb) {
+    if (acc_per_warp(adj, rb)) return 32u;
+    return (adj && rb == 3 && adjoint_two_ctas()) ? 4u : 1u;
+}
+const char *acc_call(uint32_t rb) {
+    const uint32_t l = acc_lanes(true, rb);
+    return l == 32u ? "accumulate_warp" : l == 4u ? "accumulate_quad" : "accumulate";
+}
+
+// ARCQML_ADJ_2CTA=1: compiled adjoint kernels with 3 register bits ask for two CTAs per SM.
+bool adjoint_two_ctas() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_ADJ_2CTA");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 // ARCQML_JIT_ADJ_WARP=1: adjoint kernels reduce each gradient over the warp (one accumulator
 // column per warp instead of per thread) and ask for two resident CTAs per SM.
 bool adjoint_per_warp() {
@@ -142,18 +163,19 @@ bool adjoint_per_warp() {
 
 }  // namespace
 
-// ARCQML_FWD_SINGLE=1: compiled forward kernels keep one tile buffer (the next tile prefetched
-// into L2) and ask for two resident CTAs per SM, so that one CTA's loads and shared-memory
-// exchanges overlap the other's arithmetic.
+// Compiled forward kernels keep one tile buffer (the next tile prefetched into L2) and ask for
+// two resident CTAs per SM, so that one CTA's loads and shared-memory exchanges overlap the
+// other's arithmetic (ARCQML_FWD_SINGLE=0: two buffers, one CTA per SM).
 bool jit_forward_single() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FWD_SINGLE");
-        return e && e[0] == '1';
+        return !(e && e[0] == '0');
     }();
     return on;
 }
 
-bool jit_mats_in_params() {
+bool jit_mats_in_params(bool adjoint) {
+    if (adjoint) return false;
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_JIT_MATS_SMEM");
         return !(e && e[0] == '1');
@@ -388,7 +410,7 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
     if (four && (o.rb1 >= rb || o.rb1 == o.rb0 || b.creg || !b.cond.empty())) return false;
     const std::string so = std::to_string(o.soff);
     auto put_acc = [&](uint32_t slot, bool pauli) {
-        c << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
+        c << acc_call(rb) << "(sacc, "
           << o.acc[slot] << "u * kCols, ";
         if (pauli) c << (o.sgrad ? "M[" + so + "].y * z); " : "0.5 * z); ");
         else c << (o.sgrad ? "2.0 * M[" + so + "].y * z); " : "z); ");
@@ -549,7 +571,7 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb, S, tbits)) return false;
     // 0.5 * z, times |sigma|^2 in a scaled pass
-    c << "\n        " << (acc_per_warp(true, rb) ? "accumulate_warp" : "accumulate") << "(sacc, "
+    c << "\n        " << acc_call(rb) << "(sacc, "
       << o.acc[0] << "u * kCols, ";
     if (o.sgrad) c << "M[" << o.soff << "].y * z); }";
     else c << "0.5 * z); }";
@@ -560,16 +582,15 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
 std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     std::ostringstream c;
     const uint32_t threads = 1u << (st.header.k - rb);
-    const uint32_t cols = acc_per_warp(adj, rb) ? threads / 32u : threads;
+    const uint32_t cols = threads / acc_lanes(adj, rb);
     const bool single = !adj && jit_forward_single();
-    const bool params = jit_mats_in_params();
+    const bool params = jit_mats_in_params(adj);
     // the pass's matrix table as one by-value kernel parameter (constant-bank operands)
     const size_t nmats = st.mats.empty() ? 1 : st.mats.size();
     if (params && nmats * sizeof(double2) > kJitMaxParamMats) return std::string();
     if (params) c << "struct PassMats { double2 m[" << nmats << "]; };\n";
     c << "struct PassOps {\n"
-         "    static constexpr bool kAccPerWarp = " << (acc_per_warp(adj, rb) ? "true" : "false")
-      << ";\n"
+         "    static constexpr int kAccLanes = " << acc_lanes(adj, rb) << ";\n"
          "    static constexpr bool kSingleBuffer = " << (single ? "true" : "false") << ";\n"
          "    static constexpr bool kOpsInSmem = false;\n"
          "    static constexpr bool kMatsInSmem = " << (params ? "false" : "true") << ";\n"
@@ -630,8 +651,10 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "    }\n"
          "};\n";
     const int bound = (adj || rb == 4) ? 256 : 512;
-    const int min_blocks =
-        ((adj && adjoint_per_warp() && rb == 3) || (single && threads <= 256)) ? 2 : 1;
+    const int min_blocks = ((adj && (adjoint_per_warp() || adjoint_two_ctas()) && rb == 3) ||
+                            (single && threads <= 256))
+                               ? 2
+                               : 1;
     c << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"
@@ -816,7 +839,7 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
     return fns;
 }
 
-bool jit_acc_per_warp(bool adjoint, uint32_t rb) { return acc_per_warp(adjoint, rb); }
+uint32_t jit_acc_lanes(bool adjoint, uint32_t rb) { return acc_lanes(adjoint, rb); }
 
 bool jit_schedule_compiles(const Schedule &sch, bool adjoint) {
     const std::vector<void *> fns = jit_kernels(sch, adjoint);

@@ -21,12 +21,15 @@ std::string jit_pass_code(const Step &st, bool adjoint);
 // kernel runs instead. Kernels are compiled once per circuit structure and device.
 std::vector<void *> jit_kernels(const Schedule &sch, bool adjoint);
 // True when the compiled kernel of an (adjoint, rb) pass keeps one accumulator column per warp.
-bool jit_acc_per_warp(bool adjoint, uint32_t rb);
-// Whether compiled forward kernels are single-buffered at two CTAs per SM (ARCQML_FWD_SINGLE=1).
+// Threads per gradient accumulator column of compiled adjoint kernels (1, 4 or 32).
+uint32_t jit_acc_lanes(bool adjoint, uint32_t rb);
+// Whether compiled forward kernels are single-buffered at two CTAs per SM (on unless
+// ARCQML_FWD_SINGLE=0).
 bool jit_forward_single();
-// Whether compiled kernels take their pass's matrix table as a by-value kernel parameter (on
-// unless ARCQML_JIT_MATS_SMEM=1, which stages it in shared memory as the table-driven kernel does).
-bool jit_mats_in_params();
+// Whether compiled kernels take their pass's matrix table as a by-value kernel parameter:
+// forward kernels unless ARCQML_JIT_MATS_SMEM=1; adjoint kernels stage it in shared memory (with
+// the table in parameters they measured 9 % slower: their straight-line code spills).
+bool jit_mats_in_params(bool adjoint);
 // Compiles the schedule's passes; true if every pass has a compiled kernel.
 bool jit_schedule_compiles(const Schedule &sch, bool adjoint);
 // ARCQML_ADJ_WIDE=1 (with the run-time compiler on): adjoint sweeps use 12-qubit tiles with 4

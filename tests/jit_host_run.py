@@ -91,9 +91,11 @@ int drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const dou
             if (ADJ) lam[gidx(j)] = tl[phys(j)];
         }
     }
+    // accumulator rows hold one column per Ops::kAccLanes threads
+    const uint32_t cols = threads / uint32_t(Ops::kAccLanes);
     for (uint32_t a = 0; a < h->nacc; ++a) {
         double s = 0.0;
-        for (uint32_t t = 0; t < threads; ++t) s += sacc[size_t(a) * threads + t];
+        for (uint32_t t = 0; t < cols; ++t) s += sacc[size_t(a) * cols + t];
         acc[a] = s;
     }
     for (size_t i = rows; i < rows + guard; ++i)

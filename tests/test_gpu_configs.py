@@ -185,6 +185,8 @@ def test_config5_generator_30q_on_8_emulated_ranks_matches_oracle(runtime):
     c = brickwork(n, layers, seed=1234)
     ops = c.compile_plan(0)
     terms = random_pauli_sum(n, nterms, seed=1235).compiled_terms()
+    # read the arrays here: an NpzFile reads its members lazily and is not safe across threads
+    idx, want_psi, want_hpsi = fx["indices"], fx["psi"], fx["hpsi"]
 
     def body(rank, comm):
         sim = ShardedStateVectorSimulator(n, comm=comm, backend=RuntimeBackend(),
@@ -193,8 +195,8 @@ def test_config5_generator_30q_on_8_emulated_ranks_matches_oracle(runtime):
             sim.reset()
             sim.forward(ops)
             value = sim.observe(terms, True)
-            return (value, sim.amplitudes_at(fx["indices"]),
-                    sim.amplitudes_at(fx["indices"], "lam"), sim.stats.swaps)
+            return (value, sim.amplitudes_at(idx), sim.amplitudes_at(idx, "lam"),
+                    sim.stats.swaps)
         finally:
             sim.close()
 
@@ -203,6 +205,6 @@ def test_config5_generator_30q_on_8_emulated_ranks_matches_oracle(runtime):
     for value, amps, hamps, swaps in res:
         assert swaps > 0
         assert abs(value - ref) <= 1e-10 * max(1.0, abs(ref)), (value, ref)
-        check_samples(amps, fx["psi"], "psi")
-        check_samples(hamps, fx["hpsi"], "H psi")
+        check_samples(amps, want_psi, "psi")
+        check_samples(hamps, want_hpsi, "H psi")
     torch.cuda.empty_cache()
