@@ -447,6 +447,18 @@ int32_t arcqml_rt_v2_expectation(const ArcqmlObservableHandle *observable,
     });
 }
 
+int32_t arcqml_rt_v2_observable_tile_passes(const ArcqmlObservableHandle *observable,
+                                            size_t num_qubits, uint32_t *passes) {
+    return guarded([&] {
+        if (!passes) fail("output pointer is null");
+        if (num_qubits >= kMaxQubits) fail("state dimension overflow");
+        const Observable &o = *obs_of(observable);
+        *passes = (o.num_qubits == num_qubits && pauli_tiles_enabled())
+                      ? observable_tile_passes(o, uint32_t(num_qubits))
+                      : 0u;
+    });
+}
+
 int32_t arcqml_rt_v2_expectation_and_apply(const ArcqmlObservableHandle *observable,
                                            const arcqml_c128 *amplitudes, arcqml_c128 *output,
                                            size_t batch, size_t num_qubits, double *values,

@@ -467,6 +467,14 @@ std::vector<double2> pack_pauli(const Observable &obs, uint32_t n, PauliTables &
     return pack;
 }
 
+bool pauli_tiles_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_PAULI_TILE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t batch,
                        uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
                        bool accumulate) {
@@ -474,6 +482,14 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
         std::ostringstream m;
         m << "observable acts on " << obs.num_qubits << " qubits, state has " << n;
         fail(m.str());
+    }
+    if (pauli_tiles_enabled() &&
+        observable_tiled(obs, psi, out, n, values_host, accumulate, ctx, s)) {
+        const size_t dim = size_t(1) << n;
+        for (size_t b = 1; b < batch; ++b)
+            observable_tiled(obs, psi + b * dim, out ? out + b * dim : nullptr, n,
+                             values_host + b, accumulate, ctx, s);
+        return;
     }
     PauliTables tab;
     PauliTraversal tr;

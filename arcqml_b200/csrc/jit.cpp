@@ -131,7 +131,7 @@ bool adjoint_per_warp();
 bool acc_per_warp(bool adj, uint32_t rb) { return adj && (adjoint_per_warp() || rb == 4); }
 
 bool adjoint_two_ctas();
-// Adjoint kernels on 3 register bits at two CTAs per SM (ARCQML_ADJ_2CTA=1) keep one
+// Adjoint kernels on 3 register bits at two CTAs per SM (unless ARCQML_ADJ_2CTA=0) keep one
 // accumulator column per four lanes, so that two CTAs' tiles and columns fit one SM.
 uint32_t acc_lanes(bool adj, uint32_t rb) {
     if (acc_per_warp(adj, rb)) return 32u;
@@ -142,11 +142,12 @@ const char *acc_call(uint32_t rb) {
     return l == 32u ? "accumulate_warp" : l == 4u ? "accumulate_quad" : "accumulate";
 }
 
-// ARCQML_ADJ_2CTA=1: compiled adjoint kernels with 3 register bits ask for two CTAs per SM.
+// Compiled adjoint kernels with 3 register bits ask for two CTAs per SM (ARCQML_ADJ_2CTA=0:
+// one CTA with a column per thread; two measured 4 % faster at 30 qubits).
 bool adjoint_two_ctas() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_ADJ_2CTA");
-        return e && e[0] == '1';
+        return !(e && e[0] == '0');
     }();
     return on;
 }

@@ -169,6 +169,16 @@ void observable_device(Observable &obs, const double2 *psi, double2 *out, size_t
                        uint32_t n, double *values_host, ThreadContext &ctx, cudaStream_t s,
                        bool accumulate = false);
 
+// Large states (pauli_tile.cu, n >= 20): <psi|H|psi> into *value_host and, when out != null,
+// H psi into out (added to it with `accumulate`), as passes over 12-qubit tiles that cover the
+// observable's flip masks. Returns false, having launched nothing, when the state is smaller or
+// a flip mask fits no tile. observable_tile_passes: the pass count (0: not applicable).
+bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, uint32_t n,
+                      double *value_host, bool accumulate, ThreadContext &ctx, cudaStream_t s);
+uint32_t observable_tile_passes(const Observable &obs, uint32_t n);
+// Whether large states use observable_tiled (ARCQML_PAULI_TILE=0 keeps k_pauli).
+bool pauli_tiles_enabled();
+
 // One-kernel run + backward of a small single state (small.cu): value <- <H> after the plan
 // applied to init (null: |0...0>), grads[parent] += 2 Re<lambda| dU/dp |psi> with lambda = H psi,
 // lam0 (may be null) <- lambda_0.

@@ -107,6 +107,7 @@ SIGNATURES = {
     "arcqml_rt_v2_apply_gate": (_I32, [_P, _S, _S, _P, _P, _S, _I32, _P]),
     "arcqml_rt_v2_parameter_derivative": (_I32, [_P, _P, _S, _S, _P, _P, _S, _S, _P]),
     "arcqml_rt_v2_expectation": (_I32, [_P, _P, _S, _S, _P, _P]),
+    "arcqml_rt_v2_observable_tile_passes": (_I32, [_P, _S, _P]),
     "arcqml_rt_v2_expectation_and_apply": (_I32, [_P, _P, _P, _S, _S, _P, _P]),
     "arcqml_rt_v2_expectation_and_accumulate": (_I32, [_P, _P, _P, _S, _S, _P, _P]),
     "arcqml_rt_v2_sample": (_I32, [_P, _S, C.c_uint64, C.c_uint64, _P, _P, _P]),
@@ -449,6 +450,14 @@ class Observable:
             C.byref(self.raw), _dev_ptr(state), _dev_ptr(out_state), b, num_qubits,
             vals.ctypes.data, _stream_ptr(stream)))
         return vals
+
+    def tile_passes(self, num_qubits: int) -> int:
+        """Passes over 12-qubit tiles this observable takes on a num_qubits state (0: the gather
+        kernel evaluates it)."""
+        v = C.c_uint32()
+        _status(load().arcqml_rt_v2_observable_tile_passes(C.byref(self.raw), num_qubits,
+                                                           C.byref(v)))
+        return int(v.value)
 
     def expectation_and_accumulate(self, state, out_state, num_qubits: int,
                                    stream=None) -> np.ndarray:

@@ -615,6 +615,15 @@ class ShardedStateVectorSimulator:
             buf.destroy()
         return None
 
+    def _pack_stream(self):
+        """A second CUDA stream for the peer transport's packs (None off the GPU backend)."""
+        if not isinstance(self.backend, RuntimeBackend):
+            return None
+        if getattr(self, "_packs", None) is None:
+            import torch
+            self._packs = torch.cuda.Stream()
+        return self._packs
+
     def _peer_swap(self, t, n_l, lpos, x, peers, others) -> int:
         """Moves one tensor's slices through the peers' buffers; returns the chunk length."""
         buf, addrs = self._peer
@@ -627,14 +636,30 @@ class ShardedStateVectorSimulator:
         def region(rank, c):  # buffer half of chunk c in `rank`'s buffer
             return addrs[rank] + (c & 1) * half
 
+        # On a GPU the packs run on their own stream, so that packing chunk c + 1 (local HBM)
+        # overlaps gathering chunk c (NVLink): they touch disjoint slots of the shard and
+        # different buffer halves, and every barrier synchronises the whole device.
+        ps = self._pack_stream()
+        if ps is not None:
+            import torch
+            ps.wait_stream(torch.cuda.current_stream())
+
+        def pack(c):
+            if ps is None:
+                be.pack_to(t, n_l, lpos, starts[c], chunk, x, region(self.rank, c))
+            else:
+                import torch
+                with torch.cuda.stream(ps):
+                    be.pack_to(t, n_l, lpos, starts[c], chunk, x, region(self.rank, c))
+
         # Pack chunk c into half c % 2 of this rank's buffer (block order: slice values but
         # this rank's own); after a barrier every rank gathers chunk c from the peers' halves
         # while packing chunk c + 1 into its other half; one barrier per chunk.
-        be.pack_to(t, n_l, lpos, starts[0], chunk, x, region(self.rank, 0))
+        pack(0)
         self.comm.barrier()
         for c, c0 in enumerate(starts):
             if c + 1 < len(starts):
-                be.pack_to(t, n_l, lpos, starts[c + 1], chunk, x, region(self.rank, c + 1))
+                pack(c + 1)
             sources = [None] * (1 << len(lpos))
             for y, r in peers.items():
                 blk = x - (1 if x > y else 0)  # rank r skipped its own value y when packing

@@ -55,6 +55,13 @@ int32_t arcqml_rt_v2_parameter_derivative(const arcqml_c128 *input, arcqml_c128 
                                           size_t qubits_len, size_t parameter_slot,
                                           void *stream);
 
+/* *passes <- how many passes over 12-qubit tiles the observable takes on a state of num_qubits
+ * qubits (states of 20 qubits and more, when every flip mask fits a tile); 0 when the gather
+ * kernel evaluates it instead. Host only. No counterpart in the reference (its CompiledHamiltonian
+ * is one CPU loop, crates/arcqml-observable/src/compiled_hamiltonian.rs:81-132). */
+int32_t arcqml_rt_v2_observable_tile_passes(const ArcqmlObservableHandle *observable,
+                                            size_t num_qubits, uint32_t *passes);
+
 /* values[b] <- Re<psi_b|H|psi_b> (host array of batch doubles). */
 int32_t arcqml_rt_v2_expectation(const ArcqmlObservableHandle *observable,
                                  const arcqml_c128 *amplitudes, size_t batch, size_t num_qubits,

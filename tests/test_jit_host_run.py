@@ -214,9 +214,9 @@ def test_all_switches_together_run_their_compiled_code_on_host():
     assert r.returncode == 0 and "all-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
 
 
-def test_two_cta_adjoint_code_runs_on_host():
-    """ARCQML_ADJ_2CTA=1 (subprocess): adjoint kernels with one gradient column per four lanes
-    (accumulate_quad) run on the CPU against the oracle."""
+def test_one_cta_adjoint_code_runs_on_host():
+    """ARCQML_ADJ_2CTA=0 (subprocess): adjoint kernels with one gradient column per thread (the
+    default has one per four lanes, accumulate_quad) run on the CPU against the oracle."""
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
@@ -225,7 +225,7 @@ def test_two_cta_adjoint_code_runs_on_host():
             "T.check(runtime, oracle, T.brickwork_edges(10, 3), 10, seed=3)\n"
             "T.check(runtime, oracle, T.cnot_ring(13, 13), 13, seed=13)\n"
             "T.check(runtime, oracle, T.general_shapes(12, 2), 12, seed=2, terms=20)\n"
-            "print('quad-ok')\n") % (root, here, os.path.join(root, "oracle"))
+            "print('column-ok')\n") % (root, here, os.path.join(root, "oracle"))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                       env=dict(os.environ, ARCQML_ADJ_2CTA="1"), timeout=900)
-    assert r.returncode == 0 and "quad-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+                       env=dict(os.environ, ARCQML_ADJ_2CTA="0"), timeout=900)
+    assert r.returncode == 0 and "column-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
