@@ -18,8 +18,9 @@ whole-job rate over the max-over-ranks device time. Global-qubit swaps go over N
 count, bytes and time are reported under ``swaps``.
 
 ``--impl reference`` times the CPU oracle (the f64 restatement of the reference's algorithm;
-the reference's own runtime is a closed Windows library) on the host cores with a bounded
-sample of the same workload (fewer qubits and layers), scaled to 32 qubits by state size.
+the reference's own runtime is a closed Windows library) on the host cores: each step a bounded
+sample of the same workload at 28 qubits (per-gate forward and adjoint costs of each gate kind,
+the observable's per-term cost), the 32-qubit step extrapolated from it by state size.
 """
 from __future__ import annotations
 
@@ -88,31 +89,81 @@ def config(args, c):
 # ------------------------------------------------------------------ CPU oracle sample
 
 
-def cpu_sample(args, max_qubits=22, layers=4):
-    """Times the oracle (all host threads) on a bounded sample; returns gate passes/s scaled to
-    args.qubits by state size, plus a description."""
+def cpu_sample(args, sample_qubits=28, rot=(4, 2), cz=(2, 1), term_counts=(2, 16)):
+    """Times the oracle (all host threads) on a bounded sample of the workload at
+    min(28, --qubits) qubits and returns the gate passes/s of the whole step, extrapolated to
+    --qubits by state size, with a description.
+
+    Measured at the sample size, in place on one state, for each gate kind of the workload
+    (parametrised rotations, CZ): the forward cost per gate (rot[0] / cz[0] gates) and the
+    adjoint sweep's cost per gate (a sweep over rot[1] / cz[1] gates minus an empty sweep, which
+    is the sweep's fixed part); and the observable's cost per term and its fixed part (two calls
+    with term_counts terms). The step at the sample size is the --qubits workload's gate counts
+    times these costs plus the fixed parts plus its terms times the per-term cost; every part
+    scales with the state, so the --qubits step takes 2^(qubits - sample) times as long."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes
     import oracle as O
 
     O.build()
-    n = min(max_qubits, args.qubits)
-    layers = min(layers, args.layers)
-    c, obs = workload(n, layers, args.terms, args.seed)
+    L = O.lib()
+    n = min(sample_qubits, args.qubits)
+    c, obs = workload(n, args.layers, args.terms, args.seed)
     ops = c.compile_plan(1)
+    kinds = {"rot": [o for o in ops if o.bindings], "cz": [o for o in ops if not o.bindings]}
+    full = workload(args.qubits, args.layers, args.terms, args.seed)[0].compile_plan(1)
+    counts = {"rot": sum(1 for o in full if o.bindings), "cz": sum(1 for o in full if not o.bindings)}
+    take = {"rot": rot, "cz": cz}
+    psi = np.zeros(1 << n, np.complex128)
+    psi[0] = 1.0  # the oracle's loops cost the same for any amplitude values
+    lam = psi.copy()
+    req = np.ascontiguousarray(c.requires_grad_mask(True), dtype=np.uint8)
+    grads = np.zeros(len(req))
+
+    def forward(packed):
+        t = time.perf_counter()
+        L.oracle_plan_apply(packed.ptr, packed.n, psi.ctypes.data, n)
+        return time.perf_counter() - t
+
+    def sweep(packed):
+        t = time.perf_counter()
+        L.oracle_adjoint_backward(packed.ptr, packed.n, psi.ctypes.data, lam.ctypes.data, n, 1.0,
+                                  req.ctypes.data, len(req), grads.ctypes.data, len(grads))
+        return time.perf_counter() - t
+
+    t_start = time.perf_counter()
+    adj_fixed = sweep(O._Packed([]))
+    fwd, adj = {}, {}
+    for k in ("rot", "cz"):
+        pf = O._Packed(kinds[k][:take[k][0]])
+        fwd[k] = forward(pf) / pf.n
+        pa = O._Packed(kinds[k][:take[k][1]])
+        adj[k] = max(0.0, sweep(pa) - adj_fixed) / pa.n
     terms = obs.compiled_terms()
-    init = np.zeros(1 << n, np.complex128)
-    init[0] = 1
-    req = c.requires_grad_mask(True)
-    t0 = time.perf_counter()
-    psi = O.plan_apply(ops, init, n)
-    _, lam = O.expectation_and_apply(terms, psi, n)
-    O.adjoint_backward(ops, psi, lam, n, 1.0, req, len(req))
-    dt = time.perf_counter() - t0
-    passes = 2 * len(ops)
-    rate = passes / dt * (2.0 ** (n - args.qubits))
-    sample = (f"oracle on {n} qubits, {layers} layers ({len(ops)} gates) + {args.terms}-term <H>, "
-              f"forward + adjoint in {dt:.1f} s; gate passes/s scaled by 2^({n}-{args.qubits})")
-    return rate, O.num_threads(), sample, dt
+    out = np.zeros_like(psi)  # touched before the timed calls
+    t_obs = []
+    for k in term_counts:
+        arr, nt = O._terms(terms[:k])
+        t0 = time.perf_counter()
+        L.oracle_expectation_and_apply(ctypes.addressof(arr), nt, psi.ctypes.data,
+                                       out.ctypes.data, n)
+        t_obs.append(time.perf_counter() - t0)
+    per_term = max(0.0, (t_obs[1] - t_obs[0]) / (term_counts[1] - term_counts[0]))
+    obs_fixed = max(0.0, t_obs[0] - term_counts[0] * per_term)
+    sample_dt = time.perf_counter() - t_start
+    step_at_n = (sum(counts[k] * (fwd[k] + adj[k]) for k in counts) + adj_fixed + obs_fixed +
+                 args.terms * per_term)
+    step = step_at_n * 2.0 ** (args.qubits - n)
+    gates = counts["rot"] + counts["cz"]
+    rate = 2 * gates / step
+    ms = lambda x: f"{x * 1e3:.0f} ms"  # noqa: E731
+    sample = (f"oracle at {n} qubits in place on one state, {sample_dt:.1f} s of timing: per "
+              f"rotation {ms(fwd['rot'])} forward / {ms(adj['rot'])} adjoint, per CZ "
+              f"{ms(fwd['cz'])} / {ms(adj['cz'])}, adjoint sweep fixed {ms(adj_fixed)}, <H> and "
+              f"H psi {ms(per_term)} per term + {ms(obs_fixed)}; the {args.qubits}-qubit step "
+              f"({counts['rot']} rotations, {counts['cz']} CZ, forward and adjoint, {args.terms} "
+              f"terms) extrapolated by state size x2^{args.qubits - n}: {step:.0f} s")
+    return rate, O.num_threads(), sample, sample_dt
 
 
 # ------------------------------------------------------------------ clocks
@@ -271,7 +322,7 @@ def gpu_arm(args):
     traffic = NCU_DRAM_BYTES_PER_AMP.get(dname)
     label = {"fused_adjoint": "arcqml_pass (fused adjoint passes, run-time compiled)",
              "fused_forward": "arcqml_pass (fused forward passes, run-time compiled)",
-             "observable": "k_pauli (observable)"}.get(dname, dname)
+             "observable": "k_pauli_tile (observable tile passes)"}.get(dname, dname)
     roofline = {"kernel": label,
                 "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s",
@@ -282,6 +333,26 @@ def gpu_arm(args):
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                                   "26-qubit pass of this kernel, scaled per amplitude"
                                   if traffic else None}
+    # FP64 roofline of the fused passes, which are bound by FP64 issue rather than HBM. The
+    # algorithmic FP64 work of a Pauli rotation in the scaled unit-diagonal form is one FMA per
+    # amplitude component: 4 flop per amplitude forward; the adjoint un-applies it from psi and
+    # lambda and forms the gradient sum: 12 flop. CZ and the other sign flips take none. Peak:
+    # 148 SMs x 64 FP64 FMA per clock x 2 flop at the median SM clock sampled under load (no
+    # measured FP64 figure exists for these GPUs).
+    rotations = sum(1 for o in c.compile_plan(1) if o.bindings)
+    sm_mhz = (clk or {}).get("sm_mhz") or 1965.0
+    fp64_peak = 148 * 64 * 2 * sm_mhz * 1e6 / 1e12
+    roofline_fp64 = {}
+    for cat, per_amp in (("fused_forward", 4.0), ("fused_adjoint", 12.0)):
+        if cat not in prof or not prof[cat][0] or (cat == "fused_adjoint" and args.forward_only):
+            continue
+        cl, cms, _ = prof[cat]
+        flops = per_amp * rotations * local_amps * args.steps
+        tf = flops / (cms * 1e-3) / 1e12
+        roofline_fp64[cat] = {"bound": "fp64", "achieved": round(tf, 2), "peak": round(fp64_peak, 2),
+                              "unit": "TFLOP/s", "frac": round(tf / fp64_peak, 4),
+                              "flop_per_launch": flops / cl, "avg_launch_ms": cms / cl,
+                              "peak_source": f"nominal at the sampled {sm_mhz:.0f} MHz"}
     # The rate per-gate kernels would reach at the HBM roofline: every gate one pass over the
     # state (32 B per amplitude forward, 64 B adjoint), all GPUs streaming their shards.
     step_bytes = gates * (32.0 if args.forward_only else 96.0) * 2.0 ** n
@@ -295,7 +366,8 @@ def gpu_arm(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "complex128 (f64)", "data": "synthetic (seeded brickwork + random Pauli sum)",
-            "config": config(args, c), "roofline": roofline, "swaps": swaps,
+            "config": config(args, c), "roofline": roofline, "roofline_fp64": roofline_fp64,
+            "swaps": swaps,
             "kernels": {k: {"launches": v[0], "ms": round(v[1], 3),
                             "gbs": round(v[2] / (v[1] * 1e-3) / 1e9, 1) if v[1] else 0}
                         for k, v in prof.items() if v[0]},
@@ -353,10 +425,12 @@ def reference_arm(args):
         return
     from arcqml_b200 import workloads  # noqa: F401 (generators only)
     rates, samples = [], []
+    # each step: a bounded sample of the workload at 28 qubits (a few seconds on the host)
+    small = dict(rot=(1, 1), cz=(1, 1), term_counts=(1, 4))
     for _ in range(args.warmup):
-        cpu_sample(args)
+        cpu_sample(args, **small)
     for _ in range(args.steps):
-        rate, cores, sample, _ = cpu_sample(args)
+        rate, cores, sample, _ = cpu_sample(args, **small)
         rates.append(rate)
     value = statistics.median(rates)
     c, _ = workload(args.qubits, args.layers, args.terms, args.seed)
