@@ -599,6 +599,23 @@ size_t arcqml_rt_v2_jit_info(uint64_t *kernels_compiled, uint64_t *launches, uin
     return last.size();
 }
 
+int32_t arcqml_rt_v2_shard_swap_nccl(arcqml_c128 *shard, size_t num_local_qubits,
+                                     const uint32_t *global_bits, const uint32_t *local_positions,
+                                     size_t num_pairs, void *nccl_comm, arcqml_c128 *staging,
+                                     size_t staging_len, void *stream) {
+    return guarded([&] {
+        if (!nccl_comm) fail("NCCL communicator is null");
+        if (!global_bits) fail("global bit list is null");
+        if (!staging) fail("staging buffer is null");
+        check_slices(shard, num_local_qubits, local_positions, num_pairs, 0, 0);
+        ThreadContext &ctx = thread_context();
+        shard_swap_nccl(reinterpret_cast<double2 *>(shard), uint32_t(num_local_qubits),
+                        global_bits, local_positions, uint32_t(num_pairs), nccl_comm,
+                        reinterpret_cast<double2 *>(staging), staging_len,
+                        pick_stream(ctx, stream));
+    });
+}
+
 int32_t arcqml_rt_v2_shard_slices_from(arcqml_c128 *amplitudes, size_t num_local_qubits,
                                        const uint32_t *positions, size_t num_positions,
                                        uint64_t chunk_begin, uint64_t chunk_len,

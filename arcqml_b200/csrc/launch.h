@@ -47,6 +47,12 @@ void launch_slices(double2 *amps, uint32_t n_local, const uint32_t *positions, u
                    uint64_t chunk_begin, uint64_t chunk_len, uint64_t skip, double2 *staging,
                    bool unpack, cudaStream_t s);
 constexpr uint32_t kMaxSliceBits = 8;
+// Swaps the global qubits at rank bits global_bits[i] with the shard's local positions
+// local_positions[i] over an NCCL communicator (shard_nccl.cpp): pack, grouped send/receive with
+// each peer, unpack, in chunks that fit staging (2 x (2^k - 1) x chunk amplitudes).
+void shard_swap_nccl(double2 *shard, uint32_t n_local, const uint32_t *global_bits,
+                     const uint32_t *local_positions, uint32_t k, void *comm, double2 *staging,
+                     size_t staging_len, cudaStream_t s);
 // amps[index(y, o)] <- sources[y][o - chunk_begin] for every slice value y whose source is
 // non-null (sources may be peer mappings of other GPUs' buffers).
 void launch_slices_from(double2 *amps, const uint32_t *positions, uint32_t k,

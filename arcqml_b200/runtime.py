@@ -125,6 +125,7 @@ SIGNATURES = {
     "arcqml_rt_v2_small_adam": (_I32, [_P, _P, _P, _S, _P, _P, _S, _P, _P, C.c_uint64, _S, _D,
                                       _D, _D, _D, _D, _P, _P]),
     "arcqml_rt_v2_shard_slices_from": (_I32, [_P, _S, _P, _S, C.c_uint64, C.c_uint64, _P, _P]),
+    "arcqml_rt_v2_shard_swap_nccl": (_I32, [_P, _S, _P, _P, _S, _P, _P, _S, _P]),
     "arcqml_rt_v2_peer_buffer_create": (_I32, [_S, _P, _P]),
     "arcqml_rt_v2_peer_buffer_open": (_I32, [_P, _P]),
     "arcqml_rt_v2_peer_buffer_close": (_I32, [_P]),
@@ -642,6 +643,19 @@ def shard_slices_from(shard, num_local_qubits: int, positions: Sequence[int], ch
     _status(load().arcqml_rt_v2_shard_slices_from(
         _dev_ptr(shard), num_local_qubits, pos, len(positions), chunk_begin, chunk_len, src,
         _stream_ptr(stream)))
+
+
+def shard_swap_nccl(shard, num_local_qubits: int, global_bits: Sequence[int],
+                    local_positions: Sequence[int], nccl_comm: int, staging,
+                    stream=None) -> None:
+    """Swaps the global qubits at rank bits global_bits[i] with the shard's local positions
+    local_positions[i] over a raw NCCL communicator (arcqml_rt_v2_shard_swap_nccl); staging is a
+    complex128 CUDA tensor of scratch amplitudes."""
+    gb = (C.c_uint32 * len(global_bits))(*global_bits)
+    lp = (C.c_uint32 * len(local_positions))(*local_positions)
+    _status(load().arcqml_rt_v2_shard_swap_nccl(
+        _dev_ptr(shard), num_local_qubits, gb, lp, len(global_bits), C.c_void_p(nccl_comm),
+        _dev_ptr(staging), staging.numel(), _stream_ptr(stream)))
 
 
 def shard_slices_ptr(shard, num_local_qubits: int, positions: Sequence[int], chunk_begin: int,

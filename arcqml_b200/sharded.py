@@ -312,6 +312,20 @@ class DistComm:
         for w in handle:
             w.wait()
 
+    def nccl_comm(self) -> Optional[int]:
+        """The group's raw NCCL communicator (an ncclComm_t address) for the runtime's own
+        swaps, or None when the group has none (gloo) or torch does not expose it."""
+        if not self.nccl:
+            return None
+        import torch
+        pg = self.group if self.group is not None else self.dist.distributed_c10d._get_default_group()
+        try:
+            backend = pg._get_backend(torch.device("cuda", torch.cuda.current_device()))
+            ptr = int(backend._comm_ptr())
+        except Exception:  # noqa: BLE001 - an older torch, or no communicator yet
+            return None
+        return ptr or None
+
     def allreduce_sum(self, values: np.ndarray) -> np.ndarray:
         import torch
         dev = torch.device("cuda", torch.cuda.current_device()) if self.nccl else torch.device("cpu")
@@ -431,6 +445,9 @@ class RuntimeBackend:
     def gather_from(self, shard, n_local, positions, chunk_begin, chunk_len, sources) -> None:
         self.rt.shard_slices_from(shard, n_local, positions, chunk_begin, chunk_len, sources)
 
+    def swap_nccl(self, shard, n_local, global_bits, local_positions, comm_ptr, staging) -> None:
+        self.rt.shard_swap_nccl(shard, n_local, global_bits, local_positions, comm_ptr, staging)
+
     def peer_open(self, handle: bytes) -> int:
         return self.rt.PeerBuffer.open(handle)
 
@@ -475,11 +492,17 @@ class ShardedStateVectorSimulator:
         self._staging = None
         # Swap transport: "peer" (each rank gathers its slices from the peers' packed buffers
         # over NVLink with its own kernel) when every rank can map the others' memory, else
-        # "p2p" (point-to-point sends through the communicator). ARCQML_SWAP overrides.
+        # "p2p" (point-to-point sends through the communicator); "nccl" (the runtime's
+        # arcqml_rt_v2_shard_swap_nccl on the group's own NCCL communicator) on request.
+        # ARCQML_SWAP overrides.
         import os
         want = transport or os.environ.get("ARCQML_SWAP") or "auto"
-        if want not in ("auto", "peer", "p2p"):
+        if want not in ("auto", "peer", "p2p", "nccl"):
             raise ShardError(f"unknown swap transport {want!r}")
+        if want == "nccl" and not (hasattr(self.backend, "swap_nccl") and
+                                   getattr(self.comm, "nccl_comm", lambda: None)() is not None):
+            raise ShardError("the nccl swap transport needs an NCCL process group and the "
+                             "GPU backend")
         can_peer = (size > 1 and hasattr(self.comm, "allgather_object") and
                     hasattr(self.backend, "gather_from"))
         if want == "auto":
@@ -697,6 +720,24 @@ class ShardedStateVectorSimulator:
             self._peer = self._share_peer_buffer()
             if self._peer is None:
                 self.transport = "p2p"
+        if self.transport == "nccl":
+            # the runtime's own swap (arcqml_rt_v2_shard_swap_nccl) over the group's communicator
+            chunk = min(others, max(1, self.chunk // nblk))
+            chunk = 1 << (chunk.bit_length() - 1)
+            if getattr(self, "_nccl_stage", None) is None or \
+                    self._nccl_stage.numel() < 2 * nblk * chunk:
+                self._nccl_stage = be.empty(2 * nblk * chunk)
+            ptr = self.comm.nccl_comm()
+            for t in tensors:
+                be.swap_nccl(t, n_l, gbits, lpos, ptr, self._nccl_stage)
+            if ev is not None:
+                ev[1].record()
+                self._events.append(ev)
+            self.stats.swaps += 1
+            self.stats.qubits += k
+            self.stats.bytes_sent += len(tensors) * nblk * others * 16
+            L.apply_swap(pairs)
+            return
         if self.transport == "peer":
             for t in tensors:
                 self._peer_swap(t, n_l, lpos, x, peers, others)

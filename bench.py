@@ -568,6 +568,15 @@ def small_arm(args):
             "cpu_baseline": {"value": round(per_unit / cpu_dt, 3), "unit": unit_name,
                              "cores": O.num_threads(), "kind": "port",
                              "sample": f"one unit of the same work on the oracle in {cpu_dt:.3f} s"}}
+    if args.workload == "qnn":
+        # FP64 lower bound of one full-batch gradient: every row runs the 120 gates forward, 240
+        # gate applications in the reverse sweep and one observable pass, ~14 flop per
+        # amplitude each (a complex 2x2 on a pair): B (m_fwd + 2 m_bwd + 1) 14 D flop.
+        flop = 1024 * (120 + 2 * 120 + 1) * 14 * 1024
+        tf = flop * args.steps / (ms * 1e-3) / 1e12
+        line["fp64"] = {"flop_per_gradient": flop, "achieved_tflops": round(tf, 3),
+                        "peak_tflops": 37.2, "frac": round(tf / 37.2, 4),
+                        "peak_source": "nominal: 148 SMs x 64 FP64 FMA/clock x 2 x 1965 MHz"}
     print(json.dumps(line), flush=True)
 
 

@@ -119,6 +119,23 @@ int32_t arcqml_rt_v2_shard_slices(arcqml_c128 *amplitudes, size_t num_local_qubi
 int32_t arcqml_rt_v2_sample(const arcqml_c128 *amplitudes, size_t num_qubits, uint64_t shots,
                             uint64_t seed, uint64_t *indices, double *norm_sqr, void *stream);
 
+/* Global-qubit swap of a sharded state over the caller's NCCL communicator (nccl_comm is an
+ * ncclComm_t whose ranks each hold one shard: rank r the 2^num_local_qubits amplitudes whose top
+ * log2(size) index bits equal r). Exchanges, for every i < num_pairs, the qubit at rank bit
+ * global_bits[i] with the qubit at the shard's position local_positions[i]: each rank sends the
+ * slices whose local bits differ from its own rank bits to the rank holding them and receives
+ * the matching slices in their place (the all-to-all among the 2^num_pairs ranks that differ in
+ * those rank bits). staging (device) must hold 2 x (2^num_pairs - 1) x chunk amplitudes for some
+ * chunk >= 1; larger buffers move larger chunks. Every rank of the communicator calls it with
+ * the same pairs. Runs on `stream`; the NCCL library is the one loaded in the process. No
+ * counterpart in the reference: this is the data movement under the sharded 32- and 35-qubit
+ * configurations, for callers (an arcqml-sim with device-resident shards) that own the
+ * communicator and the layout. */
+int32_t arcqml_rt_v2_shard_swap_nccl(arcqml_c128 *shard, size_t num_local_qubits,
+                                     const uint32_t *global_bits, const uint32_t *local_positions,
+                                     size_t num_pairs, void *nccl_comm, arcqml_c128 *staging,
+                                     size_t staging_len, void *stream);
+
 /* Same slice layout as arcqml_rt_v2_shard_slices, gathering into the shard: for every slice
  * value y with sources[y] != NULL (sources has 2^num_positions entries) and o in
  * [chunk_begin, chunk_begin + chunk_len): amplitudes[index(y, o)] <- sources[y][o - chunk_begin].

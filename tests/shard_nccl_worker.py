@@ -48,7 +48,7 @@ def main():
                       req=c.requires_grad_mask(True, False)))
     ok = True
     for case in cases:
-        for transport in ("p2p", "peer"):
+        for transport in ("p2p", "peer", "nccl"):
             sim = ShardedStateVectorSimulator(case["n"], comm=DistComm(), backend=RuntimeBackend(),
                                               chunk_amplitudes=case.get("chunk", 1 << 20),
                                               transport=transport, peer_bytes=1 << 20)

@@ -258,3 +258,22 @@ def test_binding_signatures_match_the_headers(runtime):
         got = [kinds[a] for a in args]
         assert got == want, (name, got, want)
         assert kinds[res] == ("void" if cres == "void" else c_kind(cres)), (name, res, cres)
+
+
+def test_shard_swap_nccl_argument_checks(runtime):
+    """arcqml_rt_v2_shard_swap_nccl rejects a missing communicator, staging buffer or bit list
+    and bad slice positions before it touches NCCL or the device."""
+    L = runtime.load()
+    gb = (C.c_uint32 * 1)(0)
+    lp = (C.c_uint32 * 1)(3)
+    fake = C.c_void_p(0x1000)  # never dereferenced: the checks fail first
+    cases = [
+        ((fake, 10, gb, lp, 1, None, fake, 64, None), "communicator is null"),
+        ((fake, 10, None, lp, 1, fake, fake, 64, None), "global bit list is null"),
+        ((fake, 10, gb, lp, 1, fake, None, 64, None), "staging buffer is null"),
+        ((fake, 2, gb, lp, 1, fake, fake, 64, None), "outside the 2-qubit shard"),
+        ((fake, 10, gb, lp, 0, fake, fake, 64, None), "between 1 and 8 positions"),
+    ]
+    for args, msg in cases:
+        assert L.arcqml_rt_v2_shard_swap_nccl(*args) != 0
+        assert msg in runtime.last_error()
