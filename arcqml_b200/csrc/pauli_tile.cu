@@ -286,7 +286,7 @@ double2 term_weight(const Observable &obs, uint64_t flip, uint32_t k) {
 
 uint32_t observable_tile_passes(const Observable &obs, uint32_t n) {
     std::vector<TilePass> passes;
-    if (n < kTileMinQubits || !cover(obs, n, passes)) return 0;
+    if (n < kTileMinQubits || n > 63 || !cover(obs, n, passes)) return 0;
     return uint32_t(passes.size());
 }
 
@@ -297,7 +297,8 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
                       double *value_host, bool accumulate, ThreadContext &ctx, cudaStream_t s) {
     if (n < kTileMinQubits || n > 63) return false;
     std::vector<TilePass> passes;
-    if (!cover(obs, n, passes)) return false;
+    // an observable without terms takes no pass: the gather kernel writes its zero H psi
+    if (!cover(obs, n, passes) || passes.empty()) return false;
     // device tables: per pass its groups then its members, 16-byte aligned
     std::vector<size_t> goff(passes.size()), moff(passes.size());
     std::vector<uint32_t> nmem(passes.size());

@@ -69,7 +69,7 @@ def c5(fixture, rank, report):
         norm = world_norm(sim)
         value = sim.observe(terms, True)
         swaps = sim.stats.swaps
-        req = np.zeros(1, dtype=np.uint8)
+        req = np.zeros(c.num_parameters() + 1, dtype=np.uint8)  # no gradient requested
         sim.adjoint(ops, 0.0, req)
         back = sim.amplitudes_at([0, 1, 1 << (n - 1), (1 << n) - 1])
         norm0 = world_norm(sim)
