@@ -743,6 +743,9 @@ struct TableRunner {
     static constexpr bool kSingleBuffer = false;
     static constexpr bool kOpsInSmem = true;
     static constexpr bool kMatsInSmem = true;
+    // the table-driven kernel scales each gradient term as it adds it
+    template <class MT>
+    __device__ static __forceinline__ double row_factor(uint32_t, const MT &) { return 1.0; }
     template <int RB, bool ADJ>
     __device__ static __forceinline__ void run(uint32_t sb, uint32_t k, double2 *tp, double2 *tl,
                                                const FOp *ops, const double2 *mats,

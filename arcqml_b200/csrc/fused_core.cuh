@@ -258,66 +258,60 @@ __device__ __forceinline__ void fs_scale(double2 (&v)[1 << RB], double2 sigma) {
 }
 
 // Gradient sums Im<lam|P|psi> and Re-forms over the thread's elements: one FMA per product
-// term (2 FP64 instructions per amplitude), four partial sums for independent chains.
+// term (2 FP64 instructions per amplitude), two partial sums (one addition to close them).
 template <int RB, int B>
 __device__ __forceinline__ double g_x(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z[4] = {0.0, 0.0, 0.0, 0.0};
-    int k = 0;
+    double a = 0.0, b = 0.0;
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
         if (e & (1 << B)) continue;
         const int f = e | (1 << B);
-        double &a = z[(k & 1) * 2], &b = z[(k & 1) * 2 + 1];
         a = fma(w[e].x, v[f].y, a);
         a = fma(-w[e].y, v[f].x, a);
         b = fma(w[f].x, v[e].y, b);
         b = fma(-w[f].y, v[e].x, b);
-        ++k;
     }
-    return (z[0] + z[1]) + (z[2] + z[3]);
+    return a + b;
 }
 
 template <int RB, int B>
 __device__ __forceinline__ double g_y(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z[4] = {0.0, 0.0, 0.0, 0.0};
-    int k = 0;
+    double a = 0.0, b = 0.0;
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
         if (e & (1 << B)) continue;
         const int f = e | (1 << B);
-        double &a = z[(k & 1) * 2], &b = z[(k & 1) * 2 + 1];
         a = fma(w[f].x, v[e].x, a);
         a = fma(w[f].y, v[e].y, a);
         b = fma(-w[e].x, v[f].x, b);
         b = fma(-w[e].y, v[f].y, b);
-        ++k;
     }
-    return (z[0] + z[1]) + (z[2] + z[3]);
+    return a + b;
 }
 
 template <int RB, int B>
 __device__ __forceinline__ double g_z(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z[4] = {0.0, 0.0, 0.0, 0.0};
+    double z[2] = {0.0, 0.0};
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
         const bool neg = (e >> B) & 1;  // compile-time: folds into the FMA operands
-        double &a = z[e & 3];
+        double &a = z[e & 1];
         a = fma(neg ? -w[e].x : w[e].x, v[e].y, a);
         a = fma(neg ? w[e].y : -w[e].y, v[e].x, a);
     }
-    return (z[0] + z[1]) + (z[2] + z[3]);
+    return z[0] + z[1];
 }
 
 template <int RB>
 __device__ __forceinline__ double g_z_uni(const double2 (&v)[1 << RB], const double2 (&w)[1 << RB]) {
-    double z[4] = {0.0, 0.0, 0.0, 0.0};
+    double z[2] = {0.0, 0.0};
 #pragma unroll
     for (int e = 0; e < (1 << RB); ++e) {
-        double &a = z[e & 3];
+        double &a = z[e & 1];
         a = fma(w[e].x, v[e].y, a);
         a = fma(-w[e].y, v[e].x, a);
     }
-    return (z[0] + z[1]) + (z[2] + z[3]);
+    return z[0] + z[1];
 }
 
 // One-target gates and gradient terms on one register pair (x0 / v0 / w0: target bit 0), for
@@ -655,7 +649,10 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
                 s3 += row[t + 3];
             }
             for (; t < nthreads; ++t) s0 += row[t];
-            partials[size_t(sacc_base + a) * stride + blockIdx.x] = (s0 + s1) + (s2 + s3);
+            double f;  // the row's factor (compiled kernels add their sums unscaled)
+            if constexpr (Runner::kMatsInSmem) f = Runner::row_factor(a, smats);
+            else f = Runner::row_factor(a, gmats);
+            partials[size_t(sacc_base + a) * stride + blockIdx.x] = ((s0 + s1) + (s2 + s3)) * f;
         }
     }
 }

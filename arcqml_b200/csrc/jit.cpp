@@ -393,6 +393,14 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
     return true;
 }
 
+// Per pass-local accumulator row, the factor its total is multiplied by (an expression in the
+// pass's matrix table M): rows are summed unscaled, the factor applied once per row per CTA.
+using RowFactors = std::vector<std::string>;
+void set_factor(RowFactors &rf, uint32_t row, const std::string &f) {
+    if (rf.size() <= row) rf.resize(row + 1, "1.0");
+    rf[row] = f;
+}
+
 // Gradients on general bit positions (on unless ARCQML_FAST_DIAG=0), in the order of the table-driven
 // kernel: a Pauli-rotation gradient Im<lam|P|psi> on psi before U^dagger (X / Y over the
 // target pairs whose controls are set, Z with the sign of the target bit), then U^dagger on
@@ -400,7 +408,7 @@ bool emit_apply(std::ostringstream &c, const FOp &o, const char *r, uint32_t rb,
 // In a scaled pass psi and lambda carry the pass factor sigma from before the op (which keeps
 // its plain form), so each sum is multiplied by |sigma|^2 = 2 * mats[soff].y.
 bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
-                          uint32_t tbits) {
+                          uint32_t tbits, RowFactors &rf) {
     const OpBits b = op_bits(o, S, rb, tbits);
     if (!b.ok) return false;
     const bool diag = o.kind == FK_D1 || o.kind == FK_D2;
@@ -410,11 +418,11 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
     if ((one || four) && (o.rb0 >= rb || (b.creg & t0))) return false;
     if (four && (o.rb1 >= rb || o.rb1 == o.rb0 || b.creg || !b.cond.empty())) return false;
     const std::string so = std::to_string(o.soff);
+    // the sum goes into the row unscaled; its factor is applied once to the row's total
     auto put_acc = [&](uint32_t slot, bool pauli) {
-        c << acc_call(rb) << "(sacc, "
-          << o.acc[slot] << "u * kCols, ";
-        if (pauli) c << (o.sgrad ? "M[" + so + "].y * z); " : "0.5 * z); ");
-        else c << (o.sgrad ? "2.0 * M[" + so + "].y * z); " : "z); ");
+        c << acc_call(rb) << "(sacc, " << o.acc[slot] << "u * kCols, z); ";
+        if (pauli) set_factor(rf, o.acc[slot], o.sgrad ? "M[" + so + "].y" : "0.5");
+        else set_factor(rf, o.acc[slot], o.sgrad ? "2.0 * M[" + so + "].y" : "1.0");
     };
     auto apply_to = [&](const char *r) {
         c << "\n        ";
@@ -543,7 +551,7 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
 
 // Gradient then U^dagger on psi and lambda, as adj_fast does it.
 bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
-                  uint32_t tbits) {
+                  uint32_t tbits, RowFactors &rf) {
     if (o.gkind == GK_NONE) {
         if (!emit_apply(c, o, "v", rb, S, tbits)) return false;
         c << "\n        ";
@@ -553,7 +561,7 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
                             (o.code == FC_RY && o.gcode == GF_Y) ||
                             (o.code == FC_D1_REG && o.gcode == GF_Z_REG) ||
                             (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
-    if (!pauli_fast) return fast_diag() && emit_adjoint_general(c, o, rb, S, tbits);
+    if (!pauli_fast) return fast_diag() && emit_adjoint_general(c, o, rb, S, tbits, rf);
     const int b0 = o.rb0;
     if (b0 >= int(rb) && o.code != FC_D1_UNI) return false;
     c << "{ double z; ";
@@ -571,11 +579,9 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
     if (!emit_apply(c, o, "v", rb, S, tbits)) return false;
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb, S, tbits)) return false;
-    // 0.5 * z, times |sigma|^2 in a scaled pass
-    c << "\n        " << acc_call(rb) << "(sacc, "
-      << o.acc[0] << "u * kCols, ";
-    if (o.sgrad) c << "M[" << o.soff << "].y * z); }";
-    else c << "0.5 * z); }";
+    // the row's factor, applied to its total: 0.5, times |sigma|^2 in a scaled pass
+    c << "\n        " << acc_call(rb) << "(sacc, " << o.acc[0] << "u * kCols, z); }";
+    set_factor(rf, o.acc[0], o.sgrad ? "M[" + std::to_string(o.soff) + "].y" : "0.5");
     return true;
 }
 
@@ -590,6 +596,7 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     const size_t nmats = st.mats.empty() ? 1 : st.mats.size();
     if (params && nmats * sizeof(double2) > kJitMaxParamMats) return std::string();
     if (params) c << "struct PassMats { double2 m[" << nmats << "]; };\n";
+    RowFactors rf;
     c << "struct PassOps {\n"
          "    static constexpr int kAccLanes = " << acc_lanes(adj, rb) << ";\n"
          "    static constexpr bool kSingleBuffer = " << (single ? "true" : "false") << ";\n"
@@ -631,7 +638,7 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
         }
         for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
             c << "        ";
-            const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb, S, kb)
+            const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb, S, kb, rf)
                                 : emit_apply(c, st.ops[oi], "v", rb, S, kb);
             if (!ok) return std::string();
             c << "\n";
@@ -649,6 +656,16 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
         c << "        break;\n";
     }
     c << "        }\n"
+         "    }\n";
+    // factors of the accumulator rows (adjoint), applied to each row's total
+    c << "    template <class MT>\n"
+         "    __device__ static __forceinline__ double row_factor(uint32_t a, const MT &MS) {\n"
+         "        const auto &M = mats_of(MS);\n"
+         "        (void)M;\n"
+         "        switch (a) {\n";
+    for (size_t r = 0; r < rf.size(); ++r) c << "        case " << r << ": return " << rf[r] << ";\n";
+    c << "        default: return 1.0;\n"
+         "        }\n"
          "    }\n"
          "};\n";
     const int bound = (adj || rb == 4) ? 256 : 512;

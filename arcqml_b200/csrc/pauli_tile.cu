@@ -36,7 +36,7 @@ struct TileMember {  // one term of a group, 32 bytes
     double2 w;       // coefficient * i^(y mod 4) * (-1)^popc(flip & z)
     uint64_t z;      // phase mask (global qubits)
     uint32_t zl;     // phase mask on the tile-local bits 0-7 (the thread-index bits)
-    uint32_t tab;    // bit i: parity(i & tile-local bits 8-11 of the phase mask), i < 16
+    uint32_t h;      // phase mask on the tile-local bits 8-11 (the element bits), 0-15
 };
 static_assert(sizeof(TileMember) == 32, "TileMember layout");
 
@@ -54,19 +54,46 @@ __device__ __forceinline__ uint32_t tphys(uint32_t j) {
 __device__ __forceinline__ double2 tcfma(double2 a, double2 b, double2 c) {
     return make_double2(fma(a.x, b.x, fma(-a.y, b.y, c.x)), fma(a.x, b.y, fma(a.y, b.x, c.y)));
 }
-// a with both components' signs flipped when bit 31 of m is set
-__device__ __forceinline__ double2 tflip(double2 a, uint32_t m) {
-    return make_double2(__hiloint2double(__double2hiint(a.x) ^ int(m), __double2loint(a.x)),
-                        __hiloint2double(__double2hiint(a.y) ^ int(m), __double2loint(a.y)));
-}
 __device__ __forceinline__ uint32_t parity64(uint64_t x) { return uint32_t(__popcll(x) & 1); }
+__host__ __device__ constexpr uint32_t cparity(uint32_t x) { return x ? (x & 1u) ^ cparity(x >> 1) : 0u; }
+__device__ __forceinline__ double2 tneg(double2 a) { return make_double2(-a.x, -a.y); }
 
-// The per-amplitude signs of member m for this thread's 16 amplitudes of the tile at `base`:
-// bit i set where (-1)^popc(t_i & z) = -1.
-__device__ __forceinline__ uint32_t member_signs(const TileMember &m, uint64_t base, uint32_t tid) {
-    const uint32_t s = parity64(base & m.z) ^ (uint32_t(__popc(tid & m.zl)) & 1u);
-    return m.tab ^ (s ? 0xffffu : 0u);
+// The sign (-1)^popc(t & z) of a member for this thread's element i of the tile at `base`:
+// (-1)^s0 * (-1)^parity(i & h), s0 from the tile base and the thread's own index bits.
+__device__ __forceinline__ double2 member_weight(const TileMember &m, uint64_t base, uint32_t tid) {
+    const uint32_t s0 = parity64(base & m.z) ^ (uint32_t(__popc(tid & m.zl)) & 1u);
+    return s0 ? tneg(m.w) : m.w;
 }
+
+__device__ __forceinline__ void cp_async16t(void *smem, const void *gmem) {
+    const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(a), "l"(gmem) : "memory");
+}
+
+// acc[i] += (-1)^parity(i & H) * w * psi[partner of element i]: the element signs are constants
+// of the code (one instantiation per phase pattern H on the element bits).
+template <uint32_t H>
+__device__ __forceinline__ void add_group(double2 (&acc)[16], const double2 *tile, uint32_t x,
+                                          double2 w) {
+    const double2 wn = tneg(w);
+#pragma unroll
+    for (uint32_t i = 0; i < 16; ++i)
+        acc[i] = tcfma(cparity(i & H) ? wn : w, tile[x ^ tphys(i << 8)], acc[i]);
+}
+
+// wi[i] += (-1)^parity((i0 + i) & H) * w for elements i0..i0+7 (a group of several terms)
+template <uint32_t H, uint32_t I0>
+__device__ __forceinline__ void add_weight(double2 (&wi)[8], double2 w) {
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) {
+        const bool neg = cparity((I0 + i) & H);
+        wi[i] = make_double2(neg ? wi[i].x - w.x : wi[i].x + w.x,
+                             neg ? wi[i].y - w.y : wi[i].y + w.y);
+    }
+}
+
+#define ARCQML_H16(M) M(0) M(1) M(2) M(3) M(4) M(5) M(6) M(7) M(8) M(9) M(10) M(11) M(12) \
+    M(13) M(14) M(15)
 
 __global__ void __launch_bounds__(kTileThreads, 2)
     k_pauli_tile(const double2 *__restrict__ psi, double2 *__restrict__ out, uint32_t n,
@@ -101,63 +128,88 @@ __global__ void __launch_bounds__(kTileThreads, 2)
     };
     // element i of this thread: tile index j = tid | i << 8, state offset base + off(i)
     auto elem_off = [&](uint32_t i) { return uint64_t(tid & 15u) | hioff[(tid >> 4) | (i << 4)]; };
+    const bool rd = P.read_out && out;
 
     double ev = 0.0;
     for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x) {
         const uint64_t base = tile_base(T);
+        // psi's tile straight into shared memory; meanwhile this thread's H psi so far
 #pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) tile[ptid ^ tphys(i << 8)] = psi[base + elem_off(i)];
+        for (uint32_t i = 0; i < 16; ++i)
+            cp_async16t(tile + (ptid ^ tphys(i << 8)), psi + base + elem_off(i));
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        double2 acc[16];
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i)
+            acc[i] = rd ? out[base + elem_off(i)] : make_double2(0.0, 0.0);
         const uint64_t Tn = T + gridDim.x;
         if (Tn < total_tiles) {  // the next tile into L2 while this one is computed
             const uint64_t nb = tile_base(Tn);
             for (uint32_t r = tid; r < 512u; r += blockDim.x) {
                 const double2 *p = psi + nb + hioff[r >> 1] + (r & 1u) * 8u;
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-                if (P.read_out && out) {
+                if (rd) {
                     const double2 *q = out + nb + hioff[r >> 1] + (r & 1u) * 8u;
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(q));
                 }
             }
         }
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncthreads();
-        double2 acc[16];
+        // <psi|contribution> = <psi|acc after> - <psi|acc before>
+        if (rd) {
 #pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) acc[i] = make_double2(0.0, 0.0);
+            for (uint32_t i = 0; i < 16; ++i) {
+                const double2 pi = tile[ptid ^ tphys(i << 8)];
+                ev -= fma(pi.x, acc[i].x, pi.y * acc[i].y);
+            }
+        }
         for (uint32_t gi = 0; gi < P.ngroups; ++gi) {
             const uint4 G = sg[gi];
             const uint32_t x = ptid ^ G.x;
             if (G.z - G.y == 1) {
                 const TileMember &m = smem_m[G.y];
-                const uint32_t sg_bits = member_signs(m, base, tid);
-                const double2 w = m.w;
-#pragma unroll
-                for (uint32_t i = 0; i < 16; ++i) {
-                    const double2 q = tile[x ^ tphys(i << 8)];
-                    acc[i] = tcfma(tflip(w, (sg_bits << (31 - i)) & 0x80000000u), q, acc[i]);
+                const double2 w = member_weight(m, base, tid);
+                switch (m.h) {
+#define ARCQML_CASE(H) \
+                case H: add_group<H>(acc, tile, x, w); break;
+                    ARCQML_H16(ARCQML_CASE)
+#undef ARCQML_CASE
+                default: break;
                 }
             } else {
-                // several terms share the flip mask: per amplitude the sum of their signed
-                // weights, in two halves of eight amplitudes (registers)
+                // several terms share the flip mask: per element the sum of their signed
+                // weights, in two halves of eight elements (registers)
 #pragma unroll
-                for (uint32_t h = 0; h < 16; h += 8) {
+                for (uint32_t half = 0; half < 2; ++half) {
                     double2 wi[8];
 #pragma unroll
                     for (uint32_t i = 0; i < 8; ++i) wi[i] = make_double2(0.0, 0.0);
                     for (uint32_t mi = G.y; mi < G.z; ++mi) {
                         const TileMember &m = smem_m[mi];
-                        const uint32_t sg_bits = member_signs(m, base, tid);
-                        const double2 w = m.w;
-#pragma unroll
-                        for (uint32_t i = 0; i < 8; ++i) {
-                            const double2 ws =
-                                tflip(w, (sg_bits << (31 - (h + i))) & 0x80000000u);
-                            wi[i] = make_double2(wi[i].x + ws.x, wi[i].y + ws.y);
+                        const double2 w = member_weight(m, base, tid);
+                        if (half == 0) {
+                            switch (m.h) {
+#define ARCQML_CASE(H) \
+                            case H: add_weight<H, 0>(wi, w); break;
+                                ARCQML_H16(ARCQML_CASE)
+#undef ARCQML_CASE
+                            default: break;
+                            }
+                        } else {
+                            switch (m.h) {
+#define ARCQML_CASE(H) \
+                            case H: add_weight<H, 8>(wi, w); break;
+                                ARCQML_H16(ARCQML_CASE)
+#undef ARCQML_CASE
+                            default: break;
+                            }
                         }
                     }
 #pragma unroll
                     for (uint32_t i = 0; i < 8; ++i) {
-                        const double2 q = tile[x ^ tphys((h + i) << 8)];
-                        acc[h + i] = tcfma(wi[i], q, acc[h + i]);
+                        const uint32_t e = half * 8 + i;
+                        acc[e] = tcfma(wi[i], tile[x ^ tphys(e << 8)], acc[e]);
                     }
                 }
             }
@@ -166,15 +218,7 @@ __global__ void __launch_bounds__(kTileThreads, 2)
         for (uint32_t i = 0; i < 16; ++i) {
             const double2 pi = tile[ptid ^ tphys(i << 8)];
             ev += fma(pi.x, acc[i].x, pi.y * acc[i].y);
-            if (out) {
-                double2 *o = out + base + elem_off(i);
-                double2 v = acc[i];
-                if (P.read_out) {
-                    const double2 prev = *o;
-                    v = make_double2(prev.x + v.x, prev.y + v.y);
-                }
-                *o = v;
-            }
+            if (out) out[base + elem_off(i)] = acc[i];
         }
         __syncthreads();  // the tile is overwritten by the next iteration
     }
@@ -329,9 +373,7 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
                 m.z = obs.zmask[k];
                 const uint32_t zl = compress(obs.zmask[k], S);
                 m.zl = zl & 0xffu;
-                m.tab = 0;
-                for (uint32_t i = 0; i < 16; ++i)
-                    if (__builtin_popcount(i & (zl >> 8)) & 1) m.tab |= 1u << i;
+                m.h = zl >> 8;
             }
         }
     }

@@ -96,7 +96,7 @@ int drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const dou
     for (uint32_t a = 0; a < h->nacc; ++a) {
         double s = 0.0;
         for (uint32_t t = 0; t < cols; ++t) s += sacc[size_t(a) * cols + t];
-        acc[a] = s;
+        acc[a] = s * Ops::row_factor(a, mats);
     }
     for (size_t i = rows; i < rows + guard; ++i)
         if (sacc[i] != 12345.0) return 1;
