@@ -58,10 +58,28 @@ __device__ __forceinline__ void accumulate_quad(double *sacc, uint32_t row, doub
     z += __shfl_xor_sync(0xffffffffu, z, 2);
     if ((threadIdx.x & 3u) == 0) sacc[row + (threadIdx.x >> 2)] += z;
 }
+
+// Two gradient sums z0 (row r0) and z1 (row r1) of this thread, each summed over its group of
+// four lanes: one shuffle round leaves lane l with the pair's partial of z(l & 1), a second sums
+// it over lane bit 1; lanes 0 and 1 of the quad add the results into rows r0 and r1. Every lane
+// of the warp calls it.
+__device__ __forceinline__ void accumulate_quad2(double *sacc, double z0, double z1, uint32_t r0,
+                                                 uint32_t r1) {
+    const bool odd = threadIdx.x & 1u;
+    double keep = odd ? z1 : z0;
+    keep += __shfl_xor_sync(0xffffffffu, odd ? z0 : z1, 1);
+    keep += __shfl_xor_sync(0xffffffffu, keep, 2);
+    if ((threadIdx.x & 2u) == 0) sacc[(odd ? r1 : r0) + (threadIdx.x >> 2)] += keep;
+}
 #else
 // Host runs execute the threads one after another: the group's column takes each lane's z.
 __device__ __forceinline__ void accumulate_quad(double *sacc, uint32_t row, double z) {
     sacc[row + (threadIdx.x >> 2)] += z;
+}
+__device__ __forceinline__ void accumulate_quad2(double *sacc, double z0, double z1, uint32_t r0,
+                                                 uint32_t r1) {
+    sacc[r0 + (threadIdx.x >> 2)] += z0;
+    sacc[r1 + (threadIdx.x >> 2)] += z1;
 }
 #endif
 

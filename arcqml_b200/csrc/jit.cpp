@@ -137,10 +137,6 @@ uint32_t acc_lanes(bool adj, uint32_t rb) {
     if (acc_per_warp(adj, rb)) return 32u;
     return (adj && rb == 3 && adjoint_two_ctas()) ? 4u : 1u;
 }
-const char *acc_call(uint32_t rb) {
-    const uint32_t l = acc_lanes(true, rb);
-    return l == 32u ? "accumulate_warp" : l == 4u ? "accumulate_quad" : "accumulate";
-}
 
 // Compiled adjoint kernels with 3 register bits ask for two CTAs per SM (ARCQML_ADJ_2CTA=0:
 // one CTA with a column per thread; two measured 4 % faster at 30 qubits).
@@ -401,6 +397,36 @@ void set_factor(RowFactors &rf, uint32_t row, const std::string &f) {
     rf[row] = f;
 }
 
+// Where the generated code puts a gradient sum `z` of accumulator row `row`. With one column per
+// four lanes, sums are paired: the first of a pair waits in zp[0], the second triggers
+// accumulate_quad2 (one shuffle round halves the pair over lane bit 0, a second sums over bit 1);
+// a sum left unpaired at the end of a sub-block goes through accumulate_quad alone.
+struct AccSink {
+    RowFactors rf;
+    uint32_t lanes = 1;
+    int pending = -1;  // row waiting in zp[0], or -1
+};
+void emit_acc(std::ostringstream &c, AccSink &a, uint32_t row) {
+    if (a.lanes != 4u) {
+        c << (a.lanes == 32u ? "accumulate_warp" : "accumulate") << "(sacc, " << row
+          << "u * kCols, z); ";
+        return;
+    }
+    if (a.pending < 0) {
+        c << "zp[0] = z; ";
+        a.pending = int(row);
+        return;
+    }
+    c << "accumulate_quad2(sacc, zp[0], z, " << a.pending << "u * kCols, " << row
+      << "u * kCols); ";
+    a.pending = -1;
+}
+void flush_acc(std::ostringstream &c, AccSink &a) {
+    if (a.pending < 0) return;
+    c << "        accumulate_quad(sacc, " << a.pending << "u * kCols, zp[0]);\n";
+    a.pending = -1;
+}
+
 // Gradients on general bit positions (on unless ARCQML_FAST_DIAG=0), in the order of the table-driven
 // kernel: a Pauli-rotation gradient Im<lam|P|psi> on psi before U^dagger (X / Y over the
 // target pairs whose controls are set, Z with the sign of the target bit), then U^dagger on
@@ -408,7 +434,7 @@ void set_factor(RowFactors &rf, uint32_t row, const std::string &f) {
 // In a scaled pass psi and lambda carry the pass factor sigma from before the op (which keeps
 // its plain form), so each sum is multiplied by |sigma|^2 = 2 * mats[soff].y.
 bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
-                          uint32_t tbits, RowFactors &rf) {
+                          uint32_t tbits, AccSink &acc) {
     const OpBits b = op_bits(o, S, rb, tbits);
     if (!b.ok) return false;
     const bool diag = o.kind == FK_D1 || o.kind == FK_D2;
@@ -420,9 +446,9 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
     const std::string so = std::to_string(o.soff);
     // the sum goes into the row unscaled; its factor is applied once to the row's total
     auto put_acc = [&](uint32_t slot, bool pauli) {
-        c << acc_call(rb) << "(sacc, " << o.acc[slot] << "u * kCols, z); ";
-        if (pauli) set_factor(rf, o.acc[slot], o.sgrad ? "M[" + so + "].y" : "0.5");
-        else set_factor(rf, o.acc[slot], o.sgrad ? "2.0 * M[" + so + "].y" : "1.0");
+        emit_acc(c, acc, o.acc[slot]);
+        if (pauli) set_factor(acc.rf, o.acc[slot], o.sgrad ? "M[" + so + "].y" : "0.5");
+        else set_factor(acc.rf, o.acc[slot], o.sgrad ? "2.0 * M[" + so + "].y" : "1.0");
     };
     auto apply_to = [&](const char *r) {
         c << "\n        ";
@@ -551,7 +577,7 @@ bool emit_adjoint_general(std::ostringstream &c, const FOp &o, uint32_t rb, cons
 
 // Gradient then U^dagger on psi and lambda, as adj_fast does it.
 bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlock &S,
-                  uint32_t tbits, RowFactors &rf) {
+                  uint32_t tbits, AccSink &acc) {
     if (o.gkind == GK_NONE) {
         if (!emit_apply(c, o, "v", rb, S, tbits)) return false;
         c << "\n        ";
@@ -561,7 +587,7 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
                             (o.code == FC_RY && o.gcode == GF_Y) ||
                             (o.code == FC_D1_REG && o.gcode == GF_Z_REG) ||
                             (o.code == FC_D1_UNI && o.gcode == GF_Z_UNI);
-    if (!pauli_fast) return fast_diag() && emit_adjoint_general(c, o, rb, S, tbits, rf);
+    if (!pauli_fast) return fast_diag() && emit_adjoint_general(c, o, rb, S, tbits, acc);
     const int b0 = o.rb0;
     if (b0 >= int(rb) && o.code != FC_D1_UNI) return false;
     c << "{ double z; ";
@@ -580,8 +606,10 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
     c << "\n        ";
     if (!emit_apply(c, o, "w", rb, S, tbits)) return false;
     // the row's factor, applied to its total: 0.5, times |sigma|^2 in a scaled pass
-    c << "\n        " << acc_call(rb) << "(sacc, " << o.acc[0] << "u * kCols, z); }";
-    set_factor(rf, o.acc[0], o.sgrad ? "M[" + std::to_string(o.soff) + "].y" : "0.5");
+    c << "\n        ";
+    emit_acc(c, acc, o.acc[0]);
+    c << "}";
+    set_factor(acc.rf, o.acc[0], o.sgrad ? "M[" + std::to_string(o.soff) + "].y" : "0.5");
     return true;
 }
 
@@ -596,7 +624,8 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     const size_t nmats = st.mats.empty() ? 1 : st.mats.size();
     if (params && nmats * sizeof(double2) > kJitMaxParamMats) return std::string();
     if (params) c << "struct PassMats { double2 m[" << nmats << "]; };\n";
-    RowFactors rf;
+    AccSink acc;
+    acc.lanes = adj ? acc_lanes(adj, rb) : 1u;
     c << "struct PassOps {\n"
          "    static constexpr int kAccLanes = " << acc_lanes(adj, rb) << ";\n"
          "    static constexpr bool kSingleBuffer = " << (single ? "true" : "false") << ";\n"
@@ -608,6 +637,8 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "            uint32_t nthreads, uint64_t gbase) {\n"
          "        const auto &M = mats_of(MS);\n"
          "        double2 v[1 << RB], w[1 << RB];\n"
+         "        double zp[1];  // a gradient sum waiting for its pair (accumulate_quad2)\n"
+         "        (void)zp;\n"
          "        constexpr uint32_t kCols = " << cols << "u;  // accumulator row stride\n"
          "        const uint32_t tid = threadIdx.x;\n"
          "        uint32_t p;\n"
@@ -638,11 +669,12 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
         }
         for (uint32_t oi = S.op_begin; oi < S.op_end; ++oi) {
             c << "        ";
-            const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb, S, kb, rf)
+            const bool ok = adj ? emit_adjoint(c, st.ops[oi], rb, S, kb, acc)
                                 : emit_apply(c, st.ops[oi], "v", rb, S, kb);
             if (!ok) return std::string();
             c << "\n";
         }
+        flush_acc(c, acc);  // a sum left unpaired: before the registers leave the sub-block
         if (st.scaled && sb + 1 == st.subs.size()) {
             c << "        fs_scale<RB>(v, M[" << st.sfin << "]);";
             if (adj) c << " fs_scale<RB>(w, M[" << st.sfin << "]);";
@@ -663,7 +695,8 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "        const auto &M = mats_of(MS);\n"
          "        (void)M;\n"
          "        switch (a) {\n";
-    for (size_t r = 0; r < rf.size(); ++r) c << "        case " << r << ": return " << rf[r] << ";\n";
+    for (size_t r = 0; r < acc.rf.size(); ++r)
+        c << "        case " << r << ": return " << acc.rf[r] << ";\n";
     c << "        default: return 1.0;\n"
          "        }\n"
          "    }\n"
