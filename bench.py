@@ -38,10 +38,12 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# DRAM bytes per amplitude of one fused pass from ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum) on 26-qubit passes of this workload: forward 1.074 + 1.015 GB, adjoint
-# 2.148 + 2.090 GB per 2^26 amplitudes; a pass's traffic grows with the state it streams.
-NCU_DRAM_BYTES_PER_AMP = {"fused_forward": 2.088e9 / 2 ** 26, "fused_adjoint": 4.240e9 / 2 ** 26}
+# DRAM bytes per amplitude of one pass from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
+# on 26-qubit passes of this workload: forward 1.106 + 1.032 GB, adjoint 2.206 + 2.088 GB,
+# observable tile pass 2.801 + 1.030 GB per 2^26 amplitudes; a pass's traffic grows with the
+# state it streams.
+NCU_DRAM_BYTES_PER_AMP = {"fused_forward": 2.138e9 / 2 ** 26, "fused_adjoint": 4.294e9 / 2 ** 26,
+                          "observable": 3.831e9 / 2 ** 26}
 
 METRIC = "gate passes/s (32q 20-layer brickwork forward + adjoint gradient, 200-term <H>)"
 UNIT = "gate_passes/s"
