@@ -573,7 +573,7 @@ int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qu
         const bool wide = adjoint && adjoint_wide_tiles() && n >= 12;
         const uint32_t k = wide ? 12u : fused_k(n, adjoint != 0);
         Schedule sch = build_schedule(*p, n, adjoint != 0, req.data(), adjoint != 0, k,
-                                      wide ? 4u : fused_rb(k, adjoint != 0));
+                                      wide ? 4u : (adjoint ? fused_rb(k, true) : forward_rb(k)));
         size_t el = 0;
         std::string err;
         const size_t ok = jit_compile_check(sch, adjoint != 0, &el, &err);
@@ -1019,7 +1019,7 @@ int32_t arcqml_rt_v2_plan_schedule_stats(const CircuitPlanHandle *plan, size_t n
         std::vector<uint8_t> req(parents, 1);
         const uint32_t k = fused_k(uint32_t(num_qubits), adjoint != 0);
         Schedule sch = build_schedule(*p, uint32_t(num_qubits), adjoint != 0, req.data(),
-                                      adjoint != 0, k, fused_rb(k, adjoint != 0));
+                                      adjoint != 0, k, adjoint ? fused_rb(k, true) : forward_rb(k));
         *passes = sch.steps.size();
         uint64_t sb = 0, g = 0;
         for (const auto &st : sch.steps) {

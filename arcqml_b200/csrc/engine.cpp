@@ -179,7 +179,7 @@ uint32_t forward_rb(uint32_t k) {
         const char *e = std::getenv("ARCQML_FORWARD_RB");
         return e ? std::atoi(e) : 0;
     }();
-    if (k >= 12 && (forced == 3 || forced == 4)) return uint32_t(forced);
+    if (k >= 11 && (forced == 3 || forced == 4)) return uint32_t(forced);
     return fused_rb(k, false);
 }
 

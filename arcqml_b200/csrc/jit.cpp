@@ -701,11 +701,12 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "        }\n"
          "    }\n"
          "};\n";
-    const int bound = (adj || rb == 4) ? 256 : 512;
-    const int min_blocks = ((adj && (adjoint_per_warp() || adjoint_two_ctas()) && rb == 3) ||
-                            (single && threads <= 256))
-                               ? 2
-                               : 1;
+    // Kernels made for several CTAs per SM ask for 512 resident threads per SM (two CTAs of
+    // 256, four of 128), which caps them at 128 registers; the others run one CTA per SM.
+    const bool multi = (adj && (adjoint_per_warp() || adjoint_two_ctas()) && rb == 3) ||
+                       (single && threads <= 256);
+    const int bound = multi ? int(threads) : ((adj || rb == 4) ? 256 : 512);
+    const int min_blocks = multi ? int(512u / threads) : 1;
     c << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"

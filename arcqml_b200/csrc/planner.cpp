@@ -436,6 +436,22 @@ void pack_subblocks(const std::vector<PGate> &gates, const std::vector<size_t> &
 
 }  // namespace
 
+uint32_t adjoint_tile_cap() {
+    static const uint32_t cap = [] {
+        const char *e = std::getenv("ARCQML_ADJ_TILE");
+        return (e && e[0] == '1' && e[1] == '0' && !e[2]) ? 10u : 11u;
+    }();
+    return cap;
+}
+
+uint32_t forward_tile_cap() {
+    static const uint32_t cap = [] {
+        const char *e = std::getenv("ARCQML_FWD_TILE");
+        return (e && e[0] == '1' && e[1] == '1' && !e[2]) ? 11u : 12u;
+    }();
+    return cap;
+}
+
 bool fast_cnot() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_FAST_CNOT");

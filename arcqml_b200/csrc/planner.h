@@ -70,9 +70,13 @@ uint32_t fused_threads(uint32_t k, uint32_t rb);
 
 // Tile shape the engine uses for an n-qubit state: forward k = min(n, 12) with 4 register bits
 // at k = 12 (3 below), adjoint k = min(n, 11) with 3. Fused passes need n >= 8 (a full warp).
+// ARCQML_ADJ_TILE=10 caps adjoint tiles at 10 qubits (128 threads, four CTAs per SM);
+// ARCQML_FWD_TILE=11 caps forward tiles at 11 (with ARCQML_FORWARD_RB=4: 128 threads, four CTAs).
 constexpr uint32_t kFusedMinQubits = 8;
+uint32_t adjoint_tile_cap();
+uint32_t forward_tile_cap();
 inline uint32_t fused_k(uint32_t n, bool adjoint) {
-    const uint32_t cap = adjoint ? 11u : 12u;
+    const uint32_t cap = adjoint ? adjoint_tile_cap() : forward_tile_cap();
     return n < cap ? n : cap;
 }
 inline uint32_t fused_rb(uint32_t k, bool adjoint) { return (!adjoint && k >= 12) ? 4u : 3u; }
