@@ -46,6 +46,9 @@ struct TileArgs {
     const TileMember *members;
     uint32_t ngroups, nmembers;
     uint32_t read_out;              // add to the H psi already in `out`
+    // single-term groups come first, ordered by their element phase pattern h: those with h
+    // are [hbeg[h], hbeg[h + 1]); groups of several terms are [hbeg[16], ngroups)
+    uint32_t hbeg[17];
 };
 
 __device__ __forceinline__ uint32_t tphys(uint32_t j) {
@@ -164,20 +167,19 @@ __global__ void __launch_bounds__(kTileThreads, 2)
                 ev -= fma(pi.x, acc[i].x, pi.y * acc[i].y);
             }
         }
-        for (uint32_t gi = 0; gi < P.ngroups; ++gi) {
+        // single-term groups: one loop per element phase pattern, its signs in the code
+#define ARCQML_LOOP(H)                                                                     \
+        _Pragma("unroll 1")                                                                \
+        for (uint32_t gi = P.hbeg[H]; gi < P.hbeg[H + 1]; ++gi) {                          \
+            const uint4 G = sg[gi];                                                        \
+            add_group<H>(acc, tile, ptid ^ G.x, member_weight(smem_m[G.y], base, tid));   \
+        }
+        ARCQML_H16(ARCQML_LOOP)
+#undef ARCQML_LOOP
+        for (uint32_t gi = P.hbeg[16]; gi < P.ngroups; ++gi) {
             const uint4 G = sg[gi];
             const uint32_t x = ptid ^ G.x;
-            if (G.z - G.y == 1) {
-                const TileMember &m = smem_m[G.y];
-                const double2 w = member_weight(m, base, tid);
-                switch (m.h) {
-#define ARCQML_CASE(H) \
-                case H: add_group<H>(acc, tile, x, w); break;
-                    ARCQML_H16(ARCQML_CASE)
-#undef ARCQML_CASE
-                default: break;
-                }
-            } else {
+            {
                 // several terms share the flip mask: per element the sum of their signed
                 // weights, in two halves of eight elements (registers)
 #pragma unroll
@@ -359,13 +361,27 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
     }
     std::vector<double2> blob((total + 15) / 16 + 1);
     char *hb = reinterpret_cast<char *>(blob.data());
+    std::vector<std::vector<uint32_t>> hbeg(passes.size());
     for (size_t p = 0; p < passes.size(); ++p) {
         const uint8_t *S = passes[p].S;
         uint4 *gs = reinterpret_cast<uint4 *>(hb + goff[p]);
         TileMember *ms = reinterpret_cast<TileMember *>(hb + moff[p]);
-        uint32_t mi = 0;
-        for (size_t gi = 0; gi < passes[p].groups.size(); ++gi) {
+        // order: single-term groups by the element phase pattern of their term, then the others
+        std::vector<uint32_t> order(passes[p].groups.size());
+        for (uint32_t gi = 0; gi < order.size(); ++gi) order[gi] = gi;
+        auto key = [&](uint32_t gi) {
             const PauliGroup &grp = obs.groups[passes[p].groups[gi]];
+            return grp.count == 1 ? compress(obs.zmask[grp.first], S) >> 8 : 16u;
+        };
+        std::stable_sort(order.begin(), order.end(),
+                         [&](uint32_t a, uint32_t b) { return key(a) < key(b); });
+        hbeg[p].assign(17, uint32_t(order.size()));
+        for (uint32_t i = order.size(); i-- > 0;) hbeg[p][key(order[i])] = i;
+        for (uint32_t h = 16; h-- > 0;) hbeg[p][h] = std::min(hbeg[p][h], hbeg[p][h + 1]);
+        uint32_t mi = 0;
+        for (size_t oi = 0; oi < order.size(); ++oi) {
+            const size_t gi = oi;
+            const PauliGroup &grp = obs.groups[passes[p].groups[order[oi]]];
             gs[gi] = make_uint4(host_phys(compress(grp.flip, S)), mi, mi + grp.count, 0u);
             for (uint32_t k = grp.first; k < grp.first + grp.count; ++k, ++mi) {
                 TileMember &m = ms[mi];
@@ -411,6 +427,7 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
         a.ngroups = uint32_t(passes[p].groups.size());
         a.nmembers = nmem[p];
         a.read_out = (out && (p > 0 || accumulate)) ? 1u : 0u;
+        for (uint32_t h = 0; h < 17; ++h) a.hbeg[h] = hbeg[p][h];
         const size_t smem = (16u << kTileQ) + (8u << (kTileQ - kTileLow)) +
                             a.ngroups * sizeof(uint4) + size_t(a.nmembers) * sizeof(TileMember);
         // algorithmic traffic of the pass: psi read, H psi written (and read back after pass 0)
