@@ -701,12 +701,17 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "        }\n"
          "    }\n"
          "};\n";
-    // Kernels made for several CTAs per SM ask for 512 resident threads per SM (two CTAs of
-    // 256, four of 128), which caps them at 128 registers; the others run one CTA per SM.
-    const bool multi = (adj && (adjoint_per_warp() || adjoint_two_ctas()) && rb == 3) ||
-                       (single && threads <= 256);
+    // Kernels made for several CTAs per SM ask for that many resident CTAs: adjoint kernels
+    // 512 resident threads per SM (two CTAs of 256, four of 128: 128 registers); forward kernels
+    // two CTAs of 256 threads, and 1024 threads per SM in smaller CTAs (64 registers: the
+    // small-state forward passes, e.g. the batched QNN's rows, run faster with more warps than
+    // with more registers). The others run one CTA per SM.
+    const bool multi_adj = adj && (adjoint_per_warp() || adjoint_two_ctas()) && rb == 3;
+    const bool multi_fwd = single && threads <= 256;
+    const uint32_t per_sm = multi_adj ? 512u : (threads >= 256 ? 512u : 1024u);
+    const bool multi = multi_adj || multi_fwd;
     const int bound = multi ? int(threads) : ((adj || rb == 4) ? 256 : 512);
-    const int min_blocks = multi ? int(512u / threads) : 1;
+    const int min_blocks = multi ? int(per_sm / threads) : 1;
     c << "extern \"C\" __global__ void __launch_bounds__(" << bound << ", " << min_blocks << ")\n"
          "arcqml_pass(double2 *__restrict__ psi, double2 *__restrict__ lam, uint32_t n,\n"
          "            uint32_t tiles_log, uint64_t total_tiles, const PassHeader *__restrict__ hdr,\n"
