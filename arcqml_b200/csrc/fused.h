@@ -102,6 +102,7 @@ struct SubBlock {
 };
 constexpr uint32_t SB_ALL_FAST = 1;  // the table-driven kernel has a fast path for every op
 constexpr uint32_t SB_JIT_FAST = 2;  // the run-time compiled kernels have one for every op
+constexpr uint32_t SB_WARP_NEXT = 4; // the next sub-block keeps every element in the same warp
 static_assert(sizeof(SubBlock) == 24, "SubBlock layout");
 
 struct PassHeader {

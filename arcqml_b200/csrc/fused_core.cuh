@@ -604,7 +604,9 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
             else
                 Runner::template run<RB, ADJ>(sb, k, tp, tl, ops, gmats, subs, sacc, nthreads,
                                               gbase);
-            __syncthreads();
+            // the next sub-block reads only elements this warp wrote: the warp's own barrier
+            if (Runner::warp_next(sb)) __syncwarp();
+            else __syncthreads();
         }
         const uint64_t off = ((T >> tiles_log) << n) + gbase;
         double2 *P = psi + off;

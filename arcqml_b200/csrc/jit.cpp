@@ -689,6 +689,15 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     }
     c << "        }\n"
          "    }\n";
+    // sub-blocks whose successor keeps every element in the same warp
+    c << "    __device__ static __forceinline__ bool warp_next(uint32_t sb) {\n"
+         "        switch (sb) {\n";
+    for (size_t sb = 0; sb < st.subs.size(); ++sb)
+        if (st.subs[sb].flags & SB_WARP_NEXT) c << "        case " << sb << ":\n";
+    c << "            return true;\n"
+         "        default: return false;\n"
+         "        }\n"
+         "    }\n";
     // factors of the accumulator rows (adjoint), applied to each row's total
     c << "    template <class MT>\n"
          "    __device__ static __forceinline__ double row_factor(uint32_t a, const MT &MS) {\n"

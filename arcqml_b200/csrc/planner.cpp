@@ -355,6 +355,58 @@ bool has_jit_fast_path(const FOp &o, bool adjoint) {
 // Residue of a tile bit under the shared-memory swizzle (fold of 3-bit groups).
 inline int residue(int bit) { return bit % 3; }
 
+// Whether `lanes` (a tile-bit mask) holds bits of all three swizzle residues (lane bits 0-2 then
+// hit distinct 16-byte bank groups: conflict-free 128-bit shared-memory accesses).
+bool all_residues(uint32_t lanes) {
+    bool seen[3] = {false, false, false};
+    for (int b = 0; b < 32; ++b)
+        if ((lanes >> b) & 1u) seen[residue(b)] = true;
+    return seen[0] && seen[1] && seen[2];
+}
+
+// Splits a pass's sub-blocks (register-bit masks R over k tile bits) into runs of consecutive
+// sub-blocks that share one set W of warp bits (k - rb - 5 tile bits outside every R of the
+// run, chosen so that each sub-block's lane bits keep all three residues). runW[sb] = W (0: the
+// sub-block is alone), warp_next[sb]: the next sub-block is in the same run.
+void plan_warp_runs(const std::vector<uint32_t> &R, uint32_t k, uint32_t rb,
+                    std::vector<uint32_t> &runW, std::vector<bool> &warp_next) {
+    const uint32_t tbits = k - rb;
+    if (tbits <= 5) return;
+    const uint32_t wbits = tbits - 5;
+    const uint32_t all = (k >= 32) ? 0xffffffffu : ((1u << k) - 1);
+    // a warp-bit set valid for sub-blocks [a, b], or 0
+    auto pick = [&](size_t a, size_t b) -> uint32_t {
+        uint32_t uni = 0;
+        for (size_t i = a; i <= b; ++i) uni |= R[i];
+        const uint32_t free = all & ~uni;
+        if (uint32_t(__builtin_popcount(free)) < wbits) return 0u;
+        // smallest subsets first: enumerate wbits-subsets of `free` in increasing order
+        for (uint32_t m = free; m; m = (m - 1) & free) {
+            if (uint32_t(__builtin_popcount(m)) != wbits) continue;
+            bool ok = true;
+            for (size_t i = a; i <= b && ok; ++i) ok = all_residues(all & ~R[i] & ~m);
+            if (ok) return m;
+        }
+        return 0u;
+    };
+    size_t a = 0;
+    while (a < R.size()) {
+        size_t b = a;
+        uint32_t W = pick(a, a);
+        while (W && b + 1 < R.size()) {
+            const uint32_t W2 = pick(a, b + 1);
+            if (!W2) break;
+            W = W2;
+            ++b;
+        }
+        if (W && b > a) {
+            for (size_t i = a; i <= b; ++i) runW[i] = W;
+            for (size_t i = a; i < b; ++i) warp_next[i] = true;
+        }
+        a = b + 1;
+    }
+}
+
 }  // namespace
 
 bool scaled_passes() {
@@ -450,6 +502,14 @@ uint32_t forward_tile_cap() {
         return (e && e[0] == '1' && e[1] == '1' && !e[2]) ? 11u : 12u;
     }();
     return cap;
+}
+
+bool warp_local_exchanges() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_WARP_LOCAL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 bool fast_cnot() {
@@ -583,20 +643,36 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 sub_R.push_back(R);
             }
         }
-        // --- emit sub-blocks, ops and matrices
+        // --- register bits of each sub-block, padded to exactly rb
+        std::vector<uint32_t> padR(subs.size());
         for (size_t sb = 0; sb < subs.size(); ++sb) {
             uint32_t R = sub_R[sb];
             for (int b = int(k) - 1; b >= 0 && uint32_t(__builtin_popcount(R)) < rb; --b)
-                R |= 1u << b;  // pad to exactly rb register bits
+                R |= 1u << b;
+            padR[sb] = R;
+        }
+        // --- warp-local runs: consecutive sub-blocks that leave the same tile bits free for the
+        // warp bits (thread bits 5 and up) hold every element in the same warp throughout, so
+        // the exchanges between them need only __syncwarp
+        std::vector<uint32_t> runW(subs.size(), 0);
+        std::vector<bool> warp_next(subs.size(), false);
+        if (warp_local_exchanges())
+            plan_warp_runs(padR, k, rb, runW, warp_next);
+        // --- emit sub-blocks, ops and matrices
+        for (size_t sb = 0; sb < subs.size(); ++sb) {
+            const uint32_t R = padR[sb];
             SubBlock s;
             std::memset(&s, 0, sizeof(s));
             int ri = 0;
             for (uint32_t b = 0; b < k; ++b)
                 if ((R >> b) & 1) s.R[ri++] = uint8_t(b);
-            // thread bits: three lane bits with distinct swizzle residues first, then the rest
+            if (warp_next[sb]) s.flags |= SB_WARP_NEXT;
+            // thread bits: three lane bits with distinct swizzle residues first, then the rest;
+            // in a warp-local run the run's warp bits come last, in the same order every time
+            const uint32_t W = runW[sb];
             std::vector<int> rest;
             for (uint32_t b = 0; b < k; ++b)
-                if (!((R >> b) & 1)) rest.push_back(int(b));
+                if (!((R >> b) & 1) && !((W >> b) & 1)) rest.push_back(int(b));
             std::vector<int> order;
             bool used_res[3] = {false, false, false};
             for (int want = 0; want < 3; ++want)
@@ -610,6 +686,8 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 }
             for (int b : rest)
                 if (b >= 0) order.push_back(b);
+            for (uint32_t b = 0; b < k; ++b)
+                if ((W >> b) & 1) order.push_back(int(b));
             for (size_t i = 0; i < order.size(); ++i) s.perm[i] = uint8_t(order[i]);
             s.op_begin = uint16_t(st.ops.size());
             auto reg_of = [&](uint32_t q) -> uint8_t {
@@ -738,7 +816,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 st.ops.push_back(o);
             }
             s.op_end = uint16_t(st.ops.size());
-            s.flags = SB_ALL_FAST | SB_JIT_FAST;
+            s.flags |= SB_ALL_FAST | SB_JIT_FAST;
             for (size_t oi = s.op_begin; oi < s.op_end; ++oi) {
                 if (!has_fast_path(st.ops[oi], adjoint)) s.flags &= ~SB_ALL_FAST;
                 if (!has_jit_fast_path(st.ops[oi], adjoint)) s.flags &= ~SB_JIT_FAST;

@@ -42,6 +42,10 @@ bool fast_cnot();
 // controlled one-target gates and generic slot gradients (on unless ARCQML_FAST_DIAG=0).
 bool fast_diag();
 
+// Whether consecutive sub-blocks that can keep every element in the same warp do so and
+// exchange with __syncwarp instead of a CTA barrier (on unless ARCQML_WARP_LOCAL=0).
+bool warp_local_exchanges();
+
 // Whether passes pack commuting gates into fewer register sub-blocks than circuit order gives
 // (on unless ARCQML_SUBBLOCK_REORDER=0).
 bool subblock_reorder();
