@@ -1,5 +1,6 @@
 """Run-time compiled pass kernels on CPU: the generated sources of a forward and an adjoint
 schedule compile for sm_100a with NVRTC (no GPU needed)."""
+import numpy as np
 import pytest
 
 from arcqml_b200 import workloads
@@ -128,3 +129,49 @@ def test_default_pass_code_is_pinned():
     with open(pass_code_pins.PINS) as f:
         pinned = json.load(f)
     assert pass_code_pins.digests() == pinned
+
+
+def warp_local_layouts(runtime, c, n, adjoint):
+    """(sub-blocks, warp-local exchanges) of the plan's schedule, checking every warp-local pair:
+    the same warp bits (thread bits 5 and up, same tile bits in the same order), outside both
+    sub-blocks' register bits, and lane bits holding all three swizzle residues."""
+    import struct
+
+    import jit_host_run as J
+    ops = c.compile_plan(1)
+    req = np.asarray(c.requires_grad_mask(True), np.uint8) if adjoint else None
+    plan = runtime.CircuitPlan.create(ops)
+    steps = J.parse(runtime.plan_schedule_export(plan, n, adjoint, req))
+    nsub = nwarp = 0
+    for kind, p in steps:
+        if kind != "pass":
+            continue
+        k, _, _, _, _, _, rb = struct.unpack_from("<7I", p.header, 0)
+        tbits = k - rb
+        subs = []
+        for i in range(len(p.subs) // 24):
+            b = p.subs[24 * i:24 * (i + 1)]
+            R = set(b[:rb])
+            perm = list(b[4:4 + tbits])
+            flags = struct.unpack_from("<I", b, 20)[0]
+            subs.append((R, perm, flags))
+        nsub += len(subs)
+        for i, (R, perm, flags) in enumerate(subs):
+            assert sorted(set(perm) | R) == list(range(k))  # a permutation of the tile bits
+            assert len({q % 3 for q in perm[:3]}) == 3 or tbits < 3
+            if not flags & 4:
+                continue
+            assert i + 1 < len(subs), "the last sub-block of a pass must end with a CTA barrier"
+            R2, perm2, _ = subs[i + 1]
+            assert perm[5:] == perm2[5:] and not (set(perm[5:]) & (R | R2))
+            nwarp += 1
+    return nsub, nwarp
+
+
+def test_warp_local_exchanges_keep_elements_in_their_warp(runtime):
+    for n, layers, adjoint in ((32, 20, False), (32, 20, True), (20, 6, True), (14, 5, False)):
+        c = workloads.brickwork(n, layers, seed=1234)
+        nsub, nwarp = warp_local_layouts(runtime, c, n, adjoint)
+        assert nsub > 0
+        if n == 32:
+            assert nwarp >= nsub // 3, (nsub, nwarp)
