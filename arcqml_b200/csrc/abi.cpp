@@ -789,6 +789,11 @@ int32_t arcqml_rt_v2_plan_schedule_export(const CircuitPlanHandle *plan, size_t 
                 const uint64_t x = pa;
                 put(&x, 8);
             }
+            put32(st.alias.size());
+            for (const auto &al : st.alias) {
+                const uint64_t x[2] = {al.first, al.second};
+                put(x, 16);
+            }
             const std::string code = jit_pass_code(st, adjoint != 0);
             put32(code.size());
             put(code.data(), code.size());

@@ -244,6 +244,7 @@ void run_step(const Step &st, bool adjoint, Emu &E, const uint8_t *req, double *
             for (auto &x : *E.lam) x *= sigma;
     }
     for (size_t a = 0; a < acc.size(); ++a) grads[st.parents[a]] += 2.0 * acc[a];
+    for (const auto &al : st.alias) grads[al.second] += 2.0 * acc[al.first];
 }
 
 }  // namespace

@@ -287,8 +287,10 @@ void adjoint_backward_device(Plan &plan, double2 *psi, double2 *lam, size_t batc
                        "cudaMemcpyAsync (gradients)");
             check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
             size_t a = 0;
-            for (const auto &st : sch.steps)
+            for (const auto &st : sch.steps) {
+                for (const auto &al : st.alias) grads_host[al.second] += 2.0 * h[a + al.first];
                 for (size_t p : st.parents) grads_host[p] += 2.0 * h[a++];
+            }
         }
         return;
     }

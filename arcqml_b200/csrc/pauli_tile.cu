@@ -10,8 +10,9 @@
 // w * (-1)^popc(t & z) * psi[t ^ f] over the pass's
 // groups for each of its amplitudes t, and writes (or adds to) H psi. Passes after the first
 // read H psi back, so one evaluation moves 32 + 48 (passes - 1) bytes per amplitude instead of
-// gathering psi once per distinct flip mask. Each pass also sums Re(conj(psi_t) * its
-// contribution); the sum over passes is <psi|H|psi>.
+// gathering psi once per distinct flip mask. The last pass, which holds the whole H psi, sums
+// Re(conj(psi_t) (H psi)_t) = <psi|H|psi>; without an output every pass sums its own
+// contribution.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -46,9 +47,14 @@ struct TileArgs {
     const TileMember *members;
     uint32_t ngroups, nmembers;
     uint32_t read_out;              // add to the H psi already in `out`
-    // single-term groups come first, ordered by their element phase pattern h: those with h
-    // are [hbeg[h], hbeg[h + 1]); groups of several terms are [hbeg[16], ngroups)
-    uint32_t hbeg[17];
+    // expectation terms of this pass: ev_sub subtracts <psi|out before the pass> (the first pass
+    // that adds to an existing H psi), ev_add adds <psi|out after the pass> (every pass without
+    // an output, else the last one: its H psi is the whole sum)
+    uint32_t ev_sub, ev_add;
+    // single-term groups come first, ordered by key 2 h + (weight imaginary), h their element
+    // phase pattern: those of key k are [hbeg[k], hbeg[k + 1]); groups of several terms are
+    // [hbeg[32], ngroups)
+    uint32_t hbeg[33];
 };
 
 __device__ __forceinline__ uint32_t tphys(uint32_t j) {
@@ -73,15 +79,26 @@ __device__ __forceinline__ void cp_async16t(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(a), "l"(gmem) : "memory");
 }
 
-// acc[i] += (-1)^parity(i & H) * w * psi[partner of element i]: the element signs are constants
-// of the code (one instantiation per phase pattern H on the element bits).
-template <uint32_t H>
+// acc[i] += (-1)^parity(i & H) * w * psi[partner of element i] for the weight w of one term,
+// real (IM false: w = (c, 0)) or imaginary (IM: w = (0, c)), so two FMAs per element: the
+// element signs are constants of the code (one instantiation per phase pattern H on the element
+// bits and kind of weight).
+template <uint32_t H, bool IM>
 __device__ __forceinline__ void add_group(double2 (&acc)[16], const double2 *tile, uint32_t x,
-                                          double2 w) {
-    const double2 wn = tneg(w);
+                                          double c) {
+    const double cn = -c;
 #pragma unroll
-    for (uint32_t i = 0; i < 16; ++i)
-        acc[i] = tcfma(cparity(i & H) ? wn : w, tile[x ^ tphys(i << 8)], acc[i]);
+    for (uint32_t i = 0; i < 16; ++i) {
+        const double s = cparity(i & H) ? cn : c;
+        const double2 p = tile[x ^ tphys(i << 8)];
+        if (IM) {
+            acc[i].x = fma(-s, p.y, acc[i].x);
+            acc[i].y = fma(s, p.x, acc[i].y);
+        } else {
+            acc[i].x = fma(s, p.x, acc[i].x);
+            acc[i].y = fma(s, p.y, acc[i].y);
+        }
+    }
 }
 
 // wi[i] += (-1)^parity((i0 + i) & H) * w for elements i0..i0+7 (a group of several terms)
@@ -159,8 +176,7 @@ __global__ void __launch_bounds__(kTileThreads, 2)
         }
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncthreads();
-        // <psi|contribution> = <psi|acc after> - <psi|acc before>
-        if (rd) {
+        if (P.ev_sub) {
 #pragma unroll
             for (uint32_t i = 0; i < 16; ++i) {
                 const double2 pi = tile[ptid ^ tphys(i << 8)];
@@ -170,13 +186,20 @@ __global__ void __launch_bounds__(kTileThreads, 2)
         // single-term groups: one loop per element phase pattern, its signs in the code
 #define ARCQML_LOOP(H)                                                                     \
         _Pragma("unroll 1")                                                                \
-        for (uint32_t gi = P.hbeg[H]; gi < P.hbeg[H + 1]; ++gi) {                          \
+        for (uint32_t gi = P.hbeg[2 * H]; gi < P.hbeg[2 * H + 1]; ++gi) {                  \
             const uint4 G = sg[gi];                                                        \
-            add_group<H>(acc, tile, ptid ^ G.x, member_weight(smem_m[G.y], base, tid));   \
+            add_group<H, false>(acc, tile, ptid ^ G.x,                                     \
+                                member_weight(smem_m[G.y], base, tid).x);                  \
+        }                                                                                  \
+        _Pragma("unroll 1")                                                                \
+        for (uint32_t gi = P.hbeg[2 * H + 1]; gi < P.hbeg[2 * H + 2]; ++gi) {              \
+            const uint4 G = sg[gi];                                                        \
+            add_group<H, true>(acc, tile, ptid ^ G.x,                                      \
+                               member_weight(smem_m[G.y], base, tid).y);                   \
         }
         ARCQML_H16(ARCQML_LOOP)
 #undef ARCQML_LOOP
-        for (uint32_t gi = P.hbeg[16]; gi < P.ngroups; ++gi) {
+        for (uint32_t gi = P.hbeg[32]; gi < P.ngroups; ++gi) {
             const uint4 G = sg[gi];
             const uint32_t x = ptid ^ G.x;
             {
@@ -216,11 +239,16 @@ __global__ void __launch_bounds__(kTileThreads, 2)
                 }
             }
         }
+        if (P.ev_add) {
 #pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) {
-            const double2 pi = tile[ptid ^ tphys(i << 8)];
-            ev += fma(pi.x, acc[i].x, pi.y * acc[i].y);
-            if (out) out[base + elem_off(i)] = acc[i];
+            for (uint32_t i = 0; i < 16; ++i) {
+                const double2 pi = tile[ptid ^ tphys(i << 8)];
+                ev += fma(pi.x, acc[i].x, pi.y * acc[i].y);
+            }
+        }
+        if (out) {
+#pragma unroll
+            for (uint32_t i = 0; i < 16; ++i) out[base + elem_off(i)] = acc[i];
         }
         __syncthreads();  // the tile is overwritten by the next iteration
     }
@@ -366,18 +394,21 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
         const uint8_t *S = passes[p].S;
         uint4 *gs = reinterpret_cast<uint4 *>(hb + goff[p]);
         TileMember *ms = reinterpret_cast<TileMember *>(hb + moff[p]);
-        // order: single-term groups by the element phase pattern of their term, then the others
+        // order: single-term groups by the element phase pattern of their term and whether its
+        // weight i^y c is imaginary, then the others
         std::vector<uint32_t> order(passes[p].groups.size());
         for (uint32_t gi = 0; gi < order.size(); ++gi) order[gi] = gi;
         auto key = [&](uint32_t gi) {
             const PauliGroup &grp = obs.groups[passes[p].groups[gi]];
-            return grp.count == 1 ? compress(obs.zmask[grp.first], S) >> 8 : 16u;
+            if (grp.count != 1) return 32u;
+            const uint32_t k = grp.first;
+            return 2u * (compress(obs.zmask[k], S) >> 8) + (obs.ymod4[k] & 1u);
         };
         std::stable_sort(order.begin(), order.end(),
                          [&](uint32_t a, uint32_t b) { return key(a) < key(b); });
-        hbeg[p].assign(17, uint32_t(order.size()));
+        hbeg[p].assign(33, uint32_t(order.size()));
         for (uint32_t i = order.size(); i-- > 0;) hbeg[p][key(order[i])] = i;
-        for (uint32_t h = 16; h-- > 0;) hbeg[p][h] = std::min(hbeg[p][h], hbeg[p][h + 1]);
+        for (uint32_t h = 32; h-- > 0;) hbeg[p][h] = std::min(hbeg[p][h], hbeg[p][h + 1]);
         uint32_t mi = 0;
         for (size_t oi = 0; oi < order.size(); ++oi) {
             const size_t gi = oi;
@@ -427,7 +458,9 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
         a.ngroups = uint32_t(passes[p].groups.size());
         a.nmembers = nmem[p];
         a.read_out = (out && (p > 0 || accumulate)) ? 1u : 0u;
-        for (uint32_t h = 0; h < 17; ++h) a.hbeg[h] = hbeg[p][h];
+        a.ev_sub = (out && p == 0 && accumulate) ? 1u : 0u;
+        a.ev_add = (!out || p + 1 == passes.size()) ? 1u : 0u;
+        for (uint32_t h = 0; h < 33; ++h) a.hbeg[h] = hbeg[p][h];
         const size_t smem = (16u << kTileQ) + (8u << (kTileQ - kTileLow)) +
                             a.ngroups * sizeof(uint4) + size_t(a.nmembers) * sizeof(TileMember);
         // algorithmic traffic of the pass: psi read, H psi written (and read back after pass 0)

@@ -536,6 +536,62 @@ bool subblock_reorder() {
     return on;
 }
 
+bool adjoint_merge() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_ADJ_MERGE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+namespace {
+
+// Adjoint passes merge a Pauli rotation exp(-i a P / 2) into the previous rotation about the
+// same axis on its qubit when nothing in between fails to commute with P: one rotation by the
+// summed angle on psi and lambda, and one gradient sum for both parameters. Both are exact:
+// the rotations commute with P, so <lam|P|psi> is the same on either side of one of them (the
+// gradient of each is that sum), and moving the later rotation back past gates that commute
+// with it changes neither the states nor their gradients. Between two RX or RY rotations no
+// gate may touch the qubit; between two RZ rotations gates acting diagonally on it (diagonal
+// gates, controls) may stand.
+//
+// The axis (ARCQML_OP_RX/RY/RZ) of a gate that can take part in such a merge, else 0.
+uint32_t merge_axis(const PGate &g) {
+    if (g.noop || g.dense_barrier || !g.controls.empty() || g.targets.size() != 1) return 0;
+    if (g.parents.size() > 1 || g.gkind == GK_GENERIC || g.m.size() != 4) return 0;
+    const uint32_t o = g.op->opcode;
+    if (o == ARCQML_OP_RZ) return g.diag ? o : 0;
+    if (o == ARCQML_OP_RX) return rotation_form(g.m.data()) == FK_RX ? o : 0;
+    if (o == ARCQML_OP_RY) return rotation_form(g.m.data()) == FK_RY ? o : 0;
+    return 0;
+}
+
+// Per qubit, the axis of the rotation later rotations may merge into (0: none).
+struct MergeChain {
+    uint32_t axis = 0;
+    int op = -1;       // its op in the pass (emission)
+    bool row = false;  // it has a gradient row (member selection)
+};
+
+// A gate g that is not merged ends the chains it does not commute with.
+void end_chains(MergeChain *chain, const PGate &g) {
+    for (uint32_t q = 0; q < 64; ++q) {
+        if (!((g.touched >> q) & 1) || chain[q].axis == 0) continue;
+        if (chain[q].axis == ARCQML_OP_RZ && !((g.needs >> q) & 1)) continue;
+        chain[q] = MergeChain{};
+    }
+}
+
+uint8_t pauli_grad_code(const FOp &o) {
+    if (o.lcmask != 0 || o.gcmask != 0) return GF_GENERIC;
+    if (o.gkind == GK_PX) return GF_X;
+    if (o.gkind == GK_PY) return GF_Y;
+    if (o.gkind == GK_PZ) return o.code == FC_D1_REG ? GF_Z_REG : GF_Z_UNI;
+    return GF_GENERIC;
+}
+
+}  // namespace
+
 Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_t *req,
                         bool grads, uint32_t k, uint32_t rb) {
     Schedule sch;
@@ -557,6 +613,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
     for (size_t i = 0; i < gates.size(); ++i) done[i] = gates[i].noop ? 1 : 0;
     size_t first = 0;
     uint32_t acc_total = 0;
+    const bool merge_adj = adjoint && adjoint_merge();
     while (true) {
         while (first < gates.size() && done[first]) ++first;
         if (first >= gates.size()) break;
@@ -575,10 +632,14 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         std::vector<size_t> members;
         size_t pass_acc = 0;
         size_t pass_mats = 0;
+        MergeChain chain[64];  // the merges the emission below makes, for the row count
         for (size_t i = first; i < gates.size(); ++i) {
             if (done[i]) continue;
             const PGate &g = gates[i];
-            if (pass_acc + g.parents.size() > size_t(kMaxPassAcc)) break;
+            const uint32_t ax = merge_adj ? merge_axis(g) : 0;
+            const bool merges = ax != 0 && chain[g.targets[0]].axis == ax;
+            const size_t rows = (merges && chain[g.targets[0]].row) ? 0 : g.parents.size();
+            if (pass_acc + rows > size_t(kMaxPassAcc)) break;
             if (pass_mats + mat_entries(g) > size_t(kMaxPassMats)) break;
             if (g.dense_barrier || (g.touched & blocked)) {
                 blocked |= g.touched;
@@ -590,8 +651,14 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 S |= extra;
                 free_slots -= cnt;
                 members.push_back(i);
-                pass_acc += g.parents.size();
+                pass_acc += rows;
                 pass_mats += mat_entries(g);
+                if (merges) {
+                    chain[g.targets[0]].row = chain[g.targets[0]].row || !g.parents.empty();
+                } else if (merge_adj) {
+                    end_chains(chain, g);
+                    if (ax) chain[g.targets[0]] = MergeChain{ax, -1, !g.parents.empty()};
+                }
                 if (members.size() >= pass_op_cap()) break;
             } else {
                 blocked |= g.touched;
@@ -659,6 +726,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         if (warp_local_exchanges())
             plan_warp_runs(padR, k, rb, runW, warp_next);
         // --- emit sub-blocks, ops and matrices
+        MergeChain echain[64];  // adjoint rotation merges (over the whole pass)
         for (size_t sb = 0; sb < subs.size(); ++sb) {
             const uint32_t R = padR[sb];
             SubBlock s;
@@ -704,6 +772,37 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
             for (int q = 0; q < 64; ++q) last1q[q] = -1;
             for (size_t gi : subs[sb]) {
                 const PGate &g = gates[gi];
+                const uint32_t ax = merge_adj ? merge_axis(g) : 0;
+                if (ax && echain[g.targets[0]].axis == ax) {
+                    FOp &e = st.ops[size_t(echain[g.targets[0]].op)];
+                    double2 ue[4], un[4], p[4];
+                    op_matrix2(e, st.mats, ue);
+                    for (int i = 0; i < 4; ++i) un[i] = g.m[i];
+                    mul2(un, ue, p);  // the earlier rotation acts first
+                    e.moff = uint32_t(st.mats.size());
+                    if (e.kind == FK_D1) {
+                        if (p[1].x != 0 || p[1].y != 0 || p[2].x != 0 || p[2].y != 0)
+                            fail("internal: merged diagonal rotation is not diagonal");
+                        st.mats.push_back(p[0]);
+                        st.mats.push_back(p[3]);
+                    } else {
+                        if (rotation_form(p) != e.kind) fail("internal: merged rotation lost its form");
+                        st.mats.push_back(make_double2(p[0].x, e.kind == FK_RX ? -p[1].y : p[2].x));
+                    }
+                    if (!g.parents.empty()) {
+                        if (e.gkind != GK_NONE) {
+                            st.alias.push_back({e.acc[0], g.parents[0]});
+                        } else {
+                            e.gkind = g.gkind;
+                            e.gcode = pauli_grad_code(e);
+                            e.nslots = 1;
+                            e.acc[0] = uint32_t(st.parents.size());
+                            st.parents.push_back(g.parents[0]);
+                        }
+                    }
+                    continue;
+                }
+                if (merge_adj) end_chains(echain, g);
                 const bool mergeable = !adjoint && g.controls.empty() && g.targets.size() == 1 &&
                                        g.gkind == GK_NONE;
                 bool merge = mergeable && last1q[g.targets[0]] >= 0;
@@ -790,12 +889,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 classify(o, g, reg_of, lpos);
                 o.gkind = g.gkind;
                 if (g.gkind != GK_NONE) {
-                    const bool plain = o.lcmask == 0 && o.gcmask == 0;
-                    o.gcode = GF_GENERIC;
-                    if (plain && g.gkind == GK_PX) o.gcode = GF_X;
-                    if (plain && g.gkind == GK_PY) o.gcode = GF_Y;
-                    if (plain && g.gkind == GK_PZ)
-                        o.gcode = o.code == FC_D1_REG ? GF_Z_REG : GF_Z_UNI;
+                    o.gcode = pauli_grad_code(o);
                     o.nslots = uint16_t(g.parents.size());
                     if (g.gkind == GK_GENERIC) {
                         // a diagonal gate's derivative is diagonal: store its diagonal only,
@@ -813,15 +907,19 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                         st.parents.push_back(g.parents[s2]);
                     }
                 }
+                if (ax) echain[g.targets[0]] = MergeChain{ax, int(st.ops.size()), false};
                 st.ops.push_back(o);
             }
             s.op_end = uint16_t(st.ops.size());
+            st.subs.push_back(s);
+        }
+        // fast-path flags once every op is final (a merge can give an earlier op a gradient)
+        for (SubBlock &s : st.subs) {
             s.flags |= SB_ALL_FAST | SB_JIT_FAST;
             for (size_t oi = s.op_begin; oi < s.op_end; ++oi) {
                 if (!has_fast_path(st.ops[oi], adjoint)) s.flags &= ~SB_ALL_FAST;
                 if (!has_jit_fast_path(st.ops[oi], adjoint)) s.flags &= ~SB_JIT_FAST;
             }
-            st.subs.push_back(s);
         }
         scale_pass(st, adjoint);
         h.nsub = uint32_t(st.subs.size());

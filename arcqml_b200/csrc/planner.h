@@ -1,6 +1,7 @@
 // planner.h — fused-pass schedules built from a plan (host side).
 #pragma once
 
+#include <utility>
 #include <vector>
 
 #include "fused.h"
@@ -16,6 +17,9 @@ struct Step {
     std::vector<FOp> ops;
     std::vector<double2> mats;
     std::vector<size_t> parents;         // per accumulator of the pass (adjoint)
+    // (accumulator, parent): further parents that receive an accumulator's gradient (rotations
+    // merged into the rotation that owns the accumulator)
+    std::vector<std::pair<uint32_t, size_t>> alias;
     // Scaled pass (compiled kernels only): the state in the tile carries a common factor sigma,
     // true = sigma * stored, multiplied in once at the end from mats[sfin].
     bool scaled = false;
@@ -37,6 +41,10 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
 // Whether X and single-control CNOT gates on register bits use their register-exchange fast
 // paths (on unless ARCQML_FAST_CNOT=0) instead of a dense 2x2 / the generic path.
 bool fast_cnot();
+
+// Whether adjoint passes merge a Pauli rotation into the previous rotation about the same axis
+// on its qubit (on unless ARCQML_ADJ_MERGE=0).
+bool adjoint_merge();
 
 // Whether the run-time compiled kernels run diagonal gates with controls, two-qubit diagonals,
 // controlled one-target gates and generic slot gradients (on unless ARCQML_FAST_DIAG=0).

@@ -760,6 +760,53 @@ def plan_schedule_export(plan: CircuitPlan, num_qubits: int, adjoint: bool = Fal
     return bytes(buf)[:size.value]
 
 
+def plan_schedule_summary(plan: CircuitPlan, num_qubits: int, adjoint: bool = False,
+                          requires_grad=None) -> dict:
+    """Counts over the engine's fused-pass schedule (plan_schedule_export): passes, ops executed,
+    rotation ops (one-qubit RX/RY forms and one-qubit phase diagonals, the ops whose FP64 work
+    the scaled forms make one FMA per amplitude component), gradient rows and the further
+    parameters that merged rotations add to a row. Layouts: arcqml_b200/csrc/fused.h."""
+    blob = plan_schedule_export(plan, num_qubits, adjoint, requires_grad)
+    off = 0
+
+    def u32():
+        nonlocal off
+        v = int.from_bytes(blob[off:off + 4], "little")
+        off += 4
+        return v
+
+    out = {"passes": 0, "ops": 0, "rotations": 0, "rows": 0, "aliases": 0, "custom": 0}
+    for _ in range(u32()):
+        if not u32():
+            u32()
+            out["custom"] += 1
+            continue
+        out["passes"] += 1
+        off += 48                       # PassHeader
+        nsub = u32()
+        off += 24 * nsub                # SubBlocks
+        nops = u32()
+        for i in range(nops):           # FOp: kind at byte 0, code at byte 28
+            kind, code = blob[off + 64 * i], blob[off + 64 * i + 28]
+            if kind in (1, 2) or (kind == 3 and code in (4, 5)):
+                out["rotations"] += 1
+        out["ops"] += nops
+        off += 64 * nops
+        nmat = u32()
+        off += 16 * nmat                # matrix entries
+        rows = u32()
+        out["rows"] += rows
+        off += 8 * rows
+        nal = u32()
+        out["aliases"] += nal
+        off += 16 * nal
+        ncode = u32()
+        off += ncode                    # compiled source
+    if off != len(blob):
+        raise RuntimeError("schedule export: unexpected length")
+    return out
+
+
 # ---------------------------------------------------------------- state analysis
 
 

@@ -338,10 +338,16 @@ def gpu_arm(args):
     # FP64 roofline of the fused passes, which are bound by FP64 issue rather than HBM. The
     # algorithmic FP64 work of a Pauli rotation in the scaled unit-diagonal form is one FMA per
     # amplitude component: 4 flop per amplitude forward; the adjoint un-applies it from psi and
-    # lambda and forms the gradient sum: 12 flop. CZ and the other sign flips take none. Peak:
-    # 148 SMs x 64 FP64 FMA per clock x 2 flop at the median SM clock sampled under load (no
-    # measured FP64 figure exists for these GPUs).
-    rotations = sum(1 for o in c.compile_plan(1) if o.bindings)
+    # lambda and forms the gradient sum: 12 flop. CZ and the other sign flips take none. The
+    # count is of the rotation ops the schedules execute: forward passes merge same-axis
+    # rotations on a qubit inside a register sub-block, adjoint passes across the pass (with one
+    # gradient sum for the merged parameters), so fewer ops run than the circuit has rotations.
+    # Peak: 148 SMs x 64 FP64 FMA per clock x 2 flop at the median SM clock sampled under load
+    # (no measured FP64 figure exists for these GPUs).
+    plan0 = rt.CircuitPlan.create(c.compile_plan(1))
+    sched = {"fused_forward": rt.plan_schedule_summary(plan0, n, False),
+             "fused_adjoint": rt.plan_schedule_summary(
+                 plan0, n, True, np.asarray(c.requires_grad_mask(True), np.uint8))}
     sm_mhz = (clk or {}).get("sm_mhz") or 1965.0
     fp64_peak = 148 * 64 * 2 * sm_mhz * 1e6 / 1e12
     roofline_fp64 = {}
@@ -349,11 +355,15 @@ def gpu_arm(args):
         if cat not in prof or not prof[cat][0] or (cat == "fused_adjoint" and args.forward_only):
             continue
         cl, cms, _ = prof[cat]
-        flops = per_amp * rotations * local_amps * args.steps
+        rot_ops = sched[cat]["rotations"]
+        flops = per_amp * rot_ops * local_amps * args.steps
         tf = flops / (cms * 1e-3) / 1e12
         roofline_fp64[cat] = {"bound": "fp64", "achieved": round(tf, 2), "peak": round(fp64_peak, 2),
                               "unit": "TFLOP/s", "frac": round(tf / fp64_peak, 4),
                               "flop_per_launch": flops / cl, "avg_launch_ms": cms / cl,
+                              "rotation_ops_executed": rot_ops,
+                              "schedule": sched[cat] if world == 1 else
+                              dict(sched[cat], note="unsharded schedule of the same circuit"),
                               "peak_source": f"nominal at the sampled {sm_mhz:.0f} MHz"}
     # The rate per-gate kernels would reach at the HBM roofline: every gate one pass over the
     # state (32 B per amplitude forward, 64 B adjoint), all GPUs streaming their shards.

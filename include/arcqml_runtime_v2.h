@@ -283,8 +283,10 @@ int32_t arcqml_rt_v2_plan_jit_check(const CircuitPlanHandle *plan, size_t num_qu
  * receives the byte count (call with buffer NULL to size it). Little-endian: u32 steps; per step
  * u32 is_pass, then for a custom gate u32 op index, else the PassHeader, u32 count + SubBlocks,
  * u32 count + FOps, u32 count + matrix entries (two doubles each), u32 count + u64 gradient
- * parents, u32 length + the `struct PassOps` source of the pass's run-time compiled kernel
- * (empty without one). The layouts are those of arcqml_b200/csrc/fused.h. */
+ * parents (one per accumulator), u32 count + (u64 accumulator, u64 parent) pairs (further
+ * parents that receive an accumulator's gradient: rotations merged in the adjoint sweep),
+ * u32 length + the `struct PassOps` source of the pass's run-time compiled kernel (empty
+ * without one). The layouts are those of arcqml_b200/csrc/fused.h. */
 int32_t arcqml_rt_v2_plan_schedule_export(const CircuitPlanHandle *plan, size_t num_qubits,
                                           int32_t adjoint, const uint8_t *parameter_requires_grad,
                                           size_t parameter_requires_grad_len, uint8_t *buffer,

@@ -106,9 +106,9 @@ int drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const dou
 
 
 class Pass:
-    def __init__(self, header, subs, ops, mats, parents, code):
+    def __init__(self, header, subs, ops, mats, parents, alias, code):
         self.header, self.subs, self.ops, self.mats = header, subs, ops, mats
-        self.parents, self.code = parents, code
+        self.parents, self.alias, self.code = parents, alias, code
         k, nsub, nops, nmat, nacc, acc_base, rb = struct.unpack_from("<7I", header, 0)
         self.k, self.nacc, self.rb = k, nacc, rb
 
@@ -139,8 +139,11 @@ def parse(blob: bytes):
         mats = np.frombuffer(take(u32() * 16), dtype=np.complex128).copy()
         npar = u32()
         parents = list(struct.unpack(f"<{npar}Q", take(8 * npar)))
+        nal = u32()
+        flat = struct.unpack(f"<{2 * nal}Q", take(16 * nal))
+        alias = list(zip(flat[0::2], flat[1::2]))  # (accumulator, further parent)
         code = take(u32()).decode()
-        steps.append(("pass", Pass(header, subs, ops, mats, parents, code)))
+        steps.append(("pass", Pass(header, subs, ops, mats, parents, alias, code)))
     assert off == len(blob)
     return steps
 
@@ -191,5 +194,7 @@ def run(runtime, plan, n, state, adjoint=False, lam=None, requires_grad=None):
                         C.c_void_p(mats.ctypes.data), C.c_void_p(acc.ctypes.data))
             assert status == 0, f"pass {i} wrote past its accumulator rows"
             for a, parent in enumerate(p.parents):
+                grads[parent] += 2.0 * acc[a]
+            for a, parent in p.alias:
                 grads[parent] += 2.0 * acc[a]
     return psi if not adjoint else (psi, lm, grads)

@@ -229,3 +229,11 @@ def test_one_cta_adjoint_code_runs_on_host():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, ARCQML_ADJ_2CTA="0"), timeout=900)
     assert r.returncode == 0 and "column-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("n", [10, 13])
+def test_merged_adjoint_rotations_run_on_host(runtime, oracle, n):
+    """Rotation runs the adjoint passes merge (test_planner_emulation.merge_runs): the compiled
+    code of the merged ops and the rows shared by several parameters."""
+    from test_planner_emulation import merge_runs
+    check(runtime, oracle, merge_runs(n, 40 + n), n, seed=n)

@@ -257,3 +257,86 @@ def test_custom_unitaries_through_the_circuit_api(runtime, oracle):
         c.custom_unitary("bad", np.eye(2) * 1.1, [0])
     with pytest.raises(cm.CircuitError, match="expected 16 entries"):
         c.custom_unitary("bad", np.eye(2), [0, 1])
+
+
+def merge_runs(n, seed):
+    """Runs of rotations the adjoint sweep merges, and neighbours that must stop a merge: RX/RY
+    pairs on one qubit, RZ runs across CZ and a CNOT control (merged) and across a CNOT target
+    or H (not), shared parameters within one run, parameters without gradients, and brickwork
+    layers around them."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    c = workloads.brickwork(n, 2, seed=seed)
+    shared = c.add_parameter(0.37)
+    frozen = c.add_parameter(-1.1, requires_grad=False)
+
+    def ang():
+        return float(g.uniform(-math.pi, math.pi))
+
+    for q in range(n):
+        r = (q + 1) % n
+        c.rot("rx", ang(), q)
+        c.rot("rx", ang(), q)
+        c.append("rx", (q,), frozen)
+        c.rot("ry", ang(), r)
+        c.append("ry", (r,), shared)
+        c.append("ry", (r,), shared)
+        c.rot("rz", ang(), q)
+        c.append("cz", (q, r))
+        c.rot("rz", ang(), q)
+        c.append("cnot", (q, r))      # q is a control: the RZ run goes on
+        c.append("rz", (q,), frozen)
+        c.rot("rz", ang(), q)
+        c.append("cnot", (r, q))      # q is the target: the RZ run ends
+        c.rot("rz", ang(), q)
+        c.rot("rx", ang(), r)
+        c.append("cz", (r, q))        # touches r: the RX run ends
+        c.rot("rx", ang(), r)
+        c.append("h", (q,))
+        c.rot("rz", ang(), q)
+    return c
+
+
+def adjoint_schedule(runtime, c, n):
+    import jit_host_run as J
+    plan = runtime.CircuitPlan.create(c.compile_plan(1))
+    req = np.asarray(c.requires_grad_mask(True), np.uint8)
+    steps = J.parse(runtime.plan_schedule_export(plan, n, True, req))
+    return [p for kind, p in steps if kind == "pass"]
+
+
+@pytest.mark.parametrize("n", [9, 12])
+def test_adjoint_rotation_merges_match_oracle(runtime, oracle, n):
+    """Adjoint passes merge each rotation into the previous one about the same axis on its
+    qubit (one rotation on psi and lambda, one gradient row for both parameters); the sweep
+    still returns every gradient, and merged rows reach every parameter they stand for."""
+    g = np.random.Generator(np.random.PCG64(70 + n))
+    c = merge_runs(n, 70 + n)
+    ops = c.compile_plan(1)
+    req = list(c.requires_grad_mask(True))
+    check(runtime, oracle, ops, n, random_terms(g, n, 20), random_state(g, n), req, 0.9)
+    passes = adjoint_schedule(runtime, c, n)
+    nops = sum(len(p.ops) // 64 for p in passes)
+    assert nops < len(ops) - 3 * n  # every qubit has at least three merges
+    assert sum(len(p.alias) for p in passes) >= n
+
+
+def test_adjoint_merges_off_emulate_correctly():
+    """ARCQML_ADJ_MERGE=0 (subprocess): every rotation keeps its own op and gradient row."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]\n"
+            "import numpy as np, oracle, test_planner_emulation as T\n"
+            "from arcqml_b200 import runtime\n"
+            "n = 10; c = T.merge_runs(n, 5); g = np.random.Generator(np.random.PCG64(5))\n"
+            "T.check(runtime, oracle, c.compile_plan(1), n, T.random_terms(g, n, 20),\n"
+            "        T.random_state(g, n), list(c.requires_grad_mask(True)), -0.4)\n"
+            "ps = T.adjoint_schedule(runtime, c, n)\n"
+            "assert sum(len(p.alias) for p in ps) == 0\n"
+            "assert sum(len(p.ops) // 64 for p in ps) == len(c.compile_plan(1))\n"
+            "print('merge-off-ok')\n") % (root, here, os.path.join(root, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_ADJ_MERGE="0"), timeout=600)
+    assert r.returncode == 0 and "merge-off-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
