@@ -931,9 +931,10 @@ void run_schedule(const Schedule &sch, double2 *psi, double2 *lam, size_t batch,
         size_t launch_smem = smem;
         if (jit[i]) {
             // compiled kernels: the op table is inlined (none in shared memory)
-            const uint32_t cols = threads / jit_acc_lanes(adj, st.header.rb);
+            const uint32_t lanes = jit_acc_lanes(adj, st.header.rb);
             launch_smem = fused_smem(adj, k, st.header.nacc, 0,
-                                     jit_mats_in_params(adj) ? 0 : st.header.nmat, cols,
+                                     jit_mats_in_params(adj) ? 0 : st.header.nmat,
+                                     acc_row_stride(threads / lanes, lanes),
                                      !adj && jit_forward_single());
             blocks = jit_grid_blocks(jit[i], threads, launch_smem);
         }

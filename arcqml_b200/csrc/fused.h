@@ -105,6 +105,17 @@ constexpr uint32_t SB_JIT_FAST = 2;  // the run-time compiled kernels have one f
 constexpr uint32_t SB_WARP_NEXT = 4; // the next sub-block keeps every element in the same warp
 static_assert(sizeof(SubBlock) == 24, "SubBlock layout");
 
+// Row stride of a pass's accumulator table (doubles, shared memory) for `cols` columns, one per
+// `lanes` threads. Kernels that reduce a gradient over four lanes first (accumulate_quad2)
+// update two rows, usually consecutive ones, in one access: a stride of cols + 8 puts row a + 1
+// in the other half of the banks, where a stride of 64 (512 bytes) would give a two-way conflict.
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+__host__ __device__
+#endif
+constexpr uint32_t acc_row_stride(uint32_t cols, uint32_t lanes) {
+    return lanes == 4u ? cols + 8u : cols;
+}
+
 struct PassHeader {
     uint32_t k;              // tile bits
     uint32_t nsub;

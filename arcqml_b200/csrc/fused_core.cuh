@@ -405,7 +405,7 @@ struct SmemLayout {
     uint32_t tile, hioff, sacc, ops, mats, total;
 };
 
-// acc_cols: accumulator columns per row (one per thread, or one per warp).
+// acc_cols: the accumulator table's row stride in doubles (acc_row_stride).
 __host__ __device__ inline SmemLayout smem_layout(bool adj, uint32_t k, uint32_t nacc,
                                                   uint32_t nops, uint32_t nmat, uint32_t acc_cols,
                                                   bool single = false) {
@@ -533,8 +533,9 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     const uint32_t D = 1u << k;
     const uint32_t L = k < uint32_t(kLowFixed) ? k : uint32_t(kLowFixed);
     const uint32_t lowmask = (1u << L) - 1;
-    // accumulator row stride: one column per Runner::kAccLanes threads (1, 4 or a warp)
-    const uint32_t nthreads = blockDim.x / uint32_t(Runner::kAccLanes);
+    // accumulator columns: one per Runner::kAccLanes threads (1, 4 or a warp); row stride
+    const uint32_t ncols = blockDim.x / uint32_t(Runner::kAccLanes);
+    const uint32_t nthreads = acc_row_stride(ncols, uint32_t(Runner::kAccLanes));
     constexpr bool kSingle = ADJ || Runner::kSingleBuffer;
     const uint32_t nops_smem = Runner::kOpsInSmem ? snops : 0u;
     const uint32_t nmat_smem = Runner::kMatsInSmem ? snmat : 0u;
@@ -662,13 +663,13 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
             const double *row = sacc + size_t(a) * nthreads;
             double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
             uint32_t t = 0;
-            for (; t + 4 <= nthreads; t += 4) {
+            for (; t + 4 <= ncols; t += 4) {
                 s0 += row[t];
                 s1 += row[t + 1];
                 s2 += row[t + 2];
                 s3 += row[t + 3];
             }
-            for (; t < nthreads; ++t) s0 += row[t];
+            for (; t < ncols; ++t) s0 += row[t];
             double f;  // the row's factor (compiled kernels add their sums unscaled)
             if constexpr (Runner::kMatsInSmem) f = Runner::row_factor(a, smats);
             else f = Runner::row_factor(a, gmats);

@@ -617,7 +617,7 @@ bool emit_adjoint(std::ostringstream &c, const FOp &o, uint32_t rb, const SubBlo
 std::string pass_source(const Step &st, bool adj, uint32_t rb) {
     std::ostringstream c;
     const uint32_t threads = 1u << (st.header.k - rb);
-    const uint32_t cols = threads / acc_lanes(adj, rb);
+    const uint32_t cols = acc_row_stride(threads / acc_lanes(adj, rb), acc_lanes(adj, rb));
     const bool single = !adj && jit_forward_single();
     const bool params = jit_mats_in_params(adj);
     // the pass's matrix table as one by-value kernel parameter (constant-bank operands)

@@ -17,6 +17,8 @@
 
 #include <algorithm>
 #include <cstring>
+#include <memory>
+#include <mutex>
 #include <vector>
 
 #include "launch.h"
@@ -275,16 +277,127 @@ uint32_t compress(uint64_t x, const uint8_t *S) {
     return r;
 }
 
+int popc64(uint64_t x) { return __builtin_popcountll(x); }
+
 struct TilePass {
     uint8_t S[16] = {};
     std::vector<uint32_t> groups;  // indices into obs.groups
 };
 
-// Covers the observable's groups with tile layouts; false when a flip mask has more than eight
-// qubits above qubit 3 (no 12-qubit tile holds it).
+// Adds `picks` qubits to cand, each the one that completes the most of the masks in todo (ties:
+// the one most of their qubits share; then the lowest).
+void grow_by_qubits(const std::vector<uint64_t> &todo, uint32_t n, uint32_t picks,
+                    uint64_t &cand) {
+    for (uint32_t pick = 0; pick < picks; ++pick) {
+        int best = -1;
+        uint64_t best_score = 0;
+        for (uint32_t q = kTileLow; q < n; ++q) {
+            if ((cand >> q) & 1u) continue;
+            const uint64_t c2 = cand | (uint64_t(1) << q);
+            uint64_t done = 0, touch = 0;
+            for (uint64_t f : todo) {
+                if ((f & ~c2) == 0) ++done;
+                touch += uint64_t(popc64(f & c2));
+            }
+            const uint64_t score = done * 4096 + touch;
+            if (best < 0 || score > best_score) {
+                best = int(q);
+                best_score = score;
+            }
+        }
+        if (best < 0) break;
+        cand |= uint64_t(1) << best;
+    }
+}
+
+// The qubits above the low four of one pass, chosen by masks: a widest remaining mask, then
+// repeatedly the mask that completes the most remaining masks per qubit it adds (ties: the
+// narrower union) while the union fits in `room` qubits. Among the widest masks `rule` picks
+// the first (0) or last (1) in order, or the one sharing the most (2) or fewest (3) qubits
+// with the others.
+uint64_t pick_by_masks(const std::vector<uint64_t> &todo, uint32_t room, int rule) {
+    int width = -1;
+    for (uint64_t h : todo) width = std::max(width, popc64(h));
+    uint64_t U = 0;
+    bool have = false;
+    uint64_t best_overlap = 0;
+    for (uint64_t h : todo) {
+        if (popc64(h) != width) continue;
+        uint64_t overlap = 0;
+        if (rule >= 2)
+            for (uint64_t g : todo) overlap += uint64_t(popc64(h & g));
+        const bool better = !have || rule == 1 || (rule == 2 && overlap > best_overlap) ||
+                            (rule == 3 && overlap < best_overlap);
+        if (better) {
+            U = h;
+            best_overlap = overlap;
+            have = true;
+        }
+    }
+    for (;;) {
+        uint32_t inside = 0;
+        for (uint64_t h : todo) inside += (h & ~U) == 0 ? 1u : 0u;
+        bool found = false;
+        double best_key = 0.0;
+        int best_width = 0;
+        uint64_t best = 0;
+        for (uint64_t h : todo) {
+            if ((h & ~U) == 0) continue;
+            const uint64_t nu = U | h;
+            const int wn = popc64(nu);
+            if (wn > int(room)) continue;
+            uint32_t in2 = 0;
+            for (uint64_t g : todo) in2 += (g & ~nu) == 0 ? 1u : 0u;
+            const double key = double(in2 - inside) / double(wn - popc64(U));
+            if (!found || key > best_key || (key == best_key && wn < best_width)) {
+                found = true;
+                best_key = key;
+                best_width = wn;
+                best = h;
+            }
+        }
+        if (!found) break;
+        U |= best;
+    }
+    return U;
+}
+
+// Tile sets (12 qubits each, the low four included) covering every flip mask in `highs` (the
+// distinct flip masks without their low four bits), by qubits (rule < 0) or by masks with the
+// given seed rule.
+std::vector<uint64_t> cover_sets(const std::vector<uint64_t> &highs, uint32_t n, int rule) {
+    const uint64_t low = (uint64_t(1) << kTileLow) - 1;
+    const uint32_t room = kTileQ - kTileLow;
+    std::vector<uint64_t> todo = highs, sets;
+    while (!todo.empty()) {
+        uint64_t cand = low | (rule >= 0 ? pick_by_masks(todo, room, rule) : 0);
+        grow_by_qubits(todo, n, kTileQ - uint32_t(popc64(cand)), cand);
+        bool any = false;
+        for (uint64_t h : todo) any = any || (h & ~cand) == 0;
+        if (!any) {
+            // the qubit greedy completed no mask: take the first one's qubits, fill up in order
+            cand = low | todo[0];
+            for (uint32_t q = kTileLow; q < n && popc64(cand) < int(kTileQ); ++q)
+                cand |= uint64_t(1) << q;
+        }
+        // n >= 20: both ways reach 12 qubits
+        if (popc64(cand) != int(kTileQ)) fail("internal: observable tile size");
+        std::vector<uint64_t> rest;
+        for (uint64_t h : todo)
+            if (h & ~cand) rest.push_back(h);
+        todo.swap(rest);
+        sets.push_back(cand);
+    }
+    return sets;
+}
+
+// Covers the observable's groups with tile layouts: the fewest passes of the greedy by qubits
+// and the greedy by masks with each seed rule (by masks only up to 256 distinct masks: its cost
+// grows with their cube); false when a flip mask has more than eight qubits above qubit 3 (no
+// 12-qubit tile holds it).
 bool cover(const Observable &obs, uint32_t n, std::vector<TilePass> &passes) {
     const uint64_t low = (uint64_t(1) << kTileLow) - 1;
-    std::vector<uint32_t> todo;
+    std::vector<uint64_t> highs;
     int diag = -1;
     for (uint32_t g = 0; g < obs.groups.size(); ++g) {
         const uint64_t f = obs.groups[g].flip;
@@ -292,56 +405,36 @@ bool cover(const Observable &obs, uint32_t n, std::vector<TilePass> &passes) {
             diag = int(g);
             continue;
         }
-        if (__builtin_popcountll(f & ~low) > int(kTileQ - kTileLow)) return false;
-        todo.push_back(g);
+        if (popc64(f & ~low) > int(kTileQ - kTileLow)) return false;
+        highs.push_back(f & ~low);
     }
-    passes.clear();
-    while (!todo.empty() || (passes.empty() && diag >= 0)) {
+    std::sort(highs.begin(), highs.end());
+    highs.erase(std::unique(highs.begin(), highs.end()), highs.end());
+    std::vector<uint64_t> sets = cover_sets(highs, n, -1);
+    for (int rule = 0; rule < 4 && highs.size() <= 256; ++rule) {
+        std::vector<uint64_t> by_masks = cover_sets(highs, n, rule);
+        if (by_masks.size() < sets.size()) sets.swap(by_masks);
+    }
+    if (sets.empty() && diag >= 0) {  // only the diagonal group: one pass over the low qubits
         uint64_t cand = low;
-        // eight more qubits, each the one that completes the most remaining flip masks (ties:
-        // the one most of their qubits share)
-        for (uint32_t pick = 0; pick < kTileQ - kTileLow; ++pick) {
-            int best = -1;
-            uint64_t best_score = 0;
-            for (uint32_t q = kTileLow; q < n; ++q) {
-                if ((cand >> q) & 1u) continue;
-                const uint64_t c2 = cand | (uint64_t(1) << q);
-                uint64_t done = 0, touch = 0;
-                for (uint32_t g : todo) {
-                    const uint64_t f = obs.groups[g].flip;
-                    if ((f & ~c2) == 0) ++done;
-                    touch += uint64_t(__builtin_popcountll(f & c2));
-                }
-                const uint64_t score = done * 4096 + touch;
-                if (best < 0 || score > best_score) {
-                    best = int(q);
-                    best_score = score;
-                }
-            }
-            if (best < 0) break;
-            cand |= uint64_t(1) << best;
-        }
-        TilePass p;
-        std::vector<uint32_t> rest;
-        for (uint32_t g : todo)
-            ((obs.groups[g].flip & ~cand) == 0 ? p.groups : rest).push_back(g);
-        if (p.groups.empty() && !todo.empty()) {
-            // greedy found no complete mask: take the first one's qubits, fill up in order
-            cand = low | obs.groups[todo[0]].flip;
-            for (uint32_t q = kTileLow; q < n && __builtin_popcountll(cand) < int(kTileQ); ++q)
-                cand |= uint64_t(1) << q;
-            rest.clear();
-            for (uint32_t g : todo)
-                ((obs.groups[g].flip & ~cand) == 0 ? p.groups : rest).push_back(g);
-        }
-        // n >= 20: the greedy always adds eight qubits, the fill-up completes the forced case
-        if (__builtin_popcountll(cand) != int(kTileQ)) fail("internal: observable tile size");
+        grow_by_qubits({}, n, kTileQ - kTileLow, cand);
+        sets.push_back(cand);
+    }
+    passes.assign(sets.size(), TilePass{});
+    std::vector<char> taken(obs.groups.size(), 0);
+    for (size_t p = 0; p < sets.size(); ++p) {
         uint32_t k = 0;
         for (uint32_t q = 0; q < n; ++q)
-            if ((cand >> q) & 1u) p.S[k++] = uint8_t(q);
-        if (passes.empty() && diag >= 0) p.groups.insert(p.groups.begin(), uint32_t(diag));
-        passes.push_back(std::move(p));
-        todo.swap(rest);
+            if ((sets[p] >> q) & 1u) passes[p].S[k++] = uint8_t(q);
+        if (p == 0 && diag >= 0) {
+            passes[p].groups.push_back(uint32_t(diag));
+            taken[size_t(diag)] = 1;
+        }
+        for (uint32_t g = 0; g < obs.groups.size(); ++g)
+            if (!taken[g] && (obs.groups[g].flip & ~sets[p]) == 0) {
+                passes[p].groups.push_back(g);
+                taken[g] = 1;
+            }
     }
     return true;
 }
@@ -356,44 +449,53 @@ double2 term_weight(const Observable &obs, uint64_t flip, uint32_t k) {
     }
 }
 
-}  // namespace
-
-uint32_t observable_tile_passes(const Observable &obs, uint32_t n) {
+// Everything host-side of an observable's tile passes for one state size: the cover and the
+// per-pass group and term tables (one blob, 16-byte aligned parts), built once per observable
+// and size. ok == false: the gather kernel evaluates the observable.
+struct TilePlan {
+    bool ok = false;
     std::vector<TilePass> passes;
-    if (n < kTileMinQubits || n > 63 || !cover(obs, n, passes)) return 0;
-    return uint32_t(passes.size());
+    std::vector<size_t> goff, moff;      // byte offsets of each pass's groups and members
+    std::vector<uint32_t> nmem;          // members per pass
+    std::vector<std::vector<uint32_t>> hbeg;
+    std::vector<double2> blob;
+    size_t max_smem = 0;
+};
+
+size_t tile_smem(size_t ngroups, size_t nmembers) {
+    return (16u << kTileQ) + (8u << (kTileQ - kTileLow)) + ngroups * sizeof(uint4) +
+           nmembers * sizeof(TileMember);
 }
 
-// <psi|H|psi> of one state (value into *value_host) and, when out is non-null, H psi written
-// to out (or added to it with accumulate). Returns false (nothing launched) when the state is
-// too small or a flip mask fits no tile; the caller then uses k_pauli.
-bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, uint32_t n,
-                      double *value_host, bool accumulate, ThreadContext &ctx, cudaStream_t s) {
-    if (n < kTileMinQubits || n > 63) return false;
-    std::vector<TilePass> passes;
+std::shared_ptr<const TilePlan> build_tile_plan(const Observable &obs, uint32_t n) {
+    auto tp = std::make_shared<TilePlan>();
     // an observable without terms takes no pass: the gather kernel writes its zero H psi
-    if (!cover(obs, n, passes) || passes.empty()) return false;
-    // device tables: per pass its groups then its members, 16-byte aligned
-    std::vector<size_t> goff(passes.size()), moff(passes.size());
-    std::vector<uint32_t> nmem(passes.size());
+    if (n < kTileMinQubits || n > 63 || !cover(obs, n, tp->passes) || tp->passes.empty())
+        return tp;
+    const std::vector<TilePass> &passes = tp->passes;
+    const size_t np = passes.size();
+    tp->goff.resize(np);
+    tp->moff.resize(np);
+    tp->nmem.resize(np);
+    tp->hbeg.resize(np);
     size_t total = 0;
-    for (size_t p = 0; p < passes.size(); ++p) {
+    for (size_t p = 0; p < np; ++p) {
         uint32_t m = 0;
         for (uint32_t g : passes[p].groups) m += obs.groups[g].count;
-        if (m > kTileMaxMembers) return false;
-        nmem[p] = m;
-        goff[p] = total;
+        if (m > kTileMaxMembers) return std::make_shared<TilePlan>();
+        tp->nmem[p] = m;
+        tp->goff[p] = total;
         total += passes[p].groups.size() * sizeof(uint4);
-        moff[p] = total;
+        tp->moff[p] = total;
         total += size_t(m) * sizeof(TileMember);
+        tp->max_smem = std::max(tp->max_smem, tile_smem(passes[p].groups.size(), m));
     }
-    std::vector<double2> blob((total + 15) / 16 + 1);
-    char *hb = reinterpret_cast<char *>(blob.data());
-    std::vector<std::vector<uint32_t>> hbeg(passes.size());
-    for (size_t p = 0; p < passes.size(); ++p) {
+    tp->blob.assign((total + 15) / 16 + 1, make_double2(0.0, 0.0));
+    char *hb = reinterpret_cast<char *>(tp->blob.data());
+    for (size_t p = 0; p < np; ++p) {
         const uint8_t *S = passes[p].S;
-        uint4 *gs = reinterpret_cast<uint4 *>(hb + goff[p]);
-        TileMember *ms = reinterpret_cast<TileMember *>(hb + moff[p]);
+        uint4 *gs = reinterpret_cast<uint4 *>(hb + tp->goff[p]);
+        TileMember *ms = reinterpret_cast<TileMember *>(hb + tp->moff[p]);
         // order: single-term groups by the element phase pattern of their term and whether its
         // weight i^y c is imaginary, then the others
         std::vector<uint32_t> order(passes[p].groups.size());
@@ -406,14 +508,14 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
         };
         std::stable_sort(order.begin(), order.end(),
                          [&](uint32_t a, uint32_t b) { return key(a) < key(b); });
-        hbeg[p].assign(33, uint32_t(order.size()));
-        for (uint32_t i = order.size(); i-- > 0;) hbeg[p][key(order[i])] = i;
-        for (uint32_t h = 32; h-- > 0;) hbeg[p][h] = std::min(hbeg[p][h], hbeg[p][h + 1]);
+        std::vector<uint32_t> &hbeg = tp->hbeg[p];
+        hbeg.assign(33, uint32_t(order.size()));
+        for (uint32_t i = order.size(); i-- > 0;) hbeg[key(order[i])] = i;
+        for (uint32_t h = 32; h-- > 0;) hbeg[h] = std::min(hbeg[h], hbeg[h + 1]);
         uint32_t mi = 0;
         for (size_t oi = 0; oi < order.size(); ++oi) {
-            const size_t gi = oi;
             const PauliGroup &grp = obs.groups[passes[p].groups[order[oi]]];
-            gs[gi] = make_uint4(host_phys(compress(grp.flip, S)), mi, mi + grp.count, 0u);
+            gs[oi] = make_uint4(host_phys(compress(grp.flip, S)), mi, mi + grp.count, 0u);
             for (uint32_t k = grp.first; k < grp.first + grp.count; ++k, ++mi) {
                 TileMember &m = ms[mi];
                 m.w = term_weight(obs, grp.flip, k);
@@ -424,45 +526,67 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
             }
         }
     }
-    std::vector<const std::vector<double2> *> refs{&blob};
+    tp->ok = true;
+    return tp;
+}
+
+// The observable's tile plan for n qubits, built on first use.
+std::shared_ptr<const TilePlan> tile_plan(const Observable &obs, uint32_t n) {
+    std::lock_guard<std::mutex> lock(obs.cache_mu);
+    for (const auto &e : obs.tile_cache)
+        if (e.first == n) return std::static_pointer_cast<const TilePlan>(e.second);
+    std::shared_ptr<const TilePlan> tp = build_tile_plan(obs, n);
+    obs.tile_cache.emplace_back(n, tp);
+    return tp;
+}
+
+}  // namespace
+
+uint32_t observable_tile_passes(const Observable &obs, uint32_t n) {
+    const std::shared_ptr<const TilePlan> tp = tile_plan(obs, n);
+    return tp->ok ? uint32_t(tp->passes.size()) : 0u;
+}
+
+// <psi|H|psi> of one state (value into *value_host) and, when out is non-null, H psi written
+// to out (or added to it with accumulate). Returns false (nothing launched) when the state is
+// too small or a flip mask fits no tile; the caller then uses k_pauli.
+bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, uint32_t n,
+                      double *value_host, bool accumulate, ThreadContext &ctx, cudaStream_t s) {
+    if (n < kTileMinQubits || n > 63) return false;
+    const std::shared_ptr<const TilePlan> tp = tile_plan(obs, n);
+    if (!tp->ok) return false;
+    const std::vector<TilePass> &passes = tp->passes;
+    std::vector<const std::vector<double2> *> refs{&tp->blob};
     const char *dev = reinterpret_cast<const char *>(upload_tables(refs, ctx, s)[0]);
 
-    static int sms = 0;
-    if (sms == 0) {
-        int d = 0;
-        check_cuda(cudaGetDevice(&d), "cudaGetDevice");
-        check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d),
-                   "cudaDeviceGetAttribute");
-    }
-    size_t max_smem = 0;
-    for (size_t p = 0; p < passes.size(); ++p)
-        max_smem = std::max(max_smem, (16u << kTileQ) + (8u << (kTileQ - kTileLow)) +
-                                          passes[p].groups.size() * sizeof(uint4) +
-                                          size_t(nmem[p]) * sizeof(TileMember));
+    int d = 0, sms = 0;
+    check_cuda(cudaGetDevice(&d), "cudaGetDevice");
+    check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d),
+               "cudaDeviceGetAttribute");
     check_cuda(cudaFuncSetAttribute(k_pauli_tile, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(max_smem)),
+                                    int(tp->max_smem)),
                "cudaFuncSetAttribute");
     int per_sm = 0;
     check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pauli_tile,
-                                                             int(kTileThreads), max_smem),
+                                                             int(kTileThreads), tp->max_smem),
                "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     const uint64_t total_tiles = uint64_t(1) << (n - kTileQ);
-    const uint32_t grid = uint32_t(std::min<uint64_t>(total_tiles, uint64_t(sms) * std::max(per_sm, 1)));
+    const uint32_t grid =
+        uint32_t(std::min<uint64_t>(total_tiles, uint64_t(sms) * std::max(per_sm, 1)));
     double *partials = ctx_partials(ctx, passes.size() * size_t(grid));
     for (size_t p = 0; p < passes.size(); ++p) {
         TileArgs a;
         std::memset(&a, 0, sizeof(a));
         std::memcpy(a.S, passes[p].S, 16);
-        a.groups = reinterpret_cast<const uint4 *>(dev + goff[p]);
-        a.members = reinterpret_cast<const TileMember *>(dev + moff[p]);
+        a.groups = reinterpret_cast<const uint4 *>(dev + tp->goff[p]);
+        a.members = reinterpret_cast<const TileMember *>(dev + tp->moff[p]);
         a.ngroups = uint32_t(passes[p].groups.size());
-        a.nmembers = nmem[p];
+        a.nmembers = tp->nmem[p];
         a.read_out = (out && (p > 0 || accumulate)) ? 1u : 0u;
         a.ev_sub = (out && p == 0 && accumulate) ? 1u : 0u;
         a.ev_add = (!out || p + 1 == passes.size()) ? 1u : 0u;
-        for (uint32_t h = 0; h < 33; ++h) a.hbeg[h] = hbeg[p][h];
-        const size_t smem = (16u << kTileQ) + (8u << (kTileQ - kTileLow)) +
-                            a.ngroups * sizeof(uint4) + size_t(a.nmembers) * sizeof(TileMember);
+        for (uint32_t h = 0; h < 33; ++h) a.hbeg[h] = tp->hbeg[p][h];
+        const size_t smem = tile_smem(a.ngroups, a.nmembers);
         // algorithmic traffic of the pass: psi read, H psi written (and read back after pass 0)
         const double per_amp = 16.0 + (out ? (a.read_out ? 32.0 : 16.0) : 0.0);
         const ProfToken tok = prof_begin(PROF_PAULI, s);

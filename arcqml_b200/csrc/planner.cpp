@@ -536,9 +536,9 @@ bool subblock_reorder() {
     return on;
 }
 
-bool adjoint_merge() {
+bool rotation_merge() {
     static const bool on = [] {
-        const char *e = std::getenv("ARCQML_ADJ_MERGE");
+        const char *e = std::getenv("ARCQML_ROT_MERGE");
         return !(e && e[0] == '0');
     }();
     return on;
@@ -546,9 +546,10 @@ bool adjoint_merge() {
 
 namespace {
 
-// Adjoint passes merge a Pauli rotation exp(-i a P / 2) into the previous rotation about the
-// same axis on its qubit when nothing in between fails to commute with P: one rotation by the
-// summed angle on psi and lambda, and one gradient sum for both parameters. Both are exact:
+// Passes merge a Pauli rotation exp(-i a P / 2) into the previous rotation about the same axis
+// on its qubit when nothing in between fails to commute with P: one rotation by the summed
+// angle (on psi, and on lambda in the adjoint sweep), and there one gradient sum for both
+// parameters. Both are exact:
 // the rotations commute with P, so <lam|P|psi> is the same on either side of one of them (the
 // gradient of each is that sum), and moving the later rotation back past gates that commute
 // with it changes neither the states nor their gradients. Between two RX or RY rotations no
@@ -613,7 +614,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
     for (size_t i = 0; i < gates.size(); ++i) done[i] = gates[i].noop ? 1 : 0;
     size_t first = 0;
     uint32_t acc_total = 0;
-    const bool merge_adj = adjoint && adjoint_merge();
+    const bool merge_rot = rotation_merge();
     while (true) {
         while (first < gates.size() && done[first]) ++first;
         if (first >= gates.size()) break;
@@ -636,7 +637,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         for (size_t i = first; i < gates.size(); ++i) {
             if (done[i]) continue;
             const PGate &g = gates[i];
-            const uint32_t ax = merge_adj ? merge_axis(g) : 0;
+            const uint32_t ax = merge_rot ? merge_axis(g) : 0;
             const bool merges = ax != 0 && chain[g.targets[0]].axis == ax;
             const size_t rows = (merges && chain[g.targets[0]].row) ? 0 : g.parents.size();
             if (pass_acc + rows > size_t(kMaxPassAcc)) break;
@@ -655,7 +656,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                 pass_mats += mat_entries(g);
                 if (merges) {
                     chain[g.targets[0]].row = chain[g.targets[0]].row || !g.parents.empty();
-                } else if (merge_adj) {
+                } else if (merge_rot) {
                     end_chains(chain, g);
                     if (ax) chain[g.targets[0]] = MergeChain{ax, -1, !g.parents.empty()};
                 }
@@ -726,7 +727,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         if (warp_local_exchanges())
             plan_warp_runs(padR, k, rb, runW, warp_next);
         // --- emit sub-blocks, ops and matrices
-        MergeChain echain[64];  // adjoint rotation merges (over the whole pass)
+        MergeChain echain[64];  // rotation merges (over the whole pass)
         for (size_t sb = 0; sb < subs.size(); ++sb) {
             const uint32_t R = padR[sb];
             SubBlock s;
@@ -772,7 +773,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
             for (int q = 0; q < 64; ++q) last1q[q] = -1;
             for (size_t gi : subs[sb]) {
                 const PGate &g = gates[gi];
-                const uint32_t ax = merge_adj ? merge_axis(g) : 0;
+                const uint32_t ax = merge_rot ? merge_axis(g) : 0;
                 if (ax && echain[g.targets[0]].axis == ax) {
                     FOp &e = st.ops[size_t(echain[g.targets[0]].op)];
                     double2 ue[4], un[4], p[4];
@@ -802,7 +803,7 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                     }
                     continue;
                 }
-                if (merge_adj) end_chains(echain, g);
+                if (merge_rot) end_chains(echain, g);
                 const bool mergeable = !adjoint && g.controls.empty() && g.targets.size() == 1 &&
                                        g.gkind == GK_NONE;
                 bool merge = mergeable && last1q[g.targets[0]] >= 0;

@@ -42,9 +42,10 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
 // paths (on unless ARCQML_FAST_CNOT=0) instead of a dense 2x2 / the generic path.
 bool fast_cnot();
 
-// Whether adjoint passes merge a Pauli rotation into the previous rotation about the same axis
-// on its qubit (on unless ARCQML_ADJ_MERGE=0).
-bool adjoint_merge();
+// Whether passes merge a Pauli rotation into the previous rotation about the same axis on its
+// qubit anywhere in the pass (on unless ARCQML_ROT_MERGE=0; forward passes still merge
+// one-qubit gates within a register sub-block without it).
+bool rotation_merge();
 
 // Whether the run-time compiled kernels run diagonal gates with controls, two-qubit diagonals,
 // controlled one-target gates and generic slot gradients (on unless ARCQML_FAST_DIAG=0).

@@ -112,6 +112,10 @@ struct Observable {
     std::vector<uint64_t> zmask;      // phase masks
     std::vector<uint32_t> ymod4;      // y count mod 4
     std::vector<PauliGroup> groups;
+    // Host tables derived from the terms on first use, per state size (pauli_tile.cu: the tile
+    // passes that cover the flip masks). The terms never change after creation.
+    mutable std::mutex cache_mu;
+    mutable std::vector<std::pair<uint32_t, std::shared_ptr<const void>>> tile_cache;
 };
 
 // ------------------------------------------------------------------ execution context

@@ -60,7 +60,10 @@ int drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const dou
     const uint32_t k = h->k, D = 1u << k, threads = 1u << (k - RB);
     const uint64_t tiles = uint64_t(1) << (n - k);
     std::vector<double2> tp(D), tl(D);
-    const size_t rows = size_t(h->nacc) * threads, guard = 64;
+    // accumulator rows hold one column per Ops::kAccLanes threads, acc_row_stride apart
+    const uint32_t cols = threads / uint32_t(Ops::kAccLanes);
+    const uint32_t stride = acc_row_stride(cols, uint32_t(Ops::kAccLanes));
+    const size_t rows = size_t(h->nacc) * stride, guard = 64;
     std::vector<double> sacc(rows + guard, 0.0);
     for (size_t i = rows; i < rows + guard; ++i) sacc[i] = 12345.0;
     blockDim.x = threads;
@@ -84,18 +87,16 @@ int drive(uint32_t n, double2 *psi, double2 *lam, const PassHeader *h, const dou
             for (uint32_t t = 0; t < threads; ++t) {
                 threadIdx.x = t;
                 Ops::template run<RB, ADJ>(sb, k, tp.data(), tl.data(), nullptr, mats, nullptr,
-                                           sacc.data(), threads, g);
+                                           sacc.data(), stride, g);
             }
         for (uint32_t j = 0; j < D; ++j) {
             psi[gidx(j)] = tp[phys(j)];
             if (ADJ) lam[gidx(j)] = tl[phys(j)];
         }
     }
-    // accumulator rows hold one column per Ops::kAccLanes threads
-    const uint32_t cols = threads / uint32_t(Ops::kAccLanes);
     for (uint32_t a = 0; a < h->nacc; ++a) {
         double s = 0.0;
-        for (uint32_t t = 0; t < cols; ++t) s += sacc[size_t(a) * cols + t];
+        for (uint32_t t = 0; t < cols; ++t) s += sacc[size_t(a) * stride + t];
         acc[a] = s * Ops::row_factor(a, mats);
     }
     for (size_t i = rows; i < rows + guard; ++i)

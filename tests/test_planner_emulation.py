@@ -318,10 +318,14 @@ def test_adjoint_rotation_merges_match_oracle(runtime, oracle, n):
     nops = sum(len(p.ops) // 64 for p in passes)
     assert nops < len(ops) - 3 * n  # every qubit has at least three merges
     assert sum(len(p.alias) for p in passes) >= n
+    plan = runtime.CircuitPlan.create(ops)
+    fwd = runtime.plan_schedule_summary(plan, n, False)  # forward passes merge the same runs
+    assert fwd["ops"] < len(ops) - 3 * n and fwd["aliases"] == 0
 
 
-def test_adjoint_merges_off_emulate_correctly():
-    """ARCQML_ADJ_MERGE=0 (subprocess): every rotation keeps its own op and gradient row."""
+def test_rotation_merges_off_emulate_correctly():
+    """ARCQML_ROT_MERGE=0 (subprocess): every adjoint rotation keeps its own op and gradient row
+    (forward passes still merge one-qubit gates within a register sub-block)."""
     import os
     import subprocess
     import sys
@@ -338,5 +342,5 @@ def test_adjoint_merges_off_emulate_correctly():
             "assert sum(len(p.ops) // 64 for p in ps) == len(c.compile_plan(1))\n"
             "print('merge-off-ok')\n") % (root, here, os.path.join(root, "oracle"))
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
-                       env=dict(os.environ, ARCQML_ADJ_MERGE="0"), timeout=600)
+                       env=dict(os.environ, ARCQML_ROT_MERGE="0"), timeout=600)
     assert r.returncode == 0 and "merge-off-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
