@@ -743,6 +743,7 @@ struct TableRunner {
     static constexpr bool kSingleBuffer = false;
     static constexpr bool kOpsInSmem = true;
     static constexpr bool kMatsInSmem = true;
+    static constexpr bool kPrefetch = true;
     // every exchange of the table-driven kernel is a CTA barrier
     __device__ static __forceinline__ bool warp_next(uint32_t) { return false; }
     // the table-driven kernel scales each gradient term as it adds it

@@ -397,9 +397,9 @@ __device__ __forceinline__ uint32_t sub_index(uint32_t tb, const uint32_t (&rm)[
 // Shared memory: [tile buffers][hioff][accumulators][ops][matrices].
 // Forward: two psi buffers; while a CTA computes tile i from one, cp.async streams tile
 // i + gridDim into the other. Forward single-buffered (`single`, the compiled kernels that run
-// two CTAs per SM): one psi buffer, the next tile prefetched into L2, the other CTA on the SM
-// computing while this one loads. Adjoint: one psi and one lambda buffer (the next tile is
-// prefetched into L2 instead) and one accumulator column per thread. Kernels that do not read
+// two CTAs per SM): one psi buffer, the other CTA on the SM computing while this one loads.
+// Adjoint: one psi and one lambda buffer (the next tile is prefetched into L2 instead) and one
+// accumulator column per thread. Kernels that do not read
 // the op table from shared memory pass nops = 0.
 struct SmemLayout {
     uint32_t tile, hioff, sacc, ops, mats, total;
@@ -481,8 +481,9 @@ __device__ __forceinline__ SubBlock load_subblock(const SubBlock *subs, uint32_t
 
 // One pass over all tiles; Runner::run<RB, ADJ>(sb, ...) applies sub-block sb of the pass to
 // the tile (it gathers the thread's registers, applies the gates and scatters them back).
-// Runner::kSingleBuffer: a forward pass keeps one tile buffer (load, compute, write back, with
-// the next tile prefetched into L2), as the adjoint does. Runner::kOpsInSmem: the runner reads
+// Runner::kSingleBuffer: a forward pass keeps one tile buffer (load, compute, write back), as
+// the adjoint does. Runner::kPrefetch: one-buffer loops ask L2 for the next tile while this one
+// is computed. Runner::kOpsInSmem: the runner reads
 // the op table from shared memory (the table-driven kernel; compiled kernels have it inlined).
 // Runner::kMatsInSmem: the matrix table `gmats` (a pointer) is staged in shared memory;
 // otherwise `gmats` is the kernel's by-value parameter struct holding the table (member m), which
@@ -620,13 +621,14 @@ __device__ __forceinline__ void fused_body(double2 *__restrict__ psi, double2 *_
     };
 
     if constexpr (kSingle) {
-        // One buffer: load tile T, ask L2 for tile T + gridDim while T is computed.
+        // One buffer: load tile T, ask L2 for tile T + gridDim while T is computed (when
+        // Runner::kPrefetch).
         const uint32_t run_bytes = 16u << L;
         const uint32_t lines = run_bytes >= 128u ? run_bytes / 128u : 1u;
         for (uint64_t T = blockIdx.x; T < total_tiles; T += gridDim.x) {
             issue_load(T, 0);
             const uint64_t Tn = T + gridDim.x;
-            if (Tn < total_tiles) {
+            if (Runner::kPrefetch && Tn < total_tiles) {
                 const uint64_t off = ((Tn >> tiles_log) << n) + tile_base(Tn);
                 const char *P = reinterpret_cast<const char *>(psi + off);
                 const char *Lm = ADJ ? reinterpret_cast<const char *>(lam + off) : nullptr;

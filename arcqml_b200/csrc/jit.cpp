@@ -160,7 +160,7 @@ bool adjoint_per_warp() {
 
 }  // namespace
 
-// Compiled forward kernels keep one tile buffer (the next tile prefetched into L2) and ask for
+// Compiled forward kernels keep one tile buffer and ask for
 // two resident CTAs per SM, so that one CTA's loads and shared-memory exchanges overlap the
 // other's arithmetic (ARCQML_FWD_SINGLE=0: two buffers, one CTA per SM).
 bool jit_forward_single() {
@@ -631,6 +631,9 @@ std::string pass_source(const Step &st, bool adj, uint32_t rb) {
          "    static constexpr bool kSingleBuffer = " << (single ? "true" : "false") << ";\n"
          "    static constexpr bool kOpsInSmem = false;\n"
          "    static constexpr bool kMatsInSmem = " << (params ? "false" : "true") << ";\n"
+         // the next tile into L2 while this one is computed: adjoint kernels only (32 qubits:
+         // adjoint passes 0.7 % faster with it, forward passes 1 % faster without)
+         "    static constexpr bool kPrefetch = " << (adj ? "true" : "false") << ";\n"
          "    template <int RB, bool ADJ, class MT>\n"
          "    __device__ static __forceinline__ void run(uint32_t sb, uint32_t, double2 *tp,\n"
          "            double2 *tl, const FOp *, const MT &MS, const SubBlock *, double *sacc,\n"

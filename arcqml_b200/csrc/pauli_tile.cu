@@ -164,18 +164,6 @@ __global__ void __launch_bounds__(kTileThreads, 2)
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i)
             acc[i] = rd ? out[base + elem_off(i)] : make_double2(0.0, 0.0);
-        const uint64_t Tn = T + gridDim.x;
-        if (Tn < total_tiles) {  // the next tile into L2 while this one is computed
-            const uint64_t nb = tile_base(Tn);
-            for (uint32_t r = tid; r < 512u; r += blockDim.x) {
-                const double2 *p = psi + nb + hioff[r >> 1] + (r & 1u) * 8u;
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-                if (rd) {
-                    const double2 *q = out + nb + hioff[r >> 1] + (r & 1u) * 8u;
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(q));
-                }
-            }
-        }
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
         __syncthreads();
         if (P.ev_sub) {

@@ -14,8 +14,9 @@ gradients read back to the host.
 
 With ``--gpus N`` (N > 1, one process per GPU under torchrun) the same 32-qubit state is sharded
 over the N GPUs on its top log2(N) qubits (``arcqml_b200.sharded``): strong scaling, the
-whole-job rate over the max-over-ranks device time. Global-qubit swaps go over NCCL; their
-count, bytes and time are reported under ``swaps``.
+whole-job rate over the max-over-ranks device time. Global-qubit swaps gather the peers'
+packed slices over NVLink from CUDA IPC buffers (``ARCQML_SWAP=p2p|nccl`` for NCCL
+point-to-point instead); their count, bytes and time are reported under ``swaps``.
 
 ``--impl reference`` times the CPU oracle (the f64 restatement of the reference's algorithm;
 the reference's own runtime is a closed Windows library) on the host cores: each step a bounded
