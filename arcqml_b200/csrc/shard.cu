@@ -9,7 +9,6 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include "launch.h"
 #include "profile.h"
 #include "rt_internal.h"
@@ -57,7 +56,6 @@ struct SliceSources {
     const double2 *src[1u << kMaxSliceBits];
 };
 
-template <bool UNROLL>
 __global__ void __launch_bounds__(kSliceThreads)
     k_shard_slices_from(double2 *__restrict__ amps, uint64_t chunk_begin, uint64_t chunk_len,
                         const __grid_constant__ SliceArgs A,
@@ -65,19 +63,9 @@ __global__ void __launch_bounds__(kSliceThreads)
     const uint64_t y = blockIdx.y;
     const double2 *src = S.src[y];
     if (!src) return;
-    // four loads in flight per thread before their stores: a peer's memory answers in
-    // microseconds, and NVLink needs megabytes in flight per GPU
-    const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; UNROLL && j + 3 * stride < chunk_len; j += 4 * stride) {
-        const double2 a0 = src[j], a1 = src[j + stride], a2 = src[j + 2 * stride],
-                      a3 = src[j + 3 * stride];
-        amps[slice_index(chunk_begin + j, y, A)] = a0;
-        amps[slice_index(chunk_begin + j + stride, y, A)] = a1;
-        amps[slice_index(chunk_begin + j + 2 * stride, y, A)] = a2;
-        amps[slice_index(chunk_begin + j + 3 * stride, y, A)] = a3;
-    }
-    for (; j < chunk_len; j += stride) amps[slice_index(chunk_begin + j, y, A)] = src[j];
+    for (uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < chunk_len;
+         j += uint64_t(gridDim.x) * blockDim.x)
+        amps[slice_index(chunk_begin + j, y, A)] = src[j];
 }
 
 int g_sms = 0;
@@ -111,16 +99,8 @@ void launch_slices_from(double2 *amps, const uint32_t *positions, uint32_t k,
     const uint64_t need = (chunk_len + kSliceThreads - 1) / kSliceThreads;
     const unsigned bx = unsigned(std::max<uint64_t>(1, std::min(want, need)));
     const ProfToken tok = prof_begin(PROF_SHARD, s);
-    static const bool unroll = [] {  // experiment switch
-        const char *e = std::getenv("ARCQML_GATHER_UNROLL");
-        return !(e && e[0] == '0');
-    }();
-    if (unroll)
-        k_shard_slices_from<true><<<dim3(bx, 1u << k), kSliceThreads, 0, s>>>(
-            amps, chunk_begin, chunk_len, A, S);
-    else
-        k_shard_slices_from<false><<<dim3(bx, 1u << k), kSliceThreads, 0, s>>>(
-            amps, chunk_begin, chunk_len, A, S);
+    k_shard_slices_from<<<dim3(bx, 1u << k), kSliceThreads, 0, s>>>(amps, chunk_begin, chunk_len,
+                                                                      A, S);
     prof_end(tok, s, 32.0 * double(chunk_len) * double(active));
     check_cuda(cudaGetLastError(), "shard slice gather kernel launch");
 }
