@@ -7,7 +7,7 @@
 // pass's gates written out in order, register bits as template constants and matrix offsets as
 // literals. The compiler then schedules across gates. Parameter values stay in the uploaded
 // matrix table, so a kernel is reused for every parameter vector of the same circuit structure
-// (kernels are cached by their source text, per device).
+// (kernels are cached by their source text, per device, and by the pass's structure).
 //
 // Compilation goes through NVRTC (loaded on first use) for sm_100a; the cubin is loaded with the
 // driver API reached through cudaGetDriverEntryPoint, so the library links no driver or NVRTC
@@ -801,6 +801,24 @@ Compiled compile(const std::string &src) {
 
 // Per device: source -> kernel (nullptr: the source failed to compile or load; not retried).
 std::unordered_map<int, std::unordered_map<std::string, CUfunction>> g_cache;
+// Per device: a pass's structure (struct_key) -> its kernel, so that a pass seen before skips
+// writing its source (the source is a function of these bytes and the process's switches; the
+// matrix values it reads at run time are not part of it).
+std::unordered_map<int, std::unordered_map<std::string, CUfunction>> g_struct_cache;
+
+std::string struct_key(const Step &st, bool adj) {
+    PassHeader h = st.header;
+    h.acc_base = 0;  // read from the header at run time
+    std::string k;
+    k.reserve(16 + sizeof(h) + st.subs.size() * sizeof(SubBlock) + st.ops.size() * sizeof(FOp));
+    const uint32_t misc[4] = {adj ? 1u : 0u, st.scaled ? 1u : 0u, st.sfin,
+                              uint32_t(st.mats.size())};
+    k.append(reinterpret_cast<const char *>(misc), sizeof(misc));
+    k.append(reinterpret_cast<const char *>(&h), sizeof(h));
+    k.append(reinterpret_cast<const char *>(st.subs.data()), st.subs.size() * sizeof(SubBlock));
+    k.append(reinterpret_cast<const char *>(st.ops.data()), st.ops.size() * sizeof(FOp));
+    return k;
+}
 std::atomic<uint64_t> g_compiled{0}, g_jit_launches{0}, g_fallbacks{0};
 std::string g_last_error;
 
@@ -821,22 +839,43 @@ bool jit_enabled() {
 std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
     std::vector<void *> fns(sch.steps.size(), nullptr);
     if (!jit_enabled()) return fns;
-    std::vector<std::string> srcs(sch.steps.size());
-    for (size_t i = 0; i < sch.steps.size(); ++i)
-        if (sch.steps[i].is_pass) {
-            const std::string pass = pass_source(sch.steps[i], adj, sch.steps[i].header.rb);
-            if (!pass.empty()) srcs[i] = full_source(pass);
-        }
     int dev = 0;
     check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    std::vector<std::string> keys(sch.steps.size());
+    std::vector<char> known(sch.steps.size(), 0);
+    for (size_t i = 0; i < sch.steps.size(); ++i)
+        if (sch.steps[i].is_pass) keys[i] = struct_key(sch.steps[i], adj);
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        auto &sc = g_struct_cache[dev];
+        for (size_t i = 0; i < keys.size(); ++i) {
+            if (keys[i].empty()) continue;
+            auto it = sc.find(keys[i]);
+            if (it == sc.end()) continue;
+            known[i] = 1;
+            fns[i] = it->second;
+            if (!fns[i]) ++g_fallbacks;
+        }
+    }
+    std::vector<std::string> srcs(sch.steps.size());
+    bool any = false;
+    for (size_t i = 0; i < sch.steps.size(); ++i)
+        if (sch.steps[i].is_pass && !known[i]) {
+            const std::string pass = pass_source(sch.steps[i], adj, sch.steps[i].header.rb);
+            if (!pass.empty()) srcs[i] = full_source(pass);
+            any = true;
+        }
+    if (!any) return fns;
     std::lock_guard<std::mutex> lock(g_mu);
     auto &cache = g_cache[dev];
+    auto &sc = g_struct_cache[dev];
     std::vector<size_t> todo;
     for (size_t i = 0; i < srcs.size(); ++i) {
         if (srcs[i].empty()) continue;
         auto it = cache.find(srcs[i]);
         if (it != cache.end()) {
             fns[i] = it->second;
+            sc[keys[i]] = it->second;
             if (!fns[i]) ++g_fallbacks;
         } else {
             bool dup = false;
@@ -902,7 +941,10 @@ std::vector<void *> jit_kernels(const Schedule &sch, bool adj) {
         for (size_t i = 0; i < srcs.size(); ++i)
             if (!srcs[i].empty() && !fns[i]) {
                 auto it = cache.find(srcs[i]);
-                if (it != cache.end()) fns[i] = it->second;
+                if (it != cache.end()) {
+                    fns[i] = it->second;
+                    sc[keys[i]] = it->second;
+                }
             }
     }
     return fns;

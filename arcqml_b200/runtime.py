@@ -746,6 +746,34 @@ def plan_emulate(plan: CircuitPlan, state, num_qubits: int, adjoint: bool = Fals
     return a, lm, grads
 
 
+def plan_structure_key(ops: Sequence[PlanOp]) -> tuple:
+    """What a plan holds besides its bound parameter values: per operation the opcode, qubits,
+    parameter bindings, constant slot values and custom matrix. Plans with equal keys differ
+    only in values that CircuitPlan.set_parameters replaces."""
+    key = []
+    for o in ops:
+        bound = {slot for slot, _ in o.bindings}
+        fixed = tuple(v for i, v in enumerate(o.params) if i not in bound)
+        mat = None if o.matrix is None else np.asarray(o.matrix, dtype=np.complex128).tobytes()
+        key.append((o.opcode, tuple(o.qubits), tuple(o.bindings), fixed, mat))
+    return tuple(key)
+
+
+def plan_bound_values(ops: Sequence[PlanOp]) -> Optional[np.ndarray]:
+    """The parent values the operations' bindings carry (index = parent), for
+    CircuitPlan.set_parameters; None when one parent carries two different values."""
+    vals = {}
+    for o in ops:
+        for slot, parent in o.bindings:
+            v = float(o.params[slot])
+            if vals.setdefault(int(parent), v) != v:
+                return None
+    out = np.zeros(max(vals) + 1 if vals else 0)
+    for p, v in vals.items():
+        out[p] = v
+    return out
+
+
 def plan_schedule_export(plan: CircuitPlan, num_qubits: int, adjoint: bool = False,
                          requires_grad=None) -> bytes:
     """The engine's fused-pass schedule for the plan, serialised (arcqml_rt_v2_plan_schedule_export)."""

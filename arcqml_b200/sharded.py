@@ -389,19 +389,35 @@ class RuntimeBackend:
         """shard <- |index> (every other amplitude zero)."""
         self.rt.set_basis_state_device(shard, int(shard.numel()).bit_length() - 1, index)
 
+    def _plan(self, ops: Sequence[PlanOp]):
+        """A plan of these operations. Plans are kept by structure (rt.plan_structure_key): one
+        seen before gets the operations' bound values (arcqml_rt_v2_plan_set_parameters)
+        instead of every operation being marshalled through the C ABI again. Each plan is used
+        at once by the call that asks for it."""
+        key = self.rt.plan_structure_key(ops)
+        plans = self.__dict__.setdefault("_plans", {})
+        plan = plans.get(key)
+        values = None if plan is None else self.rt.plan_bound_values(ops)
+        if plan is not None and values is not None:
+            plan.set_parameters(values)
+            return plan
+        plan = self.rt.CircuitPlan.create(ops)
+        if len(plans) >= 256:
+            plans.clear()
+        plans[key] = plan
+        return plan
+
     def apply(self, ops: Sequence[PlanOp], shard, n_local: int) -> None:
         if not ops:
             return
-        plan = self.rt.CircuitPlan.create(ops)
-        self.rt.plan_apply_device(plan, shard, n_local)
+        self.rt.plan_apply_device(self._plan(ops), shard, n_local)
 
     def adjoint(self, ops: Sequence[PlanOp], psi, lam, n_local: int, upstream, req,
                 grads: np.ndarray) -> None:
         """Reverse sweep over [rows, 2^n_local] psi/lambda; upstream is a scalar or one factor
         per row; gradients (summed over rows) are added to grads."""
-        plan = self.rt.CircuitPlan.create(ops)
-        grads += self.rt.adjoint_backward_device(plan, psi, lam, n_local, upstream, req,
-                                                 len(grads))
+        grads += self.rt.adjoint_backward_device(self._plan(ops), psi, lam, n_local, upstream,
+                                                 req, len(grads))
 
     def observable(self, coef, flip, phase, psi, out, n_local: int) -> float:
         return float(self.observable_rows(coef, flip, phase, psi, out, n_local)[0])

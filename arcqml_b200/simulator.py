@@ -16,6 +16,7 @@ keep the context for a second backward.
 from __future__ import annotations
 
 import os
+import weakref
 from dataclasses import dataclass
 from typing import Optional
 
@@ -45,7 +46,7 @@ def _new_state(num_qubits: int, batch: Optional[int], device):
     return torch.empty(shape, dtype=torch.complex128, device=device)
 
 
-@dataclass
+@dataclass(eq=False)  # identity hashing: plan pools hold contexts in weak sets
 class _Context:
     num_qubits: int
     batch: Optional[int]
@@ -67,6 +68,41 @@ class _SmallContext:
 
 def _small_enabled() -> bool:
     return os.environ.get("ARCQML_SMALL", "1") != "0"
+
+
+def _pool(sim) -> "_PlanPool":
+    return sim.__dict__.setdefault("_plan_pool", _PlanPool())
+
+
+class _PlanPool:
+    """Device plans by circuit structure. Creating a plan marshals every operation through the
+    C ABI (milliseconds of host time for a hundred gates, more than a small batch's whole step);
+    a run whose circuit has the structure of an earlier one takes a plan of that structure that
+    no live result still holds and replaces its bound parameter values
+    (arcqml_rt_v2_plan_set_parameters). A result keeps its plan until it is dropped, so its
+    backward sweep always sees the values it ran with."""
+
+    def __init__(self, limit: int = 64, per_key: int = 4):
+        self._plans = {}
+        self._limit, self._per_key = limit, per_key
+
+    def get(self, circuit: Circuit, offset: int):
+        """(plan, users): the caller adds the result context that holds the plan to users."""
+        ops = circuit.compile_plan(offset)
+        key = (offset, rt.plan_structure_key(ops))
+        entries = self._plans.get(key)
+        if entries is None:
+            if len(self._plans) >= self._limit:
+                self._plans.clear()
+            entries = self._plans[key] = []
+        for plan, users in entries:
+            if len(users) == 0:
+                plan.set_parameters(np.array([0.0] * offset + [p.f64() for p in circuit.parameters]))
+                return plan, users
+        plan, users = rt.CircuitPlan.create(ops), weakref.WeakSet()
+        if len(entries) < self._per_key:
+            entries.append((plan, users))
+        return plan, users
 
 
 class RunResult:
@@ -235,28 +271,24 @@ class StateVectorSimulator:
             rt.set_basis_state_device(psi, self.num_qubits, 0)
         else:
             psi.copy_(self._state)
-        plan = rt.CircuitPlan.create(circuit.compile_plan(1 if records else 0))
+        plan, users = _pool(self).get(circuit, 1 if records else 0)
         rt.plan_apply_device(plan, psi, self.num_qubits)
         obs = rt.Observable.from_sparse_pauli_op(observable)
         if not records:
             return RunResult(obs.expectation(psi, self.num_qubits), None)
         lam = torch.empty_like(psi)
         vals = obs.expectation_and_apply(psi, lam, self.num_qubits)
-        return RunResult(vals, _Context(self.num_qubits, None, psi, lam, plan, circuit,
-                                        self.initial_requires_grad))
+        ctx = _Context(self.num_qubits, None, psi, lam, plan, circuit, self.initial_requires_grad)
+        users.add(ctx)
+        return RunResult(vals, ctx)
 
     # -- small states: one kernel for forward, <H> and the adjoint sweep ----------------------
     def _small_plan(self, circuit: Circuit):
         """A plan for the circuit's structure, reused across runs with its bound parameter
-        values replaced (plan creation costs more host time than the step itself)."""
+        values replaced (plan creation costs more host time than the step itself; the one-kernel
+        step uses the plan at once, so no result holds it)."""
         ops = circuit.compile_plan(1)
-        key = []
-        for o in ops:
-            bound = {slot for slot, _ in o.bindings}
-            fixed = tuple(v for i, v in enumerate(o.params) if i not in bound)
-            mat = None if o.matrix is None else np.asarray(o.matrix, dtype=np.complex128).tobytes()
-            key.append((o.opcode, tuple(o.qubits), tuple(o.bindings), fixed, mat))
-        key = tuple(key)
+        key = rt.plan_structure_key(ops)
         plans = self.__dict__.setdefault("_plans", {})
         plan = plans.get(key)
         if plan is None:
@@ -356,12 +388,14 @@ class BatchStateVectorSimulator:
             raise SimError("circuit, observable and state qubit counts differ")
         records = grad and (self.initial_requires_grad or any(p.requires_grad for p in circuit.parameters))
         psi = self.state.clone()
-        plan = rt.CircuitPlan.create(circuit.compile_plan(1 if records else 0))
+        plan, users = _pool(self).get(circuit, 1 if records else 0)
         rt.plan_apply_device(plan, psi, self.num_qubits)
         obs = rt.Observable.from_sparse_pauli_op(observable)
         if not records:
             return RunResult(obs.expectation(psi, self.num_qubits), None)
         lam = _torch().empty_like(psi)
         vals = obs.expectation_and_apply(psi, lam, self.num_qubits)
-        return RunResult(vals, _Context(self.num_qubits, self.batch_size, psi, lam, plan, circuit,
-                                        self.initial_requires_grad))
+        ctx = _Context(self.num_qubits, self.batch_size, psi, lam, plan, circuit,
+                       self.initial_requires_grad)
+        users.add(ctx)
+        return RunResult(vals, ctx)
