@@ -172,7 +172,7 @@ bool jit_forward_single() {
 }
 
 bool jit_mats_in_params(bool adjoint) {
-    if (adjoint) return false;
+    (void)adjoint;  // forward and adjoint kernels alike
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_JIT_MATS_SMEM");
         return !(e && e[0] == '1');

@@ -26,9 +26,9 @@ uint32_t jit_acc_lanes(bool adjoint, uint32_t rb);
 // Whether compiled forward kernels are single-buffered at two CTAs per SM (on unless
 // ARCQML_FWD_SINGLE=0).
 bool jit_forward_single();
-// Whether compiled kernels take their pass's matrix table as a by-value kernel parameter:
-// forward kernels unless ARCQML_JIT_MATS_SMEM=1; adjoint kernels stage it in shared memory (with
-// the table in parameters they measured 9 % slower: their straight-line code spills).
+// Whether compiled kernels take their pass's matrix table as a by-value kernel parameter
+// (constant-bank operands; forward and adjoint kernels unless ARCQML_JIT_MATS_SMEM=1, which
+// stages it in shared memory: 30-qubit adjoint passes 6.3 % slower that way).
 bool jit_mats_in_params(bool adjoint);
 // Compiles the schedule's passes; true if every pass has a compiled kernel.
 bool jit_schedule_compiles(const Schedule &sch, bool adjoint);
