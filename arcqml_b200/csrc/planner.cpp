@@ -528,6 +528,14 @@ bool fast_diag() {
     return on;
 }
 
+bool lookahead_tiles() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_LOOKAHEAD");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 bool subblock_reorder() {
     static const bool on = [] {
         const char *e = std::getenv("ARCQML_SUBBLOCK_REORDER");
@@ -562,6 +570,8 @@ uint32_t merge_axis(const PGate &g) {
     if (g.parents.size() > 1 || g.gkind == GK_GENERIC || g.m.size() != 4) return 0;
     const uint32_t o = g.op->opcode;
     if (o == ARCQML_OP_RZ) return g.diag ? o : 0;
+    // an RX or RY at angle 0 is the identity: it is emitted as a diagonal, not a rotation form
+    if (g.diag) return 0;
     if (o == ARCQML_OP_RX) return rotation_form(g.m.data()) == FK_RX ? o : 0;
     if (o == ARCQML_OP_RY) return rotation_form(g.m.data()) == FK_RY ? o : 0;
     return 0;
@@ -626,43 +636,91 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
             done[first] = 1;
             continue;
         }
-        // --- choose S and collect the pass's gates (first-come greedy)
-        uint64_t S = low_mask;
-        uint32_t free_slots = k - L;
-        uint64_t blocked = 0;
-        std::vector<size_t> members;
-        size_t pass_acc = 0;
-        size_t pass_mats = 0;
-        MergeChain chain[64];  // the merges the emission below makes, for the row count
-        for (size_t i = first; i < gates.size(); ++i) {
-            if (done[i]) continue;
-            const PGate &g = gates[i];
-            const uint32_t ax = merge_rot ? merge_axis(g) : 0;
-            const bool merges = ax != 0 && chain[g.targets[0]].axis == ax;
-            const size_t rows = (merges && chain[g.targets[0]].row) ? 0 : g.parents.size();
-            if (pass_acc + rows > size_t(kMaxPassAcc)) break;
-            if (pass_mats + mat_entries(g) > size_t(kMaxPassMats)) break;
-            if (g.dense_barrier || (g.touched & blocked)) {
-                blocked |= g.touched;
-                continue;
-            }
-            const uint64_t extra = g.needs & ~S;
-            const uint32_t cnt = uint32_t(__builtin_popcountll(extra));
-            if (cnt <= free_slots) {
-                S |= extra;
-                free_slots -= cnt;
-                members.push_back(i);
-                pass_acc += rows;
-                pass_mats += mat_entries(g);
-                if (merges) {
-                    chain[g.targets[0]].row = chain[g.targets[0]].row || !g.parents.empty();
-                } else if (merge_rot) {
-                    end_chains(chain, g);
-                    if (ax) chain[g.targets[0]] = MergeChain{ax, -1, !g.parents.empty()};
+        // --- choose S and collect the pass's gates. take(S0, free0) walks the remaining gates
+        // in order from tile qubits S0, adding the non-diagonal targets of a gate while free0
+        // qubits are left, and takes every gate the tile holds that no skipped gate blocks.
+        auto take = [&](uint64_t S0, uint32_t free0, std::vector<size_t> &mem) -> uint64_t {
+            uint64_t S = S0, blocked = 0;
+            uint32_t free_slots = free0;
+            size_t pass_acc = 0, pass_mats = 0;
+            MergeChain chain[64];  // the merges the emission below makes, for the row count
+            mem.clear();
+            for (size_t i = first; i < gates.size(); ++i) {
+                if (done[i]) continue;
+                const PGate &g = gates[i];
+                const uint32_t ax = merge_rot ? merge_axis(g) : 0;
+                const bool merges = ax != 0 && chain[g.targets[0]].axis == ax;
+                const size_t rows = (merges && chain[g.targets[0]].row) ? 0 : g.parents.size();
+                if (pass_acc + rows > size_t(kMaxPassAcc)) break;
+                if (pass_mats + mat_entries(g) > size_t(kMaxPassMats)) break;
+                if (g.dense_barrier || (g.touched & blocked)) {
+                    blocked |= g.touched;
+                    continue;
                 }
-                if (members.size() >= pass_op_cap()) break;
-            } else {
-                blocked |= g.touched;
+                const uint64_t extra = g.needs & ~S;
+                const uint32_t cnt = uint32_t(__builtin_popcountll(extra));
+                if (cnt <= free_slots) {
+                    S |= extra;
+                    free_slots -= cnt;
+                    mem.push_back(i);
+                    pass_acc += rows;
+                    pass_mats += mat_entries(g);
+                    if (merges) {
+                        chain[g.targets[0]].row = chain[g.targets[0]].row || !g.parents.empty();
+                    } else if (merge_rot) {
+                        end_chains(chain, g);
+                        if (ax) chain[g.targets[0]] = MergeChain{ax, -1, !g.parents.empty()};
+                    }
+                    if (mem.size() >= pass_op_cap()) break;
+                } else {
+                    blocked |= g.touched;
+                }
+            }
+            return S;
+        };
+        std::vector<size_t> members;
+        uint64_t S = take(low_mask, k - L, members);  // first come: targets in gate order
+        if (lookahead_tiles() && n > k) {
+            // Lookahead: the qubits beyond the low ones one at a time, each the one whose tile
+            // (the low qubits, those picked so far and it) holds the most of the remaining
+            // gates; the pass keeps the choice that takes more gates.
+            auto held = [&](uint64_t Sx) {
+                uint64_t blk = 0;
+                size_t cnt = 0, acc = 0, mats = 0;
+                for (size_t i = first; i < gates.size(); ++i) {
+                    if (done[i]) continue;
+                    const PGate &g = gates[i];
+                    if (acc + g.parents.size() > size_t(kMaxPassAcc)) break;
+                    if (mats + mat_entries(g) > size_t(kMaxPassMats)) break;
+                    if (g.dense_barrier || (g.touched & blk) || (g.needs & ~Sx)) {
+                        blk |= g.touched;
+                        continue;
+                    }
+                    ++cnt;
+                    acc += g.parents.size();
+                    mats += mat_entries(g);
+                }
+                return cnt;
+            };
+            uint64_t SL = low_mask;
+            for (uint32_t pick = L; pick < k; ++pick) {
+                int best = -1;
+                size_t best_n = 0;
+                for (uint32_t q = L; q < n; ++q) {
+                    if ((SL >> q) & 1) continue;
+                    const size_t c = held(SL | (uint64_t(1) << q));
+                    if (best < 0 || c > best_n) {
+                        best = int(q);
+                        best_n = c;
+                    }
+                }
+                SL |= uint64_t(1) << best;
+            }
+            std::vector<size_t> alt;
+            take(SL, 0, alt);
+            if (alt.size() > members.size()) {
+                members.swap(alt);
+                S = SL;
             }
         }
         // fill S up to k bits with the lowest unused qubits (keeps runs long)
@@ -908,6 +966,9 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                         st.parents.push_back(g.parents[s2]);
                     }
                 }
+                // the op must carry the axis's form (merges above rewrite it as that form)
+                const uint8_t want = ax == ARCQML_OP_RZ ? FK_D1 : ax == ARCQML_OP_RX ? FK_RX : FK_RY;
+                if (ax && o.kind != want) fail("internal: rotation emitted without its form");
                 if (ax) echain[g.targets[0]] = MergeChain{ax, int(st.ops.size()), false};
                 st.ops.push_back(o);
             }

@@ -47,6 +47,11 @@ bool fast_cnot();
 // one-qubit gates within a register sub-block without it).
 bool rotation_merge();
 
+// Whether each pass also tries tile qubits picked by lookahead (each qubit the one whose tile
+// holds the most remaining gates) and keeps whichever choice takes more gates (on unless
+// ARCQML_LOOKAHEAD=0: tile qubits in the order the gates need them).
+bool lookahead_tiles();
+
 // Whether the run-time compiled kernels run diagonal gates with controls, two-qubit diagonals,
 // controlled one-target gates and generic slot gradients (on unless ARCQML_FAST_DIAG=0).
 bool fast_diag();

@@ -113,7 +113,7 @@ def test_benchmark_schedule_compiles_completely(runtime):
         r = plan.jit_check(32, adjoint)
         if r["eligible"] == 0 and "not found" in r["message"]:
             pytest.skip("NVRTC is not available: " + r["message"])
-        assert r["eligible"] >= 20 and r["compiled"] == r["eligible"], r
+        assert r["eligible"] >= 15 and r["compiled"] == r["eligible"], r
         assert plan.schedule_stats(32, adjoint)["passes"] == r["eligible"]
 
 

@@ -141,12 +141,12 @@ def general_shapes(n, seed):
     return c
 
 
-SWITCHES = ("ARCQML_SUBBLOCK_REORDER", "ARCQML_FAST_CNOT", "ARCQML_FAST_DIAG")
+SWITCHES = ("ARCQML_SUBBLOCK_REORDER", "ARCQML_FAST_CNOT", "ARCQML_FAST_DIAG", "ARCQML_LOOKAHEAD")
 
 
 @pytest.mark.parametrize("env", SWITCHES + ("all",))
 def test_switches_off_run_their_compiled_code_on_host(env):
-    """Each switch turned off alone, and all three off (subprocesses): the brickwork and
+    """Each switch turned off alone, and all of them off (subprocesses): the brickwork and
     fast-path circuits, and the CNOT rings while one of FAST_CNOT / FAST_DIAG still gives them
     compiled code."""
     here = os.path.dirname(os.path.abspath(__file__))

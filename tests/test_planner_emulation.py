@@ -344,3 +344,56 @@ def test_rotation_merges_off_emulate_correctly():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        env=dict(os.environ, ARCQML_ROT_MERGE="0"), timeout=600)
     assert r.returncode == 0 and "merge-off-ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_lookahead_tiles_take_fewer_passes(runtime):
+    """By default each pass keeps the better of two tile choices, targets in gate order or
+    lookahead (each qubit the one whose tile holds the most remaining gates); with
+    ARCQML_LOOKAHEAD=0 (subprocess) only the first. The 32-qubit benchmark's schedules take fewer
+    passes by default, and the first-come schedules still emulate correctly."""
+    import json
+    import os
+    import subprocess
+    import sys
+    c = workloads.brickwork(32, 20, seed=1234)
+    plan = runtime.CircuitPlan.create(c.compile_plan(1))
+    default = [plan.schedule_stats(32, adj)["passes"] for adj in (False, True)]
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = ("import sys, json; sys.path[:0] = [%r, %r, %r]\n"
+            "import numpy as np, oracle, test_planner_emulation as T\n"
+            "from arcqml_b200 import runtime, workloads as W\n"
+            "c = W.brickwork(32, 20, seed=1234); p = runtime.CircuitPlan.create(c.compile_plan(1))\n"
+            "counts = [p.schedule_stats(32, a)['passes'] for a in (False, True)]\n"
+            "T.test_brickwork_and_edge_angles(runtime, oracle, 12)\n"
+            "print(json.dumps(counts))\n") % (root, here, os.path.join(root, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       env=dict(os.environ, ARCQML_LOOKAHEAD="0"), timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    first_come = json.loads(r.stdout.strip().splitlines()[-1])
+    assert default[0] < first_come[0] and default[1] < first_come[1], (default, first_come)
+
+
+def test_identity_angle_rotations_beside_merged_runs(runtime, oracle):
+    """RX / RY at angle 0 are the identity and are emitted as diagonals, so they must not head a
+    run that later rotations about the same axis merge into: each qubit gets a CZ, then RX(0) or
+    RY(0) as its first one-qubit gate, then rotations about the same axis; forward and adjoint
+    against the oracle, with and without gradients on the zero-angle rotations."""
+    n = 10
+    g = np.random.Generator(np.random.PCG64(37))
+    c = cm.Circuit(n)
+    for layer in range(4):
+        for a in range(layer % 2, n - 1, 2):
+            c.append("cz", (a, a + 1))
+        for q in range(n):
+            axis = ("rx", "ry")[(q + layer) % 2]
+            if (q + layer) % 3 == 0:
+                c.append(axis, (q,), 0.0)  # a constant identity
+            else:
+                c.rot(axis, 0.0, q)
+            for _ in range(2):
+                c.rot(axis, float(g.uniform(-math.pi, math.pi)), q)
+            c.rot("rz", float(g.uniform(-math.pi, math.pi)), q)
+    ops = c.compile_plan(1)
+    check(runtime, oracle, ops, n, random_terms(g, n, 20), random_state(g, n),
+          list(c.requires_grad_mask(True)), 0.6)
