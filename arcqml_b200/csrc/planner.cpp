@@ -1,10 +1,11 @@
 // planner.cpp — partitions a gate sequence into fused passes (see fused.h).
 //
-// Greedy, order-preserving: a pass picks its tile qubits S (qubits 0..L-1 plus the first
-// non-diagonal targets met in circuit order) and takes every gate it can, in order, whose
-// non-diagonal targets lie in S and that does not need to move past a gate it left behind
-// (a gate sharing a qubit with a skipped gate is skipped too, so the relative order of all gates
-// on any qubit is kept). Inside a pass, consecutive gates are grouped into sub-blocks whose
+// Greedy, order-preserving: a pass picks its tile qubits S (qubits 0..L-1 plus either the first
+// non-diagonal targets met in circuit order, or qubits picked by lookahead, each the one whose
+// tile holds the most remaining gates: whichever takes more gates) and takes every gate it can,
+// in order, whose non-diagonal targets lie in S and that does not need to move past a gate it
+// left behind (a gate sharing a qubit with a skipped gate is skipped too, so the relative order
+// of all gates on any qubit is kept). Inside a pass, consecutive gates are grouped into sub-blocks whose
 // non-diagonal targets fit in RB register bits. Custom gates on more than two targets cannot be
 // fused and run as separate per-gate kernels between passes.
 #include <algorithm>
