@@ -626,6 +626,26 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
     size_t first = 0;
     uint32_t acc_total = 0;
     const bool merge_rot = rotation_merge();
+    // Tile choices of an earlier schedule of this plan with the same gate structure (what the
+    // member walk below reads of each gate: its qubits, non-diagonal targets, table size, rows,
+    // merge axis) are taken again instead of searched.
+    std::vector<uint64_t> sig;
+    sig.reserve(3 * gates.size());
+    for (const PGate &g : gates) {
+        sig.push_back(g.touched);
+        sig.push_back(g.needs);
+        sig.push_back(uint64_t(g.noop) | uint64_t(g.dense_barrier) << 1 |
+                      uint64_t(g.parents.size()) << 2 | uint64_t(merge_rot ? merge_axis(g) : 0) << 8 |
+                      uint64_t(mat_entries(g)) << 16 | uint64_t(g.targets.empty() ? 0 : g.targets[0]) << 40);
+    }
+    const uint64_t ckey = uint64_t(n) | uint64_t(k) << 8 | uint64_t(rb) << 16 |
+                          uint64_t(adjoint) << 24 | uint64_t(lookahead_tiles()) << 25;
+    std::vector<std::pair<uint64_t, uint32_t>> cached, chosen;
+    {
+        std::lock_guard<std::mutex> lock(plan.tiles_mu);
+        for (const TileChoices &t : plan.tiles)
+            if (t.key == ckey && t.signature == sig) cached = t.take;
+    }
     while (true) {
         while (first < gates.size() && done[first]) ++first;
         if (first >= gates.size()) break;
@@ -646,7 +666,9 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
             size_t pass_acc = 0, pass_mats = 0;
             MergeChain chain[64];  // the merges the emission below makes, for the row count
             mem.clear();
+            const uint64_t all = n >= 64 ? ~uint64_t(0) : (uint64_t(1) << n) - 1;
             for (size_t i = first; i < gates.size(); ++i) {
+                if (blocked == all) break;  // every later gate is blocked
                 if (done[i]) continue;
                 const PGate &g = gates[i];
                 const uint32_t ax = merge_rot ? merge_axis(g) : 0;
@@ -680,48 +702,58 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
             return S;
         };
         std::vector<size_t> members;
-        uint64_t S = take(low_mask, k - L, members);  // first come: targets in gate order
-        if (lookahead_tiles() && n > k) {
-            // Lookahead: the qubits beyond the low ones one at a time, each the one whose tile
-            // (the low qubits, those picked so far and it) holds the most of the remaining
-            // gates; the pass keeps the choice that takes more gates.
-            auto held = [&](uint64_t Sx) {
-                uint64_t blk = 0;
-                size_t cnt = 0, acc = 0, mats = 0;
-                for (size_t i = first; i < gates.size(); ++i) {
-                    if (done[i]) continue;
-                    const PGate &g = gates[i];
-                    if (acc + g.parents.size() > size_t(kMaxPassAcc)) break;
-                    if (mats + mat_entries(g) > size_t(kMaxPassMats)) break;
-                    if (g.dense_barrier || (g.touched & blk) || (g.needs & ~Sx)) {
-                        blk |= g.touched;
-                        continue;
+        uint64_t S;
+        if (chosen.size() < cached.size()) {  // as an earlier schedule of this structure
+            chosen.push_back(cached[chosen.size()]);
+            S = take(chosen.back().first, chosen.back().second, members);
+        } else {  // search: first come, then lookahead
+            chosen.push_back({low_mask, k - L});
+            S = take(low_mask, k - L, members);  // first come: targets in gate order
+            if (lookahead_tiles() && n > k) {
+                // Lookahead: the qubits beyond the low ones one at a time, each the one whose tile
+                // (the low qubits, those picked so far and it) holds the most of the remaining
+                // gates; the pass keeps the choice that takes more gates.
+                const uint64_t all = n >= 64 ? ~uint64_t(0) : (uint64_t(1) << n) - 1;
+                auto held = [&](uint64_t Sx) {
+                    uint64_t blk = 0;
+                    size_t cnt = 0, acc = 0, mats = 0;
+                    for (size_t i = first; i < gates.size(); ++i) {
+                        if (blk == all) break;  // every later gate is blocked
+                        if (done[i]) continue;
+                        const PGate &g = gates[i];
+                        if (acc + g.parents.size() > size_t(kMaxPassAcc)) break;
+                        if (mats + mat_entries(g) > size_t(kMaxPassMats)) break;
+                        if (g.dense_barrier || (g.touched & blk) || (g.needs & ~Sx)) {
+                            blk |= g.touched;
+                            continue;
+                        }
+                        ++cnt;
+                        acc += g.parents.size();
+                        mats += mat_entries(g);
                     }
-                    ++cnt;
-                    acc += g.parents.size();
-                    mats += mat_entries(g);
-                }
-                return cnt;
-            };
-            uint64_t SL = low_mask;
-            for (uint32_t pick = L; pick < k; ++pick) {
-                int best = -1;
-                size_t best_n = 0;
-                for (uint32_t q = L; q < n; ++q) {
-                    if ((SL >> q) & 1) continue;
-                    const size_t c = held(SL | (uint64_t(1) << q));
-                    if (best < 0 || c > best_n) {
-                        best = int(q);
-                        best_n = c;
+                    return cnt;
+                };
+                uint64_t SL = low_mask;
+                for (uint32_t pick = L; pick < k; ++pick) {
+                    int best = -1;
+                    size_t best_n = 0;
+                    for (uint32_t q = L; q < n; ++q) {
+                        if ((SL >> q) & 1) continue;
+                        const size_t c = held(SL | (uint64_t(1) << q));
+                        if (best < 0 || c > best_n) {
+                            best = int(q);
+                            best_n = c;
+                        }
                     }
+                    SL |= uint64_t(1) << best;
                 }
-                SL |= uint64_t(1) << best;
-            }
-            std::vector<size_t> alt;
-            take(SL, 0, alt);
-            if (alt.size() > members.size()) {
-                members.swap(alt);
-                S = SL;
+                std::vector<size_t> alt;
+                take(SL, 0, alt);
+                if (alt.size() > members.size()) {
+                    members.swap(alt);
+                    S = SL;
+                    chosen.back() = {SL, 0u};
+                }
             }
         }
         // fill S up to k bits with the lowest unused qubits (keeps runs long)
@@ -995,6 +1027,20 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
         sch.steps.push_back(std::move(st));
     }
     sch.total_acc = acc_total;
+    if (cached.empty()) {
+        std::lock_guard<std::mutex> lock(plan.tiles_mu);
+        bool stored = false;
+        for (TileChoices &t : plan.tiles)
+            if (t.key == ckey) {
+                t.signature = sig;
+                t.take = chosen;
+                stored = true;
+            }
+        if (!stored) {
+            if (plan.tiles.size() >= 8) plan.tiles.erase(plan.tiles.begin());
+            plan.tiles.push_back(TileChoices{ckey, sig, chosen});
+        }
+    }
     return sch;
 }
 

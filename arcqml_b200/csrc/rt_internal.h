@@ -93,8 +93,18 @@ std::vector<double2> dense_matrix(const OpRecord &op, bool derivative, uint32_t 
 
 // ------------------------------------------------------------------ plans
 
+// The tile qubits each pass of a schedule took (planner.cpp), kept with the plan so that a
+// schedule of the same gate structure skips the lookahead search.
+struct TileChoices {
+    uint64_t key = 0;                                // n, k, rb, direction
+    std::vector<uint64_t> signature;                 // per gate, what the choice depended on
+    std::vector<std::pair<uint64_t, uint32_t>> take; // per pass: start tile, free qubits
+};
+
 struct Plan {
     std::vector<OpRecord> ops;
+    mutable std::mutex tiles_mu;
+    mutable std::vector<TileChoices> tiles;  // a few entries (one per schedule kind)
 };
 
 // ------------------------------------------------------------------ observables

@@ -397,3 +397,35 @@ def test_identity_angle_rotations_beside_merged_runs(runtime, oracle):
     ops = c.compile_plan(1)
     check(runtime, oracle, ops, n, random_terms(g, n, 20), random_state(g, n),
           list(c.requires_grad_mask(True)), 0.6)
+
+
+def test_cached_tile_choices_follow_the_gate_structure(runtime, oracle):
+    """A plan keeps the tile qubits its schedules took, keyed by the gates' structure: the same
+    schedule again is identical, and new values that change the structure (rotations set to 0
+    become diagonals) are planned afresh; forward and adjoint of the changed plan against the
+    oracle."""
+    n = 12
+    g = np.random.Generator(np.random.PCG64(55))
+    c = workloads.brickwork(n, 5, seed=55)
+    ops = c.compile_plan(1)
+    req = list(c.requires_grad_mask(True))
+    plan = runtime.CircuitPlan.create(ops)
+    for adjoint in (False, True):
+        a = runtime.plan_schedule_export(plan, n, adjoint, req if adjoint else None)
+        b = runtime.plan_schedule_export(plan, n, adjoint, req if adjoint else None)
+        assert a == b
+    vals = np.array([p.f64() for p in c.parameters])
+    vals[::3] = 0.0
+    c.set_parameter_values(vals)
+    plan.set_parameters(np.concatenate([[0.0], vals]))
+    ops2 = c.compile_plan(1)
+    init = random_state(g, n)
+    psi = runtime.plan_emulate(plan, init, n)
+    ref = oracle.plan_apply(ops2, init, n)
+    assert float(np.max(np.abs(psi - ref))) < 1e-12
+    _, lam = oracle.expectation_and_apply(random_terms(g, n, 15), ref, n)
+    p0, l0, grads = runtime.plan_emulate(plan, psi, n, adjoint=True, lam=lam,
+                                         requires_grad=req, num_gradients=len(req))
+    _, rl0, rg = oracle.adjoint_backward(ops2, ref, lam, n, 1.0, req, len(req))
+    assert float(np.max(np.abs(p0 - init))) < 1e-10
+    assert float(np.max(np.abs(grads - rg))) <= 1e-10 * max(1.0, float(np.max(np.abs(rg))))
