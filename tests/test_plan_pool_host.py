@@ -87,3 +87,25 @@ def test_bound_values_of_a_parent_must_agree(runtime):
                              ops[1].bindings, ops[1].name)]
     assert runtime.plan_bound_values(bad) is None
     assert runtime.plan_structure_key(bad) == runtime.plan_structure_key(ops)
+
+
+def test_schedule_summary_counts(runtime):
+    """plan_schedule_summary (the counts bench.py's FP64 roofline uses) agrees with the
+    schedule's own statistics: passes, ops (= gates after merges), one gradient row per
+    rotation op that has a gradient, merged parameters as aliases."""
+    from arcqml_b200.workloads import brickwork
+    n = 20
+    c = brickwork(n, 6, seed=3)
+    plan = runtime.CircuitPlan.create(c.compile_plan(1))
+    req = np.asarray(c.requires_grad_mask(True), np.uint8)
+    for adj in (False, True):
+        summ = runtime.plan_schedule_summary(plan, n, adj, req if adj else None)
+        stats = plan.schedule_stats(n, adj)
+        assert summ["passes"] == stats["passes"] and summ["ops"] == stats["gates"]
+        assert summ["custom"] == 0 and summ["rotations"] <= summ["ops"]
+        if adj:
+            # every rotation of the brickwork has a parameter: rows + aliases = rotations
+            assert summ["rows"] + summ["aliases"] == c.num_parameters()
+            assert summ["rows"] == summ["rotations"]
+        else:
+            assert summ["rows"] == 0 and summ["aliases"] == 0
