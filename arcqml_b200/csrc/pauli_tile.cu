@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -57,6 +58,17 @@ struct TileArgs {
     // phase pattern: those of key k are [hbeg[k], hbeg[k + 1]); groups of several terms are
     // [hbeg[32], ngroups)
     uint32_t hbeg[33];
+};
+
+// A pass's group and term tables as a by-value kernel parameter (constant-bank reads, uniform
+// over the warp), for passes small enough; larger ones are copied into shared memory.
+constexpr uint32_t kInlineGroups = 128, kInlineMembers = 512;
+struct TileTables {
+    uint4 g[kInlineGroups];
+    TileMember m[kInlineMembers];
+};
+struct NoTileTables {
+    uint32_t unused;
 };
 
 __device__ __forceinline__ uint32_t tphys(uint32_t j) {
@@ -117,15 +129,24 @@ __device__ __forceinline__ void add_weight(double2 (&wi)[8], double2 w) {
 #define ARCQML_H16(M) M(0) M(1) M(2) M(3) M(4) M(5) M(6) M(7) M(8) M(9) M(10) M(11) M(12) \
     M(13) M(14) M(15)
 
+template <bool INL, class TT>
 __global__ void __launch_bounds__(kTileThreads, 2)
     k_pauli_tile(const double2 *__restrict__ psi, double2 *__restrict__ out, uint32_t n,
                  uint64_t total_tiles, const __grid_constant__ TileArgs P,
-                 double *__restrict__ partials) {
+                 const __grid_constant__ TT T, double *__restrict__ partials) {
     extern __shared__ __align__(16) unsigned char sm[];
     double2 *tile = reinterpret_cast<double2 *>(sm);                        // 64 KB
     uint64_t *hioff = reinterpret_cast<uint64_t *>(sm + (16u << kTileQ));  // 256 entries
     uint4 *sg = reinterpret_cast<uint4 *>(hioff + (1u << (kTileQ - kTileLow)));
     TileMember *smem_m = reinterpret_cast<TileMember *>(sg + P.ngroups);
+    auto grp = [&](uint32_t gi) -> uint4 {
+        if constexpr (INL) return T.g[gi];
+        else return sg[gi];
+    };
+    auto mem = [&](uint32_t mi) -> const TileMember & {
+        if constexpr (INL) return T.m[mi];
+        else return smem_m[mi];
+    };
     __shared__ double red[kTileThreads / 32];
     const uint32_t tid = threadIdx.x;
     for (uint32_t h = tid; h < (1u << (kTileQ - kTileLow)); h += blockDim.x) {
@@ -134,8 +155,10 @@ __global__ void __launch_bounds__(kTileThreads, 2)
             if ((h >> b) & 1u) off |= uint64_t(1) << P.S[kTileLow + b];
         hioff[h] = off;
     }
-    for (uint32_t g = tid; g < P.ngroups; g += blockDim.x) sg[g] = P.groups[g];
-    for (uint32_t m = tid; m < P.nmembers; m += blockDim.x) smem_m[m] = P.members[m];
+    if constexpr (!INL) {
+        for (uint32_t g = tid; g < P.ngroups; g += blockDim.x) sg[g] = P.groups[g];
+        for (uint32_t m = tid; m < P.nmembers; m += blockDim.x) smem_m[m] = P.members[m];
+    }
     __syncthreads();
 
     const uint32_t ptid = tphys(tid);
@@ -177,20 +200,20 @@ __global__ void __launch_bounds__(kTileThreads, 2)
 #define ARCQML_LOOP(H)                                                                     \
         _Pragma("unroll 1")                                                                \
         for (uint32_t gi = P.hbeg[2 * H]; gi < P.hbeg[2 * H + 1]; ++gi) {                  \
-            const uint4 G = sg[gi];                                                        \
+            const uint4 G = grp(gi);                                                       \
             add_group<H, false>(acc, tile, ptid ^ G.x,                                     \
-                                member_weight(smem_m[G.y], base, tid).x);                  \
+                                member_weight(mem(G.y), base, tid).x);                     \
         }                                                                                  \
         _Pragma("unroll 1")                                                                \
         for (uint32_t gi = P.hbeg[2 * H + 1]; gi < P.hbeg[2 * H + 2]; ++gi) {              \
-            const uint4 G = sg[gi];                                                        \
+            const uint4 G = grp(gi);                                                       \
             add_group<H, true>(acc, tile, ptid ^ G.x,                                      \
-                               member_weight(smem_m[G.y], base, tid).y);                   \
+                               member_weight(mem(G.y), base, tid).y);                      \
         }
         ARCQML_H16(ARCQML_LOOP)
 #undef ARCQML_LOOP
         for (uint32_t gi = P.hbeg[32]; gi < P.ngroups; ++gi) {
-            const uint4 G = sg[gi];
+            const uint4 G = grp(gi);
             const uint32_t x = ptid ^ G.x;
             {
                 // several terms share the flip mask: per element the sum of their signed
@@ -201,7 +224,7 @@ __global__ void __launch_bounds__(kTileThreads, 2)
 #pragma unroll
                     for (uint32_t i = 0; i < 8; ++i) wi[i] = make_double2(0.0, 0.0);
                     for (uint32_t mi = G.y; mi < G.z; ++mi) {
-                        const TileMember &m = smem_m[mi];
+                        const TileMember &m = mem(mi);
                         const double2 w = member_weight(m, base, tid);
                         if (half == 0) {
                             switch (m.h) {
@@ -528,6 +551,16 @@ std::shared_ptr<const TilePlan> tile_plan(const Observable &obs, uint32_t n) {
     return tp;
 }
 
+// Whether passes small enough take their tables as a kernel parameter (on unless
+// ARCQML_TILE_TABLES_SMEM=1: always through shared memory).
+bool tile_tables_inline() {
+    static const bool on = [] {
+        const char *e = std::getenv("ARCQML_TILE_TABLES_SMEM");
+        return !(e && e[0] == '1');
+    }();
+    return on;
+}
+
 }  // namespace
 
 uint32_t observable_tile_passes(const Observable &obs, uint32_t n) {
@@ -551,13 +584,19 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
     check_cuda(cudaGetDevice(&d), "cudaGetDevice");
     check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d),
                "cudaDeviceGetAttribute");
-    check_cuda(cudaFuncSetAttribute(k_pauli_tile, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const auto k_smem = k_pauli_tile<false, NoTileTables>;
+    const auto k_inl = k_pauli_tile<true, TileTables>;
+    check_cuda(cudaFuncSetAttribute(k_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(tp->max_smem)),
                "cudaFuncSetAttribute");
-    int per_sm = 0;
-    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_pauli_tile,
+    check_cuda(cudaFuncSetAttribute(k_inl, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(tile_smem(0, 0))),
+               "cudaFuncSetAttribute");
+    int per_sm = 0;  // the shared-memory kernel's occupancy; the other one needs less memory
+    check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_smem,
                                                              int(kTileThreads), tp->max_smem),
                "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    std::vector<TileTables> tables(1);  // the inline tables of the pass being launched
     const uint64_t total_tiles = uint64_t(1) << (n - kTileQ);
     const uint32_t grid =
         uint32_t(std::min<uint64_t>(total_tiles, uint64_t(sms) * std::max(per_sm, 1)));
@@ -574,13 +613,23 @@ bool observable_tiled(const Observable &obs, const double2 *psi, double2 *out, u
         a.ev_sub = (out && p == 0 && accumulate) ? 1u : 0u;
         a.ev_add = (!out || p + 1 == passes.size()) ? 1u : 0u;
         for (uint32_t h = 0; h < 33; ++h) a.hbeg[h] = tp->hbeg[p][h];
-        const size_t smem = tile_smem(a.ngroups, a.nmembers);
+        const bool inl = tile_tables_inline() && a.ngroups <= kInlineGroups &&
+                         a.nmembers <= kInlineMembers;
+        const size_t smem = inl ? tile_smem(0, 0) : tile_smem(a.ngroups, a.nmembers);
         // algorithmic traffic of the pass: psi read, H psi written (and read back after pass 0)
         const double per_amp = 16.0 + (out ? (a.read_out ? 32.0 : 16.0) : 0.0);
         const ProfToken tok = prof_begin(PROF_PAULI, s);
         prof_count_launch();
-        k_pauli_tile<<<grid, kTileThreads, smem, s>>>(psi, out, n, total_tiles, a,
-                                                      partials + p * size_t(grid));
+        if (inl) {
+            const char *hb = reinterpret_cast<const char *>(tp->blob.data());
+            std::memcpy(tables[0].g, hb + tp->goff[p], a.ngroups * sizeof(uint4));
+            std::memcpy(tables[0].m, hb + tp->moff[p], a.nmembers * sizeof(TileMember));
+            k_inl<<<grid, kTileThreads, smem, s>>>(psi, out, n, total_tiles, a, tables[0],
+                                                   partials + p * size_t(grid));
+        } else {
+            k_smem<<<grid, kTileThreads, smem, s>>>(psi, out, n, total_tiles, a, NoTileTables{},
+                                                    partials + p * size_t(grid));
+        }
         prof_end(tok, s, per_amp * double(uint64_t(1) << n));
         check_cuda(cudaGetLastError(), "observable tile pass launch");
     }
