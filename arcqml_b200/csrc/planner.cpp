@@ -146,6 +146,15 @@ int rotation_form(const double2 m[4]) {
     return 0;
 }
 
+// Whether a 2x2 (row-major) has the form of `kind` (FK_RX or FK_RY). rotation_form tests the RX
+// form first, so it calls the identity (either form with s = 0) an RX form.
+bool has_rotation_form(const double2 m[4], int kind) {
+    const bool same_diag = eq(m[0], m[3]) && m[0].y == 0.0;
+    if (kind == FK_RX) return same_diag && m[1].x == 0.0 && eq(m[1], m[2]);
+    if (kind == FK_RY) return same_diag && m[1].y == 0.0 && m[2].y == 0.0 && m[1].x == -m[2].x;
+    return false;
+}
+
 // Whether a 2x2 (row-major) has a scaled unit-diagonal form: an RX- or RY-form rotation or a
 // diagonal with |d0| = |d1| (what scale_pass below rewrites).
 bool scalable_1q(const double2 m[4]) {
@@ -878,7 +887,9 @@ Schedule build_schedule(const Plan &plan, uint32_t n, bool adjoint, const uint8_
                         st.mats.push_back(p[0]);
                         st.mats.push_back(p[3]);
                     } else {
-                        if (rotation_form(p) != e.kind) fail("internal: merged rotation lost its form");
+                        // (two rotations about one axis make one about it, the identity included)
+                        if (!has_rotation_form(p, e.kind))
+                            fail("internal: merged rotation lost its form");
                         st.mats.push_back(make_double2(p[0].x, e.kind == FK_RX ? -p[1].y : p[2].x));
                     }
                     if (!g.parents.empty()) {

@@ -237,3 +237,10 @@ def test_merged_adjoint_rotations_run_on_host(runtime, oracle, n):
     code of the merged ops and the rows shared by several parameters."""
     from test_planner_emulation import merge_runs
     check(runtime, oracle, merge_runs(n, 40 + n), n, seed=n)
+
+
+def test_cancelling_rotation_runs_run_on_host(runtime, oracle):
+    """Merged runs whose angles cancel (test_planner_emulation.cancel_runs): the compiled code
+    of the identity-valued merged rotations."""
+    from test_planner_emulation import cancel_runs
+    check(runtime, oracle, cancel_runs(10, 62), 10, seed=62)

@@ -429,3 +429,31 @@ def test_cached_tile_choices_follow_the_gate_structure(runtime, oracle):
     _, rl0, rg = oracle.adjoint_backward(ops2, ref, lam, n, 1.0, req, len(req))
     assert float(np.max(np.abs(p0 - init))) < 1e-10
     assert float(np.max(np.abs(grads - rg))) <= 1e-10 * max(1.0, float(np.max(np.abs(rg))))
+
+
+def cancel_runs(n, seed):
+    """Same-axis runs whose angles cancel (RY(a) RY(-a), RX(a) RX(-a)) after a CZ layer, then a
+    further rotation about that axis and an RZ, on every qubit."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    c = cm.Circuit(n)
+    for layer in range(4):
+        for a in range(layer % 2, n - 1, 2):
+            c.append("cz", (a, a + 1))
+        for q in range(n):
+            axis = ("rx", "ry")[(q + layer) % 2]
+            t = float(g.uniform(-math.pi, math.pi))
+            c.rot(axis, t, q)
+            c.rot(axis, -t, q)
+            c.rot(axis, float(g.uniform(-math.pi, math.pi)), q)
+            c.rot("rz", float(g.uniform(-math.pi, math.pi)), q)
+    return c
+
+
+def test_rotation_runs_that_cancel(runtime, oracle):
+    """Runs whose angles cancel merge into the identity, which is still a rotation of the run's
+    axis for the rotations merged after it; forward and adjoint against the oracle."""
+    n = 9
+    g = np.random.Generator(np.random.PCG64(61))
+    c = cancel_runs(n, 61)
+    check(runtime, oracle, c.compile_plan(1), n, random_terms(g, n, 15), random_state(g, n),
+          list(c.requires_grad_mask(True)), -0.8)
