@@ -457,3 +457,40 @@ def test_rotation_runs_that_cancel(runtime, oracle):
     c = cancel_runs(n, 61)
     check(runtime, oracle, c.compile_plan(1), n, random_terms(g, n, 15), random_state(g, n),
           list(c.requires_grad_mask(True)), -0.8)
+
+
+def edge_family(n, seed):
+    """Random layers of rotations about random axes, 40 % of them at edge angles (0, pi, -pi,
+    pi (1 - 1e-9), 1e-300, 2 pi), some with constant angles, phase and X-type gates, then CZ or
+    CNOT between neighbours: the circuits in which the merge and form edge cases turned up."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    c = cm.Circuit(n)
+    angles = (0.0, math.pi, -math.pi, math.pi * (1 - 1e-9), 1e-300, 2 * math.pi)
+    for layer in range(int(g.integers(3, 8))):
+        for q in range(n):
+            for _ in range(int(g.integers(1, 4))):
+                axis = ("rx", "ry", "rz")[int(g.integers(0, 3))]
+                a = angles[int(g.integers(0, len(angles)))] if g.uniform() < 0.4 \
+                    else float(g.uniform(-3, 3))
+                if g.uniform() < 0.2:
+                    c.append(axis, (q,), a)
+                else:
+                    c.rot(axis, a, q)
+            if g.uniform() < 0.2:
+                c.append(("s", "t", "h", "x", "sdg")[int(g.integers(0, 5))], (q,))
+        for a in range(layer % 2, n - 1, 2):
+            r = g.uniform()
+            c.append("cz" if r < 0.6 else "cnot", (a, a + 1) if r < 0.8 else (a + 1, a))
+    return c
+
+
+@pytest.mark.parametrize("seed", [5, 6, 17, 33, 64, 72, 73, 98])
+def test_edge_family_sweep(runtime, oracle, seed):
+    """Seeded circuits of the edge family, forward and adjoint against the oracle (in all but
+    seed 6 a merged run of rotations that cancel made the planner fail before it tested the
+    run's own axis form)."""
+    g = np.random.Generator(np.random.PCG64(1000 + seed))
+    n = int(g.integers(9, 14))
+    c = edge_family(n, seed)
+    check(runtime, oracle, c.compile_plan(1), n, random_terms(g, n, 15), random_state(g, n),
+          list(c.requires_grad_mask(True)), float(g.normal()))
